@@ -1,0 +1,12 @@
+"""Test configuration: the `gpu` marker selects tests that need a B200 (`pytest -m gpu`)."""
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+  sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+  config.addinivalue_line("markers", "gpu: needs a CUDA B200 and the built libaf_cuda.so")
+  config.addinivalue_line("markers", "slow: long-running CPU test")
