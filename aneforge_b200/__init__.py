@@ -1,0 +1,12 @@
+"""aneforge_b200: a B200-native (sm_100a) drop-in for ANEForge's quantized LLM inference hot path.
+
+`load_llm` / `llm.LlamaPrefill.generate` and the compress= weight policy keep the reference's
+surface; the work runs as hand-written CUDA kernels sequenced by the C-ABI program runtime in
+`_lib/libaf_cuda.so`. There is no CPU fallback: without a CUDA device the runtime raises.
+"""
+from . import llm  # noqa: F401
+from .llm import LlamaConfig, LayerSpec, LlamaPrefill, from_pretrained, rope_tables  # noqa: F401
+
+load_llm = from_pretrained
+
+__all__ = ["llm", "LlamaConfig", "LayerSpec", "LlamaPrefill", "load_llm", "from_pretrained", "rope_tables"]

@@ -1,0 +1,87 @@
+// Shared device helpers for the B200 (sm_100a) decode/prefill kernels.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define AF_DEV __device__ __forceinline__
+
+// Error codes a kernel may record in the program's device error word (first error wins).
+enum AfDevErr : int {
+  AF_DEV_OK = 0,
+  AF_DEV_BAD_TOKEN = 1,     // embedding index outside [0, vocab)
+  AF_DEV_BAD_POS = 2,       // decode position outside [0, max_len)
+  AF_DEV_WAIT_TIMEOUT = 3,  // a bounded spin-wait gave up
+};
+
+AF_DEV void af_set_err(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+// Programmatic dependent launch (sm_90+): wait for the preceding grid's memory to be visible /
+// allow the next grid in the stream to start its prologue.
+AF_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+AF_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// 16-byte streaming load that bypasses L1 (weights are read once per decode step).
+AF_DEV uint4 ldg_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+
+// Activations written by the preceding kernel. With programmatic dependent launch a kernel starts
+// while its producer is still writing, so its data must not come through the non-coherent
+// (read-only) path, whose L1 lines may predate the producer's stores: load at L2 (.cg) instead.
+AF_DEV uint4 ld_act_v4(const void* p) {
+  return __ldcg(reinterpret_cast<const uint4*>(p));
+}
+
+// Four signed int8 lanes of `w` -> four exact floats. Each byte b is biased to b+128, placed in
+// the low mantissa byte of 2^23 (0x4B000000) with a byte permute, and the bias 2^23+128 is
+// subtracted: exact for every int8 value, two integer/float ops per element and no I2F.
+AF_DEV void i8x4_to_f32(uint32_t w, float& f0, float& f1, float& f2, float& f3) {
+  const uint32_t u = w ^ 0x80808080u;
+  const float bias = 8388736.0f;  // 2^23 + 128
+  f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - bias;
+  f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - bias;
+  f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - bias;
+  f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - bias;
+}
+
+// Eight unsigned 4-bit codes (low nibble first) minus 8 -> eight exact floats.
+AF_DEV void u4x8_to_f32(uint32_t w, float* f) {
+  // nibble k of w holds code for element k; value = code - 8
+#pragma unroll
+  for (int k = 0; k < 8; ++k) f[k] = (float)((int)((w >> (4 * k)) & 0xFu) - 8);
+}
+
+AF_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+AF_DEV float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+AF_DEV float h2f(__half h) { return __half2float(h); }
+AF_DEV __half f2h(float f) { return __float2half_rn(f); }
+AF_DEV float round_f16(float f) { return __half2float(__float2half_rn(f)); }
+
+// Eight fp16 packed in a uint4 -> floats.
+AF_DEV void h8_to_f32(const uint4& v, float* f) {
+  const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __half22float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+AF_DEV float silu_f(float g) { return g / (1.0f + expf(-g)); }

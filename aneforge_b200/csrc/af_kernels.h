@@ -1,0 +1,104 @@
+// Internal C++ interface between the program runtime and the sm_100a kernels.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace af {
+
+enum WFormat : int { W_I8 = 0, W_F16 = 1, W_I4G32 = 2 };
+enum Epilogue : int { EPI_F32 = 0, EPI_F16 = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
+
+struct GemvArgs {
+  int wf = W_I8, epi = EPI_F32;
+  const __half* x = nullptr;   // [NB][ldx] fp16
+  int ldx = 0;
+  const void* w = nullptr;     // codes / fp16 weights, [N] rows
+  const __half* scale = nullptr;   // int8: [N] per-row scale
+  const __half* gscale = nullptr;  // int4: [N][K/32] group scales
+  const __half* bias = nullptr;    // [N] or null
+  void* y = nullptr;           // output (see Epilogue); ARGMAX: optional fp32 logits
+  int ldy = 0;
+  int N = 0, K = 0, NB = 1;
+  int tg = 256;                // set by the dispatcher
+  // ARGMAX scratch: [ctas][NB] partials + one launch counter (must start at 0; reset by the kernel)
+  float* am_val = nullptr;
+  int* am_idx = nullptr;
+  int* am_count = nullptr;
+  int am_grid_cap = 0;         // partial slots available (0 = unchecked)
+  int* tok_out = nullptr;      // [NB] greedy token
+  int* pos_adv = nullptr;      // [NB] decode position, advanced by one when non-null
+  int* hist = nullptr;         // [NB][hist_ld] token history: hist[b][pos[b]] = token (needs pos_adv)
+  int hist_ld = 0;
+};
+
+cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t st, bool pdl);
+int gemv_argmax_ctas(int wf, int N, int K, int NB);
+void gemv_argmax_scratch(int wf, int N, int K, int NB, size_t* slot_floats, size_t* counters);
+
+// Per-row int8 quantizer, bit-exact to the reference's numpy `quantize_per_row`.
+// src: [N][K] fp32 (src_f16 = 0) or fp16 (src_f16 = 1); codes [N][K] int8; scales [N] fp16.
+cudaError_t quantize_rows_i8(const void* src, int src_f16, int N, int K, int8_t* codes, __half* scales,
+                             cudaStream_t st);
+// Group-32 int4 quantizer (this build's format): packed [N][K/2] bytes, scales [N][K/32] fp16.
+cudaError_t quantize_g32_i4(const void* src, int src_f16, int N, int K, uint8_t* packed, __half* scales,
+                            cudaStream_t st);
+
+// out[b] = f16( x[b] / max(||x[b]||_2, floor) * g )  (the reference's RMSNorm lowering)
+cudaError_t rmsnorm_launch(const void* x, int x_f16, int ldx, const __half* g, float floor, __half* out,
+                           int ldo, int NB, int D, cudaStream_t st, bool pdl);
+
+// h[b][:] = f32(table[tok[b]][:]); records AF_DEV_BAD_TOKEN and writes zeros on an out-of-range id.
+cudaError_t embed_launch(const int* tok, const __half* table, int vocab, float* h, int ldh, int NB, int D,
+                         int* err, cudaStream_t st, bool pdl);
+
+// elementwise dtype conversion: mode 0 fp16 -> fp32, mode 1 fp32 -> fp16
+cudaError_t cast_launch(const void* src, void* dst, size_t n, int mode, cudaStream_t st, bool pdl);
+
+struct AttnDecodeArgs {
+  const float* qkv = nullptr;  // [NB][ld_qkv] fp32: q (H*dh) | k (KV*dh) | v (KV*dh)
+  int ld_qkv = 0;
+  __half* kc = nullptr;        // [NB][KV][M][dh]
+  __half* vc = nullptr;
+  const int* pos = nullptr;    // [NB]
+  const __half* cos_t = nullptr;  // [M][dh] (null: no RoPE)
+  const __half* sin_t = nullptr;
+  const __half* qn_g = nullptr;   // optional per-head RMSNorm (QK-norm) g_eff [dh]
+  const __half* kn_g = nullptr;
+  float qn_floor = 0.f, kn_floor = 0.f;
+  __half* out = nullptr;       // [NB][ld_out] fp16, head-major (h*dh + d)
+  int ld_out = 0;
+  float* part = nullptr;       // scratch [NB][KV][n_split][G][dh + 2]
+  int* counters = nullptr;     // scratch [NB][KV], zero at first launch, reset by the kernel
+  int* err = nullptr;
+  int NB = 1, H = 0, KV = 0, dh = 0, M = 0, n_split = 1;
+  float scale = 0.f;           // fp16-rounded 1/sqrt(dh)
+  float kv_c = 1.f;            // GQA expansion factor (applied as f16(c * f16(k)))
+  int expand = 0;
+};
+cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st, bool pdl);
+size_t attn_decode_scratch_floats(int NB, int KV, int n_split, int G, int dh);
+
+// Prefill causal attention over S prompt rows (CUDA-core flash form, fp16 q/K/V operands).
+struct AttnPrefillArgs {
+  const float* qkv = nullptr;  // [S][ld_qkv] fp32 (q | k | v), bias included
+  int ld_qkv = 0;
+  const __half* cos_t = nullptr;
+  const __half* sin_t = nullptr;
+  const __half* qn_g = nullptr;
+  const __half* kn_g = nullptr;
+  float qn_floor = 0.f, kn_floor = 0.f;
+  __half* kc = nullptr;        // [KV][ldm][dh]: roped K written at rows 0..S-1 (cache layout)
+  __half* vc = nullptr;
+  int ldm = 0;
+  __half* out = nullptr;       // [S][H*dh]
+  int S = 0, H = 0, KV = 0, dh = 0;
+  float scale = 0.f, kv_c = 1.f;
+  int expand = 0;
+};
+// rope q (-> qbuf [H][S][dh] fp16) and k, write roped K / raw V into cache rows 0..S-1
+cudaError_t rope_kv_prefill_launch(const AttnPrefillArgs& a, __half* qbuf, cudaStream_t st);
+// causal attention of the staged q rows against cache rows 0..i
+cudaError_t attn_prefill_with_q(const AttnPrefillArgs& a, const __half* qbuf, cudaStream_t st);
+
+}  // namespace af

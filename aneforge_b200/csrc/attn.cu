@@ -1,0 +1,392 @@
+// GQA attention over the resident fp16 KV cache.
+//
+// K5 decode (one new token per sequence): one CTA per (split, kv head, sequence). The CTA
+//   1. takes the G = H/KV query heads of its kv head from the fused QKV output, applies the optional
+//      per-head RMSNorm (QK-norm) and RoPE (neox half split: the partner of lane l is lane l^16), and
+//      rounds q to fp16 (the bmm operand);
+//   2. if its key range holds `pos`, ropes the new k, writes k and v into the cache slot `pos`
+//      (the reference's `Kin*inv + k*oh` write of llm.py:232, without touching the other M-1 slots);
+//   3. runs an online softmax over its keys (split-K / flash-decode), each key expanded as the
+//      reference's 0/1 GQA matmul does (f16(c * k), c = 1 without expansion, llm.py:205-211);
+//   4. writes (m, l, acc) partials to scratch; the last CTA of the (sequence, kv head) to finish
+//      (atomic ticket) merges the splits and writes the fp16 head outputs.
+// Keys after `pos` carry the reference's additive -1e4 mask, whose exp underflows to exactly 0 in
+// fp32, so they are skipped. Probabilities stay fp32.
+//
+// Prefill (S prompt rows): rope_kv_prefill ropes q/k for every row, writes the roped K and raw V
+// straight into cache rows 0..S-1 (the decode layout, so no seeding copy), and attn_prefill runs a
+// causal online softmax with one warp per query row.
+#include "af_common.cuh"
+#include "af_kernels.h"
+
+namespace af {
+
+template <int DH>
+struct HeadLayout {
+  static constexpr int EPL = DH >= 32 ? DH / 32 : 1;   // elements per lane
+  static constexpr int LANES = DH >= 32 ? 32 : DH;     // lanes holding the head vector
+  static constexpr int PARTNER = LANES / 2;            // xor distance of the rotate-half partner
+};
+
+// One head vector held as EPL contiguous elements per lane: optional RMSNorm, RoPE at row `p`.
+template <int DH>
+AF_DEV void norm_rope_head(float (&v)[HeadLayout<DH>::EPL], int lane, const __half* ng, float nfloor,
+                           const __half* cos_t, const __half* sin_t, int p) {
+  using HL = HeadLayout<DH>;
+  const bool active = lane < HL::LANES;
+  if (ng) {
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < HL::EPL; ++e) ss = fmaf(v[e], v[e], ss);
+    ss = active ? ss : 0.f;
+    ss = warp_sum(ss);
+    const float sn = fmaxf(sqrtf(ss), nfloor);
+#pragma unroll
+    for (int e = 0; e < HL::EPL; ++e) {
+      const int d = lane * HL::EPL + e;
+      v[e] = active ? __fmul_rn(__fdiv_rn(v[e], sn), h2f(ng[d])) : 0.f;
+    }
+  }
+  if (cos_t) {
+#pragma unroll
+    for (int e = 0; e < HL::EPL; ++e) {
+      const float other = __shfl_xor_sync(0xffffffffu, v[e], HL::PARTNER);
+      if (active) {
+        const int d = lane * HL::EPL + e;
+        const float rot = d < DH / 2 ? -other : other;
+        const float c = h2f(cos_t[(size_t)p * DH + d]), s = h2f(sin_t[(size_t)p * DH + d]);
+        v[e] = __fadd_rn(__fmul_rn(v[e], c), __fmul_rn(rot, s));
+      }
+    }
+  }
+}
+
+template <int DH>
+AF_DEV void load_row_f16(const __half* p, int lane, float (&f)[HeadLayout<DH>::EPL]) {
+  using HL = HeadLayout<DH>;
+  if (lane >= HL::LANES) {
+#pragma unroll
+    for (int e = 0; e < HL::EPL; ++e) f[e] = 0.f;
+    return;
+  }
+  const __half* q = p + lane * HL::EPL;
+  if constexpr (HL::EPL == 4) {
+    const uint2 u = __ldcg(reinterpret_cast<const uint2*>(q));
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+    const float2 x = __half22float2(h[0]), y = __half22float2(h[1]);
+    f[0] = x.x; f[1] = x.y; f[2] = y.x; f[3] = y.y;
+  } else if constexpr (HL::EPL == 2) {
+    const float2 x = __half22float2(__ldcg(reinterpret_cast<const __half2*>(q)));
+    f[0] = x.x; f[1] = x.y;
+  } else {
+#pragma unroll
+    for (int e = 0; e < HL::EPL; ++e) f[e] = h2f(__ldcg(q + e));
+  }
+}
+
+template <int DH, int G>
+__global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
+  using HL = HeadLayout<DH>;
+  constexpr int EPL = HL::EPL;
+  constexpr int NW = 4;
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool active = lane < HL::LANES;
+
+  __shared__ float q_s[G][DH];
+  __shared__ float kn_s[DH], vn_s[DH];
+  __shared__ float wm[NW][G], wl[NW][G];
+  __shared__ float wacc[NW][G][DH];
+  __shared__ int last_s;
+
+  pdl_wait();
+  const int pos = __ldcg(a.pos + b);
+  if (pos < 0 || pos >= a.M) {
+    if (threadIdx.x == 0 && split == 0 && kvh == 0) af_set_err(a.err, AF_DEV_BAD_POS);
+    return;
+  }
+  const int len = (pos + a.n_split) / a.n_split;      // ceil((pos + 1) / n_split)
+  const int j0 = split * len;
+  const int j1 = min(j0 + len, pos + 1);
+  const bool owns_pos = j0 <= pos && pos < j1;
+  const float* qkv = a.qkv + (size_t)b * a.ld_qkv;
+  const int H = a.H, KV = a.KV;
+
+  // ---- q heads (and the new k/v in the CTA that owns pos)
+  for (int g = warp; g < G; g += NW) {
+    float v[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) v[e] = active ? __ldcg(qkv + (size_t)(kvh * G + g) * DH + lane * EPL + e) : 0.f;
+    norm_rope_head<DH>(v, lane, a.qn_g, a.qn_floor, a.cos_t, a.sin_t, pos);
+    if (active)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) q_s[g][lane * EPL + e] = round_f16(v[e]);
+  }
+  if (owns_pos && warp == NW - 1) {
+    float k[EPL], vv[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      k[e] = active ? __ldcg(qkv + (size_t)H * DH + (size_t)kvh * DH + lane * EPL + e) : 0.f;
+      vv[e] = active ? __ldcg(qkv + (size_t)(H + KV) * DH + (size_t)kvh * DH + lane * EPL + e) : 0.f;
+    }
+    norm_rope_head<DH>(k, lane, a.kn_g, a.kn_floor, a.cos_t, a.sin_t, pos);
+    const size_t slot = (((size_t)b * KV + kvh) * a.M + pos) * DH;
+    if (active)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        const __half kh = f2h(k[e]), vh = f2h(vv[e]);
+        a.kc[slot + lane * EPL + e] = kh;
+        a.vc[slot + lane * EPL + e] = vh;
+        kn_s[lane * EPL + e] = h2f(kh);
+        vn_s[lane * EPL + e] = h2f(vh);
+      }
+  }
+  __syncthreads();
+  pdl_trigger();
+
+  float qr[G][EPL];
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) qr[g][e] = active ? q_s[g][lane * EPL + e] : 0.f;
+
+  float m[G], l[G], acc[G][EPL];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY; l[g] = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[g][e] = 0.f;
+  }
+  const __half* kbase = a.kc + ((size_t)b * KV + kvh) * a.M * DH;
+  const __half* vbase = a.vc + ((size_t)b * KV + kvh) * a.M * DH;
+  const float c = a.kv_c;
+  for (int j = j0 + warp; j < j1; j += NW) {
+    float kf[EPL], vf[EPL];
+    if (j == pos) {
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        kf[e] = active ? kn_s[lane * EPL + e] : 0.f;
+        vf[e] = active ? vn_s[lane * EPL + e] : 0.f;
+      }
+    } else {
+      load_row_f16<DH>(kbase + (size_t)j * DH, lane, kf);
+      load_row_f16<DH>(vbase + (size_t)j * DH, lane, vf);
+    }
+    if (a.expand) {
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) { kf[e] = round_f16(c * kf[e]); vf[e] = round_f16(c * vf[e]); }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) s = fmaf(qr[g][e], kf[e], s);
+      s = warp_sum(s) * a.scale;
+      const float mn = fmaxf(m[g], s);
+      const float corr = expf(m[g] - mn);
+      const float p = expf(s - mn);
+      l[g] = l[g] * corr + p;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) acc[g][e] = fmaf(p, vf[e], acc[g][e] * corr);
+      m[g] = mn;
+    }
+  }
+  // ---- merge the warps of this CTA
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    if (lane == 0) { wm[warp][g] = m[g]; wl[warp][g] = l[g]; }
+    if (active)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) wacc[warp][g][lane * EPL + e] = acc[g][e];
+  }
+  __syncthreads();
+  const size_t pair = (size_t)b * KV + kvh;
+  float* part = a.part + (pair * a.n_split + split) * G * (DH + 2);
+  for (int i = threadIdx.x; i < G * DH; i += blockDim.x) {
+    const int g = i / DH, d = i - g * DH;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][g]);
+    float num = 0.f, den = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        const float f = expf(wm[w][g] - M);
+        num = fmaf(f, wacc[w][g][d], num);
+        den = fmaf(f, wl[w][g], den);
+      }
+    }
+    if (a.n_split == 1) {
+      a.out[(size_t)b * a.ld_out + (size_t)(kvh * G + g) * DH + d] = f2h(num / den);
+    } else {
+      part[g * (DH + 2) + d] = num;
+      if (d == 0) { part[g * (DH + 2) + DH] = M; part[g * (DH + 2) + DH + 1] = den; }
+    }
+  }
+  if (a.n_split == 1) return;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last_s = atomicAdd(a.counters + pair, 1) == a.n_split - 1;
+  __syncthreads();
+  if (!last_s) return;
+  __threadfence();
+  const float* pp = a.part + pair * a.n_split * G * (DH + 2);
+  for (int i = threadIdx.x; i < G * DH; i += blockDim.x) {
+    const int g = i / DH, d = i - g * DH;
+    float M = -INFINITY;
+    for (int s = 0; s < a.n_split; ++s) M = fmaxf(M, __ldcg(pp + (s * G + g) * (DH + 2) + DH));
+    float num = 0.f, den = 0.f;
+    for (int s = 0; s < a.n_split; ++s) {
+      const float* q = pp + (s * G + g) * (DH + 2);
+      const float ms = __ldcg(q + DH);
+      if (ms == -INFINITY) continue;
+      const float f = expf(ms - M);
+      num = fmaf(f, __ldcg(q + d), num);
+      den = fmaf(f, __ldcg(q + DH + 1), den);
+    }
+    a.out[(size_t)b * a.ld_out + (size_t)(kvh * G + g) * DH + d] = f2h(num / den);
+  }
+  if (threadIdx.x == 0) a.counters[pair] = 0;
+}
+
+size_t attn_decode_scratch_floats(int NB, int KV, int n_split, int G, int dh) {
+  return (size_t)NB * KV * n_split * G * (dh + 2);
+}
+
+template <int DH, int G>
+static cudaError_t launch_decode(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.n_split, a.KV, a.NB);
+  cfg.blockDim = dim3(128);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, attn_decode_kernel<DH, G>, a);
+}
+
+template <int DH>
+static cudaError_t decode_g(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
+  switch (a.H / a.KV) {
+    case 1: return launch_decode<DH, 1>(a, st, pdl);
+    case 2: return launch_decode<DH, 2>(a, st, pdl);
+    case 4: return launch_decode<DH, 4>(a, st, pdl);
+    case 8: return launch_decode<DH, 8>(a, st, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
+  if (a.KV <= 0 || a.H % a.KV || a.n_split < 1) return cudaErrorInvalidValue;
+  if (a.n_split > 1 && (!a.part || !a.counters)) return cudaErrorInvalidValue;
+  switch (a.dh) {
+    case 16: return decode_g<16>(a, st, pdl);
+    case 32: return decode_g<32>(a, st, pdl);
+    case 64: return decode_g<64>(a, st, pdl);
+    case 128: return decode_g<128>(a, st, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// ----------------------------------------------------------------------------------- prefill
+
+// grid (S, H + KV): block y < H ropes query head y of row x into qbuf [H][S][DH]; the others rope
+// key head (y - H) and write K (roped) and V into cache rows.
+template <int DH>
+__global__ void __launch_bounds__(32) rope_kv_prefill_kernel(AttnPrefillArgs a, __half* qbuf) {
+  using HL = HeadLayout<DH>;
+  constexpr int EPL = HL::EPL;
+  const int s = blockIdx.x, y = blockIdx.y, lane = threadIdx.x;
+  const bool active = lane < HL::LANES;
+  const float* row = a.qkv + (size_t)s * a.ld_qkv;
+  float v[EPL];
+  if (y < a.H) {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) v[e] = active ? row[(size_t)y * DH + lane * EPL + e] : 0.f;
+    norm_rope_head<DH>(v, lane, a.qn_g, a.qn_floor, a.cos_t, a.sin_t, s);
+    if (active)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) qbuf[((size_t)y * a.S + s) * DH + lane * EPL + e] = f2h(v[e]);
+  } else {
+    const int kvh = y - a.H;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) v[e] = active ? row[(size_t)(a.H + kvh) * DH + lane * EPL + e] : 0.f;
+    norm_rope_head<DH>(v, lane, a.kn_g, a.kn_floor, a.cos_t, a.sin_t, s);
+    if (active)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        const size_t o = ((size_t)kvh * a.ldm + s) * DH + lane * EPL + e;
+        a.kc[o] = f2h(v[e]);
+        a.vc[o] = f2h(row[(size_t)(a.H + a.KV + kvh) * DH + lane * EPL + e]);
+      }
+  }
+}
+
+// grid (H, ceil(S/4)), 4 warps: warp w handles query row i = blockIdx.y*4 + w over keys 0..i.
+template <int DH>
+__global__ void __launch_bounds__(128) attn_prefill_kernel(AttnPrefillArgs a, const __half* qbuf) {
+  using HL = HeadLayout<DH>;
+  constexpr int EPL = HL::EPL;
+  const int h = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = blockIdx.y * 4 + warp;
+  if (i >= a.S) return;
+  const int G = a.H / a.KV, kvh = h / G;
+  float q[EPL];
+  load_row_f16<DH>(qbuf + ((size_t)h * a.S + i) * DH, lane, q);
+  const __half* kb = a.kc + (size_t)kvh * a.ldm * DH;
+  const __half* vb = a.vc + (size_t)kvh * a.ldm * DH;
+  float m = -INFINITY, l = 0.f, acc[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
+  for (int j = 0; j <= i; ++j) {
+    float kf[EPL], vf[EPL];
+    load_row_f16<DH>(kb + (size_t)j * DH, lane, kf);
+    load_row_f16<DH>(vb + (size_t)j * DH, lane, vf);
+    if (a.expand) {
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) { kf[e] = round_f16(a.kv_c * kf[e]); vf[e] = round_f16(a.kv_c * vf[e]); }
+    }
+    float sc = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) sc = fmaf(q[e], kf[e], sc);
+    sc = warp_sum(sc) * a.scale;
+    const float mn = fmaxf(m, sc);
+    const float corr = expf(m - mn), p = expf(sc - mn);
+    l = l * corr + p;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[e] = fmaf(p, vf[e], acc[e] * corr);
+    m = mn;
+  }
+  if (lane < HL::LANES)
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) a.out[(size_t)i * a.H * DH + (size_t)h * DH + lane * EPL + e] = f2h(acc[e] / l);
+}
+
+cudaError_t rope_kv_prefill_launch(const AttnPrefillArgs& a, __half* qbuf, cudaStream_t st) {
+  if (a.S <= 0 || a.KV <= 0 || a.H % a.KV) return cudaErrorInvalidValue;
+  dim3 grid(a.S, a.H + a.KV);
+  switch (a.dh) {
+    case 16: rope_kv_prefill_kernel<16><<<grid, 32, 0, st>>>(a, qbuf); break;
+    case 32: rope_kv_prefill_kernel<32><<<grid, 32, 0, st>>>(a, qbuf); break;
+    case 64: rope_kv_prefill_kernel<64><<<grid, 32, 0, st>>>(a, qbuf); break;
+    case 128: rope_kv_prefill_kernel<128><<<grid, 32, 0, st>>>(a, qbuf); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t attn_prefill_with_q(const AttnPrefillArgs& a, const __half* qbuf, cudaStream_t st) {
+  dim3 grid(a.H, (a.S + 3) / 4);
+  switch (a.dh) {
+    case 16: attn_prefill_kernel<16><<<grid, 128, 0, st>>>(a, qbuf); break;
+    case 32: attn_prefill_kernel<32><<<grid, 128, 0, st>>>(a, qbuf); break;
+    case 64: attn_prefill_kernel<64><<<grid, 128, 0, st>>>(a, qbuf); break;
+    case 128: attn_prefill_kernel<128><<<grid, 128, 0, st>>>(a, qbuf); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace af

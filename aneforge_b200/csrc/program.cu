@@ -1,0 +1,769 @@
+// The CUDA invoker: a "program" is a lowered plan of fused sm_100a kernel launches over named
+// device buffers (ports, resident state, weights, activations, scratch), replayed as one CUDA graph
+// with programmatic dependent launch between kernels. It replaces the reference's e5rt program
+// (aneforge/_lib/ane_e5rt_dispatch.mm): same port model (named fp16 ports, zero-initialised,
+// zero-copy buffer pointers, output->input aliasing for resident state, synchronous execute whose
+// first call finalises the program), with device memory instead of shared ANE buffers.
+//
+// Plan text (one statement per line, '#' comments):
+//   AFPLAN 1
+//   buf <name> <bytes> <role>          role: in | out | state | tmp | weight | scratch
+//   wfile <name> <offset>              load a weight buffer from <plan dir>/weights.bin
+//   op <kind> key=value ...            buffer refs are `name`, `name@byte_offset`, or `-` (null)
+#include <climits>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <map>
+#include <mutex>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "af_common.cuh"
+#include "af_kernels.h"
+#include "../../include/af_cuda.h"
+
+namespace af {
+
+static thread_local std::string g_last_error;
+
+static void set_error(const std::string& msg) {
+  g_last_error = msg;
+  fprintf(stderr, "[aneforge_b200] %s\n", msg.c_str());
+}
+
+void set_error_public(const std::string& msg) { set_error(msg); }
+
+enum Role { R_IN, R_OUT, R_STATE, R_TMP, R_WEIGHT, R_SCRATCH };
+
+struct Buffer {
+  std::string name;
+  size_t bytes = 0;
+  Role role = R_TMP;
+  void* dev = nullptr;
+  bool owned = false;
+  bool ready = false;          // weights: uploaded/bound/loaded
+  long long file_off = -1;
+  int alias_of = -1;           // share_buffer: this input reads buffer `alias_of`
+};
+
+struct Op {
+  std::string kind;
+  std::map<std::string, std::string> kv;
+  int line = 0;
+};
+
+struct Program {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::vector<Buffer> bufs;
+  std::map<std::string, int> idx;
+  std::vector<Op> ops;
+  std::string dir;
+  bool finalized = false;
+  bool use_graph = true;
+  bool use_pdl = true;
+  cudaGraphExec_t exec = nullptr;
+  int* d_err = nullptr;
+};
+
+// ------------------------------------------------------------------------------------ helpers
+
+static bool parse_role(const std::string& s, Role& r) {
+  if (s == "in") r = R_IN;
+  else if (s == "out") r = R_OUT;
+  else if (s == "state") r = R_STATE;
+  else if (s == "tmp") r = R_TMP;
+  else if (s == "weight") r = R_WEIGHT;
+  else if (s == "scratch") r = R_SCRATCH;
+  else return false;
+  return true;
+}
+
+static int find_buf(Program& p, const std::string& name) {
+  auto it = p.idx.find(name);
+  return it == p.idx.end() ? -1 : it->second;
+}
+
+struct OpCtx {
+  Program& p;
+  const Op& op;
+  std::string err;
+  bool has(const char* k) const { return op.kv.count(k) && op.kv.at(k) != "-"; }
+  const std::string* raw(const char* k) {
+    auto it = op.kv.find(k);
+    if (it == op.kv.end()) { err = std::string("missing key '") + k + "'"; return nullptr; }
+    return &it->second;
+  }
+  long long i(const char* k, long long dflt = LLONG_MIN) {
+    auto it = op.kv.find(k);
+    if (it == op.kv.end()) {
+      if (dflt == LLONG_MIN) err = std::string("missing int '") + k + "'";
+      return dflt == LLONG_MIN ? 0 : dflt;
+    }
+    return strtoll(it->second.c_str(), nullptr, 10);
+  }
+  double f(const char* k, double dflt = NAN) {
+    auto it = op.kv.find(k);
+    if (it == op.kv.end()) {
+      if (std::isnan(dflt)) err = std::string("missing float '") + k + "'";
+      return std::isnan(dflt) ? 0.0 : dflt;
+    }
+    return strtod(it->second.c_str(), nullptr);
+  }
+  // buffer reference with optional byte offset; `need` bytes must fit
+  void* ptr(const char* k, size_t need = 0, bool optional = false) {
+    auto it = op.kv.find(k);
+    if (it == op.kv.end() || it->second == "-") {
+      if (!optional) err = std::string("missing buffer '") + k + "'";
+      return nullptr;
+    }
+    std::string s = it->second;
+    size_t off = 0;
+    auto at = s.find('@');
+    if (at != std::string::npos) {
+      off = strtoull(s.c_str() + at + 1, nullptr, 10);
+      s = s.substr(0, at);
+    }
+    int bi = find_buf(p, s);
+    if (bi < 0) { err = "unknown buffer '" + s + "'"; return nullptr; }
+    int root = bi;
+    while (p.bufs[root].alias_of >= 0) root = p.bufs[root].alias_of;
+    if (off + need > p.bufs[root].bytes) {
+      err = "buffer '" + s + "' too small for key '" + k + "' (" + std::to_string(off + need) + " > " +
+            std::to_string(p.bufs[root].bytes) + ")";
+      return nullptr;
+    }
+    return static_cast<char*>(p.bufs[root].dev) + off;
+  }
+};
+
+static int wf_of(const std::string& s) {
+  if (s == "i8") return W_I8;
+  if (s == "f16") return W_F16;
+  if (s == "i4") return W_I4G32;
+  return -1;
+}
+static int epi_of(const std::string& s) {
+  if (s == "f32") return EPI_F32;
+  if (s == "f16") return EPI_F16;
+  if (s == "resid") return EPI_RESID;
+  if (s == "swiglu") return EPI_SWIGLU;
+  if (s == "argmax") return EPI_ARGMAX;
+  return -1;
+}
+
+// ------------------------------------------------------------------------------------ op launchers
+
+static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) {
+  OpCtx c{p, op, {}};
+  cudaStream_t st = p.stream;
+  const bool pdl = p.use_pdl;
+  cudaError_t e = cudaSuccess;
+  if (op.kind == "embed") {
+    const int nb = c.i("nb"), d = c.i("d"), vocab = c.i("vocab"), ldh = c.i("ldh", d);
+    const int* tok = (const int*)c.ptr("tok", 4 * (size_t)nb);
+    const __half* table = (const __half*)c.ptr("table", 2 * (size_t)vocab * d);
+    float* h = (float*)c.ptr("h", 4 * ((size_t)(nb - 1) * ldh + d));
+    if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+    if (!dry) e = embed_launch(tok, table, vocab, h, ldh, nb, d, p.d_err, st, pdl);
+  } else if (op.kind == "rmsnorm") {
+    const int nb = c.i("nb"), d = c.i("d"), xf16 = c.i("xf16", 0);
+    const int ldx = c.i("ldx", d), ldo = c.i("ldo", d);
+    const void* x = c.ptr("x", (xf16 ? 2 : 4) * ((size_t)(nb - 1) * ldx + d));
+    const __half* g = (const __half*)c.ptr("g", 2 * (size_t)d);
+    __half* out = (__half*)c.ptr("out", 2 * ((size_t)(nb - 1) * ldo + d));
+    const float floor = (float)c.f("floor");
+    if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+    if (!dry) e = rmsnorm_launch(x, xf16, ldx, g, floor, out, ldo, nb, d, st, pdl);
+  } else if (op.kind == "gemv") {
+    GemvArgs a;
+    const std::string* wfs = c.raw("wf");
+    const std::string* eps = c.raw("epi");
+    if (!wfs || !eps) { why = c.err; return cudaErrorInvalidValue; }
+    a.wf = wf_of(*wfs);
+    a.epi = epi_of(*eps);
+    if (a.wf < 0 || a.epi < 0) { why = "bad wf/epi"; return cudaErrorInvalidValue; }
+    a.NB = c.i("nb"); a.N = c.i("n"); a.K = c.i("k");
+    a.ldx = c.i("ldx", a.K);
+    const int out_cols = a.epi == EPI_SWIGLU ? a.N / 2 : a.N;
+    a.ldy = c.i("ldy", out_cols);
+    a.x = (const __half*)c.ptr("x", 2 * ((size_t)(a.NB - 1) * a.ldx + a.K));
+    const size_t wbytes = a.wf == W_I8 ? (size_t)a.N * a.K : a.wf == W_F16 ? (size_t)a.N * a.K * 2 : (size_t)a.N * a.K / 2;
+    a.w = c.ptr("w", wbytes);
+    if (a.wf == W_I8) a.scale = (const __half*)c.ptr("s", 2 * (size_t)a.N);
+    if (a.wf == W_I4G32) a.gscale = (const __half*)c.ptr("gs", 2 * (size_t)a.N * (a.K / 32));
+    a.bias = (const __half*)c.ptr("bias", 2 * (size_t)a.N, true);
+    const size_t esz = (a.epi == EPI_F16 || a.epi == EPI_SWIGLU) ? 2 : 4;
+    a.y = c.ptr("y", esz * ((size_t)(a.NB - 1) * a.ldy + out_cols), a.epi == EPI_ARGMAX);
+    if (a.epi == EPI_ARGMAX) {
+      size_t slots = 0, counters = 0;
+      gemv_argmax_scratch(a.wf, a.N, a.K, a.NB, &slots, &counters);
+      a.am_val = (float*)c.ptr("amv", 4 * slots);
+      a.am_idx = (int*)c.ptr("ami", 4 * slots);
+      a.am_count = (int*)c.ptr("amc", 4 * counters);
+      const int ctas = gemv_argmax_ctas(a.wf, a.N, a.K, a.NB);
+      a.tok_out = (int*)c.ptr("tok", 4 * (size_t)a.NB);
+      a.pos_adv = (int*)c.ptr("pos", 4 * (size_t)a.NB, true);
+      a.hist_ld = (int)c.i("histld", 0);
+      a.hist = (int*)c.ptr("hist", 4 * (size_t)a.NB * a.hist_ld, true);
+      if (a.hist && !a.pos_adv) c.err = "hist needs pos";
+      a.am_grid_cap = ctas;
+    }
+    if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+    if (!dry) e = gemv_launch(a, st, pdl);
+  } else if (op.kind == "attn_decode") {
+    AttnDecodeArgs a;
+    a.NB = c.i("nb"); a.H = c.i("h"); a.KV = c.i("kv"); a.dh = c.i("dh"); a.M = c.i("m");
+    a.n_split = c.i("nsplit", 1);
+    a.ld_qkv = c.i("ldqkv", (a.H + 2 * a.KV) * a.dh);
+    a.ld_out = c.i("ldo", a.H * a.dh);
+    const size_t cache = 2 * (size_t)a.NB * a.KV * a.M * a.dh;
+    a.qkv = (const float*)c.ptr("qkv", 4 * ((size_t)(a.NB - 1) * a.ld_qkv + (a.H + 2 * a.KV) * a.dh));
+    a.kc = (__half*)c.ptr("kc", cache);
+    a.vc = (__half*)c.ptr("vc", cache);
+    a.pos = (const int*)c.ptr("pos", 4 * (size_t)a.NB);
+    a.cos_t = (const __half*)c.ptr("cos", 2 * (size_t)a.M * a.dh, true);
+    a.sin_t = (const __half*)c.ptr("sin", 2 * (size_t)a.M * a.dh, true);
+    a.qn_g = (const __half*)c.ptr("qn", 2 * (size_t)a.dh, true);
+    a.kn_g = (const __half*)c.ptr("kn", 2 * (size_t)a.dh, true);
+    a.qn_floor = (float)c.f("qnf", 0.0);
+    a.kn_floor = (float)c.f("knf", 0.0);
+    a.out = (__half*)c.ptr("out", 2 * ((size_t)(a.NB - 1) * a.ld_out + a.H * a.dh));
+    if (a.n_split > 1) {
+      a.part = (float*)c.ptr("part", 4 * attn_decode_scratch_floats(a.NB, a.KV, a.n_split, a.H / a.KV, a.dh));
+      a.counters = (int*)c.ptr("cnt", 4 * (size_t)a.NB * a.KV);
+    }
+    a.scale = (float)c.f("scale");
+    a.kv_c = (float)c.f("kvc", 1.0);
+    a.expand = c.i("expand", 0);
+    a.err = p.d_err;
+    if ((a.cos_t == nullptr) != (a.sin_t == nullptr)) c.err = "cos/sin must both be given";
+    if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+    if (!dry) e = attn_decode_launch(a, st, pdl);
+  } else if (op.kind == "attn_prefill") {
+    AttnPrefillArgs a;
+    a.S = c.i("s"); a.H = c.i("h"); a.KV = c.i("kv"); a.dh = c.i("dh");
+    a.ldm = c.i("ldm", a.S);
+    a.ld_qkv = c.i("ldqkv", (a.H + 2 * a.KV) * a.dh);
+    a.qkv = (const float*)c.ptr("qkv", 4 * ((size_t)(a.S - 1) * a.ld_qkv + (a.H + 2 * a.KV) * a.dh));
+    a.kc = (__half*)c.ptr("kc", 2 * (size_t)a.KV * a.ldm * a.dh);
+    a.vc = (__half*)c.ptr("vc", 2 * (size_t)a.KV * a.ldm * a.dh);
+    a.cos_t = (const __half*)c.ptr("cos", 2 * (size_t)a.S * a.dh, true);
+    a.sin_t = (const __half*)c.ptr("sin", 2 * (size_t)a.S * a.dh, true);
+    a.qn_g = (const __half*)c.ptr("qn", 2 * (size_t)a.dh, true);
+    a.kn_g = (const __half*)c.ptr("kn", 2 * (size_t)a.dh, true);
+    a.qn_floor = (float)c.f("qnf", 0.0);
+    a.kn_floor = (float)c.f("knf", 0.0);
+    a.out = (__half*)c.ptr("out", 2 * (size_t)a.S * a.H * a.dh);
+    __half* qbuf = (__half*)c.ptr("qbuf", 2 * (size_t)a.H * a.S * a.dh);
+    a.scale = (float)c.f("scale");
+    a.kv_c = (float)c.f("kvc", 1.0);
+    a.expand = c.i("expand", 0);
+    if (a.ldm < a.S) c.err = "ldm < s";
+    if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+    if (!dry) {
+      e = rope_kv_prefill_launch(a, qbuf, st);
+      if (e == cudaSuccess) e = attn_prefill_with_q(a, qbuf, st);
+    }
+  } else if (op.kind == "cast") {
+    const size_t n = (size_t)c.i("n");
+    const int mode = (int)c.i("mode");
+    const void* src = c.ptr("src", n * (mode == 0 ? 2 : 4));
+    void* dst = c.ptr("dst", n * (mode == 0 ? 4 : 2));
+    if (mode != 0 && mode != 1) c.err = "cast mode must be 0 or 1";
+    if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+    if (!dry) e = cast_launch(src, dst, n, mode, st, pdl);
+  } else if (op.kind == "copy") {
+    const size_t bytes = (size_t)c.i("bytes");
+    void* dst = c.ptr("dst", bytes);
+    const void* src = c.ptr("src", bytes);
+    if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+    if (!dry) e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, st);
+  } else if (op.kind == "fill") {
+    const size_t bytes = (size_t)c.i("bytes");
+    void* dst = c.ptr("dst", bytes);
+    if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+    if (!dry) e = cudaMemsetAsync(dst, (int)c.i("value", 0), bytes, st);
+  } else {
+    why = "unknown op kind '" + op.kind + "'";
+    return cudaErrorInvalidValue;
+  }
+  if (e != cudaSuccess) why = std::string("launch failed: ") + cudaGetErrorString(e);
+  return e;
+}
+
+// ------------------------------------------------------------------------------------ parsing
+
+static bool parse_plan(Program& p, const std::string& text, std::string& err) {
+  std::istringstream in(text);
+  std::string line;
+  int ln = 0;
+  bool header = false;
+  while (std::getline(in, line)) {
+    ++ln;
+    auto hash = line.find('#');
+    if (hash != std::string::npos) line = line.substr(0, hash);
+    std::istringstream ls(line);
+    std::string kw;
+    if (!(ls >> kw)) continue;
+    if (!header) {
+      int ver = 0;
+      if (kw != "AFPLAN" || !(ls >> ver) || ver != 1) { err = "plan must start with 'AFPLAN 1'"; return false; }
+      header = true;
+      continue;
+    }
+    if (kw == "buf") {
+      Buffer b;
+      std::string role;
+      if (!(ls >> b.name >> b.bytes >> role) || !parse_role(role, b.role)) {
+        err = "line " + std::to_string(ln) + ": bad buf statement";
+        return false;
+      }
+      if (p.idx.count(b.name)) { err = "line " + std::to_string(ln) + ": duplicate buffer " + b.name; return false; }
+      p.idx[b.name] = (int)p.bufs.size();
+      p.bufs.push_back(b);
+    } else if (kw == "wfile") {
+      std::string name;
+      long long off;
+      if (!(ls >> name >> off) || find_buf(p, name) < 0) { err = "line " + std::to_string(ln) + ": bad wfile"; return false; }
+      p.bufs[find_buf(p, name)].file_off = off;
+    } else if (kw == "op") {
+      Op op;
+      op.line = ln;
+      if (!(ls >> op.kind)) { err = "line " + std::to_string(ln) + ": op without kind"; return false; }
+      std::string tok;
+      while (ls >> tok) {
+        auto eq = tok.find('=');
+        if (eq == std::string::npos) { err = "line " + std::to_string(ln) + ": expected key=value, got " + tok; return false; }
+        op.kv[tok.substr(0, eq)] = tok.substr(eq + 1);
+      }
+      p.ops.push_back(op);
+    } else {
+      err = "line " + std::to_string(ln) + ": unknown statement " + kw;
+      return false;
+    }
+  }
+  if (!header) { err = "empty plan"; return false; }
+  return true;
+}
+
+static bool alloc_buffers(Program& p, std::string& err) {
+  for (auto& b : p.bufs) {
+    const size_t bytes = ((b.bytes + 255) / 256) * 256;
+    if (bytes == 0) continue;
+    cudaError_t e = cudaMalloc(&b.dev, bytes);
+    if (e != cudaSuccess) { err = "cudaMalloc(" + b.name + ", " + std::to_string(bytes) + ") failed: " + cudaGetErrorString(e); return false; }
+    b.owned = true;
+    if (b.role != R_WEIGHT) {
+      cudaMemset(b.dev, 0, bytes);   // ports and state start zeroed, like the e5rt ports
+      b.ready = true;
+    }
+  }
+  cudaError_t e = cudaMalloc(&p.d_err, 256);
+  if (e != cudaSuccess) { err = "cudaMalloc(err) failed"; return false; }
+  cudaMemset(p.d_err, 0, 256);
+  return true;
+}
+
+static bool load_weight_file(Program& p, std::string& err) {
+  bool any = false;
+  for (auto& b : p.bufs) any |= b.file_off >= 0;
+  if (!any) return true;
+  std::ifstream f(p.dir + "/weights.bin", std::ios::binary);
+  if (!f) { err = "cannot open " + p.dir + "/weights.bin"; return false; }
+  std::vector<char> tmp;
+  for (auto& b : p.bufs) {
+    if (b.file_off < 0) continue;
+    tmp.resize(b.bytes);
+    f.seekg(b.file_off);
+    f.read(tmp.data(), (std::streamsize)b.bytes);
+    if (!f) { err = "short read of weight " + b.name; return false; }
+    cudaError_t e = cudaMemcpy(b.dev, tmp.data(), b.bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) { err = "upload of " + b.name + " failed"; return false; }
+    b.ready = true;
+  }
+  return true;
+}
+
+static void free_program(Program* p) {
+  if (!p) return;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(p->device);
+  if (p->stream) cudaStreamSynchronize(p->stream);
+  if (p->exec) cudaGraphExecDestroy(p->exec);
+  for (auto& b : p->bufs)
+    if (b.owned && b.dev) cudaFree(b.dev);
+  if (p->d_err) cudaFree(p->d_err);
+  if (p->stream) cudaStreamDestroy(p->stream);
+  cudaSetDevice(prev);
+  delete p;
+}
+
+static int device_from_mask(uint64_t mask) {
+  if (mask == 0) {
+    int d = 0;
+    cudaGetDevice(&d);
+    return d;
+  }
+  for (int i = 0; i < 64; ++i)
+    if (mask & (1ull << i)) return i;
+  return 0;
+}
+
+struct DeviceGuard {
+  int prev = 0;
+  explicit DeviceGuard(int d) { cudaGetDevice(&prev); cudaSetDevice(d); }
+  ~DeviceGuard() { cudaSetDevice(prev); }
+};
+
+static Program* build_program(const std::string& text, const std::string& dir, uint64_t mask) {
+  Program* p = new Program();
+  p->dir = dir;
+  p->device = device_from_mask(mask);
+  std::string err;
+  if (!parse_plan(*p, text, err)) { set_error("plan parse: " + err); delete p; return nullptr; }
+  // validate every op against the declared buffers before touching the device
+  for (auto& op : p->ops) {
+    std::string why;
+    // dry validation needs buffer sizes only; device pointers are still null
+    if (run_op(*p, op, true, why) != cudaSuccess) {
+      set_error("plan line " + std::to_string(op.line) + " (" + op.kind + "): " + why);
+      delete p;
+      return nullptr;
+    }
+  }
+  DeviceGuard g(p->device);
+  if (cudaStreamCreateWithFlags(&p->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    set_error("cudaStreamCreate failed");
+    delete p;
+    return nullptr;
+  }
+  if (!alloc_buffers(*p, err) || !load_weight_file(*p, err)) { set_error(err); free_program(p); return nullptr; }
+  if (getenv("AF_CUDA_NO_GRAPH")) p->use_graph = false;
+  if (getenv("AF_CUDA_NO_PDL")) p->use_pdl = false;
+  return p;
+}
+
+static int launch_all(Program& p) {
+  for (auto& op : p.ops) {
+    std::string why;
+    if (run_op(p, op, false, why) != cudaSuccess) {
+      set_error("op line " + std::to_string(op.line) + " (" + op.kind + "): " + why);
+      return -1;
+    }
+  }
+  return 0;
+}
+
+static int finalize(Program& p) {
+  for (auto& b : p.bufs)
+    if (b.role == R_WEIGHT && !b.ready && b.alias_of < 0) {
+      set_error("weight buffer '" + b.name + "' was never uploaded or bound");
+      return -1;
+    }
+  if (p.use_graph) {
+    cudaGraph_t graph = nullptr;
+    if (cudaStreamBeginCapture(p.stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+      set_error("stream capture failed to start");
+      return -1;
+    }
+    const int rc = launch_all(p);
+    cudaError_t e = cudaStreamEndCapture(p.stream, &graph);
+    if (rc != 0 || e != cudaSuccess) {
+      if (graph) cudaGraphDestroy(graph);
+      if (rc == 0) set_error(std::string("stream capture failed: ") + cudaGetErrorString(e));
+      cudaGetLastError();
+      return -1;
+    }
+    e = cudaGraphInstantiate(&p.exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) { set_error(std::string("graph instantiate failed: ") + cudaGetErrorString(e)); return -1; }
+  }
+  p.finalized = true;
+  return 0;
+}
+
+static int check_err(Program& p) {
+  int h = 0;
+  if (cudaMemcpyAsync(&h, p.d_err, 4, cudaMemcpyDeviceToHost, p.stream) != cudaSuccess ||
+      cudaStreamSynchronize(p.stream) != cudaSuccess) {
+    set_error(std::string("device failure: ") + cudaGetErrorString(cudaGetLastError()));
+    return -1;
+  }
+  if (h != 0) {
+    static const char* names[] = {"ok", "token id out of range", "decode position out of range", "bounded wait timed out"};
+    set_error(std::string("kernel reported error ") + std::to_string(h) + " (" + (h > 0 && h < 4 ? names[h] : "?") + ")");
+    cudaMemsetAsync(p.d_err, 0, 4, p.stream);
+    cudaStreamSynchronize(p.stream);
+    return -2;
+  }
+  return 0;
+}
+
+static int execute(Program& p, bool sync) {
+  DeviceGuard g(p.device);
+  if (!p.finalized && finalize(p) != 0) return -1;
+  cudaError_t e;
+  if (p.use_graph) {
+    e = cudaGraphLaunch(p.exec, p.stream);
+    if (e != cudaSuccess) { set_error(std::string("graph launch failed: ") + cudaGetErrorString(e)); return -1; }
+  } else if (launch_all(p) != 0) {
+    return -1;
+  }
+  return sync ? check_err(p) : 0;
+}
+
+static Buffer* port(Program& p, const char* name, bool input) {
+  int i = find_buf(p, name);
+  if (i < 0) return nullptr;
+  Buffer& b = p.bufs[i];
+  if (input && !(b.role == R_IN || b.role == R_STATE)) return nullptr;
+  if (!input && b.role != R_OUT) return nullptr;
+  return &b;
+}
+
+static Buffer& root(Program& p, Buffer& b) {
+  int i = (int)(&b - p.bufs.data());
+  while (p.bufs[i].alias_of >= 0) i = p.bufs[i].alias_of;
+  return p.bufs[i];
+}
+
+}  // namespace af
+
+using namespace af;
+
+// ============================================================================= C ABI
+
+extern "C" {
+
+const char* af_last_error(void) { return g_last_error.c_str(); }
+
+int af_abi_version(void) { return AF_CUDA_ABI_VERSION; }
+
+void* af_program_compile(const char* program_path, const char* cache_dir, uint64_t device_mask,
+                         const char* const* in_names, const size_t* in_bytes, size_t n_in,
+                         const char* const* out_names, const size_t* out_bytes, size_t n_out) {
+  (void)cache_dir;
+  if (!program_path) { set_error("null program path"); return nullptr; }
+  std::string dir(program_path);
+  std::ifstream f(dir + "/plan.txt");
+  if (!f) { set_error("cannot open " + dir + "/plan.txt"); return nullptr; }
+  std::stringstream ss;
+  ss << f.rdbuf();
+  Program* p = build_program(ss.str(), dir, device_mask);
+  if (!p) return nullptr;
+  // the declared ports must match the plan's (names, roles, sizes)
+  for (size_t i = 0; i < n_in; ++i) {
+    Buffer* b = port(*p, in_names[i], true);
+    if (!b || b->bytes < in_bytes[i]) {
+      set_error(std::string("input port '") + in_names[i] + "' missing or smaller than declared");
+      free_program(p);
+      return nullptr;
+    }
+  }
+  for (size_t i = 0; i < n_out; ++i) {
+    Buffer* b = port(*p, out_names[i], false);
+    if (!b || b->bytes < out_bytes[i]) {
+      set_error(std::string("output port '") + out_names[i] + "' missing or smaller than declared");
+      free_program(p);
+      return nullptr;
+    }
+  }
+  return p;
+}
+
+void* af_program_compile_text(const char* plan_text, const char* weights_dir, uint64_t device_mask) {
+  if (!plan_text) { set_error("null plan"); return nullptr; }
+  return build_program(plan_text, weights_dir ? weights_dir : ".", device_mask);
+}
+
+int af_compile_check(const char* program_path, const char* cache_dir, uint64_t device_mask,
+                     const char* custom_options) {
+  (void)cache_dir; (void)device_mask; (void)custom_options;
+  std::ifstream f(std::string(program_path ? program_path : "") + "/plan.txt");
+  if (!f) { set_error("cannot open plan"); return -1; }
+  std::stringstream ss;
+  ss << f.rdbuf();
+  Program p;
+  std::string err;
+  if (!parse_plan(p, ss.str(), err)) { set_error(err); return -1; }
+  for (auto& op : p.ops) {
+    std::string why;
+    if (run_op(p, op, true, why) != cudaSuccess) { set_error(why); return -1; }
+  }
+  return 0;
+}
+
+static int copy_in(void* h, const char* name, const void* src, size_t nbytes, bool any_buffer, size_t off) {
+  if (!h || !name || (!src && nbytes)) return -1;
+  Program& p = *static_cast<Program*>(h);
+  Buffer* b = nullptr;
+  if (any_buffer) {
+    int i = find_buf(p, name);
+    b = i < 0 ? nullptr : &p.bufs[i];
+  } else {
+    b = port(p, name, true);
+  }
+  if (!b) { set_error(std::string("unknown input port '") + name + "'"); return -1; }
+  Buffer& r = root(p, *b);
+  if (off + nbytes > r.bytes) { set_error(std::string("copy into '") + name + "' exceeds its size"); return -1; }
+  DeviceGuard g(p.device);
+  if (cudaMemcpyAsync(static_cast<char*>(r.dev) + off, src, nbytes, cudaMemcpyHostToDevice, p.stream) != cudaSuccess ||
+      cudaStreamSynchronize(p.stream) != cudaSuccess) {
+    set_error(std::string("upload to '") + name + "' failed");
+    return -1;
+  }
+  r.ready = true;
+  return 0;
+}
+
+int af_program_set_input_fp16(void* h, const char* port_name, const uint16_t* src, size_t n_elems) {
+  return copy_in(h, port_name, src, 2 * n_elems, false, 0);
+}
+
+int af_program_set_input_bytes(void* h, const char* port_name, const void* src, size_t nbytes) {
+  return copy_in(h, port_name, src, nbytes, false, 0);
+}
+
+int af_program_upload(void* h, const char* name, const void* src, size_t nbytes, size_t offset) {
+  return copy_in(h, name, src, nbytes, true, offset);
+}
+
+static int copy_out(void* h, const char* name, void* dst, size_t nbytes, bool any_buffer) {
+  if (!h || !name || !dst) return -1;
+  Program& p = *static_cast<Program*>(h);
+  Buffer* b = nullptr;
+  if (any_buffer) {
+    int i = find_buf(p, name);
+    b = i < 0 ? nullptr : &p.bufs[i];
+  } else {
+    b = port(p, name, false);
+  }
+  if (!b) { set_error(std::string("unknown output port '") + name + "'"); return -1; }
+  Buffer& r = root(p, *b);
+  const size_t n = nbytes < r.bytes ? nbytes : r.bytes;
+  DeviceGuard g(p.device);
+  if (cudaMemcpyAsync(dst, r.dev, n, cudaMemcpyDeviceToHost, p.stream) != cudaSuccess ||
+      cudaStreamSynchronize(p.stream) != cudaSuccess) {
+    set_error(std::string("download of '") + name + "' failed");
+    return -1;
+  }
+  return 0;
+}
+
+int af_program_get_output_fp16(void* h, const char* port_name, uint16_t* dst, size_t n_elems) {
+  return copy_out(h, port_name, dst, 2 * n_elems, false);
+}
+
+int af_program_get_output_bytes(void* h, const char* port_name, void* dst, size_t nbytes) {
+  return copy_out(h, port_name, dst, nbytes, false);
+}
+
+int af_program_download(void* h, const char* name, void* dst, size_t nbytes) {
+  return copy_out(h, name, dst, nbytes, true);
+}
+
+static int buffer_of(void* h, const char* name, void** ptr, size_t* bytes, int want) {
+  if (!h || !name || !ptr || !bytes) return -1;
+  Program& p = *static_cast<Program*>(h);
+  Buffer* b = nullptr;
+  if (want == 0) b = port(p, name, true);
+  else if (want == 1) b = port(p, name, false);
+  else {
+    int i = find_buf(p, name);
+    b = i < 0 ? nullptr : &p.bufs[i];
+  }
+  if (!b) { set_error(std::string("unknown buffer '") + name + "'"); return -1; }
+  Buffer& r = root(p, *b);
+  *ptr = r.dev;
+  *bytes = r.bytes;
+  return 0;
+}
+
+int af_program_input_buffer(void* h, const char* port_name, void** ptr, size_t* bytes) {
+  return buffer_of(h, port_name, ptr, bytes, 0);
+}
+
+int af_program_output_buffer(void* h, const char* port_name, void** ptr, size_t* bytes) {
+  return buffer_of(h, port_name, ptr, bytes, 1);
+}
+
+int af_program_buffer(void* h, const char* name, void** ptr, size_t* bytes) {
+  return buffer_of(h, name, ptr, bytes, 2);
+}
+
+int af_program_bind_buffer(void* h, const char* name, void* dev, size_t bytes) {
+  if (!h || !name || !dev) return -1;
+  Program& p = *static_cast<Program*>(h);
+  if (p.finalized) { set_error("bind_buffer after the first execute"); return -1; }
+  int i = find_buf(p, name);
+  if (i < 0) { set_error(std::string("unknown buffer '") + name + "'"); return -1; }
+  Buffer& b = p.bufs[i];
+  if (bytes < b.bytes) { set_error(std::string("bound memory smaller than buffer '") + name + "'"); return -1; }
+  if ((reinterpret_cast<uintptr_t>(dev) & 15) != 0) { set_error("bound memory must be 16-byte aligned"); return -1; }
+  DeviceGuard g(p.device);
+  if (b.owned && b.dev) cudaFree(b.dev);
+  b.dev = dev;
+  b.owned = false;
+  b.ready = true;
+  return 0;
+}
+
+int af_program_execute(void* h) {
+  if (!h) return -1;
+  return execute(*static_cast<Program*>(h), true);
+}
+
+int af_program_execute_async(void* h) {
+  if (!h) return -1;
+  return execute(*static_cast<Program*>(h), false);
+}
+
+int af_program_sync(void* h) {
+  if (!h) return -1;
+  Program& p = *static_cast<Program*>(h);
+  DeviceGuard g(p.device);
+  return check_err(p);
+}
+
+int af_program_stream(void* h, void** stream) {
+  if (!h || !stream) return -1;
+  *stream = static_cast<Program*>(h)->stream;
+  return 0;
+}
+
+int af_program_set_options(void* h, int use_graph, int use_pdl) {
+  if (!h) return -1;
+  Program& p = *static_cast<Program*>(h);
+  if (p.finalized) { set_error("set_options after the first execute"); return -1; }
+  p.use_graph = use_graph != 0;
+  p.use_pdl = use_pdl != 0;
+  return 0;
+}
+
+int af_program_share_buffer(void* h, size_t src_op, const char* src_out, size_t dst_op, const char* dst_in) {
+  if (!h || !src_out || !dst_in) return -1;
+  Program& p = *static_cast<Program*>(h);
+  if (src_op != 0 || dst_op != 0) { set_error("share_buffer: a program has one op index (0)"); return -1; }
+  if (p.finalized) { set_error("share_buffer after the first execute"); return -1; }
+  Buffer* o = port(p, src_out, false);
+  Buffer* in = port(p, dst_in, true);
+  if (!o || !in) { set_error("share_buffer: unknown port"); return -1; }
+  Buffer& ro = root(p, *o);
+  if (ro.bytes < in->bytes) { set_error("share_buffer: source smaller than destination"); return -1; }
+  DeviceGuard g(p.device);
+  if (in->owned && in->dev) cudaFree(in->dev);   // the destination's own buffer is freed exactly once
+  in->dev = nullptr;
+  in->owned = false;
+  in->alias_of = (int)(&ro - p.bufs.data());
+  return 0;
+}
+
+void af_program_release(void* h) { free_program(static_cast<Program*>(h)); }
+
+}  // extern "C"

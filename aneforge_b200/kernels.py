@@ -1,0 +1,113 @@
+"""Python wrappers of the kernel-level C ABI (include/af_cuda.h). Tensors are torch CUDA tensors used
+only as device memory; every call goes through libaf_cuda.so on torch's current stream and raises on
+a non-zero return code. No CPU path exists."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _runtime as R
+
+
+def _stream(t) -> int:
+  import torch
+  return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _p(t) -> int:
+  return 0 if t is None else t.data_ptr()
+
+
+def _need(cond, msg):
+  if not cond:
+    raise ValueError(msg)
+
+
+def quantize_per_row_i8(W):
+  """Per-row int8 codes [N,K] + fp16 scales [N] (bit-exact to the reference numpy encoder)."""
+  import torch
+  _need(W.is_cuda and W.dim() == 2 and W.is_contiguous(), "W must be a contiguous 2-D CUDA tensor")
+  _need(W.dtype in (torch.float16, torch.float32), "W must be fp16 or fp32")
+  N, K = W.shape
+  q = torch.empty((N, K), dtype=torch.int8, device=W.device)
+  s = torch.empty((N,), dtype=torch.float16, device=W.device)
+  R.check(R.lib().af_quantize_per_row_i8(_p(W), int(W.dtype == torch.float16), N, K, _p(q), _p(s), _stream(W)),
+          "af_quantize_per_row_i8")
+  return q, s
+
+
+def quantize_g32_i4(W):
+  """Group-32 int4: packed [N, K/2] uint8 + fp16 scales [N, K/32]."""
+  import torch
+  _need(W.is_cuda and W.dim() == 2 and W.is_contiguous(), "W must be a contiguous 2-D CUDA tensor")
+  N, K = W.shape
+  _need(K % 32 == 0, "K must be a multiple of 32")
+  p = torch.empty((N, K // 2), dtype=torch.uint8, device=W.device)
+  s = torch.empty((N, K // 32), dtype=torch.float16, device=W.device)
+  R.check(R.lib().af_quantize_g32_i4(_p(W), int(W.dtype == torch.float16), N, K, _p(p), _p(s), _stream(W)),
+          "af_quantize_g32_i4")
+  return p, s
+
+
+def gemv(x, w, scales=None, bias=None, wf=R.W_I8, epi=R.EPI_F32, y=None, n_out=None):
+  """y = epi(scales (.) (x . W^T) + bias). x [NB, K] fp16; w rows [N, ...]."""
+  import torch
+  _need(x.is_cuda and x.dtype == torch.float16 and x.dim() == 2, "x must be [NB, K] fp16 CUDA")
+  NB, K = x.shape
+  N = w.shape[0]
+  cols = N // 2 if epi == R.EPI_SWIGLU else N
+  if y is None:
+    dt = torch.float16 if epi in (R.EPI_F16, R.EPI_SWIGLU) else torch.float32
+    y = torch.zeros((NB, cols), dtype=dt, device=x.device)
+  R.check(R.lib().af_gemv(wf, epi, _p(x), x.stride(0), _p(w), _p(scales), _p(bias), _p(y), y.stride(0), NB, N, K,
+                          _stream(x)), "af_gemv")
+  return y
+
+
+def lm_head_argmax(x, w, scales=None, wf=R.W_F16, logits=True, pos=None):
+  """Greedy token per row of x [NB, K] fp16 against head rows w [V, K]; optional fp32 logits."""
+  import torch
+  NB, K = x.shape
+  V = w.shape[0]
+  L = R.lib()
+  nbytes = ctypes.c_size_t()
+  R.check(L.af_lm_head_argmax_scratch(wf, V, K, NB, ctypes.byref(nbytes)), "scratch")
+  scratch = torch.zeros((nbytes.value,), dtype=torch.uint8, device=x.device)
+  tok = torch.zeros((NB,), dtype=torch.int32, device=x.device)
+  lg = torch.zeros((NB, V), dtype=torch.float32, device=x.device) if logits else None
+  R.check(L.af_lm_head_argmax(wf, _p(x), x.stride(0), _p(w), _p(scales), _p(lg), NB, V, K, _p(tok), _p(pos),
+                              _p(scratch), nbytes.value, _stream(x)), "af_lm_head_argmax")
+  return tok, lg
+
+
+def rmsnorm(x, g, floor):
+  import torch
+  NB, D = x.shape
+  out = torch.empty((NB, D), dtype=torch.float16, device=x.device)
+  R.check(R.lib().af_rmsnorm(_p(x), int(x.dtype == torch.float16), x.stride(0), _p(g), float(floor), _p(out),
+                             out.stride(0), NB, D, _stream(x)), "af_rmsnorm")
+  return out
+
+
+def attn_decode_scratch_bytes(nb, kv, n_split, g, dh) -> int:
+  n = ctypes.c_size_t()
+  R.check(R.load_library().af_attn_decode_scratch(nb, kv, n_split, g, dh, ctypes.byref(n)), "scratch")
+  return n.value
+
+
+def attn_decode(qkv, kc, vc, pos, cos_t, sin_t, H, KV, dh, scale, kv_c=1.0, expand=False, n_split=1, scratch=None,
+                err=None):
+  """Decode attention; updates kc/vc at pos in place; returns fp16 [NB, H*dh]."""
+  import torch
+  NB = qkv.shape[0]
+  M = kc.shape[2]
+  out = torch.zeros((NB, H * dh), dtype=torch.float16, device=qkv.device)
+  if n_split > 1 and scratch is None:
+    scratch = torch.zeros((attn_decode_scratch_bytes(NB, KV, n_split, H // KV, dh),), dtype=torch.uint8,
+                          device=qkv.device)
+  nbytes = 0 if scratch is None else scratch.numel()
+  R.check(R.lib().af_attn_decode(_p(qkv), qkv.stride(0), _p(kc), _p(vc), _p(pos), _p(cos_t), _p(sin_t), _p(out),
+                                 out.stride(0), NB, H, KV, dh, M, n_split, float(scale), float(kv_c), int(expand),
+                                 _p(scratch), nbytes, _p(err), _stream(qkv)), "af_attn_decode")
+  return out

@@ -1,0 +1,48 @@
+"""Device weight layouts (the B200 re-pack of the reference's `_blob.py` payloads).
+
+* int8 per-row: codes [N][K] row-major + fp16 scales [N] - each 16-byte load is 16 codes of one row,
+  so a warp streams 512 contiguous bytes.
+* int4 group-32: packed [N][K/2] (element 2i in the low nibble) + fp16 scales [N][K/32]; one 16-byte
+  load is exactly one group.
+* Fused projections: q|k|v rows are concatenated (one GEMV over the shared normalised input); gate
+  and up rows are interleaved in blocks of SWIGLU_BLOCK rows (4 gate rows, then the 4 matching up
+  rows) so one CTA row-block produces silu(gate)*up for 4 outputs in its epilogue.
+
+Packers accept numpy arrays or torch tensors (on any device) and return the same kind.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+SWIGLU_BLOCK = 8          # rows per gate/up block in the packed matrix (must match gemv.cu)
+SWIGLU_HALF = SWIGLU_BLOCK // 2
+
+
+def _cat(parts, like):
+  if isinstance(like, np.ndarray):
+    return np.concatenate(parts, axis=0)
+  import torch
+  return torch.cat(parts, dim=0)
+
+
+def interleave_blocks(g, u, half: int = SWIGLU_HALF):
+  """Rows [g0..g3, u0..u3, g4..g7, u4..u7, ...]: blocks of `half` rows of g then of u."""
+  F = g.shape[0]
+  if F % half:
+    raise ValueError(f"gate/up rows ({F}) must be a multiple of {half}")
+  rest = tuple(g.shape[1:])
+  if isinstance(g, np.ndarray):
+    out = np.stack([g.reshape((F // half, half) + rest), u.reshape((F // half, half) + rest)], axis=1)
+    return np.ascontiguousarray(out.reshape((2 * F,) + rest))
+  import torch
+  out = torch.stack([g.reshape((F // half, half) + rest), u.reshape((F // half, half) + rest)], dim=1)
+  return out.reshape((2 * F,) + rest).contiguous()
+
+
+def pack_gate_up(qg, qu, sg, su):
+  """int8 codes and per-row scales of gate and up -> the packed swiglu matrix."""
+  return interleave_blocks(qg, qu), interleave_blocks(sg, su)
+
+
+def concat_rows(*mats):
+  return _cat(list(mats), mats[0])

@@ -1,0 +1,758 @@
+"""LLM decode/prefill on B200: the drop-in for the reference's `aneforge/llm.py` runner.
+
+Same surface: `LlamaConfig`, `LayerSpec`, `rope_tables`, the builder registries
+(`PREFILL_MIXERS`, `PREFILL_MLPS`, `DECODE_MIXERS`, `DECODE_MLPS`), `ADAPTERS`, `from_pretrained`
+(re-exported as `load_llm`), and `LlamaPrefill` with `compile/prefill/warmup/generate/release`.
+
+What changes underneath (B200-first):
+  * Weights are quantized on the GPU (bit-exact to the reference encoders) and packed into fused
+    projections (q|k|v rows concatenated, gate/up rows interleaved) that stay resident in HBM.
+  * A decode step is ONE program (all layers + final norm + lm_head + greedy argmax) replayed as a
+    CUDA graph; registry values are plan emitters that append fused kernel launches.
+  * The KV cache is device-resident per layer ([NB, KV, M, dh] fp16); a step writes only slot `pos`.
+  * The greedy token and the position stay on the device (the token output port is aliased onto
+    the token input port with `share_buffer`, the reference's own resident-state mechanism), so
+    steps run back to back with no host round trip; the host reads the token history at the end.
+  * Batched prefill writes K/V in the decode cache layout, then seeds the cache with one device copy.
+"""
+from __future__ import annotations
+
+import time
+import warnings
+from dataclasses import dataclass, field
+from enum import Enum
+
+import numpy as np
+
+from . import _blob
+from . import _runtime as R
+from .plan import PlanBuilder, at
+from .weights import DevLinear, encode_linear, rms_weights, to_device, fp16_bits_exact
+
+F16, F32 = np.float16, np.float32
+
+
+class ModelType(str, Enum):
+  GPT2 = "gpt2"
+  GEMMA = "gemma"
+  GEMMA2 = "gemma2"
+  GEMMA3 = "gemma3"
+  GEMMA3_TEXT = "gemma3_text"
+  MISTRAL = "mistral"
+  LLAMA = "llama"
+  QWEN = "qwen"
+
+
+_DENSE_INCOMPATIBLE = {ModelType.GEMMA2, ModelType.GEMMA3, ModelType.GEMMA3_TEXT}
+
+
+@dataclass
+class LayerSpec:
+  """Per-layer plan (reference `aneforge/llm.py:36-42`)."""
+  mixer: str = "attention"
+  mlp: str = "swiglu"
+  qk_norm: bool = False
+
+
+@dataclass
+class LlamaConfig:
+  """Decoder config (reference `aneforge/llm.py:45-59`)."""
+  dim: int; n_layers: int; n_heads: int; n_kv_heads: int; ffn_dim: int; vocab: int
+  rope_base: float = 10000.0; norm_eps: float = 1e-5; head_dim: int = 0
+  rotary_dim: int = 0; rope_interleaved: bool = False
+  rope_scaling: dict | None = None
+  layers: list = field(default_factory=list)
+  extra: dict = field(default_factory=dict)
+  norm_type: str = "rms"
+  rope: bool = True
+
+  @property
+  def dh(self) -> int:
+    return self.head_dim or self.dim // self.n_heads
+
+
+def _llama3_rope_scale(inv, s):
+  """Llama-3.1 "llama3" inverse-frequency rescaling (reference `llm.py:62-73`)."""
+  factor, lo, hi = float(s["factor"]), float(s["low_freq_factor"]), float(s["high_freq_factor"])
+  old = float(s["original_max_position_embeddings"])
+  low_wl, high_wl = old / lo, old / hi
+  wl = 2.0 * np.pi / inv
+  scaled = np.where(wl > low_wl, inv / factor, inv)
+  smooth = (old / wl - lo) / (hi - lo)
+  smoothed = (1.0 - smooth) * scaled / factor + smooth * scaled
+  return np.where((wl >= high_wl) & (wl <= low_wl), smoothed, scaled)
+
+
+def rope_tables(seq: int, dh: int, base: float = 10000.0, rotary_dim: int = 0, interleaved: bool = False,
+                scaling: dict | None = None):
+  """[seq, dh] fp16 cos/sin tables, float64 math (reference `llm.py:76-94`)."""
+  rd = rotary_dim or dh
+  inv = 1.0 / (base ** (np.arange(0, rd, 2) / rd))
+  if scaling and scaling.get("rope_type") == "llama3":
+    inv = _llama3_rope_scale(inv, scaling)
+  pos = np.arange(seq)[:, None] * inv[None, :]
+  if interleaved:
+    c = np.repeat(np.cos(pos), 2, axis=1); s = np.repeat(np.sin(pos), 2, axis=1)
+  else:
+    emb = np.concatenate([pos, pos], -1); c = np.cos(emb); s = np.sin(emb)
+  if rd < dh:
+    c = np.concatenate([c, np.ones((seq, dh - rd))], 1); s = np.concatenate([s, np.zeros((seq, dh - rd))], 1)
+  return c.astype(F16), s.astype(F16)
+
+
+# ------------------------------------------------------------------------------ plan emitters
+#
+# A registry value appends the fused launches of one block to a plan. `ctx` carries the program's
+# activation buffers and shapes: h (fp32 residual [NB, D]), xn (fp16 [NB, D]), qkv, att, act, pos,
+# NB, M; `lw` is the layer's packed device weights (names of bound buffers, see _bind_layer).
+
+def _emit_linear(pb, ctx, name, lin: DevLinear, x, y, epi, nb=None):
+  kv = dict(wf=lin.wf, epi=epi, x=x, w=f"{name}.w", y=y, nb=nb or ctx["NB"], n=lin.N, k=lin.K)
+  if lin.kind == "int8":
+    kv["s"] = f"{name}.s"
+  elif lin.kind == "int4_g32":
+    kv["gs"] = f"{name}.s"
+  if lin.bias is not None:
+    kv["bias"] = f"{name}.b"
+  pb.op("gemv", **kv)
+
+
+def emit_attention_decode(pb, ctx, li, lw, cfg, ls):
+  """`_attn_decode` (reference `llm.py:214-237`): norm -> fused QKV GEMV -> RoPE + cache write at
+  pos + GQA split-K attention -> o_proj GEMV with the residual add fused."""
+  D, H, KV, dh, NB, M = cfg.dim, cfg.n_heads, cfg.n_kv_heads, cfg.dh, ctx["NB"], ctx["M"]
+  pre = f"L{li}"
+  pb.op("rmsnorm", x="h", g=f"{pre}.attn_g", out="xn", nb=NB, d=D, floor=lw["attn_floor"])
+  _emit_linear(pb, ctx, f"{pre}.qkv", lw["qkv"], "xn", "qkv", "f32")
+  kv = dict(qkv="qkv", kc=f"{pre}.K", vc=f"{pre}.V", pos="pos", out="att", nb=NB, h=H, kv=KV, dh=dh, m=M,
+            nsplit=ctx["nsplit"], scale=ctx["scale"], kvc=ctx["kvc"], expand=int(ctx["expand"]))
+  if cfg.rope:
+    kv.update(cos="rope.cos", sin="rope.sin")
+  if ls.qk_norm:
+    kv.update(qn=f"{pre}.qn", kn=f"{pre}.kn", qnf=lw["qn_floor"], knf=lw["kn_floor"])
+  if ctx["nsplit"] > 1:
+    kv.update(part="attn.part", cnt="attn.cnt")
+  pb.op("attn_decode", **kv)
+  _emit_linear(pb, ctx, f"{pre}.o", lw["o"], "att", "h", "resid")
+
+
+def emit_attention_prefill(pb, ctx, li, lw, cfg, ls):
+  """`_attn_prefill_kv` (reference `llm.py:149-169`): K (roped) and V land in cache layout."""
+  D, H, KV, dh, S = cfg.dim, cfg.n_heads, cfg.n_kv_heads, cfg.dh, ctx["NB"]
+  pre = f"L{li}"
+  pb.op("rmsnorm", x="h", g=f"{pre}.attn_g", out="xn", nb=S, d=D, floor=lw["attn_floor"])
+  _emit_linear(pb, ctx, f"{pre}.qkv", lw["qkv"], "xn", "qkv", "f32")
+  kv = dict(qkv="qkv", kc=f"{pre}.K", vc=f"{pre}.V", out="att", qbuf="qbuf", s=S, h=H, kv=KV, dh=dh, ldm=S,
+            scale=ctx["scale"], kvc=ctx["kvc"], expand=int(ctx["expand"]))
+  if cfg.rope:
+    kv.update(cos="rope.cos", sin="rope.sin")
+  if ls.qk_norm:
+    kv.update(qn=f"{pre}.qn", kn=f"{pre}.kn", qnf=lw["qn_floor"], knf=lw["kn_floor"])
+  pb.op("attn_prefill", **kv)
+  _emit_linear(pb, ctx, f"{pre}.o", lw["o"], "att", "h", "resid")
+
+
+def emit_swiglu(pb, ctx, li, lw, cfg, ls):
+  """`_swiglu` (reference `llm.py:171-175`): norm -> fused gate|up GEMV with silu(g)*u epilogue ->
+  down GEMV with the residual add fused."""
+  pre = f"L{li}"
+  pb.op("rmsnorm", x="h", g=f"{pre}.mlp_g", out="xn", nb=ctx["NB"], d=cfg.dim, floor=lw["mlp_floor"])
+  _emit_linear(pb, ctx, f"{pre}.gu", lw["gu"], "xn", "act", "swiglu")
+  _emit_linear(pb, ctx, f"{pre}.down", lw["down"], "act", "h", "resid")
+
+
+PREFILL_MIXERS = {"attention": emit_attention_prefill}
+PREFILL_MLPS = {"swiglu": emit_swiglu}
+DECODE_MIXERS = {"attention": emit_attention_decode}
+DECODE_MLPS = {"swiglu": emit_swiglu}
+_DECODE_CTX = ("pos",)
+
+
+# ------------------------------------------------------------------------------ the runner
+
+class LlamaPrefill:
+  """A decoder resident on one B200. `prefill(ids)` returns next-token logits; `generate(...)` runs
+  greedy / sampled decode over a device-resident KV cache. Weights: the reference's dict layout
+  (`aneforge/llm.py:636-654`) of numpy arrays or torch tensors (host or device)."""
+
+  def __init__(self, cfg: LlamaConfig, weights: dict, compress: str | None = None, ane_lm_head: bool = True,
+               device: int = 0, compress_atol: float = 0.05, block_size: int = 32):
+    self.cfg = cfg; self.w = weights; self.compress = compress
+    self.compress_atol, self.block_size = compress_atol, block_size
+    self.device = int(device)
+    self.ane_lm_head = ane_lm_head          # kept for API parity: the head always runs on the device
+    self.lmhead_tie_margin = 3e-3
+    self._chunk_bytes = 1e15                # one program holds every layer on a 180 GB device
+    self._chunk_max_layers = 1 << 30
+    self._dev = None
+    self._dec = None
+    self._pre = None
+    self._head = None
+    self._lmT = None
+
+  # -- weights
+  def _spec(self, i: int) -> LayerSpec:
+    if self.cfg.layers:
+      return self.cfg.layers[i]
+    return LayerSpec(qk_norm="q_norm" in self.w["layers"][i])
+
+  def _layer_chunks(self):
+    """Reference chunk plan (`llm.py:425-433`); on B200 decode always runs as one program, which
+    is output-invariant to the chunking (there is no ~2 GB per-program ceiling to respect)."""
+    per = sum(int(np.prod(np.shape(v))) for v in self.w["layers"][0].values()) * 2
+    if self.compress in ("int8", "blockwise"):
+      per //= 2
+    elif self.compress in ("int4", "int4_g32"):
+      per //= 4
+    n = max(1, min(self.cfg.n_layers, self._chunk_max_layers, int(self._chunk_bytes // max(per, 1))))
+    return [range(i, min(i + n, self.cfg.n_layers)) for i in range(0, self.cfg.n_layers, n)]
+
+  def _load(self):
+    """Quantize + pack every weight onto the device once (the reference bakes them per compile)."""
+    if self._dev is not None:
+      return self._dev
+    import torch
+    R.lib()
+    cfg, dev = self.cfg, torch.device("cuda", self.device)
+    c, atol, bs = self.compress, self.compress_atol, self.block_size
+    layers = []
+    for i in range(cfg.n_layers):
+      lw = self.w["layers"][i]
+      ls = self._spec(i)
+      if ls.mixer != "attention":
+        raise NotImplementedError(f"mixer {ls.mixer!r} has no B200 emitter")
+      if ls.mlp not in DECODE_MLPS:
+        raise NotImplementedError(f"mlp {ls.mlp!r} has no B200 emitter")
+      d = {}
+      d["qkv"] = encode_linear([lw["wq"], lw["wk"], lw["wv"]], c, dev,
+                               biases=[lw.get("q_bias"), lw.get("k_bias"), lw.get("v_bias")], atol=atol,
+                               block_size=bs)
+      d["o"] = encode_linear([lw["wo"]], c, dev, biases=[lw.get("o_bias")], atol=atol, block_size=bs)
+      d["attn_g"], d["attn_floor"] = rms_weights(lw["attn_norm"], cfg.norm_eps, dev)
+      d["mlp_g"], d["mlp_floor"] = rms_weights(lw["mlp_norm"], cfg.norm_eps, dev)
+      if ls.qk_norm:
+        d["qn"], d["qn_floor"] = rms_weights(lw["q_norm"], cfg.norm_eps, dev)
+        d["kn"], d["kn_floor"] = rms_weights(lw["k_norm"], cfg.norm_eps, dev)
+      if ls.mlp == "swiglu":
+        d["gu"] = encode_linear([lw["wgate"], lw["wup"]], c, dev, swiglu=True, atol=atol, block_size=bs)
+        d["down"] = encode_linear([lw["wdown"]], c, dev, atol=atol, block_size=bs)
+      else:
+        d.update(DECODE_MLP_LOADERS[ls.mlp](self, lw, dev))
+      layers.append(d)
+    fg, ff = rms_weights(self.w["final_norm"], cfg.norm_eps, dev)
+    lm = self.w["lm_head"]
+    self._head_exact = fp16_bits_exact(lm)
+    self._dev = {"layers": layers, "final_g": fg, "final_floor": ff,
+                 "embed": to_device(self.w["embed"], dev, torch.float16),
+                 "lm_head": to_device(lm, dev, torch.float16),
+                 "kvc": _blob.gqa_expand_factor(cfg.n_kv_heads, cfg.n_heads // cfg.n_kv_heads, c, atol, bs),
+                 "scale": float(np.float16(1.0 / cfg.dh ** 0.5))}
+    return self._dev
+
+  def weight_bytes(self) -> dict:
+    """Device bytes by role (for roofline accounting)."""
+    d = self._load()
+    proj = sum(l[k].nbytes for l in d["layers"] for k in ("qkv", "o", "gu", "down") if k in l)
+    return {"projections": proj, "lm_head": d["lm_head"].numel() * 2,
+            "norms": sum(l["attn_g"].numel() * 2 + l["mlp_g"].numel() * 2 for l in d["layers"])}
+
+  def _bind_layer(self, prog, li, d, with_kv_state=True):
+    for key in ("qkv", "o", "gu", "down"):
+      if key not in d:
+        continue
+      lin = d[key]
+      prog.bind(f"L{li}.{key}.w", lin.w)
+      if lin.s is not None:
+        prog.bind(f"L{li}.{key}.s", lin.s)
+      if lin.bias is not None:
+        prog.bind(f"L{li}.{key}.b", lin.bias)
+    for key in ("attn_g", "mlp_g", "qn", "kn"):
+      if key in d:
+        prog.bind(f"L{li}.{key}", d[key])
+
+  def _declare_layer_weights(self, pb, li, d):
+    for key in ("qkv", "o", "gu", "down"):
+      if key not in d:
+        continue
+      lin = d[key]
+      pb.buf(f"L{li}.{key}.w", lin.w.numel() * lin.w.element_size(), "weight")
+      if lin.s is not None:
+        pb.buf(f"L{li}.{key}.s", lin.s.numel() * 2, "weight")
+      if lin.bias is not None:
+        pb.buf(f"L{li}.{key}.b", lin.bias.numel() * 2, "weight")
+    for key in ("attn_g", "mlp_g", "qn", "kn"):
+      if key in d:
+        pb.buf(f"L{li}.{key}", d[key].numel() * 2, "weight")
+
+  def _ctx(self, NB, M):
+    cfg, d = self.cfg, self._load()
+    G = cfg.n_heads // cfg.n_kv_heads
+    # split-K over the cache: enough CTAs to cover the SMs for short batches, one split per 64 keys
+    nsplit = max(1, min(64, (M + 63) // 64, (4 * 148) // max(1, cfg.n_kv_heads * NB)))
+    return {"NB": NB, "M": M, "nsplit": nsplit, "scale": d["scale"], "kvc": d["kvc"], "expand": G > 1 and d["kvc"] != 1.0}
+
+  # -- programs
+  def _decoder(self, M, NB=1):
+    """Build (once, cached by (M, NB)) the decode-step program: embedding gather -> all layers ->
+    final norm -> lm_head + greedy argmax; KV caches and the token/position are resident state."""
+    M, NB = int(M), int(NB)
+    if self._dec is not None and self._dec["M"] == M and self._dec["NB"] == NB:
+      return self._dec
+    if self._dec is not None:
+      self._dec["prog"].release()
+      self._dec = None
+    cfg, d = self.cfg, self._load()
+    D, H, KV, dh, V = cfg.dim, cfg.n_heads, cfg.n_kv_heads, cfg.dh, cfg.vocab
+    Q = (H + 2 * KV) * dh
+    ctx = self._ctx(NB, M)
+    pb = PlanBuilder()
+    pb.buf("tok", 4 * NB, "state"); pb.buf("pos", 4 * NB, "state")
+    pb.buf("tok_out", 4 * NB, "out"); pb.buf("hist", 4 * NB * M, "out")
+    pb.buf("hid", 2 * NB * D, "out"); pb.buf("logits", 4 * NB * V, "out")
+    pb.buf("h", 4 * NB * D, "tmp"); pb.buf("xn", 2 * NB * D, "tmp"); pb.buf("qkv", 4 * NB * Q, "tmp")
+    pb.buf("att", 2 * NB * H * dh, "tmp")
+    F = max((l["gu"].N // 2 for l in d["layers"] if "gu" in l), default=1)
+    pb.buf("act", 2 * NB * F, "tmp")
+    pb.buf("embed", 2 * V * D, "weight"); pb.buf("lm_head", 2 * V * D, "weight"); pb.buf("final_g", 2 * D, "weight")
+    if cfg.rope:
+      pb.buf("rope.cos", 2 * M * dh, "weight"); pb.buf("rope.sin", 2 * M * dh, "weight")
+    from . import kernels
+    if ctx["nsplit"] > 1:
+      pb.buf("attn.part", kernels.attn_decode_scratch_bytes(NB, KV, ctx["nsplit"], H // KV, dh), "scratch")
+      pb.buf("attn.cnt", 4 * NB * KV, "scratch")
+    import ctypes
+    nb = ctypes.c_size_t()
+    R.check(R.load_library().af_lm_head_argmax_scratch(R.W_F16, V, D, NB, ctypes.byref(nb)), "scratch")
+    pb.buf("am.val", nb.value, "scratch"); pb.buf("am.idx", nb.value, "scratch")
+    pb.buf("am.cnt", 4 * ((NB + 3) // 4), "scratch")
+    for li in range(cfg.n_layers):
+      self._declare_layer_weights(pb, li, d["layers"][li])
+      pb.buf(f"L{li}.K", 2 * NB * KV * M * dh, "state"); pb.buf(f"L{li}.V", 2 * NB * KV * M * dh, "state")
+    pb.op("embed", tok="tok", table="embed", h="h", vocab=V, d=D, nb=NB)
+    for li in range(cfg.n_layers):
+      ls = self._spec(li)
+      DECODE_MIXERS[ls.mixer](pb, ctx, li, d["layers"][li], cfg, ls)
+      DECODE_MLPS[ls.mlp](pb, ctx, li, d["layers"][li], cfg, ls)
+    pb.op("rmsnorm", x="h", g="final_g", out="hid", nb=NB, d=D, floor=d["final_floor"])
+    pb.op("gemv", wf="f16", epi="argmax", x="hid", w="lm_head", y="logits", nb=NB, n=V, k=D, amv="am.val",
+          ami="am.idx", amc="am.cnt", tok="tok_out", pos="pos", hist="hist", histld=M)
+    ins = {"tok": (NB,), "pos": (NB,)}
+    for li in range(cfg.n_layers):
+      ins[f"L{li}.K"] = (NB, KV, M, dh); ins[f"L{li}.V"] = (NB, KV, M, dh)
+    outs = {"tok_out": (NB,), "hist": (NB, M), "hid": (NB, D), "logits": (NB, V)}
+    dt = {"tok": "int32", "pos": "int32", "tok_out": "int32", "hist": "int32", "logits": "fp32"}
+    prog = R.Program.from_text(pb.text(), ins, outs, self.device, dt)
+    prog.share_buffer(0, "tok_out", 0, "tok")              # device-resident token feedback
+    prog.bind("embed", d["embed"]); prog.bind("lm_head", d["lm_head"]); prog.bind("final_g", d["final_g"])
+    if cfg.rope:
+      cos_t, sin_t = rope_tables(M, dh, cfg.rope_base, cfg.rotary_dim, cfg.rope_interleaved, cfg.rope_scaling)
+      prog.upload("rope.cos", cos_t); prog.upload("rope.sin", sin_t)
+    for li in range(cfg.n_layers):
+      self._bind_layer(prog, li, d["layers"][li])
+    self._dec = {"M": M, "NB": NB, "prog": prog, "plan": pb}
+    return self._dec
+
+  def _prefiller(self, seq):
+    """Build (once, cached by seq) the batched-prefill program: all layers over `seq` rows, each
+    attention layer's K (roped) / V written as [KV, seq, dh] outputs, final norm -> hidden."""
+    seq = int(seq)
+    if self._pre is not None and self._pre["seq"] == seq:
+      return self._pre
+    if self._pre is not None:
+      self._pre["prog"].release()
+      self._pre = None
+    cfg, d = self.cfg, self._load()
+    D, H, KV, dh, V = cfg.dim, cfg.n_heads, cfg.n_kv_heads, cfg.dh, cfg.vocab
+    Q = (H + 2 * KV) * dh
+    ctx = self._ctx(seq, seq)
+    pb = PlanBuilder()
+    pb.buf("ids", 4 * seq, "in"); pb.buf("hid", 2 * seq * D, "out")
+    pb.buf("h", 4 * seq * D, "tmp"); pb.buf("xn", 2 * seq * D, "tmp"); pb.buf("qkv", 4 * seq * Q, "tmp")
+    pb.buf("att", 2 * seq * H * dh, "tmp"); pb.buf("qbuf", 2 * seq * H * dh, "tmp")
+    F = max((l["gu"].N // 2 for l in d["layers"] if "gu" in l), default=1)
+    pb.buf("act", 2 * seq * F, "tmp")
+    pb.buf("embed", 2 * V * D, "weight"); pb.buf("final_g", 2 * D, "weight")
+    if cfg.rope:
+      pb.buf("rope.cos", 2 * seq * dh, "weight"); pb.buf("rope.sin", 2 * seq * dh, "weight")
+    for li in range(cfg.n_layers):
+      self._declare_layer_weights(pb, li, d["layers"][li])
+      pb.buf(f"L{li}.K", 2 * KV * seq * dh, "out"); pb.buf(f"L{li}.V", 2 * KV * seq * dh, "out")
+    pb.op("embed", tok="ids", table="embed", h="h", vocab=V, d=D, nb=seq)
+    for li in range(cfg.n_layers):
+      ls = self._spec(li)
+      if ls.mixer != "attention":
+        raise NotImplementedError("batched prefill supports attention layers only")
+      PREFILL_MIXERS[ls.mixer](pb, ctx, li, d["layers"][li], cfg, ls)
+      PREFILL_MLPS[ls.mlp](pb, ctx, li, d["layers"][li], cfg, ls)
+    pb.op("rmsnorm", x="h", g="final_g", out="hid", nb=seq, d=D, floor=d["final_floor"])
+    outs = {"hid": (seq, D)}
+    for li in range(cfg.n_layers):
+      outs[f"L{li}.K"] = (KV, seq, dh); outs[f"L{li}.V"] = (KV, seq, dh)
+    prog = R.Program.from_text(pb.text(), {"ids": (seq,)}, outs, self.device, {"ids": "int32"})
+    prog.bind("embed", d["embed"]); prog.bind("final_g", d["final_g"])
+    if cfg.rope:
+      cos_t, sin_t = rope_tables(seq, dh, cfg.rope_base, cfg.rotary_dim, cfg.rope_interleaved, cfg.rope_scaling)
+      prog.upload("rope.cos", cos_t); prog.upload("rope.sin", sin_t)
+    for li in range(cfg.n_layers):
+      self._bind_layer(prog, li, d["layers"][li])
+    self._pre = {"seq": seq, "prog": prog}
+    return self._pre
+
+  def _head_program(self, NB=1):
+    """lm_head + argmax over NB fp16 hidden rows (the reference's `_lm_head_program`, `llm.py:357-385`)."""
+    if self._head is not None and self._head["NB"] == NB:
+      return self._head
+    if self._head is not None:
+      self._head["prog"].release()
+    cfg, d = self.cfg, self._load()
+    D, V = cfg.dim, cfg.vocab
+    import ctypes
+    nb = ctypes.c_size_t()
+    R.check(R.load_library().af_lm_head_argmax_scratch(R.W_F16, V, D, NB, ctypes.byref(nb)), "scratch")
+    pb = PlanBuilder()
+    pb.buf("x", 2 * NB * D, "in"); pb.buf("logits", 4 * NB * V, "out"); pb.buf("tok", 4 * NB, "out")
+    pb.buf("lm_head", 2 * V * D, "weight")
+    pb.buf("am.val", nb.value, "scratch"); pb.buf("am.idx", nb.value, "scratch")
+    pb.buf("am.cnt", 4 * ((NB + 3) // 4), "scratch")
+    pb.op("gemv", wf="f16", epi="argmax", x="x", w="lm_head", y="logits", nb=NB, n=V, k=D, amv="am.val",
+          ami="am.idx", amc="am.cnt", tok="tok")
+    prog = R.Program.from_text(pb.text(), {"x": (NB, D)}, {"logits": (NB, V), "tok": (NB,)}, self.device,
+                               {"logits": "fp32", "tok": "int32"})
+    prog.bind("lm_head", d["lm_head"])
+    self._head = {"NB": NB, "prog": prog}
+    return self._head
+
+  # -- reference API
+  def compile(self, seq: int):
+    self._prefiller(seq)
+    return self
+
+  def warmup(self, max_len):
+    self._decoder(int(max_len))
+    self._head_program()
+    return self
+
+  def release(self) -> None:
+    for k in ("_dec", "_pre", "_head"):
+      v = getattr(self, k)
+      if v is not None:
+        v["prog"].release()
+      setattr(self, k, None)
+    self._dev = None
+    self._lmT = None
+
+  def _host_logits(self, hidden_row):
+    if self._lmT is None:
+      self._lmT = np.ascontiguousarray(np.asarray(
+        self.w["lm_head"].detach().float().cpu().numpy() if hasattr(self.w["lm_head"], "detach")
+        else self.w["lm_head"]).T, F32)
+    return np.asarray(hidden_row, F32) @ self._lmT
+
+  def _logits(self, hidden_row, ane=None):
+    """Device lm_head (fp16 weights, fp32 accumulation) for one fp16 hidden row [D]."""
+    hp = self._head_program()["prog"]
+    hp.set_input("x", np.asarray(hidden_row).astype(F16)[None])
+    hp.execute()
+    return hp.read_output("logits")[0]
+
+  def _decode_logits(self, hidden_row, use_ane, greedy):
+    """Logits with the reference's greedy tie-margin protocol (`llm.py:395-404`): only a head whose
+    weights are not exactly fp16 can differ from the host fp32 head, and then a near tie is
+    recomputed on the host."""
+    logits = self._logits(hidden_row)
+    if greedy and not self._head_exact:
+      p = np.partition(logits, -2)
+      if p[-1] - p[-2] < self.lmhead_tie_margin * (float(np.abs(logits).max()) + 1e-9):
+        logits = self._host_logits(np.asarray(hidden_row, F16).astype(F32))
+    return logits
+
+  @staticmethod
+  def _sample(logits, temperature, top_p, top_k):
+    """Reference `LlamaPrefill._sample` (`llm.py:407-419`)."""
+    if temperature <= 0.0:
+      return int(np.argmax(logits))
+    lg = logits.astype(np.float64) / temperature
+    if top_k and 0 < top_k < lg.size:
+      lg[lg < np.partition(lg, -top_k)[-top_k]] = -np.inf
+    p = np.exp(lg - lg.max()); p /= p.sum()
+    if 0.0 < top_p < 1.0:
+      order = np.argsort(p)[::-1]; cum = np.cumsum(p[order])
+      keep = order[:int(np.searchsorted(cum, top_p)) + 1]
+      m = np.zeros_like(p); m[keep] = p[keep]; p = m / m.sum()
+    return int(np.random.choice(p.size, p=p))
+
+  def _prefill_hidden(self, token_ids, pad_to=None):
+    real = len(token_ids)
+    seq = max(int(pad_to), real) if pad_to else real
+    pre = self._prefiller(seq)
+    ids = np.asarray(list(token_ids) + [0] * (seq - real), np.int32)
+    self._check_ids(ids)
+    pre["prog"].set_input("ids", ids)
+    pre["prog"].execute()
+    return pre, real, seq
+
+  def _check_ids(self, ids):
+    ids = np.asarray(ids)
+    if ids.size and (ids.min() < 0 or ids.max() >= self.cfg.vocab):
+      raise ValueError(f"token id out of range [0, {self.cfg.vocab})")
+
+  def prefill(self, token_ids):
+    """Prefill and return next-token logits [1, vocab] (reference `llm.py:421-423`)."""
+    pre, real, _ = self._prefill_hidden(token_ids)
+    hid = pre["prog"].read_output("hid")
+    return self._logits(hid[real - 1])[None]
+
+  def _seed_cache(self, dec, pre, real, slot=0):
+    """Copy the prefill K/V [KV, real, dh] into decode cache slot `slot`, positions [0, real)
+    (reference `_seed_cache`, `llm.py:546-558`) - device to device."""
+    cfg = self.cfg
+    KV, dh, M, NB = cfg.n_kv_heads, cfg.dh, dec["M"], dec["NB"]
+    seq = pre["seq"]
+    for li in range(cfg.n_layers):
+      for nm in ("K", "V"):
+        src = pre["prog"].tensor(f"L{li}.{nm}", (KV, seq, dh))
+        dst = dec["prog"].tensor(f"L{li}.{nm}", (NB, KV, M, dh))
+        dst[slot, :, :real].copy_(src[:, :real])
+
+  def _reset_state(self, dec):
+    for li in range(self.cfg.n_layers):
+      for nm in ("K", "V"):
+        dec["prog"].tensor(f"L{li}.{nm}", (dec["NB"], self.cfg.n_kv_heads, dec["M"], self.cfg.dh)).zero_()
+
+  def generate(self, token_ids, max_new_tokens=40, eos_id=None, max_len=None, on_token=None,
+               temperature=0.0, top_p=1.0, top_k=0, batched_prefill=True, prefill_pad=None, on_stage=None,
+               ane_lm_head=None):
+    """Autoregressive generation over the device-resident KV cache (reference `llm.py:560-633`)."""
+    import torch
+    cfg = self.cfg
+    prompt = [int(t) for t in token_ids]
+    self._check_ids(prompt)
+    M = int(max_len or len(prompt) + max_new_tokens)
+    eos = {int(eos_id)} if isinstance(eos_id, int) else {int(e) for e in (eos_id or ())}
+    greedy = temperature <= 0.0
+    dec = self._decoder(M, 1)
+    prog = dec["prog"]
+    with torch.cuda.device(self.device):
+      torch.cuda.synchronize()
+      self._reset_state(dec)
+      torch.cuda.synchronize()
+    out = []
+    t0 = time.perf_counter()
+    if batched_prefill and len(prompt) > 1:
+      pre, real, seq = self._prefill_hidden(prompt, prefill_pad)
+      hid = pre["prog"].read_output("hid")
+      logits0 = self._decode_logits(hid[real - 1], None, greedy)
+      with torch.cuda.device(self.device):
+        self._seed_cache(dec, pre, real)
+        torch.cuda.synchronize()
+      cur = self._sample(logits0, temperature, top_p, top_k)
+      out.append(cur)
+      if on_stage is not None:
+        on_stage("prefill", time.perf_counter() - t0)
+      if cur in eos:
+        return out
+      if on_token is not None:
+        on_token(cur)
+      pos = real
+    else:
+      for p, tok in enumerate(prompt[:-1]):
+        prog.set_input("tok", np.array([tok], np.int32)); prog.set_input("pos", np.array([p], np.int32))
+        prog.execute()
+      cur, pos = prompt[-1], len(prompt) - 1
+    prog.set_input("tok", np.array([cur], np.int32)); prog.set_input("pos", np.array([pos], np.int32))
+    n_steps = min(max_new_tokens - len(out), M - 1 - pos)
+    if n_steps <= 0:
+      return out
+    exact_head = greedy and self._head_exact
+    if exact_head and on_token is None and on_stage is None:
+      # greedy with an exact head: every step's token stays on the device; run the steps back to
+      # back and read the token history once (EOS cuts the list where the reference would stop).
+      for _ in range(n_steps):
+        prog.execute_async()
+      prog.sync()
+      hist = prog.read_output("hist")[0]
+      for t in hist[pos:pos + n_steps]:
+        out.append(int(t))
+        if int(t) in eos:
+          break
+      return out
+    for _ in range(n_steps):
+      ts = time.perf_counter()
+      prog.execute()
+      if exact_head:
+        nxt = int(prog.read_output("tok_out")[0])
+      else:
+        hid = prog.read_output("hid")[0]
+        logits = self._decode_logits(hid, None, greedy) if greedy else prog.read_output("logits")[0]
+        nxt = self._sample(logits, temperature, top_p, top_k)
+        prog.set_input("tok", np.array([nxt], np.int32))
+      if on_stage is not None:
+        on_stage("step", time.perf_counter() - ts)
+      out.append(nxt)
+      if nxt in eos:
+        break
+      if on_token is not None:
+        on_token(nxt)
+    return out
+
+  def generate_batch(self, prompts, max_new_tokens=40, max_len=None):
+    """Greedy decode of NB independent prompts in one batched program (B200 extension; the
+    reference runner is batch 1). Each sequence has its own cache slot and position."""
+    import torch
+    NB = len(prompts)
+    prompts = [[int(t) for t in p] for p in prompts]
+    for p in prompts:
+      self._check_ids(p)
+    M = int(max_len or max(len(p) for p in prompts) + max_new_tokens)
+    dec = self._decoder(M, NB)
+    prog = dec["prog"]
+    with torch.cuda.device(self.device):
+      torch.cuda.synchronize()
+      self._reset_state(dec)
+    first, pos = [], []
+    for b, p in enumerate(prompts):
+      pre, real, _ = self._prefill_hidden(p)
+      hid = pre["prog"].read_output("hid")
+      first.append(int(np.argmax(self._decode_logits(hid[real - 1], None, True))))
+      with torch.cuda.device(self.device):
+        self._seed_cache(dec, pre, real, slot=b)
+      pos.append(real)
+    with torch.cuda.device(self.device):
+      torch.cuda.synchronize()
+    prog.set_input("tok", np.array(first, np.int32)); prog.set_input("pos", np.array(pos, np.int32))
+    n_steps = min(max_new_tokens - 1, M - 1 - max(pos))
+    for _ in range(max(0, n_steps)):
+      prog.execute_async()
+    prog.sync()
+    hist = prog.read_output("hist")
+    return [[first[b]] + [int(t) for t in hist[b, pos[b]:pos[b] + max(0, n_steps)]] for b in range(NB)]
+
+
+DECODE_MLP_LOADERS: dict = {}
+
+
+def decoder_block_step(cfg: LlamaConfig, lw: dict, h, Kc, Vc, pos: int, compress="int8", device: int = 0):
+  """One decode step of ONE block (no embedding, final norm or head) through a program: the
+  BASELINE config-2 unit. h [1, D] fp16; Kc/Vc [KV, M, dh] fp16 prior cache. Returns (fp16 block
+  output [1, D], updated K, updated V)."""
+  M = int(Kc.shape[1])
+  w = {"embed": np.zeros((1, cfg.dim), F16), "lm_head": np.zeros((1, cfg.dim), F16),
+       "final_norm": np.ones(cfg.dim, F32), "layers": [lw]}
+  c1 = LlamaConfig(**{**cfg.__dict__, "n_layers": 1, "layers": [cfg.layers[0] if cfg.layers else LayerSpec()]})
+  m = LlamaPrefill(c1, w, compress=compress, device=device)
+  d = m._load()
+  D, H, KV, dh = c1.dim, c1.n_heads, c1.n_kv_heads, c1.dh
+  ctx = m._ctx(1, M)
+  pb = PlanBuilder()
+  pb.buf("x", 2 * D, "in"); pb.buf("pos", 4, "state"); pb.buf("out", 2 * D, "out")
+  pb.buf("h", 4 * D, "tmp"); pb.buf("xn", 2 * D, "tmp"); pb.buf("qkv", 4 * (H + 2 * KV) * dh, "tmp")
+  pb.buf("att", 2 * H * dh, "tmp"); pb.buf("act", 2 * d["layers"][0]["gu"].N // 2, "tmp")
+  pb.buf("rope.cos", 2 * M * dh, "weight"); pb.buf("rope.sin", 2 * M * dh, "weight")
+  from . import kernels
+  if ctx["nsplit"] > 1:
+    pb.buf("attn.part", kernels.attn_decode_scratch_bytes(1, KV, ctx["nsplit"], H // KV, dh), "scratch")
+    pb.buf("attn.cnt", 4 * KV, "scratch")
+  m._declare_layer_weights(pb, 0, d["layers"][0])
+  pb.buf("L0.K", 2 * KV * M * dh, "state"); pb.buf("L0.V", 2 * KV * M * dh, "state")
+  pb.op("cast", src="x", dst="h", n=D, mode=0)
+  ls = c1.layers[0]
+  DECODE_MIXERS[ls.mixer](pb, ctx, 0, d["layers"][0], c1, ls)
+  DECODE_MLPS[ls.mlp](pb, ctx, 0, d["layers"][0], c1, ls)
+  pb.op("cast", src="h", dst="out", n=D, mode=1)
+  prog = R.Program.from_text(pb.text(), {"x": (1, D), "pos": (1,), "L0.K": (1, KV, M, dh), "L0.V": (1, KV, M, dh)},
+                             {"out": (1, D)}, device, {"pos": "int32"})
+  cos_t, sin_t = rope_tables(M, dh, c1.rope_base, c1.rotary_dim, c1.rope_interleaved, c1.rope_scaling)
+  prog.upload("rope.cos", cos_t); prog.upload("rope.sin", sin_t)
+  m._bind_layer(prog, 0, d["layers"][0])
+  prog.set_input("x", np.asarray(h, F16).reshape(1, D))
+  prog.set_input("pos", np.array([pos], np.int32))
+  prog.set_input("L0.K", np.asarray(Kc, F16)[None]); prog.set_input("L0.V", np.asarray(Vc, F16)[None])
+  prog.execute()
+  out = prog.read_output("out")
+  K = prog.download("L0.K", (KV, M, dh)); V = prog.download("L0.V", (KV, M, dh))
+  prog.release(); m.release()
+  return out, K, V
+
+
+# ------------------------------------------------------------------------------ loaders
+
+def _weights_from_state_dict(sd, cfg: LlamaConfig) -> dict:
+  """HF Llama/Qwen state_dict -> the reference weight layout (reference `llm.py:636-654`)."""
+  w = {"embed": sd["model.embed_tokens.weight"], "final_norm": sd["model.norm.weight"],
+       "lm_head": sd.get("lm_head.weight", sd["model.embed_tokens.weight"]), "layers": []}
+  for L in range(cfg.n_layers):
+    p = f"model.layers.{L}."
+    lw = {"wq": sd[p + "self_attn.q_proj.weight"], "wk": sd[p + "self_attn.k_proj.weight"],
+          "wv": sd[p + "self_attn.v_proj.weight"], "wo": sd[p + "self_attn.o_proj.weight"],
+          "wgate": sd[p + "mlp.gate_proj.weight"], "wup": sd[p + "mlp.up_proj.weight"],
+          "wdown": sd[p + "mlp.down_proj.weight"], "attn_norm": sd[p + "input_layernorm.weight"],
+          "mlp_norm": sd[p + "post_attention_layernorm.weight"]}
+    if p + "self_attn.q_norm.weight" in sd:
+      lw["q_norm"] = sd[p + "self_attn.q_norm.weight"]; lw["k_norm"] = sd[p + "self_attn.k_norm.weight"]
+    for proj, key in (("q_proj", "q_bias"), ("k_proj", "k_bias"), ("v_proj", "v_bias"), ("o_proj", "o_bias")):
+      b = sd.get(p + f"self_attn.{proj}.bias")
+      if b is not None:
+        lw[key] = b
+    w["layers"].append(lw)
+  return w
+
+
+def _rope_theta(c) -> float:
+  rp = getattr(c, "rope_parameters", None)
+  if isinstance(rp, dict) and "rope_theta" in rp:
+    return float(rp["rope_theta"])
+  return float(getattr(c, "rope_theta", 10000.0))
+
+
+def _rope_scaling(c):
+  s = getattr(c, "rope_scaling", None)
+  return s if isinstance(s, dict) and s.get("rope_type") == "llama3" else None
+
+
+def _dense_adapter(c, sd):
+  """Dense Llama/Qwen adapter (reference `llm.py:657-668`)."""
+  n = int(c.num_hidden_layers)
+  qk = "model.layers.0.self_attn.q_norm.weight" in sd
+  cfg = LlamaConfig(dim=c.hidden_size, n_layers=n, n_heads=c.num_attention_heads,
+                    n_kv_heads=getattr(c, "num_key_value_heads", c.num_attention_heads),
+                    ffn_dim=c.intermediate_size, vocab=c.vocab_size, rope_base=_rope_theta(c),
+                    norm_eps=float(c.rms_norm_eps), head_dim=int(getattr(c, "head_dim", 0) or 0),
+                    rope_scaling=_rope_scaling(c),
+                    layers=[LayerSpec(mixer="attention", mlp="swiglu", qk_norm=qk) for _ in range(n)])
+  return cfg, _weights_from_state_dict(sd, cfg)
+
+
+def _mistral_adapter(c, sd):
+  """Mistral adapter (reference `llm.py:705-718`): sliding window surfaced in `cfg.extra`."""
+  cfg, w = _dense_adapter(c, sd)
+  cfg.rope_scaling = None
+  if getattr(c, "sliding_window", None):
+    cfg.extra["sliding_window"] = int(c.sliding_window)
+  return cfg, w
+
+
+ADAPTERS: list = [
+  (lambda c: getattr(c, "model_type", None) == ModelType.MISTRAL, _mistral_adapter),
+]
+
+
+def _assert_dense_compatible(c) -> None:
+  """Reference `llm.py:776-788`."""
+  mt = getattr(c, "model_type", "?")
+  cap = getattr(c, "attn_logit_softcapping", None) or getattr(c, "final_logit_softcapping", None)
+  if cap or mt in _DENSE_INCOMPATIBLE or mt in (ModelType.GEMMA, ModelType.GPT2):
+    why = "logit softcapping" if cap else "architecture-specific semantics"
+    raise ValueError(f"load_llm: {mt!r} needs {why} that the B200 dense loader does not implement")
+
+
+def from_pretrained(name: str, compress: str | None = None, ane_lm_head: bool = True, device: int = 0) -> LlamaPrefill:
+  """Load a Hugging Face decoder (reference `llm.py:791-806`) onto one B200."""
+  import torch
+  from transformers import AutoModelForCausalLM
+  hf = AutoModelForCausalLM.from_pretrained(name)
+  adapt = next((fn for pred, fn in ADAPTERS if pred(hf.config)), _dense_adapter)
+  if adapt is _dense_adapter:
+    _assert_dense_compatible(hf.config)
+  sd = {k: v.detach().to(torch.float16) for k, v in hf.state_dict().items()}
+  cfg, weights = adapt(hf.config, sd)
+  return LlamaPrefill(cfg, weights, compress=compress, ane_lm_head=ane_lm_head, device=device)

@@ -1,0 +1,136 @@
+"""Packing reference-layout weights (numpy or torch, host or device) into device-resident fused
+projections: the B200 replacement for baking weights into the e5rt BLOBFILE
+(`aneforge/_compile.py:112-188`, `_blob.py:67-86`)."""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _blob
+from . import _runtime as R
+from . import layout
+
+F16, F32 = np.float16, np.float32
+_HOST_DECIDE_LIMIT = 1 << 22        # run the host encoding gates only on tensors this small
+
+
+def torch_mod():
+  import torch
+  return torch
+
+
+def to_device(a, device, dtype=None):
+  """numpy / torch (any device) -> contiguous CUDA tensor on `device`."""
+  torch = torch_mod()
+  if isinstance(a, torch.Tensor):
+    t = a.to(device=device, non_blocking=False)
+  else:
+    t = torch.from_numpy(np.ascontiguousarray(np.asarray(a))).to(device)
+  if dtype is not None:
+    t = t.to(dtype)
+  return t.contiguous()
+
+
+def fp16_bits_exact(a) -> bool:
+  """True when every value of `a` is exactly representable in fp16."""
+  torch = torch_mod()
+  if isinstance(a, torch.Tensor):
+    return bool(a.dtype == torch.float16 or torch.equal(a.float(), a.half().float()))
+  a = np.asarray(a)
+  return a.dtype == F16 or bool(np.array_equal(a.astype(F32), a.astype(F16).astype(F32)))
+
+
+@dataclass
+class DevLinear:
+  kind: str            # "int8" | "fp16" | "int4_g32"
+  w: object            # packed codes / fp16 weights (torch CUDA)
+  s: object            # int8: [N] fp16 scales; int4_g32: [N, K/32] fp16; fp16: None
+  bias: object         # [N] fp16 or None
+  N: int
+  K: int
+
+  @property
+  def wf(self) -> str:
+    return {"int8": "i8", "fp16": "f16", "int4_g32": "i4"}[self.kind]
+
+  @property
+  def nbytes(self) -> int:
+    n = self.w.numel() * self.w.element_size()
+    if self.s is not None:
+      n += self.s.numel() * self.s.element_size()
+    return n
+
+
+def decide_kind(W, compress, atol=0.05, block_size=32) -> str:
+  """The reference policy's encoding kind for one matmul weight (`_compile.py:112-188`)."""
+  K = int(W.shape[1])
+  if compress is None:
+    return "fp16"
+  if compress == "int8":
+    return "int8"
+  if compress == "int4_g32":
+    return "int4_g32" if K % 32 == 0 else "fp16"
+  numel = int(np.prod(W.shape))
+  if numel > _HOST_DECIDE_LIMIT and compress == "int4":
+    # the reference's LUT gate on a large near-Gaussian weight: run it on a host copy
+    pass
+  Wh = W.detach().float().cpu().numpy() if hasattr(W, "detach") else np.asarray(W, F32)
+  kind, _ = _blob.decide(Wh, compress, atol, block_size)
+  if kind not in ("int8", "fp16", "int4_g32"):
+    raise NotImplementedError(f"compress={compress!r}: the {kind} device decoder is not built yet")
+  return kind
+
+
+def _quantize(W, kind, device):
+  """One matrix -> (codes, scales) on the device (bit-exact to the reference encoders)."""
+  from . import kernels
+  torch = torch_mod()
+  Wd = to_device(W, device)
+  if Wd.dtype not in (torch.float16, torch.float32):
+    Wd = Wd.float()
+  if kind == "int8":
+    return kernels.quantize_per_row_i8(Wd)
+  if kind == "int4_g32":
+    return kernels.quantize_g32_i4(Wd)
+  return Wd.half().contiguous(), None
+
+
+def encode_linear(parts, compress, device, biases=None, swiglu=False, atol=0.05, block_size=32) -> DevLinear:
+  """Encode one or more [N_i, K] matrices sharing their input into one device projection.
+  `swiglu=True` takes (gate, up) and interleaves them for the fused silu(gate)*up epilogue;
+  otherwise the rows are concatenated (q|k|v)."""
+  torch = torch_mod()
+  kinds = {decide_kind(P, compress, atol, block_size) for P in parts}
+  if len(kinds) != 1:
+    raise NotImplementedError(f"fused projection parts encode differently: {sorted(kinds)}")
+  kind = kinds.pop()
+  K = int(parts[0].shape[1])
+  enc = [_quantize(P, kind, device) for P in parts]
+  if swiglu:
+    (wg, sg), (wu, su) = enc
+    w = layout.interleave_blocks(wg, wu)
+    s = None if sg is None else layout.interleave_blocks(sg, su)
+  else:
+    w = torch.cat([e[0] for e in enc], 0) if len(enc) > 1 else enc[0][0]
+    s = None if enc[0][1] is None else (torch.cat([e[1] for e in enc], 0) if len(enc) > 1 else enc[0][1])
+  N = int(w.shape[0])
+  b = None
+  if biases is not None and any(x is not None for x in biases):
+    if swiglu:
+      raise NotImplementedError("bias on a gate/up projection")
+    cols = []
+    for P, x in zip(parts, biases):
+      cols.append(torch.zeros(int(P.shape[0]), dtype=torch.float16, device=device) if x is None
+                  else to_device(x, device).float().half())
+    b = torch.cat(cols, 0).contiguous()
+  return DevLinear(kind, w.contiguous(), None if s is None else s.contiguous(), b, N, K)
+
+
+def rms_weights(gamma, eps, device):
+  """(g_eff fp16 tensor, floor float) as the reference bakes them (`_compile.py:738-748`)."""
+  g = np.asarray(gamma.detach().float().cpu().numpy() if hasattr(gamma, "detach") else gamma)
+  D = int(g.shape[-1])
+  g_eff = (g.reshape(1, D).astype(F32) * float(np.sqrt(D))).astype(F16).reshape(D)
+  floor = float(np.float16((D * float(eps)) ** 0.5))
+  return to_device(g_eff, device), floor

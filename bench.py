@@ -1,0 +1,335 @@
+"""Benchmark: int8 decode tokens/s of a Llama-3-8B-shaped model on B200.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl reference]
+
+One step = one decode token for each of the B sequences (B = 1 by default), all 32 layers, the
+final norm, the lm_head and the greedy argmax, replayed as one CUDA graph over a device-resident
+KV cache. Weights are random N(0, 0.02) (no checkpoints here), quantized per row to int8 on the
+GPU with the reference's encoder; the prompt is 512 uniform token ids, prefilled before timing.
+
+Under torchrun (N > 1) each rank runs an independent replica of the whole model (weak scaling);
+the timed region is bracketed by a barrier + device sync on every rank and the slowest rank's time
+is reported.
+
+`--impl reference` times the reference algorithm's CPU path (the numpy restatement of ANEForge's
+decode driver in `oracle/`, run with every host thread BLAS offers) on the same workload, on a
+bounded sample: a few decode steps of a 2-layer slice of the same model plus its lm_head, scaled to
+32 layers.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG = dict(dim=4096, n_layers=32, n_heads=32, n_kv_heads=8, ffn_dim=14336, vocab=128256, rope_base=500000.0,
+           norm_eps=1e-5)
+PROMPT = 512
+METRIC = "int8 decode tokens/s (Llama-3-8B-shaped, greedy)"
+
+
+def _dist():
+  ws = int(os.environ.get("WORLD_SIZE", "1"))
+  rank = int(os.environ.get("RANK", "0"))
+  local = int(os.environ.get("LOCAL_RANK", "0"))
+  return ws, rank, local
+
+
+def _peaks():
+  try:
+    with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+      p = json.load(f)
+    return float(p["hbm_gbs"]), "measured"
+  except Exception:
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+  """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+  def __init__(self, index: int):
+    self.index, self.samples, self._stop = index, [], threading.Event()
+    self._t = threading.Thread(target=self._run, daemon=True)
+
+  def _run(self):
+    q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+    while not self._stop.is_set():
+      try:
+        out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}", "--format=csv,noheader,nounits"],
+                             capture_output=True, text=True, timeout=5).stdout.strip()
+        if out:
+          self.samples.append([x.strip() for x in out.split(",")])
+      except Exception:
+        pass
+      self._stop.wait(0.2)
+
+  def __enter__(self):
+    self._t.start()
+    return self
+
+  def __exit__(self, *a):
+    self._stop.set()
+    self._t.join(timeout=10)
+
+  def summary(self):
+    if not self.samples:
+      return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+    sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+    mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > 3 + i and s[3 + i] == "Active"})
+    return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+            "reasons": reasons, "samples": len(self.samples)}
+
+
+def make_weights(cfg, device, seed=0):
+  """Seeded N(0, 0.02) fp16 weights generated on the device, reference dict layout."""
+  import torch
+  g = torch.Generator(device=device)
+  g.manual_seed(seed)
+  R = lambda *s: (torch.randn(*s, generator=g, device=device, dtype=torch.float32) * 0.02).half()
+  D, dh = cfg.dim, cfg.dh
+  w = {"embed": R(cfg.vocab, D), "lm_head": R(cfg.vocab, D), "final_norm": torch.ones(D, device=device), "layers": []}
+  for _ in range(cfg.n_layers):
+    w["layers"].append({"wq": R(cfg.n_heads * dh, D), "wk": R(cfg.n_kv_heads * dh, D), "wv": R(cfg.n_kv_heads * dh, D),
+                        "wo": R(D, cfg.n_heads * dh), "wgate": R(cfg.ffn_dim, D), "wup": R(cfg.ffn_dim, D),
+                        "wdown": R(D, cfg.ffn_dim), "attn_norm": torch.ones(D, device=device),
+                        "mlp_norm": torch.ones(D, device=device)})
+  return w
+
+
+def algorithmic_bytes_per_step(cfg, NB, pos):
+  """Bytes a decode step must move once (SURVEY 8(d) accounting): int8 codes + fp16 scales of every
+  projection, the fp16 lm_head, norms, KV cache read (positions 0..pos) + the new slot write, and
+  the step's activations in/out."""
+  D, H, KV, dh, F, V, L = cfg.dim, cfg.n_heads, cfg.n_kv_heads, cfg.dh, cfg.ffn_dim, cfg.vocab, cfg.n_layers
+  proj_rows = (H + 2 * KV) * dh + D + 2 * F + D
+  proj_params = ((H + 2 * KV) * dh * D) + D * H * dh + 2 * F * D + D * F
+  per_layer = proj_params + 2 * proj_rows + 2 * D * 2
+  kv = L * NB * (2 * KV * (pos + 1) * dh * 2)
+  return L * per_layer + V * D * 2 + D * 2 + kv + NB * (4 + 4)
+
+
+def run_b200(args):
+  import torch
+  import torch.distributed as dist
+  from aneforge_b200 import llm as L, _runtime as R, kernels
+  ws, rank, local = _dist()
+  if ws > 1:
+    dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=600))
+  torch.cuda.set_device(local)
+  dev = torch.device("cuda", local)
+  cfg = L.LlamaConfig(**CFG, layers=[L.LayerSpec() for _ in range(CFG["n_layers"])])
+  NB = args.batch
+  t_load = time.perf_counter()
+  w = make_weights(cfg, dev, seed=1234 + rank)
+  m = L.LlamaPrefill(cfg, w, compress="int8", device=local)
+  m._load()
+  del w
+  torch.cuda.empty_cache()
+  load_s = time.perf_counter() - t_load
+  M = PROMPT + args.warmup + args.steps + 8
+  rng = np.random.default_rng(99 + rank)
+  prompts = [list(rng.integers(0, cfg.vocab, PROMPT)) for _ in range(NB)]
+  dec = m._decoder(M, NB)
+  prog = dec["prog"]
+  m._reset_state(dec)
+  first, pos = [], []
+  t_pf = time.perf_counter()
+  for b, p in enumerate(prompts):
+    pre, real, _ = m._prefill_hidden(p)
+    hid = pre["prog"].read_output("hid")
+    first.append(int(np.argmax(m._logits(hid[real - 1]))))
+    m._seed_cache(dec, pre, real, slot=b)
+    pos.append(real)
+  torch.cuda.synchronize()
+  prefill_s = time.perf_counter() - t_pf
+  prog.set_input("tok", np.array(first, np.int32)); prog.set_input("pos", np.array(pos, np.int32))
+  stream = torch.cuda.ExternalStream(prog.stream(), device=dev)
+  for _ in range(args.warmup):
+    prog.execute_async()
+  prog.sync()
+  if ws > 1:
+    dist.barrier()
+  torch.cuda.synchronize()
+  e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+  with ClockSampler(local) as clk:
+    e0.record(stream)
+    for _ in range(args.steps):
+      prog.execute_async()
+    e1.record(stream)
+    prog.sync()
+  torch.cuda.synchronize()
+  ms = e0.elapsed_time(e1)
+  if ws > 1:
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    dist.barrier()
+  ms_step = ms / args.steps
+  tok_s = NB * args.steps * ws / (ms / 1e3)
+  launches_per_step = sum(1 for _ in dec["plan"].ops)
+
+  # ---- end-to-end through the public program API with host buffers: per step one H2D of the
+  # input token ids (pinned host -> tok port) and one D2H of the produced ids
+  host_tok = torch.empty(NB, dtype=torch.int32).pin_memory()
+  host_out = torch.empty(NB, dtype=torch.int32).pin_memory()
+  tok_dev = prog.tensor("tok", (NB,), "int32")
+  out_dev = prog.tensor("tok_out", (NB,), "int32")
+  host_tok.copy_(out_dev.cpu())
+  e2e_steps = max(8, args.steps // 2)
+  torch.cuda.synchronize()
+  t0 = time.perf_counter()
+  with torch.cuda.stream(stream):
+    for _ in range(e2e_steps):
+      tok_dev.copy_(host_tok, non_blocking=True)
+      prog.execute_async()
+      host_out.copy_(out_dev, non_blocking=True)
+      stream.synchronize()
+      host_tok.copy_(host_out)
+  e2e_s = time.perf_counter() - t0
+  e2e_tok_s = NB * e2e_steps * ws / e2e_s
+
+  # ---- dominant kernel: the fused gate|up int8 GEMV, timed alone on the program stream over the
+  # 32 layers' own weights (3.7 GB > L2, so every launch streams from HBM)
+  gu = [m._dev["layers"][i]["gu"] for i in range(cfg.n_layers)]
+  x = torch.randn(NB, cfg.dim, device=dev).half()
+  y = torch.empty(NB, cfg.ffn_dim, device=dev, dtype=torch.float16)
+  reps = 3 * cfg.n_layers
+  with torch.cuda.stream(stream):
+    for i in range(cfg.n_layers):
+      kernels.gemv(x, gu[i].w, gu[i].s, wf=R.W_I8, epi=R.EPI_SWIGLU, y=y)
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k0.record(stream)
+    for i in range(reps):
+      kernels.gemv(x, gu[i % cfg.n_layers].w, gu[i % cfg.n_layers].s, wf=R.W_I8, epi=R.EPI_SWIGLU, y=y)
+    k1.record(stream)
+  torch.cuda.synchronize()
+  k_us = k0.elapsed_time(k1) * 1e3 / reps
+  gu_bytes = gu[0].nbytes + NB * cfg.dim * 2 + NB * cfg.ffn_dim * 2
+  peak, peak_kind = _peaks()
+  step_bytes = algorithmic_bytes_per_step(cfg, NB, PROMPT + args.warmup + args.steps // 2)
+  result = None
+  if rank == 0:
+    achieved = gu_bytes / (k_us * 1e-6) / 1e9
+    result = {
+      "metric": METRIC, "value": round(tok_s, 2), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+      "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+      "vs_baseline": None, "dtype": "int8 weights, fp16 activations, fp32 accumulation", "data": "synthetic",
+      "config": {"workload": "BASELINE config 3: Llama-3-8B-shaped int8 greedy decode", "model": "llama-3-8b-shaped",
+                 "global_batch": NB * ws, "batch_per_gpu": NB, "seq_len": PROMPT, "decode_pos": f"{PROMPT}..{M}",
+                 "parallelism": f"replicas{ws}" if ws > 1 else "single",
+                 "l2": "weights 7.0 GB per step >> 126 MB L2 (no flush needed)"},
+      "e2e": {"value": round(e2e_tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * NB,
+              "d2h_bytes_per_step": 4 * NB,
+              "how": "program API, pinned host token ids in/out every step, host sync per step"},
+      "roofline": {"bound": "hbm", "kernel": "gemv int8 gate|up + silu*mul (28672x4096)", "achieved": round(achieved, 1),
+                   "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                   "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+                   "launch_us": round(k_us, 2), "algorithmic_bytes": gu_bytes},
+      "step_roofline": {"algorithmic_bytes": int(step_bytes), "achieved_gbs": round(step_bytes / (ms_step * 1e-3) / 1e9, 1),
+                        "frac": round(step_bytes / (ms_step * 1e-3) / 1e9 / peak, 4)},
+      "gpu_launches": launches_per_step * args.steps,
+      "clocks": clk.summary(),
+      "load_s": round(load_s, 2), "prefill_s": round(prefill_s, 3),
+    }
+  # torch objects that touched the program's stream go before the stream itself
+  del host_tok, host_out, tok_dev, out_dev, x, y, gu, stream
+  torch.cuda.synchronize()
+  import gc
+  gc.collect()
+  m.release()
+  if ws > 1:
+    dist.barrier()
+    dist.destroy_process_group()
+  return result
+
+
+def cpu_baseline(steps=3, layers=1):
+  """The reference path on the host: oracle decode of a `layers`-deep slice of the same model +
+  the full lm_head, scaled to 32 layers. Returns (tokens/s, description)."""
+  from oracle.model import OracleModel, Config, random_llama_weights
+  cfg = Config(dim=CFG["dim"], n_layers=layers, n_heads=CFG["n_heads"], n_kv_heads=CFG["n_kv_heads"],
+               ffn_dim=CFG["ffn_dim"], vocab=CFG["vocab"], rope_base=CFG["rope_base"])
+  w = random_llama_weights(cfg, seed=5)
+  w["embed"] = np.zeros((cfg.vocab, cfg.dim), np.float16)   # only gathered rows are read; values do not change the time
+  om = OracleModel(cfg, w, "int8", precision="device")
+  M = PROMPT + steps + 2
+  om._tables(M)
+  caches = om.new_caches(M)
+  rng = np.random.default_rng(1)
+  for Kc, Vc in caches:
+    Kc[:, :PROMPT] = rng.standard_normal(Kc[:, :PROMPT].shape, dtype=np.float32).astype(np.float16)
+    Vc[:, :PROMPT] = rng.standard_normal(Vc[:, :PROMPT].shape, dtype=np.float32).astype(np.float16)
+  tok = 7
+  om.decode_step(tok, PROMPT - 1, caches)                 # warm BLAS / page in
+  t_layers, t_head = 0.0, 0.0
+  for s in range(steps):
+    t0 = time.perf_counter()
+    hid = om.decode_step(tok, PROMPT + s, caches)
+    t1 = time.perf_counter()
+    tok = int(np.argmax(om.logits(hid.astype(np.float32))))
+    t2 = time.perf_counter()
+    t_layers += t1 - t0; t_head += t2 - t1
+  per_tok = t_layers / steps * (CFG["n_layers"] / layers) + t_head / steps
+  return 1.0 / per_tok, f"{steps} decode steps of a {layers}-layer slice + full lm_head, scaled to 32 layers"
+
+
+def blas_threads():
+  try:
+    from threadpoolctl import threadpool_info
+    return max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+  except Exception:
+    return os.cpu_count() or 1
+
+
+def main():
+  ap = argparse.ArgumentParser()
+  ap.add_argument("--gpus", type=int, default=1)
+  ap.add_argument("--steps", type=int, default=200)
+  ap.add_argument("--warmup", type=int, default=10)
+  ap.add_argument("--batch", type=int, default=1)
+  ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+  ap.add_argument("--no-cpu-baseline", action="store_true")
+  args = ap.parse_args()
+  ws, rank, _ = _dist()
+  if args.impl == "reference":
+    if rank != 0:
+      return
+    vals = []
+    for _ in range(max(1, min(args.steps, 3))):
+      v, how = cpu_baseline()
+      vals.append(v)
+    v = float(np.median(vals))
+    print(json.dumps({"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tokens/s",
+                      "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                      "scaling": "weak", "vs_baseline": None, "dtype": "int8 weights, fp32 numpy", "data": "synthetic",
+                      "config": {"workload": "BASELINE config 3: Llama-3-8B-shaped int8 greedy decode",
+                                 "global_batch": args.batch, "seq_len": PROMPT},
+                      "cpu_baseline": {"value": round(v, 4), "unit": "tokens/s", "cores": blas_threads(),
+                                       "kind": "port", "sample": how},
+                      "e2e": {"value": round(v, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                              "d2h_bytes_per_step": 0}}))
+    return
+  res = run_b200(args)
+  if rank == 0 and res is not None:
+    if not args.no_cpu_baseline and ws == 1:
+      v, how = cpu_baseline()
+      res["cpu_baseline"] = {"value": round(v, 4), "unit": "tokens/s", "cores": blas_threads(), "kind": "port",
+                             "sample": how}
+    print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+  main()

@@ -10,10 +10,11 @@ computes everything else in fp32. This oracle has two modes:
   * precision="fp32"   - fp16 at ports (program inputs/outputs, resident KV state), fp32 for every
                          internal node. Pinned against golden vectors from the reference's own
                          `LlamaPrefill` driving a numpy interpreter of its graph IR.
-  * precision="device" - the same, plus every activation operand of a matmul (`linear`, `bmm`,
-                         `bmm_weight`) rounded to fp16 first, which is what the fp16 device
-                         operands of the B200 kernels (and of the ANE) see. The GPU parity tests
-                         use this mode.
+  * precision="device" - the same, plus every activation operand of a matmul (`linear`,
+                         `bmm_weight`, and the q/K/V operands of attention's `bmm`s) rounded to fp16
+                         first, which is what the fp16 device operands of the B200 kernels (and of
+                         the ANE) see. Attention probabilities stay fp32. The GPU parity tests use
+                         this mode.
 
 Reference quirks restated here (each cites where the reference does it):
   * RMSNorm is `x / max(||x||_2, f16(sqrt(D*eps))) * f16(gamma*sqrt(D))` (`_compile.py:738-755`).
@@ -240,7 +241,8 @@ class OracleModel:
     for i in range(Sq):
       mask[i, n_valid(i):] = F32(np.float16(-1e4))
     p = softmax(sc + mask[None])
-    return np.einsum("hqk,hkd->hqd", self._mm_in(p), self._mm_in(Vr), dtype=F32).astype(F32)
+    # probabilities stay fp32: a flash-style kernel never materialises the normalised fp16 P
+    return np.einsum("hqk,hkd->hqd", p, self._mm_in(Vr), dtype=F32).astype(F32)
 
   def _mlp(self, L, h):
     if "moe" in L:
