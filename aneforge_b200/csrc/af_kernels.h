@@ -33,6 +33,31 @@ struct GemvArgs {
 };
 
 cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t st, bool pdl);
+
+// Tensor-core int8 GEMV over fragment-tile packed weights (gemv_tc.cu). Epilogues F32/F16/RESID/SWIGLU.
+struct GemvTcArgs {
+  int epi = EPI_F32;
+  const __half* x = nullptr;   // [NB][ldx] fp16, ldx % 8 == 0
+  int ldx = 0;
+  const void* w = nullptr;     // pack_i8_tiles layout
+  const __half* scale = nullptr;   // [N] per-row
+  const __half* bias = nullptr;
+  void* y = nullptr;
+  int ldy = 0;
+  int N = 0, K = 0, NB = 1;
+  void* scratch = nullptr;     // split-K partials + counters (gemv_tc_scratch_bytes); zero before first use
+  size_t scratch_bytes = 0;
+  int* err = nullptr;          // device error word (AF_DEV_WAIT_TIMEOUT if a pipeline wait gives up)
+  // set by the launcher
+  int Np = 0, Kp = 0, S = 1, maxc = 1;
+  float* part = nullptr;
+  int* counters = nullptr;
+};
+cudaError_t gemv_tc_launch(const GemvTcArgs& a, cudaStream_t st, bool pdl);
+size_t gemv_tc_scratch_bytes(int N, int K, int NB);
+void gemv_tc_plan(int N, int K, int NB, int* S, int* NT);
+cudaError_t pack_i8_tiles(const int8_t* src, int N, int K, uint8_t* dst, cudaStream_t st);
+size_t pack_i8_tiles_bytes(int N, int K);
 int gemv_argmax_ctas(int wf, int N, int K, int NB);
 void gemv_argmax_scratch(int wf, int N, int K, int NB, size_t* slot_floats, size_t* counters);
 

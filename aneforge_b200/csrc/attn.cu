@@ -84,11 +84,50 @@ AF_DEV void load_row_f16(const __half* p, int lane, float (&f)[HeadLayout<DH>::E
   }
 }
 
+// Each warp walks its keys in batches of PB positions: all PB K rows and PB V rows of a batch are
+// loaded before any math (2*PB loads in flight per lane), the G*PB partial dot products are summed
+// across the warp with a transpose-reduce (each shuffle level halves the values a lane keeps, so 32
+// sums cost 31 shuffles instead of 160) and the online softmax then runs once per batch.
+template <int DH, int G>
+struct DecodeBatch {
+  static constexpr int PB = (32 / G) < 8 ? (32 / G) : 8;   // positions per batch
+  static constexpr int NV = G * PB;                         // dot products per batch (power of 2)
+  static constexpr int LOGNV = NV == 32 ? 5 : NV == 16 ? 4 : NV == 8 ? 3 : NV == 4 ? 2 : 1;
+  static constexpr int SHIFT = 5 - LOGNV;                   // lane L holds value index L >> SHIFT
+  static constexpr int GS = 32 / G;                         // lanes per head after the reduce
+};
+
+template <int NV>
+AF_DEV float transpose_reduce(float (&v)[NV], int lane) {
+  // level `off` keeps the lower or upper half of the remaining values and adds the partner's copy
+  int n = NV;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    if (n > 1) {
+      const bool upper = lane & off;
+#pragma unroll
+      for (int i = 0; i < NV / 2; ++i) {
+        if (i < n / 2) {
+          const float send = upper ? v[i] : v[i + n / 2];
+          const float keep = upper ? v[i + n / 2] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      }
+      n >>= 1;
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+    }
+  }
+  return v[0];
+}
+
 template <int DH, int G>
 __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
   using HL = HeadLayout<DH>;
+  using DB = DecodeBatch<DH, G>;
   constexpr int EPL = HL::EPL;
   constexpr int NW = 4;
+  constexpr int PB = DB::PB;
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool active = lane < HL::LANES;
@@ -160,34 +199,73 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
   const __half* kbase = a.kc + ((size_t)b * KV + kvh) * a.M * DH;
   const __half* vbase = a.vc + ((size_t)b * KV + kvh) * a.M * DH;
   const float c = a.kv_c;
-  for (int j = j0 + warp; j < j1; j += NW) {
-    float kf[EPL], vf[EPL];
-    if (j == pos) {
+  const int my_idx = lane >> DB::SHIFT;                 // value index this lane ends up holding
+  const int my_g = my_idx / PB, my_p = my_idx % PB;
+  const bool rep0 = (lane & ((1 << DB::SHIFT) - 1)) == 0;
+  for (int base = j0 + warp * PB; base < j1; base += NW * PB) {
+    float kf[PB][EPL], vf[PB][EPL];
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) {
-        kf[e] = active ? kn_s[lane * EPL + e] : 0.f;
-        vf[e] = active ? vn_s[lane * EPL + e] : 0.f;
+    for (int p = 0; p < PB; ++p) {
+      const int j = base + p;
+      const bool in_range = j < j1;                // keys past this CTA's range are zeros
+      if (in_range && j != pos) {
+        load_row_f16<DH>(kbase + (size_t)j * DH, lane, kf[p]);
+        load_row_f16<DH>(vbase + (size_t)j * DH, lane, vf[p]);
+      } else {
+        // the new key/value live in shared memory, written only by the CTA whose range holds pos
+        const bool nw = in_range && active;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          kf[p][e] = nw ? kn_s[lane * EPL + e] : 0.f;
+          vf[p][e] = nw ? vn_s[lane * EPL + e] : 0.f;
+        }
       }
-    } else {
-      load_row_f16<DH>(kbase + (size_t)j * DH, lane, kf);
-      load_row_f16<DH>(vbase + (size_t)j * DH, lane, vf);
     }
     if (a.expand) {
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) { kf[e] = round_f16(c * kf[e]); vf[e] = round_f16(c * vf[e]); }
+      for (int p = 0; p < PB; ++p)
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) { kf[p][e] = round_f16(c * kf[p][e]); vf[p][e] = round_f16(c * vf[p][e]); }
     }
+    float d[DB::NV];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int p = 0; p < PB; ++p) {
+        float sdot = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) sdot = fmaf(qr[g][e], kf[p][e], sdot);
+        d[g * PB + p] = sdot;
+      }
+    const float sc = transpose_reduce<DB::NV>(d, lane) * a.scale;
+    const bool valid = base + my_p < j1;
+    const float s = valid ? sc : -INFINITY;
+    // per-head tile max / sum over the head's lane group
+    float tmax = s;
+#pragma unroll
+    for (int off = DB::GS / 2; off >= 1; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
+    float mnew_mine = fmaxf(m[0], tmax);
+#pragma unroll
+    for (int g = 1; g < G; ++g) if (g == my_g) mnew_mine = fmaxf(m[g], tmax);
+    const float pe = valid ? expf(s - mnew_mine) : 0.f;
+    float tsum = rep0 ? pe : 0.f;
+#pragma unroll
+    for (int off = DB::GS / 2; off >= 1; off >>= 1) tsum += __shfl_xor_sync(0xffffffffu, tsum, off);
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      float s = 0.f;
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) s = fmaf(qr[g][e], kf[e], s);
-      s = warp_sum(s) * a.scale;
-      const float mn = fmaxf(m[g], s);
+      const float mg = __shfl_sync(0xffffffffu, tmax, g * DB::GS);
+      const float sg = __shfl_sync(0xffffffffu, tsum, g * DB::GS);
+      const float mn = fmaxf(m[g], mg);
       const float corr = expf(m[g] - mn);
-      const float p = expf(s - mn);
-      l[g] = l[g] * corr + p;
+      l[g] = l[g] * corr + sg;
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) acc[g][e] = fmaf(p, vf[e], acc[g][e] * corr);
+      for (int e = 0; e < EPL; ++e) acc[g][e] *= corr;
+#pragma unroll
+      for (int p = 0; p < PB; ++p) {
+        const float pp = __shfl_sync(0xffffffffu, pe, (g * PB + p) << DB::SHIFT);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[g][e] = fmaf(pp, vf[p][e], acc[g][e]);
+      }
       m[g] = mn;
     }
   }
@@ -203,7 +281,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
   const size_t pair = (size_t)b * KV + kvh;
   float* part = a.part + (pair * a.n_split + split) * G * (DH + 2);
   for (int i = threadIdx.x; i < G * DH; i += blockDim.x) {
-    const int g = i / DH, d = i - g * DH;
+    const int g = i / DH, dd = i - g * DH;
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][g]);
@@ -212,15 +290,15 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
 #pragma unroll
       for (int w = 0; w < NW; ++w) {
         const float f = expf(wm[w][g] - M);
-        num = fmaf(f, wacc[w][g][d], num);
+        num = fmaf(f, wacc[w][g][dd], num);
         den = fmaf(f, wl[w][g], den);
       }
     }
     if (a.n_split == 1) {
-      a.out[(size_t)b * a.ld_out + (size_t)(kvh * G + g) * DH + d] = f2h(num / den);
+      a.out[(size_t)b * a.ld_out + (size_t)(kvh * G + g) * DH + dd] = f2h(num / den);
     } else {
-      part[g * (DH + 2) + d] = num;
-      if (d == 0) { part[g * (DH + 2) + DH] = M; part[g * (DH + 2) + DH + 1] = den; }
+      __stcg(part + g * (DH + 2) + dd, num);
+      if (dd == 0) { __stcg(part + g * (DH + 2) + DH, M); __stcg(part + g * (DH + 2) + DH + 1, den); }
     }
   }
   if (a.n_split == 1) return;
@@ -232,19 +310,19 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
   __threadfence();
   const float* pp = a.part + pair * a.n_split * G * (DH + 2);
   for (int i = threadIdx.x; i < G * DH; i += blockDim.x) {
-    const int g = i / DH, d = i - g * DH;
+    const int g = i / DH, dd = i - g * DH;
     float M = -INFINITY;
-    for (int s = 0; s < a.n_split; ++s) M = fmaxf(M, __ldcg(pp + (s * G + g) * (DH + 2) + DH));
+    for (int sp = 0; sp < a.n_split; ++sp) M = fmaxf(M, __ldcg(pp + (sp * G + g) * (DH + 2) + DH));
     float num = 0.f, den = 0.f;
-    for (int s = 0; s < a.n_split; ++s) {
-      const float* q = pp + (s * G + g) * (DH + 2);
+    for (int sp = 0; sp < a.n_split; ++sp) {
+      const float* q = pp + (sp * G + g) * (DH + 2);
       const float ms = __ldcg(q + DH);
       if (ms == -INFINITY) continue;
       const float f = expf(ms - M);
-      num = fmaf(f, __ldcg(q + d), num);
+      num = fmaf(f, __ldcg(q + dd), num);
       den = fmaf(f, __ldcg(q + DH + 1), den);
     }
-    a.out[(size_t)b * a.ld_out + (size_t)(kvh * G + g) * DH + d] = f2h(num / den);
+    a.out[(size_t)b * a.ld_out + (size_t)(kvh * G + g) * DH + dd] = f2h(num / den);
   }
   if (threadIdx.x == 0) a.counters[pair] = 0;
 }

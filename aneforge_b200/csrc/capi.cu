@@ -89,6 +89,25 @@ int af_lm_head_argmax(int wf, const uint16_t* x, int ldx, const void* w, const u
   return rc_of(af::gemv_launch(a, static_cast<cudaStream_t>(stream), false), "af_lm_head_argmax");
 }
 
+int af_pack_i8_tiles(const int8_t* codes, int n, int k, uint8_t* tiles, void* stream) {
+  return rc_of(af::pack_i8_tiles(codes, n, k, tiles, static_cast<cudaStream_t>(stream)), "af_pack_i8_tiles");
+}
+
+size_t af_pack_i8_tiles_bytes(int n, int k) { return af::pack_i8_tiles_bytes(n, k); }
+
+size_t af_gemv_tc_scratch_bytes(int n, int k, int nb) { return af::gemv_tc_scratch_bytes(n, k, nb); }
+
+int af_gemv_tc(int epi, const uint16_t* x, int ldx, const void* tiles, const uint16_t* scales, const uint16_t* bias,
+               void* y, int ldy, int nb, int n, int k, void* scratch, size_t scratch_bytes, void* stream) {
+  af::GemvTcArgs a;
+  a.epi = epi;
+  a.x = reinterpret_cast<const __half*>(x); a.ldx = ldx;
+  a.w = tiles; a.scale = reinterpret_cast<const __half*>(scales); a.bias = reinterpret_cast<const __half*>(bias);
+  a.y = y; a.ldy = ldy; a.NB = nb; a.N = n; a.K = k;
+  a.scratch = scratch; a.scratch_bytes = scratch_bytes;
+  return rc_of(af::gemv_tc_launch(a, static_cast<cudaStream_t>(stream), false), "af_gemv_tc");
+}
+
 int af_rmsnorm(const void* x, int x_f16, int ldx, const uint16_t* g, float floor, uint16_t* out, int ldo, int nb,
                int d, void* stream) {
   return rc_of(af::rmsnorm_launch(x, x_f16, ldx, reinterpret_cast<const __half*>(g), floor,

@@ -1,0 +1,551 @@
+// K1: int8 per-row dequant GEMV for decode on B200 - a persistent, stream-K kernel that streams the
+// weights through a TMA (cp.async.bulk) shared-memory ring and multiplies on the tensor cores.
+//
+// Why this shape. The GEMV is bound by HBM: every weight byte is read once per decode step. Keeping
+// ~6.5 TB/s in flight needs tens of KB of outstanding loads per SM, more than registers can hold at
+// useful occupancy, so one producer thread per CTA issues 8 KB bulk copies into a 6-stage ring
+// (tracked by mbarriers, 4 CTAs per SM: ~190 KB in flight per SM); four consumer warps per CTA read
+// their 16-byte A fragments from shared memory,
+// dequantise them (a byte permute places each int8 code under the fp16 exponent of 1024, one half2
+// subtract removes the bias - exact for every code) and run mma.sync m16n8k16 (fp16 x fp16 ->
+// fp32). The batch (1..16 sequences) is the MMA's N dimension, so batching adds no weight traffic.
+//
+// Weight layout (pack_i8_tiles): a 16-row x 32-column tile is 512 bytes; lane l owns bytes
+// [16l, 16l+16) = its A fragment for the tile's two k-steps:
+//   bytes [8s .. 8s+7] (k-step s): (g,2t) (g,2t+1) (g+8,2t) (g+8,2t+1) (g,2t+8) (g,2t+9) (g+8,2t+8) (g+8,2t+9)
+// with g = l/4, t = l%4. Tiles are grouped [row block of 64 rows][k tile][4 row tiles][512 B].
+//
+// Work split (stream-K): the RB x KT "units" (one k tile of one row block = 2 KB) are cut into one
+// contiguous range per CTA of a persistent grid, so every CTA streams the same number of bytes from
+// one contiguous address range. A row block covered by a single CTA gets its epilogue directly; a
+// row block shared by n CTAs (at most two per CTA: its first and last) is finished by the CTA that
+// takes the last ticket, which adds the n fp32 partials in CTA order - deterministic. x is
+// bulk-copied per chunk (<= 16 k tiles) into a 2-slot ring by the producer, after the programmatic
+// launch wait; the first chunk's weights are requested before that wait.
+//
+// Epilogues: F32 / F16 / RESID (y += ..) / SWIGLU (tiles hold 8 gate rows then the matching 8 up).
+// Every mbarrier wait is bounded: on timeout the kernel records AF_DEV_WAIT_TIMEOUT in the error
+// word, consumers leave together after a barrier, and the producer waits (bounded) for the copies
+// it issued before its thread exits.
+#include <cstdlib>
+
+#include "af_common.cuh"
+#include "af_kernels.h"
+
+namespace af {
+
+namespace tc {
+constexpr int WARPS = 4;                   // consumer warps = row tiles per row block
+constexpr int KS = 4;                      // k tiles per weight stage
+constexpr int TILE = 512;                  // bytes per 16x32 int8 tile
+constexpr int UNIT = WARPS * TILE;         // one k tile of one row block
+constexpr int STAGE_BYTES = KS * UNIT;     // 8 KB
+constexpr int STAGES = 6;
+constexpr int XKT = 16;                    // k tiles per x chunk
+constexpr int XSTRIDE = XKT * 32 + 8;      // halves per staged x row (+8: conflict-free B loads)
+constexpr int XSLOTS = 2;
+constexpr size_t CNT_BYTES = 16384;        // scratch: per-row-block tickets, then partial slots
+constexpr long long WAIT_LIMIT = 1ll << 26;
+}  // namespace tc
+
+AF_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+AF_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+AF_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+
+AF_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {   // bounded
+  for (long long i = 0; i < tc::WAIT_LIMIT; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+AF_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+AF_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// 1-D bulk copy global -> this CTA's shared memory (no multicast), completion counted on `bar`
+AF_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+AF_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(tc::WARPS * 32) : "memory"); }
+
+AF_DEV void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// 4 int8 codes (bytes of w) -> two half2: (byte0, byte1) and (byte2, byte3), exact.
+AF_DEV void i8x4_to_h2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;                        // b + 128 as an unsigned byte
+  const uint32_t blo = __byte_perm(u, 0x64646464u, 0x5140);  // fp16 bits 0x64uu = 1024 + u
+  const uint32_t bhi = __byte_perm(u, 0x64646464u, 0x7362);
+  const __half2 bias = __half2half2(__ushort_as_half(0x6480));  // 1152 = 1024 + 128
+  __half2 l = __hsub2(*reinterpret_cast<const __half2*>(&blo), bias);
+  __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&bhi), bias);
+  lo = *reinterpret_cast<uint32_t*>(&l);
+  hi = *reinterpret_cast<uint32_t*>(&h);
+}
+
+struct TcShared {
+  uint64_t full[tc::STAGES];
+  uint64_t empty[tc::STAGES];
+  uint64_t xfull[tc::XSLOTS];
+  uint64_t xempty[tc::XSLOTS];
+  int ticket;
+  int cabort;   // a consumer gave up: written by consumers only, read after a consumer barrier
+};
+constexpr int SH_BYTES = 256;
+static_assert(sizeof(TcShared) <= SH_BYTES, "TcShared grew past its slot");
+
+// ---- stream-K geometry (identical on host and device)
+AF_DEV long long unit_begin(int c, long long U, int G) { return (long long)c * U / G; }
+
+// the CTA whose range holds unit u
+AF_DEV int owner_of(long long u, long long U, int G) {
+  int c = (int)((u * G) / U);
+  while (c + 1 < G && unit_begin(c + 1, U, G) <= u) ++c;
+  while (c > 0 && unit_begin(c, U, G) > u) --c;
+  return c;
+}
+
+template <int NT, int EPI>
+AF_DEV void epilogue(const GemvTcArgs& a, float (&acc)[NT][4], int rt, int g, int t) {
+  const int r0 = rt * 16 + g, r1 = r0 + 8;
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int b = n * 8 + 2 * t + h;
+      if (b >= a.NB) continue;
+      const float v0 = acc[n][h], v1 = acc[n][2 + h];
+      if (EPI == EPI_SWIGLU) {
+        if (r1 >= a.N) continue;
+        float gv = __fmul_rn(v0, h2f(a.scale[r0]));
+        float uv = __fmul_rn(v1, h2f(a.scale[r1]));
+        if (a.bias) { gv = __fadd_rn(gv, h2f(a.bias[r0])); uv = __fadd_rn(uv, h2f(a.bias[r1])); }
+        reinterpret_cast<__half*>(a.y)[(size_t)b * a.ldy + rt * 8 + g] = f2h(silu_f(gv) * uv);
+      } else {
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          const int row = rr ? r1 : r0;
+          if (row >= a.N) continue;
+          float v = __fmul_rn(rr ? v1 : v0, h2f(a.scale[row]));
+          if (a.bias) v = __fadd_rn(v, h2f(a.bias[row]));
+          const size_t o = (size_t)b * a.ldy + row;
+          if (EPI == EPI_F32) reinterpret_cast<float*>(a.y)[o] = v;
+          else if (EPI == EPI_F16) reinterpret_cast<__half*>(a.y)[o] = f2h(v);
+          else if (EPI == EPI_RESID)
+            reinterpret_cast<float*>(a.y)[o] = __ldcg(reinterpret_cast<const float*>(a.y) + o) + v;
+        }
+      }
+    }
+  }
+}
+
+template <int NT, int EPI>
+__global__ void __launch_bounds__((tc::WARPS + 1) * 32) gemv_tc_kernel(GemvTcArgs a) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  unsigned char* ring = smem_raw;                                          // [STAGES][STAGE_BYTES]
+  TcShared* sh = reinterpret_cast<TcShared*>(smem_raw + tc::STAGES * tc::STAGE_BYTES);
+  __half* xring = reinterpret_cast<__half*>(smem_raw + tc::STAGES * tc::STAGE_BYTES + SH_BYTES);
+  const int xslot_halves = a.NB * tc::XSTRIDE;                             // one x chunk
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KT = a.Kp / 32;
+  const int RB = a.Np / 64;
+  const long long U = (long long)RB * KT;
+  const int G = gridDim.x, c = blockIdx.x;
+  const long long u0 = unit_begin(c, U, G), u1 = unit_begin(c + 1, U, G);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < tc::STAGES; ++s) {
+      mbar_init(&sh->full[s], 1);
+      mbar_init(&sh->empty[s], tc::WARPS);
+    }
+    for (int s = 0; s < tc::XSLOTS; ++s) {
+      mbar_init(&sh->xfull[s], 1);
+      mbar_init(&sh->xempty[s], tc::WARPS);
+    }
+    sh->cabort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == tc::WARPS) {
+    // -------------------------------------------------------------- producer (one thread)
+    if (lane != 0) return;
+    const char* W = reinterpret_cast<const char*>(a.w);
+    int stage = 0, xs = 0;
+    uint32_t phase = 0, xphase = 0;
+    int in_flight = 0;
+    bool ok = true, waited = false;
+    // the first chunk's weights go out before the programmatic-launch wait (weights never change)
+    long long u = u0;
+    while (u < u1 && ok) {
+      const int rb = (int)(u / KT), kta = (int)(u % KT);
+      const int ktb = (int)min((long long)KT, kta + (u1 - u));
+      for (int kc = kta; kc < ktb && ok; kc += tc::XKT) {
+        const int kce = min(kc + tc::XKT, ktb);
+        int kt = kc;
+        if (!waited) {
+          // chunk 0: weights first, then wait for the producer kernel of x, then x
+          for (; kt < kce && in_flight < tc::STAGES; kt += tc::KS) {
+            const int nk = min(tc::KS, kce - kt);
+            mbar_arrive_expect_tx(&sh->full[stage], (uint32_t)nk * tc::UNIT);
+            bulk_g2s(ring + (size_t)stage * tc::STAGE_BYTES, W + ((size_t)rb * KT + kt) * tc::UNIT, nk * tc::UNIT,
+                     &sh->full[stage]);
+            ++in_flight;
+            if (++stage == tc::STAGES) { stage = 0; phase ^= 1; }
+          }
+          pdl_wait();
+          waited = true;
+        }
+        // x chunk [kc, kce) for every real batch row
+        if (!mbar_wait(&sh->xempty[xs], xphase ^ 1)) { ok = false; break; }
+        const uint32_t xbytes = (uint32_t)(kce - kc) * 32 * 2;
+        mbar_arrive_expect_tx(&sh->xfull[xs], xbytes * a.NB);
+        for (int b = 0; b < a.NB; ++b)
+          bulk_g2s(xring + (size_t)xs * xslot_halves + (size_t)b * tc::XSTRIDE, a.x + (size_t)b * a.ldx + (size_t)kc * 32,
+                   xbytes, &sh->xfull[xs]);
+        if (++xs == tc::XSLOTS) { xs = 0; xphase ^= 1; }
+        for (; kt < kce; kt += tc::KS) {
+          const int nk = min(tc::KS, kce - kt);
+          if (!mbar_wait(&sh->empty[stage], phase ^ 1)) { ok = false; break; }
+          mbar_arrive_expect_tx(&sh->full[stage], (uint32_t)nk * tc::UNIT);
+          bulk_g2s(ring + (size_t)stage * tc::STAGE_BYTES, W + ((size_t)rb * KT + kt) * tc::UNIT, nk * tc::UNIT,
+                   &sh->full[stage]);
+          in_flight = min(in_flight + 1, tc::STAGES);
+          if (++stage == tc::STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      u += ktb - kta;
+    }
+    if (!waited) pdl_wait();
+    if (!ok) af_set_err(a.err, AF_DEV_WAIT_TIMEOUT);
+    // shared memory must outlive every copy this thread issued: wait (bounded) for the last use of
+    // each weight stage and x slot to land before the thread exits
+    for (int i = 0; i < in_flight; ++i) {
+      if (--stage < 0) { stage = tc::STAGES - 1; phase ^= 1; }
+      mbar_wait(&sh->full[stage], phase);
+    }
+    for (int i = 0; i < tc::XSLOTS; ++i) {
+      if (--xs < 0) { xs = tc::XSLOTS - 1; xphase ^= 1; }
+      mbar_wait(&sh->xfull[xs], xphase);
+    }
+    return;
+  }
+
+  // ---------------------------------------------------------------- consumers (4 warps)
+  const int g = lane >> 2, t = lane & 3;
+  pdl_wait();
+  pdl_trigger();
+  int stage = 0, xs = 0;
+  uint32_t phase = 0, xphase = 0;
+  long long u = u0;
+  while (u < u1) {
+    const int rb = (int)(u / KT), kta = (int)(u % KT);
+    const int ktb = (int)min((long long)KT, kta + (u1 - u));
+    float acc[NT][4], acc2[NT][4];              // two independent MMA chains (even / odd k tiles)
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) { acc[n][q] = 0.f; acc2[n][q] = 0.f; }
+    bool stuck = false;
+    for (int kc = kta; kc < ktb && !stuck; kc += tc::XKT) {
+      const int kce = min(kc + tc::XKT, ktb);
+      if (!mbar_wait(&sh->xfull[xs], xphase)) { stuck = true; break; }
+      const __half* xsl = xring + (size_t)xs * xslot_halves;
+      for (int kt = kc; kt < kce; kt += tc::KS) {
+        const int nk = min(tc::KS, kce - kt);
+        if (!mbar_wait(&sh->full[stage], phase)) { stuck = true; break; }
+        const unsigned char* sbase = ring + (size_t)stage * tc::STAGE_BYTES + warp * tc::TILE + lane * 16;
+#pragma unroll
+        for (int kk = 0; kk < tc::KS; ++kk) {
+          if (kk >= nk) break;
+          const uint4 w = *reinterpret_cast<const uint4*>(sbase + kk * tc::UNIT);
+          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int st = 0; st < 2; ++st) {
+            uint32_t A[4];
+            i8x4_to_h2x2(wv[2 * st], A[0], A[1]);
+            i8x4_to_h2x2(wv[2 * st + 1], A[2], A[3]);
+            const int kb = (kt - kc + kk) * 32 + st * 16 + 2 * t;
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+              const bool real = n * 8 + g < a.NB;
+              const __half* xr = xsl + (size_t)(real ? n * 8 + g : 0) * tc::XSTRIDE + kb;
+              const uint32_t b0 = real ? *reinterpret_cast<const uint32_t*>(xr) : 0u;
+              const uint32_t b1 = real ? *reinterpret_cast<const uint32_t*>(xr + 8) : 0u;
+              if (kk & 1) mma_16816(acc2[n], A, b0, b1);
+              else mma_16816(acc[n], A, b0, b1);
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh->empty[stage]);
+        if (++stage == tc::STAGES) { stage = 0; phase ^= 1; }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh->xempty[xs]);
+      if (++xs == tc::XSLOTS) { xs = 0; xphase ^= 1; }
+    }
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[n][q] += acc2[n][q];
+    if (stuck) {
+      af_set_err(a.err, AF_DEV_WAIT_TIMEOUT);
+      *reinterpret_cast<volatile int*>(&sh->cabort) = 1;
+    }
+    const int rt = rb * tc::WARPS + warp;
+    if (kta == 0 && ktb == KT) {
+      // this CTA owns the whole row block
+      consumer_sync();
+      if (*reinterpret_cast<volatile int*>(&sh->cabort)) break;
+      epilogue<NT, EPI>(a, acc, rt, g, t);
+    } else {
+      // shared row block: partial to slot j, the last ticket holder reduces in CTA order
+      const int cf = owner_of((long long)rb * KT, U, G), cl = owner_of((long long)rb * KT + KT - 1, U, G);
+      const int nc = cl - cf + 1, j = c - cf;
+      constexpr int NBP = NT * 8;
+      float* slot = a.part + (((size_t)rb * a.maxc + j) * 64) * NBP;
+      const int r0 = warp * 16 + g, r1 = r0 + 8;
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const int c0 = n * 8 + 2 * t;
+        if (c0 >= a.NB) continue;
+        __stcg(reinterpret_cast<float2*>(slot + (size_t)r0 * NBP + c0), make_float2(acc[n][0], acc[n][1]));
+        __stcg(reinterpret_cast<float2*>(slot + (size_t)r1 * NBP + c0), make_float2(acc[n][2], acc[n][3]));
+      }
+      __threadfence();
+      consumer_sync();
+      if (*reinterpret_cast<volatile int*>(&sh->cabort)) break;
+      if (threadIdx.x == 0) sh->ticket = atomicAdd(a.counters + rb, 1) == nc - 1;
+      consumer_sync();
+      if (sh->ticket) {
+        __threadfence();
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+          const int c0 = n * 8 + 2 * t;
+          if (c0 >= a.NB) continue;
+          float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+          for (int jj = 0; jj < nc; ++jj) {
+            const float* sp = a.part + (((size_t)rb * a.maxc + jj) * 64) * NBP;
+            const float2 p = __ldcg(reinterpret_cast<const float2*>(sp + (size_t)r0 * NBP + c0));
+            const float2 q = __ldcg(reinterpret_cast<const float2*>(sp + (size_t)r1 * NBP + c0));
+            s0 += p.x; s1 += p.y; s2 += q.x; s3 += q.y;
+          }
+          acc[n][0] = s0; acc[n][1] = s1; acc[n][2] = s2; acc[n][3] = s3;
+        }
+        epilogue<NT, EPI>(a, acc, rt, g, t);
+        if (threadIdx.x == 0) a.counters[rb] = 0;
+      }
+    }
+    u += ktb - kta;
+  }
+}
+
+// ------------------------------------------------------------------------------------ host side
+
+static int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+static int env_int(const char* name, int dflt) {
+  const char* v = getenv(name);
+  return v && *v ? atoi(v) : dflt;
+}
+
+static size_t smem_bytes(int NB) {
+  return (size_t)tc::STAGES * tc::STAGE_BYTES + SH_BYTES + (size_t)tc::XSLOTS * NB * tc::XSTRIDE * 2;
+}
+
+template <int NT, int EPI>
+static int grid_for(int NB) {
+  static int occ[17] = {};
+  if (!occ[NB]) {
+    cudaFuncSetAttribute(gemv_tc_kernel<NT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes(16));
+    int o = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, gemv_tc_kernel<NT, EPI>, (tc::WARPS + 1) * 32,
+                                                      smem_bytes(NB)) != cudaSuccess || o < 1)
+      o = 1;
+    const int cap = env_int("AF_TC_CTAS_PER_SM", 4);
+    occ[NB] = o < cap ? o : cap;
+  }
+  return occ[NB] * sm_count();
+}
+
+static int grid_any(int NB, int epi) {
+  const bool two = NB > 8;
+  switch (epi) {
+    case EPI_F32: return two ? grid_for<2, EPI_F32>(NB) : grid_for<1, EPI_F32>(NB);
+    case EPI_F16: return two ? grid_for<2, EPI_F16>(NB) : grid_for<1, EPI_F16>(NB);
+    case EPI_RESID: return two ? grid_for<2, EPI_RESID>(NB) : grid_for<1, EPI_RESID>(NB);
+    default: return two ? grid_for<2, EPI_SWIGLU>(NB) : grid_for<1, EPI_SWIGLU>(NB);
+  }
+}
+
+// Stream-K geometry on the host: grid G (all resident), units U = RB*KT, the largest number of CTAs
+// sharing one row block (`maxc`, partial slots per row block).
+static void plan_geometry(int N, int K, int NB, int epi, int* G, int* maxc) {
+  static const long long min_bytes = 1024ll * env_int("AF_TC_MIN_KB", 96);
+  const long long RB = (N + 63) / 64, KT = (K + 31) / 32;
+  const long long U = RB * KT;
+  long long g = grid_any(NB, epi);
+  // every CTA pays a fixed ramp (barrier setup, first-copy latency) and, on a shared row block, a
+  // ticket: give each at least `min_bytes` of weights so those costs stay small against streaming
+  const long long by_bytes = (U * tc::UNIT + min_bytes - 1) / min_bytes;
+  if (g > by_bytes) g = by_bytes;
+  if (g > U) g = U;
+  if (g < 1) g = 1;
+  *G = (int)g;
+  const long long per = U / g;                       // a CTA holds >= per units
+  *maxc = (int)((KT + per - 1) / (per > 0 ? per : 1)) + 1;
+}
+
+void gemv_tc_plan(int N, int K, int NB, int* S_out, int* nt_out) {
+  int G, maxc;
+  plan_geometry(N, K, NB > 16 ? 16 : NB, EPI_F32, &G, &maxc);
+  *S_out = maxc;
+  *nt_out = NB <= 8 ? 1 : 2;
+}
+
+size_t gemv_tc_scratch_bytes(int N, int K, int NB) {
+  const int nb = NB > 16 ? 16 : NB;
+  int G = 0, maxc = 0;
+  plan_geometry(N, K, nb, EPI_F32, &G, &maxc);
+  const int NT = nb <= 8 ? 1 : 2;
+  const size_t RB = (N + 63) / 64;
+  return tc::CNT_BYTES + RB * maxc * 64 * NT * 8 * 4;
+}
+
+template <int NT, int EPI>
+static cudaError_t launch_tc(GemvTcArgs a, cudaStream_t st, bool pdl) {
+  int G = 0, maxc = 0;
+  plan_geometry(a.N, a.K, a.NB, EPI, &G, &maxc);
+  a.maxc = maxc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(G);
+  cfg.blockDim = dim3((tc::WARPS + 1) * 32);
+  cfg.dynamicSmemBytes = smem_bytes(a.NB);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gemv_tc_kernel<NT, EPI>, a);
+}
+
+static cudaError_t gemv_tc_launch16(GemvTcArgs a, cudaStream_t st, bool pdl);
+
+// Batches above 16 run as 16-row slices of x (the weights stream once per slice).
+cudaError_t gemv_tc_launch(const GemvTcArgs& a0, cudaStream_t st, bool pdl) {
+  if (a0.NB < 1) return cudaErrorInvalidValue;
+  for (int b0 = 0; b0 < a0.NB; b0 += 16) {
+    GemvTcArgs a = a0;
+    a.NB = a0.NB - b0 < 16 ? a0.NB - b0 : 16;
+    a.x = a0.x + (size_t)b0 * a0.ldx;
+    const size_t esz = (a0.epi == EPI_F16 || a0.epi == EPI_SWIGLU) ? 2 : 4;
+    a.y = static_cast<char*>(a0.y) + (size_t)b0 * a0.ldy * esz;
+    cudaError_t e = gemv_tc_launch16(a, st, pdl && b0 == 0);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+static cudaError_t gemv_tc_launch16(GemvTcArgs a, cudaStream_t st, bool pdl) {
+  if (a.NB < 1 || a.NB > 16 || a.N <= 0 || a.K <= 0) return cudaErrorInvalidValue;
+  if (a.K % 32 || a.ldx % 8) return cudaErrorInvalidValue;            // whole x chunks, 16-byte rows
+  if (a.epi == EPI_SWIGLU && a.N % 16) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(a.w) & 15) || (reinterpret_cast<uintptr_t>(a.x) & 15)) return cudaErrorInvalidValue;
+  a.Np = (a.N + 63) / 64 * 64;
+  a.Kp = a.K;
+  const size_t RB = a.Np / 64;
+  if (RB * 4 > tc::CNT_BYTES) return cudaErrorInvalidValue;
+  if (!a.scratch || a.scratch_bytes < gemv_tc_scratch_bytes(a.N, a.K, a.NB)) return cudaErrorInvalidValue;
+  a.counters = reinterpret_cast<int*>(a.scratch);
+  a.part = reinterpret_cast<float*>(static_cast<char*>(a.scratch) + tc::CNT_BYTES);
+  cudaError_t e = cudaErrorInvalidValue;
+  const bool two = a.NB > 8;
+#define AF_TC_CASE(EPIV) \
+  if (a.epi == EPIV) e = two ? launch_tc<2, EPIV>(a, st, pdl) : launch_tc<1, EPIV>(a, st, pdl);
+  AF_TC_CASE(EPI_F32)
+  AF_TC_CASE(EPI_F16)
+  AF_TC_CASE(EPI_RESID)
+  AF_TC_CASE(EPI_SWIGLU)
+#undef AF_TC_CASE
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+// row-major int8 codes [N][K] -> [Np/64][Kp/32][4 row tiles][32 lanes][16 B], zero padded
+__global__ void pack_i8_tiles_kernel(const int8_t* src, int N, int K, uint8_t* dst, int Np, int Kp) {
+  const size_t total = (size_t)(Np / 16) * (Kp / 32) * 32;
+  const int KT = Kp / 32;
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total; idx += (size_t)gridDim.x * blockDim.x) {
+    const int lane = (int)(idx & 31);
+    const size_t q = idx >> 5;                    // (rb, kt, w) flattened
+    const int w = (int)(q % tc::WARPS);
+    const size_t rk = q / tc::WARPS;
+    const int kt = (int)(rk % KT);
+    const int rb = (int)(rk / KT);
+    const int rt = rb * tc::WARPS + w;
+    const int g = lane >> 2, t = lane & 3;
+    uint8_t out[16];
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const int kb = kt * 32 + s * 16;
+      const int rows[8] = {g, g, g + 8, g + 8, g, g, g + 8, g + 8};
+      const int cols[8] = {2 * t, 2 * t + 1, 2 * t, 2 * t + 1, 2 * t + 8, 2 * t + 9, 2 * t + 8, 2 * t + 9};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int r = rt * 16 + rows[j], c = kb + cols[j];
+        out[8 * s + j] = (r < N && c < K) ? (uint8_t)src[(size_t)r * K + c] : 0;
+      }
+    }
+    uint4 v;
+    memcpy(&v, out, 16);
+    reinterpret_cast<uint4*>(dst)[idx] = v;
+  }
+}
+
+cudaError_t pack_i8_tiles(const int8_t* src, int N, int K, uint8_t* dst, cudaStream_t st) {
+  const int Np = (N + 63) / 64 * 64, Kp = (K + 31) / 32 * 32;
+  const size_t total = (size_t)(Np / 16) * (Kp / 32) * 32;
+  unsigned blocks = (unsigned)((total + 255) / 256);
+  if (blocks > 65535u * 8) blocks = 65535u * 8;
+  pack_i8_tiles_kernel<<<blocks, 256, 0, st>>>(src, N, K, dst, Np, Kp);
+  return cudaGetLastError();
+}
+
+size_t pack_i8_tiles_bytes(int N, int K) {
+  return (size_t)((N + 63) / 64 * 64) * ((K + 31) / 32 * 32);
+}
+
+}  // namespace af

@@ -111,3 +111,36 @@ def attn_decode(qkv, kc, vc, pos, cos_t, sin_t, H, KV, dh, scale, kv_c=1.0, expa
                                  out.stride(0), NB, H, KV, dh, M, n_split, float(scale), float(kv_c), int(expand),
                                  _p(scratch), nbytes, _p(err), _stream(qkv)), "af_attn_decode")
   return out
+
+
+def pack_i8_tiles(q):
+  """Per-row int8 codes [N, K] -> the tensor-core fragment-tile layout (uint8, flat)."""
+  import torch
+  N, K = q.shape
+  L = R.lib()
+  out = torch.empty((L.af_pack_i8_tiles_bytes(N, K),), dtype=torch.uint8, device=q.device)
+  R.check(L.af_pack_i8_tiles(_p(q), N, K, _p(out), _stream(q)), "af_pack_i8_tiles")
+  return out
+
+
+def gemv_tc_scratch(N, K, NB, device):
+  import torch
+  n = R.load_library().af_gemv_tc_scratch_bytes(N, K, NB)
+  return torch.zeros((max(n, 1),), dtype=torch.uint8, device=device), n
+
+
+def gemv_tc(x, tiles, scales, N, K, bias=None, epi=R.EPI_F32, y=None, scratch=None):
+  """Tensor-core int8 GEMV over packed tiles. x [NB, K] fp16."""
+  import torch
+  NB = x.shape[0]
+  cols = N // 2 if epi == R.EPI_SWIGLU else N
+  if y is None:
+    dt = torch.float16 if epi in (R.EPI_F16, R.EPI_SWIGLU) else torch.float32
+    y = torch.zeros((NB, cols), dtype=dt, device=x.device)
+  if scratch is None:
+    scratch, nbytes = gemv_tc_scratch(N, K, NB, x.device)
+  else:
+    nbytes = scratch.numel()
+  R.check(R.lib().af_gemv_tc(epi, _p(x), x.stride(0), _p(tiles), _p(scales), _p(bias), _p(y), y.stride(0), NB, N, K,
+                             _p(scratch), nbytes, _stream(x)), "af_gemv_tc")
+  return y

@@ -4,9 +4,11 @@
   so a warp streams 512 contiguous bytes.
 * int4 group-32: packed [N][K/2] (element 2i in the low nibble) + fp16 scales [N][K/32]; one 16-byte
   load is exactly one group.
+* int8 on the tensor-core GEMV: the per-row codes are re-packed into 16x32 fragment tiles
+  (csrc/gemv_tc.cu) so each lane's 16-byte load is exactly its mma.sync A fragment.
 * Fused projections: q|k|v rows are concatenated (one GEMV over the shared normalised input); gate
-  and up rows are interleaved in blocks of SWIGLU_BLOCK rows (4 gate rows, then the 4 matching up
-  rows) so one CTA row-block produces silu(gate)*up for 4 outputs in its epilogue.
+  and up rows are interleaved in blocks (4+4 rows for the CUDA-core GEMV, 8+8 rows = one 16-row
+  tile for the tensor-core GEMV) so the epilogue produces silu(gate)*up from rows it already holds.
 
 Packers accept numpy arrays or torch tensors (on any device) and return the same kind.
 """
@@ -14,8 +16,9 @@ from __future__ import annotations
 
 import numpy as np
 
-SWIGLU_BLOCK = 8          # rows per gate/up block in the packed matrix (must match gemv.cu)
+SWIGLU_BLOCK = 8          # rows per gate/up block for the CUDA-core GEMV (must match gemv.cu)
 SWIGLU_HALF = SWIGLU_BLOCK // 2
+SWIGLU_HALF_TC = 8        # the tensor-core GEMV: each 16-row tile = 8 gate rows + 8 up rows (gemv_tc.cu)
 
 
 def _cat(parts, like):

@@ -107,9 +107,15 @@ def rope_tables(seq: int, dh: int, base: float = 10000.0, rotary_dim: int = 0, i
 # NB, M; `lw` is the layer's packed device weights (names of bound buffers, see _bind_layer).
 
 def _emit_linear(pb, ctx, name, lin: DevLinear, x, y, epi, nb=None):
-  kv = dict(wf=lin.wf, epi=epi, x=x, w=f"{name}.w", y=y, nb=nb or ctx["NB"], n=lin.N, k=lin.K)
+  nb = nb or ctx["NB"]
+  kv = dict(wf=lin.wf, epi=epi, x=x, w=f"{name}.w", y=y, nb=nb, n=lin.N, k=lin.K)
   if lin.kind == "int8":
     kv["s"] = f"{name}.s"
+  if lin.kind == "int8" and lin.tiled:
+    nbytes = R.load_library().af_gemv_tc_scratch_bytes(lin.N, lin.K, nb)
+    if nbytes:
+      pb.buf("gemv.scr", nbytes, "scratch")          # one split-K scratch shared by every GEMV
+      kv["scr"] = "gemv.scr"
   elif lin.kind == "int4_g32":
     kv["gs"] = f"{name}.s"
   if lin.bias is not None:
@@ -287,8 +293,9 @@ class LlamaPrefill:
   def _ctx(self, NB, M):
     cfg, d = self.cfg, self._load()
     G = cfg.n_heads // cfg.n_kv_heads
-    # split-K over the cache: enough CTAs to cover the SMs for short batches, one split per 64 keys
-    nsplit = max(1, min(64, (M + 63) // 64, (4 * 148) // max(1, cfg.n_kv_heads * NB)))
+    # split-K over the cache: ~2 CTAs per SM in total, each split at least 32 keys (one batch of
+    # 8 keys per warp), at most 64 splits (the last CTA merges them)
+    nsplit = max(1, min(64, (M + 31) // 32, -(-(2 * 148) // max(1, cfg.n_kv_heads * NB))))
     return {"NB": NB, "M": M, "nsplit": nsplit, "scale": d["scale"], "kvc": d["kvc"], "expand": G > 1 and d["kvc"] != 1.0}
 
   # -- programs

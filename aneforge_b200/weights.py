@@ -49,10 +49,13 @@ class DevLinear:
   bias: object         # [N] fp16 or None
   N: int
   K: int
+  tiled: bool = False  # int8 in tensor-core fragment tiles (K % 32 == 0) vs row-major
 
   @property
   def wf(self) -> str:
-    return {"int8": "i8", "fp16": "f16", "int4_g32": "i4"}[self.kind]
+    if self.kind == "int8":
+      return "i8t" if self.tiled else "i8"
+    return {"fp16": "f16", "int4_g32": "i4"}[self.kind]
 
   @property
   def nbytes(self) -> int:
@@ -109,8 +112,9 @@ def encode_linear(parts, compress, device, biases=None, swiglu=False, atol=0.05,
   enc = [_quantize(P, kind, device) for P in parts]
   if swiglu:
     (wg, sg), (wu, su) = enc
-    w = layout.interleave_blocks(wg, wu)
-    s = None if sg is None else layout.interleave_blocks(sg, su)
+    half = layout.SWIGLU_HALF_TC if kind == "int8" else layout.SWIGLU_HALF
+    w = layout.interleave_blocks(wg, wu, half)
+    s = None if sg is None else layout.interleave_blocks(sg, su, half)
   else:
     w = torch.cat([e[0] for e in enc], 0) if len(enc) > 1 else enc[0][0]
     s = None if enc[0][1] is None else (torch.cat([e[1] for e in enc], 0) if len(enc) > 1 else enc[0][1])
@@ -124,7 +128,17 @@ def encode_linear(parts, compress, device, biases=None, swiglu=False, atol=0.05,
       cols.append(torch.zeros(int(P.shape[0]), dtype=torch.float16, device=device) if x is None
                   else to_device(x, device).float().half())
     b = torch.cat(cols, 0).contiguous()
-  return DevLinear(kind, w.contiguous(), None if s is None else s.contiguous(), b, N, K)
+  tiled = False
+  if kind == "int8" and K % 32 == 0:
+    from . import kernels
+    w = kernels.pack_i8_tiles(w.contiguous())          # tensor-core fragment tiles
+    tiled = True
+  elif kind == "int8" and swiglu:
+    # the CUDA-core GEMV pairs gate/up rows in blocks of 4: re-interleave at that granularity
+    g, u = enc[0][0], enc[1][0]
+    w = layout.interleave_blocks(g, u, layout.SWIGLU_HALF)
+    s = layout.interleave_blocks(enc[0][1], enc[1][1], layout.SWIGLU_HALF)
+  return DevLinear(kind, w.contiguous(), None if s is None else s.contiguous(), b, N, K, tiled)
 
 
 def rms_weights(gamma, eps, device):

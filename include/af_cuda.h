@@ -126,6 +126,17 @@ int af_quantize_g32_i4(const void* src, int src_f16, int n, int k, uint8_t* pack
 int af_gemv(int wf, int epi, const uint16_t* x, int ldx, const void* w, const uint16_t* scales,
             const uint16_t* bias, void* y, int ldy, int nb, int n, int k, void* stream);
 
+/* Tensor-core int8 GEMV (the decode K1 kernel): weights re-packed once into 16x32 fragment tiles
+ * (af_pack_i8_tiles, [ceil(n/16)][ceil(k/32)][512 B]) from per-row int8 codes [n][k]; same epilogues as
+ * af_gemv (AF_EPI_SWIGLU tiles hold 8 gate rows then the 8 matching up rows). Replaces the same
+ * reference `matmul` (_compile.py:375-385). Scratch (split-K partials + counters):
+ * af_gemv_tc_scratch_bytes, zero before the first call, left zeroed; 0 bytes needs no scratch. */
+size_t af_pack_i8_tiles_bytes(int n, int k);
+int af_pack_i8_tiles(const int8_t* codes, int n, int k, uint8_t* tiles, void* stream);
+size_t af_gemv_tc_scratch_bytes(int n, int k, int nb);
+int af_gemv_tc(int epi, const uint16_t* x, int ldx, const void* tiles, const uint16_t* scales, const uint16_t* bias,
+               void* y, int ldy, int nb, int n, int k, void* scratch, size_t scratch_bytes, void* stream);
+
 /* lm_head GEMV + greedy argmax (lowest index on ties): replaces the host `hidden @ lm_head.T` and
  * np.argmax of LlamaPrefill._logits/_sample (aneforge/llm.py:349-355, :407-410). `logits` [nb][n]
  * may be NULL; `pos_advance` (may be NULL) is incremented per row. Scratch: see _scratch; it must be

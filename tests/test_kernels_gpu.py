@@ -193,13 +193,14 @@ def _attn_ref(qkv, Kc, Vc, pos, cos, sin, H, KV, dh, kv_c, expand):
   return np.einsum("hk,hkd->hd", p, Vr).reshape(-1).astype(F16), k.astype(F16), v.astype(F16)
 
 
-@pytest.mark.parametrize("dh,H,KV", [(128, 32, 8), (128, 16, 4), (64, 8, 8), (32, 4, 1), (16, 4, 2)])
-@pytest.mark.parametrize("n_split", [1, 4, 16])
+@pytest.mark.parametrize("dh,H,KV", [(128, 32, 8), (128, 16, 4), (64, 8, 8), (64, 8, 2), (64, 16, 2), (32, 4, 1),
+                                     (16, 4, 2)])
+@pytest.mark.parametrize("n_split", [1, 2, 4, 16])
 @pytest.mark.parametrize("expand", [False, True])
 def test_attn_decode(K, dh, H, KV, n_split, expand):
   rng = np.random.default_rng(dh + H + n_split)
-  NB, M = 2, 300
-  pos_h = np.array([257, 3], np.int32)
+  NB, M = 3, 300
+  pos_h = np.array([257, 3, 16], np.int32)
   Kc = rng.standard_normal((NB, KV, M, dh), dtype=F32).astype(F16)
   Vc = rng.standard_normal((NB, KV, M, dh), dtype=F32).astype(F16)
   qkv = rng.standard_normal((NB, (H + 2 * KV) * dh), dtype=F32)
@@ -218,3 +219,58 @@ def test_attn_decode(K, dh, H, KV, n_split, expand):
     assert np.array_equal(kc_h[b][:, p], kn) and np.array_equal(vc_h[b][:, p], vn)
     untouched = np.ones(M, bool); untouched[p] = False
     assert np.array_equal(kc_h[b][:, untouched], Kc[b][:, untouched])
+
+
+@pytest.mark.parametrize("NB", [1, 2, 3, 8, 9, 16, 40])
+@pytest.mark.parametrize("N,Kd", [(16, 32), (37, 64), (520, 2048), (300, 3584), (6144, 4096), (4096, 14336)])
+def test_gemv_tensor_core_int8(K, NB, N, Kd):
+  from aneforge_b200 import _runtime as R
+  rng = np.random.default_rng(NB * 7 + N)
+  W = (rng.standard_normal((N, Kd), dtype=F32) * F32(0.02)).astype(F16)
+  x = rng.standard_normal((NB, Kd), dtype=F32).astype(F16)
+  bias = (rng.standard_normal(N, dtype=F32) * F32(0.1)).astype(F16)
+  qr, sr = Q.quantize_per_row(W)
+  tiles = K.pack_i8_tiles(cuda(qr))
+  ref = (x.astype(F32) @ qr.astype(F32).T) * sr.astype(F32) + bias.astype(F32)
+  y = K.gemv_tc(cuda(x), tiles, cuda(sr), N, Kd, bias=cuda(bias), epi=R.EPI_F32).cpu().numpy()
+  assert np.abs(y - ref).max() <= 1e-4 * np.abs(ref).max() + 1e-5
+  y0 = rng.standard_normal((NB, N), dtype=F32)
+  yr = torch.from_numpy(y0.copy()).cuda()
+  K.gemv_tc(cuda(x), tiles, cuda(sr), N, Kd, bias=cuda(bias), epi=R.EPI_RESID, y=yr)
+  assert np.abs(yr.cpu().numpy() - (y0 + ref)).max() <= 1e-4 * np.abs(y0 + ref).max()
+  y16 = K.gemv_tc(cuda(x), tiles, cuda(sr), N, Kd, bias=cuda(bias), epi=R.EPI_F16).cpu().numpy()
+  assert np.abs(y16.astype(F32) - ref).max() <= 2 ** -10 * np.abs(ref).max() + 1e-4
+
+
+@pytest.mark.parametrize("NB", [1, 5, 16])
+def test_gemv_tensor_core_swiglu(K, NB):
+  from aneforge_b200 import _runtime as R
+  from aneforge_b200.layout import interleave_blocks, SWIGLU_HALF_TC
+  rng = np.random.default_rng(15)
+  F, Kd = 96, 512
+  Wg = (rng.standard_normal((F, Kd), dtype=F32) * F32(0.05)).astype(F16)
+  Wu = (rng.standard_normal((F, Kd), dtype=F32) * F32(0.05)).astype(F16)
+  x = rng.standard_normal((NB, Kd), dtype=F32).astype(F16)
+  qg, sg = Q.quantize_per_row(Wg); qu, su = Q.quantize_per_row(Wu)
+  qp = interleave_blocks(qg, qu, SWIGLU_HALF_TC); sp = interleave_blocks(sg, su, SWIGLU_HALF_TC)
+  y = K.gemv_tc(cuda(x), K.pack_i8_tiles(cuda(qp)), cuda(sp), 2 * F, Kd, epi=R.EPI_SWIGLU).cpu().numpy()
+  xf = x.astype(F32)
+  g = (xf @ qg.astype(F32).T) * sg.astype(F32); u = (xf @ qu.astype(F32).T) * su.astype(F32)
+  ref = OM.silu(g) * u
+  assert relerr(y.astype(F32), ref) < 2e-3 and cosine(y, ref) > 0.9999
+
+
+def test_gemv_tensor_core_shared_scratch_across_shapes(K):
+  """One scratch buffer serves GEMVs of different shapes back to back (as in a program)."""
+  from aneforge_b200 import _runtime as R
+  rng = np.random.default_rng(21)
+  shapes = [(1536, 1024), (7168, 1024), (1024, 3584), (1536, 1024)]
+  need = max(R.load_library().af_gemv_tc_scratch_bytes(n, k, 4) for n, k in shapes)
+  scratch = torch.zeros((need,), dtype=torch.uint8, device="cuda")
+  for N, Kd in shapes * 2:
+    W = (rng.standard_normal((N, Kd), dtype=F32) * F32(0.02)).astype(F16)
+    x = rng.standard_normal((4, Kd), dtype=F32).astype(F16)
+    qr, sr = Q.quantize_per_row(W)
+    y = K.gemv_tc(cuda(x), K.pack_i8_tiles(cuda(qr)), cuda(sr), N, Kd, scratch=scratch).cpu().numpy()
+    ref = (x.astype(F32) @ qr.astype(F32).T) * sr.astype(F32)
+    assert np.abs(y - ref).max() <= 1e-4 * np.abs(ref).max()

@@ -147,4 +147,7 @@ def test_config2_decoder_block_step():
   ya, ra = y.astype(F32).ravel(), ref.astype(F32).ravel()
   assert np.linalg.norm(ya - ra) / np.linalg.norm(ra) < 1e-2
   assert cosine(ya, ra) > 0.999
-  assert np.array_equal(Kg[:, pos], Ko[:, pos]) and np.array_equal(Vg[:, pos], Vo[:, pos])
+  # the new cache slot: fp16 of an fp32 value whose summation order differs -> equal up to one ulp
+  for got, ref in ((Kg[:, pos], Ko[:, pos]), (Vg[:, pos], Vo[:, pos])):
+    d = np.abs(got.astype(F32) - ref.astype(F32))
+    assert np.all(d <= np.abs(ref.astype(F32)) * 2 ** -10 + 1e-7) and (d > 0).mean() < 0.01
