@@ -121,12 +121,14 @@ AF_DEV float transpose_reduce(float (&v)[NV], int lane) {
   return v[0];
 }
 
+constexpr int DEC_WARPS = 8;
+
 template <int DH, int G>
-__global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
+__global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDecodeArgs a) {
   using HL = HeadLayout<DH>;
   using DB = DecodeBatch<DH, G>;
   constexpr int EPL = HL::EPL;
-  constexpr int NW = 4;
+  constexpr int NW = DEC_WARPS;
   constexpr int PB = DB::PB;
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -308,21 +310,37 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
   __syncthreads();
   if (!last_s) return;
   __threadfence();
+  // ---- merge the splits: (m_s, l_s) of every split land in shared memory in one parallel pass, the
+  // per-head weights exp(m_s - M) are formed once, then each output issues its n_split loads together
+  __shared__ float fw[64][G];      // m_s, then the weight exp(m_s - M)
+  __shared__ float lw[64][G];      // l_s
+  __shared__ float den_s[G];
   const float* pp = a.part + pair * a.n_split * G * (DH + 2);
+  for (int i = threadIdx.x; i < a.n_split * G; i += blockDim.x) {
+    const int sp = i / G, g = i - sp * G;
+    fw[sp][g] = __ldcg(pp + (sp * G + g) * (DH + 2) + DH);
+    lw[sp][g] = __ldcg(pp + (sp * G + g) * (DH + 2) + DH + 1);
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int g = threadIdx.x;
+    float M = -INFINITY;
+    for (int sp = 0; sp < a.n_split; ++sp) M = fmaxf(M, fw[sp][g]);
+    float den = 0.f;
+    for (int sp = 0; sp < a.n_split; ++sp) {
+      const float f = fw[sp][g] == -INFINITY ? 0.f : expf(fw[sp][g] - M);
+      den = fmaf(f, lw[sp][g], den);
+      fw[sp][g] = f;
+    }
+    den_s[g] = den;
+  }
+  __syncthreads();
   for (int i = threadIdx.x; i < G * DH; i += blockDim.x) {
     const int g = i / DH, dd = i - g * DH;
-    float M = -INFINITY;
-    for (int sp = 0; sp < a.n_split; ++sp) M = fmaxf(M, __ldcg(pp + (sp * G + g) * (DH + 2) + DH));
-    float num = 0.f, den = 0.f;
-    for (int sp = 0; sp < a.n_split; ++sp) {
-      const float* q = pp + (sp * G + g) * (DH + 2);
-      const float ms = __ldcg(q + DH);
-      if (ms == -INFINITY) continue;
-      const float f = expf(ms - M);
-      num = fmaf(f, __ldcg(q + dd), num);
-      den = fmaf(f, __ldcg(q + DH + 1), den);
-    }
-    a.out[(size_t)b * a.ld_out + (size_t)(kvh * G + g) * DH + dd] = f2h(num / den);
+    float num = 0.f;
+#pragma unroll 8
+    for (int sp = 0; sp < a.n_split; ++sp) num = fmaf(fw[sp][g], __ldcg(pp + (sp * G + g) * (DH + 2) + dd), num);
+    a.out[(size_t)b * a.ld_out + (size_t)(kvh * G + g) * DH + dd] = f2h(num / den_s[g]);
   }
   if (threadIdx.x == 0) a.counters[pair] = 0;
 }
@@ -335,7 +353,7 @@ template <int DH, int G>
 static cudaError_t launch_decode(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.n_split, a.KV, a.NB);
-  cfg.blockDim = dim3(128);
+  cfg.blockDim = dim3(DEC_WARPS * 32);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -357,7 +375,7 @@ static cudaError_t decode_g(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) 
 }
 
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
-  if (a.KV <= 0 || a.H % a.KV || a.n_split < 1) return cudaErrorInvalidValue;
+  if (a.KV <= 0 || a.H % a.KV || a.n_split < 1 || a.n_split > 64) return cudaErrorInvalidValue;
   if (a.n_split > 1 && (!a.part || !a.counters)) return cudaErrorInvalidValue;
   switch (a.dh) {
     case 16: return decode_g<16>(a, st, pdl);

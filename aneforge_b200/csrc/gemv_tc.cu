@@ -413,18 +413,21 @@ static int grid_any(int NB, int epi) {
 // Stream-K geometry on the host: grid G (all resident), units U = RB*KT, the largest number of CTAs
 // sharing one row block (`maxc`, partial slots per row block).
 static void plan_geometry(int N, int K, int NB, int epi, int* G, int* maxc) {
-  static const long long min_bytes = 1024ll * env_int("AF_TC_MIN_KB", 96);
+  // G = RB * d: each row block is split evenly between d CTAs, so a CTA's range lies inside one row
+  // block (at most one ticket per CTA, none when d == 1). d is the smallest split giving at least
+  // `min_ctas` CTAs (enough bytes in flight), bounded by the resident capacity and by KT.
+  static const int min_ctas = env_int("AF_TC_MIN_CTAS", 220);
   const long long RB = (N + 63) / 64, KT = (K + 31) / 32;
-  const long long U = RB * KT;
-  long long g = grid_any(NB, epi);
-  // every CTA pays a fixed ramp (barrier setup, first-copy latency) and, on a shared row block, a
-  // ticket: give each at least `min_bytes` of weights so those costs stay small against streaming
-  const long long by_bytes = (U * tc::UNIT + min_bytes - 1) / min_bytes;
-  if (g > by_bytes) g = by_bytes;
-  if (g > U) g = U;
-  if (g < 1) g = 1;
+  const long long slots = grid_any(NB, epi);
+  long long d = (min_ctas + RB - 1) / RB;
+  if (d < 1) d = 1;
+  while (d > 1 && RB * d > slots) --d;
+  if (d > KT) d = KT;
+  long long g = RB * d;
+  if (g > slots) g = slots;                 // more row blocks than resident CTAs: plain stream-K
   *G = (int)g;
-  const long long per = U / g;                       // a CTA holds >= per units
+  const long long U = RB * KT;
+  const long long per = U / g;
   *maxc = (int)((KT + per - 1) / (per > 0 ? per : 1)) + 1;
 }
 

@@ -293,9 +293,10 @@ class LlamaPrefill:
   def _ctx(self, NB, M):
     cfg, d = self.cfg, self._load()
     G = cfg.n_heads // cfg.n_kv_heads
-    # split-K over the cache: ~2 CTAs per SM in total, each split at least 32 keys (one batch of
-    # 8 keys per warp), at most 64 splits (the last CTA merges them)
-    nsplit = max(1, min(64, (M + 31) // 32, -(-(2 * 148) // max(1, cfg.n_kv_heads * NB))))
+    # split-K over the cache: one split per 32 keys, but all CTAs in one wave (2 CTAs of 8 warps per
+    # SM) and at most 64 splits (the last CTA of each head merges them)
+    cap = max(1, (2 * 148) // max(1, cfg.n_kv_heads * NB))
+    nsplit = max(1, min(64, cap, -(-M // 32)))
     return {"NB": NB, "M": M, "nsplit": nsplit, "scale": d["scale"], "kvc": d["kvc"], "expand": G > 1 and d["kvc"] != 1.0}
 
   # -- programs
