@@ -641,7 +641,7 @@ DECODE_MLP_LOADERS: dict = {}
 
 def decoder_block_step(cfg: LlamaConfig, lw: dict, h, Kc, Vc, pos: int, compress="int8", device: int = 0):
   """One decode step of ONE block (no embedding, final norm or head) through a program: the
-  BASELINE config-2 unit. h [1, D] fp16; Kc/Vc [KV, M, dh] fp16 prior cache. Returns (fp16 block
+  single-block decode workload (d 2048, GQA 16/4, FFN 8192 at pos 1024 is the benchmarked case). h [1, D] fp16; Kc/Vc [KV, M, dh] fp16 prior cache. Returns (fp16 block
   output [1, D], updated K, updated V)."""
   M = int(Kc.shape[1])
   w = {"embed": np.zeros((1, cfg.dim), F16), "lm_head": np.zeros((1, cfg.dim), F16),

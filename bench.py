@@ -1,4 +1,4 @@
-"""Benchmark: int8 decode tokens/s of a Llama-3-8B-shaped model on B200.
+"""Benchmark: int8 decode tokens/s of a Llama-3-8B-shaped model (the headline decode workload) on B200.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl reference]
 
@@ -110,7 +110,7 @@ def make_weights(cfg, device, seed=0):
 
 
 def algorithmic_bytes_per_step(cfg, NB, pos):
-  """Bytes a decode step must move once (SURVEY 8(d) accounting): int8 codes + fp16 scales of every
+  """Bytes a decode step must move once (each byte counted once per step): int8 codes + fp16 scales of every
   projection, the fp16 lm_head, norms, KV cache read (positions 0..pos) + the new slot write, and
   the step's activations in/out."""
   D, H, KV, dh, F, V, L = cfg.dim, cfg.n_heads, cfg.n_kv_heads, cfg.dh, cfg.ffn_dim, cfg.vocab, cfg.n_layers

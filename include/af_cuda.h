@@ -127,7 +127,7 @@ int af_gemv(int wf, int epi, const uint16_t* x, int ldx, const void* w, const ui
             const uint16_t* bias, void* y, int ldy, int nb, int n, int k, void* stream);
 
 /* Tensor-core int8 GEMV (the decode K1 kernel): weights re-packed once into 16x32 fragment tiles
- * (af_pack_i8_tiles, [ceil(n/16)][ceil(k/32)][512 B]) from per-row int8 codes [n][k]; same epilogues as
+ * (af_pack_i8_tiles, [ceil(n/64)][ceil(k/32)][4 row tiles of 16][512 B]: 16 rows x 32 codes per tile) from per-row int8 codes [n][k]; same epilogues as
  * af_gemv (AF_EPI_SWIGLU tiles hold 8 gate rows then the 8 matching up rows). Replaces the same
  * reference `matmul` (_compile.py:375-385). Scratch (split-K partials + counters):
  * af_gemv_tc_scratch_bytes, zero before the first call, left zeroed; 0 bytes needs no scratch. */

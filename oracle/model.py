@@ -445,7 +445,7 @@ def decoder_block_step(cfg: Config, lw: dict, h: np.ndarray, Kc, Vc, pos: int, c
 def random_llama_weights(cfg: Config, seed: int = 0, std: float = 0.02, dtype=F16, moe: bool = False,
                          qkv_bias: bool = False):
   """Seeded N(0, std) weights in the reference layout, unit norms (the shape of
-  `tests/_helpers.py:make_random_llama_model`, with BASELINE's N(0, 0.02))."""
+  `tests/_helpers.py:make_random_llama_model`, with the benchmark's N(0, 0.02))."""
   rng = np.random.default_rng(seed)
   R = lambda *s: (rng.standard_normal(s, dtype=F32) * F32(std)).astype(dtype)
   dh, D = cfg.dh, cfg.dim

@@ -2,7 +2,7 @@
 
 Run ONLY where the reference is mounted (it imports the reference package read-only):
 
-    REF=/path/to/ANEForge python tests/golden/make_golden.py
+    ANEFORGE_REF=/path/to/ANEForge python tests/golden/make_golden.py
 
 Nothing at test time imports the reference; the tests read the `.npz` files written here.
 
@@ -30,7 +30,9 @@ from unittest import mock
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = os.environ.get("REF", "/root/reference")
+REF = os.environ.get("ANEFORGE_REF", "")
+if not REF or not os.path.isdir(os.path.join(REF, "aneforge")):
+  sys.exit("set ANEFORGE_REF to a checkout of the reference (the directory holding aneforge/)")
 sys.path.insert(0, REF)
 
 import aneforge as af                               # noqa: E402  (reference package)

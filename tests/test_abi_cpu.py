@@ -1,0 +1,100 @@
+"""CPU checks of the C-ABI boundary and the host-side logic (no kernel is launched).
+
+* libaf_cuda.so loads and exports every function include/af_cuda.h declares, and the ctypes
+  signature table of the Python runtime names exactly those functions.
+* The package's weight-encoding policy (`aneforge_b200._blob`, the device-side restatement of the
+  reference's `_compile.py:112-188`) picks the same encoding and the same dequantized matrix as the
+  reference did on the golden inputs.
+* RoPE tables, RMSNorm constants and the gate/up interleave are the ones the oracle uses.
+"""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from tests._golden import load
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+F16, F32 = np.float16, np.float32
+
+
+def declared_functions():
+  src = open(os.path.join(ROOT, "include", "af_cuda.h")).read()
+  src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+  return sorted(set(re.findall(r"\b(af_[a-z0-9_]+)\s*\(", src)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+  from aneforge_b200 import build
+  return ctypes.CDLL(str(build.build()))
+
+
+def test_library_exports_every_declared_symbol(lib):
+  names = declared_functions()
+  assert len(names) >= 30
+  missing = [n for n in names if not hasattr(lib, n)]
+  assert not missing, missing
+
+
+def test_runtime_signature_table_matches_header():
+  from aneforge_b200 import _runtime as R
+  table = sorted(n for n, _, _ in R.SIGNATURES)
+  assert table == declared_functions()
+
+
+def test_abi_version_and_error_channel(lib):
+  lib.af_abi_version.restype = ctypes.c_int
+  assert lib.af_abi_version() == 1
+  lib.af_last_error.restype = ctypes.c_char_p
+
+
+def test_pack_tile_and_scratch_sizes(lib):
+  """Host-side size helpers: fragment tiles are [ceil(n/64)][ceil(k/32)][4][512 B]."""
+  lib.af_pack_i8_tiles_bytes.restype = ctypes.c_size_t
+  for n, k in ((16, 32), (37, 64), (4096, 4096), (28672, 4096)):
+    assert lib.af_pack_i8_tiles_bytes(n, k) == (-(-n // 64)) * (-(-k // 32)) * 4 * 512
+
+
+@pytest.mark.parametrize("name", ["W", "Ws", "Mx", "Wl"])
+@pytest.mark.parametrize("mode", ["None", "int8", "int4", "blockwise", "sparse", "auto"])
+def test_package_encoding_policy_matches_reference(name, mode):
+  from aneforge_b200 import _blob
+  qz = load("quant.npz")
+  M = {"W": qz["W"], "Ws": qz["Ws"], "Wl": qz["Wl"], "Mx": np.repeat(np.eye(4, dtype=F16), 2, axis=0)}[name]
+  comp = None if mode == "None" else mode
+  kind, _ = _blob.decide(M, comp)
+  ref_kind = str(qz[f"enc_{name}_{mode}_kind"])
+  assert {"lut4": "lut4", "int8": "int8", "fp16": "fp16", "blockwise": "blockwise",
+          "sparse": "sparse"}.get(kind, kind) == ref_kind
+  np.testing.assert_array_equal(_blob.dense_of(M, comp).astype(F32), qz[f"enc_{name}_{mode}_deq"])
+
+
+def test_gqa_expand_factor():
+  from aneforge_b200 import _blob
+  assert _blob.gqa_expand_factor(8, 4, "int8") == 127 * float(np.float16(1 / 127))
+  assert _blob.gqa_expand_factor(8, 4, None) == 1.0
+  assert _blob.gqa_expand_factor(8, 1, "int8") == 1.0
+
+
+@pytest.mark.parametrize("M,dh,base", [(64, 128, 500000.0), (300, 64, 10000.0)])
+def test_rope_tables_match_oracle(M, dh, base):
+  from aneforge_b200.llm import rope_tables
+  from oracle.model import rope_tables as orope
+  c, s = rope_tables(M, dh, base)
+  oc, os_ = orope(M, dh, base)
+  assert np.array_equal(c.view(np.uint16), oc.view(np.uint16))
+  assert np.array_equal(s.view(np.uint16), os_.view(np.uint16))
+
+
+def test_swiglu_interleave_layout():
+  torch = pytest.importorskip("torch")
+  from aneforge_b200 import layout
+  g = torch.arange(32).reshape(16, 2)
+  u = 100 + torch.arange(32).reshape(16, 2)
+  w = layout.interleave_blocks(g, u, 8)
+  assert w.shape == (32, 2)
+  assert torch.equal(w[:8], g[:8]) and torch.equal(w[8:16], u[:8])
+  assert torch.equal(w[16:24], g[8:]) and torch.equal(w[24:], u[8:])

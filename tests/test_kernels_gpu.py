@@ -64,7 +64,7 @@ def test_quantize_g32_int4_bit_exact(K, shape):
 
 
 def test_gemv_config1_int8_4096(K):
-  """W 4096x4096 ~ N(0,0.02) int8 per row, x 1x4096 ~ N(0,1) fp16, y fp16."""
+  """Benchmark config 1: W 4096x4096 ~ N(0,0.02) int8 per row, x 1x4096 ~ N(0,1) fp16, y fp16."""
   rng = np.random.default_rng(0)
   W = rng.standard_normal((4096, 4096), dtype=F32) * F32(0.02)
   x = rng.standard_normal((1, 4096), dtype=F32).astype(F16)

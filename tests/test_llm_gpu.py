@@ -129,7 +129,7 @@ def test_batched_decode_matches_single_sequences():
 
 
 def test_config2_decoder_block_step():
-  """one Llama block (d 2048, 16/4 heads, FFN 8192), cache of 1024 N(0,1) positions,
+  """Benchmark config 2: one Llama block (d 2048, 16/4 heads, FFN 8192), cache of 1024 N(0,1) positions,
   hidden N(0,1), pos 1024, int8 weights N(0,0.02): block output vs oracle."""
   from aneforge_b200.llm import decoder_block_step
   from oracle.model import decoder_block_step as oracle_block
