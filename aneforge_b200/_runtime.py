@@ -63,6 +63,10 @@ SIGNATURES = [
   ("af_attn_decode", c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
                              c_int, c_int, c_int, c_int, c_int, c_float, c_float, c_int, c_void_p, c_size_t, c_void_p,
                              c_void_p]),
+  ("af_attn_decode_noalloc_max_bytes", c_size_t, []),
+  ("af_attn_decode_noalloc", c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                                     c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_float, c_int, c_void_p,
+                                     c_void_p]),
 ]
 
 W_I8, W_F16, W_I4G32 = 0, 1, 2

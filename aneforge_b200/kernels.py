@@ -144,3 +144,16 @@ def gemv_tc(x, tiles, scales, N, K, bias=None, epi=R.EPI_F32, y=None, scratch=No
   R.check(R.lib().af_gemv_tc(epi, _p(x), x.stride(0), _p(tiles), _p(scales), _p(bias), _p(y), y.stride(0), NB, N, K,
                              _p(scratch), nbytes, _stream(x)), "af_gemv_tc")
   return y
+
+
+def attn_decode_noalloc(qkv, kc, vc, pos, cos_t, sin_t, H, KV, dh, scale, kv_c=1.0, expand=False, n_split=1, err=None):
+  """Decode attention using the library's built-in scratch (no allocation by the entry point).
+  Returns (rc, out); rc != 0 means the shape was rejected (reason in _runtime.last_error())."""
+  import torch
+  NB = qkv.shape[0]
+  M = kc.shape[2]
+  out = torch.zeros((NB, H * dh), dtype=torch.float16, device=qkv.device)
+  rc = R.lib().af_attn_decode_noalloc(_p(qkv), qkv.stride(0), _p(kc), _p(vc), _p(pos), _p(cos_t), _p(sin_t),
+                                      _p(out), out.stride(0), NB, H, KV, dh, M, n_split, float(scale), float(kv_c),
+                                      int(expand), _p(err), _stream(qkv))
+  return rc, out

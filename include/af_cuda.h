@@ -160,6 +160,22 @@ int af_attn_decode(const float* qkv, int ld_qkv, uint16_t* kc, uint16_t* vc, con
                    int n_split, float scale, float kv_c, int expand, void* scratch, size_t scratch_bytes,
                    int* err, void* stream);
 
+/* af_attn_decode without caller scratch, for callers that cannot allocate device memory (a host
+ * framework that owns every allocation, code running while a memory pool is locked, plug-ins that
+ * must not touch the process allocator). No counterpart in the reference: the ANE runtime had no
+ * split-K scratch. The scratch is a fixed AF_ATTN_NOALLOC_SCRATCH_BYTES array inside the library,
+ * resident on every GPU that loads it until exit; shapes needing more return -1 before launching.
+ * All calls on a GPU share that array: calls that overlap on the GPU race (order them on one
+ * stream). The first call on a device looks the array's address up; make it before any stream
+ * capture. Same arguments as af_attn_decode minus the scratch pair; the current device must be the
+ * stream's device. */
+#define AF_ATTN_NOALLOC_SCRATCH_BYTES (2u << 20)
+size_t af_attn_decode_noalloc_max_bytes(void);
+int af_attn_decode_noalloc(const float* qkv, int ld_qkv, uint16_t* kc, uint16_t* vc, const int* pos,
+                           const uint16_t* cos_t, const uint16_t* sin_t, uint16_t* out, int ld_out, int nb, int h,
+                           int kv, int dh, int m, int n_split, float scale, float kv_c, int expand, int* err,
+                           void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -49,6 +49,8 @@ def test_abi_version_and_error_channel(lib):
   lib.af_abi_version.restype = ctypes.c_int
   assert lib.af_abi_version() == 1
   lib.af_last_error.restype = ctypes.c_char_p
+  lib.af_attn_decode_noalloc_max_bytes.restype = ctypes.c_size_t
+  assert lib.af_attn_decode_noalloc_max_bytes() == 2 << 20
 
 
 def test_pack_tile_and_scratch_sizes(lib):
