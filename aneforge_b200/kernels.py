@@ -65,19 +65,26 @@ def gemv(x, w, scales=None, bias=None, wf=R.W_I8, epi=R.EPI_F32, y=None, n_out=N
   return y
 
 
-def lm_head_argmax(x, w, scales=None, wf=R.W_F16, logits=True, pos=None):
-  """Greedy token per row of x [NB, K] fp16 against head rows w [V, K]; optional fp32 logits."""
+def lm_head_argmax(x, w, scales=None, wf=R.W_F16, logits=True, pos=None, scratch=None, out=None):
+  """Greedy token per row of x [NB, K] fp16 against head rows w [V, K]; optional fp32 logits.
+  `scratch` (zeroed, left zeroed) may be reused across calls of one shape; `out` = (tok, logits)
+  preallocated outputs."""
   import torch
   NB, K = x.shape
   V = w.shape[0]
   L = R.lib()
   nbytes = ctypes.c_size_t()
   R.check(L.af_lm_head_argmax_scratch(wf, V, K, NB, ctypes.byref(nbytes)), "scratch")
-  scratch = torch.zeros((nbytes.value,), dtype=torch.uint8, device=x.device)
-  tok = torch.zeros((NB,), dtype=torch.int32, device=x.device)
-  lg = torch.zeros((NB, V), dtype=torch.float32, device=x.device) if logits else None
+  if scratch is None:
+    scratch = torch.zeros((nbytes.value,), dtype=torch.uint8, device=x.device)
+  _need(scratch.numel() >= nbytes.value, "lm_head scratch too small")
+  if out is not None:
+    tok, lg = out
+  else:
+    tok = torch.zeros((NB,), dtype=torch.int32, device=x.device)
+    lg = torch.zeros((NB, V), dtype=torch.float32, device=x.device) if logits else None
   R.check(L.af_lm_head_argmax(wf, _p(x), x.stride(0), _p(w), _p(scales), _p(lg), NB, V, K, _p(tok), _p(pos),
-                              _p(scratch), nbytes.value, _stream(x)), "af_lm_head_argmax")
+                              _p(scratch), scratch.numel(), _stream(x)), "af_lm_head_argmax")
   return tok, lg
 
 
@@ -97,12 +104,13 @@ def attn_decode_scratch_bytes(nb, kv, n_split, g, dh) -> int:
 
 
 def attn_decode(qkv, kc, vc, pos, cos_t, sin_t, H, KV, dh, scale, kv_c=1.0, expand=False, n_split=1, scratch=None,
-                err=None):
+                err=None, out=None):
   """Decode attention; updates kc/vc at pos in place; returns fp16 [NB, H*dh]."""
   import torch
   NB = qkv.shape[0]
   M = kc.shape[2]
-  out = torch.zeros((NB, H * dh), dtype=torch.float16, device=qkv.device)
+  if out is None:
+    out = torch.zeros((NB, H * dh), dtype=torch.float16, device=qkv.device)
   if n_split > 1 and scratch is None:
     scratch = torch.zeros((attn_decode_scratch_bytes(NB, KV, n_split, H // KV, dh),), dtype=torch.uint8,
                           device=qkv.device)

@@ -54,43 +54,67 @@ def _peaks():
 
 
 class ClockSampler:
-  """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+  """SM clocks and throttle reasons of one GPU sampled every 200 ms through NVML (in-process: no
+  nvidia-smi child processes competing with the timed region)."""
+
+  _REASONS = (("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20), ("hw_thermal_slowdown", 0x40),
+              ("sw_power_cap", 0x4))
 
   def __init__(self, index: int):
     self.index, self.samples, self._stop = index, [], threading.Event()
     self._t = threading.Thread(target=self._run, daemon=True)
+    self._h = None
+    try:
+      import pynvml
+      pynvml.nvmlInit()
+      self._nv = pynvml
+      self._h = pynvml.nvmlDeviceGetHandleByIndex(self._physical_index(index))
+    except Exception:
+      self._h = None
+
+  @staticmethod
+  def _physical_index(index):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    ids = [v.strip() for v in vis.split(",") if v.strip()]
+    return int(ids[index]) if index < len(ids) and ids[index].isdigit() else index
+
+  def _sample(self):
+    nv, h = self._nv, self._h
+    sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+    mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+    mask = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+    self.samples.append((sm, mx, mask))
 
   def _run(self):
-    q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
     while not self._stop.is_set():
       try:
-        out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}", "--format=csv,noheader,nounits"],
-                             capture_output=True, text=True, timeout=5).stdout.strip()
-        if out:
-          self.samples.append([x.strip() for x in out.split(",")])
+        self._sample()
       except Exception:
         pass
       self._stop.wait(0.2)
 
   def __enter__(self):
-    self._t.start()
+    if self._h is not None:
+      self._t.start()
     return self
 
   def __exit__(self, *a):
     self._stop.set()
-    self._t.join(timeout=10)
+    if self._t.is_alive():
+      self._t.join(timeout=10)
+    if self._h is not None:
+      try:
+        self._sample()                      # at least one sample at the end of the region
+      except Exception:
+        pass
 
   def summary(self):
     if not self.samples:
       return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-    sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
-    mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-    reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > 3 + i and s[3 + i] == "Active"})
-    return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-            "reasons": reasons, "samples": len(self.samples)}
+    sm = [s[0] for s in self.samples]
+    reasons = sorted({n for s in self.samples for n, bit in self._REASONS if s[2] & bit})
+    return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(s[1] for s in self.samples), "reasons": reasons,
+            "samples": len(self.samples), "source": "nvml"}
 
 
 def make_weights(cfg, device, seed=0):
@@ -139,7 +163,8 @@ def run_b200(args):
   del w
   torch.cuda.empty_cache()
   load_s = time.perf_counter() - t_load
-  M = PROMPT + args.warmup + args.steps + 8
+  e2e_steps = max(8, args.steps // 2)
+  M = PROMPT + args.warmup + args.steps + e2e_steps + 8      # every step (timed, warm-up, e2e) fits the cache
   rng = np.random.default_rng(99 + rank)
   prompts = [list(rng.integers(0, cfg.vocab, PROMPT)) for _ in range(NB)]
   dec = m._decoder(M, NB)
@@ -164,12 +189,16 @@ def run_b200(args):
     dist.barrier()
   torch.cuda.synchronize()
   e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+  if args.profile_region:
+    torch.cuda.profiler.start()         # ncu --profile-from-start off sees the timed steps only
   with ClockSampler(local) as clk:
     e0.record(stream)
     for _ in range(args.steps):
       prog.execute_async()
     e1.record(stream)
     prog.sync()
+  if args.profile_region:
+    torch.cuda.profiler.stop()
   torch.cuda.synchronize()
   ms = e0.elapsed_time(e1)
   if ws > 1:
@@ -188,7 +217,6 @@ def run_b200(args):
   tok_dev = prog.tensor("tok", (NB,), "int32")
   out_dev = prog.tensor("tok_out", (NB,), "int32")
   host_tok.copy_(out_dev.cpu())
-  e2e_steps = max(8, args.steps // 2)
   torch.cuda.synchronize()
   t0 = time.perf_counter()
   with torch.cuda.stream(stream):
@@ -199,6 +227,7 @@ def run_b200(args):
       stream.synchronize()
       host_tok.copy_(host_out)
   e2e_s = time.perf_counter() - t0
+  prog.sync()                                              # raises if any step recorded a device error
   e2e_tok_s = NB * e2e_steps * ws / e2e_s
 
   # ---- dominant kernel: the fused gate|up int8 GEMV, timed alone on the program stream over the
@@ -211,14 +240,21 @@ def run_b200(args):
   with torch.cuda.stream(stream):
     for i in range(cfg.n_layers):
       kernels.gemv_tc(x, gu[i].w, gu[i].s, gu[i].N, gu[i].K, epi=R.EPI_SWIGLU, y=y, scratch=scr)
+    torch.cuda.synchronize()
+    kgraph = torch.cuda.CUDAGraph()                       # launches back to back, not paced by the host
+    with torch.cuda.graph(kgraph, stream=stream):
+      for i in range(reps):
+        l = gu[i % cfg.n_layers]
+        kernels.gemv_tc(x, l.w, l.s, l.N, l.K, epi=R.EPI_SWIGLU, y=y, scratch=scr)
+    kgraph.replay()
+    torch.cuda.synchronize()
     k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     k0.record(stream)
-    for i in range(reps):
-      l = gu[i % cfg.n_layers]
-      kernels.gemv_tc(x, l.w, l.s, l.N, l.K, epi=R.EPI_SWIGLU, y=y, scratch=scr)
+    kgraph.replay()
     k1.record(stream)
   torch.cuda.synchronize()
   k_us = k0.elapsed_time(k1) * 1e3 / reps
+  del kgraph
   gu_bytes = gu[0].nbytes + NB * cfg.dim * 2 + NB * cfg.ffn_dim * 2
   peak, peak_kind = _peaks()
   step_bytes = algorithmic_bytes_per_step(cfg, NB, PROMPT + args.warmup + args.steps // 2)
@@ -237,7 +273,8 @@ def run_b200(args):
               "d2h_bytes_per_step": 4 * NB,
               "how": "program API, pinned host token ids in/out every step, host sync per step"},
       "roofline": {"bound": "hbm", "kernel": "gemv_tc int8 gate|up + silu*mul (28672x4096, mma.sync)", "achieved": round(achieved, 1),
-                   "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                   "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": profile_traffic(),
+                   "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/gemv_tc_gate_up_llama8b.md",
                    "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
                    "launch_us": round(k_us, 2), "algorithmic_bytes": gu_bytes},
       "step_roofline": {"algorithmic_bytes": int(step_bytes), "achieved_gbs": round(step_bytes / (ms_step * 1e-3) / 1e9, 1),
@@ -256,6 +293,99 @@ def run_b200(args):
     dist.barrier()
     dist.destroy_process_group()
   return result
+
+
+def kernel_bench(name, reps, warmup):
+  """One hot kernel alone on the device (the `--kernel` mode; the small case the ncu summaries in
+  profiles/ are captured on). Weights rotate over enough copies that every launch streams from HBM.
+  Returns a dict with the launch time (CUDA events on the launching stream) and algorithmic GB/s."""
+  import torch
+  from aneforge_b200 import kernels as K, _runtime as R
+  from aneforge_b200.llm import rope_tables
+  dev = torch.device("cuda", 0)
+  torch.cuda.set_device(dev)
+  g = torch.Generator(device=dev)
+  g.manual_seed(7)
+  D, F, H, KV, dh, V = CFG["dim"], CFG["ffn_dim"], CFG["n_heads"], CFG["n_kv_heads"], 128, CFG["vocab"]
+  st = torch.cuda.Stream(dev)
+
+  def int8_tiles(N, Kd, copies):
+    W = (torch.randn(N, Kd, generator=g, device=dev) * 0.02).half()
+    q, sc = K.quantize_per_row_i8(W)
+    t = K.pack_i8_tiles(q)
+    return [t] + [t.clone() for _ in range(copies - 1)], sc
+
+  if name in ("gemv_gu", "gemv_cfg1", "gemv_qkv", "gemv_o", "gemv_down"):
+    N, Kd, epi = {"gemv_gu": (2 * F, D, R.EPI_SWIGLU), "gemv_cfg1": (4096, 4096, R.EPI_F16),
+                  "gemv_qkv": ((H + 2 * KV) * dh, D, R.EPI_F32), "gemv_o": (D, H * dh, R.EPI_RESID),
+                  "gemv_down": (D, F, R.EPI_RESID)}[name]
+    copies = max(2, -(-300_000_000 // (N * Kd)))            # > 2x L2 of weights in rotation
+    tiles, sc = int8_tiles(N, Kd, copies)
+    x = torch.randn(1, Kd, generator=g, device=dev).half()
+    y = K.gemv_tc(x, tiles[0], sc, N, Kd, epi=epi)
+    scr, _ = K.gemv_tc_scratch(N, Kd, 1, dev)
+    nbytes = N * Kd + 2 * N + 2 * Kd + y.numel() * y.element_size() * (2 if epi == R.EPI_RESID else 1)
+    fn = lambda i: K.gemv_tc(x, tiles[i % copies], sc, N, Kd, epi=epi, y=y, scratch=scr)
+    what = f"gemv_tc int8 {N}x{Kd} epi={epi}"
+  elif name == "attn":
+    M, pos = 1024, 576
+    kc = torch.randn(1, KV, M, dh, generator=g, device=dev).half()
+    vc = torch.randn(1, KV, M, dh, generator=g, device=dev).half()
+    qkv = torch.randn(1, (H + 2 * KV) * dh, generator=g, device=dev)
+    p = torch.tensor([pos], dtype=torch.int32, device=dev)
+    c, s_ = (torch.from_numpy(a).to(dev) for a in rope_tables(M, dh, CFG["rope_base"]))
+    nsplit = max(1, min(64, (2 * 148) // KV, -(-M // 32)))
+    scr = torch.zeros(K.attn_decode_scratch_bytes(1, KV, nsplit, H // KV, dh), dtype=torch.uint8, device=dev)
+    kv_c = 127 * float(np.float16(1 / 127))
+    nbytes = 2 * KV * (pos + 1) * dh * 2 + qkv.numel() * 4 + H * dh * 2
+    o = torch.zeros(1, H * dh, dtype=torch.float16, device=dev)
+    fn = lambda i: K.attn_decode(qkv, kc, vc, p, c, s_, H, KV, dh, float(np.float16(1 / np.sqrt(dh))), kv_c, True,
+                                 nsplit, scr, out=o)
+    what = f"attn_decode H{H}/KV{KV} dh{dh} pos {pos} nsplit {nsplit} (KV cache {2 * KV * (pos + 1) * dh * 2} B)"
+  elif name == "lm_head":
+    W = (torch.randn(V, D, generator=g, device=dev) * 0.02).half()
+    x = torch.randn(1, D, generator=g, device=dev).half()
+    nbytes = V * D * 2 + D * 2 + V * 4
+    scr = torch.zeros(1 << 20, dtype=torch.uint8, device=dev)
+    outs = (torch.zeros(1, dtype=torch.int32, device=dev), torch.zeros(1, V, dtype=torch.float32, device=dev))
+    fn = lambda i: K.lm_head_argmax(x, W, scratch=scr, out=outs)
+    what = f"lm_head fp16 {V}x{D} + argmax"
+  else:
+    raise SystemExit(f"unknown --kernel {name}")
+  # the launches are captured in one CUDA graph so that host-side call overhead does not pace them
+  with torch.cuda.stream(st):
+    for i in range(warmup):
+      fn(i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
+      for i in range(reps):
+        fn(warmup + i)
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    graph.replay()
+    e1.record(st)
+  torch.cuda.synchronize()
+  us = e0.elapsed_time(e1) * 1e3 / reps
+  del graph
+  peak, kind = _peaks()
+  gbs = nbytes / (us * 1e-6) / 1e9
+  return {"kernel": name, "what": what, "us_per_launch": round(us, 2), "algorithmic_bytes": int(nbytes),
+          "achieved_gbs": round(gbs, 1), "peak_gbs": peak, "peak_kind": kind, "frac": round(gbs / peak, 4),
+          "reps": reps, "warmup": warmup, "timing": "CUDA events around one CUDA-graph replay of `reps` back-to-back launches"}
+
+
+def profile_traffic(name="gemv_tc_gate_up_llama8b.md"):
+  """DRAM bytes per launch of the dominant kernel from the committed ncu summary (or None)."""
+  import re
+  try:
+    with open(os.path.join(ROOT, "profiles", name)) as f:
+      m = re.search(r"traffic_bytes_per_launch:\s*([0-9,]+)", f.read())
+    return int(m.group(1).replace(",", "")) if m else None
+  except OSError:
+    return None
 
 
 def cpu_baseline(steps=3, layers=1):
@@ -304,8 +434,17 @@ def main():
   ap.add_argument("--batch", type=int, default=1)
   ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
   ap.add_argument("--no-cpu-baseline", action="store_true")
+  ap.add_argument("--kernel", default=None,
+                  help="time one kernel alone: gemv_gu | gemv_qkv | gemv_o | gemv_down | gemv_cfg1 | attn | lm_head")
+  ap.add_argument("--reps", type=int, default=50)
+  ap.add_argument("--profile-region", action="store_true",
+                  help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
   args = ap.parse_args()
   ws, rank, _ = _dist()
+  if args.kernel:
+    for name in args.kernel.split(","):
+      print(json.dumps(kernel_bench(name, args.reps, max(args.warmup, 3))), flush=True)
+    return
   if args.impl == "reference":
     if rank != 0:
       return
