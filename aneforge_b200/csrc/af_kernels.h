@@ -36,6 +36,7 @@ cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t st, bool pdl);
 
 // Tensor-core int8 GEMV over fragment-tile packed weights (gemv_tc.cu). Epilogues F32/F16/RESID/SWIGLU.
 struct GemvTcArgs {
+  int wf = W_I8;               // W_I8: pack_i8_tiles layout + per-row scales; W_I4G32: pack_i4_tiles (scales inside)
   int epi = EPI_F32;
   const __half* x = nullptr;   // [NB][ldx] fp16, ldx % 8 == 0
   int ldx = 0;
@@ -58,6 +59,8 @@ size_t gemv_tc_scratch_bytes(int N, int K, int NB);
 void gemv_tc_plan(int N, int K, int NB, int* S, int* NT);
 cudaError_t pack_i8_tiles(const int8_t* src, int N, int K, uint8_t* dst, cudaStream_t st);
 size_t pack_i8_tiles_bytes(int N, int K);
+cudaError_t pack_i4_tiles(const uint8_t* src, const __half* scales, int N, int K, uint8_t* dst, cudaStream_t st);
+size_t pack_i4_tiles_bytes(int N, int K);
 int gemv_argmax_ctas(int wf, int N, int K, int NB);
 void gemv_argmax_scratch(int wf, int N, int K, int NB, size_t* slot_floats, size_t* counters);
 

@@ -108,6 +108,25 @@ int af_gemv_tc(int epi, const uint16_t* x, int ldx, const void* tiles, const uin
   return rc_of(af::gemv_tc_launch(a, static_cast<cudaStream_t>(stream), false), "af_gemv_tc");
 }
 
+size_t af_pack_i4_tiles_bytes(int n, int k) { return k % 32 ? 0 : af::pack_i4_tiles_bytes(n, k); }
+
+int af_pack_i4_tiles(const uint8_t* packed, const uint16_t* scales, int n, int k, uint8_t* tiles, void* stream) {
+  return rc_of(af::pack_i4_tiles(packed, reinterpret_cast<const __half*>(scales), n, k, tiles,
+                                 static_cast<cudaStream_t>(stream)), "af_pack_i4_tiles");
+}
+
+int af_gemv_tc_i4(int epi, const uint16_t* x, int ldx, const void* tiles, const uint16_t* bias, void* y, int ldy,
+                  int nb, int n, int k, void* scratch, size_t scratch_bytes, void* stream) {
+  af::GemvTcArgs a;
+  a.wf = af::W_I4G32;
+  a.epi = epi;
+  a.x = reinterpret_cast<const __half*>(x); a.ldx = ldx;
+  a.w = tiles; a.bias = reinterpret_cast<const __half*>(bias);
+  a.y = y; a.ldy = ldy; a.NB = nb; a.N = n; a.K = k;
+  a.scratch = scratch; a.scratch_bytes = scratch_bytes;
+  return rc_of(af::gemv_tc_launch(a, static_cast<cudaStream_t>(stream), false), "af_gemv_tc_i4");
+}
+
 int af_rmsnorm(const void* x, int x_f16, int ldx, const uint16_t* g, float floor, uint16_t* out, int ldo, int nb,
                int d, void* stream) {
   return rc_of(af::rmsnorm_launch(x, x_f16, ldx, reinterpret_cast<const __half*>(g), floor,

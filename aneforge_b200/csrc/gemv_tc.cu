@@ -23,6 +23,14 @@
 // bulk-copied per chunk (<= 16 k tiles) into a 2-slot ring by the producer, after the programmatic
 // launch wait; the first chunk's weights are requested before that wait.
 //
+// Group-32 int4 weights (I4 = true) use the same tiling at half the bytes: a 16x32 tile is 256 bytes
+// (lane l owns bytes [8l, 8l+8), one 32-bit word per k-step whose nibbles at bit offsets
+// (0,16) (4,20) (8,24) (12,28) are the fragment pairs a0a1, a2a3, a4a5, a6a7), and each unit ends
+// with the 64 fp16 group scales of its rows for that k tile (unit = 4 x 256 + 128 = 1152 bytes). A
+// nibble n (= code + 8) becomes fp16 1024 + n with one mask-or, minus 1032 exactly; each k tile's
+// product is accumulated fresh and added to the running sum times its group scale, so the scale is
+// applied in fp32 as the dequantised weight s * code would be.
+//
 // Epilogues: F32 / F16 / RESID (y += ..) / SWIGLU (tiles hold 8 gate rows then the matching 8 up).
 // Every mbarrier wait is bounded: on timeout the kernel records AF_DEV_WAIT_TIMEOUT in the error
 // word, consumers leave together after a barrier, and the producer waits (bounded) for the copies
@@ -36,16 +44,27 @@ namespace af {
 
 namespace tc {
 constexpr int WARPS = 4;                   // consumer warps = row tiles per row block
-constexpr int KS = 4;                      // k tiles per weight stage
+constexpr int KS = 4;                      // k tiles per weight stage (int8)
 constexpr int TILE = 512;                  // bytes per 16x32 int8 tile
 constexpr int UNIT = WARPS * TILE;         // one k tile of one row block
 constexpr int STAGE_BYTES = KS * UNIT;     // 8 KB
+constexpr int KS4 = 8;                     // int4: k tiles per stage
+constexpr int TILE4 = 256;                 // bytes per 16x32 int4 tile
+constexpr int UNIT4 = WARPS * TILE4 + 64 * 2;   // 4 tiles + 64 fp16 group scales
+constexpr int STAGE_BYTES4 = KS4 * UNIT4;  // 9 KB
+constexpr int STAGE_MAX = STAGE_BYTES4 > STAGE_BYTES ? STAGE_BYTES4 : STAGE_BYTES;
 constexpr int STAGES = 6;
 constexpr int XKT = 16;                    // k tiles per x chunk
 constexpr int XSTRIDE = XKT * 32 + 8;      // halves per staged x row (+8: conflict-free B loads)
 constexpr int XSLOTS = 2;
 constexpr size_t CNT_BYTES = 16384;        // scratch: per-row-block tickets, then partial slots
 constexpr long long WAIT_LIMIT = 1ll << 26;
+template <bool I4> struct Fmt {
+  static constexpr int ks = I4 ? KS4 : KS;
+  static constexpr int unit = I4 ? UNIT4 : UNIT;
+  static constexpr int tile = I4 ? TILE4 : TILE;
+  static constexpr int stage = ks * unit;
+};
 }  // namespace tc
 
 AF_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -104,6 +123,17 @@ AF_DEV void i8x4_to_h2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
   hi = *reinterpret_cast<uint32_t*>(&h);
 }
 
+// 8 int4 nibbles (code + 8) of one k-step -> the four A-fragment registers, exact.
+AF_DEV void i4x8_to_frag(uint32_t w, uint32_t (&A)[4]) {
+  const __half2 bias = __half2half2(__ushort_as_half(0x6408));  // 1032 = 1024 + 8
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t v = ((w >> (4 * i)) & 0x000F000Fu) | 0x64006400u;   // fp16 1024 + nibble
+    __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&v), bias);
+    A[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
 struct TcShared {
   uint64_t full[tc::STAGES];
   uint64_t empty[tc::STAGES];
@@ -126,7 +156,7 @@ AF_DEV int owner_of(long long u, long long U, int G) {
   return c;
 }
 
-template <int NT, int EPI>
+template <int NT, int EPI, bool I4>
 AF_DEV void epilogue(const GemvTcArgs& a, float (&acc)[NT][4], int rt, int g, int t) {
   const int r0 = rt * 16 + g, r1 = r0 + 8;
 #pragma unroll
@@ -138,8 +168,8 @@ AF_DEV void epilogue(const GemvTcArgs& a, float (&acc)[NT][4], int rt, int g, in
       const float v0 = acc[n][h], v1 = acc[n][2 + h];
       if (EPI == EPI_SWIGLU) {
         if (r1 >= a.N) continue;
-        float gv = __fmul_rn(v0, h2f(a.scale[r0]));
-        float uv = __fmul_rn(v1, h2f(a.scale[r1]));
+        float gv = I4 ? v0 : __fmul_rn(v0, h2f(a.scale[r0]));
+        float uv = I4 ? v1 : __fmul_rn(v1, h2f(a.scale[r1]));
         if (a.bias) { gv = __fadd_rn(gv, h2f(a.bias[r0])); uv = __fadd_rn(uv, h2f(a.bias[r1])); }
         reinterpret_cast<__half*>(a.y)[(size_t)b * a.ldy + rt * 8 + g] = f2h(silu_f(gv) * uv);
       } else {
@@ -147,7 +177,7 @@ AF_DEV void epilogue(const GemvTcArgs& a, float (&acc)[NT][4], int rt, int g, in
         for (int rr = 0; rr < 2; ++rr) {
           const int row = rr ? r1 : r0;
           if (row >= a.N) continue;
-          float v = __fmul_rn(rr ? v1 : v0, h2f(a.scale[row]));
+          float v = I4 ? (rr ? v1 : v0) : __fmul_rn(rr ? v1 : v0, h2f(a.scale[row]));
           if (a.bias) v = __fadd_rn(v, h2f(a.bias[row]));
           const size_t o = (size_t)b * a.ldy + row;
           if (EPI == EPI_F32) reinterpret_cast<float*>(a.y)[o] = v;
@@ -160,12 +190,13 @@ AF_DEV void epilogue(const GemvTcArgs& a, float (&acc)[NT][4], int rt, int g, in
   }
 }
 
-template <int NT, int EPI>
+template <int NT, int EPI, bool I4>
 __global__ void __launch_bounds__((tc::WARPS + 1) * 32) gemv_tc_kernel(GemvTcArgs a) {
+  using F = tc::Fmt<I4>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  unsigned char* ring = smem_raw;                                          // [STAGES][STAGE_BYTES]
-  TcShared* sh = reinterpret_cast<TcShared*>(smem_raw + tc::STAGES * tc::STAGE_BYTES);
-  __half* xring = reinterpret_cast<__half*>(smem_raw + tc::STAGES * tc::STAGE_BYTES + SH_BYTES);
+  unsigned char* ring = smem_raw;                                          // [STAGES][F::stage]
+  TcShared* sh = reinterpret_cast<TcShared*>(smem_raw + tc::STAGES * F::stage);
+  __half* xring = reinterpret_cast<__half*>(smem_raw + tc::STAGES * F::stage + SH_BYTES);
   const int xslot_halves = a.NB * tc::XSTRIDE;                             // one x chunk
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -207,10 +238,10 @@ __global__ void __launch_bounds__((tc::WARPS + 1) * 32) gemv_tc_kernel(GemvTcArg
         int kt = kc;
         if (!waited) {
           // chunk 0: weights first, then wait for the producer kernel of x, then x
-          for (; kt < kce && in_flight < tc::STAGES; kt += tc::KS) {
-            const int nk = min(tc::KS, kce - kt);
-            mbar_arrive_expect_tx(&sh->full[stage], (uint32_t)nk * tc::UNIT);
-            bulk_g2s(ring + (size_t)stage * tc::STAGE_BYTES, W + ((size_t)rb * KT + kt) * tc::UNIT, nk * tc::UNIT,
+          for (; kt < kce && in_flight < tc::STAGES; kt += F::ks) {
+            const int nk = min(F::ks, kce - kt);
+            mbar_arrive_expect_tx(&sh->full[stage], (uint32_t)nk * F::unit);
+            bulk_g2s(ring + (size_t)stage * F::stage, W + ((size_t)rb * KT + kt) * F::unit, nk * F::unit,
                      &sh->full[stage]);
             ++in_flight;
             if (++stage == tc::STAGES) { stage = 0; phase ^= 1; }
@@ -226,11 +257,11 @@ __global__ void __launch_bounds__((tc::WARPS + 1) * 32) gemv_tc_kernel(GemvTcArg
           bulk_g2s(xring + (size_t)xs * xslot_halves + (size_t)b * tc::XSTRIDE, a.x + (size_t)b * a.ldx + (size_t)kc * 32,
                    xbytes, &sh->xfull[xs]);
         if (++xs == tc::XSLOTS) { xs = 0; xphase ^= 1; }
-        for (; kt < kce; kt += tc::KS) {
-          const int nk = min(tc::KS, kce - kt);
+        for (; kt < kce; kt += F::ks) {
+          const int nk = min(F::ks, kce - kt);
           if (!mbar_wait(&sh->empty[stage], phase ^ 1)) { ok = false; break; }
-          mbar_arrive_expect_tx(&sh->full[stage], (uint32_t)nk * tc::UNIT);
-          bulk_g2s(ring + (size_t)stage * tc::STAGE_BYTES, W + ((size_t)rb * KT + kt) * tc::UNIT, nk * tc::UNIT,
+          mbar_arrive_expect_tx(&sh->full[stage], (uint32_t)nk * F::unit);
+          bulk_g2s(ring + (size_t)stage * F::stage, W + ((size_t)rb * KT + kt) * F::unit, nk * F::unit,
                    &sh->full[stage]);
           in_flight = min(in_flight + 1, tc::STAGES);
           if (++stage == tc::STAGES) { stage = 0; phase ^= 1; }
@@ -273,10 +304,48 @@ __global__ void __launch_bounds__((tc::WARPS + 1) * 32) gemv_tc_kernel(GemvTcArg
       const int kce = min(kc + tc::XKT, ktb);
       if (!mbar_wait(&sh->xfull[xs], xphase)) { stuck = true; break; }
       const __half* xsl = xring + (size_t)xs * xslot_halves;
-      for (int kt = kc; kt < kce; kt += tc::KS) {
-        const int nk = min(tc::KS, kce - kt);
+      for (int kt = kc; kt < kce; kt += F::ks) {
+        const int nk = min(F::ks, kce - kt);
         if (!mbar_wait(&sh->full[stage], phase)) { stuck = true; break; }
-        const unsigned char* sbase = ring + (size_t)stage * tc::STAGE_BYTES + warp * tc::TILE + lane * 16;
+        if constexpr (I4) {
+          const unsigned char* sb = ring + (size_t)stage * F::stage;
+#pragma unroll
+          for (int kk = 0; kk < F::ks; ++kk) {
+            if (kk >= nk) break;
+            const unsigned char* ub = sb + kk * F::unit;
+            const uint2 w = *reinterpret_cast<const uint2*>(ub + warp * F::tile + lane * 8);
+            const __half* gsc = reinterpret_cast<const __half*>(ub + tc::WARPS * F::tile);
+            const float s_lo = h2f(gsc[warp * 16 + g]), s_hi = h2f(gsc[warp * 16 + g + 8]);
+            float tmp[NT][4];
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+#pragma unroll
+              for (int q = 0; q < 4; ++q) tmp[n][q] = 0.f;
+#pragma unroll
+            for (int st = 0; st < 2; ++st) {
+              uint32_t A[4];
+              i4x8_to_frag(st ? w.y : w.x, A);
+              const int kb = (kt - kc + kk) * 32 + st * 16 + 2 * t;
+#pragma unroll
+              for (int n = 0; n < NT; ++n) {
+                const bool real = n * 8 + g < a.NB;
+                const __half* xr = xsl + (size_t)(real ? n * 8 + g : 0) * tc::XSTRIDE + kb;
+                const uint32_t b0 = real ? *reinterpret_cast<const uint32_t*>(xr) : 0u;
+                const uint32_t b1 = real ? *reinterpret_cast<const uint32_t*>(xr + 8) : 0u;
+                mma_16816(tmp[n], A, b0, b1);
+              }
+            }
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+              float (&d)[4] = (kk & 1) ? acc2[n] : acc[n];
+              d[0] = fmaf(s_lo, tmp[n][0], d[0]);
+              d[1] = fmaf(s_lo, tmp[n][1], d[1]);
+              d[2] = fmaf(s_hi, tmp[n][2], d[2]);
+              d[3] = fmaf(s_hi, tmp[n][3], d[3]);
+            }
+          }
+        } else {
+        const unsigned char* sbase = ring + (size_t)stage * F::stage + warp * tc::TILE + lane * 16;
 #pragma unroll
         for (int kk = 0; kk < tc::KS; ++kk) {
           if (kk >= nk) break;
@@ -299,6 +368,7 @@ __global__ void __launch_bounds__((tc::WARPS + 1) * 32) gemv_tc_kernel(GemvTcArg
             }
           }
         }
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh->empty[stage]);
         if (++stage == tc::STAGES) { stage = 0; phase ^= 1; }
@@ -320,7 +390,7 @@ __global__ void __launch_bounds__((tc::WARPS + 1) * 32) gemv_tc_kernel(GemvTcArg
       // this CTA owns the whole row block
       consumer_sync();
       if (*reinterpret_cast<volatile int*>(&sh->cabort)) break;
-      epilogue<NT, EPI>(a, acc, rt, g, t);
+      epilogue<NT, EPI, I4>(a, acc, rt, g, t);
     } else {
       // shared row block: partial to slot j, the last ticket holder reduces in CTA order
       const int cf = owner_of((long long)rb * KT, U, G), cl = owner_of((long long)rb * KT + KT - 1, U, G);
@@ -355,7 +425,7 @@ __global__ void __launch_bounds__((tc::WARPS + 1) * 32) gemv_tc_kernel(GemvTcArg
           }
           acc[n][0] = s0; acc[n][1] = s1; acc[n][2] = s2; acc[n][3] = s3;
         }
-        epilogue<NT, EPI>(a, acc, rt, g, t);
+        epilogue<NT, EPI, I4>(a, acc, rt, g, t);
         if (threadIdx.x == 0) a.counters[rb] = 0;
       }
     }
@@ -381,18 +451,20 @@ static int env_int(const char* name, int dflt) {
   return v && *v ? atoi(v) : dflt;
 }
 
-static size_t smem_bytes(int NB) {
-  return (size_t)tc::STAGES * tc::STAGE_BYTES + SH_BYTES + (size_t)tc::XSLOTS * NB * tc::XSTRIDE * 2;
+static size_t smem_bytes(int NB, bool i4) {
+  return (size_t)tc::STAGES * (i4 ? tc::STAGE_BYTES4 : tc::STAGE_BYTES) + SH_BYTES +
+         (size_t)tc::XSLOTS * NB * tc::XSTRIDE * 2;
 }
 
-template <int NT, int EPI>
+template <int NT, int EPI, bool I4>
 static int grid_for(int NB) {
   static int occ[17] = {};
   if (!occ[NB]) {
-    cudaFuncSetAttribute(gemv_tc_kernel<NT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes(16));
+    cudaFuncSetAttribute(gemv_tc_kernel<NT, EPI, I4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem_bytes(16, I4));
     int o = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, gemv_tc_kernel<NT, EPI>, (tc::WARPS + 1) * 32,
-                                                      smem_bytes(NB)) != cudaSuccess || o < 1)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, gemv_tc_kernel<NT, EPI, I4>, (tc::WARPS + 1) * 32,
+                                                      smem_bytes(NB, I4)) != cudaSuccess || o < 1)
       o = 1;
     const int cap = env_int("AF_TC_CTAS_PER_SM", 4);
     occ[NB] = o < cap ? o : cap;
@@ -400,25 +472,26 @@ static int grid_for(int NB) {
   return occ[NB] * sm_count();
 }
 
+template <bool I4>
 static int grid_any(int NB, int epi) {
   const bool two = NB > 8;
   switch (epi) {
-    case EPI_F32: return two ? grid_for<2, EPI_F32>(NB) : grid_for<1, EPI_F32>(NB);
-    case EPI_F16: return two ? grid_for<2, EPI_F16>(NB) : grid_for<1, EPI_F16>(NB);
-    case EPI_RESID: return two ? grid_for<2, EPI_RESID>(NB) : grid_for<1, EPI_RESID>(NB);
-    default: return two ? grid_for<2, EPI_SWIGLU>(NB) : grid_for<1, EPI_SWIGLU>(NB);
+    case EPI_F32: return two ? grid_for<2, EPI_F32, I4>(NB) : grid_for<1, EPI_F32, I4>(NB);
+    case EPI_F16: return two ? grid_for<2, EPI_F16, I4>(NB) : grid_for<1, EPI_F16, I4>(NB);
+    case EPI_RESID: return two ? grid_for<2, EPI_RESID, I4>(NB) : grid_for<1, EPI_RESID, I4>(NB);
+    default: return two ? grid_for<2, EPI_SWIGLU, I4>(NB) : grid_for<1, EPI_SWIGLU, I4>(NB);
   }
 }
 
 // Stream-K geometry on the host: grid G (all resident), units U = RB*KT, the largest number of CTAs
 // sharing one row block (`maxc`, partial slots per row block).
-static void plan_geometry(int N, int K, int NB, int epi, int* G, int* maxc) {
+static void plan_geometry(int N, int K, int NB, int epi, bool i4, int* G, int* maxc) {
   // G = RB * d: each row block is split evenly between d CTAs, so a CTA's range lies inside one row
   // block (at most one ticket per CTA, none when d == 1). d is the smallest split giving at least
   // `min_ctas` CTAs (enough bytes in flight), bounded by the resident capacity and by KT.
   static const int min_ctas = env_int("AF_TC_MIN_CTAS", 220);
   const long long RB = (N + 63) / 64, KT = (K + 31) / 32;
-  const long long slots = grid_any(NB, epi);
+  const long long slots = i4 ? grid_any<true>(NB, epi) : grid_any<false>(NB, epi);
   long long d = (min_ctas + RB - 1) / RB;
   if (d < 1) d = 1;
   while (d > 1 && RB * d > slots) --d;
@@ -433,36 +506,39 @@ static void plan_geometry(int N, int K, int NB, int epi, int* G, int* maxc) {
 
 void gemv_tc_plan(int N, int K, int NB, int* S_out, int* nt_out) {
   int G, maxc;
-  plan_geometry(N, K, NB > 16 ? 16 : NB, EPI_F32, &G, &maxc);
+  plan_geometry(N, K, NB > 16 ? 16 : NB, EPI_F32, false, &G, &maxc);
   *S_out = maxc;
   *nt_out = NB <= 8 ? 1 : 2;
 }
 
 size_t gemv_tc_scratch_bytes(int N, int K, int NB) {
+  // enough for either weight format and every epilogue (the grid may differ with shared memory)
   const int nb = NB > 16 ? 16 : NB;
-  int G = 0, maxc = 0;
-  plan_geometry(N, K, nb, EPI_F32, &G, &maxc);
+  int G = 0, maxc = 0, maxc4 = 0;
+  plan_geometry(N, K, nb, EPI_F32, false, &G, &maxc);
+  plan_geometry(N, K, nb, EPI_F32, true, &G, &maxc4);
+  if (maxc4 > maxc) maxc = maxc4;
   const int NT = nb <= 8 ? 1 : 2;
   const size_t RB = (N + 63) / 64;
   return tc::CNT_BYTES + RB * maxc * 64 * NT * 8 * 4;
 }
 
-template <int NT, int EPI>
+template <int NT, int EPI, bool I4>
 static cudaError_t launch_tc(GemvTcArgs a, cudaStream_t st, bool pdl) {
   int G = 0, maxc = 0;
-  plan_geometry(a.N, a.K, a.NB, EPI, &G, &maxc);
+  plan_geometry(a.N, a.K, a.NB, EPI, I4, &G, &maxc);
   a.maxc = maxc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G);
   cfg.blockDim = dim3((tc::WARPS + 1) * 32);
-  cfg.dynamicSmemBytes = smem_bytes(a.NB);
+  cfg.dynamicSmemBytes = smem_bytes(a.NB, I4);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemv_tc_kernel<NT, EPI>, a);
+  return cudaLaunchKernelEx(&cfg, gemv_tc_kernel<NT, EPI, I4>, a);
 }
 
 static cudaError_t gemv_tc_launch16(GemvTcArgs a, cudaStream_t st, bool pdl);
@@ -496,8 +572,13 @@ static cudaError_t gemv_tc_launch16(GemvTcArgs a, cudaStream_t st, bool pdl) {
   a.part = reinterpret_cast<float*>(static_cast<char*>(a.scratch) + tc::CNT_BYTES);
   cudaError_t e = cudaErrorInvalidValue;
   const bool two = a.NB > 8;
-#define AF_TC_CASE(EPIV) \
-  if (a.epi == EPIV) e = two ? launch_tc<2, EPIV>(a, st, pdl) : launch_tc<1, EPIV>(a, st, pdl);
+  if (a.wf != W_I8 && a.wf != W_I4G32) return cudaErrorInvalidValue;
+  const bool i4 = a.wf == W_I4G32;
+  if (!i4 && !a.scale) return cudaErrorInvalidValue;
+#define AF_TC_CASE(EPIV)                                                                            \
+  if (a.epi == EPIV)                                                                               \
+    e = i4 ? (two ? launch_tc<2, EPIV, true>(a, st, pdl) : launch_tc<1, EPIV, true>(a, st, pdl))  \
+           : (two ? launch_tc<2, EPIV, false>(a, st, pdl) : launch_tc<1, EPIV, false>(a, st, pdl));
   AF_TC_CASE(EPI_F32)
   AF_TC_CASE(EPI_F16)
   AF_TC_CASE(EPI_RESID)
@@ -550,5 +631,67 @@ cudaError_t pack_i8_tiles(const int8_t* src, int N, int K, uint8_t* dst, cudaStr
 size_t pack_i8_tiles_bytes(int N, int K) {
   return (size_t)((N + 63) / 64 * 64) * ((K + 31) / 32 * 32);
 }
+
+// group-32 int4 [N][K/2] (low nibble first, nibble = code + 8) + scales [N][K/32] ->
+// [Np/64][K/32][4 row tiles x 32 lanes x 8 B | 64 fp16 scales]. Padding rows hold nibble 8 (code 0)
+// and scale 0. One thread per (row block, k tile, 16-byte piece of the unit).
+__global__ void pack_i4_tiles_kernel(const uint8_t* src, const __half* sc, int N, int K, uint8_t* dst, int Np) {
+  const int KT = K / 32;
+  constexpr int PIECES = tc::UNIT4 / 16;                   // 72: 64 weight pieces + 8 scale pieces
+  const size_t total = (size_t)(Np / 64) * KT * PIECES;
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total; idx += (size_t)gridDim.x * blockDim.x) {
+    const int piece = (int)(idx % PIECES);
+    const size_t u = idx / PIECES;
+    const int kt = (int)(u % KT), rb = (int)(u / KT);
+    uint8_t out[16];
+    if (piece < 64) {
+      // pieces 0..63: two lanes (8 bytes each) of row tile piece / 16
+      const int w = piece / 16;
+      for (int half = 0; half < 2; ++half) {
+        const int lane = (piece % 16) * 2 + half;
+        const int g = lane >> 2, t = lane & 3;
+        const int rt = rb * tc::WARPS + w;
+        for (int s = 0; s < 2; ++s) {
+          uint32_t word = 0;
+          const int kb = kt * 32 + s * 16;
+          const int rows[8] = {g, g + 8, g, g + 8, g, g + 8, g, g + 8};
+          const int cols[8] = {2 * t, 2 * t, 2 * t + 8, 2 * t + 8, 2 * t + 1, 2 * t + 1, 2 * t + 9, 2 * t + 9};
+          for (int j = 0; j < 8; ++j) {                     // nibble slot j sits at bit 4j
+            const int r = rt * 16 + rows[j], c = kb + cols[j];
+            uint32_t nib = 8;
+            if (r < N) {
+              const uint8_t b = src[(size_t)r * (K / 2) + c / 2];
+              nib = (c & 1) ? (b >> 4) : (b & 15);
+            }
+            word |= nib << (4 * j);
+          }
+          memcpy(out + half * 8 + s * 4, &word, 4);
+        }
+      }
+    } else {
+      const int r0 = (piece - 64) * 8;
+      for (int i = 0; i < 8; ++i) {
+        const int r = rb * 64 + r0 + i;
+        const __half v = r < N ? sc[(size_t)r * KT + kt] : __float2half(0.f);
+        memcpy(out + 2 * i, &v, 2);
+      }
+    }
+    uint4 v;
+    memcpy(&v, out, 16);
+    reinterpret_cast<uint4*>(dst)[idx] = v;
+  }
+}
+
+cudaError_t pack_i4_tiles(const uint8_t* src, const __half* scales, int N, int K, uint8_t* dst, cudaStream_t st) {
+  if (K % 32) return cudaErrorInvalidValue;
+  const int Np = (N + 63) / 64 * 64;
+  const size_t total = (size_t)(Np / 64) * (K / 32) * (tc::UNIT4 / 16);
+  unsigned blocks = (unsigned)((total + 255) / 256);
+  if (blocks > 65535u * 8) blocks = 65535u * 8;
+  pack_i4_tiles_kernel<<<blocks, 256, 0, st>>>(src, scales, N, K, dst, Np);
+  return cudaGetLastError();
+}
+
+size_t pack_i4_tiles_bytes(int N, int K) { return (size_t)((N + 63) / 64) * (K / 32) * tc::UNIT4; }
 
 }  // namespace af

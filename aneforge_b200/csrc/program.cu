@@ -179,19 +179,21 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     const float floor = (float)c.f("floor");
     if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
     if (!dry) e = rmsnorm_launch(x, xf16, ldx, g, floor, out, ldo, nb, d, st, pdl);
-  } else if (op.kind == "gemv" && c.has("wf") && op.kv.at("wf") == "i8t") {
+  } else if (op.kind == "gemv" && c.has("wf") && (op.kv.at("wf") == "i8t" || op.kv.at("wf") == "i4t")) {
     GemvTcArgs a;
+    const bool i4 = op.kv.at("wf") == "i4t";
+    a.wf = i4 ? W_I4G32 : W_I8;
     const std::string* eps = c.raw("epi");
     if (!eps) { why = c.err; return cudaErrorInvalidValue; }
     a.epi = epi_of(*eps);
-    if (a.epi < 0 || a.epi == EPI_ARGMAX) { why = "bad epi for i8t"; return cudaErrorInvalidValue; }
+    if (a.epi < 0 || a.epi == EPI_ARGMAX) { why = "bad epi for a tiled gemv"; return cudaErrorInvalidValue; }
     a.NB = c.i("nb"); a.N = c.i("n"); a.K = c.i("k");
     a.ldx = c.i("ldx", a.K);
     const int out_cols = a.epi == EPI_SWIGLU ? a.N / 2 : a.N;
     a.ldy = c.i("ldy", out_cols);
     a.x = (const __half*)c.ptr("x", 2 * ((size_t)(a.NB - 1) * a.ldx + a.K));
-    a.w = c.ptr("w", pack_i8_tiles_bytes(a.N, a.K));
-    a.scale = (const __half*)c.ptr("s", 2 * (size_t)a.N);
+    a.w = c.ptr("w", i4 ? pack_i4_tiles_bytes(a.N, a.K) : pack_i8_tiles_bytes(a.N, a.K));
+    if (!i4) a.scale = (const __half*)c.ptr("s", 2 * (size_t)a.N);
     a.bias = (const __half*)c.ptr("bias", 2 * (size_t)a.N, true);
     const size_t esz = (a.epi == EPI_F16 || a.epi == EPI_SWIGLU) ? 2 : 4;
     a.y = c.ptr("y", esz * ((size_t)(a.NB - 1) * a.ldy + out_cols));

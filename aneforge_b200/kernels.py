@@ -137,6 +137,32 @@ def gemv_tc_scratch(N, K, NB, device):
   return torch.zeros((max(n, 1),), dtype=torch.uint8, device=device), n
 
 
+def pack_i4_tiles(packed, scales, N, K):
+  """Group-32 int4 (packed [N, K/2] + scales [N, K/32]) -> tensor-core tiles with the scales inside."""
+  import torch
+  L = R.lib()
+  out = torch.empty((L.af_pack_i4_tiles_bytes(N, K),), dtype=torch.uint8, device=packed.device)
+  R.check(L.af_pack_i4_tiles(_p(packed), _p(scales), N, K, _p(out), _stream(packed)), "af_pack_i4_tiles")
+  return out
+
+
+def gemv_tc_i4(x, tiles, N, K, bias=None, epi=R.EPI_F32, y=None, scratch=None):
+  """Tensor-core group-32 int4 GEMV over pack_i4_tiles output. x [NB, K] fp16."""
+  import torch
+  NB = x.shape[0]
+  cols = N // 2 if epi == R.EPI_SWIGLU else N
+  if y is None:
+    dt = torch.float16 if epi in (R.EPI_F16, R.EPI_SWIGLU) else torch.float32
+    y = torch.zeros((NB, cols), dtype=dt, device=x.device)
+  if scratch is None:
+    scratch, nbytes = gemv_tc_scratch(N, K, NB, x.device)
+  else:
+    nbytes = scratch.numel()
+  R.check(R.lib().af_gemv_tc_i4(epi, _p(x), x.stride(0), _p(tiles), _p(bias), _p(y), y.stride(0), NB, N, K,
+                                _p(scratch), nbytes, _stream(x)), "af_gemv_tc_i4")
+  return y
+
+
 def gemv_tc(x, tiles, scales, N, K, bias=None, epi=R.EPI_F32, y=None, scratch=None):
   """Tensor-core int8 GEMV over packed tiles. x [NB, K] fp16."""
   import torch

@@ -111,12 +111,12 @@ def _emit_linear(pb, ctx, name, lin: DevLinear, x, y, epi, nb=None):
   kv = dict(wf=lin.wf, epi=epi, x=x, w=f"{name}.w", y=y, nb=nb, n=lin.N, k=lin.K)
   if lin.kind == "int8":
     kv["s"] = f"{name}.s"
-  if lin.kind == "int8" and lin.tiled:
+  if lin.kind in ("int8", "int4_g32") and lin.tiled:
     nbytes = R.load_library().af_gemv_tc_scratch_bytes(lin.N, lin.K, nb)
     if nbytes:
       pb.buf("gemv.scr", nbytes, "scratch")          # one split-K scratch shared by every GEMV
       kv["scr"] = "gemv.scr"
-  elif lin.kind == "int4_g32":
+  elif lin.kind == "int4_g32" and not lin.tiled:
     kv["gs"] = f"{name}.s"
   if lin.bias is not None:
     kv["bias"] = f"{name}.b"

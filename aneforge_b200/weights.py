@@ -49,13 +49,15 @@ class DevLinear:
   bias: object         # [N] fp16 or None
   N: int
   K: int
-  tiled: bool = False  # int8 in tensor-core fragment tiles (K % 32 == 0) vs row-major
+  tiled: bool = False  # int8 / int4_g32 in tensor-core fragment tiles (K % 32 == 0) vs row-major
 
   @property
   def wf(self) -> str:
     if self.kind == "int8":
       return "i8t" if self.tiled else "i8"
-    return {"fp16": "f16", "int4_g32": "i4"}[self.kind]
+    if self.kind == "int4_g32":
+      return "i4t" if self.tiled else "i4"
+    return "f16"
 
   @property
   def nbytes(self) -> int:
@@ -112,7 +114,7 @@ def encode_linear(parts, compress, device, biases=None, swiglu=False, atol=0.05,
   enc = [_quantize(P, kind, device) for P in parts]
   if swiglu:
     (wg, sg), (wu, su) = enc
-    half = layout.SWIGLU_HALF_TC if kind == "int8" else layout.SWIGLU_HALF
+    half = layout.SWIGLU_HALF_TC if kind in ("int8", "int4_g32") else layout.SWIGLU_HALF
     w = layout.interleave_blocks(wg, wu, half)
     s = None if sg is None else layout.interleave_blocks(sg, su, half)
   else:
@@ -132,6 +134,11 @@ def encode_linear(parts, compress, device, biases=None, swiglu=False, atol=0.05,
   if kind == "int8" and K % 32 == 0:
     from . import kernels
     w = kernels.pack_i8_tiles(w.contiguous())          # tensor-core fragment tiles
+    tiled = True
+  elif kind == "int4_g32":
+    from . import kernels
+    w = kernels.pack_i4_tiles(w.contiguous(), s.contiguous(), N, K)   # tiles carry their group scales
+    s = None
     tiled = True
   elif kind == "int8" and swiglu:
     # the CUDA-core GEMV pairs gate/up rows in blocks of 4: re-interleave at that granularity

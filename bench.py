@@ -31,10 +31,33 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-CFG = dict(dim=4096, n_layers=32, n_heads=32, n_kv_heads=8, ffn_dim=14336, vocab=128256, rope_base=500000.0,
-           norm_eps=1e-5)
-PROMPT = 512
-METRIC = "int8 decode tokens/s (Llama-3-8B-shaped, greedy)"
+# The benchmarked models (random-init, seeded; no checkpoints). `--model` picks one; the default is
+# the Llama-3-8B-shaped int8 decode the headline metric is quoted on.
+MODELS = {
+  "llama3-8b": dict(
+    cfg=dict(dim=4096, n_layers=32, n_heads=32, n_kv_heads=8, ffn_dim=14336, vocab=128256, rope_base=500000.0,
+             norm_eps=1e-5),
+    compress="int8", prompt=512, qkv_bias=False, traffic_profile="gemv_tc_gate_up_llama8b.md",
+    metric="int8 decode tokens/s (Llama-3-8B-shaped, greedy)",
+    workload="config 3: Llama-3-8B-shaped int8 per-row greedy decode",
+    dtype="int8 weights, fp16 activations, fp32 accumulation"),
+  "qwen2-72b": dict(
+    cfg=dict(dim=8192, n_layers=80, n_heads=64, n_kv_heads=8, ffn_dim=29568, vocab=152064, rope_base=1e6,
+             norm_eps=1e-6),
+    compress="int4_g32", prompt=2048, qkv_bias=True, traffic_profile="gemv_tc_i4_gate_up_qwen72b.md",
+    metric="int4 decode tokens/s (Qwen2-72B-shaped, greedy)",
+    workload="config 4: Qwen2-72B-shaped group-32 int4 greedy decode",
+    dtype="int4 group-32 weights, fp16 activations, fp32 accumulation"),
+}
+MODEL = "llama3-8b"
+CFG = MODELS[MODEL]["cfg"]
+PROMPT = MODELS[MODEL]["prompt"]
+METRIC = MODELS[MODEL]["metric"]
+
+
+def select_model(name):
+  global MODEL, CFG, PROMPT, METRIC
+  MODEL, CFG, PROMPT, METRIC = name, MODELS[name]["cfg"], MODELS[name]["prompt"], MODELS[name]["metric"]
 
 
 def _dist():
@@ -117,32 +140,71 @@ class ClockSampler:
             "samples": len(self.samples), "source": "nvml"}
 
 
-def make_weights(cfg, device, seed=0):
-  """Seeded N(0, 0.02) fp16 weights generated on the device, reference dict layout."""
+class _LazyLayers:
+  """The model's layer list, generated on access (seeded per layer) and not kept: a 72B model's fp16
+  weights (145 GB) never exist at once, only the packed int4 copy the loader keeps."""
+
+  def __init__(self, cfg, device, seed, qkv_bias):
+    self.cfg, self.device, self.seed, self.qkv_bias = cfg, device, seed, qkv_bias
+
+  def __len__(self):
+    return self.cfg.n_layers
+
+  def __getitem__(self, i):
+    import torch
+    if not 0 <= i < len(self):
+      raise IndexError(i)
+    cfg, dev = self.cfg, self.device
+    g = torch.Generator(device=dev)
+    g.manual_seed(self.seed * 1000 + i)
+    R = lambda *s: (torch.randn(*s, generator=g, device=dev, dtype=torch.float32) * 0.02).half()
+    D, dh = cfg.dim, cfg.dh
+    lw = {"wq": R(cfg.n_heads * dh, D), "wk": R(cfg.n_kv_heads * dh, D), "wv": R(cfg.n_kv_heads * dh, D),
+          "wo": R(D, cfg.n_heads * dh), "wgate": R(cfg.ffn_dim, D), "wup": R(cfg.ffn_dim, D),
+          "wdown": R(D, cfg.ffn_dim), "attn_norm": torch.ones(D, device=dev), "mlp_norm": torch.ones(D, device=dev)}
+    if self.qkv_bias:
+      lw.update(q_bias=R(cfg.n_heads * dh), k_bias=R(cfg.n_kv_heads * dh), v_bias=R(cfg.n_kv_heads * dh))
+    return lw
+
+  def __iter__(self):
+    return (self[i] for i in range(len(self)))
+
+
+def make_weights(cfg, device, seed=0, qkv_bias=False):
+  """Seeded N(0, 0.02) fp16 weights generated on the device, reference dict layout (layers lazily)."""
   import torch
   g = torch.Generator(device=device)
   g.manual_seed(seed)
   R = lambda *s: (torch.randn(*s, generator=g, device=device, dtype=torch.float32) * 0.02).half()
-  D, dh = cfg.dim, cfg.dh
-  w = {"embed": R(cfg.vocab, D), "lm_head": R(cfg.vocab, D), "final_norm": torch.ones(D, device=device), "layers": []}
-  for _ in range(cfg.n_layers):
-    w["layers"].append({"wq": R(cfg.n_heads * dh, D), "wk": R(cfg.n_kv_heads * dh, D), "wv": R(cfg.n_kv_heads * dh, D),
-                        "wo": R(D, cfg.n_heads * dh), "wgate": R(cfg.ffn_dim, D), "wup": R(cfg.ffn_dim, D),
-                        "wdown": R(D, cfg.ffn_dim), "attn_norm": torch.ones(D, device=device),
-                        "mlp_norm": torch.ones(D, device=device)})
-  return w
+  D = cfg.dim
+  return {"embed": R(cfg.vocab, D), "lm_head": R(cfg.vocab, D), "final_norm": torch.ones(D, device=device),
+          "layers": _LazyLayers(cfg, device, seed, qkv_bias)}
 
 
-def algorithmic_bytes_per_step(cfg, NB, pos):
-  """Bytes a decode step must move once (each byte counted once per step): int8 codes + fp16 scales of every
-  projection, the fp16 lm_head, norms, KV cache read (positions 0..pos) + the new slot write, and
-  the step's activations in/out."""
+def algorithmic_bytes_per_step(cfg, NB, pos, compress="int8", qkv_bias=False):
+  """Bytes a decode step must move once (each byte counted once per step): codes + fp16 scales of every
+  projection (int8: 1 B/param + one scale per row; int4_g32: 0.5 B/param + one scale per 32), qkv
+  biases, the fp16 lm_head, norms, KV cache read (positions 0..pos) + the new slot write, and the
+  step's activations in/out."""
   D, H, KV, dh, F, V, L = cfg.dim, cfg.n_heads, cfg.n_kv_heads, cfg.dh, cfg.ffn_dim, cfg.vocab, cfg.n_layers
   proj_rows = (H + 2 * KV) * dh + D + 2 * F + D
   proj_params = ((H + 2 * KV) * dh * D) + D * H * dh + 2 * F * D + D * F
-  per_layer = proj_params + 2 * proj_rows + 2 * D * 2
+  if compress == "int4_g32":
+    per_layer = proj_params // 2 + 2 * (proj_params // 32) + 2 * D * 2
+  else:
+    per_layer = proj_params + 2 * proj_rows + 2 * D * 2
+  if qkv_bias:
+    per_layer += 2 * (H + 2 * KV) * dh
   kv = L * NB * (2 * KV * (pos + 1) * dh * 2)
   return L * per_layer + V * D * 2 + D * 2 + kv + NB * (4 + 4)
+
+
+def _run_lin(kernels, R, x, lin, y, scr):
+  """One fused gate|up projection launch in whatever tiled format the loader chose."""
+  if lin.kind == "int4_g32":
+    kernels.gemv_tc_i4(x, lin.w, lin.N, lin.K, epi=R.EPI_SWIGLU, y=y, scratch=scr)
+  else:
+    kernels.gemv_tc(x, lin.w, lin.s, lin.N, lin.K, epi=R.EPI_SWIGLU, y=y, scratch=scr)
 
 
 def run_b200(args):
@@ -157,8 +219,9 @@ def run_b200(args):
   cfg = L.LlamaConfig(**CFG, layers=[L.LayerSpec() for _ in range(CFG["n_layers"])])
   NB = args.batch
   t_load = time.perf_counter()
-  w = make_weights(cfg, dev, seed=1234 + rank)
-  m = L.LlamaPrefill(cfg, w, compress="int8", device=local)
+  spec = MODELS[MODEL]
+  w = make_weights(cfg, dev, seed=1234 + rank, qkv_bias=spec["qkv_bias"])
+  m = L.LlamaPrefill(cfg, w, compress=spec["compress"], device=local)
   m._load()
   del w
   torch.cuda.empty_cache()
@@ -239,13 +302,13 @@ def run_b200(args):
   scr, _ = kernels.gemv_tc_scratch(gu[0].N, gu[0].K, NB, dev)
   with torch.cuda.stream(stream):
     for i in range(cfg.n_layers):
-      kernels.gemv_tc(x, gu[i].w, gu[i].s, gu[i].N, gu[i].K, epi=R.EPI_SWIGLU, y=y, scratch=scr)
+      _run_lin(kernels, R, x, gu[i], y, scr)
     torch.cuda.synchronize()
     kgraph = torch.cuda.CUDAGraph()                       # launches back to back, not paced by the host
     with torch.cuda.graph(kgraph, stream=stream):
       for i in range(reps):
         l = gu[i % cfg.n_layers]
-        kernels.gemv_tc(x, l.w, l.s, l.N, l.K, epi=R.EPI_SWIGLU, y=y, scratch=scr)
+        _run_lin(kernels, R, x, l, y, scr)
     kgraph.replay()
     torch.cuda.synchronize()
     k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -257,24 +320,26 @@ def run_b200(args):
   del kgraph
   gu_bytes = gu[0].nbytes + NB * cfg.dim * 2 + NB * cfg.ffn_dim * 2
   peak, peak_kind = _peaks()
-  step_bytes = algorithmic_bytes_per_step(cfg, NB, PROMPT + args.warmup + args.steps // 2)
+  step_bytes = algorithmic_bytes_per_step(cfg, NB, PROMPT + args.warmup + args.steps // 2, spec["compress"],
+                                          spec["qkv_bias"])
   result = None
   if rank == 0:
     achieved = gu_bytes / (k_us * 1e-6) / 1e9
     result = {
       "metric": METRIC, "value": round(tok_s, 2), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
       "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
-      "vs_baseline": None, "dtype": "int8 weights, fp16 activations, fp32 accumulation", "data": "synthetic",
-      "config": {"workload": "BASELINE config 3: Llama-3-8B-shaped int8 greedy decode", "model": "llama-3-8b-shaped",
+      "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic",
+      "config": {"workload": spec["workload"], "model": MODEL + "-shaped",
                  "global_batch": NB * ws, "batch_per_gpu": NB, "seq_len": PROMPT, "decode_pos": f"{PROMPT}..{M}",
                  "parallelism": f"replicas{ws}" if ws > 1 else "single",
-                 "l2": "weights 7.0 GB per step >> 126 MB L2 (no flush needed)"},
+                 "l2": f"weights {step_bytes / 1e9:.1f} GB per step >> 126 MB L2 (no flush needed)"},
       "e2e": {"value": round(e2e_tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * NB,
               "d2h_bytes_per_step": 4 * NB,
               "how": "program API, pinned host token ids in/out every step, host sync per step"},
-      "roofline": {"bound": "hbm", "kernel": "gemv_tc int8 gate|up + silu*mul (28672x4096, mma.sync)", "achieved": round(achieved, 1),
-                   "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": profile_traffic(),
-                   "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/gemv_tc_gate_up_llama8b.md",
+      "roofline": {"bound": "hbm", "kernel": f"gemv_tc {gu[0].kind} gate|up + silu*mul ({gu[0].N}x{gu[0].K}, mma.sync)",
+                   "achieved": round(achieved, 1),
+                   "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": profile_traffic(spec["traffic_profile"]),
+                   "traffic_source": f"ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/{spec['traffic_profile']}",
                    "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
                    "launch_us": round(k_us, 2), "algorithmic_bytes": gu_bytes},
       "step_roofline": {"algorithmic_bytes": int(step_bytes), "achieved_gbs": round(step_bytes / (ms_step * 1e-3) / 1e9, 1),
@@ -390,13 +455,14 @@ def profile_traffic(name="gemv_tc_gate_up_llama8b.md"):
 
 def cpu_baseline(steps=3, layers=1):
   """The reference path on the host: oracle decode of a `layers`-deep slice of the same model +
-  the full lm_head, scaled to 32 layers. Returns (tokens/s, description)."""
+  the full lm_head, scaled to the model's depth. Returns (tokens/s, description)."""
   from oracle.model import OracleModel, Config, random_llama_weights
+  spec = MODELS[MODEL]
   cfg = Config(dim=CFG["dim"], n_layers=layers, n_heads=CFG["n_heads"], n_kv_heads=CFG["n_kv_heads"],
-               ffn_dim=CFG["ffn_dim"], vocab=CFG["vocab"], rope_base=CFG["rope_base"])
-  w = random_llama_weights(cfg, seed=5)
+               ffn_dim=CFG["ffn_dim"], vocab=CFG["vocab"], rope_base=CFG["rope_base"], norm_eps=CFG["norm_eps"])
+  w = random_llama_weights(cfg, seed=5, qkv_bias=spec["qkv_bias"])
   w["embed"] = np.zeros((cfg.vocab, cfg.dim), np.float16)   # only gathered rows are read; values do not change the time
-  om = OracleModel(cfg, w, "int8", precision="device")
+  om = OracleModel(cfg, w, spec["compress"], precision="device")
   M = PROMPT + steps + 2
   om._tables(M)
   caches = om.new_caches(M)
@@ -415,7 +481,8 @@ def cpu_baseline(steps=3, layers=1):
     t2 = time.perf_counter()
     t_layers += t1 - t0; t_head += t2 - t1
   per_tok = t_layers / steps * (CFG["n_layers"] / layers) + t_head / steps
-  return 1.0 / per_tok, f"{steps} decode steps of a {layers}-layer slice + full lm_head, scaled to 32 layers"
+  return 1.0 / per_tok, (f"{steps} decode steps of a {layers}-layer slice + full lm_head, scaled to "
+                         f"{CFG['n_layers']} layers")
 
 
 def blas_threads():
@@ -432,6 +499,7 @@ def main():
   ap.add_argument("--steps", type=int, default=200)
   ap.add_argument("--warmup", type=int, default=10)
   ap.add_argument("--batch", type=int, default=1)
+  ap.add_argument("--model", default="llama3-8b", choices=sorted(MODELS))
   ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
   ap.add_argument("--no-cpu-baseline", action="store_true")
   ap.add_argument("--kernel", default=None,
@@ -440,6 +508,7 @@ def main():
   ap.add_argument("--profile-region", action="store_true",
                   help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
   args = ap.parse_args()
+  select_model(args.model)
   ws, rank, _ = _dist()
   if args.kernel:
     for name in args.kernel.split(","):
@@ -456,7 +525,7 @@ def main():
     print(json.dumps({"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tokens/s",
                       "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
                       "scaling": "weak", "vs_baseline": None, "dtype": "int8 weights, fp32 numpy", "data": "synthetic",
-                      "config": {"workload": "BASELINE config 3: Llama-3-8B-shaped int8 greedy decode",
+                      "config": {"workload": MODELS[MODEL]["workload"],
                                  "global_batch": args.batch, "seq_len": PROMPT},
                       "cpu_baseline": {"value": round(v, 4), "unit": "tokens/s", "cores": blas_threads(),
                                        "kind": "port", "sample": how},

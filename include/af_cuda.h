@@ -137,6 +137,16 @@ size_t af_gemv_tc_scratch_bytes(int n, int k, int nb);
 int af_gemv_tc(int epi, const uint16_t* x, int ldx, const void* tiles, const uint16_t* scales, const uint16_t* bias,
                void* y, int ldy, int nb, int n, int k, void* scratch, size_t scratch_bytes, void* stream);
 
+/* Group-32 int4 on the tensor pipe: codes from af_quantize_g32_i4 (packed [n][k/2] + scales [n][k/32])
+ * re-packed once into 16x32 fragment tiles with each k tile's 64 row scales appended
+ * ([ceil(n/64)][k/32][4 x 256 B | 64 fp16], k % 32 == 0). y = sum over groups of s_g * (x . codes_g),
+ * fp32 accumulation, same epilogues and scratch rule as af_gemv_tc. Replaces the reference `matmul`
+ * (_compile.py:375-385) for this build's int4_g32 weights (no reference counterpart for the format). */
+size_t af_pack_i4_tiles_bytes(int n, int k);
+int af_pack_i4_tiles(const uint8_t* packed, const uint16_t* scales, int n, int k, uint8_t* tiles, void* stream);
+int af_gemv_tc_i4(int epi, const uint16_t* x, int ldx, const void* tiles, const uint16_t* bias, void* y, int ldy,
+                  int nb, int n, int k, void* scratch, size_t scratch_bytes, void* stream);
+
 /* lm_head GEMV + greedy argmax (lowest index on ties): replaces the host `hidden @ lm_head.T` and
  * np.argmax of LlamaPrefill._logits/_sample (aneforge/llm.py:349-355, :407-410). `logits` [nb][n]
  * may be NULL; `pos_advance` (may be NULL) is incremented per row. Scratch: see _scratch; it must be

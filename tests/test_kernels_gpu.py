@@ -274,3 +274,46 @@ def test_gemv_tensor_core_shared_scratch_across_shapes(K):
     y = K.gemv_tc(cuda(x), K.pack_i8_tiles(cuda(qr)), cuda(sr), N, Kd, scratch=scratch).cpu().numpy()
     ref = (x.astype(F32) @ qr.astype(F32).T) * sr.astype(F32)
     assert np.abs(y - ref).max() <= 1e-4 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("NB", [1, 3, 8, 9, 16, 20])
+@pytest.mark.parametrize("N,Kd", [(16, 32), (37, 64), (520, 2048), (300, 3584), (7392, 8192), (8192, 3712)])
+def test_gemv_tensor_core_int4_g32(K, NB, N, Kd):
+  """Group-32 int4 tiles: y = sum_g s_g (x . codes_g) against the oracle's fp32 dequantised matrix."""
+  from aneforge_b200 import _runtime as R
+  rng = np.random.default_rng(NB * 11 + N)
+  W = (rng.standard_normal((N, Kd), dtype=F32) * F32(0.02)).astype(F16)
+  x = rng.standard_normal((NB, Kd), dtype=F32).astype(F16)
+  bias = (rng.standard_normal(N, dtype=F32) * F32(0.1)).astype(F16)
+  p, s = Q.quantize_g32_int4(W)
+  Wd = Q.dequant_g32_int4(p, s)
+  tiles = K.pack_i4_tiles(cuda(p), cuda(s), N, Kd)
+  assert tiles.numel() == (-(-N // 64)) * (Kd // 32) * 1152
+  ref = x.astype(F32) @ Wd.T + bias.astype(F32)
+  y = K.gemv_tc_i4(cuda(x), tiles, N, Kd, bias=cuda(bias), epi=R.EPI_F32).cpu().numpy()
+  assert np.abs(y - ref).max() <= 1e-4 * np.abs(ref).max() + 1e-5
+  y0 = rng.standard_normal((NB, N), dtype=F32)
+  yr = torch.from_numpy(y0.copy()).cuda()
+  K.gemv_tc_i4(cuda(x), tiles, N, Kd, bias=cuda(bias), epi=R.EPI_RESID, y=yr)
+  assert np.abs(yr.cpu().numpy() - (y0 + ref)).max() <= 1e-4 * np.abs(y0 + ref).max()
+  y16 = K.gemv_tc_i4(cuda(x), tiles, N, Kd, bias=cuda(bias), epi=R.EPI_F16).cpu().numpy()
+  assert np.abs(y16.astype(F32) - ref).max() <= 2 ** -10 * np.abs(ref).max() + 1e-4
+
+
+@pytest.mark.parametrize("NB", [1, 4, 16])
+def test_gemv_tensor_core_int4_swiglu(K, NB):
+  from aneforge_b200 import _runtime as R
+  from aneforge_b200.layout import interleave_blocks, SWIGLU_HALF_TC
+  rng = np.random.default_rng(25)
+  F, Kd = 160, 1024
+  Wg = (rng.standard_normal((F, Kd), dtype=F32) * F32(0.05)).astype(F16)
+  Wu = (rng.standard_normal((F, Kd), dtype=F32) * F32(0.05)).astype(F16)
+  x = rng.standard_normal((NB, Kd), dtype=F32).astype(F16)
+  pg, sg = Q.quantize_g32_int4(Wg); pu, su = Q.quantize_g32_int4(Wu)
+  pp = interleave_blocks(pg, pu, SWIGLU_HALF_TC); sp = interleave_blocks(sg, su, SWIGLU_HALF_TC)
+  y = K.gemv_tc_i4(cuda(x), K.pack_i4_tiles(cuda(pp), cuda(sp), 2 * F, Kd), 2 * F, Kd,
+                   epi=R.EPI_SWIGLU).cpu().numpy()
+  xf = x.astype(F32)
+  g = xf @ Q.dequant_g32_int4(pg, sg).T; u = xf @ Q.dequant_g32_int4(pu, su).T
+  ref = OM.silu(g) * u
+  assert relerr(y.astype(F32), ref) < 2e-3 and cosine(y, ref) > 0.9999
