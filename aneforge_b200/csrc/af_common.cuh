@@ -5,6 +5,7 @@
 #include <stdint.h>
 
 #define AF_DEV __device__ __forceinline__
+#define AF_HD __host__ __device__ __forceinline__
 
 // Error codes a kernel may record in the program's device error word (first error wins).
 enum AfDevErr : int {

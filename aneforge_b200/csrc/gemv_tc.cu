@@ -43,7 +43,8 @@
 namespace af {
 
 namespace tc {
-constexpr int WARPS = 4;                   // consumer warps = row tiles per row block
+constexpr int WARPS = 4;                   // row tiles per row block
+constexpr int CWARPS = 8;                  // consumer warps: two per row tile (even / odd k tiles)
 constexpr int KS = 4;                      // k tiles per weight stage (int8)
 constexpr int TILE = 512;                  // bytes per 16x32 int8 tile
 constexpr int UNIT = WARPS * TILE;         // one k tile of one row block
@@ -55,7 +56,7 @@ constexpr int STAGE_BYTES4 = KS4 * UNIT4;  // 9 KB
 constexpr int STAGE_MAX = STAGE_BYTES4 > STAGE_BYTES ? STAGE_BYTES4 : STAGE_BYTES;
 constexpr int STAGES = 6;
 constexpr int XKT = 16;                    // k tiles per x chunk
-constexpr int XSTRIDE = XKT * 32 + 8;      // halves per staged x row (+8: conflict-free B loads)
+constexpr int XSTRIDE = XKT * 32 + 32;     // halves per staged x row (+32: rows 16 banks apart)
 constexpr int XSLOTS = 2;
 constexpr size_t CNT_BYTES = 16384;        // scratch: per-row-block tickets, then partial slots
 constexpr long long WAIT_LIMIT = 1ll << 26;
@@ -101,7 +102,7 @@ AF_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) 
                ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 
-AF_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(tc::WARPS * 32) : "memory"); }
+AF_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(tc::CWARPS * 32) : "memory"); }
 
 AF_DEV void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -109,6 +110,16 @@ AF_DEV void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32
       "{%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// d = a . b (a fresh accumulation: the C operand is zero)
+AF_DEV void mma_16816_z(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  const float z = 0.f;
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(z));
 }
 
 // 4 int8 codes (bytes of w) -> two half2: (byte0, byte1) and (byte2, byte3), exact.
@@ -123,15 +134,29 @@ AF_DEV void i8x4_to_h2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
   hi = *reinterpret_cast<uint32_t*>(&h);
 }
 
-// 8 int4 nibbles (code + 8) of one k-step -> the four A-fragment registers, exact.
+// 8 int4 nibbles (code + 8) of one k-step -> the four A-fragment registers, exact. A nibble in bits
+// 0-3 of a half becomes fp16 1024 + n (minus 1032 = code); one in bits 4-7 becomes 1024 + 16 n
+// (times 1/16 minus 72 = code); the second pair of slots is reached through w >> 8.
+AF_DEV uint32_t lop_or(uint32_t w, uint32_t mask) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(w), "r"(mask), "r"(0x64006400u));   // (w & mask) | magic
+  return r;
+}
 AF_DEV void i4x8_to_frag(uint32_t w, uint32_t (&A)[4]) {
-  const __half2 bias = __half2half2(__ushort_as_half(0x6408));  // 1032 = 1024 + 8
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t v = ((w >> (4 * i)) & 0x000F000Fu) | 0x64006400u;   // fp16 1024 + nibble
-    __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&v), bias);
-    A[i] = *reinterpret_cast<uint32_t*>(&h);
-  }
+  const __half2 b_lo = __half2half2(__ushort_as_half(0x6408));   // 1032
+  const __half2 m_hi = __half2half2(__ushort_as_half(0x2C00));   // 1/16
+  const __half2 b_hi = __half2half2(__ushort_as_half(0xD480));   // -72
+  const uint32_t w8 = w >> 8;
+  uint32_t v0 = lop_or(w, 0x000F000Fu), v1 = lop_or(w, 0x00F000F0u);
+  uint32_t v2 = lop_or(w8, 0x000F000Fu), v3 = lop_or(w8, 0x00F000F0u);
+  __half2 h0 = __hsub2(*reinterpret_cast<const __half2*>(&v0), b_lo);
+  __half2 h1 = __hfma2(*reinterpret_cast<const __half2*>(&v1), m_hi, b_hi);
+  __half2 h2 = __hsub2(*reinterpret_cast<const __half2*>(&v2), b_lo);
+  __half2 h3 = __hfma2(*reinterpret_cast<const __half2*>(&v3), m_hi, b_hi);
+  A[0] = *reinterpret_cast<uint32_t*>(&h0);
+  A[1] = *reinterpret_cast<uint32_t*>(&h1);
+  A[2] = *reinterpret_cast<uint32_t*>(&h2);
+  A[3] = *reinterpret_cast<uint32_t*>(&h3);
 }
 
 struct TcShared {
@@ -191,7 +216,7 @@ AF_DEV void epilogue(const GemvTcArgs& a, float (&acc)[NT][4], int rt, int g, in
 }
 
 template <int NT, int EPI, bool I4>
-__global__ void __launch_bounds__((tc::WARPS + 1) * 32) gemv_tc_kernel(GemvTcArgs a) {
+__global__ void __launch_bounds__((tc::CWARPS + 1) * 32) gemv_tc_kernel(GemvTcArgs a) {
   using F = tc::Fmt<I4>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   unsigned char* ring = smem_raw;                                          // [STAGES][F::stage]
@@ -209,18 +234,18 @@ __global__ void __launch_bounds__((tc::WARPS + 1) * 32) gemv_tc_kernel(GemvTcArg
   if (threadIdx.x == 0) {
     for (int s = 0; s < tc::STAGES; ++s) {
       mbar_init(&sh->full[s], 1);
-      mbar_init(&sh->empty[s], tc::WARPS);
+      mbar_init(&sh->empty[s], tc::CWARPS);
     }
     for (int s = 0; s < tc::XSLOTS; ++s) {
       mbar_init(&sh->xfull[s], 1);
-      mbar_init(&sh->xempty[s], tc::WARPS);
+      mbar_init(&sh->xempty[s], tc::CWARPS);
     }
     sh->cabort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
 
-  if (warp == tc::WARPS) {
+  if (warp == tc::CWARPS) {
     // -------------------------------------------------------------- producer (one thread)
     if (lane != 0) return;
     const char* W = reinterpret_cast<const char*>(a.w);
@@ -284,8 +309,15 @@ __global__ void __launch_bounds__((tc::WARPS + 1) * 32) gemv_tc_kernel(GemvTcArg
     return;
   }
 
-  // ---------------------------------------------------------------- consumers (4 warps)
+  // ---------------------------------------------------------------- consumers (8 warps)
+  // Warps w and w + 4 share row tile w of the row block: within every stage the first multiplies the
+  // even k tiles, the second the odd ones; their sums meet in shared memory at the end of each
+  // row-block range. The tiles' columns are permuted so that a lane's B fragments for both k-steps
+  // of a k tile are 8 consecutive x values: one 16-byte shared load per k tile.
   const int g = lane >> 2, t = lane & 3;
+  const int rtw = warp & 3, par = warp >> 2;
+  float* red = reinterpret_cast<float*>(smem_raw + tc::STAGES * F::stage + SH_BYTES +
+                                        (size_t)tc::XSLOTS * xslot_halves * 2);       // [4][32][NT*4]
   pdl_wait();
   pdl_trigger();
   int stage = 0, xs = 0;
@@ -294,11 +326,11 @@ __global__ void __launch_bounds__((tc::WARPS + 1) * 32) gemv_tc_kernel(GemvTcArg
   while (u < u1) {
     const int rb = (int)(u / KT), kta = (int)(u % KT);
     const int ktb = (int)min((long long)KT, kta + (u1 - u));
-    float acc[NT][4], acc2[NT][4];              // two independent MMA chains (even / odd k tiles)
+    float acc[NT][4];
 #pragma unroll
     for (int n = 0; n < NT; ++n)
 #pragma unroll
-      for (int q = 0; q < 4; ++q) { acc[n][q] = 0.f; acc2[n][q] = 0.f; }
+      for (int q = 0; q < 4; ++q) acc[n][q] = 0.f;
     bool stuck = false;
     for (int kc = kta; kc < ktb && !stuck; kc += tc::XKT) {
       const int kce = min(kc + tc::XKT, ktb);
@@ -307,67 +339,49 @@ __global__ void __launch_bounds__((tc::WARPS + 1) * 32) gemv_tc_kernel(GemvTcArg
       for (int kt = kc; kt < kce; kt += F::ks) {
         const int nk = min(F::ks, kce - kt);
         if (!mbar_wait(&sh->full[stage], phase)) { stuck = true; break; }
-        if constexpr (I4) {
-          const unsigned char* sb = ring + (size_t)stage * F::stage;
+        const unsigned char* sb = ring + (size_t)stage * F::stage;
 #pragma unroll
-          for (int kk = 0; kk < F::ks; ++kk) {
-            if (kk >= nk) break;
-            const unsigned char* ub = sb + kk * F::unit;
-            const uint2 w = *reinterpret_cast<const uint2*>(ub + warp * F::tile + lane * 8);
-            const __half* gsc = reinterpret_cast<const __half*>(ub + tc::WARPS * F::tile);
-            const float s_lo = h2f(gsc[warp * 16 + g]), s_hi = h2f(gsc[warp * 16 + g + 8]);
-            float tmp[NT][4];
+        for (int kk = 0; kk < F::ks; kk += 2) {
+          const int k2 = kk + par;
+          if (k2 >= nk) break;
+          uint4 xb[NT];
 #pragma unroll
-            for (int n = 0; n < NT; ++n)
-#pragma unroll
-              for (int q = 0; q < 4; ++q) tmp[n][q] = 0.f;
-#pragma unroll
-            for (int st = 0; st < 2; ++st) {
-              uint32_t A[4];
-              i4x8_to_frag(st ? w.y : w.x, A);
-              const int kb = (kt - kc + kk) * 32 + st * 16 + 2 * t;
-#pragma unroll
-              for (int n = 0; n < NT; ++n) {
-                const bool real = n * 8 + g < a.NB;
-                const __half* xr = xsl + (size_t)(real ? n * 8 + g : 0) * tc::XSTRIDE + kb;
-                const uint32_t b0 = real ? *reinterpret_cast<const uint32_t*>(xr) : 0u;
-                const uint32_t b1 = real ? *reinterpret_cast<const uint32_t*>(xr + 8) : 0u;
-                mma_16816(tmp[n], A, b0, b1);
-              }
-            }
-#pragma unroll
-            for (int n = 0; n < NT; ++n) {
-              float (&d)[4] = (kk & 1) ? acc2[n] : acc[n];
-              d[0] = fmaf(s_lo, tmp[n][0], d[0]);
-              d[1] = fmaf(s_lo, tmp[n][1], d[1]);
-              d[2] = fmaf(s_hi, tmp[n][2], d[2]);
-              d[3] = fmaf(s_hi, tmp[n][3], d[3]);
-            }
+          for (int n = 0; n < NT; ++n) {
+            const int row = n * 8 + g;
+            xb[n] = row < a.NB ? *reinterpret_cast<const uint4*>(xsl + (size_t)row * tc::XSTRIDE + (kt - kc + k2) * 32 + 8 * t)
+                               : make_uint4(0u, 0u, 0u, 0u);
           }
-        } else {
-        const unsigned char* sbase = ring + (size_t)stage * F::stage + warp * tc::TILE + lane * 16;
-#pragma unroll
-        for (int kk = 0; kk < tc::KS; ++kk) {
-          if (kk >= nk) break;
-          const uint4 w = *reinterpret_cast<const uint4*>(sbase + kk * tc::UNIT);
-          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-          for (int st = 0; st < 2; ++st) {
+          if constexpr (I4) {
+            const unsigned char* ub = sb + k2 * F::unit;
+            const uint2 w = *reinterpret_cast<const uint2*>(ub + rtw * F::tile + lane * 8);
+            const float2 sc = __half22float2(
+                *reinterpret_cast<const __half2*>(ub + tc::WARPS * F::tile + (rtw * 16 + 2 * g) * 2));
             uint32_t A[4];
-            i8x4_to_h2x2(wv[2 * st], A[0], A[1]);
-            i8x4_to_h2x2(wv[2 * st + 1], A[2], A[3]);
-            const int kb = (kt - kc + kk) * 32 + st * 16 + 2 * t;
+            float tmp[NT][4];
+            i4x8_to_frag(w.x, A);
+#pragma unroll
+            for (int n = 0; n < NT; ++n) mma_16816_z(tmp[n], A, xb[n].x, xb[n].y);
+            i4x8_to_frag(w.y, A);
 #pragma unroll
             for (int n = 0; n < NT; ++n) {
-              const bool real = n * 8 + g < a.NB;
-              const __half* xr = xsl + (size_t)(real ? n * 8 + g : 0) * tc::XSTRIDE + kb;
-              const uint32_t b0 = real ? *reinterpret_cast<const uint32_t*>(xr) : 0u;
-              const uint32_t b1 = real ? *reinterpret_cast<const uint32_t*>(xr + 8) : 0u;
-              if (kk & 1) mma_16816(acc2[n], A, b0, b1);
-              else mma_16816(acc[n], A, b0, b1);
+              mma_16816(tmp[n], A, xb[n].z, xb[n].w);
+              acc[n][0] = fmaf(sc.x, tmp[n][0], acc[n][0]);
+              acc[n][1] = fmaf(sc.x, tmp[n][1], acc[n][1]);
+              acc[n][2] = fmaf(sc.y, tmp[n][2], acc[n][2]);
+              acc[n][3] = fmaf(sc.y, tmp[n][3], acc[n][3]);
             }
+          } else {
+            const uint4 w = *reinterpret_cast<const uint4*>(sb + k2 * F::unit + rtw * F::tile + lane * 16);
+            uint32_t A[4];
+            i8x4_to_h2x2(w.x, A[0], A[1]);
+            i8x4_to_h2x2(w.y, A[2], A[3]);
+#pragma unroll
+            for (int n = 0; n < NT; ++n) mma_16816(acc[n], A, xb[n].x, xb[n].y);
+            i8x4_to_h2x2(w.z, A[0], A[1]);
+            i8x4_to_h2x2(w.w, A[2], A[3]);
+#pragma unroll
+            for (int n = 0; n < NT; ++n) mma_16816(acc[n], A, xb[n].z, xb[n].w);
           }
-        }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh->empty[stage]);
@@ -377,40 +391,51 @@ __global__ void __launch_bounds__((tc::WARPS + 1) * 32) gemv_tc_kernel(GemvTcArg
       if (lane == 0) mbar_arrive(&sh->xempty[xs]);
       if (++xs == tc::XSLOTS) { xs = 0; xphase ^= 1; }
     }
-#pragma unroll
-    for (int n = 0; n < NT; ++n)
-#pragma unroll
-      for (int q = 0; q < 4; ++q) acc[n][q] += acc2[n][q];
     if (stuck) {
       af_set_err(a.err, AF_DEV_WAIT_TIMEOUT);
       *reinterpret_cast<volatile int*>(&sh->cabort) = 1;
     }
-    const int rt = rb * tc::WARPS + warp;
+    // odd-tile warps hand their sums to the even-tile warps of the same row tile
+    float* rw = red + ((size_t)rtw * 32 + lane) * (NT * 4);
+    if (par) {
+#pragma unroll
+      for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) rw[n * 4 + q] = acc[n][q];
+    }
+    consumer_sync();
+    if (*reinterpret_cast<volatile int*>(&sh->cabort)) break;
+    if (!par) {
+#pragma unroll
+      for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[n][q] += rw[n * 4 + q];
+    }
+    const int rt = rb * tc::WARPS + rtw;
     if (kta == 0 && ktb == KT) {
       // this CTA owns the whole row block
-      consumer_sync();
-      if (*reinterpret_cast<volatile int*>(&sh->cabort)) break;
-      epilogue<NT, EPI, I4>(a, acc, rt, g, t);
+      if (!par) epilogue<NT, EPI, I4>(a, acc, rt, g, t);
     } else {
       // shared row block: partial to slot j, the last ticket holder reduces in CTA order
       const int cf = owner_of((long long)rb * KT, U, G), cl = owner_of((long long)rb * KT + KT - 1, U, G);
       const int nc = cl - cf + 1, j = c - cf;
       constexpr int NBP = NT * 8;
       float* slot = a.part + (((size_t)rb * a.maxc + j) * 64) * NBP;
-      const int r0 = warp * 16 + g, r1 = r0 + 8;
+      const int r0 = rtw * 16 + g, r1 = r0 + 8;
+      if (!par) {
 #pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        const int c0 = n * 8 + 2 * t;
-        if (c0 >= a.NB) continue;
-        __stcg(reinterpret_cast<float2*>(slot + (size_t)r0 * NBP + c0), make_float2(acc[n][0], acc[n][1]));
-        __stcg(reinterpret_cast<float2*>(slot + (size_t)r1 * NBP + c0), make_float2(acc[n][2], acc[n][3]));
+        for (int n = 0; n < NT; ++n) {
+          const int c0 = n * 8 + 2 * t;
+          if (c0 >= a.NB) continue;
+          __stcg(reinterpret_cast<float2*>(slot + (size_t)r0 * NBP + c0), make_float2(acc[n][0], acc[n][1]));
+          __stcg(reinterpret_cast<float2*>(slot + (size_t)r1 * NBP + c0), make_float2(acc[n][2], acc[n][3]));
+        }
+        __threadfence();
       }
-      __threadfence();
       consumer_sync();
-      if (*reinterpret_cast<volatile int*>(&sh->cabort)) break;
       if (threadIdx.x == 0) sh->ticket = atomicAdd(a.counters + rb, 1) == nc - 1;
       consumer_sync();
-      if (sh->ticket) {
+      if (sh->ticket && !par) {
         __threadfence();
 #pragma unroll
         for (int n = 0; n < NT; ++n) {
@@ -429,6 +454,7 @@ __global__ void __launch_bounds__((tc::WARPS + 1) * 32) gemv_tc_kernel(GemvTcArg
         if (threadIdx.x == 0) a.counters[rb] = 0;
       }
     }
+    consumer_sync();          // the reduction slots in shared memory are free for the next range
     u += ktb - kta;
   }
 }
@@ -452,8 +478,9 @@ static int env_int(const char* name, int dflt) {
 }
 
 static size_t smem_bytes(int NB, bool i4) {
+  // weight ring | barriers | x ring | odd-warp sums [4 row tiles][32 lanes][8 floats]
   return (size_t)tc::STAGES * (i4 ? tc::STAGE_BYTES4 : tc::STAGE_BYTES) + SH_BYTES +
-         (size_t)tc::XSLOTS * NB * tc::XSTRIDE * 2;
+         (size_t)tc::XSLOTS * NB * tc::XSTRIDE * 2 + tc::WARPS * 32 * 8 * 4;
 }
 
 template <int NT, int EPI, bool I4>
@@ -463,7 +490,7 @@ static int grid_for(int NB) {
     cudaFuncSetAttribute(gemv_tc_kernel<NT, EPI, I4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem_bytes(16, I4));
     int o = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, gemv_tc_kernel<NT, EPI, I4>, (tc::WARPS + 1) * 32,
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, gemv_tc_kernel<NT, EPI, I4>, (tc::CWARPS + 1) * 32,
                                                       smem_bytes(NB, I4)) != cudaSuccess || o < 1)
       o = 1;
     const int cap = env_int("AF_TC_CTAS_PER_SM", 4);
@@ -530,7 +557,7 @@ static cudaError_t launch_tc(GemvTcArgs a, cudaStream_t st, bool pdl) {
   a.maxc = maxc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G);
-  cfg.blockDim = dim3((tc::WARPS + 1) * 32);
+  cfg.blockDim = dim3((tc::CWARPS + 1) * 32);
   cfg.dynamicSmemBytes = smem_bytes(a.NB, I4);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -588,6 +615,10 @@ static cudaError_t gemv_tc_launch16(GemvTcArgs a, cudaStream_t st, bool pdl) {
   return cudaGetLastError();
 }
 
+// Column of the k tile that mma k-index j of k-step s multiplies: lane t's B fragments (k 2t, 2t+1,
+// 2t+8, 2t+9 of both k-steps) become the 8 consecutive x values [8t, 8t + 8) of the k tile.
+AF_HD int tile_col(int s, int j) { return 8 * ((j & 7) >> 1) + 4 * s + 2 * (j >> 3) + (j & 1); }
+
 // row-major int8 codes [N][K] -> [Np/64][Kp/32][4 row tiles][32 lanes][16 B], zero padded
 __global__ void pack_i8_tiles_kernel(const int8_t* src, int N, int K, uint8_t* dst, int Np, int Kp) {
   const size_t total = (size_t)(Np / 16) * (Kp / 32) * 32;
@@ -604,12 +635,11 @@ __global__ void pack_i8_tiles_kernel(const int8_t* src, int N, int K, uint8_t* d
     uint8_t out[16];
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
-      const int kb = kt * 32 + s * 16;
       const int rows[8] = {g, g, g + 8, g + 8, g, g, g + 8, g + 8};
-      const int cols[8] = {2 * t, 2 * t + 1, 2 * t, 2 * t + 1, 2 * t + 8, 2 * t + 9, 2 * t + 8, 2 * t + 9};
+      const int js[8] = {2 * t, 2 * t + 1, 2 * t, 2 * t + 1, 2 * t + 8, 2 * t + 9, 2 * t + 8, 2 * t + 9};
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int r = rt * 16 + rows[j], c = kb + cols[j];
+        const int r = rt * 16 + rows[j], c = kt * 32 + tile_col(s, js[j]);
         out[8 * s + j] = (r < N && c < K) ? (uint8_t)src[(size_t)r * K + c] : 0;
       }
     }
@@ -653,11 +683,10 @@ __global__ void pack_i4_tiles_kernel(const uint8_t* src, const __half* sc, int N
         const int rt = rb * tc::WARPS + w;
         for (int s = 0; s < 2; ++s) {
           uint32_t word = 0;
-          const int kb = kt * 32 + s * 16;
           const int rows[8] = {g, g + 8, g, g + 8, g, g + 8, g, g + 8};
-          const int cols[8] = {2 * t, 2 * t, 2 * t + 8, 2 * t + 8, 2 * t + 1, 2 * t + 1, 2 * t + 9, 2 * t + 9};
+          const int js[8] = {2 * t, 2 * t, 2 * t + 8, 2 * t + 8, 2 * t + 1, 2 * t + 1, 2 * t + 9, 2 * t + 9};
           for (int j = 0; j < 8; ++j) {                     // nibble slot j sits at bit 4j
-            const int r = rt * 16 + rows[j], c = kb + cols[j];
+            const int r = rt * 16 + rows[j], c = kt * 32 + tile_col(s, js[j]);
             uint32_t nib = 8;
             if (r < N) {
               const uint8_t b = src[(size_t)r * (K / 2) + c / 2];
@@ -669,9 +698,11 @@ __global__ void pack_i4_tiles_kernel(const uint8_t* src, const __half* sc, int N
         }
       }
     } else {
-      const int r0 = (piece - 64) * 8;
+      // scales of row tile w in the order (g, g + 8) for g = 0..7: one 32-bit load per lane
+      const int i0 = (piece - 64) * 8;
       for (int i = 0; i < 8; ++i) {
-        const int r = rb * 64 + r0 + i;
+        const int idx = i0 + i, w = idx / 16, gg = (idx % 16) / 2, hi = idx & 1;
+        const int r = rb * 64 + w * 16 + gg + 8 * hi;
         const __half v = r < N ? sc[(size_t)r * KT + kt] : __float2half(0.f);
         memcpy(out + 2 * i, &v, 2);
       }

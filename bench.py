@@ -380,7 +380,23 @@ def kernel_bench(name, reps, warmup):
     t = K.pack_i8_tiles(q)
     return [t] + [t.clone() for _ in range(copies - 1)], sc
 
-  if name in ("gemv_gu", "gemv_cfg1", "gemv_qkv", "gemv_o", "gemv_down"):
+  I4 = {"gemv_i4_gu": (2 * 29568, 8192, R.EPI_SWIGLU), "gemv_i4_qkv": (80 * 128, 8192, R.EPI_F32),
+        "gemv_i4_o": (8192, 8192, R.EPI_RESID), "gemv_i4_down": (8192, 29568, R.EPI_RESID)}
+  if name in I4:                                            # Qwen2-72B shapes, group-32 int4
+    N, Kd, epi = I4[name]
+    copies = max(2, -(-300_000_000 // (N * Kd // 2)))
+    W = (torch.randn(N, Kd, generator=g, device=dev) * 0.02).half()
+    pk, sc = K.quantize_g32_i4(W)
+    del W
+    t0 = K.pack_i4_tiles(pk, sc, N, Kd)
+    tiles = [t0] + [t0.clone() for _ in range(copies - 1)]
+    x = torch.randn(1, Kd, generator=g, device=dev).half()
+    y = K.gemv_tc_i4(x, tiles[0], N, Kd, epi=epi)
+    scr, _ = K.gemv_tc_scratch(N, Kd, 1, dev)
+    nbytes = N * Kd // 2 + 2 * (N * Kd // 32) + 2 * Kd + y.numel() * y.element_size() * (2 if epi == R.EPI_RESID else 1)
+    fn = lambda i: K.gemv_tc_i4(x, tiles[i % copies], N, Kd, epi=epi, y=y, scratch=scr)
+    what = f"gemv_tc int4_g32 {N}x{Kd} epi={epi}"
+  elif name in ("gemv_gu", "gemv_cfg1", "gemv_qkv", "gemv_o", "gemv_down"):
     N, Kd, epi = {"gemv_gu": (2 * F, D, R.EPI_SWIGLU), "gemv_cfg1": (4096, 4096, R.EPI_F16),
                   "gemv_qkv": ((H + 2 * KV) * dh, D, R.EPI_F32), "gemv_o": (D, H * dh, R.EPI_RESID),
                   "gemv_down": (D, F, R.EPI_RESID)}[name]
@@ -503,7 +519,8 @@ def main():
   ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
   ap.add_argument("--no-cpu-baseline", action="store_true")
   ap.add_argument("--kernel", default=None,
-                  help="time one kernel alone: gemv_gu | gemv_qkv | gemv_o | gemv_down | gemv_cfg1 | attn | lm_head")
+                  help="time one kernel alone: gemv_gu | gemv_qkv | gemv_o | gemv_down | gemv_cfg1 | attn | lm_head "
+                       "| gemv_i4_gu | gemv_i4_qkv | gemv_i4_o | gemv_i4_down")
   ap.add_argument("--reps", type=int, default=50)
   ap.add_argument("--profile-region", action="store_true",
                   help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
