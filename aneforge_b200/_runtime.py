@@ -62,6 +62,8 @@ SIGNATURES = [
   ("af_pack_i4_tiles", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
   ("af_gemv_tc_i4", c_int, [c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                             c_void_p, c_size_t, c_void_p]),
+  ("af_decode_mk_scratch", c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                   ctypes.POINTER(c_size_t), ctypes.POINTER(c_size_t)]),
   ("af_rmsnorm", c_int, [c_void_p, c_int, c_int, c_void_p, c_float, c_void_p, c_int, c_int, c_int, c_void_p]),
   ("af_attn_decode_scratch", c_int, [c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(c_size_t)]),
   ("af_attn_decode", c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,

@@ -195,6 +195,7 @@ class LlamaPrefill:
     self._pre = None
     self._head = None
     self._lmT = None
+    self.mk_profile = False                 # record per-CTA barrier timestamps in the megakernel
 
   # -- weights
   def _spec(self, i: int) -> LayerSpec:
@@ -336,12 +337,35 @@ class LlamaPrefill:
     for li in range(cfg.n_layers):
       self._declare_layer_weights(pb, li, d["layers"][li])
       pb.buf(f"L{li}.K", 2 * NB * KV * M * dh, "state"); pb.buf(f"L{li}.V", 2 * NB * KV * M * dh, "state")
-    pb.op("embed", tok="tok", table="embed", h="h", vocab=V, d=D, nb=NB)
-    for li in range(cfg.n_layers):
-      ls = self._spec(li)
-      DECODE_MIXERS[ls.mixer](pb, ctx, li, d["layers"][li], cfg, ls)
-      DECODE_MLPS[ls.mlp](pb, ctx, li, d["layers"][li], cfg, ls)
-    pb.op("rmsnorm", x="h", g="final_g", out="hid", nb=NB, d=D, floor=d["final_floor"])
+    mk = self._megakernel_plan(NB, M)
+    if mk is not None:
+      # one persistent launch for embed + every layer + final norm
+      if mk["nsplit"] > 1:
+        pb.buf("attn.part", kernels.attn_decode_scratch_bytes(NB, KV, mk["nsplit"], H // KV, dh), "scratch")
+        pb.buf("attn.cnt", 4 * NB * KV, "scratch")
+      pb.buf("mk.part", mk["part"], "scratch"); pb.buf("mk.cnt", mk["cnt"], "scratch"); pb.buf("mk.bar", 16, "scratch")
+      L = d["layers"]
+      kv = dict(wf=mk["wf"], layers=cfg.n_layers, nb=NB, d=D, h=H, kv=KV, dh=dh, ffn=F, m=M, nsplit=mk["nsplit"],
+                vocab=V, scale=ctx["scale"], kvc=ctx["kvc"], expand=int(ctx["expand"]), ffloor=d["final_floor"],
+                tok="tok", pos="pos", embed="embed", cos="rope.cos" if cfg.rope else None,
+                sin="rope.sin" if cfg.rope else None, res="h", qkv="qkv", att="att", act="act", final_g="final_g",
+                hid="hid", bar="mk.bar", part="mk.part", cnt="mk.cnt",
+                apart="attn.part" if mk["nsplit"] > 1 else None, acnt="attn.cnt" if mk["nsplit"] > 1 else None,
+                fa=",".join(repr(float(l["attn_floor"])) for l in L), fm=",".join(repr(float(l["mlp_floor"])) for l in L))
+      if all("qn" in l for l in L):
+        kv.update(fq=",".join(repr(float(l["qn_floor"])) for l in L), fk=",".join(repr(float(l["kn_floor"])) for l in L))
+      if self.mk_profile:
+        # per-CTA barrier timestamps (diagnostics): [grid][1 + 5 L][4] u64
+        pb.buf("mk.prof", 8 * 2 * 148 * (1 + 5 * cfg.n_layers) * 4, "out")
+        kv.update(prof="mk.prof")
+      pb.op("decode_mk", **kv)
+    else:
+      pb.op("embed", tok="tok", table="embed", h="h", vocab=V, d=D, nb=NB)
+      for li in range(cfg.n_layers):
+        ls = self._spec(li)
+        DECODE_MIXERS[ls.mixer](pb, ctx, li, d["layers"][li], cfg, ls)
+        DECODE_MLPS[ls.mlp](pb, ctx, li, d["layers"][li], cfg, ls)
+      pb.op("rmsnorm", x="h", g="final_g", out="hid", nb=NB, d=D, floor=d["final_floor"])
     pb.op("gemv", wf="f16", epi="argmax", x="hid", w="lm_head", y="logits", nb=NB, n=V, k=D, amv="am.val",
           ami="am.idx", amc="am.cnt", tok="tok_out", pos="pos", hist="hist", histld=M)
     ins = {"tok": (NB,), "pos": (NB,)}
@@ -357,8 +381,40 @@ class LlamaPrefill:
       prog.upload("rope.cos", cos_t); prog.upload("rope.sin", sin_t)
     for li in range(cfg.n_layers):
       self._bind_layer(prog, li, d["layers"][li])
-    self._dec = {"M": M, "NB": NB, "prog": prog, "plan": pb}
+    self._dec = {"M": M, "NB": NB, "prog": prog, "plan": pb, "megakernel": mk is not None}
     return self._dec
+
+  def _megakernel_plan(self, NB, M):
+    """Scratch sizes + split count when the whole decode step fits the persistent megakernel
+    (`decode_mk`: every projection tiled int8 or int4-g32, attention mixer + SwiGLU MLP in every
+    layer, NB <= 8), else None (the per-op kernels run). Opt-in with AF_DECODE_MK=1: on B200 the
+    per-op path with programmatic dependent launch is still the faster one at batch 1."""
+    import ctypes
+    import os
+    if os.environ.get("AF_DECODE_MK", "0") != "1":
+      return None
+    cfg, d = self.cfg, self._load()
+    L = d["layers"]
+    kinds = {l[k].wf for l in L for k in ("qkv", "o", "gu", "down") if k in l}
+    if len(kinds) != 1 or kinds.pop() not in ("i8t", "i4t") or NB > 8:
+      return None
+    if any(self._spec(i).mixer != "attention" or self._spec(i).mlp != "swiglu" for i in range(cfg.n_layers)):
+      return None
+    qk = ["qn" in l for l in L]
+    if any(qk) and not all(qk):
+      return None
+    wf = L[0]["qkv"].wf
+    KV, H, dh = cfg.n_kv_heads, cfg.n_heads, cfg.dh
+    F = L[0]["gu"].N // 2
+    if any(l["gu"].N // 2 != F for l in L):
+      return None
+    ns = int(os.environ.get("AF_MK_NSPLIT", "0")) or max(1, min(64, -(-M // 64), (2 * 148) // max(1, KV * NB)))
+    part, cnt = ctypes.c_size_t(), ctypes.c_size_t()
+    rc = R.load_library().af_decode_mk_scratch(R.W_I4G32 if wf == "i4t" else R.W_I8, NB, cfg.dim, H, KV, dh, F, ns,
+                                               ctypes.byref(part), ctypes.byref(cnt))
+    if rc != 0:
+      return None
+    return {"wf": wf, "nsplit": ns, "part": part.value, "cnt": cnt.value}
 
   def _prefiller(self, seq):
     """Build (once, cached by seq) the batched-prefill program: all layers over `seq` rows, each

@@ -147,6 +147,14 @@ int af_pack_i4_tiles(const uint8_t* packed, const uint16_t* scales, int n, int k
 int af_gemv_tc_i4(int epi, const uint16_t* x, int ldx, const void* tiles, const uint16_t* bias, void* y, int ldy,
                   int nb, int n, int k, void* scratch, size_t scratch_bytes, void* stream);
 
+/* Decode megakernel support query: 0 when one persistent launch can run a decode step of this shape
+ * (all projections tiled int8 (wf 0) or int4 group-32 (wf 2), nb <= 8, head dim 64/128, GQA group
+ * 1/2/4/8), with the byte sizes of its GEMV split-K partials and tickets; -1 otherwise. The step
+ * itself runs as the plan op `decode_mk` (no reference counterpart: the ANE program ran a whole
+ * decode chunk as one dispatch, llm.py:435-478; this is the B200 analogue). Needs a CUDA device. */
+int af_decode_mk_scratch(int wf, int nb, int d, int h, int kv, int dh, int ffn, int nsplit, size_t* part_bytes,
+                         size_t* cnt_bytes);
+
 /* lm_head GEMV + greedy argmax (lowest index on ties): replaces the host `hidden @ lm_head.T` and
  * np.argmax of LlamaPrefill._logits/_sample (aneforge/llm.py:349-355, :407-410). `logits` [nb][n]
  * may be NULL; `pos_advance` (may be NULL) is incremented per row. Scratch: see _scratch; it must be
