@@ -64,6 +64,10 @@ SIGNATURES = [
                             c_void_p, c_size_t, c_void_p]),
   ("af_decode_mk_scratch", c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                    ctypes.POINTER(c_size_t), ctypes.POINTER(c_size_t)]),
+  ("af_comm_unique_id", c_int, [c_void_p, c_size_t]),
+  ("af_comm_init", c_int, [c_void_p, c_int, c_int, c_int, ctypes.POINTER(c_void_p)]),
+  ("af_comm_destroy", None, [c_void_p]),
+  ("af_program_set_comm", c_int, [c_void_p, c_void_p]),
   ("af_rmsnorm", c_int, [c_void_p, c_int, c_int, c_void_p, c_float, c_void_p, c_int, c_int, c_int, c_void_p]),
   ("af_attn_decode_scratch", c_int, [c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(c_size_t)]),
   ("af_attn_decode", c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
@@ -276,6 +280,12 @@ class Program:
     s = c_void_p()
     check(self._L.af_program_stream(self._handle, ctypes.byref(s)), "af_program_stream")
     return s.value or 0
+
+  def set_comm(self, comm) -> None:
+    """Attach a tensor-parallel communicator (before the first execute; it must outlive the program)."""
+    rc = self._L.af_program_set_comm(self._handle, comm)
+    if rc != 0:
+      raise RuntimeError(f"set_comm failed rc={rc}: {last_error()}")
 
   def set_options(self, use_graph: bool = True, use_pdl: bool = True) -> None:
     check(self._L.af_program_set_options(self._handle, int(use_graph), int(use_pdl)), "set_options")

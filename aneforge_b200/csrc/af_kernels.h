@@ -1,5 +1,6 @@
 // Internal C++ interface between the program runtime and the sm_100a kernels.
 #pragma once
+#include <string>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -30,6 +31,8 @@ struct GemvArgs {
   int* pos_adv = nullptr;      // [NB] decode position, advanced by one when non-null
   int* hist = nullptr;         // [NB][hist_ld] token history: hist[b][pos[b]] = token (needs pos_adv)
   int hist_ld = 0;
+  float* val_out = nullptr;    // [NB] best logit (optional; a vocabulary shard's candidate)
+  int idx_base = 0;            // added to the row index written to tok_out (vocabulary shard offset)
 };
 
 cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t st, bool pdl);
@@ -106,6 +109,15 @@ struct AttnDecodeArgs {
 };
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st, bool pdl);
 size_t attn_decode_scratch_floats(int NB, int KV, int n_split, int G, int dh);
+
+// ---- tensor parallel (comm.cu): collectives on a program's stream, cross-rank argmax, residual add
+cudaError_t comm_all_reduce_f32(void* comm, const float* src, float* dst, size_t n, cudaStream_t st, std::string& why);
+cudaError_t comm_all_gather_i32(void* comm, const int* src, int* dst, size_t n, cudaStream_t st, std::string& why);
+int comm_size(void* comm);
+int comm_rank(void* comm);
+cudaError_t tp_argmax_launch(const int* gathered, int T, int NB, int* tok_out, int* pos_adv, int* hist, int hist_ld,
+                             cudaStream_t st);
+cudaError_t add_f32_launch(float* y, const float* x, size_t n, cudaStream_t st);
 
 // ---- decode megakernel: one persistent, cooperatively launched grid runs a whole decode step (embed,
 // every layer, final norm) with grid-wide barriers between the dependent phases.

@@ -190,7 +190,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
       if (threadIdx.x == 0) {
         for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
           if (sv[w] > best || (sv[w] == best && si[w] < bi)) { best = sv[w]; bi = si[w]; }
-        a.tok_out[b] = bi;
+        a.tok_out[b] = bi + a.idx_base;
+        if (a.val_out) a.val_out[b] = best;
         if (a.pos_adv) {
           const int p = __ldcg(a.pos_adv + b);
           if (a.hist && p >= 0 && p < a.hist_ld) a.hist[(size_t)b * a.hist_ld + p] = bi;
@@ -312,6 +313,7 @@ cudaError_t gemv_launch(const GemvArgs& a0, cudaStream_t st, bool pdl) {
       a.am_val = a0.am_val + (size_t)t * ctas_am * 4;
       a.am_idx = a0.am_idx + (size_t)t * ctas_am * 4;
       a.tok_out = a0.tok_out + b0;
+      if (a0.val_out) a.val_out = a0.val_out + b0;
       if (a0.pos_adv) a.pos_adv = a0.pos_adv + b0;
       if (a0.hist) a.hist = a0.hist + (size_t)b0 * a0.hist_ld;
     }

@@ -75,6 +75,7 @@ struct Program {
   bool use_pdl = true;
   cudaGraphExec_t exec = nullptr;
   int* d_err = nullptr;
+  void* comm = nullptr;        // tensor-parallel communicator (af_program_set_comm), not owned
 };
 
 // ------------------------------------------------------------------------------------ helpers
@@ -347,6 +348,8 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
       a.hist_ld = (int)c.i("histld", 0);
       a.hist = (int*)c.ptr("hist", 4 * (size_t)a.NB * a.hist_ld, true);
       if (a.hist && !a.pos_adv) c.err = "hist needs pos";
+      a.val_out = (float*)c.ptr("val", 4 * (size_t)a.NB, true);
+      a.idx_base = (int)c.i("ibase", 0);
       a.am_grid_cap = ctas;
     }
     if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
@@ -419,6 +422,36 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
       a.layers = it->second.dev_layers;
       e = decode_mk_launch(a, it->second.plan, st);
     }
+  } else if (op.kind == "allreduce" || op.kind == "allgather") {
+    // fp32 sum over the ranks / int32 gather of n elements per rank, on the program's communicator
+    const size_t n = (size_t)c.i("n");
+    const int T = comm_size(p.comm);
+    const bool red = op.kind == "allreduce";
+    void* src = c.ptr("src", 4 * n);
+    void* dst = c.ptr("dst", 4 * n * (red ? 1 : (size_t)c.i("ranks")));
+    if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+    if (!dry) {
+      if (!p.comm) { why = op.kind + " needs a communicator (af_program_set_comm)"; return cudaErrorInvalidValue; }
+      if (!red && c.i("ranks") != T) { why = "allgather: ranks does not match the communicator"; return cudaErrorInvalidValue; }
+      e = red ? comm_all_reduce_f32(p.comm, (const float*)src, (float*)dst, n, st, why)
+              : comm_all_gather_i32(p.comm, (const int*)src, (int*)dst, n, st, why);
+      if (e != cudaSuccess) return e;
+    }
+  } else if (op.kind == "tp_argmax") {
+    const int T = (int)c.i("ranks"), nb = (int)c.i("nb");
+    const int* g = (const int*)c.ptr("src", 4 * (size_t)T * 2 * nb);
+    int* tok = (int*)c.ptr("tok", 4 * (size_t)nb);
+    int* pos = (int*)c.ptr("pos", 4 * (size_t)nb, true);
+    const int hist_ld = (int)c.i("histld", 0);
+    int* hist = (int*)c.ptr("hist", 4 * (size_t)nb * hist_ld, true);
+    if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+    if (!dry) e = tp_argmax_launch(g, T, nb, tok, pos, hist, hist_ld, st);
+  } else if (op.kind == "add") {
+    const size_t n = (size_t)c.i("n");
+    float* y = (float*)c.ptr("y", 4 * n);
+    const float* x = (const float*)c.ptr("x", 4 * n);
+    if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+    if (!dry) e = add_f32_launch(y, x, n, st);
   } else if (op.kind == "cast") {
     const size_t n = (size_t)c.i("n");
     const int mode = (int)c.i("mode");
@@ -907,6 +940,14 @@ int af_program_sync(void* h) {
 int af_program_stream(void* h, void** stream) {
   if (!h || !stream) return -1;
   *stream = static_cast<Program*>(h)->stream;
+  return 0;
+}
+
+int af_program_set_comm(void* h, void* comm) {
+  if (!h) return -1;
+  Program& p = *static_cast<Program*>(h);
+  if (p.finalized) { set_error("set_comm after the first execute"); return -1; }
+  p.comm = comm;
   return 0;
 }
 

@@ -123,6 +123,19 @@ def _emit_linear(pb, ctx, name, lin: DevLinear, x, y, epi, nb=None):
   pb.op("gemv", **kv)
 
 
+def _emit_row_parallel(pb, ctx, name, lin: DevLinear, x):
+  """A projection whose output is added to the fp32 residual `h`. Under tensor parallelism each rank
+  holds a slice of its input columns: the partial goes to `tp.part`, is all-reduced over the ranks
+  and then added to the (replicated) residual."""
+  if ctx.get("tp"):
+    n = ctx["NB"] * ctx["D"]
+    _emit_linear(pb, ctx, name, lin, x, "tp.part", "f32")
+    pb.op("allreduce", src="tp.part", dst="tp.part", n=n)
+    pb.op("add", y="h", x="tp.part", n=n)
+  else:
+    _emit_linear(pb, ctx, name, lin, x, "h", "resid")
+
+
 def emit_attention_decode(pb, ctx, li, lw, cfg, ls):
   """`_attn_decode` (reference `llm.py:214-237`): norm -> fused QKV GEMV -> RoPE + cache write at
   pos + GQA split-K attention -> o_proj GEMV with the residual add fused."""
@@ -139,7 +152,7 @@ def emit_attention_decode(pb, ctx, li, lw, cfg, ls):
   if ctx["nsplit"] > 1:
     kv.update(part="attn.part", cnt="attn.cnt")
   pb.op("attn_decode", **kv)
-  _emit_linear(pb, ctx, f"{pre}.o", lw["o"], "att", "h", "resid")
+  _emit_row_parallel(pb, ctx, f"{pre}.o", lw["o"], "att")
 
 
 def emit_attention_prefill(pb, ctx, li, lw, cfg, ls):
@@ -155,7 +168,7 @@ def emit_attention_prefill(pb, ctx, li, lw, cfg, ls):
   if ls.qk_norm:
     kv.update(qn=f"{pre}.qn", kn=f"{pre}.kn", qnf=lw["qn_floor"], knf=lw["kn_floor"])
   pb.op("attn_prefill", **kv)
-  _emit_linear(pb, ctx, f"{pre}.o", lw["o"], "att", "h", "resid")
+  _emit_row_parallel(pb, ctx, f"{pre}.o", lw["o"], "att")
 
 
 def emit_swiglu(pb, ctx, li, lw, cfg, ls):
@@ -164,7 +177,7 @@ def emit_swiglu(pb, ctx, li, lw, cfg, ls):
   pre = f"L{li}"
   pb.op("rmsnorm", x="h", g=f"{pre}.mlp_g", out="xn", nb=ctx["NB"], d=cfg.dim, floor=lw["mlp_floor"])
   _emit_linear(pb, ctx, f"{pre}.gu", lw["gu"], "xn", "act", "swiglu")
-  _emit_linear(pb, ctx, f"{pre}.down", lw["down"], "act", "h", "resid")
+  _emit_row_parallel(pb, ctx, f"{pre}.down", lw["down"], "act")
 
 
 PREFILL_MIXERS = {"attention": emit_attention_prefill}
@@ -182,7 +195,14 @@ class LlamaPrefill:
   (`aneforge/llm.py:636-654`) of numpy arrays or torch tensors (host or device)."""
 
   def __init__(self, cfg: LlamaConfig, weights: dict, compress: str | None = None, ane_lm_head: bool = True,
-               device: int = 0, compress_atol: float = 0.05, block_size: int = 32):
+               device: int = 0, compress_atol: float = 0.05, block_size: int = 32, tp=None):
+    self.tp = tp if tp is not None and tp.world > 1 else None
+    self.full_cfg, self._w_full = cfg, weights
+    if self.tp is not None:
+      # this rank's shard (aneforge_b200.tp): local heads / FFN rows / vocabulary rows
+      from .tp import plan_shard, shard_model
+      self.shard = plan_shard(cfg, self.tp.rank, self.tp.world)
+      cfg, weights = shard_model(cfg, weights, self.shard)
     self.cfg = cfg; self.w = weights; self.compress = compress
     self.compress_atol, self.block_size = compress_atol, block_size
     self.device = int(device)
@@ -298,7 +318,8 @@ class LlamaPrefill:
     # SM) and at most 64 splits (the last CTA of each head merges them)
     cap = max(1, (2 * 148) // max(1, cfg.n_kv_heads * NB))
     nsplit = max(1, min(64, cap, -(-M // 32)))
-    return {"NB": NB, "M": M, "nsplit": nsplit, "scale": d["scale"], "kvc": d["kvc"], "expand": G > 1 and d["kvc"] != 1.0}
+    return {"NB": NB, "M": M, "nsplit": nsplit, "scale": d["scale"], "kvc": d["kvc"], "expand": G > 1 and d["kvc"] != 1.0,
+            "tp": self.tp is not None, "D": cfg.dim}
 
   # -- programs
   def _decoder(self, M, NB=1):
@@ -322,16 +343,21 @@ class LlamaPrefill:
     pb.buf("att", 2 * NB * H * dh, "tmp")
     F = max((l["gu"].N // 2 for l in d["layers"] if "gu" in l), default=1)
     pb.buf("act", 2 * NB * F, "tmp")
-    pb.buf("embed", 2 * V * D, "weight"); pb.buf("lm_head", 2 * V * D, "weight"); pb.buf("final_g", 2 * D, "weight")
+    VL = int(d["lm_head"].shape[0])                       # local vocabulary rows (all of them without TP)
+    pb.buf("embed", 2 * V * D, "weight"); pb.buf("lm_head", 2 * VL * D, "weight"); pb.buf("final_g", 2 * D, "weight")
     if cfg.rope:
       pb.buf("rope.cos", 2 * M * dh, "weight"); pb.buf("rope.sin", 2 * M * dh, "weight")
+    if self.tp is not None:
+      pb.buf("tp.part", 4 * NB * D, "tmp")
+      pb.buf("tp.cand", 8 * NB, "tmp"); pb.buf("tp.gath", 8 * NB * self.tp.world, "tmp")
+      pb.buf("logits", 4 * NB * VL, "out")
     from . import kernels
     if ctx["nsplit"] > 1:
       pb.buf("attn.part", kernels.attn_decode_scratch_bytes(NB, KV, ctx["nsplit"], H // KV, dh), "scratch")
       pb.buf("attn.cnt", 4 * NB * KV, "scratch")
     import ctypes
     nb = ctypes.c_size_t()
-    R.check(R.load_library().af_lm_head_argmax_scratch(R.W_F16, V, D, NB, ctypes.byref(nb)), "scratch")
+    R.check(R.load_library().af_lm_head_argmax_scratch(R.W_F16, VL, D, NB, ctypes.byref(nb)), "scratch")
     pb.buf("am.val", nb.value, "scratch"); pb.buf("am.idx", nb.value, "scratch")
     pb.buf("am.cnt", 4 * ((NB + 3) // 4), "scratch")
     for li in range(cfg.n_layers):
@@ -366,14 +392,23 @@ class LlamaPrefill:
         DECODE_MIXERS[ls.mixer](pb, ctx, li, d["layers"][li], cfg, ls)
         DECODE_MLPS[ls.mlp](pb, ctx, li, d["layers"][li], cfg, ls)
       pb.op("rmsnorm", x="h", g="final_g", out="hid", nb=NB, d=D, floor=d["final_floor"])
-    pb.op("gemv", wf="f16", epi="argmax", x="hid", w="lm_head", y="logits", nb=NB, n=V, k=D, amv="am.val",
-          ami="am.idx", amc="am.cnt", tok="tok_out", pos="pos", hist="hist", histld=M)
+    if self.tp is None:
+      pb.op("gemv", wf="f16", epi="argmax", x="hid", w="lm_head", y="logits", nb=NB, n=V, k=D, amv="am.val",
+            ami="am.idx", amc="am.cnt", tok="tok_out", pos="pos", hist="hist", histld=M)
+    else:
+      # vocabulary shard: local (best logit, global index) -> all-gather -> cross-rank argmax
+      pb.op("gemv", wf="f16", epi="argmax", x="hid", w="lm_head", y="logits", nb=NB, n=VL, k=D, amv="am.val",
+            ami="am.idx", amc="am.cnt", tok=at("tp.cand", 4 * NB), val="tp.cand", ibase=self.shard.vocab[0])
+      pb.op("allgather", src="tp.cand", dst="tp.gath", n=2 * NB, ranks=self.tp.world)
+      pb.op("tp_argmax", src="tp.gath", ranks=self.tp.world, nb=NB, tok="tok_out", pos="pos", hist="hist", histld=M)
     ins = {"tok": (NB,), "pos": (NB,)}
     for li in range(cfg.n_layers):
       ins[f"L{li}.K"] = (NB, KV, M, dh); ins[f"L{li}.V"] = (NB, KV, M, dh)
-    outs = {"tok_out": (NB,), "hist": (NB, M), "hid": (NB, D), "logits": (NB, V)}
+    outs = {"tok_out": (NB,), "hist": (NB, M), "hid": (NB, D), "logits": (NB, VL)}
     dt = {"tok": "int32", "pos": "int32", "tok_out": "int32", "hist": "int32", "logits": "fp32"}
     prog = R.Program.from_text(pb.text(), ins, outs, self.device, dt)
+    if self.tp is not None:
+      prog.set_comm(self.tp.handle)
     prog.share_buffer(0, "tok_out", 0, "tok")              # device-resident token feedback
     prog.bind("embed", d["embed"]); prog.bind("lm_head", d["lm_head"]); prog.bind("final_g", d["final_g"])
     if cfg.rope:
@@ -391,7 +426,7 @@ class LlamaPrefill:
     per-op path with programmatic dependent launch is still the faster one at batch 1."""
     import ctypes
     import os
-    if os.environ.get("AF_DECODE_MK", "0") != "1":
+    if os.environ.get("AF_DECODE_MK", "0") != "1" or self.tp is not None:
       return None
     cfg, d = self.cfg, self._load()
     L = d["layers"]
@@ -435,6 +470,8 @@ class LlamaPrefill:
     pb.buf("att", 2 * seq * H * dh, "tmp"); pb.buf("qbuf", 2 * seq * H * dh, "tmp")
     F = max((l["gu"].N // 2 for l in d["layers"] if "gu" in l), default=1)
     pb.buf("act", 2 * seq * F, "tmp")
+    if self.tp is not None:
+      pb.buf("tp.part", 4 * seq * D, "tmp")
     pb.buf("embed", 2 * V * D, "weight"); pb.buf("final_g", 2 * D, "weight")
     if cfg.rope:
       pb.buf("rope.cos", 2 * seq * dh, "weight"); pb.buf("rope.sin", 2 * seq * dh, "weight")
@@ -453,6 +490,8 @@ class LlamaPrefill:
     for li in range(cfg.n_layers):
       outs[f"L{li}.K"] = (KV, seq, dh); outs[f"L{li}.V"] = (KV, seq, dh)
     prog = R.Program.from_text(pb.text(), {"ids": (seq,)}, outs, self.device, {"ids": "int32"})
+    if self.tp is not None:
+      prog.set_comm(self.tp.handle)
     prog.bind("embed", d["embed"]); prog.bind("final_g", d["final_g"])
     if cfg.rope:
       cos_t, sin_t = rope_tables(seq, dh, cfg.rope_base, cfg.rotary_dim, cfg.rope_interleaved, cfg.rope_scaling)
@@ -507,13 +546,16 @@ class LlamaPrefill:
 
   def _host_logits(self, hidden_row):
     if self._lmT is None:
+      lm = self._w_full["lm_head"]                       # the whole head, also under tensor parallelism
       self._lmT = np.ascontiguousarray(np.asarray(
-        self.w["lm_head"].detach().float().cpu().numpy() if hasattr(self.w["lm_head"], "detach")
-        else self.w["lm_head"]).T, F32)
+        lm.detach().float().cpu().numpy() if hasattr(lm, "detach") else lm).T, F32)
     return np.asarray(hidden_row, F32) @ self._lmT
 
   def _logits(self, hidden_row, ane=None):
-    """Device lm_head (fp16 weights, fp32 accumulation) for one fp16 hidden row [D]."""
+    """Device lm_head (fp16 weights, fp32 accumulation) for one fp16 hidden row [D]; under tensor
+    parallelism each rank holds only a vocabulary shard, so the full-row logits come from the host."""
+    if self.tp is not None:
+      return self._host_logits(np.asarray(hidden_row, F16).astype(F32))
     hp = self._head_program()["prog"]
     hp.set_input("x", np.asarray(hidden_row).astype(F16)[None])
     hp.execute()
@@ -628,6 +670,8 @@ class LlamaPrefill:
     if n_steps <= 0:
       return out
     exact_head = greedy and self._head_exact
+    if self.tp is not None and not (exact_head and on_token is None and on_stage is None):
+      raise NotImplementedError("tensor-parallel generate runs greedy decode with the on-device head only")
     if exact_head and on_token is None and on_stage is None:
       # greedy with an exact head: every step's token stays on the device; run the steps back to
       # back and read the token history once (EOS cuts the list where the reference would stop).

@@ -212,23 +212,29 @@ def run_b200(args):
   import torch.distributed as dist
   from aneforge_b200 import llm as L, _runtime as R, kernels
   ws, rank, local = _dist()
-  if ws > 1:
-    dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=600))
   torch.cuda.set_device(local)
   dev = torch.device("cuda", local)
+  if ws > 1:
+    dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=600))
+  tp = None
+  if args.tp and ws > 1:
+    # one model sharded over the ranks (tensor parallel, strong scaling): same weights and prompt on
+    # every rank; otherwise every rank runs its own replica on its own sequences (weak scaling)
+    from aneforge_b200.tp import TensorParallel
+    tp = TensorParallel.from_torch_distributed(local)
   cfg = L.LlamaConfig(**CFG, layers=[L.LayerSpec() for _ in range(CFG["n_layers"])])
   NB = args.batch
   t_load = time.perf_counter()
   spec = MODELS[MODEL]
-  w = make_weights(cfg, dev, seed=1234 + rank, qkv_bias=spec["qkv_bias"])
-  m = L.LlamaPrefill(cfg, w, compress=spec["compress"], device=local)
+  w = make_weights(cfg, dev, seed=1234 + (0 if tp else rank), qkv_bias=spec["qkv_bias"])
+  m = L.LlamaPrefill(cfg, w, compress=spec["compress"], device=local, tp=tp)
   m._load()
   del w
   torch.cuda.empty_cache()
   load_s = time.perf_counter() - t_load
   e2e_steps = max(8, args.steps // 2)
   M = PROMPT + args.warmup + args.steps + e2e_steps + 8      # every step (timed, warm-up, e2e) fits the cache
-  rng = np.random.default_rng(99 + rank)
+  rng = np.random.default_rng(99 + (0 if tp else rank))
   prompts = [list(rng.integers(0, cfg.vocab, PROMPT)) for _ in range(NB)]
   dec = m._decoder(M, NB)
   prog = dec["prog"]
@@ -270,7 +276,8 @@ def run_b200(args):
     ms = float(t.item())
     dist.barrier()
   ms_step = ms / args.steps
-  tok_s = NB * args.steps * ws / (ms / 1e3)
+  units = 1 if tp else ws                                  # sequences advanced per step, whole job
+  tok_s = NB * args.steps * units / (ms / 1e3)
   launches_per_step = sum(1 for _ in dec["plan"].ops)
 
   # ---- end-to-end through the public program API with host buffers: per step one H2D of the
@@ -291,7 +298,7 @@ def run_b200(args):
       host_tok.copy_(host_out)
   e2e_s = time.perf_counter() - t0
   prog.sync()                                              # raises if any step recorded a device error
-  e2e_tok_s = NB * e2e_steps * ws / e2e_s
+  e2e_tok_s = NB * e2e_steps * units / e2e_s
 
   # ---- dominant kernel: the fused gate|up int8 GEMV, timed alone on the program stream over the
   # 32 layers' own weights (3.7 GB > L2, so every launch streams from HBM)
@@ -327,11 +334,12 @@ def run_b200(args):
     achieved = gu_bytes / (k_us * 1e-6) / 1e9
     result = {
       "metric": METRIC, "value": round(tok_s, 2), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
-      "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+      "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+      "scaling": "strong" if tp else "weak",
       "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic",
       "config": {"workload": spec["workload"], "model": MODEL + "-shaped",
                  "global_batch": NB * ws, "batch_per_gpu": NB, "seq_len": PROMPT, "decode_pos": f"{PROMPT}..{M}",
-                 "parallelism": f"replicas{ws}" if ws > 1 else "single",
+                 "parallelism": f"tp{ws}" if tp else (f"replicas{ws}" if ws > 1 else "single"),
                  "l2": f"weights {step_bytes / 1e9:.1f} GB per step >> 126 MB L2 (no flush needed)"},
       "e2e": {"value": round(e2e_tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * NB,
               "d2h_bytes_per_step": 4 * NB,
@@ -343,7 +351,8 @@ def run_b200(args):
                    "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
                    "launch_us": round(k_us, 2), "algorithmic_bytes": gu_bytes},
       "step_roofline": {"algorithmic_bytes": int(step_bytes), "achieved_gbs": round(step_bytes / (ms_step * 1e-3) / 1e9, 1),
-                        "frac": round(step_bytes / (ms_step * 1e-3) / 1e9 / peak, 4)},
+                        "frac": round(step_bytes / (ms_step * 1e-3) / 1e9 / peak / (ws if tp else 1), 4),
+                        "per": "GPU (the model's bytes are split over the tensor-parallel ranks)" if tp else "GPU"},
       "gpu_launches": launches_per_step * args.steps,
       "clocks": clk.summary(),
       "load_s": round(load_s, 2), "prefill_s": round(prefill_s, 3),
@@ -354,6 +363,8 @@ def run_b200(args):
   import gc
   gc.collect()
   m.release()
+  if tp is not None:
+    tp.close()
   if ws > 1:
     dist.barrier()
     dist.destroy_process_group()
@@ -516,6 +527,8 @@ def main():
   ap.add_argument("--warmup", type=int, default=10)
   ap.add_argument("--batch", type=int, default=1)
   ap.add_argument("--model", default="llama3-8b", choices=sorted(MODELS))
+  ap.add_argument("--tp", action="store_true",
+                  help="with --gpus N > 1: shard one model over the N ranks (tensor parallel) instead of N replicas")
   ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
   ap.add_argument("--no-cpu-baseline", action="store_true")
   ap.add_argument("--kernel", default=None,

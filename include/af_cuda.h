@@ -99,6 +99,15 @@ int af_program_stream(void* prog, void** stream);
 /* Before the first execute: disable CUDA-graph replay / programmatic dependent launch. */
 int af_program_set_options(void* prog, int use_graph, int use_pdl);
 
+/* Tensor parallel (no reference counterpart: the ANE runtime is single-device). One communicator per
+ * rank over NCCL (loaded at run time): rank 0 makes the unique id, every rank passes it to
+ * af_comm_init with its GPU. A program whose plan holds collective ops (allreduce / allgather) gets
+ * the communicator before its first execute; the communicator must outlive the program. */
+int af_comm_unique_id(void* out, size_t bytes);
+int af_comm_init(const void* id, int nranks, int rank, int device, void** comm);
+void af_comm_destroy(void* comm);
+int af_program_set_comm(void* prog, void* comm);
+
 /* Replaces ane_e5rt_program_share_buffer (ane_e5rt_dispatch.mm:687-714): rebind input `dst_in` to
  * output `src_out`'s buffer (resident state). Op indices must be 0. Before the first execute only;
  * the destination's own buffer is freed exactly once. */

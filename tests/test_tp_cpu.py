@@ -1,0 +1,132 @@
+"""Tensor-parallel host logic on the CPU: the shard plan, the sharded weights' algebra (row-parallel
+partials sum to the unsharded product, column-parallel pieces concatenate to it), the cross-rank
+argmax rule, and the communicator-id exchange over a 2-rank gloo group."""
+import os
+
+import numpy as np
+import pytest
+
+from aneforge_b200 import tp as TP
+from aneforge_b200.llm import LlamaConfig
+
+F32 = np.float32
+
+
+def test_split_even_covers_and_aligns():
+  assert TP.split_even(10, 3) == [(0, 4), (4, 7), (7, 10)]
+  parts = TP.split_even(29568, 8, 32)                 # Qwen2-72B FFN: 924 groups of 32 over 8 ranks
+  sizes = [(b - a) // 32 for a, b in parts]
+  assert sizes == [116, 116, 116, 116, 115, 115, 115, 115]
+  assert parts[0][0] == 0 and parts[-1][1] == 29568
+  assert all(parts[i][1] == parts[i + 1][0] for i in range(7))
+  with pytest.raises(ValueError):
+    TP.split_even(100, 3, 32)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_plan_shard_partitions_every_axis(world):
+  cfg = LlamaConfig(dim=4096, n_layers=1, n_heads=32, n_kv_heads=8, ffn_dim=14336, vocab=128256)
+  shards = [TP.plan_shard(cfg, r, world) for r in range(world)]
+  for axis, total in (("q_heads", 32), ("kv_heads", 8), ("ffn", 14336), ("vocab", 128256)):
+    spans = [getattr(s, axis) for s in shards]
+    assert spans[0][0] == 0 and spans[-1][1] == total
+    assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
+  assert all((s.ffn[1] - s.ffn[0]) % 32 == 0 for s in shards)
+  with pytest.raises(ValueError):
+    TP.plan_shard(LlamaConfig(dim=64, n_layers=1, n_heads=4, n_kv_heads=2, ffn_dim=64, vocab=10), 0, 4)
+
+
+def _layer(rng, D, H, KV, dh, F, bias=True):
+  R = lambda *s: rng.standard_normal(s).astype(F32)
+  lw = {"wq": R(H * dh, D), "wk": R(KV * dh, D), "wv": R(KV * dh, D), "wo": R(D, H * dh),
+        "wgate": R(F, D), "wup": R(F, D), "wdown": R(D, F), "attn_norm": R(D), "mlp_norm": R(D)}
+  if bias:
+    lw.update(q_bias=R(H * dh), k_bias=R(KV * dh), v_bias=R(KV * dh))
+  return lw
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_layer_algebra(world):
+  rng = np.random.default_rng(world)
+  D, H, KV, dh, F = 64, 8, 4, 8, 96
+  cfg = LlamaConfig(dim=D, n_layers=1, n_heads=H, n_kv_heads=KV, ffn_dim=F, vocab=50, head_dim=dh)
+  lw = _layer(rng, D, H, KV, dh, F)
+  x = rng.standard_normal(D).astype(F32)
+  att = rng.standard_normal(H * dh).astype(F32)
+  act_full = (x @ lw["wgate"].T) * (x @ lw["wup"].T)
+  q, k, v = [], [], []
+  o_sum = np.zeros(D, F32)
+  d_sum = np.zeros(D, F32)
+  for r in range(world):
+    s = TP.plan_shard(cfg, r, world)
+    sl = TP.shard_layer(lw, cfg, s)
+    q.append(x @ sl["wq"].T + sl["q_bias"]); k.append(x @ sl["wk"].T + sl["k_bias"]); v.append(x @ sl["wv"].T + sl["v_bias"])
+    a0, a1 = s.q_heads[0] * dh, s.q_heads[1] * dh
+    o_sum += att[a0:a1] @ sl["wo"].T
+    d_sum += ((x @ sl["wgate"].T) * (x @ sl["wup"].T)) @ sl["wdown"].T
+    assert np.array_equal(sl["attn_norm"], lw["attn_norm"])
+  np.testing.assert_allclose(np.concatenate(q), x @ lw["wq"].T + lw["q_bias"], rtol=1e-5, atol=1e-4)
+  np.testing.assert_allclose(np.concatenate(k), x @ lw["wk"].T + lw["k_bias"], rtol=1e-5, atol=1e-4)
+  np.testing.assert_allclose(np.concatenate(v), x @ lw["wv"].T + lw["v_bias"], rtol=1e-5, atol=1e-4)
+  np.testing.assert_allclose(o_sum, att @ lw["wo"].T, rtol=1e-4, atol=1e-3)
+  np.testing.assert_allclose(d_sum, act_full @ lw["wdown"].T, rtol=1e-4, atol=1e-2)
+
+
+def test_shard_model_local_config_and_head():
+  cfg = LlamaConfig(dim=64, n_layers=2, n_heads=8, n_kv_heads=4, ffn_dim=96, vocab=50, head_dim=8)
+  rng = np.random.default_rng(0)
+  w = {"embed": rng.standard_normal((50, 64)), "lm_head": rng.standard_normal((50, 64)),
+       "final_norm": np.ones(64), "layers": [_layer(rng, 64, 8, 4, 8, 96) for _ in range(2)]}
+  s = TP.plan_shard(cfg, 1, 2)
+  local, lw = TP.shard_model(cfg, w, s)
+  assert (local.n_heads, local.n_kv_heads, local.ffn_dim, local.dim, local.vocab) == (4, 2, 32, 64, 50)
+  assert local.dh == 8
+  assert np.array_equal(lw["lm_head"], w["lm_head"][25:50]) and lw["embed"] is w["embed"]
+  assert lw["layers"][1]["wq"].shape == (32, 64) and lw["layers"][1]["wdown"].shape == (64, 32)
+
+
+def test_cross_rank_argmax_rule():
+  """The combine kernel's rule: best value over the ranks' candidates, ties to the lowest global
+  index - identical to the single-device argmax of the concatenated logits."""
+  rng = np.random.default_rng(3)
+  for _ in range(200):
+    V, T = 37, 4
+    logits = rng.integers(-3, 3, V).astype(F32)           # many exact ties
+    spans = TP.split_even(V, T)
+    cands = [(float(logits[a:b].max()), a + int(np.argmax(logits[a:b]))) for a, b in spans]
+    best, bi = -np.inf, None
+    for v, i in cands:
+      if bi is None or v > best or (v == best and i < bi):
+        best, bi = v, i
+    assert bi == int(np.argmax(logits))
+
+
+def _gloo_rank(rank, world, port, q):
+  import torch.distributed as dist
+  os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+  dist.init_process_group("gloo", rank=rank, world_size=world)
+  made = {}
+  TP.TensorParallel.unique_id = staticmethod(lambda: bytes(range(128)))
+  TP.TensorParallel.create = classmethod(lambda cls, r, w, d, uid: made.setdefault("x", (r, w, d, uid)))
+  TP.TensorParallel.from_torch_distributed(device=rank)
+  dist.barrier()
+  dist.destroy_process_group()
+  q.put(made["x"])
+
+
+def test_communicator_id_exchange_over_gloo():
+  import multiprocessing as mp
+  import socket
+  with socket.socket() as s:
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+  ctx = mp.get_context("spawn")
+  q = ctx.Queue()
+  procs = [ctx.Process(target=_gloo_rank, args=(r, 2, port, q)) for r in range(2)]
+  for p in procs:
+    p.start()
+  got = sorted(q.get(timeout=120) for _ in procs)
+  for p in procs:
+    p.join(timeout=60)
+    assert p.exitcode == 0
+  assert [g[0] for g in got] == [0, 1] and all(g[1] == 2 and g[3] == bytes(range(128)) for g in got)
