@@ -7,7 +7,7 @@
 // Layout of a CTA (2 per SM when shared memory allows): one producer warp + 8 consumer warps.
 //  * The producer (one thread) walks the WHOLE step's weight stream — layer by layer, qkv, o,
 //    gate|up, down, each split stream-K over the grid exactly as the consumers will walk it — and
-//    bulk-copies (cp.async.bulk, no multicast) 8-9 KB stages into an mbarrier ring. Weights do not
+//    bulk-copies (cp.async.bulk into its own shared memory) 8-9 KB stages into an mbarrier ring. Weights do not
 //    depend on activations, so it runs ahead across phase boundaries and keeps HBM busy while the
 //    consumers wait at a grid barrier, compute attention or stage the next input.
 //  * The consumers run the phases in order. GEMV phase: stage the CTA's slice of x in shared
