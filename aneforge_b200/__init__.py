@@ -5,6 +5,7 @@ surface; the work runs as hand-written CUDA kernels sequenced by the C-ABI progr
 `_lib/libaf_cuda.so`. There is no CPU fallback: without a CUDA device the runtime raises.
 """
 from . import llm  # noqa: F401
+from . import moe  # noqa: F401  (registers the "moe" MLP with the runner)
 from .llm import LlamaConfig, LayerSpec, LlamaPrefill, from_pretrained, rope_tables  # noqa: F401
 
 load_llm = from_pretrained

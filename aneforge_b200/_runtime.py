@@ -68,6 +68,10 @@ SIGNATURES = [
   ("af_comm_init", c_int, [c_void_p, c_int, c_int, c_int, ctypes.POINTER(c_void_p)]),
   ("af_comm_destroy", None, [c_void_p]),
   ("af_program_set_comm", c_int, [c_void_p, c_void_p]),
+  ("af_moe_gate", c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+  ("af_gemv_tc_expert", c_int, [c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                c_void_p, c_int, c_int, ctypes.c_longlong, c_int, c_void_p, c_int, c_void_p, c_size_t,
+                                c_void_p]),
   ("af_rmsnorm", c_int, [c_void_p, c_int, c_int, c_void_p, c_float, c_void_p, c_int, c_int, c_int, c_void_p]),
   ("af_attn_decode_scratch", c_int, [c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(c_size_t)]),
   ("af_attn_decode", c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,

@@ -52,6 +52,15 @@ struct GemvTcArgs {
   void* scratch = nullptr;     // split-K partials + counters (gemv_tc_scratch_bytes); zero before first use
   size_t scratch_bytes = 0;
   int* err = nullptr;          // device error word (AF_DEV_WAIT_TIMEOUT if a pipeline wait gives up)
+  // mixture of experts: the weights are E experts' tiles back to back; the expert is `sel[slot]`
+  // (device memory, written by the gate kernel) or `fixed_e`; the RESID epilogue scales each batch
+  // row's contribution by rw[b * rw_e + expert] when rw is given
+  const int* sel = nullptr;
+  int slot = 0, fixed_e = 0;
+  long long w_stride = 0;      // bytes between experts' tiles
+  int s_stride = 0;            // halves between experts' per-row scales
+  const float* rw = nullptr;
+  int rw_e = 0;
   // set by the launcher
   int Np = 0, Kp = 0, S = 1, maxc = 1;
   float* part = nullptr;
@@ -109,6 +118,11 @@ struct AttnDecodeArgs {
 };
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st, bool pdl);
 size_t attn_decode_scratch_floats(int NB, int KV, int n_split, int G, int dh);
+
+// MoE router tail (moe.cu): softmax over E, top-k by repeated row-max peel (lowest index on ties),
+// optional renormalisation -> gw [NB][E] (zeros off the top k) and sel [NB][k] (peel order)
+cudaError_t moe_gate_launch(const float* logits, int ld, int NB, int E, int k, int renorm, float* gw, int* sel,
+                            cudaStream_t st, bool pdl);
 
 // ---- tensor parallel (comm.cu): collectives on a program's stream, cross-rank argmax, residual add
 cudaError_t comm_all_reduce_f32(void* comm, const float* src, float* dst, size_t n, cudaStream_t st, std::string& why);

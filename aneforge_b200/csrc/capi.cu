@@ -147,6 +147,20 @@ int af_decode_mk_scratch(int wf, int nb, int d, int h, int kv, int dh, int ffn, 
   return 0;
 }
 
+int af_gemv_tc_expert(int wf, int epi, const uint16_t* x, int ldx, const void* tiles, const uint16_t* scales,
+                      void* y, int ldy, int nb, int n, int k, const int* sel, int slot, int fixed_e, long long w_stride,
+                      int s_stride, const float* rw, int rw_e, void* scratch, size_t scratch_bytes, void* stream) {
+  af::GemvTcArgs a;
+  a.wf = wf; a.epi = epi;
+  a.x = reinterpret_cast<const __half*>(x); a.ldx = ldx;
+  a.w = tiles; a.scale = reinterpret_cast<const __half*>(scales);
+  a.y = y; a.ldy = ldy; a.NB = nb; a.N = n; a.K = k;
+  a.sel = sel; a.slot = slot; a.fixed_e = fixed_e; a.w_stride = w_stride; a.s_stride = s_stride;
+  a.rw = rw; a.rw_e = rw_e;
+  a.scratch = scratch; a.scratch_bytes = scratch_bytes;
+  return rc_of(af::gemv_tc_launch(a, static_cast<cudaStream_t>(stream), false), "af_gemv_tc_expert");
+}
+
 int af_rmsnorm(const void* x, int x_f16, int ldx, const uint16_t* g, float floor, uint16_t* out, int ldo, int nb,
                int d, void* stream) {
   return rc_of(af::rmsnorm_launch(x, x_f16, ldx, reinterpret_cast<const __half*>(g), floor,

@@ -69,8 +69,10 @@ AF_DEV void epilogue(const GemvTcArgs& a, float (&acc)[NT][4], int rt, int g, in
           const size_t o = (size_t)b * a.ldy + row;
           if (EPI == EPI_F32) reinterpret_cast<float*>(a.y)[o] = v;
           else if (EPI == EPI_F16) reinterpret_cast<__half*>(a.y)[o] = f2h(v);
-          else if (EPI == EPI_RESID)
+          else if (EPI == EPI_RESID) {
+            if (a.rw) v *= __ldcg(a.rw + (size_t)b * a.rw_e + a.fixed_e);
             reinterpret_cast<float*>(a.y)[o] = __ldcg(reinterpret_cast<const float*>(a.y) + o) + v;
+          }
         }
       }
     }
@@ -79,6 +81,18 @@ AF_DEV void epilogue(const GemvTcArgs& a, float (&acc)[NT][4], int rt, int g, in
 
 template <int NT, int EPI, bool I4>
 __global__ void __launch_bounds__((tc::CWARPS + 1) * 32) gemv_tc_kernel(GemvTcArgs a) {
+  // expert selection (MoE): the expert index may be produced by the preceding kernel, so with `sel`
+  // the weights are addressed only after the programmatic-launch wait
+  int expert = a.fixed_e;
+  if (a.sel) {
+    pdl_wait();
+    expert = __ldcg(a.sel + a.slot);
+  }
+  if (a.sel || a.fixed_e) {
+    a.w = static_cast<const char*>(a.w) + (size_t)expert * a.w_stride;
+    if (a.scale) a.scale += (size_t)expert * a.s_stride;
+  }
+  a.fixed_e = expert;
   using F = tc::Fmt<I4>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   unsigned char* ring = smem_raw;                                          // [STAGES][F::stage]

@@ -306,8 +306,22 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     const int out_cols = a.epi == EPI_SWIGLU ? a.N / 2 : a.N;
     a.ldy = c.i("ldy", out_cols);
     a.x = (const __half*)c.ptr("x", 2 * ((size_t)(a.NB - 1) * a.ldx + a.K));
-    a.w = c.ptr("w", i4 ? pack_i4_tiles_bytes(a.N, a.K) : pack_i8_tiles_bytes(a.N, a.K));
-    if (!i4) a.scale = (const __half*)c.ptr("s", 2 * (size_t)a.N);
+    // experts (MoE): E experts' tiles back to back, expert from `sel[slot]` or `fixe`
+    const int nexp = (int)c.i("experts", 1);
+    const size_t tile_bytes = i4 ? pack_i4_tiles_bytes(a.N, a.K) : pack_i8_tiles_bytes(a.N, a.K);
+    a.w = c.ptr("w", tile_bytes * nexp);
+    if (!i4) a.scale = (const __half*)c.ptr("s", 2 * (size_t)a.N * nexp);
+    if (nexp > 1) {
+      a.w_stride = (long long)tile_bytes;
+      a.s_stride = i4 ? 0 : a.N;
+      a.sel = (const int*)c.ptr("sel", 4 * ((size_t)c.i("slot", 0) + 1), true);
+      a.slot = (int)c.i("slot", 0);
+      a.fixed_e = (int)c.i("fixe", 0);
+      if (a.fixed_e < 0 || a.fixed_e >= nexp) c.err = "fixe out of range";
+    }
+    a.rw_e = (int)c.i("rwe", 0);
+    a.rw = (const float*)c.ptr("rw", 4 * (size_t)a.NB * (a.rw_e > 0 ? a.rw_e : 1), true);
+    if (a.rw && a.epi != EPI_RESID) c.err = "rw needs epi=resid";
     a.bias = (const __half*)c.ptr("bias", 2 * (size_t)a.N, true);
     const size_t esz = (a.epi == EPI_F16 || a.epi == EPI_SWIGLU) ? 2 : 4;
     a.y = c.ptr("y", esz * ((size_t)(a.NB - 1) * a.ldy + out_cols));
@@ -422,6 +436,14 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
       a.layers = it->second.dev_layers;
       e = decode_mk_launch(a, it->second.plan, st);
     }
+  } else if (op.kind == "moe_gate") {
+    const int nb = (int)c.i("nb"), E = (int)c.i("e"), k = (int)c.i("k"), ld = (int)c.i("ld", E);
+    const float* lg = (const float*)c.ptr("logits", 4 * ((size_t)(nb - 1) * ld + E));
+    float* gw = (float*)c.ptr("gw", 4 * (size_t)nb * E);
+    int* sel = (int*)c.ptr("sel", 4 * (size_t)nb * k);
+    const int renorm = (int)c.i("renorm", 1);
+    if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+    if (!dry) e = moe_gate_launch(lg, ld, nb, E, k, renorm, gw, sel, st, pdl);
   } else if (op.kind == "allreduce" || op.kind == "allgather") {
     // fp32 sum over the ranks / int32 gather of n elements per rank, on the program's communicator
     const size_t n = (size_t)c.i("n");

@@ -191,3 +191,34 @@ def attn_decode_noalloc(qkv, kc, vc, pos, cos_t, sin_t, H, KV, dh, scale, kv_c=1
                                       _p(out), out.stride(0), NB, H, KV, dh, M, n_split, float(scale), float(kv_c),
                                       int(expand), _p(err), _stream(qkv))
   return rc, out
+
+
+def moe_gate(logits, k, renorm=True):
+  """Router logits [NB, E] fp32 -> (gw [NB, E] fp32, sel [NB, k] int32) on the device."""
+  import torch
+  NB, E = logits.shape
+  gw = torch.zeros((NB, E), dtype=torch.float32, device=logits.device)
+  sel = torch.zeros((NB, k), dtype=torch.int32, device=logits.device)
+  R.check(R.lib().af_moe_gate(_p(logits), logits.stride(0), NB, E, k, int(renorm), _p(gw), _p(sel), _stream(logits)),
+          "af_moe_gate")
+  return gw, sel
+
+
+def gemv_tc_expert(x, tiles, scales, N, K, E, wf=R.W_I8, epi=R.EPI_F32, y=None, sel=None, slot=0, fixed_e=0, rw=None,
+                   scratch=None):
+  """Tensor-core GEMV over E experts' tiles stored back to back; expert = sel[slot] or fixed_e."""
+  import torch
+  NB = x.shape[0]
+  cols = N // 2 if epi == R.EPI_SWIGLU else N
+  if y is None:
+    dt = torch.float16 if epi in (R.EPI_F16, R.EPI_SWIGLU) else torch.float32
+    y = torch.zeros((NB, cols), dtype=dt, device=x.device)
+  if scratch is None:
+    scratch, nbytes = gemv_tc_scratch(N, K, NB, x.device)
+  else:
+    nbytes = scratch.numel()
+  stride = tiles.numel() // E
+  R.check(R.lib().af_gemv_tc_expert(wf, epi, _p(x), x.stride(0), _p(tiles), _p(scales), _p(y), y.stride(0), NB, N, K,
+                                    _p(sel), slot, fixed_e, stride, N if scales is not None else 0, _p(rw), E,
+                                    _p(scratch), nbytes, _stream(x)), "af_gemv_tc_expert")
+  return y

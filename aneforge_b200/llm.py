@@ -195,7 +195,9 @@ class LlamaPrefill:
   (`aneforge/llm.py:636-654`) of numpy arrays or torch tensors (host or device)."""
 
   def __init__(self, cfg: LlamaConfig, weights: dict, compress: str | None = None, ane_lm_head: bool = True,
-               device: int = 0, compress_atol: float = 0.05, block_size: int = 32, tp=None):
+               device: int = 0, compress_atol: float = 0.05, block_size: int = 32, tp=None, moe_compress="same"):
+    # expert weights may use their own format (e.g. int4_g32 experts with int8 attention)
+    self.moe_compress = compress if moe_compress == "same" else moe_compress
     self.tp = tp if tp is not None and tp.world > 1 else None
     self.full_cfg, self._w_full = cfg, weights
     if self.tp is not None:
@@ -221,7 +223,8 @@ class LlamaPrefill:
   def _spec(self, i: int) -> LayerSpec:
     if self.cfg.layers:
       return self.cfg.layers[i]
-    return LayerSpec(qk_norm="q_norm" in self.w["layers"][i])
+    lw = self.w["layers"][i]
+    return LayerSpec(qk_norm="q_norm" in lw, mlp="moe" if "router" in lw else "swiglu")
 
   def _layer_chunks(self):
     """Reference chunk plan (`llm.py:425-433`); on B200 decode always runs as one program, which
@@ -284,7 +287,12 @@ class LlamaPrefill:
             "norms": sum(l["attn_g"].numel() * 2 + l["mlp_g"].numel() * 2 for l in d["layers"])}
 
   def _bind_layer(self, prog, li, d, with_kv_state=True):
-    for key in ("qkv", "o", "gu", "down"):
+    if "experts" in d:
+      ex = d["experts"]
+      prog.bind(f"L{li}.egu.w", ex.gu_w); prog.bind(f"L{li}.edown.w", ex.down_w)
+      if ex.gu_s is not None:
+        prog.bind(f"L{li}.egu.s", ex.gu_s); prog.bind(f"L{li}.edown.s", ex.down_s)
+    for key in ("qkv", "o", "gu", "down", "router"):
       if key not in d:
         continue
       lin = d[key]
@@ -298,7 +306,12 @@ class LlamaPrefill:
         prog.bind(f"L{li}.{key}", d[key])
 
   def _declare_layer_weights(self, pb, li, d):
-    for key in ("qkv", "o", "gu", "down"):
+    if "experts" in d:
+      ex = d["experts"]
+      pb.buf(f"L{li}.egu.w", ex.gu_w.numel(), "weight"); pb.buf(f"L{li}.edown.w", ex.down_w.numel(), "weight")
+      if ex.gu_s is not None:
+        pb.buf(f"L{li}.egu.s", ex.gu_s.numel() * 2, "weight"); pb.buf(f"L{li}.edown.s", ex.down_s.numel() * 2, "weight")
+    for key in ("qkv", "o", "gu", "down", "router"):
       if key not in d:
         continue
       lin = d[key]
@@ -341,7 +354,8 @@ class LlamaPrefill:
     pb.buf("hid", 2 * NB * D, "out"); pb.buf("logits", 4 * NB * V, "out")
     pb.buf("h", 4 * NB * D, "tmp"); pb.buf("xn", 2 * NB * D, "tmp"); pb.buf("qkv", 4 * NB * Q, "tmp")
     pb.buf("att", 2 * NB * H * dh, "tmp")
-    F = max((l["gu"].N // 2 for l in d["layers"] if "gu" in l), default=1)
+    F = max([l["gu"].N // 2 for l in d["layers"] if "gu" in l] + [l["experts"].F for l in d["layers"] if "experts" in l]
+            + [1])
     pb.buf("act", 2 * NB * F, "tmp")
     VL = int(d["lm_head"].shape[0])                       # local vocabulary rows (all of them without TP)
     pb.buf("embed", 2 * V * D, "weight"); pb.buf("lm_head", 2 * VL * D, "weight"); pb.buf("final_g", 2 * D, "weight")
@@ -468,7 +482,8 @@ class LlamaPrefill:
     pb.buf("ids", 4 * seq, "in"); pb.buf("hid", 2 * seq * D, "out")
     pb.buf("h", 4 * seq * D, "tmp"); pb.buf("xn", 2 * seq * D, "tmp"); pb.buf("qkv", 4 * seq * Q, "tmp")
     pb.buf("att", 2 * seq * H * dh, "tmp"); pb.buf("qbuf", 2 * seq * H * dh, "tmp")
-    F = max((l["gu"].N // 2 for l in d["layers"] if "gu" in l), default=1)
+    F = max([l["gu"].N // 2 for l in d["layers"] if "gu" in l] + [l["experts"].F for l in d["layers"] if "experts" in l]
+            + [1])
     pb.buf("act", 2 * seq * F, "tmp")
     if self.tp is not None:
       pb.buf("tp.part", 4 * seq * D, "tmp")

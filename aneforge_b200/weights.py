@@ -155,3 +155,75 @@ def rms_weights(gamma, eps, device):
   g_eff = (g.reshape(1, D).astype(F32) * float(np.sqrt(D))).astype(F16).reshape(D)
   floor = float(np.float16((D * float(eps)) ** 0.5))
   return to_device(g_eff, device), floor
+
+
+@dataclass
+class DevExperts:
+  """E experts' SwiGLU weights on the device, each expert's tiles back to back (the layout the expert
+  GEMVs index with `w_stride`): gate|up rows interleaved for the fused silu(gate)*up epilogue, down
+  with the FFN axis as its contraction."""
+  kind: str            # "int8" | "int4_g32"
+  gu_w: object         # uint8 [E * gu_bytes]
+  gu_s: object         # int8: fp16 [E * 2F] per-row scales; int4_g32: None (scales inside the tiles)
+  down_w: object       # uint8 [E * down_bytes]
+  down_s: object       # int8: fp16 [E * D] (one scale per expert, repeated per row); int4_g32: None
+  E: int
+  F: int
+  D: int
+
+  @property
+  def wf(self) -> str:
+    return "i4t" if self.kind == "int4_g32" else "i8t"
+
+  @property
+  def nbytes(self) -> int:
+    n = self.gu_w.numel() + self.down_w.numel()
+    for s in (self.gu_s, self.down_s):
+      if s is not None:
+        n += s.numel() * 2
+    return n
+
+
+def _per_expert_int8(W):
+  """The reference's `bmm_weight` encoding of one expert's down matrix (`aneforge/moe.py:60`, encoded
+  as one row of [E, ffn*dim]): one fp32 scale max|W|/127 for the whole expert, codes round-half-even
+  of W / scale clipped to +-127, scale stored fp16 - `_blob.quantize_per_row` on that row."""
+  torch = torch_mod()
+  W32 = W.float()
+  s = torch.clamp(W32.abs().max() / 127.0, min=1e-8)
+  q = torch.round(W32 / s).clamp(-127, 127).to(torch.int8)
+  return q, s.to(torch.float16)
+
+
+def encode_experts(wgate, wup, wdown, compress, device) -> DevExperts:
+  """wgate / wup / wdown: [E, F, D] (reference `moe.py` layout: down stored transposed for act @ w)."""
+  from . import kernels
+  torch = torch_mod()
+  E, F, D = (int(v) for v in wgate.shape)
+  kind = "int4_g32" if compress == "int4_g32" else "int8"
+  if kind == "int8" and compress not in ("int8", "int4", None):
+    raise NotImplementedError(f"expert compress={compress!r}")
+  if compress is None:
+    raise NotImplementedError("fp16 experts have no tiled device path; use compress='int8' or 'int4_g32'")
+  gu_w, gu_s, dn_w, dn_s = [], [], [], []
+  for e in range(E):
+    g = to_device(wgate[e], device); u = to_device(wup[e], device)
+    dT = to_device(wdown[e], device).t().contiguous()         # [D, F]: contraction over F
+    if kind == "int8":
+      qg, sg = kernels.quantize_per_row_i8(g.half() if g.dtype != torch.float32 else g)
+      qu, su = kernels.quantize_per_row_i8(u.half() if u.dtype != torch.float32 else u)
+      gu_w.append(kernels.pack_i8_tiles(layout.interleave_blocks(qg, qu, layout.SWIGLU_HALF_TC).contiguous()))
+      gu_s.append(layout.interleave_blocks(sg, su, layout.SWIGLU_HALF_TC))
+      q, s = _per_expert_int8(dT)
+      dn_w.append(kernels.pack_i8_tiles(q.contiguous()))
+      dn_s.append(s.reshape(1).expand(D).contiguous())
+    else:
+      pg, sg = kernels.quantize_g32_i4(g if g.dtype in (torch.float16, torch.float32) else g.float())
+      pu, su = kernels.quantize_g32_i4(u if u.dtype in (torch.float16, torch.float32) else u.float())
+      pp = layout.interleave_blocks(pg, pu, layout.SWIGLU_HALF_TC).contiguous()
+      sp = layout.interleave_blocks(sg, su, layout.SWIGLU_HALF_TC).contiguous()
+      gu_w.append(kernels.pack_i4_tiles(pp, sp, 2 * F, D))
+      pd, sd = kernels.quantize_g32_i4(dT if dT.dtype in (torch.float16, torch.float32) else dT.float())
+      dn_w.append(kernels.pack_i4_tiles(pd, sd, D, F))
+  cat = lambda xs: torch.cat(xs).contiguous() if xs else None
+  return DevExperts(kind, cat(gu_w), cat(gu_s), cat(dn_w), cat(dn_s), E, F, D)

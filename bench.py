@@ -48,6 +48,14 @@ MODELS = {
     metric="int4 decode tokens/s (Qwen2-72B-shaped, greedy)",
     workload="config 4: Qwen2-72B-shaped group-32 int4 greedy decode",
     dtype="int4 group-32 weights, fp16 activations, fp32 accumulation"),
+  "mixtral-8x7b": dict(
+    cfg=dict(dim=4096, n_layers=32, n_heads=32, n_kv_heads=8, ffn_dim=14336, vocab=32000, rope_base=1e6,
+             norm_eps=1e-5, extra={"n_experts": 8, "n_experts_per_tok": 2, "norm_topk_prob": True}),
+    compress="int8", moe_compress="int4_g32", prompt=1024, qkv_bias=False, moe=True,
+    traffic_profile="gemv_tc_i4_expert_gate_up_mixtral.md",
+    metric="int4-expert MoE decode tokens/s (Mixtral-8x7B-shaped, greedy)",
+    workload="config 5: Mixtral-8x7B-shaped MoE greedy decode, group-32 int4 experts, int8 attention",
+    dtype="int4 group-32 expert weights, int8 attention weights, fp16 activations, fp32 accumulation"),
 }
 MODEL = "llama3-8b"
 CFG = MODELS[MODEL]["cfg"]
@@ -144,8 +152,8 @@ class _LazyLayers:
   """The model's layer list, generated on access (seeded per layer) and not kept: a 72B model's fp16
   weights (145 GB) never exist at once, only the packed int4 copy the loader keeps."""
 
-  def __init__(self, cfg, device, seed, qkv_bias):
-    self.cfg, self.device, self.seed, self.qkv_bias = cfg, device, seed, qkv_bias
+  def __init__(self, cfg, device, seed, qkv_bias, moe=False):
+    self.cfg, self.device, self.seed, self.qkv_bias, self.moe = cfg, device, seed, qkv_bias, moe
 
   def __len__(self):
     return self.cfg.n_layers
@@ -160,8 +168,12 @@ class _LazyLayers:
     R = lambda *s: (torch.randn(*s, generator=g, device=dev, dtype=torch.float32) * 0.02).half()
     D, dh = cfg.dim, cfg.dh
     lw = {"wq": R(cfg.n_heads * dh, D), "wk": R(cfg.n_kv_heads * dh, D), "wv": R(cfg.n_kv_heads * dh, D),
-          "wo": R(D, cfg.n_heads * dh), "wgate": R(cfg.ffn_dim, D), "wup": R(cfg.ffn_dim, D),
-          "wdown": R(D, cfg.ffn_dim), "attn_norm": torch.ones(D, device=dev), "mlp_norm": torch.ones(D, device=dev)}
+          "wo": R(D, cfg.n_heads * dh), "attn_norm": torch.ones(D, device=dev), "mlp_norm": torch.ones(D, device=dev)}
+    if self.moe:
+      E, F = cfg.extra["n_experts"], cfg.ffn_dim
+      lw.update(router=R(E, D), wgate_exps=R(E, F, D), wup_exps=R(E, F, D), wdown_exps=R(E, F, D))
+    else:
+      lw.update(wgate=R(cfg.ffn_dim, D), wup=R(cfg.ffn_dim, D), wdown=R(D, cfg.ffn_dim))
     if self.qkv_bias:
       lw.update(q_bias=R(cfg.n_heads * dh), k_bias=R(cfg.n_kv_heads * dh), v_bias=R(cfg.n_kv_heads * dh))
     return lw
@@ -170,7 +182,7 @@ class _LazyLayers:
     return (self[i] for i in range(len(self)))
 
 
-def make_weights(cfg, device, seed=0, qkv_bias=False):
+def make_weights(cfg, device, seed=0, qkv_bias=False, moe=False):
   """Seeded N(0, 0.02) fp16 weights generated on the device, reference dict layout (layers lazily)."""
   import torch
   g = torch.Generator(device=device)
@@ -178,15 +190,32 @@ def make_weights(cfg, device, seed=0, qkv_bias=False):
   R = lambda *s: (torch.randn(*s, generator=g, device=device, dtype=torch.float32) * 0.02).half()
   D = cfg.dim
   return {"embed": R(cfg.vocab, D), "lm_head": R(cfg.vocab, D), "final_norm": torch.ones(D, device=device),
-          "layers": _LazyLayers(cfg, device, seed, qkv_bias)}
+          "layers": _LazyLayers(cfg, device, seed, qkv_bias, moe)}
 
 
-def algorithmic_bytes_per_step(cfg, NB, pos, compress="int8", qkv_bias=False):
+def _proj_bytes(n_params, rows, fmt):
+  """Codes + fp16 scales of one projection in a weight format."""
+  if fmt == "int4_g32":
+    return n_params // 2 + 2 * (n_params // 32)
+  return n_params + 2 * rows
+
+
+def algorithmic_bytes_per_step(cfg, NB, pos, compress="int8", qkv_bias=False, moe_compress=None):
   """Bytes a decode step must move once (each byte counted once per step): codes + fp16 scales of every
   projection (int8: 1 B/param + one scale per row; int4_g32: 0.5 B/param + one scale per 32), qkv
   biases, the fp16 lm_head, norms, KV cache read (positions 0..pos) + the new slot write, and the
   step's activations in/out."""
   D, H, KV, dh, F, V, L = cfg.dim, cfg.n_heads, cfg.n_kv_heads, cfg.dh, cfg.ffn_dim, cfg.vocab, cfg.n_layers
+  if cfg.extra.get("n_experts"):
+    # MoE: attention + router in `compress`; the experts a step reads in `moe_compress` - the top k at
+    # batch 1, every expert for larger batches (the dense per-row-weighted path)
+    E, k = cfg.extra["n_experts"], cfg.extra["n_experts_per_tok"]
+    attn = _proj_bytes((H + 2 * KV) * dh * D, (H + 2 * KV) * dh, compress) + _proj_bytes(D * H * dh, D, compress)
+    router = _proj_bytes(E * D, E, compress)
+    expert = _proj_bytes(2 * F * D, 2 * F, moe_compress) + _proj_bytes(D * F, D, moe_compress)
+    per_layer = attn + router + (k if NB == 1 else E) * expert + 2 * D * 2
+    kv = L * NB * (2 * KV * (pos + 1) * dh * 2)
+    return L * per_layer + V * D * 2 + D * 2 + kv + NB * (4 + 4)
   proj_rows = (H + 2 * KV) * dh + D + 2 * F + D
   proj_params = ((H + 2 * KV) * dh * D) + D * H * dh + 2 * F * D + D * F
   if compress == "int4_g32":
@@ -199,9 +228,22 @@ def algorithmic_bytes_per_step(cfg, NB, pos, compress="int8", qkv_bias=False):
   return L * per_layer + V * D * 2 + D * 2 + kv + NB * (4 + 4)
 
 
+class _ExpertGU:
+  """Expert e's fused gate|up projection of a layer, shaped like a DevLinear for the timing loop."""
+
+  def __init__(self, ex, e):
+    self.ex, self.e, self.kind = ex, e, "expert-" + ex.kind
+    self.N, self.K = 2 * ex.F, ex.D
+    self.nbytes = (ex.gu_w.numel() + (ex.gu_s.numel() * 2 if ex.gu_s is not None else 0)) // ex.E
+
+
 def _run_lin(kernels, R, x, lin, y, scr):
   """One fused gate|up projection launch in whatever tiled format the loader chose."""
-  if lin.kind == "int4_g32":
+  if isinstance(lin, _ExpertGU):
+    ex = lin.ex
+    kernels.gemv_tc_expert(x, ex.gu_w, ex.gu_s, lin.N, lin.K, ex.E, wf=R.W_I4G32 if ex.kind == "int4_g32" else R.W_I8,
+                           epi=R.EPI_SWIGLU, y=y, fixed_e=lin.e, scratch=scr)
+  elif lin.kind == "int4_g32":
     kernels.gemv_tc_i4(x, lin.w, lin.N, lin.K, epi=R.EPI_SWIGLU, y=y, scratch=scr)
   else:
     kernels.gemv_tc(x, lin.w, lin.s, lin.N, lin.K, epi=R.EPI_SWIGLU, y=y, scratch=scr)
@@ -222,12 +264,14 @@ def run_b200(args):
     # every rank; otherwise every rank runs its own replica on its own sequences (weak scaling)
     from aneforge_b200.tp import TensorParallel
     tp = TensorParallel.from_torch_distributed(local)
-  cfg = L.LlamaConfig(**CFG, layers=[L.LayerSpec() for _ in range(CFG["n_layers"])])
+  spec = MODELS[MODEL]
+  mlp = "moe" if spec.get("moe") else "swiglu"
+  cfg = L.LlamaConfig(**CFG, layers=[L.LayerSpec(mlp=mlp) for _ in range(CFG["n_layers"])])
   NB = args.batch
   t_load = time.perf_counter()
-  spec = MODELS[MODEL]
-  w = make_weights(cfg, dev, seed=1234 + (0 if tp else rank), qkv_bias=spec["qkv_bias"])
-  m = L.LlamaPrefill(cfg, w, compress=spec["compress"], device=local, tp=tp)
+  w = make_weights(cfg, dev, seed=1234 + (0 if tp else rank), qkv_bias=spec["qkv_bias"], moe=bool(spec.get("moe")))
+  m = L.LlamaPrefill(cfg, w, compress=spec["compress"], device=local, tp=tp,
+                     moe_compress=spec.get("moe_compress", "same"))
   m._load()
   del w
   torch.cuda.empty_cache()
@@ -302,20 +346,24 @@ def run_b200(args):
 
   # ---- dominant kernel: the fused gate|up int8 GEMV, timed alone on the program stream over the
   # 32 layers' own weights (3.7 GB > L2, so every launch streams from HBM)
-  gu = [m._dev["layers"][i]["gu"] for i in range(cfg.n_layers)]
+  if "experts" in m._dev["layers"][0]:
+    # MoE: one expert's gate|up (2 F x D) per launch, cycling over the layers' experts
+    E = cfg.extra["n_experts"]
+    gu = [_ExpertGU(m._dev["layers"][i]["experts"], e) for i in range(cfg.n_layers) for e in range(E)][:4 * cfg.n_layers]
+  else:
+    gu = [m._dev["layers"][i]["gu"] for i in range(cfg.n_layers)]
   x = torch.randn(NB, cfg.dim, device=dev).half()
   y = torch.empty(NB, cfg.ffn_dim, device=dev, dtype=torch.float16)
-  reps = 3 * cfg.n_layers
+  reps = 3 * len(gu)
   scr, _ = kernels.gemv_tc_scratch(gu[0].N, gu[0].K, NB, dev)
   with torch.cuda.stream(stream):
-    for i in range(cfg.n_layers):
-      _run_lin(kernels, R, x, gu[i], y, scr)
+    for l in gu:
+      _run_lin(kernels, R, x, l, y, scr)
     torch.cuda.synchronize()
     kgraph = torch.cuda.CUDAGraph()                       # launches back to back, not paced by the host
     with torch.cuda.graph(kgraph, stream=stream):
       for i in range(reps):
-        l = gu[i % cfg.n_layers]
-        _run_lin(kernels, R, x, l, y, scr)
+        _run_lin(kernels, R, x, gu[i % len(gu)], y, scr)
     kgraph.replay()
     torch.cuda.synchronize()
     k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -328,7 +376,7 @@ def run_b200(args):
   gu_bytes = gu[0].nbytes + NB * cfg.dim * 2 + NB * cfg.ffn_dim * 2
   peak, peak_kind = _peaks()
   step_bytes = algorithmic_bytes_per_step(cfg, NB, PROMPT + args.warmup + args.steps // 2, spec["compress"],
-                                          spec["qkv_bias"])
+                                          spec["qkv_bias"], spec.get("moe_compress"))
   result = None
   if rank == 0:
     achieved = gu_bytes / (k_us * 1e-6) / 1e9
@@ -338,7 +386,7 @@ def run_b200(args):
       "scaling": "strong" if tp else "weak",
       "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic",
       "config": {"workload": spec["workload"], "model": MODEL + "-shaped",
-                 "global_batch": NB * ws, "batch_per_gpu": NB, "seq_len": PROMPT, "decode_pos": f"{PROMPT}..{M}",
+                 "global_batch": NB * units, "batch_per_gpu": NB, "seq_len": PROMPT, "decode_pos": f"{PROMPT}..{M}",
                  "parallelism": f"tp{ws}" if tp else (f"replicas{ws}" if ws > 1 else "single"),
                  "l2": f"weights {step_bytes / 1e9:.1f} GB per step >> 126 MB L2 (no flush needed)"},
       "e2e": {"value": round(e2e_tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * NB,

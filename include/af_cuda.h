@@ -164,6 +164,18 @@ int af_gemv_tc_i4(int epi, const uint16_t* x, int ldx, const void* tiles, const 
 int af_decode_mk_scratch(int wf, int nb, int d, int h, int kv, int dh, int ffn, int nsplit, size_t* part_bytes,
                          size_t* cnt_bytes);
 
+/* Mixture of experts (reference aneforge/moe.py:21-63). af_moe_gate: router logits [nb][ld] fp32 ->
+ * softmax, top-k by k row-max peels (lowest index on ties, peel value f16(-3e4)), renormalised when
+ * renorm -> gw [nb][e] (0 off the top k) and sel [nb][k]. af_gemv_tc_expert: the tensor-core GEMV
+ * (wf AF_W_I8 tiles + scales, or AF_W_I4G32 tiles) over E experts stored back to back
+ * (`w_stride` bytes, `s_stride` scale halves apart), expert = sel[slot] (sel non-NULL, read on the
+ * device) or fixed_e; with epi AF_EPI_RESID and rw non-NULL each batch row's contribution is scaled
+ * by rw[b * rw_e + expert]. */
+int af_moe_gate(const float* logits, int ld, int nb, int e, int k, int renorm, float* gw, int* sel, void* stream);
+int af_gemv_tc_expert(int wf, int epi, const uint16_t* x, int ldx, const void* tiles, const uint16_t* scales,
+                      void* y, int ldy, int nb, int n, int k, const int* sel, int slot, int fixed_e, long long w_stride,
+                      int s_stride, const float* rw, int rw_e, void* scratch, size_t scratch_bytes, void* stream);
+
 /* lm_head GEMV + greedy argmax (lowest index on ties): replaces the host `hidden @ lm_head.T` and
  * np.argmax of LlamaPrefill._logits/_sample (aneforge/llm.py:349-355, :407-410). `logits` [nb][n]
  * may be NULL; `pos_advance` (may be NULL) is incremented per row. Scratch: see _scratch; it must be

@@ -34,6 +34,7 @@ from dataclasses import dataclass, field
 
 import numpy as np
 
+from . import quant
 from .quant import encode_weight
 
 F16, F32 = np.float16, np.float32
@@ -150,10 +151,14 @@ class OracleModel:
   optional q/k/v/o biases and q/k norms; MoE layers carry router/wgate_exps/wup_exps/wdown_exps)."""
 
   def __init__(self, cfg: Config, weights: dict, compress: str | None = None,
-               precision: str = "device", compress_atol: float = 0.05, block_size: int = 32):
+               precision: str = "device", compress_atol: float = 0.05, block_size: int = 32,
+               moe_compress: str | None = "same"):
     if precision not in ("fp32", "device"):
       raise ValueError(precision)
     self.cfg, self.w, self.compress, self.precision = cfg, weights, compress, precision
+    # expert weights may use their own format (e.g. int4_g32 experts with int8 attention); the
+    # reference has one compress= for the whole graph, which is the default here
+    self.moe_compress = compress if moe_compress == "same" else moe_compress
     self.atol, self.bs = compress_atol, block_size
     H, KV, dh, D = cfg.n_heads, cfg.n_kv_heads, cfg.dh, cfg.dim
     self.g = H // KV
@@ -191,7 +196,7 @@ class OracleModel:
     `linear`; gate/up are `linear`s over the expert-concatenated [g*ffn, dim] tiles of
     `_experts_gate` (tile = 65536 // ffn experts); down is one `bmm_weight` whose encoding sees
     [E, ffn*dim] (one row per expert)."""
-    c = self.compress
+    c = self.moe_compress
     E, ffn, dim = lw["wgate_exps"].shape
     gtile = max(1, min(E, 65536 // ffn))
     m = {"router": Linear(lw["router"], None, c, self.atol, self.bs), "E": E, "ffn": ffn}
@@ -202,6 +207,13 @@ class OracleModel:
         tiles.append(Linear(lw[key][s0:s0 + n].reshape(n * ffn, dim), None, c, self.atol, self.bs))
       m[key] = (tiles, gtile)
     Wd = np.asarray(lw["wdown_exps"])
+    m["router"] = Linear(lw["router"], None, self.compress, self.atol, self.bs)
+    if c == "int4_g32":
+      # this build's group-32 format groups along the contraction axis: each expert's down matrix is
+      # quantized as [dim, ffn] (groups of 32 along ffn); no reference counterpart
+      deq = [quant.dequant_g32_int4(*quant.quantize_g32_int4(np.ascontiguousarray(Wd[e].T))).T for e in range(E)]
+      m["wdown"] = np.stack(deq).astype(F32)
+      return m
     enc = encode_weight(Wd, c, self.atol, self.bs, allow_int8=True, allow_int4=True, allow_sparse=False)
     m["wdown"] = enc.deq.reshape(E, ffn, dim).astype(F32)
     return m

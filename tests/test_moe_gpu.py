@@ -1,0 +1,109 @@
+"""Mixture-of-experts on the device against the oracle: the router tail (softmax + top-k peel with
+lowest-index ties + renormalisation), expert selection inside the tensor-core GEMV (index read from
+device memory, routing-weighted residual epilogue), and whole MoE decoders (sparse top-k at batch 1,
+dense with per-row weights at batch 3) with int8 and group-32 int4 experts."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+from oracle import quant as Q                                                   # noqa: E402
+from oracle.model import Config, OracleModel, random_llama_weights, softmax, topk_gate   # noqa: E402
+
+F16, F32 = np.float16, np.float32
+
+
+@pytest.fixture(scope="module", autouse=True)
+def need_gpu():
+  if not torch.cuda.is_available():
+    pytest.skip("no CUDA device")
+
+
+def cuda(a):
+  return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("E,k", [(8, 2), (16, 4), (60, 8), (4, 1)])
+def test_moe_gate_matches_reference_rule(E, k):
+  from aneforge_b200 import kernels as K
+  rng = np.random.default_rng(E + k)
+  lg = rng.standard_normal((37, E)).astype(F32)
+  lg[0, :] = 0.5                                   # a full tie: the lowest indices win
+  lg[1, 3:] = lg[1, 2]                             # partial ties
+  gw, sel = K.moe_gate(cuda(lg), k)
+  gw, sel = gw.cpu().numpy(), sel.cpu().numpy()
+  probs = softmax(lg)
+  ref = topk_gate(probs, k)
+  ref = ref / ref.sum(axis=1, keepdims=True)
+  chosen = ref > 0
+  assert np.array_equal(gw > 0, chosen)
+  np.testing.assert_allclose(gw, ref, rtol=1e-5, atol=1e-7)
+  assert list(sel[0]) == list(range(k))
+  for b in range(37):
+    assert set(sel[b]) == set(np.nonzero(chosen[b])[0])
+
+
+@pytest.mark.parametrize("fmt", ["int8", "int4_g32"])
+@pytest.mark.parametrize("NB", [1, 3])
+def test_expert_gemv_selection_and_weighting(fmt, NB):
+  from aneforge_b200 import kernels as K, _runtime as R
+  rng = np.random.default_rng(5 + NB)
+  E, N, Kd = 4, 192, 512
+  Ws = [(rng.standard_normal((N, Kd)) * 0.02).astype(F16) for _ in range(E)]
+  x = rng.standard_normal((NB, Kd)).astype(F16)
+  if fmt == "int8":
+    enc = [Q.quantize_per_row(W) for W in Ws]
+    deq = [q.astype(F32) * s.astype(F32)[:, None] for q, s in enc]
+    tiles = torch.cat([K.pack_i8_tiles(cuda(q)) for q, _ in enc])
+    scales = cuda(np.concatenate([s for _, s in enc]))
+    wf = R.W_I8
+  else:
+    enc = [Q.quantize_g32_int4(W) for W in Ws]
+    deq = [Q.dequant_g32_int4(p, s) for p, s in enc]
+    tiles = torch.cat([K.pack_i4_tiles(cuda(p), cuda(s), N, Kd) for p, s in enc])
+    scales, wf = None, R.W_I4G32
+  sel = cuda(np.array([2, 1], np.int32))
+  for slot, e in ((0, 2), (1, 1)):
+    y = K.gemv_tc_expert(cuda(x), tiles, scales, N, Kd, E, wf=wf, sel=sel, slot=slot).cpu().numpy()
+    ref = x.astype(F32) @ deq[e].T
+    assert np.abs(y - ref).max() <= 1e-4 * np.abs(ref).max() + 1e-5
+  rw = rng.random((NB, E)).astype(F32)
+  y0 = rng.standard_normal((NB, N)).astype(F32)
+  yr = cuda(y0.copy())
+  K.gemv_tc_expert(cuda(x), tiles, scales, N, Kd, E, wf=wf, epi=R.EPI_RESID, y=yr, fixed_e=3, rw=cuda(rw))
+  ref = y0 + rw[:, 3:4] * (x.astype(F32) @ deq[3].T)
+  assert np.abs(yr.cpu().numpy() - ref).max() <= 1e-4 * np.abs(ref).max() + 1e-5
+
+
+def _moe_cfg():
+  return Config(dim=512, n_layers=2, n_heads=8, n_kv_heads=2, ffn_dim=384, vocab=2048, rope_base=10000.0,
+                head_dim=64, extra={"n_experts": 8, "n_experts_per_tok": 2, "norm_topk_prob": True})
+
+
+def _b200_cfg(cfg):
+  from aneforge_b200.llm import LlamaConfig, LayerSpec
+  return LlamaConfig(dim=cfg.dim, n_layers=cfg.n_layers, n_heads=cfg.n_heads, n_kv_heads=cfg.n_kv_heads,
+                     ffn_dim=cfg.ffn_dim, vocab=cfg.vocab, rope_base=cfg.rope_base, norm_eps=cfg.norm_eps,
+                     head_dim=cfg.head_dim, extra=dict(cfg.extra),
+                     layers=[LayerSpec(mlp="moe") for _ in range(cfg.n_layers)])
+
+
+@pytest.mark.parametrize("experts", ["int8", "int4_g32"])
+def test_moe_decoder_matches_oracle(experts):
+  from aneforge_b200.llm import LlamaPrefill
+  from tests.test_llm_gpu import teacher_forced_check
+  cfg = _moe_cfg()
+  w = random_llama_weights(cfg, seed=31, std=0.05, moe=True)
+  m = LlamaPrefill(_b200_cfg(cfg), w, compress="int8", moe_compress=experts)
+  prompt = list(np.random.default_rng(32).integers(0, cfg.vocab, 21))
+  toks = m.generate(prompt, 24, max_len=64)
+  om = OracleModel(cfg, w, "int8", precision="device", moe_compress=experts)
+  assert teacher_forced_check(om, prompt, toks, 64, n_check=24) <= 2
+  # batch 3 runs the dense per-row-weighted experts: the same tokens as batch 1 for each sequence
+  prompts = [prompt, list(np.random.default_rng(33).integers(0, cfg.vocab, 9)),
+             list(np.random.default_rng(34).integers(0, cfg.vocab, 14))]
+  batch = m.generate_batch(prompts, 12, max_len=48)
+  for p, b in zip(prompts, batch):
+    assert m.generate(p, 12, max_len=48) == b
+  m.release()
