@@ -413,6 +413,7 @@ cudaError_t gemv_tc_launch(const GemvTcArgs& a0, cudaStream_t st, bool pdl) {
     a.x = a0.x + (size_t)b0 * a0.ldx;
     const size_t esz = (a0.epi == EPI_F16 || a0.epi == EPI_SWIGLU) ? 2 : 4;
     a.y = static_cast<char*>(a0.y) + (size_t)b0 * a0.ldy * esz;
+    if (a0.rw) a.rw = a0.rw + (size_t)b0 * a0.rw_e;           // routing weights follow the rows
     cudaError_t e = gemv_tc_launch16(a, st, pdl && b0 == 0);
     if (e != cudaSuccess) return e;
   }
