@@ -72,6 +72,8 @@ SIGNATURES = [
   ("af_gemv_tc_expert", c_int, [c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                 c_void_p, c_int, c_int, ctypes.c_longlong, c_int, c_void_p, c_int, c_void_p, c_size_t,
                                 c_void_p]),
+  ("af_gemm_tc", c_int, [c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                         c_int, c_void_p]),
   ("af_rmsnorm", c_int, [c_void_p, c_int, c_int, c_void_p, c_float, c_void_p, c_int, c_int, c_int, c_void_p]),
   ("af_attn_decode_scratch", c_int, [c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(c_size_t)]),
   ("af_attn_decode", c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,

@@ -67,6 +67,8 @@ struct GemvTcArgs {
   int* counters = nullptr;
 };
 cudaError_t gemv_tc_launch(const GemvTcArgs& a, cudaStream_t st, bool pdl);
+// Prefill GEMM on tcgen05 (gemm_tc.cu): same arguments as the tiled GEMV with NB = M prompt rows.
+cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl);
 size_t gemv_tc_scratch_bytes(int N, int K, int NB);
 void gemv_tc_plan(int N, int K, int NB, int* S, int* NT);
 cudaError_t pack_i8_tiles(const int8_t* src, int N, int K, uint8_t* dst, cudaStream_t st);

@@ -161,6 +161,16 @@ int af_gemv_tc_expert(int wf, int epi, const uint16_t* x, int ldx, const void* t
   return rc_of(af::gemv_tc_launch(a, static_cast<cudaStream_t>(stream), false), "af_gemv_tc_expert");
 }
 
+int af_gemm_tc(int wf, int epi, const uint16_t* x, int ldx, const void* tiles, const uint16_t* scales,
+               const uint16_t* bias, void* y, int ldy, int m, int n, int k, void* stream) {
+  af::GemvTcArgs a;
+  a.wf = wf; a.epi = epi;
+  a.x = reinterpret_cast<const __half*>(x); a.ldx = ldx;
+  a.w = tiles; a.scale = reinterpret_cast<const __half*>(scales); a.bias = reinterpret_cast<const __half*>(bias);
+  a.y = y; a.ldy = ldy; a.NB = m; a.N = n; a.K = k;
+  return rc_of(af::gemm_tc_launch(a, static_cast<cudaStream_t>(stream), false), "af_gemm_tc");
+}
+
 int af_rmsnorm(const void* x, int x_f16, int ldx, const uint16_t* g, float floor, uint16_t* out, int ldo, int nb,
                int d, void* stream) {
   return rc_of(af::rmsnorm_launch(x, x_f16, ldx, reinterpret_cast<const __half*>(g), floor,

@@ -1,0 +1,314 @@
+// Prefill GEMM on the 5th-generation tensor cores: C[M, N] = X[M, K] . W[N, K]^T for the prompt rows
+// of a prefill (M = prompt length), W the same packed int8 / group-32 int4 fragment tiles the decode
+// GEMV streams, X fp16 activations.
+//
+// One CTA per 128 x 256 output tile (tcgen05.mma M=128, N=256, K=16 per instruction, fp32
+// accumulators in tensor memory: 256 TMEM columns x 128 lanes). A 4-stage shared-memory ring holds
+// 64-deep K slices of A (16 KB) and B (32 KB), both in the canonical K-major 128-byte-swizzled layout
+// the MMA reads through shared-memory descriptors:
+//   row r, 16-byte chunk c (8 fp16 along K) of a slice lives at (r / 8) * 1024 + (r % 8) * 128 +
+//   ((c ^ (r % 8)) * 16)  - eight-row atoms 1024 bytes apart (the descriptor's stride offset).
+// Warps 0-3 load A (global fp16 rows) and dequantise B into that layout: a weight tile lane's 16 bytes
+// are 2 rows x 8 consecutive columns (the GEMV's column permutation), int8 codes become exact fp16
+// (byte permute under the exponent of 1024, one subtract; the per-row scale is applied to the fp32
+// result), group-32 int4 codes become fp16 code * scale (the scale varies along K inside a slice).
+// Warp 4 owns the tensor memory and one of its threads issues the MMAs; each slice's MMAs commit to
+// the slice's "empty" barrier, the last commit to the accumulator barrier. Warps 0-3 then read the
+// accumulators (tcgen05.ld, 32 lanes each) and run the GEMV's epilogues (F32 / F16 / RESID / SWIGLU).
+// Every wait is bounded; on a timeout the CTA records AF_DEV_WAIT_TIMEOUT, waits (bounded) for the MMAs
+// it issued, frees its tensor memory and returns.
+#include "af_common.cuh"
+#include "af_kernels.h"
+#include "tc_common.cuh"
+
+namespace af {
+
+namespace gm {
+constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;          // 16 KB
+constexpr int B_BYTES = BN * BK * 2;          // 32 KB
+constexpr int STAGE = A_BYTES + B_BYTES;
+constexpr int LOADERS = 128;                  // warps 0-3
+constexpr int THREADS = LOADERS + 32;         // + warp 4 (TMEM owner, MMA issuer)
+constexpr int TMEM_COLS = 256;
+constexpr long long LIMIT = 1ll << 26;
+}  // namespace gm
+
+struct GemmShared {
+  uint64_t full[gm::STAGES];
+  uint64_t empty[gm::STAGES];
+  uint64_t accum;
+  uint32_t tmem;
+  int abort;
+};
+
+AF_DEV bool gm_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  for (long long i = 0; i < gm::LIMIT; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023) == 1023 && *abort) return false;
+  }
+  return false;
+}
+
+// offset of 16-byte chunk c of row r in a 128-byte-swizzled K-major slice
+AF_DEV uint32_t sw128(int r, int c) { return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)); }
+
+// shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 bytes apart
+AF_DEV uint64_t smem_desc(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) |
+         ((uint64_t)2 << 61);
+}
+
+// kind::f16, fp16 A and B (K-major), fp32 accumulate, M = 128, N = 256
+constexpr uint32_t GEMM_IDESC = (1u << 4) | ((uint32_t)(gm::BN >> 3) << 17) | ((uint32_t)(gm::BM >> 4) << 24);
+
+AF_DEV void mma_f16(uint32_t tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+      ::"r"(tmem), "l"(adesc), "l"(bdesc), "r"(GEMM_IDESC), "r"(accumulate) : "memory");
+}
+
+AF_DEV void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+AF_DEV void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// group-32 int4: 8 nibbles of one k-step (fragment slot order of pack_i4_tiles) -> the lane's two
+// rows' 4 values each, as code * scale in fp16
+AF_DEV void i4_rows(uint32_t w, __half2 s_lo, __half2 s_hi, uint32_t& row_lo0, uint32_t& row_lo1, uint32_t& row_hi0,
+                    uint32_t& row_hi1) {
+  uint32_t A[4];
+  i4x8_to_frag(w, A);                       // A0 = row g (c0, c1), A1 = row g+8 (c0, c1), A2 = row g (c2, c3), A3 = row g+8 (c2, c3)
+  __half2 a0 = __hmul2(*reinterpret_cast<__half2*>(&A[0]), s_lo);
+  __half2 a2 = __hmul2(*reinterpret_cast<__half2*>(&A[2]), s_lo);
+  __half2 a1 = __hmul2(*reinterpret_cast<__half2*>(&A[1]), s_hi);
+  __half2 a3 = __hmul2(*reinterpret_cast<__half2*>(&A[3]), s_hi);
+  row_lo0 = *reinterpret_cast<uint32_t*>(&a0);
+  row_lo1 = *reinterpret_cast<uint32_t*>(&a2);
+  row_hi0 = *reinterpret_cast<uint32_t*>(&a1);
+  row_hi1 = *reinterpret_cast<uint32_t*>(&a3);
+}
+
+template <bool I4>
+__global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  // the swizzled slices need 1024-byte aligned bases
+  const uint32_t raw = smem_u32(smem_raw);
+  unsigned char* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+  GemmShared* sh = reinterpret_cast<GemmShared*>(smem + gm::STAGES * gm::STAGE);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int MT = (a.NB + gm::BM - 1) / gm::BM;
+  const int mt = blockIdx.x % MT, nt = blockIdx.x / MT;     // M fastest: CTAs sharing a weight tile run together
+  const int m0 = mt * gm::BM, n0 = nt * gm::BN;
+  const int KT = a.K / 32, RB = a.Np / 64;
+  const int KB = (a.K + gm::BK - 1) / gm::BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < gm::STAGES; ++s) {
+      mbar_init(&sh->full[s], gm::LOADERS);
+      mbar_init(&sh->empty[s], 1);
+    }
+    mbar_init(&sh->accum, 1);
+    sh->abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 4) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(smem_u32(&sh->tmem)), "r"(gm::TMEM_COLS) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = sh->tmem;
+  volatile int* abort = &sh->abort;
+  pdl_wait();
+
+  if (warp == 4) {
+    // ------------------------------------------------------------------ MMA issuer (one thread)
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < KB; ++kb) {
+        const int s = kb % gm::STAGES;
+        if (!gm_wait(&sh->full[s], (uint32_t)((kb / gm::STAGES) & 1), abort)) { *abort = 1; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t abase = smem_u32(smem + s * gm::STAGE);
+        const uint32_t bbase = abase + gm::A_BYTES;
+#pragma unroll
+        for (int ks = 0; ks < gm::BK / 16; ++ks)
+          mma_f16(tmem, smem_desc(abase + ks * 32), smem_desc(bbase + ks * 32), (kb | ks) != 0);
+        mma_commit(&sh->empty[s]);
+        issued = kb + 1;
+      }
+      // the accumulator barrier completes once every MMA issued so far has finished (also on abort,
+      // so that the tensor memory is idle before it is freed)
+      mma_commit(&sh->accum);
+      (void)issued;
+    }
+  } else {
+    // ------------------------------------------------------------------ loaders (warps 0-3)
+    const int t = threadIdx.x;
+    const char* W = reinterpret_cast<const char*>(a.w);
+    for (int kb = 0; kb < KB && !*abort; ++kb) {
+      const int s = kb % gm::STAGES;
+      if (kb >= gm::STAGES && !gm_wait(&sh->empty[s], (uint32_t)(((kb / gm::STAGES) - 1) & 1), abort)) {
+        *abort = 1;
+        break;
+      }
+      unsigned char* As = smem + s * gm::STAGE;
+      unsigned char* Bs = As + gm::A_BYTES;
+      const int k0 = kb * gm::BK;
+      // A: 128 rows x 8 chunks of 8 fp16
+#pragma unroll 4
+      for (int c = t; c < gm::BM * 8; c += gm::LOADERS) {
+        const int r = c >> 3, kc = c & 7;
+        const int m = m0 + r, k = k0 + kc * 8;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (m < a.NB && k < a.K) v = __ldcg(reinterpret_cast<const uint4*>(a.x + (size_t)m * a.ldx + k));
+        *reinterpret_cast<uint4*>(As + sw128(r, kc)) = v;
+      }
+      // B: 4 row blocks x 2 k tiles of packed weight units, one tile lane (2 rows x 8 columns) each
+#pragma unroll 2
+      for (int q = t; q < gm::BN / 64 * 2 * 128; q += gm::LOADERS) {
+        const int u = q >> 7, rbi = u >> 1, kti = u & 1;
+        const int w = (q >> 5) & 3, ln = q & 31, g = ln >> 2, t4 = ln & 3;
+        const int rb = n0 / 64 + rbi, kt = k0 / 32 + kti;
+        const int nb = rbi * 64 + w * 16 + g;                 // row of the B slice (and nb + 8)
+        const int kc = kti * 4 + t4;                          // 16-byte chunk of the slice's K
+        uint32_t lo[4] = {0u, 0u, 0u, 0u}, hi[4] = {0u, 0u, 0u, 0u};
+        if (rb < RB && kt < KT) {
+          if constexpr (I4) {
+            const char* unit = W + ((size_t)rb * KT + kt) * tc::UNIT4;
+            const uint2 wv = __ldg(reinterpret_cast<const uint2*>(unit + w * tc::TILE4 + ln * 8));
+            const __half2 sc = __ldg(reinterpret_cast<const __half2*>(unit + tc::WARPS * tc::TILE4 + (w * 16 + 2 * g) * 2));
+            const __half2 s_lo = __half2half2(__low2half(sc)), s_hi = __half2half2(__high2half(sc));
+            i4_rows(wv.x, s_lo, s_hi, lo[0], lo[1], hi[0], hi[1]);
+            i4_rows(wv.y, s_lo, s_hi, lo[2], lo[3], hi[2], hi[3]);
+          } else {
+            const uint4 wv = __ldg(reinterpret_cast<const uint4*>(W + ((size_t)rb * KT + kt) * tc::UNIT + w * tc::TILE +
+                                                                 ln * 16));
+            i8x4_to_h2x2(wv.x, lo[0], hi[0]);
+            i8x4_to_h2x2(wv.y, lo[1], hi[1]);
+            i8x4_to_h2x2(wv.z, lo[2], hi[2]);
+            i8x4_to_h2x2(wv.w, lo[3], hi[3]);
+          }
+        }
+        *reinterpret_cast<uint4*>(Bs + sw128(nb, kc)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        *reinterpret_cast<uint4*>(Bs + sw128(nb + 8, kc)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      }
+      // generic-proxy stores -> visible to the tensor core's async proxy, then signal the slice
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive(&sh->full[s]);
+    }
+  }
+
+  // ---------------------------------------------------------------- epilogue (warps 0-3)
+  if (warp < 4) {
+    const bool ok = gm_wait(&sh->accum, 0, abort) && !*abort;
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (!ok) {
+      af_set_err(a.err, AF_DEV_WAIT_TIMEOUT);
+    } else {
+      const int m = m0 + warp * 32 + lane;
+#pragma unroll 1
+      for (int c0 = 0; c0 < gm::BN; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+        if (m >= a.NB) continue;
+        const int nbase = n0 + c0;
+        float f[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int n = nbase + j;
+          float x = __uint_as_float(v[j]);
+          if (n < a.N) {
+            if (!I4) x = __fmul_rn(x, h2f(a.scale[n]));
+            if (a.bias) x = __fadd_rn(x, h2f(a.bias[n]));
+          }
+          f[j] = x;
+        }
+        if (a.epi == EPI_SWIGLU) {
+          // rows 16i..16i+7 gate, 16i+8..16i+15 up -> 8 outputs per 16 rows
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int r0 = nbase + 16 * i;
+            if (r0 + 15 >= a.N + 0 && r0 >= a.N) continue;
+            __half o[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = f2h(silu_f(f[16 * i + j]) * f[16 * i + 8 + j]);
+            if (r0 + 16 <= a.N)
+              *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(a.y) + (size_t)m * a.ldy + r0 / 2) =
+                  *reinterpret_cast<const uint4*>(o);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int n = nbase + j;
+            if (n >= a.N) break;
+            const size_t o = (size_t)m * a.ldy + n;
+            if (a.epi == EPI_F32) reinterpret_cast<float*>(a.y)[o] = f[j];
+            else if (a.epi == EPI_F16) reinterpret_cast<__half*>(a.y)[o] = f2h(f[j]);
+            else reinterpret_cast<float*>(a.y)[o] = reinterpret_cast<float*>(a.y)[o] + f[j];
+          }
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 4) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(gm::TMEM_COLS) : "memory");
+  }
+}
+
+size_t gemm_tc_smem_bytes() { return (size_t)gm::STAGES * gm::STAGE + sizeof(GemmShared) + 1024; }
+
+// x [M][ldx] fp16 (M = a.NB rows), weights as for gemv_tc, y per epilogue (ldy); M >= 1, K % 32 == 0.
+cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
+  if (a.NB < 1 || a.N <= 0 || a.K <= 0 || a.K % 32 || a.ldx % 8) return cudaErrorInvalidValue;
+  if (a.epi != EPI_F32 && a.epi != EPI_F16 && a.epi != EPI_RESID && a.epi != EPI_SWIGLU) return cudaErrorInvalidValue;
+  if (a.epi == EPI_SWIGLU && a.N % 16) return cudaErrorInvalidValue;
+  if (a.sel || a.rw) return cudaErrorInvalidValue;            // experts run through the GEMV
+  const bool i4 = a.wf == W_I4G32;
+  if (!i4 && (a.wf != W_I8 || !a.scale)) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(a.x) & 15) || (reinterpret_cast<uintptr_t>(a.w) & 15)) return cudaErrorInvalidValue;
+  a.Np = (a.N + 63) / 64 * 64;
+  const int MT = (a.NB + gm::BM - 1) / gm::BM, NT = (a.N + gm::BN - 1) / gm::BN;
+  const size_t smem = gemm_tc_smem_bytes();
+  void* fn = i4 ? (void*)gemm_tc_kernel<true> : (void*)gemm_tc_kernel<false>;
+  static bool attr[2] = {false, false};
+  if (!attr[i4]) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr[i4] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(MT * NT));
+  cfg.blockDim = dim3(gm::THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  void* args[] = {&a};
+  return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+}  // namespace af

@@ -329,7 +329,9 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     if (a.scratch_bytes) a.scratch = c.ptr("scr", a.scratch_bytes);
     a.err = p.d_err;
     if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
-    if (!dry) e = gemv_tc_launch(a, st, pdl);
+    // prompt-sized row counts (prefill) run as a tensor-core GEMM unless the op asks for the GEMV
+    const bool gemm = c.i("gemm", 0) != 0 && nexp == 1;
+    if (!dry) e = gemm ? gemm_tc_launch(a, st, pdl) : gemv_tc_launch(a, st, pdl);
   } else if (op.kind == "gemv") {
     GemvArgs a;
     const std::string* wfs = c.raw("wf");

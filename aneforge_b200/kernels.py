@@ -222,3 +222,16 @@ def gemv_tc_expert(x, tiles, scales, N, K, E, wf=R.W_I8, epi=R.EPI_F32, y=None, 
                                     _p(sel), slot, fixed_e, stride, N if scales is not None else 0, _p(rw), E,
                                     _p(scratch), nbytes, _stream(x)), "af_gemv_tc_expert")
   return y
+
+
+def gemm_tc(x, tiles, scales, N, K, wf=R.W_I8, bias=None, epi=R.EPI_F32, y=None):
+  """Prefill GEMM on tcgen05 over packed tiles: x [M, K] fp16 -> y [M, N] (or [M, N/2] for SWIGLU)."""
+  import torch
+  M = x.shape[0]
+  cols = N // 2 if epi == R.EPI_SWIGLU else N
+  if y is None:
+    dt = torch.float16 if epi in (R.EPI_F16, R.EPI_SWIGLU) else torch.float32
+    y = torch.zeros((M, cols), dtype=dt, device=x.device)
+  R.check(R.lib().af_gemm_tc(wf, epi, _p(x), x.stride(0), _p(tiles), _p(scales), _p(bias), _p(y), y.stride(0), M, N, K,
+                             _stream(x)), "af_gemm_tc")
+  return y

@@ -146,6 +146,15 @@ size_t af_gemv_tc_scratch_bytes(int n, int k, int nb);
 int af_gemv_tc(int epi, const uint16_t* x, int ldx, const void* tiles, const uint16_t* scales, const uint16_t* bias,
                void* y, int ldy, int nb, int n, int k, void* scratch, size_t scratch_bytes, void* stream);
 
+/* Prefill GEMM on the 5th-generation tensor cores (tcgen05.mma, fp32 accumulators in tensor memory):
+ * y[m][n] = epilogue(sum_k x[m][k] * w[n][k]) for m prompt rows, over the same packed tiles as the
+ * decode GEMVs (wf AF_W_I8: af_pack_i8_tiles + per-row scales applied to the fp32 sums; AF_W_I4G32:
+ * af_pack_i4_tiles, dequantised to fp16 code * scale before the MMA). Epilogues AF_EPI_F32 / F16 /
+ * RESID / SWIGLU as af_gemv_tc; k % 32 == 0. Replaces the reference's prefill `matmul`
+ * (_compile.py:375-385 inside the prefill graph, llm.py:118-169). */
+int af_gemm_tc(int wf, int epi, const uint16_t* x, int ldx, const void* tiles, const uint16_t* scales,
+               const uint16_t* bias, void* y, int ldy, int m, int n, int k, void* stream);
+
 /* Group-32 int4 on the tensor pipe: codes from af_quantize_g32_i4 (packed [n][k/2] + scales [n][k/32])
  * re-packed once into 16x32 fragment tiles with each k tile's 64 row scales appended
  * ([ceil(n/64)][k/32][4 x 256 B | 64 fp16], k % 32 == 0). y = sum over groups of s_g * (x . codes_g),
