@@ -3,20 +3,25 @@
 // GEMV streams, X fp16 activations.
 //
 // One CTA per 128 x 256 output tile (tcgen05.mma M=128, N=256, K=16 per instruction, fp32
-// accumulators in tensor memory: 256 TMEM columns x 128 lanes). A 4-stage shared-memory ring holds
+// accumulators in tensor memory: 256 TMEM columns x 128 lanes). A 3-stage shared-memory ring holds
 // 64-deep K slices of A (16 KB) and B (32 KB), both in the canonical K-major 128-byte-swizzled layout
 // the MMA reads through shared-memory descriptors:
 //   row r, 16-byte chunk c (8 fp16 along K) of a slice lives at (r / 8) * 1024 + (r % 8) * 128 +
 //   ((c ^ (r % 8)) * 16)  - eight-row atoms 1024 bytes apart (the descriptor's stride offset).
-// Warps 0-3 load A (global fp16 rows) and dequantise B into that layout: a weight tile lane's 16 bytes
-// are 2 rows x 8 consecutive columns (the GEMV's column permutation), int8 codes become exact fp16
-// (byte permute under the exponent of 1024, one subtract; the per-row scale is applied to the fp32
-// result), group-32 int4 codes become fp16 code * scale (the scale varies along K inside a slice).
-// Warp 4 owns the tensor memory and one of its threads issues the MMAs; each slice's MMAs commit to
-// the slice's "empty" barrier, the last commit to the accumulator barrier. Warps 0-3 then read the
-// accumulators (tcgen05.ld, 32 lanes each) and run the GEMV's epilogues (F32 / F16 / RESID / SWIGLU).
-// Every wait is bounded; on a timeout the CTA records AF_DEV_WAIT_TIMEOUT, waits (bounded) for the MMAs
-// it issued, frees its tensor memory and returns.
+// Roles: warp 5 (one thread) issues, per slice, a TMA tensor copy of the A tile (the copy engine
+// applies the 128-byte swizzle; rows past M read as zeros) and bulk copies of the raw packed weight
+// units of the slice (4 row blocks x 2 k tiles); warps 0-3 turn the raw units into the fp16 B slice
+// (a weight tile lane's 16 bytes are 2 rows x 8 consecutive columns - the GEMV's column permutation;
+// int8 codes become exact fp16 by a byte permute under the exponent of 1024 and one subtract, the
+// per-row scale is applied to the fp32 result; group-32 int4 codes become fp16 code * scale since
+// the scale changes along K inside a slice); warp 4 owns the tensor memory and one of its threads
+// issues the MMAs, committing each slice to its "empty" barrier and the last to the accumulator
+// barrier. Warps 0-3 then read the accumulators (tcgen05.ld, 32 lanes each) and run the GEMV's
+// epilogues (F32 / F16 / RESID / SWIGLU).
+// Every wait is bounded; on a timeout the CTA records AF_DEV_WAIT_TIMEOUT, waits (bounded) for the
+// MMAs it issued, frees its tensor memory and returns. No copy uses cluster multicast.
+#include <cuda.h>
+
 #include "af_common.cuh"
 #include "af_kernels.h"
 #include "tc_common.cuh"
@@ -25,19 +30,21 @@ namespace af {
 
 namespace gm {
 constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int STAGES = 4;
+constexpr int STAGES = 3;
 constexpr int A_BYTES = BM * BK * 2;          // 16 KB
 constexpr int B_BYTES = BN * BK * 2;          // 32 KB
-constexpr int STAGE = A_BYTES + B_BYTES;
-constexpr int LOADERS = 128;                  // warps 0-3
-constexpr int THREADS = LOADERS + 32;         // + warp 4 (TMEM owner, MMA issuer)
+constexpr int RAW_BYTES = (BN / 64) * 2 * tc::UNIT;   // 16 KB: raw int8 units of one slice (int4: less)
+constexpr int STAGE = A_BYTES + B_BYTES + RAW_BYTES;
+constexpr int CONV = 128;                     // warps 0-3: converters, then epilogue
+constexpr int THREADS = CONV + 64;            // + warp 4 (TMEM owner, MMA issuer) + warp 5 (copies)
 constexpr int TMEM_COLS = 256;
 constexpr long long LIMIT = 1ll << 26;
 }  // namespace gm
 
 struct GemmShared {
-  uint64_t full[gm::STAGES];
-  uint64_t empty[gm::STAGES];
+  uint64_t raw[gm::STAGES];                   // A tile + raw weight units landed (copy bytes)
+  uint64_t full[gm::STAGES];                  // fp16 B slice written (converters)
+  uint64_t empty[gm::STAGES];                 // the slice's MMAs finished reading (tcgen05.commit)
   uint64_t accum;
   uint32_t tmem;
   int abort;
@@ -103,8 +110,15 @@ AF_DEV void i4_rows(uint32_t w, __half2 s_lo, __half2 s_hi, uint32_t& row_lo0, u
   row_hi1 = *reinterpret_cast<uint32_t*>(&a3);
 }
 
+// 2-D TMA tile load (no multicast) of box {64 K, 128 rows} at (k0, m0), completion on `bar`
+AF_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int k0, int m0, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(k0), "r"(m0), "r"(smem_u32(bar)) : "memory");
+}
+
 template <bool I4>
-__global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a) {
+__global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, const __grid_constant__ CUtensorMap amap) {
   extern __shared__ unsigned char smem_raw[];
   // the swizzled slices need 1024-byte aligned bases
   const uint32_t raw = smem_u32(smem_raw);
@@ -116,10 +130,12 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a) {
   const int m0 = mt * gm::BM, n0 = nt * gm::BN;
   const int KT = a.K / 32, RB = a.Np / 64;
   const int KB = (a.K + gm::BK - 1) / gm::BK;
+  constexpr int UNIT = I4 ? tc::UNIT4 : tc::UNIT;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < gm::STAGES; ++s) {
-      mbar_init(&sh->full[s], gm::LOADERS);
+      mbar_init(&sh->raw[s], 1);
+      mbar_init(&sh->full[s], gm::CONV);
       mbar_init(&sh->empty[s], 1);
     }
     mbar_init(&sh->accum, 1);
@@ -136,12 +152,46 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a) {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = sh->tmem;
   volatile int* abort = &sh->abort;
-  pdl_wait();
 
-  if (warp == 4) {
-    // ------------------------------------------------------------------ MMA issuer (one thread)
+  if (warp == 5) {
+    // ---------------------------------------------------------------- copies (one thread)
     if (lane == 0) {
+      const char* W = reinterpret_cast<const char*>(a.w);
       int issued = 0;
+      // weights never change: the first slices' units may go out before the programmatic wait
+      for (int kb = 0; kb < KB; ++kb) {
+        const int s = kb % gm::STAGES;
+        if (kb >= gm::STAGES && !gm_wait(&sh->empty[s], (uint32_t)(((kb / gm::STAGES) - 1) & 1), abort)) {
+          *abort = 1;
+          break;
+        }
+        unsigned char* st = smem + s * gm::STAGE;
+        const int kt = kb * 2, nk = min(2, KT - kt);
+        uint32_t bytes = 0;
+        for (int rbi = 0; rbi < gm::BN / 64; ++rbi)
+          if (n0 / 64 + rbi < RB) bytes += (uint32_t)nk * UNIT;
+        mbar_arrive_expect_tx(&sh->raw[s], bytes + gm::A_BYTES);
+        for (int rbi = 0; rbi < gm::BN / 64; ++rbi) {
+          const int rb = n0 / 64 + rbi;
+          if (rb < RB)
+            bulk_g2s(st + gm::A_BYTES + gm::B_BYTES + rbi * 2 * UNIT, W + ((size_t)rb * KT + kt) * UNIT, nk * UNIT,
+                     &sh->raw[s]);
+        }
+        if (kb == 0) pdl_wait();                      // A is the preceding kernel's output
+        tma_load_2d(st, &amap, kb * gm::BK, m0, &sh->raw[s]);
+        issued = kb + 1;
+      }
+      if (issued == 0) pdl_wait();
+      // shared memory must outlive every copy issued: wait (time-bounded only) for the last slices
+      for (int kb = issued - 1; kb >= 0 && kb >= issued - gm::STAGES; --kb) {
+        const int s = kb % gm::STAGES;
+        for (long long i = 0; i < gm::LIMIT && !mbar_try_wait(&sh->raw[s], (uint32_t)((kb / gm::STAGES) & 1)); ++i) {
+        }
+      }
+    }
+  } else if (warp == 4) {
+    // ---------------------------------------------------------------- MMA issuer (one thread)
+    if (lane == 0) {
       for (int kb = 0; kb < KB; ++kb) {
         const int s = kb % gm::STAGES;
         if (!gm_wait(&sh->full[s], (uint32_t)((kb / gm::STAGES) & 1), abort)) { *abort = 1; break; }
@@ -152,55 +202,38 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a) {
         for (int ks = 0; ks < gm::BK / 16; ++ks)
           mma_f16(tmem, smem_desc(abase + ks * 32), smem_desc(bbase + ks * 32), (kb | ks) != 0);
         mma_commit(&sh->empty[s]);
-        issued = kb + 1;
       }
-      // the accumulator barrier completes once every MMA issued so far has finished (also on abort,
-      // so that the tensor memory is idle before it is freed)
+      // completes once every MMA issued so far has finished (also on abort, so that the tensor
+      // memory is idle before it is freed)
       mma_commit(&sh->accum);
-      (void)issued;
     }
   } else {
-    // ------------------------------------------------------------------ loaders (warps 0-3)
+    // ---------------------------------------------------------------- converters (warps 0-3)
     const int t = threadIdx.x;
-    const char* W = reinterpret_cast<const char*>(a.w);
-    for (int kb = 0; kb < KB && !*abort; ++kb) {
+    for (int kb = 0; kb < KB; ++kb) {
       const int s = kb % gm::STAGES;
-      if (kb >= gm::STAGES && !gm_wait(&sh->empty[s], (uint32_t)(((kb / gm::STAGES) - 1) & 1), abort)) {
-        *abort = 1;
-        break;
-      }
-      unsigned char* As = smem + s * gm::STAGE;
-      unsigned char* Bs = As + gm::A_BYTES;
-      const int k0 = kb * gm::BK;
-      // A: 128 rows x 8 chunks of 8 fp16
+      if (!gm_wait(&sh->raw[s], (uint32_t)((kb / gm::STAGES) & 1), abort)) { *abort = 1; break; }
+      unsigned char* st = smem + s * gm::STAGE;
+      unsigned char* Bs = st + gm::A_BYTES;
+      const unsigned char* Rw = Bs + gm::B_BYTES;
+      const int kt0 = kb * 2;
 #pragma unroll 4
-      for (int c = t; c < gm::BM * 8; c += gm::LOADERS) {
-        const int r = c >> 3, kc = c & 7;
-        const int m = m0 + r, k = k0 + kc * 8;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (m < a.NB && k < a.K) v = __ldcg(reinterpret_cast<const uint4*>(a.x + (size_t)m * a.ldx + k));
-        *reinterpret_cast<uint4*>(As + sw128(r, kc)) = v;
-      }
-      // B: 4 row blocks x 2 k tiles of packed weight units, one tile lane (2 rows x 8 columns) each
-#pragma unroll 2
-      for (int q = t; q < gm::BN / 64 * 2 * 128; q += gm::LOADERS) {
+      for (int q = t; q < gm::BN / 64 * 2 * 128; q += gm::CONV) {
         const int u = q >> 7, rbi = u >> 1, kti = u & 1;
         const int w = (q >> 5) & 3, ln = q & 31, g = ln >> 2, t4 = ln & 3;
-        const int rb = n0 / 64 + rbi, kt = k0 / 32 + kti;
         const int nb = rbi * 64 + w * 16 + g;                 // row of the B slice (and nb + 8)
         const int kc = kti * 4 + t4;                          // 16-byte chunk of the slice's K
         uint32_t lo[4] = {0u, 0u, 0u, 0u}, hi[4] = {0u, 0u, 0u, 0u};
-        if (rb < RB && kt < KT) {
+        if (n0 / 64 + rbi < RB && kt0 + kti < KT) {
+          const unsigned char* unit = Rw + (rbi * 2 + kti) * UNIT;
           if constexpr (I4) {
-            const char* unit = W + ((size_t)rb * KT + kt) * tc::UNIT4;
-            const uint2 wv = __ldg(reinterpret_cast<const uint2*>(unit + w * tc::TILE4 + ln * 8));
-            const __half2 sc = __ldg(reinterpret_cast<const __half2*>(unit + tc::WARPS * tc::TILE4 + (w * 16 + 2 * g) * 2));
+            const uint2 wv = *reinterpret_cast<const uint2*>(unit + w * tc::TILE4 + ln * 8);
+            const __half2 sc = *reinterpret_cast<const __half2*>(unit + tc::WARPS * tc::TILE4 + (w * 16 + 2 * g) * 2);
             const __half2 s_lo = __half2half2(__low2half(sc)), s_hi = __half2half2(__high2half(sc));
             i4_rows(wv.x, s_lo, s_hi, lo[0], lo[1], hi[0], hi[1]);
             i4_rows(wv.y, s_lo, s_hi, lo[2], lo[3], hi[2], hi[3]);
           } else {
-            const uint4 wv = __ldg(reinterpret_cast<const uint4*>(W + ((size_t)rb * KT + kt) * tc::UNIT + w * tc::TILE +
-                                                                 ln * 16));
+            const uint4 wv = *reinterpret_cast<const uint4*>(unit + w * tc::TILE + ln * 16);
             i8x4_to_h2x2(wv.x, lo[0], hi[0]);
             i8x4_to_h2x2(wv.y, lo[1], hi[1]);
             i8x4_to_h2x2(wv.z, lo[2], hi[2]);
@@ -246,13 +279,12 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a) {
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
             const int r0 = nbase + 16 * i;
-            if (r0 + 15 >= a.N + 0 && r0 >= a.N) continue;
+            if (r0 + 16 > a.N) continue;
             __half o[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) o[j] = f2h(silu_f(f[16 * i + j]) * f[16 * i + 8 + j]);
-            if (r0 + 16 <= a.N)
-              *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(a.y) + (size_t)m * a.ldy + r0 / 2) =
-                  *reinterpret_cast<const uint4*>(o);
+            *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(a.y) + (size_t)m * a.ldy + r0 / 2) =
+                *reinterpret_cast<const uint4*>(o);
           }
         } else {
 #pragma unroll
@@ -262,7 +294,7 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a) {
             const size_t o = (size_t)m * a.ldy + n;
             if (a.epi == EPI_F32) reinterpret_cast<float*>(a.y)[o] = f[j];
             else if (a.epi == EPI_F16) reinterpret_cast<__half*>(a.y)[o] = f2h(f[j]);
-            else reinterpret_cast<float*>(a.y)[o] = reinterpret_cast<float*>(a.y)[o] + f[j];
+            else reinterpret_cast<float*>(a.y)[o] = __ldcg(reinterpret_cast<const float*>(a.y) + o) + f[j];
           }
         }
       }
@@ -278,6 +310,17 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a) {
 
 size_t gemm_tc_smem_bytes() { return (size_t)gm::STAGES * gm::STAGE + sizeof(GemmShared) + 1024; }
 
+// The A operand's tensor map: fp16 [M rows][K] with row stride ldx, 64 x 128 boxes, 128-byte swizzle.
+static bool make_amap(const GemvTcArgs& a, CUtensorMap* map) {
+  const cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.NB};
+  const cuuint64_t strides[1] = {(cuuint64_t)a.ldx * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)gm::BK, (cuuint32_t)gm::BM};
+  const cuuint32_t estr[2] = {1, 1};
+  return cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(a.x), dims, strides, box,
+                                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // x [M][ldx] fp16 (M = a.NB rows), weights as for gemv_tc, y per epilogue (ldy); M >= 1, K % 32 == 0.
 cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
   if (a.NB < 1 || a.N <= 0 || a.K <= 0 || a.K % 32 || a.ldx % 8) return cudaErrorInvalidValue;
@@ -288,6 +331,8 @@ cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
   if (!i4 && (a.wf != W_I8 || !a.scale)) return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(a.x) & 15) || (reinterpret_cast<uintptr_t>(a.w) & 15)) return cudaErrorInvalidValue;
   a.Np = (a.N + 63) / 64 * 64;
+  CUtensorMap amap;
+  if (!make_amap(a, &amap)) return cudaErrorInvalidValue;
   const int MT = (a.NB + gm::BM - 1) / gm::BM, NT = (a.N + gm::BN - 1) / gm::BN;
   const size_t smem = gemm_tc_smem_bytes();
   void* fn = i4 ? (void*)gemm_tc_kernel<true> : (void*)gemm_tc_kernel<false>;
@@ -307,7 +352,7 @@ cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
-  void* args[] = {&a};
+  void* args[] = {&a, &amap};
   return cudaLaunchKernelExC(&cfg, fn, args);
 }
 

@@ -325,12 +325,13 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     a.bias = (const __half*)c.ptr("bias", 2 * (size_t)a.N, true);
     const size_t esz = (a.epi == EPI_F16 || a.epi == EPI_SWIGLU) ? 2 : 4;
     a.y = c.ptr("y", esz * ((size_t)(a.NB - 1) * a.ldy + out_cols));
-    a.scratch_bytes = gemv_tc_scratch_bytes(a.N, a.K, a.NB);
+    const bool want_gemm = c.i("gemm", 0) != 0;
+    a.scratch_bytes = want_gemm ? 0 : gemv_tc_scratch_bytes(a.N, a.K, a.NB);
     if (a.scratch_bytes) a.scratch = c.ptr("scr", a.scratch_bytes);
     a.err = p.d_err;
     if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
     // prompt-sized row counts (prefill) run as a tensor-core GEMM unless the op asks for the GEMV
-    const bool gemm = c.i("gemm", 0) != 0 && nexp == 1;
+    const bool gemm = want_gemm && nexp == 1;
     if (!dry) e = gemm ? gemm_tc_launch(a, st, pdl) : gemv_tc_launch(a, st, pdl);
   } else if (op.kind == "gemv") {
     GemvArgs a;

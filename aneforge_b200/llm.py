@@ -106,16 +106,24 @@ def rope_tables(seq: int, dh: int, base: float = 10000.0, rotary_dim: int = 0, i
 # activation buffers and shapes: h (fp32 residual [NB, D]), xn (fp16 [NB, D]), qkv, att, act, pos,
 # NB, M; `lw` is the layer's packed device weights (names of bound buffers, see _bind_layer).
 
+# Row counts from which a tiled projection runs as the tensor-core GEMM (prefill) instead of the GEMV:
+# the GEMV streams the weights once per 16 rows, the GEMM once per 128.
+GEMM_MIN_ROWS = 32
+
+
 def _emit_linear(pb, ctx, name, lin: DevLinear, x, y, epi, nb=None):
   nb = nb or ctx["NB"]
   kv = dict(wf=lin.wf, epi=epi, x=x, w=f"{name}.w", y=y, nb=nb, n=lin.N, k=lin.K)
   if lin.kind == "int8":
     kv["s"] = f"{name}.s"
   if lin.kind in ("int8", "int4_g32") and lin.tiled:
-    nbytes = R.load_library().af_gemv_tc_scratch_bytes(lin.N, lin.K, nb)
-    if nbytes:
-      pb.buf("gemv.scr", nbytes, "scratch")          # one split-K scratch shared by every GEMV
-      kv["scr"] = "gemv.scr"
+    if nb >= GEMM_MIN_ROWS:
+      kv["gemm"] = 1                                 # prompt rows: the tcgen05 GEMM
+    else:
+      nbytes = R.load_library().af_gemv_tc_scratch_bytes(lin.N, lin.K, nb)
+      if nbytes:
+        pb.buf("gemv.scr", nbytes, "scratch")        # one split-K scratch shared by every GEMV
+        kv["scr"] = "gemv.scr"
   elif lin.kind == "int4_g32" and not lin.tiled:
     kv["gs"] = f"{name}.s"
   if lin.bias is not None:

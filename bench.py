@@ -441,6 +441,40 @@ def kernel_bench(name, reps, warmup):
 
   I4 = {"gemv_i4_gu": (2 * 29568, 8192, R.EPI_SWIGLU), "gemv_i4_qkv": (80 * 128, 8192, R.EPI_F32),
         "gemv_i4_o": (8192, 8192, R.EPI_RESID), "gemv_i4_down": (8192, 29568, R.EPI_RESID)}
+  if name in ("gemm_gu", "gemm_i4_gu"):
+    # prefill: the tcgen05 GEMM over a 512-row (8B) / 2048-row (72B) prompt; FLOP-bound
+    i4 = name == "gemm_i4_gu"
+    M, N, Kd = (2048, 2 * 29568, 8192) if i4 else (512, 2 * F, D)
+    W = (torch.randn(N, Kd, generator=g, device=dev) * 0.02).half()
+    if i4:
+      pk, sc = K.quantize_g32_i4(W); tiles = K.pack_i4_tiles(pk, sc, N, Kd); sc = None
+    else:
+      q, sc = K.quantize_per_row_i8(W); tiles = K.pack_i8_tiles(q)
+    del W
+    x = torch.randn(M, Kd, generator=g, device=dev).half()
+    y = torch.empty(M, N // 2, device=dev, dtype=torch.float16)
+    fn = lambda i: K.gemm_tc(x, tiles, sc, N, Kd, wf=R.W_I4G32 if i4 else R.W_I8, epi=R.EPI_SWIGLU, y=y)
+    flops = 2.0 * M * N * Kd
+    with torch.cuda.stream(st):
+      for i in range(warmup):
+        fn(i)
+      torch.cuda.synchronize()
+      e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+      e0.record(st)
+      for i in range(reps):
+        fn(i)
+      e1.record(st)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    try:
+      with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+        tpk, tkind = float(json.load(f)["bf16_tflops"]), "measured bf16 dense (cuBLAS burst)"
+    except Exception:
+      tpk, tkind = 1590.0, "fallback"
+    tf = flops / (us * 1e-6) / 1e12
+    return {"kernel": name, "what": f"gemm_tc {'int4_g32' if i4 else 'int8'} M={M} N={N} K={Kd} swiglu",
+            "us_per_launch": round(us, 1), "tflops": round(tf, 1), "peak_tflops": tpk, "peak_kind": tkind,
+            "frac": round(tf / tpk, 4), "reps": reps, "warmup": warmup}
   if name in I4:                                            # Qwen2-72B shapes, group-32 int4
     N, Kd, epi = I4[name]
     copies = max(2, -(-300_000_000 // (N * Kd // 2)))
@@ -581,7 +615,7 @@ def main():
   ap.add_argument("--no-cpu-baseline", action="store_true")
   ap.add_argument("--kernel", default=None,
                   help="time one kernel alone: gemv_gu | gemv_qkv | gemv_o | gemv_down | gemv_cfg1 | attn | lm_head "
-                       "| gemv_i4_gu | gemv_i4_qkv | gemv_i4_o | gemv_i4_down")
+                       "| gemv_i4_gu | gemv_i4_qkv | gemv_i4_o | gemv_i4_down | gemm_gu | gemm_i4_gu")
   ap.add_argument("--reps", type=int, default=50)
   ap.add_argument("--profile-region", action="store_true",
                   help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
