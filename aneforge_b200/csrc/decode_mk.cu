@@ -258,16 +258,17 @@ AF_DEV bool gemv_phase(const MkArgs& a, const MkGemv& gd, MkShared* sh, unsigned
     const int rb = (int)(u / KT), kta = (int)(u % KT);
     const int ktb = (int)min((long long)KT, kta + (u1 - u));
     const int xb = x_base(xp, si);
-    float acc[NT][4];
+    float acc[NT][4], acc2[NT][4];
 #pragma unroll
     for (int n = 0; n < NT; ++n)
 #pragma unroll
-      for (int q = 0; q < 4; ++q) acc[n][q] = 0.f;
+      for (int q = 0; q < 4; ++q) { acc[n][q] = 0.f; acc2[n][q] = 0.f; }
     bool stuck = false;
     for (int kt = kta; kt < ktb; kt += F::ks) {
       const int nk = min(F::ks, ktb - kt);
       if (!mk_wait(&sh->full[stage], phase, a.err)) { stuck = true; break; }
-      consume_stage<I4, NT>(ring + (size_t)stage * F::stage, nk, xs + xb + kt * 32, xstride, a.NB, lane, rtw, par, acc);
+      consume_stage<I4, NT, 2>(ring + (size_t)stage * F::stage, nk, xs + xb + kt * 32, xstride, a.NB, lane, rtw, par, acc,
+                               acc2);
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh->empty[stage]);
       if (++stage == nst) { stage = 0; phase ^= 1; }
@@ -277,6 +278,10 @@ AF_DEV bool gemv_phase(const MkArgs& a, const MkGemv& gd, MkShared* sh, unsigned
       *reinterpret_cast<volatile int*>(&sh->cabort) = 1;
     }
     if (prof && threadIdx.x == 0) prof[3] = gtimer();
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[n][q] += acc2[n][q];
     float* rw = red + ((size_t)rtw * 32 + lane) * (NT * 4);
     if (par) {
 #pragma unroll

@@ -79,8 +79,16 @@ AF_DEV void epilogue(const GemvTcArgs& a, float (&acc)[NT][4], int rt, int g, in
   }
 }
 
+// consumer warps per CTA: one per row tile (int8), or two splitting the k tiles (int4, whose
+// conversion costs more instructions per byte)
+template <bool I4> struct Cw { static constexpr int n = I4 ? 8 : 4; };
+
+template <int CW>
+AF_DEV void consumer_sync_n() { asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory"); }
+
 template <int NT, int EPI, bool I4>
-__global__ void __launch_bounds__((tc::CWARPS + 1) * 32) gemv_tc_kernel(GemvTcArgs a) {
+__global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArgs a) {
+  constexpr int CW = Cw<I4>::n;
   // expert selection (MoE): the expert index may be produced by the preceding kernel, so with `sel`
   // the weights are addressed only after the programmatic-launch wait
   int expert = a.fixed_e;
@@ -110,18 +118,18 @@ __global__ void __launch_bounds__((tc::CWARPS + 1) * 32) gemv_tc_kernel(GemvTcAr
   if (threadIdx.x == 0) {
     for (int s = 0; s < tc::STAGES; ++s) {
       mbar_init(&sh->full[s], 1);
-      mbar_init(&sh->empty[s], tc::CWARPS);
+      mbar_init(&sh->empty[s], CW);
     }
     for (int s = 0; s < tc::XSLOTS; ++s) {
       mbar_init(&sh->xfull[s], 1);
-      mbar_init(&sh->xempty[s], tc::CWARPS);
+      mbar_init(&sh->xempty[s], CW);
     }
     sh->cabort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
 
-  if (warp == tc::CWARPS) {
+  if (warp == CW) {
     // -------------------------------------------------------------- producer (one thread)
     if (lane != 0) return;
     const char* W = reinterpret_cast<const char*>(a.w);
@@ -185,13 +193,13 @@ __global__ void __launch_bounds__((tc::CWARPS + 1) * 32) gemv_tc_kernel(GemvTcAr
     return;
   }
 
-  // ---------------------------------------------------------------- consumers (8 warps)
+  // ---------------------------------------------------------------- consumers (4 or 8 warps)
   // Warps w and w + 4 share row tile w of the row block: within every stage the first multiplies the
   // even k tiles, the second the odd ones; their sums meet in shared memory at the end of each
   // row-block range. The tiles' columns are permuted so that a lane's B fragments for both k-steps
   // of a k tile are 8 consecutive x values: one 16-byte shared load per k tile.
   const int g = lane >> 2, t = lane & 3;
-  const int rtw = warp & 3, par = warp >> 2;
+  const int rtw = warp & 3, par = warp >> 2;          // par: 0 with 4 consumer warps
   float* red = reinterpret_cast<float*>(smem_raw + tc::STAGES * F::stage + SH_BYTES +
                                         (size_t)tc::XSLOTS * xslot_halves * 2);       // [4][32][NT*4]
   pdl_wait();
@@ -202,11 +210,11 @@ __global__ void __launch_bounds__((tc::CWARPS + 1) * 32) gemv_tc_kernel(GemvTcAr
   while (u < u1) {
     const int rb = (int)(u / KT), kta = (int)(u % KT);
     const int ktb = (int)min((long long)KT, kta + (u1 - u));
-    float acc[NT][4];
+    float acc[NT][4], acc2[NT][4];
 #pragma unroll
     for (int n = 0; n < NT; ++n)
 #pragma unroll
-      for (int q = 0; q < 4; ++q) acc[n][q] = 0.f;
+      for (int q = 0; q < 4; ++q) { acc[n][q] = 0.f; acc2[n][q] = 0.f; }
     bool stuck = false;
     for (int kc = kta; kc < ktb && !stuck; kc += tc::XKT) {
       const int kce = min(kc + tc::XKT, ktb);
@@ -215,8 +223,8 @@ __global__ void __launch_bounds__((tc::CWARPS + 1) * 32) gemv_tc_kernel(GemvTcAr
       for (int kt = kc; kt < kce; kt += F::ks) {
         const int nk = min(F::ks, kce - kt);
         if (!mbar_wait(&sh->full[stage], phase)) { stuck = true; break; }
-        consume_stage<I4, NT>(ring + (size_t)stage * F::stage, nk, xsl + (kt - kc) * 32, tc::XSTRIDE, a.NB, lane, rtw,
-                              par, acc);
+        consume_stage<I4, NT, CW / 4>(ring + (size_t)stage * F::stage, nk, xsl + (kt - kc) * 32, tc::XSTRIDE, a.NB, lane,
+                                      rtw, par, acc, acc2);
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh->empty[stage]);
         if (++stage == tc::STAGES) { stage = 0; phase ^= 1; }
@@ -230,16 +238,20 @@ __global__ void __launch_bounds__((tc::CWARPS + 1) * 32) gemv_tc_kernel(GemvTcAr
       *reinterpret_cast<volatile int*>(&sh->cabort) = 1;
     }
     // odd-tile warps hand their sums to the even-tile warps of the same row tile
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[n][q] += acc2[n][q];
     float* rw = red + ((size_t)rtw * 32 + lane) * (NT * 4);
-    if (par) {
+    if (CW == 8 && par) {
 #pragma unroll
       for (int n = 0; n < NT; ++n)
 #pragma unroll
         for (int q = 0; q < 4; ++q) rw[n * 4 + q] = acc[n][q];
     }
-    consumer_sync();
+    consumer_sync_n<CW>();
     if (*reinterpret_cast<volatile int*>(&sh->cabort)) break;
-    if (!par) {
+    if (CW == 8 && !par) {
 #pragma unroll
       for (int n = 0; n < NT; ++n)
 #pragma unroll
@@ -266,9 +278,9 @@ __global__ void __launch_bounds__((tc::CWARPS + 1) * 32) gemv_tc_kernel(GemvTcAr
         }
         __threadfence();
       }
-      consumer_sync();
+      consumer_sync_n<CW>();
       if (threadIdx.x == 0) sh->ticket = atomicAdd(a.counters + rb, 1) == nc - 1;
-      consumer_sync();
+      consumer_sync_n<CW>();
       if (sh->ticket && !par) {
         __threadfence();
 #pragma unroll
@@ -288,7 +300,7 @@ __global__ void __launch_bounds__((tc::CWARPS + 1) * 32) gemv_tc_kernel(GemvTcAr
         if (threadIdx.x == 0) a.counters[rb] = 0;
       }
     }
-    consumer_sync();          // the reduction slots in shared memory are free for the next range
+    consumer_sync_n<CW>();          // the reduction slots in shared memory are free for the next range
     u += ktb - kta;
   }
 }
@@ -324,7 +336,7 @@ static int grid_for(int NB) {
     cudaFuncSetAttribute(gemv_tc_kernel<NT, EPI, I4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem_bytes(16, I4));
     int o = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, gemv_tc_kernel<NT, EPI, I4>, (tc::CWARPS + 1) * 32,
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, gemv_tc_kernel<NT, EPI, I4>, (Cw<I4>::n + 1) * 32,
                                                       smem_bytes(NB, I4)) != cudaSuccess || o < 1)
       o = 1;
     const int cap = env_int("AF_TC_CTAS_PER_SM", 4);
@@ -391,7 +403,7 @@ static cudaError_t launch_tc(GemvTcArgs a, cudaStream_t st, bool pdl) {
   a.maxc = maxc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G);
-  cfg.blockDim = dim3((tc::CWARPS + 1) * 32);
+  cfg.blockDim = dim3((Cw<I4>::n + 1) * 32);
   cfg.dynamicSmemBytes = smem_bytes(a.NB, I4);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

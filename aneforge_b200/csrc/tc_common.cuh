@@ -123,20 +123,22 @@ AF_DEV void i4x8_to_frag(uint32_t w, uint32_t (&A)[4]) {
   A[3] = *reinterpret_cast<uint32_t*>(&h3);
 }
 
-// One ring stage on one consumer warp: the warp owns row tile `rtw` and the k tiles par, par + 2,
-// ... of the stage (its partner warp takes the others). `xk` points at the staged x of the stage's
-// first k tile (row stride `xstride` halves); the tiles' column permutation makes a lane's B
-// fragments for both k-steps of a tile one 16-byte load. Products accumulate into acc (int4:
-// each tile's product is formed fresh and added times its group scale).
-template <bool I4, int NT>
+// One ring stage on one consumer warp: the warp owns row tile `rtw` and the k tiles par, par + PSTEP,
+// ... of the stage (with PSTEP = 2 a partner warp takes the others). Consecutive tiles of the warp
+// alternate between two accumulator sets (acc, acc2) so that two MMA chains are in flight. `xk`
+// points at the staged x of the stage's first k tile (row stride `xstride` halves); the tiles' column
+// permutation makes a lane's B fragments for both k-steps of a tile one 16-byte load. int4 products
+// are formed fresh per tile and added times the tile's group scale.
+template <bool I4, int NT, int PSTEP>
 AF_DEV void consume_stage(const unsigned char* sb, int nk, const __half* xk, int xstride, int NB, int lane, int rtw,
-                          int par, float (&acc)[NT][4]) {
+                          int par, float (&acc)[NT][4], float (&acc2)[NT][4]) {
   using F = tc::Fmt<I4>;
   const int g = lane >> 2, t = lane & 3;
 #pragma unroll
-  for (int kk = 0; kk < F::ks; kk += 2) {
-    const int k2 = kk + par;
+  for (int i = 0; i < F::ks / PSTEP; ++i) {
+    const int k2 = par + PSTEP * i;
     if (k2 >= nk) break;
+    float (&ac)[NT][4] = (i & 1) ? acc2 : acc;
     uint4 xv[NT];
 #pragma unroll
     for (int n = 0; n < NT; ++n) {
@@ -158,10 +160,10 @@ AF_DEV void consume_stage(const unsigned char* sb, int nk, const __half* xk, int
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
         mma_16816(tmp[n], A, xv[n].z, xv[n].w);
-        acc[n][0] = fmaf(sc.x, tmp[n][0], acc[n][0]);
-        acc[n][1] = fmaf(sc.x, tmp[n][1], acc[n][1]);
-        acc[n][2] = fmaf(sc.y, tmp[n][2], acc[n][2]);
-        acc[n][3] = fmaf(sc.y, tmp[n][3], acc[n][3]);
+        ac[n][0] = fmaf(sc.x, tmp[n][0], ac[n][0]);
+        ac[n][1] = fmaf(sc.x, tmp[n][1], ac[n][1]);
+        ac[n][2] = fmaf(sc.y, tmp[n][2], ac[n][2]);
+        ac[n][3] = fmaf(sc.y, tmp[n][3], ac[n][3]);
       }
     } else {
       const uint4 w = *reinterpret_cast<const uint4*>(sb + k2 * F::unit + rtw * F::tile + lane * 16);
@@ -169,11 +171,11 @@ AF_DEV void consume_stage(const unsigned char* sb, int nk, const __half* xk, int
       i8x4_to_h2x2(w.x, A[0], A[1]);
       i8x4_to_h2x2(w.y, A[2], A[3]);
 #pragma unroll
-      for (int n = 0; n < NT; ++n) mma_16816(acc[n], A, xv[n].x, xv[n].y);
+      for (int n = 0; n < NT; ++n) mma_16816(ac[n], A, xv[n].x, xv[n].y);
       i8x4_to_h2x2(w.z, A[0], A[1]);
       i8x4_to_h2x2(w.w, A[2], A[3]);
 #pragma unroll
-      for (int n = 0; n < NT; ++n) mma_16816(acc[n], A, xv[n].z, xv[n].w);
+      for (int n = 0; n < NT; ++n) mma_16816(ac[n], A, xv[n].z, xv[n].w);
     }
   }
 }
