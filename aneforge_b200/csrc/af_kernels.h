@@ -117,6 +117,10 @@ struct AttnDecodeArgs {
   float scale = 0.f;           // fp16-rounded 1/sqrt(dh)
   float kv_c = 1.f;            // GQA expansion factor (applied as f16(c * f16(k)))
   int expand = 0;
+  // 1: `pos` was written before the preceding kernel started (a decode step's position is advanced
+  // by the step's last kernel), so each CTA may read it and bulk-copy its first cache rows into
+  // shared memory before the programmatic-launch wait, overlapping the qkv projection's tail
+  int prefetch = 0;
 };
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st, bool pdl);
 size_t attn_decode_scratch_floats(int NB, int KV, int n_split, int G, int dh);

@@ -23,6 +23,15 @@
 namespace af {
 
 constexpr int DEC_WARPS = 8;
+constexpr int DEC_PRE = 32;                    // cache rows per CTA staged in shared memory up front
+
+AF_DEV void load_row_f16_sh(const __half* p, int lane, float* f, int epl, int lanes) {
+  if (lane >= lanes) {
+    for (int e = 0; e < epl; ++e) f[e] = 0.f;
+    return;
+  }
+  for (int e = 0; e < epl; ++e) f[e] = __half2float(p[lane * epl + e]);
+}
 
 template <int DH, int G>
 __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDecodeArgs a) {
@@ -40,9 +49,39 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
   __shared__ float wm[NW][G], wl[NW][G];
   __shared__ float wacc[NW][G][DH];
   __shared__ int last_s;
+  __shared__ uint64_t kv_bar;
+  extern __shared__ __align__(16) unsigned char kv_pre[];     // [K rows | V rows] x DEC_PRE x DH fp16
 
+  // with `prefetch`, the first DEC_PRE cache rows of this CTA's key range (all before pos, so
+  // written in earlier steps) are requested before waiting for the qkv projection
+  int n_pre = 0;
+  int pos = 0;
+  if (a.prefetch) {
+    pos = __ldcg(a.pos + b);
+    if (pos >= 0 && pos < a.M) {
+      const int len0 = (pos + a.n_split) / a.n_split;
+      const int j00 = split * len0;
+      n_pre = max(0, min(min(j00 + len0, pos), j00 + DEC_PRE) - j00);
+      if (threadIdx.x == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"((uint32_t)__cvta_generic_to_shared(&kv_bar)) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        if (n_pre > 0) {
+          const uint32_t bytes = (uint32_t)n_pre * DH * 2;
+          const __half* kb0 = a.kc + (((size_t)b * a.KV + kvh) * a.M + j00) * DH;
+          const __half* vb0 = a.vc + (((size_t)b * a.KV + kvh) * a.M + j00) * DH;
+          const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&kv_bar);
+          asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(2 * bytes) : "memory");
+          asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                       ::"r"((uint32_t)__cvta_generic_to_shared(kv_pre)), "l"(kb0), "r"(bytes), "r"(bar) : "memory");
+          asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                       ::"r"((uint32_t)__cvta_generic_to_shared(kv_pre + DEC_PRE * DH * 2)), "l"(vb0), "r"(bytes), "r"(bar)
+                       : "memory");
+        }
+      }
+    }
+  }
   pdl_wait();
-  const int pos = __ldcg(a.pos + b);
+  if (!a.prefetch) pos = __ldcg(a.pos + b);
   if (pos < 0 || pos >= a.M) {
     if (threadIdx.x == 0 && split == 0 && kvh == 0) af_set_err(a.err, AF_DEV_BAD_POS);
     return;
@@ -105,13 +144,33 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
   const int my_idx = lane >> DB::SHIFT;                 // value index this lane ends up holding
   const int my_g = my_idx / PB, my_p = my_idx % PB;
   const bool rep0 = (lane & ((1 << DB::SHIFT) - 1)) == 0;
+  if (n_pre > 0) {
+    // bounded wait for the staged rows; on a timeout they are read from global memory instead
+    const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&kv_bar);
+    bool ok = false;
+    for (long long i = 0; i < (1ll << 24) && !ok; ++i) {
+      uint32_t r;
+      asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n selp.u32 %0, 1, 0, p;\n}\n"
+                   : "=r"(r) : "r"(bar) : "memory");
+      ok = r != 0;
+    }
+    if (!ok) {
+      if (threadIdx.x == 0) af_set_err(a.err, AF_DEV_WAIT_TIMEOUT);
+      n_pre = 0;
+    }
+  }
+  const __half* kpre = reinterpret_cast<const __half*>(kv_pre);
+  const __half* vpre = kpre + DEC_PRE * DH;
   for (int base = j0 + warp * PB; base < j1; base += NW * PB) {
     float kf[PB][EPL], vf[PB][EPL];
 #pragma unroll
     for (int p = 0; p < PB; ++p) {
       const int j = base + p;
       const bool in_range = j < j1;                // keys past this CTA's range are zeros
-      if (in_range && j != pos) {
+      if (in_range && j != pos && j - j0 < n_pre) {
+        load_row_f16_sh(kpre + (size_t)(j - j0) * DH, lane, kf[p], EPL, HL::LANES);
+        load_row_f16_sh(vpre + (size_t)(j - j0) * DH, lane, vf[p], EPL, HL::LANES);
+      } else if (in_range && j != pos) {
         load_row_f16<DH>(kbase + (size_t)j * DH, lane, kf[p]);
         load_row_f16<DH>(vbase + (size_t)j * DH, lane, vf[p]);
       } else {
@@ -255,6 +314,14 @@ static cudaError_t launch_decode(const AttnDecodeArgs& a, cudaStream_t st, bool 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.n_split, a.KV, a.NB);
   cfg.blockDim = dim3(DEC_WARPS * 32);
+  cfg.dynamicSmemBytes = a.prefetch ? 2 * DEC_PRE * DH * 2 : 0;
+  static bool smem_opt = false;                // static + dynamic shared memory may pass 48 KB (G = 8)
+  if (a.prefetch && !smem_opt) {
+    const cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<DH, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               2 * DEC_PRE * DH * 2);
+    if (e != cudaSuccess) return e;
+    smem_opt = true;
+  }
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

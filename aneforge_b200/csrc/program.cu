@@ -396,6 +396,7 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     a.scale = (float)c.f("scale");
     a.kv_c = (float)c.f("kvc", 1.0);
     a.expand = c.i("expand", 0);
+    a.prefetch = (int)c.i("prefetch", 0);
     a.err = p.d_err;
     if ((a.cos_t == nullptr) != (a.sin_t == nullptr)) c.err = "cos/sin must both be given";
     if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }

@@ -151,8 +151,10 @@ def emit_attention_decode(pb, ctx, li, lw, cfg, ls):
   pre = f"L{li}"
   pb.op("rmsnorm", x="h", g=f"{pre}.attn_g", out="xn", nb=NB, d=D, floor=lw["attn_floor"])
   _emit_linear(pb, ctx, f"{pre}.qkv", lw["qkv"], "xn", "qkv", "f32")
+  # prefetch=1: the step's position is only advanced by its last kernel (the head), so attention may
+  # stage its first cache rows before the qkv projection finishes
   kv = dict(qkv="qkv", kc=f"{pre}.K", vc=f"{pre}.V", pos="pos", out="att", nb=NB, h=H, kv=KV, dh=dh, m=M,
-            nsplit=ctx["nsplit"], scale=ctx["scale"], kvc=ctx["kvc"], expand=int(ctx["expand"]))
+            nsplit=ctx["nsplit"], scale=ctx["scale"], kvc=ctx["kvc"], expand=int(ctx["expand"]), prefetch=1)
   if cfg.rope:
     kv.update(cos="rope.cos", sin="rope.sin")
   if ls.qk_norm:
