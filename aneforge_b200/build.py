@@ -69,7 +69,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     msg = "\n".join(f"--- {s.name}\n{o}" for s, o in failed)
     raise RuntimeError(f"nvcc failed:\n{msg}")
   tmp = LIB.with_suffix(".so.tmp")
-  link = [nvcc(), "-shared", "-o", str(tmp)] + [str(o) for o in objs] + ARCH + ["-lcudart", "-lcuda"]
+  link = [nvcc(), "-shared", "-o", str(tmp)] + [str(o) for o in objs] + ARCH + ["-lcudart"]
   r = subprocess.run(link, capture_output=True, text=True)
   if r.returncode != 0:
     raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

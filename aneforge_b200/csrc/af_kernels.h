@@ -4,8 +4,15 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 namespace af {
+
+// integer tuning knob from the environment (read once by each caller)
+inline int env_int(const char* name, int dflt) {
+  const char* v = getenv(name);
+  return v && *v ? atoi(v) : dflt;
+}
 
 enum WFormat : int { W_I8 = 0, W_F16 = 1, W_I4G32 = 2 };
 enum Epilogue : int { EPI_F32 = 0, EPI_F16 = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
@@ -121,6 +128,10 @@ struct AttnDecodeArgs {
   // by the step's last kernel), so each CTA may read it and bulk-copy its first cache rows into
   // shared memory before the programmatic-launch wait, overlapping the qkv projection's tail
   int prefetch = 0;
+  // set by attn_decode_launch: cache rows staged per CTA with `prefetch`; 1 when the splits of a
+  // (sequence, kv head) run as one thread-block cluster and merge through its shared memory
+  int pre_rows = 0;
+  int cluster = 0;
 };
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st, bool pdl);
 size_t attn_decode_scratch_floats(int NB, int KV, int n_split, int G, int dh);

@@ -8,8 +8,10 @@
 //      (the reference's `Kin*inv + k*oh` write of llm.py:232, without touching the other M-1 slots);
 //   3. runs an online softmax over its keys (split-K / flash-decode), each key expanded as the
 //      reference's 0/1 GQA matmul does (f16(c * k), c = 1 without expansion, llm.py:205-211);
-//   4. writes (m, l, acc) partials to scratch; the last CTA of the (sequence, kv head) to finish
-//      (atomic ticket) merges the splits and writes the fp16 head outputs.
+//   4. merges the splits of its (sequence, kv head): with up to 16 splits they form one thread-block
+//      cluster and rank 0 reads every split's (m, l, acc) from the others' shared memory (no global
+//      round trips); otherwise each writes its partial to scratch and the last CTA to finish
+//      (atomic ticket) merges them. Either way the merge runs in split order, so it is deterministic.
 // Keys after `pos` carry the reference's additive -1e4 mask, whose exp underflows to exactly 0 in
 // fp32, so they are skipped. Probabilities stay fp32.
 //
@@ -23,7 +25,26 @@
 namespace af {
 
 constexpr int DEC_WARPS = 8;
-constexpr int DEC_PRE = 32;                    // cache rows per CTA staged in shared memory up front
+constexpr int DEC_PRE_MAX = 128;               // cache rows per CTA staged in shared memory up front (max)
+constexpr int DEC_CLUSTER_MAX = 16;            // splits merged inside one cluster
+
+AF_DEV uint32_t cluster_addr(const void* p, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"((uint32_t)__cvta_generic_to_shared(p)), "r"(rank));
+  return r;
+}
+
+AF_DEV float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// every thread of every CTA in the cluster; release/acquire orders the shared-memory writes before
+// it against the remote reads after it
+AF_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 
 AF_DEV void load_row_f16_sh(const __half* p, int lane, float* f, int epl, int lanes) {
   if (lane >= lanes) {
@@ -50,18 +71,21 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
   __shared__ float wacc[NW][G][DH];
   __shared__ int last_s;
   __shared__ uint64_t kv_bar;
-  extern __shared__ __align__(16) unsigned char kv_pre[];     // [K rows | V rows] x DEC_PRE x DH fp16
+  extern __shared__ __align__(16) unsigned char kv_pre[];     // [K rows | V rows] x pre_rows x DH fp16
 
-  // with `prefetch`, the first DEC_PRE cache rows of this CTA's key range (all before pos, so
-  // written in earlier steps) are requested before waiting for the qkv projection
+  // with `prefetch`, the first pre_rows cache rows of this CTA's key range (all before pos, so
+  // written in earlier steps) and the RoPE factors of row pos are requested before waiting for the
+  // qkv projection
   int n_pre = 0;
   int pos = 0;
+  float rc[EPL], rs[EPL];
   if (a.prefetch) {
     pos = __ldcg(a.pos + b);
     if (pos >= 0 && pos < a.M) {
+      load_rope_row<DH>(a.cos_t, a.sin_t, pos, lane, rc, rs);
       const int len0 = (pos + a.n_split) / a.n_split;
       const int j00 = split * len0;
-      n_pre = max(0, min(min(j00 + len0, pos), j00 + DEC_PRE) - j00);
+      n_pre = max(0, min(min(j00 + len0, pos), j00 + a.pre_rows) - j00);
       if (threadIdx.x == 0) {
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"((uint32_t)__cvta_generic_to_shared(&kv_bar)) : "memory");
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -74,7 +98,8 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
           asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                        ::"r"((uint32_t)__cvta_generic_to_shared(kv_pre)), "l"(kb0), "r"(bytes), "r"(bar) : "memory");
           asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                       ::"r"((uint32_t)__cvta_generic_to_shared(kv_pre + DEC_PRE * DH * 2)), "l"(vb0), "r"(bytes), "r"(bar)
+                       ::"r"((uint32_t)__cvta_generic_to_shared(kv_pre + (size_t)a.pre_rows * DH * 2)), "l"(vb0),
+                         "r"(bytes), "r"(bar)
                        : "memory");
         }
       }
@@ -83,9 +108,12 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
   pdl_wait();
   if (!a.prefetch) pos = __ldcg(a.pos + b);
   if (pos < 0 || pos >= a.M) {
+    // every CTA of a cluster holds the same sequence, so the whole cluster leaves here together
     if (threadIdx.x == 0 && split == 0 && kvh == 0) af_set_err(a.err, AF_DEV_BAD_POS);
     return;
   }
+  if (!a.prefetch) load_rope_row<DH>(a.cos_t, a.sin_t, pos, lane, rc, rs);
+  const bool rope = a.cos_t != nullptr;
   const int len = (pos + a.n_split) / a.n_split;      // ceil((pos + 1) / n_split)
   const int j0 = split * len;
   const int j1 = min(j0 + len, pos + 1);
@@ -98,7 +126,7 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
     float v[EPL];
 #pragma unroll
     for (int e = 0; e < EPL; ++e) v[e] = active ? __ldcg(qkv + (size_t)(kvh * G + g) * DH + lane * EPL + e) : 0.f;
-    norm_rope_head<DH>(v, lane, a.qn_g, a.qn_floor, a.cos_t, a.sin_t, pos);
+    norm_rope_head_pre<DH>(v, lane, a.qn_g, a.qn_floor, rope, rc, rs);
     if (active)
 #pragma unroll
       for (int e = 0; e < EPL; ++e) q_s[g][lane * EPL + e] = round_f16(v[e]);
@@ -110,7 +138,7 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
       k[e] = active ? __ldcg(qkv + (size_t)H * DH + (size_t)kvh * DH + lane * EPL + e) : 0.f;
       vv[e] = active ? __ldcg(qkv + (size_t)(H + KV) * DH + (size_t)kvh * DH + lane * EPL + e) : 0.f;
     }
-    norm_rope_head<DH>(k, lane, a.kn_g, a.kn_floor, a.cos_t, a.sin_t, pos);
+    norm_rope_head_pre<DH>(k, lane, a.kn_g, a.kn_floor, rope, rc, rs);
     const size_t slot = (((size_t)b * KV + kvh) * a.M + pos) * DH;
     if (active)
 #pragma unroll
@@ -160,7 +188,7 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
     }
   }
   const __half* kpre = reinterpret_cast<const __half*>(kv_pre);
-  const __half* vpre = kpre + DEC_PRE * DH;
+  const __half* vpre = kpre + (size_t)a.pre_rows * DH;
   for (int base = j0 + warp * PB; base < j1; base += NW * PB) {
     float kf[PB][EPL], vf[PB][EPL];
 #pragma unroll
@@ -241,6 +269,63 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
   }
   __syncthreads();
   const size_t pair = (size_t)b * KV + kvh;
+  __shared__ float fw[64][G];      // per split: m_s, then the weight exp(m_s - M)
+  __shared__ float lw[64][G];      // per split: l_s
+  __shared__ float den_s[G];
+  if (a.cluster) {
+    // ---- cluster merge: this CTA's (acc, m, l) stay in its shared memory; rank 0 (split 0) reads
+    // every rank's through the cluster window and writes the head outputs
+    __shared__ float c_acc[G][DH];
+    __shared__ float c_m[G], c_l[G];
+    for (int i = threadIdx.x; i < G * DH; i += blockDim.x) {
+      const int g = i / DH, dd = i - g * DH;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][g]);
+      float num = 0.f, den = 0.f;
+      if (M != -INFINITY) {
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+          const float f = expf(wm[w][g] - M);
+          num = fmaf(f, wacc[w][g][dd], num);
+          den = fmaf(f, wl[w][g], den);
+        }
+      }
+      c_acc[g][dd] = num;
+      if (dd == 0) { c_m[g] = M; c_l[g] = den; }
+    }
+    cluster_sync_all();
+    if (split == 0) {
+      for (int i = threadIdx.x; i < a.n_split * G; i += blockDim.x) {
+        const int sp = i / G, g = i - sp * G;
+        fw[sp][g] = ld_cluster_f32(cluster_addr(&c_m[g], sp));
+        lw[sp][g] = ld_cluster_f32(cluster_addr(&c_l[g], sp));
+      }
+      __syncthreads();
+      if (threadIdx.x < G) {
+        const int g = threadIdx.x;
+        float M = -INFINITY;
+        for (int sp = 0; sp < a.n_split; ++sp) M = fmaxf(M, fw[sp][g]);
+        float den = 0.f;
+        for (int sp = 0; sp < a.n_split; ++sp) {
+          const float f = fw[sp][g] == -INFINITY ? 0.f : expf(fw[sp][g] - M);
+          den = fmaf(f, lw[sp][g], den);
+          fw[sp][g] = f;
+        }
+        den_s[g] = den;
+      }
+      __syncthreads();
+      for (int i = threadIdx.x; i < G * DH; i += blockDim.x) {
+        const int g = i / DH, dd = i - g * DH;
+        float num = 0.f;
+#pragma unroll 4
+        for (int sp = 0; sp < a.n_split; ++sp) num = fmaf(fw[sp][g], ld_cluster_f32(cluster_addr(&c_acc[g][dd], sp)), num);
+        a.out[(size_t)b * a.ld_out + (size_t)(kvh * G + g) * DH + dd] = f2h(num / den_s[g]);
+      }
+    }
+    cluster_sync_all();          // no CTA leaves while rank 0 may still read its shared memory
+    return;
+  }
   float* part = a.part + (pair * a.n_split + split) * G * (DH + 2);
   for (int i = threadIdx.x; i < G * DH; i += blockDim.x) {
     const int g = i / DH, dd = i - g * DH;
@@ -272,9 +357,6 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
   __threadfence();
   // ---- merge the splits: (m_s, l_s) of every split land in shared memory in one parallel pass, the
   // per-head weights exp(m_s - M) are formed once, then each output issues its n_split loads together
-  __shared__ float fw[64][G];      // m_s, then the weight exp(m_s - M)
-  __shared__ float lw[64][G];      // l_s
-  __shared__ float den_s[G];
   const float* pp = a.part + pair * a.n_split * G * (DH + 2);
   for (int i = threadIdx.x; i < a.n_split * G; i += blockDim.x) {
     const int sp = i / G, g = i - sp * G;
@@ -314,20 +396,33 @@ static cudaError_t launch_decode(const AttnDecodeArgs& a, cudaStream_t st, bool 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.n_split, a.KV, a.NB);
   cfg.blockDim = dim3(DEC_WARPS * 32);
-  cfg.dynamicSmemBytes = a.prefetch ? 2 * DEC_PRE * DH * 2 : 0;
-  static bool smem_opt = false;                // static + dynamic shared memory may pass 48 KB (G = 8)
-  if (a.prefetch && !smem_opt) {
-    const cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<DH, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               2 * DEC_PRE * DH * 2);
+  cfg.dynamicSmemBytes = a.prefetch ? 2 * (size_t)a.pre_rows * DH * 2 : 0;
+  static bool attrs_set = false;               // static + dynamic shared memory may pass 48 KB
+  if (!attrs_set) {
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<DH, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         2 * DEC_PRE_MAX * DH * 2);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attn_decode_kernel<DH, G>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
-    smem_opt = true;
+    attrs_set = true;
   }
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (a.cluster) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = a.n_split;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, attn_decode_kernel<DH, G>, a);
 }
 
@@ -342,9 +437,16 @@ static cudaError_t decode_g(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) 
   }
 }
 
-cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
+cudaError_t attn_decode_launch(const AttnDecodeArgs& a0, cudaStream_t st, bool pdl) {
+  AttnDecodeArgs a = a0;
   if (a.KV <= 0 || a.H % a.KV || a.n_split < 1 || a.n_split > 64) return cudaErrorInvalidValue;
   if (a.n_split > 1 && (!a.part || !a.counters)) return cudaErrorInvalidValue;
+  // splits merge inside a cluster when they fit one (AF_ATTN_CLUSTER=0: always through scratch)
+  static const int use_cluster = env_int("AF_ATTN_CLUSTER", 1);
+  a.cluster = use_cluster && a.n_split > 1 && a.n_split <= DEC_CLUSTER_MAX ? 1 : 0;
+  // staged rows: a CTA's whole key range when it fits, else its first DEC_PRE_MAX rows
+  const int per_split = (a.M + a.n_split - 1) / a.n_split;
+  a.pre_rows = a.prefetch ? (per_split < DEC_PRE_MAX ? (per_split + 1) / 2 * 2 : DEC_PRE_MAX) : 0;
   switch (a.dh) {
     case 16: return decode_g<16>(a, st, pdl);
     case 32: return decode_g<32>(a, st, pdl);

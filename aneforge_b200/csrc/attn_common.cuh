@@ -13,10 +13,25 @@ struct HeadLayout {
   static constexpr int PARTNER = LANES / 2;            // xor distance of the rotate-half partner
 };
 
-// One head vector held as EPL contiguous elements per lane: optional RMSNorm, RoPE at row `p`.
+// This lane's RoPE factors of row `p` (cos, sin of its EPL elements); zeros without RoPE.
 template <int DH>
-AF_DEV void norm_rope_head(float (&v)[HeadLayout<DH>::EPL], int lane, const __half* ng, float nfloor,
-                           const __half* cos_t, const __half* sin_t, int p) {
+AF_DEV void load_rope_row(const __half* cos_t, const __half* sin_t, int p, int lane, float (&cs)[HeadLayout<DH>::EPL],
+                          float (&sn)[HeadLayout<DH>::EPL]) {
+  using HL = HeadLayout<DH>;
+#pragma unroll
+  for (int e = 0; e < HL::EPL; ++e) {
+    const int d = lane * HL::EPL + e;
+    const bool ok = cos_t && lane < HL::LANES;
+    cs[e] = ok ? h2f(cos_t[(size_t)p * DH + d]) : 0.f;
+    sn[e] = ok ? h2f(sin_t[(size_t)p * DH + d]) : 0.f;
+  }
+}
+
+// One head vector held as EPL contiguous elements per lane: optional RMSNorm, then RoPE with this
+// lane's factors (`rope` false: none).
+template <int DH>
+AF_DEV void norm_rope_head_pre(float (&v)[HeadLayout<DH>::EPL], int lane, const __half* ng, float nfloor, bool rope,
+                               const float (&cs)[HeadLayout<DH>::EPL], const float (&sn)[HeadLayout<DH>::EPL]) {
   using HL = HeadLayout<DH>;
   const bool active = lane < HL::LANES;
   if (ng) {
@@ -25,25 +40,33 @@ AF_DEV void norm_rope_head(float (&v)[HeadLayout<DH>::EPL], int lane, const __ha
     for (int e = 0; e < HL::EPL; ++e) ss = fmaf(v[e], v[e], ss);
     ss = active ? ss : 0.f;
     ss = warp_sum(ss);
-    const float sn = fmaxf(sqrtf(ss), nfloor);
+    const float sq = fmaxf(sqrtf(ss), nfloor);
 #pragma unroll
     for (int e = 0; e < HL::EPL; ++e) {
       const int d = lane * HL::EPL + e;
-      v[e] = active ? __fmul_rn(__fdiv_rn(v[e], sn), h2f(ng[d])) : 0.f;
+      v[e] = active ? __fmul_rn(__fdiv_rn(v[e], sq), h2f(ng[d])) : 0.f;
     }
   }
-  if (cos_t) {
+  if (rope) {
 #pragma unroll
     for (int e = 0; e < HL::EPL; ++e) {
       const float other = __shfl_xor_sync(0xffffffffu, v[e], HL::PARTNER);
       if (active) {
         const int d = lane * HL::EPL + e;
         const float rot = d < DH / 2 ? -other : other;
-        const float c = h2f(cos_t[(size_t)p * DH + d]), s = h2f(sin_t[(size_t)p * DH + d]);
-        v[e] = __fadd_rn(__fmul_rn(v[e], c), __fmul_rn(rot, s));
+        v[e] = __fadd_rn(__fmul_rn(v[e], cs[e]), __fmul_rn(rot, sn[e]));
       }
     }
   }
+}
+
+// One head vector held as EPL contiguous elements per lane: optional RMSNorm, RoPE at row `p`.
+template <int DH>
+AF_DEV void norm_rope_head(float (&v)[HeadLayout<DH>::EPL], int lane, const __half* ng, float nfloor,
+                           const __half* cos_t, const __half* sin_t, int p) {
+  float cs[HeadLayout<DH>::EPL], sn[HeadLayout<DH>::EPL];
+  load_rope_row<DH>(cos_t, sin_t, p, lane, cs, sn);
+  norm_rope_head_pre<DH>(v, lane, ng, nfloor, cos_t != nullptr, cs, sn);
 }
 
 template <int DH>

@@ -310,15 +310,35 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
 
 size_t gemm_tc_smem_bytes() { return (size_t)gm::STAGES * gm::STAGE + sizeof(GemmShared) + 1024; }
 
+// cuTensorMapEncodeTiled, resolved through the runtime at first use: the library does not link the
+// driver library, so it loads (and exports its symbols) on hosts without a GPU driver
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
 // The A operand's tensor map: fp16 [M rows][K] with row stride ldx, 64 x 128 boxes, 128-byte swizzle.
 static bool make_amap(const GemvTcArgs& a, CUtensorMap* map) {
+  const EncodeTiledFn enc = encode_tiled();
+  if (!enc) return false;
   const cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.NB};
   const cuuint64_t strides[1] = {(cuuint64_t)a.ldx * 2};
   const cuuint32_t box[2] = {(cuuint32_t)gm::BK, (cuuint32_t)gm::BM};
   const cuuint32_t estr[2] = {1, 1};
-  return cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(a.x), dims, strides, box,
-                                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(a.x), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // x [M][ldx] fp16 (M = a.NB rows), weights as for gemv_tc, y per epilogue (ldy); M >= 1, K % 32 == 0.

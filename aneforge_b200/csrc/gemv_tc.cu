@@ -318,11 +318,6 @@ static int sm_count() {
   return n;
 }
 
-static int env_int(const char* name, int dflt) {
-  const char* v = getenv(name);
-  return v && *v ? atoi(v) : dflt;
-}
-
 static size_t smem_bytes(int NB, bool i4) {
   // weight ring | barriers | x ring | odd-warp sums [4 row tiles][32 lanes][8 floats]
   return (size_t)tc::STAGES * (i4 ? tc::STAGE_BYTES4 : tc::STAGE_BYTES) + SH_BYTES +
