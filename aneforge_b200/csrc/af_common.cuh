@@ -24,6 +24,38 @@ AF_DEV void af_set_err(int* err, int code) {
 AF_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 AF_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// ---- thread-block clusters: another CTA's shared memory, and the cluster-wide barrier
+// address of `p` (this CTA's shared memory) in the shared window of cluster rank `rank`
+AF_DEV uint32_t cluster_addr(const void* p, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"((uint32_t)__cvta_generic_to_shared(p)), "r"(rank));
+  return r;
+}
+
+AF_DEV float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+AF_DEV float4 ld_cluster_v4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr)
+               : "memory");
+  return v;
+}
+
+// every thread of every CTA in the cluster, warps converged; release/acquire orders the
+// shared-memory writes before it against the remote reads after it
+AF_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// the same barrier for threads that may arrive from divergent code
+AF_DEV void cluster_sync_any() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
 // 16-byte streaming load that bypasses L1 (weights are read once per decode step).
 AF_DEV uint4 ldg_stream(const void* p) {
   uint4 r;

@@ -70,6 +70,7 @@ struct GemvTcArgs {
   int rw_e = 0;
   // set by the launcher
   int Np = 0, Kp = 0, S = 1, maxc = 1;
+  int csize = 0;               // > 1: thread-block clusters of csize CTAs split each row block's k range
   float* part = nullptr;
   int* counters = nullptr;
 };

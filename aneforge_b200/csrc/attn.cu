@@ -28,23 +28,6 @@ constexpr int DEC_WARPS = 8;
 constexpr int DEC_PRE_MAX = 128;               // cache rows per CTA staged in shared memory up front (max)
 constexpr int DEC_CLUSTER_MAX = 16;            // splits merged inside one cluster
 
-AF_DEV uint32_t cluster_addr(const void* p, int rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"((uint32_t)__cvta_generic_to_shared(p)), "r"(rank));
-  return r;
-}
-
-AF_DEV float ld_cluster_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
-}
-
-// every thread of every CTA in the cluster; release/acquire orders the shared-memory writes before
-// it against the remote reads after it
-AF_DEV void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
 
 AF_DEV void load_row_f16_sh(const __half* p, int lane, float* f, int epl, int lanes) {
   if (lane >= lanes) {

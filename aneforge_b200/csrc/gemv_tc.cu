@@ -113,7 +113,13 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
   const int RB = a.Np / 64;
   const long long U = (long long)RB * KT;
   const int G = gridDim.x, c = blockIdx.x;
-  const long long u0 = unit_begin(c, U, G), u1 = unit_begin(c + 1, U, G);
+  long long u0 = unit_begin(c, U, G), u1 = unit_begin(c + 1, U, G);
+  if (a.csize > 1) {
+    // one thread-block cluster per row block: rank r takes k tiles [r KT / d, (r + 1) KT / d)
+    const long long rb0 = c / a.csize, r = c % a.csize;
+    u0 = rb0 * KT + r * KT / a.csize;
+    u1 = rb0 * KT + (r + 1) * KT / a.csize;
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < tc::STAGES; ++s) {
@@ -131,7 +137,11 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
 
   if (warp == CW) {
     // -------------------------------------------------------------- producer (one thread)
-    if (lane != 0) return;
+    // (with clusters every thread still takes part in the two cluster barriers of the reduction)
+    if (lane != 0) {
+      if (a.csize > 1) { cluster_sync_any(); cluster_sync_any(); }
+      return;
+    }
     const char* W = reinterpret_cast<const char*>(a.w);
     int stage = 0, xs = 0;
     uint32_t phase = 0, xphase = 0;
@@ -190,6 +200,7 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
       if (--xs < 0) { xs = tc::XSLOTS - 1; xphase ^= 1; }
       mbar_wait(&sh->xfull[xs], xphase);
     }
+    if (a.csize > 1) { cluster_sync_any(); cluster_sync_any(); }
     return;
   }
 
@@ -261,6 +272,15 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
     if (kta == 0 && ktb == KT) {
       // this CTA owns the whole row block
       if (!par) epilogue<NT, EPI, I4>(a, acc, rt, g, t);
+    } else if (a.csize > 1) {
+      // cluster rank: the partial waits at the start of this CTA's weight ring (every stage has
+      // been consumed) until rank 0 reads it after the cluster barrier below
+      if (!par) {
+        float* slot = reinterpret_cast<float*>(ring) + (size_t)(rtw * 32 + lane) * (NT * 4);
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+          *reinterpret_cast<float4*>(slot + n * 4) = make_float4(acc[n][0], acc[n][1], acc[n][2], acc[n][3]);
+      }
     } else {
       // shared row block: partial to slot j, the last ticket holder reduces in CTA order
       const int cf = owner_of((long long)rb * KT, U, G), cl = owner_of((long long)rb * KT + KT - 1, U, G);
@@ -302,6 +322,29 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
     }
     consumer_sync_n<CW>();          // the reduction slots in shared memory are free for the next range
     u += ktb - kta;
+  }
+  if (a.csize > 1) {
+    // rank 0 sums the ranks' partials in rank order (deterministic) straight from their shared
+    // memory and runs the epilogue; no global scratch, fence or ticket
+    cluster_sync_any();
+    if (c % a.csize == 0 && !par) {
+      float acc[NT][4];
+#pragma unroll
+      for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[n][q] = 0.f;
+      const float* mine = reinterpret_cast<const float*>(ring) + (size_t)(rtw * 32 + lane) * (NT * 4);
+      for (int r = 0; r < a.csize; ++r) {
+        const uint32_t src = cluster_addr(mine, r);
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+          const float4 v = ld_cluster_v4(src + n * 16);
+          acc[n][0] += v.x; acc[n][1] += v.y; acc[n][2] += v.z; acc[n][3] += v.w;
+        }
+      }
+      epilogue<NT, EPI, I4>(a, acc, (c / a.csize) * tc::WARPS + rtw, g, t);
+    }
+    cluster_sync_any();             // no rank leaves while rank 0 may still read its shared memory
   }
 }
 
@@ -351,15 +394,30 @@ static int grid_any(int NB, int epi) {
   }
 }
 
-// Stream-K geometry on the host: grid G (all resident), units U = RB*KT, the largest number of CTAs
-// sharing one row block (`maxc`, partial slots per row block).
-static void plan_geometry(int N, int K, int NB, int epi, bool i4, int* G, int* maxc) {
-  // G = RB * d: each row block is split evenly between d CTAs, so a CTA's range lies inside one row
-  // block (at most one ticket per CTA, none when d == 1). d is the smallest split giving at least
-  // `min_ctas` CTAs (enough bytes in flight), bounded by the resident capacity and by KT.
-  static const int min_ctas = env_int("AF_TC_MIN_CTAS", 220);
+// Grid geometry on the host. While every row block fits the resident CTAs, each row block gets a
+// thread-block cluster of d CTAs (csize = d, d <= 8) splitting its k range evenly; d is the smallest
+// split giving at least `min_ctas` CTAs (enough bytes in flight), bounded by the resident capacity
+// and by KT, and the cluster's partials meet in rank 0's shared memory. Otherwise (more row blocks
+// than resident CTAs, or `allow_cluster` false) the grid is plain stream-K over U = RB*KT units
+// with per-row-block tickets; `maxc` is then the most CTAs sharing one row block (partial slots).
+static void plan_geometry(int N, int K, int NB, int epi, bool i4, int* G, int* maxc, int* csize,
+                          bool allow_cluster = true) {
+  static const int min_ctas = env_int("AF_TC_MIN_CTAS", 450);
+  static const int use_cluster = env_int("AF_TC_CLUSTER", 1);
   const long long RB = (N + 63) / 64, KT = (K + 31) / 32;
   const long long slots = i4 ? grid_any<true>(NB, epi) : grid_any<false>(NB, epi);
+  *csize = 0;
+  if (allow_cluster && use_cluster && RB <= slots) {
+    long long d = (min_ctas + RB - 1) / RB;
+    if (d > 8) d = 8;
+    if (d > KT) d = KT;
+    while (d > 1 && RB * d > slots) --d;
+    if (d < 1) d = 1;
+    *G = (int)(RB * d);
+    *csize = (int)d;
+    *maxc = 1;
+    return;
+  }
   long long d = (min_ctas + RB - 1) / RB;
   if (d < 1) d = 1;
   while (d > 1 && RB * d > slots) --d;
@@ -373,8 +431,8 @@ static void plan_geometry(int N, int K, int NB, int epi, bool i4, int* G, int* m
 }
 
 void gemv_tc_plan(int N, int K, int NB, int* S_out, int* nt_out) {
-  int G, maxc;
-  plan_geometry(N, K, NB > 16 ? 16 : NB, EPI_F32, false, &G, &maxc);
+  int G, maxc, cs;
+  plan_geometry(N, K, NB > 16 ? 16 : NB, EPI_F32, false, &G, &maxc, &cs, false);
   *S_out = maxc;
   *nt_out = NB <= 8 ? 1 : 2;
 }
@@ -382,9 +440,9 @@ void gemv_tc_plan(int N, int K, int NB, int* S_out, int* nt_out) {
 size_t gemv_tc_scratch_bytes(int N, int K, int NB) {
   // enough for either weight format and every epilogue (the grid may differ with shared memory)
   const int nb = NB > 16 ? 16 : NB;
-  int G = 0, maxc = 0, maxc4 = 0;
-  plan_geometry(N, K, nb, EPI_F32, false, &G, &maxc);
-  plan_geometry(N, K, nb, EPI_F32, true, &G, &maxc4);
+  int G = 0, maxc = 0, maxc4 = 0, cs = 0;
+  plan_geometry(N, K, nb, EPI_F32, false, &G, &maxc, &cs, false);
+  plan_geometry(N, K, nb, EPI_F32, true, &G, &maxc4, &cs, false);
   if (maxc4 > maxc) maxc = maxc4;
   const int NT = nb <= 8 ? 1 : 2;
   const size_t RB = (N + 63) / 64;
@@ -393,19 +451,31 @@ size_t gemv_tc_scratch_bytes(int N, int K, int NB) {
 
 template <int NT, int EPI, bool I4>
 static cudaError_t launch_tc(GemvTcArgs a, cudaStream_t st, bool pdl) {
-  int G = 0, maxc = 0;
-  plan_geometry(a.N, a.K, a.NB, EPI, I4, &G, &maxc);
+  int G = 0, maxc = 0, cs = 0;
+  plan_geometry(a.N, a.K, a.NB, EPI, I4, &G, &maxc, &cs);
   a.maxc = maxc;
+  a.csize = cs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G);
   cfg.blockDim = dim3((Cw<I4>::n + 1) * 32);
   cfg.dynamicSmemBytes = smem_bytes(a.NB, I4);
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (cs > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = cs;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, gemv_tc_kernel<NT, EPI, I4>, a);
 }
 
