@@ -133,6 +133,9 @@ struct AttnDecodeArgs {
   // (sequence, kv head) run as one thread-block cluster and merge through its shared memory
   int pre_rows = 0;
   int cluster = 0;
+  // fewest keys per split: at short positions only ceil((pos + 1) / min_keys) splits hold keys
+  // (0: the launcher's default)
+  int min_keys = 0;
 };
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st, bool pdl);
 size_t attn_decode_scratch_floats(int NB, int KV, int n_split, int G, int dh);

@@ -28,6 +28,13 @@ constexpr int DEC_WARPS = 8;
 constexpr int DEC_PRE_MAX = 128;               // cache rows per CTA staged in shared memory up front (max)
 constexpr int DEC_CLUSTER_MAX = 16;            // splits merged inside one cluster
 
+// Keys per split at position pos: the first ns splits share the pos + 1 keys evenly, where ns is
+// n_split but at most one split per `min_keys` keys (short prefixes leave the other splits idle).
+AF_DEV int split_len(int pos, int n_split, int min_keys) {
+  const int ns = min(n_split, max(1, (pos + min_keys) / min_keys));
+  return (pos + ns) / ns;                      // ceil((pos + 1) / ns)
+}
+
 
 AF_DEV void load_row_f16_sh(const __half* p, int lane, float* f, int epl, int lanes) {
   if (lane >= lanes) {
@@ -66,7 +73,7 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
     pos = __ldcg(a.pos + b);
     if (pos >= 0 && pos < a.M) {
       load_rope_row<DH>(a.cos_t, a.sin_t, pos, lane, rc, rs);
-      const int len0 = (pos + a.n_split) / a.n_split;
+      const int len0 = split_len(pos, a.n_split, a.min_keys);
       const int j00 = split * len0;
       n_pre = max(0, min(min(j00 + len0, pos), j00 + a.pre_rows) - j00);
       if (threadIdx.x == 0) {
@@ -97,7 +104,7 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
   }
   if (!a.prefetch) load_rope_row<DH>(a.cos_t, a.sin_t, pos, lane, rc, rs);
   const bool rope = a.cos_t != nullptr;
-  const int len = (pos + a.n_split) / a.n_split;      // ceil((pos + 1) / n_split)
+  const int len = split_len(pos, a.n_split, a.min_keys);
   const int j0 = split * len;
   const int j1 = min(j0 + len, pos + 1);
   const bool owns_pos = j0 <= pos && pos < j1;
@@ -427,8 +434,10 @@ cudaError_t attn_decode_launch(const AttnDecodeArgs& a0, cudaStream_t st, bool p
   // splits merge inside a cluster when they fit one (AF_ATTN_CLUSTER=0: always through scratch)
   static const int use_cluster = env_int("AF_ATTN_CLUSTER", 1);
   a.cluster = use_cluster && a.n_split > 1 && a.n_split <= DEC_CLUSTER_MAX ? 1 : 0;
+  static const int min_keys = env_int("AF_ATTN_MIN_KEYS", 64);
+  a.min_keys = a.min_keys > 0 ? a.min_keys : min_keys;
   // staged rows: a CTA's whole key range when it fits, else its first DEC_PRE_MAX rows
-  const int per_split = (a.M + a.n_split - 1) / a.n_split;
+  const int per_split = max((a.M + a.n_split - 1) / a.n_split, a.min_keys);
   a.pre_rows = a.prefetch ? (per_split < DEC_PRE_MAX ? (per_split + 1) / 2 * 2 : DEC_PRE_MAX) : 0;
   switch (a.dh) {
     case 16: return decode_g<16>(a, st, pdl);

@@ -383,6 +383,44 @@ static int grid_for(int NB) {
   return occ[NB] * sm_count();
 }
 
+// clusters of d CTAs that can be resident at once (0 if the query fails)
+template <int NT, int EPI, bool I4>
+static int clusters_for(int NB, int d) {
+  static int cache[17][9] = {};
+  if (!cache[NB][d]) {
+    grid_for<NT, EPI, I4>(NB);                  // sets the kernel's shared-memory limit
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(d * 64);
+    cfg.blockDim = dim3((Cw<I4>::n + 1) * 32);
+    cfg.dynamicSmemBytes = smem_bytes(NB, I4);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = d;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemv_tc_kernel<NT, EPI, I4>, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    cache[NB][d] = n > 0 ? n : -1;
+  }
+  return cache[NB][d] > 0 ? cache[NB][d] : 0;
+}
+
+template <bool I4>
+static int clusters_any(int NB, int epi, int d) {
+  const bool two = NB > 8;
+  switch (epi) {
+    case EPI_F32: return two ? clusters_for<2, EPI_F32, I4>(NB, d) : clusters_for<1, EPI_F32, I4>(NB, d);
+    case EPI_F16: return two ? clusters_for<2, EPI_F16, I4>(NB, d) : clusters_for<1, EPI_F16, I4>(NB, d);
+    case EPI_RESID: return two ? clusters_for<2, EPI_RESID, I4>(NB, d) : clusters_for<1, EPI_RESID, I4>(NB, d);
+    default: return two ? clusters_for<2, EPI_SWIGLU, I4>(NB, d) : clusters_for<1, EPI_SWIGLU, I4>(NB, d);
+  }
+}
+
 template <bool I4>
 static int grid_any(int NB, int epi) {
   const bool two = NB > 8;
@@ -396,8 +434,11 @@ static int grid_any(int NB, int epi) {
 
 // Grid geometry on the host. While every row block fits the resident CTAs, each row block gets a
 // thread-block cluster of d CTAs (csize = d, d <= 8) splitting its k range evenly; d is the smallest
-// split giving at least `min_ctas` CTAs (enough bytes in flight), bounded by the resident capacity
-// and by KT, and the cluster's partials meet in rank 0's shared memory. Otherwise (more row blocks
+// split giving at least `min_ctas` CTAs (enough bytes in flight), bounded by KT and by the resident
+// capacity: the row blocks' clusters must fit within `cfrac` percent of the clusters of d CTAs the
+// GPU can hold at once (clusters are placed whole within a GPC, and a programmatic launch starts
+// while the previous kernel still holds some of the SMs). The cluster's partials meet in rank 0's
+// shared memory. Otherwise (more row blocks
 // than resident CTAs, or `allow_cluster` false) the grid is plain stream-K over U = RB*KT units
 // with per-row-block tickets; `maxc` is then the most CTAs sharing one row block (partial slots).
 static void plan_geometry(int N, int K, int NB, int epi, bool i4, int* G, int* maxc, int* csize,
@@ -408,11 +449,21 @@ static void plan_geometry(int N, int K, int NB, int epi, bool i4, int* G, int* m
   const long long slots = i4 ? grid_any<true>(NB, epi) : grid_any<false>(NB, epi);
   *csize = 0;
   if (allow_cluster && use_cluster && RB <= slots) {
+    static const int cfrac = env_int("AF_TC_CFRAC", 100);
     long long d = (min_ctas + RB - 1) / RB;
     if (d > 8) d = 8;
     if (d > KT) d = KT;
     while (d > 1 && RB * d > slots) --d;
+    while (d > 1) {
+      const long long fit = i4 ? clusters_any<true>(NB, epi, (int)d) : clusters_any<false>(NB, epi, (int)d);
+      if (RB * 100 <= fit * cfrac) break;
+      --d;
+    }
     if (d < 1) d = 1;
+    if (env_int("AF_TC_DEBUG", 0))
+      fprintf(stderr, "[gemv_tc] N=%d K=%d NB=%d epi=%d i4=%d: RB=%lld slots=%lld d=%lld clusters(d)=%d\n", N, K, NB,
+              epi, (int)i4, RB, slots, d,
+              d > 1 ? (i4 ? clusters_any<true>(NB, epi, (int)d) : clusters_any<false>(NB, epi, (int)d)) : -1);
     *G = (int)(RB * d);
     *csize = (int)d;
     *maxc = 1;

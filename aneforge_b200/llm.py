@@ -338,13 +338,17 @@ class LlamaPrefill:
   def _ctx(self, NB, M):
     cfg, d = self.cfg, self._load()
     G = cfg.n_heads // cfg.n_kv_heads
-    # split-K over the cache: one split per 128 cache rows, but all CTAs in one wave (2 CTAs of 8
-    # warps per SM) and at most 64 splits. Up to 16 splits of a head run as one thread-block cluster
-    # and merge in its shared memory, so 16 is preferred while each split then holds at most 512
-    # keys; past that the splits merge through scratch (the last CTA of each head merges them).
+    # split-K over the cache: one split per 64 cache rows (the kernel also keeps >= 64 keys per
+    # busy split at shorter positions), but all CTAs in one wave (2 CTAs of 8 warps per SM) and at
+    # most 64 splits. Up to 16 splits of a head run as one thread-block cluster and merge in its
+    # shared memory; 8 (then 16) is preferred while each split then holds at most 512 keys (on B200
+    # clusters of 8 beat 16 at a few hundred keys); past that the splits merge through scratch (the
+    # last CTA of each head merges them).
     cap = max(1, (2 * 148) // max(1, cfg.n_kv_heads * NB))
-    nsplit = max(1, min(64, cap, -(-M // 128)))
-    if nsplit > 16 and -(-M // 16) <= 512:
+    nsplit = max(1, min(64, cap, -(-M // 64)))
+    if nsplit > 8 and -(-M // 8) <= 512:
+      nsplit = 8
+    elif nsplit > 16 and -(-M // 16) <= 512:
       nsplit = 16
     nsplit = int(os.environ.get("AF_ATTN_NSPLIT", nsplit))
     return {"NB": NB, "M": M, "nsplit": nsplit, "scale": d["scale"], "kvc": d["kvc"], "expand": G > 1 and d["kvc"] != 1.0,
