@@ -24,6 +24,19 @@ AF_DEV void af_set_err(int* err, int code) {
 AF_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 AF_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Issue this thread's share (pieces idx, idx + n, ...) of an L2 prefetch spec; fire and forget.
+template <class PF>
+AF_DEV void l2_prefetch(const PF& pf, unsigned idx, unsigned n) {
+  if (!pf.base) return;
+  for (size_t j = idx; j * pf.stride < pf.bytes; j += n) {
+    const size_t off = j * pf.stride;
+    const size_t left = pf.bytes - off;
+    const unsigned len = (unsigned)((left < pf.piece ? left : pf.piece) & ~(size_t)15);
+    if (len)
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(pf.base + off), "r"(len) : "memory");
+  }
+}
+
 // ---- thread-block clusters: another CTA's shared memory, and the cluster-wide barrier
 // address of `p` (this CTA's shared memory) in the shared window of cluster rank `rank`
 AF_DEV uint32_t cluster_addr(const void* p, int rank) {

@@ -15,6 +15,14 @@ inline int env_int(const char* name, int dflt) {
 }
 
 enum WFormat : int { W_I8 = 0, W_F16 = 1, W_I4G32 = 2 };
+
+// L2 prefetch of (part of) a later kernel's weights, issued by a kernel whose own phase leaves HBM
+// idle: pieces of `piece` bytes every `stride` bytes of [base, base + bytes), spread evenly over the
+// issuing threads, so every CTA of the consuming kernel finds the same share of its range in L2.
+struct L2Pf {
+  const char* base = nullptr;
+  size_t bytes = 0, piece = 0, stride = 0;
+};
 enum Epilogue : int { EPI_F32 = 0, EPI_F16 = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
 
 struct GemvArgs {
@@ -71,6 +79,7 @@ struct GemvTcArgs {
   // set by the launcher
   int Np = 0, Kp = 0, S = 1, maxc = 1;
   int csize = 0;               // > 1: thread-block clusters of csize CTAs split each row block's k range
+  L2Pf pf;                     // issued by each CTA once its own weight copies are all requested
   float* part = nullptr;
   int* counters = nullptr;
 };
@@ -79,6 +88,7 @@ cudaError_t gemv_tc_launch(const GemvTcArgs& a, cudaStream_t st, bool pdl);
 cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl);
 size_t gemv_tc_scratch_bytes(int N, int K, int NB);
 void gemv_tc_plan(int N, int K, int NB, int* S, int* NT);
+void gemv_tc_grid(int N, int K, int NB, int epi, bool i4, int* G, int* csize);
 cudaError_t pack_i8_tiles(const int8_t* src, int N, int K, uint8_t* dst, cudaStream_t st);
 size_t pack_i8_tiles_bytes(int N, int K);
 cudaError_t pack_i4_tiles(const uint8_t* src, const __half* scales, int N, int K, uint8_t* dst, cudaStream_t st);
@@ -96,7 +106,8 @@ cudaError_t quantize_g32_i4(const void* src, int src_f16, int N, int K, uint8_t*
 
 // out[b] = f16( x[b] / max(||x[b]||_2, floor) * g )  (the reference's RMSNorm lowering)
 cudaError_t rmsnorm_launch(const void* x, int x_f16, int ldx, const __half* g, float floor, __half* out,
-                           int ldo, int NB, int D, cudaStream_t st, bool pdl);
+                           int ldo, int NB, int D, cudaStream_t st, bool pdl,
+                           const L2Pf& pf = L2Pf());
 
 // h[b][:] = f32(table[tok[b]][:]); records AF_DEV_BAD_TOKEN and writes zeros on an out-of-range id.
 cudaError_t embed_launch(const int* tok, const __half* table, int vocab, float* h, int ldh, int NB, int D,
@@ -136,6 +147,7 @@ struct AttnDecodeArgs {
   // fewest keys per split: at short positions only ceil((pos + 1) / min_keys) splits hold keys
   // (0: the launcher's default)
   int min_keys = 0;
+  L2Pf pf;                     // issued at kernel start (the attention phase reads little from HBM)
 };
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st, bool pdl);
 size_t attn_decode_scratch_floats(int NB, int KV, int n_split, int G, int dh);

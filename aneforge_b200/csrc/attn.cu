@@ -27,6 +27,8 @@ namespace af {
 constexpr int DEC_WARPS = 8;
 constexpr int DEC_PRE_MAX = 128;               // cache rows per CTA staged in shared memory up front (max)
 constexpr int DEC_CLUSTER_MAX = 16;            // splits merged inside one cluster
+// keys per CTA for the three-phase path (its score table must fit the static shared memory)
+template <int G> struct DirectMax { static constexpr int n = G <= 4 ? 128 : 64; };
 
 // Keys per split at position pos: the first ns splits share the pos + 1 keys evenly, where ns is
 // n_split but at most one split per `min_keys` keys (short prefixes leave the other splits idle).
@@ -44,7 +46,7 @@ AF_DEV void load_row_f16_sh(const __half* p, int lane, float* f, int epl, int la
   for (int e = 0; e < epl; ++e) f[e] = __half2float(p[lane * epl + e]);
 }
 
-template <int DH, int G>
+template <int DH, int G, bool DIRECT>
 __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDecodeArgs a) {
   using HL = HeadLayout<DH>;
   using DB = DecodeBatch<DH, G>;
@@ -69,6 +71,9 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
   int n_pre = 0;
   int pos = 0;
   float rc[EPL], rs[EPL];
+  if (warp == 0)
+    l2_prefetch(a.pf, ((blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * 32 + lane,
+                gridDim.x * gridDim.y * gridDim.z * 32);
   if (a.prefetch) {
     pos = __ldcg(a.pos + b);
     if (pos >= 0 && pos < a.M) {
@@ -179,6 +184,97 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
   }
   const __half* kpre = reinterpret_cast<const __half*>(kv_pre);
   const __half* vpre = kpre + (size_t)a.pre_rows * DH;
+  // DIRECT (every split holds at most DirectMax keys): the split runs as three short phases
+  // instead of one long per-warp online softmax: scores (each warp a batch of PB keys: dot products
+  // + transpose-reduce) -> per-head max, exp and sum (one warp per head) -> P.V with the keys dealt
+  // over the warps, partial sums per warp. Rows come from the staged copy when it holds them.
+  constexpr bool direct = DIRECT;
+  const int n_keys = j1 > j0 ? j1 - j0 : 0;
+  __shared__ float s_s[G][DIRECT ? DirectMax<G>::n : 1];        // scores, then exp(s - m)
+  __shared__ float dm[G], dl[G];
+  if constexpr (DIRECT) {
+    for (int base = j0 + warp * PB; base < j1; base += NW * PB) {
+      float kf[PB][EPL];
+#pragma unroll
+      for (int p = 0; p < PB; ++p) {
+        const int j = base + p;
+        if (j < j1 && j != pos && j - j0 < n_pre) {
+          load_row_f16_sh(kpre + (size_t)(j - j0) * DH, lane, kf[p], EPL, HL::LANES);
+        } else if (j < j1 && j != pos) {
+          load_row_f16<DH>(kbase + (size_t)j * DH, lane, kf[p]);
+        } else {
+          const bool nw = j < j1 && active;
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) kf[p][e] = nw ? kn_s[lane * EPL + e] : 0.f;
+        }
+      }
+      if (a.expand) {
+#pragma unroll
+        for (int p = 0; p < PB; ++p)
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) kf[p][e] = round_f16(c * kf[p][e]);
+      }
+      float d[DB::NV];
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int p = 0; p < PB; ++p) {
+          float sdot = 0.f;
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) sdot = fmaf(qr[g][e], kf[p][e], sdot);
+          d[g * PB + p] = sdot;
+        }
+      const float sc = transpose_reduce<DB::NV>(d, lane) * a.scale;
+      if (rep0 && base + my_p < j1) s_s[my_g][base + my_p - j0] = sc;
+    }
+    __syncthreads();
+    if (warp < G) {
+      float mx = -INFINITY;
+      for (int k = lane; k < n_keys; k += 32) mx = fmaxf(mx, s_s[warp][k]);
+      mx = warp_max(mx);
+      float sum = 0.f;
+      for (int k = lane; k < n_keys; k += 32) {
+        const float pe = expf(s_s[warp][k] - mx);
+        s_s[warp][k] = pe;
+        sum += pe;
+      }
+      sum = warp_sum(sum);
+      if (lane == 0) { dm[warp] = mx; dl[warp] = sum; }
+    }
+    __syncthreads();
+    float pacc[G][EPL];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) pacc[g][e] = 0.f;
+    for (int k = warp; k < n_keys; k += NW) {
+      float vf[EPL];
+      if (j0 + k != pos && k < n_pre) {
+        load_row_f16_sh(vpre + (size_t)k * DH, lane, vf, EPL, HL::LANES);
+      } else if (j0 + k != pos) {
+        load_row_f16<DH>(vbase + (size_t)(j0 + k) * DH, lane, vf);
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) vf[e] = active ? vn_s[lane * EPL + e] : 0.f;
+      }
+      if (a.expand) {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) vf[e] = round_f16(c * vf[e]);
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float pg = s_s[g][k];
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) pacc[g][e] = fmaf(pg, vf[e], pacc[g][e]);
+      }
+    }
+    if (active)
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) wacc[warp][g][lane * EPL + e] = pacc[g][e];
+  }
+  if constexpr (!DIRECT)
   for (int base = j0 + warp * PB; base < j1; base += NW * PB) {
     float kf[PB][EPL], vf[PB][EPL];
 #pragma unroll
@@ -249,15 +345,39 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
       m[g] = mn;
     }
   }
-  // ---- merge the warps of this CTA
+  // ---- merge the warps of this CTA: (num, M, den) of head g, element dd
+  if constexpr (!DIRECT) {
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    if (lane == 0) { wm[warp][g] = m[g]; wl[warp][g] = l[g]; }
-    if (active)
+    for (int g = 0; g < G; ++g) {
+      if (lane == 0) { wm[warp][g] = m[g]; wl[warp][g] = l[g]; }
+      if (active)
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) wacc[warp][g][lane * EPL + e] = acc[g][e];
+        for (int e = 0; e < EPL; ++e) wacc[warp][g][lane * EPL + e] = acc[g][e];
+    }
   }
   __syncthreads();
+  auto merge_warps = [&](int g, int dd, float& num, float& M, float& den) {
+    num = 0.f;
+    if constexpr (DIRECT) {
+      M = dm[g];
+      den = dl[g];
+#pragma unroll
+      for (int w = 0; w < NW; ++w) num += wacc[w][g][dd];
+      return;
+    }
+    M = -INFINITY;
+    den = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][g]);
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        const float f = expf(wm[w][g] - M);
+        num = fmaf(f, wacc[w][g][dd], num);
+        den = fmaf(f, wl[w][g], den);
+      }
+    }
+  };
   const size_t pair = (size_t)b * KV + kvh;
   __shared__ float fw[64][G];      // per split: m_s, then the weight exp(m_s - M)
   __shared__ float lw[64][G];      // per split: l_s
@@ -269,18 +389,8 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
     __shared__ float c_m[G], c_l[G];
     for (int i = threadIdx.x; i < G * DH; i += blockDim.x) {
       const int g = i / DH, dd = i - g * DH;
-      float M = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][g]);
-      float num = 0.f, den = 0.f;
-      if (M != -INFINITY) {
-#pragma unroll
-        for (int w = 0; w < NW; ++w) {
-          const float f = expf(wm[w][g] - M);
-          num = fmaf(f, wacc[w][g][dd], num);
-          den = fmaf(f, wl[w][g], den);
-        }
-      }
+      float num, M, den;
+      merge_warps(g, dd, num, M, den);
       c_acc[g][dd] = num;
       if (dd == 0) { c_m[g] = M; c_l[g] = den; }
     }
@@ -319,18 +429,8 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
   float* part = a.part + (pair * a.n_split + split) * G * (DH + 2);
   for (int i = threadIdx.x; i < G * DH; i += blockDim.x) {
     const int g = i / DH, dd = i - g * DH;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][g]);
-    float num = 0.f, den = 0.f;
-    if (M != -INFINITY) {
-#pragma unroll
-      for (int w = 0; w < NW; ++w) {
-        const float f = expf(wm[w][g] - M);
-        num = fmaf(f, wacc[w][g][dd], num);
-        den = fmaf(f, wl[w][g], den);
-      }
-    }
+    float num, M, den;
+    merge_warps(g, dd, num, M, den);
     if (a.n_split == 1) {
       a.out[(size_t)b * a.ld_out + (size_t)(kvh * G + g) * DH + dd] = f2h(num / den);
     } else {
@@ -381,7 +481,7 @@ size_t attn_decode_scratch_floats(int NB, int KV, int n_split, int G, int dh) {
   return (size_t)NB * KV * n_split * G * (dh + 2);
 }
 
-template <int DH, int G>
+template <int DH, int G, bool DIRECT>
 static cudaError_t launch_decode(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.n_split, a.KV, a.NB);
@@ -389,10 +489,10 @@ static cudaError_t launch_decode(const AttnDecodeArgs& a, cudaStream_t st, bool 
   cfg.dynamicSmemBytes = a.prefetch ? 2 * (size_t)a.pre_rows * DH * 2 : 0;
   static bool attrs_set = false;               // static + dynamic shared memory may pass 48 KB
   if (!attrs_set) {
-    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<DH, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<DH, G, DIRECT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          2 * DEC_PRE_MAX * DH * 2);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(attn_decode_kernel<DH, G>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      e = cudaFuncSetAttribute(attn_decode_kernel<DH, G, DIRECT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
     attrs_set = true;
   }
@@ -413,16 +513,26 @@ static cudaError_t launch_decode(const AttnDecodeArgs& a, cudaStream_t st, bool 
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, attn_decode_kernel<DH, G>, a);
+  return cudaLaunchKernelEx(&cfg, attn_decode_kernel<DH, G, DIRECT>, a);
+}
+
+// the three-phase kernel when no split can hold more than DirectMax keys: at most
+// max(min_keys, ceil(M / n_split)) keys per split
+template <int DH, int G>
+static cudaError_t decode_d(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
+  static const int use_direct = env_int("AF_ATTN_DIRECT", 1);
+  const int most = max((a.M + a.n_split - 1) / a.n_split, a.min_keys);
+  if (use_direct && most <= DirectMax<G>::n) return launch_decode<DH, G, true>(a, st, pdl);
+  return launch_decode<DH, G, false>(a, st, pdl);
 }
 
 template <int DH>
 static cudaError_t decode_g(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
   switch (a.H / a.KV) {
-    case 1: return launch_decode<DH, 1>(a, st, pdl);
-    case 2: return launch_decode<DH, 2>(a, st, pdl);
-    case 4: return launch_decode<DH, 4>(a, st, pdl);
-    case 8: return launch_decode<DH, 8>(a, st, pdl);
+    case 1: return decode_d<DH, 1>(a, st, pdl);
+    case 2: return decode_d<DH, 2>(a, st, pdl);
+    case 4: return decode_d<DH, 4>(a, st, pdl);
+    case 8: return decode_d<DH, 8>(a, st, pdl);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -96,6 +96,13 @@ int af_pack_i8_tiles(const int8_t* codes, int n, int k, uint8_t* tiles, void* st
 size_t af_pack_i8_tiles_bytes(int n, int k) { return af::pack_i8_tiles_bytes(n, k); }
 
 size_t af_gemv_tc_scratch_bytes(int n, int k, int nb) { return af::gemv_tc_scratch_bytes(n, k, nb); }
+int af_gemv_tc_grid(int n, int k, int nb, int epi, int wf, int* grid, int* csize) {
+  if (!grid || !csize || n <= 0 || k <= 0 || nb < 1 || (wf != af::W_I8 && wf != af::W_I4G32) || epi < 0 ||
+      epi > af::EPI_SWIGLU)
+    return -1;
+  af::gemv_tc_grid(n, k, nb > 16 ? 16 : nb, epi, wf == af::W_I4G32, grid, csize);
+  return 0;
+}
 
 int af_gemv_tc(int epi, const uint16_t* x, int ldx, const void* tiles, const uint16_t* scales, const uint16_t* bias,
                void* y, int ldy, int nb, int n, int k, void* scratch, size_t scratch_bytes, void* stream) {

@@ -190,6 +190,7 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
     }
     if (!waited) pdl_wait();
     if (!ok) af_set_err(a.err, AF_DEV_WAIT_TIMEOUT);
+    l2_prefetch(a.pf, c, G);        // this CTA's share of a later kernel's weights
     // shared memory must outlive every copy this thread issued: wait (bounded) for the last use of
     // each weight stage and x slot to land before the thread exits
     for (int i = 0; i < in_flight; ++i) {
@@ -282,41 +283,57 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
           *reinterpret_cast<float4*>(slot + n * 4) = make_float4(acc[n][0], acc[n][1], acc[n][2], acc[n][3]);
       }
     } else {
-      // shared row block: partial to slot j, the last ticket holder reduces in CTA order
+      // stream-K row block shared by CTAs cf..cl: the owner cf holds its first k tiles and reaches
+      // them last (they end its range), the others start with theirs. Those publish a partial in
+      // slot j = c - cf and count it on the row block's counter; the owner waits (bounded) until
+      // all nc - 1 are in and sums them in CTA order onto its own, so the result is deterministic
       const int cf = owner_of((long long)rb * KT, U, G), cl = owner_of((long long)rb * KT + KT - 1, U, G);
       const int nc = cl - cf + 1, j = c - cf;
       constexpr int NBP = NT * 8;
-      float* slot = a.part + (((size_t)rb * a.maxc + j) * 64) * NBP;
       const int r0 = rtw * 16 + g, r1 = r0 + 8;
-      if (!par) {
+      if (j > 0) {
+        float* slot = a.part + (((size_t)rb * a.maxc + j) * 64) * NBP;
+        if (!par) {
 #pragma unroll
-        for (int n = 0; n < NT; ++n) {
-          const int c0 = n * 8 + 2 * t;
-          if (c0 >= a.NB) continue;
-          __stcg(reinterpret_cast<float2*>(slot + (size_t)r0 * NBP + c0), make_float2(acc[n][0], acc[n][1]));
-          __stcg(reinterpret_cast<float2*>(slot + (size_t)r1 * NBP + c0), make_float2(acc[n][2], acc[n][3]));
-        }
-        __threadfence();
-      }
-      consumer_sync_n<CW>();
-      if (threadIdx.x == 0) sh->ticket = atomicAdd(a.counters + rb, 1) == nc - 1;
-      consumer_sync_n<CW>();
-      if (sh->ticket && !par) {
-        __threadfence();
-#pragma unroll
-        for (int n = 0; n < NT; ++n) {
-          const int c0 = n * 8 + 2 * t;
-          if (c0 >= a.NB) continue;
-          float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-          for (int jj = 0; jj < nc; ++jj) {
-            const float* sp = a.part + (((size_t)rb * a.maxc + jj) * 64) * NBP;
-            const float2 p = __ldcg(reinterpret_cast<const float2*>(sp + (size_t)r0 * NBP + c0));
-            const float2 q = __ldcg(reinterpret_cast<const float2*>(sp + (size_t)r1 * NBP + c0));
-            s0 += p.x; s1 += p.y; s2 += q.x; s3 += q.y;
+          for (int n = 0; n < NT; ++n) {
+            const int c0 = n * 8 + 2 * t;
+            if (c0 >= a.NB) continue;
+            __stcg(reinterpret_cast<float2*>(slot + (size_t)r0 * NBP + c0), make_float2(acc[n][0], acc[n][1]));
+            __stcg(reinterpret_cast<float2*>(slot + (size_t)r1 * NBP + c0), make_float2(acc[n][2], acc[n][3]));
           }
-          acc[n][0] = s0; acc[n][1] = s1; acc[n][2] = s2; acc[n][3] = s3;
+          __threadfence();
         }
-        epilogue<NT, EPI, I4>(a, acc, rt, g, t);
+        consumer_sync_n<CW>();
+        if (threadIdx.x == 0) atomicAdd(a.counters + rb, 1);
+      } else {
+        if (threadIdx.x == 0) {
+          bool in = false;
+          for (long long i = 0; i < tc::WAIT_LIMIT && !in; ++i) {
+            int v;
+            asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(a.counters + rb) : "memory");
+            in = v >= nc - 1;
+          }
+          if (!in) {
+            af_set_err(a.err, AF_DEV_WAIT_TIMEOUT);
+            sh->cabort = 1;
+          }
+        }
+        consumer_sync_n<CW>();
+        if (!par) {
+          __threadfence();
+#pragma unroll
+          for (int n = 0; n < NT; ++n) {
+            const int c0 = n * 8 + 2 * t;
+            if (c0 >= a.NB) continue;
+            for (int jj = 1; jj < nc; ++jj) {
+              const float* sp = a.part + (((size_t)rb * a.maxc + jj) * 64) * NBP;
+              const float2 p = __ldcg(reinterpret_cast<const float2*>(sp + (size_t)r0 * NBP + c0));
+              const float2 q = __ldcg(reinterpret_cast<const float2*>(sp + (size_t)r1 * NBP + c0));
+              acc[n][0] += p.x; acc[n][1] += p.y; acc[n][2] += q.x; acc[n][3] += q.y;
+            }
+          }
+          epilogue<NT, EPI, I4>(a, acc, rt, g, t);
+        }
         if (threadIdx.x == 0) a.counters[rb] = 0;
       }
     }
@@ -350,6 +367,27 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
 
 // ------------------------------------------------------------------------------------ host side
 
+// Shared memory to request so that at most k CTAs fit on one SM: the grid is sized for k per SM,
+// and a programmatic launch places CTAs on whichever SMs free up first, so without the cap an SM
+// that frees early takes one CTA more than the others and finishes last.
+static size_t smem_for_ctas_per_sm(size_t need, int k) {
+  static int per_sm = 0, reserved = 0, per_block = 0;
+  if (!per_sm) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+    cudaDeviceGetAttribute(&per_block, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (per_sm <= 0) per_sm = 1;
+  }
+  static const int cap = env_int("AF_TC_OCC_CAP", 0);     // measured slower on B200: off by default
+  if (!cap || k < 1 || per_sm <= 1) return need;
+  const long long floor_k = (long long)per_sm / (k + 1) - reserved + 16;   // k + 1 CTAs no longer fit
+  size_t want = floor_k > (long long)need ? (size_t)((floor_k + 127) / 128 * 128) : need;
+  if (per_block > 0 && want > (size_t)per_block) want = need;
+  return want;
+}
+
 static int sm_count() {
   static int n = 0;
   if (!n) {
@@ -371,8 +409,12 @@ template <int NT, int EPI, bool I4>
 static int grid_for(int NB) {
   static int occ[17] = {};
   if (!occ[NB]) {
+    int dev = 0, optin = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaFuncSetAttribute(gemv_tc_kernel<NT, EPI, I4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem_bytes(16, I4));
+                         optin > (int)smem_bytes(16, I4) ? optin : (int)smem_bytes(16, I4));
+    cudaFuncSetAttribute(gemv_tc_kernel<NT, EPI, I4>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     int o = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, gemv_tc_kernel<NT, EPI, I4>, (Cw<I4>::n + 1) * 32,
                                                       smem_bytes(NB, I4)) != cudaSuccess || o < 1)
@@ -386,7 +428,7 @@ static int grid_for(int NB) {
 // clusters of d CTAs that can be resident at once (0 if the query fails)
 template <int NT, int EPI, bool I4>
 static int clusters_for(int NB, int d) {
-  static int cache[17][9] = {};
+  static int cache[17][17] = {};
   if (!cache[NB][d]) {
     grid_for<NT, EPI, I4>(NB);                  // sets the kernel's shared-memory limit
     cudaLaunchConfig_t cfg = {};
@@ -432,53 +474,66 @@ static int grid_any(int NB, int epi) {
   }
 }
 
-// Grid geometry on the host. While every row block fits the resident CTAs, each row block gets a
-// thread-block cluster of d CTAs (csize = d, d <= 8) splitting its k range evenly; d is the smallest
-// split giving at least `min_ctas` CTAs (enough bytes in flight), bounded by KT and by the resident
-// capacity: the row blocks' clusters must fit within `cfrac` percent of the clusters of d CTAs the
-// GPU can hold at once (clusters are placed whole within a GPC, and a programmatic launch starts
-// while the previous kernel still holds some of the SMs). The cluster's partials meet in rank 0's
-// shared memory. Otherwise (more row blocks
-// than resident CTAs, or `allow_cluster` false) the grid is plain stream-K over U = RB*KT units
-// with per-row-block tickets; `maxc` is then the most CTAs sharing one row block (partial slots).
+// Grid geometry on the host. The bytes a CTA streams should be the same on every SM: a CTA is bound
+// to one SM, and an SM hosting one more CTA than the others finishes last (at 4 CTAs against 3,
+// a third later). Two layouts:
+//  * more row blocks than resident CTAs: stream-K over all G = resident CTAs, U = RB * KT units split
+//    evenly, so every CTA range spans at least one row block and a row block is shared by at most
+//    two CTAs (owner fixup in the kernel);
+//  * otherwise thread-block clusters: each row block gets a cluster of d CTAs (csize = d <= 16)
+//    splitting its k range, the partials meeting in rank 0's shared memory. d maximises
+//    balance * fill, balance = G / (SMs * ceil(G / SMs)) (how evenly the G = RB * d CTAs spread over
+//    the SMs), fill = min(1, G / min_ctas) (enough bytes in flight), with G within the resident
+//    capacity and the row blocks' clusters within `cfrac` percent of the clusters of d CTAs the GPU
+//    holds at once (a cluster is placed whole within a GPC).
+// `allow_cluster` false (scratch sizing, the megakernel's plan) always describes the stream-K
+// layout at the resident capacity; `maxc` is then the most CTAs sharing one row block.
 static void plan_geometry(int N, int K, int NB, int epi, bool i4, int* G, int* maxc, int* csize,
                           bool allow_cluster = true) {
   static const int min_ctas = env_int("AF_TC_MIN_CTAS", 450);
   static const int use_cluster = env_int("AF_TC_CLUSTER", 1);
+  static const int cfrac = env_int("AF_TC_CFRAC", 100);
+  static const int max_d = env_int("AF_TC_MAX_CLUSTER", 16);
   const long long RB = (N + 63) / 64, KT = (K + 31) / 32;
   const long long slots = i4 ? grid_any<true>(NB, epi) : grid_any<false>(NB, epi);
+  const long long sms = sm_count(), occ = slots / sms > 0 ? slots / sms : 1;
   *csize = 0;
+  *maxc = 1;
   if (allow_cluster && use_cluster && RB <= slots) {
-    static const int cfrac = env_int("AF_TC_CFRAC", 100);
-    long long d = (min_ctas + RB - 1) / RB;
-    if (d > 8) d = 8;
-    if (d > KT) d = KT;
-    while (d > 1 && RB * d > slots) --d;
-    while (d > 1) {
-      const long long fit = i4 ? clusters_any<true>(NB, epi, (int)d) : clusters_any<false>(NB, epi, (int)d);
-      if (RB * 100 <= fit * cfrac) break;
-      --d;
+    long long best_d = 1;
+    double best = -1.0;
+    for (long long d = 1; d <= max_d && d <= KT; ++d) {
+      const long long g = RB * d;
+      if (g > slots) break;
+      if (d > 1) {
+        const long long fit = i4 ? clusters_any<true>(NB, epi, (int)d) : clusters_any<false>(NB, epi, (int)d);
+        if (RB * 100 > fit * cfrac) continue;
+      }
+      const double balance = (double)g / (double)(sms * ((g + sms - 1) / sms));
+      const double fill = g >= min_ctas ? 1.0 : (double)g / min_ctas;
+      const double score = balance * fill;
+      if (score > best + 1e-9) { best = score; best_d = d; }
     }
-    if (d < 1) d = 1;
     if (env_int("AF_TC_DEBUG", 0))
-      fprintf(stderr, "[gemv_tc] N=%d K=%d NB=%d epi=%d i4=%d: RB=%lld slots=%lld d=%lld clusters(d)=%d\n", N, K, NB,
-              epi, (int)i4, RB, slots, d,
-              d > 1 ? (i4 ? clusters_any<true>(NB, epi, (int)d) : clusters_any<false>(NB, epi, (int)d)) : -1);
-    *G = (int)(RB * d);
-    *csize = (int)d;
-    *maxc = 1;
+      fprintf(stderr, "[gemv_tc] N=%d K=%d NB=%d epi=%d i4=%d: RB=%lld slots=%lld cluster d=%lld (score %.3f)\n", N, K,
+              NB, epi, (int)i4, RB, slots, best_d, best);
+    *G = (int)(RB * best_d);
+    *csize = (int)best_d;
     return;
   }
-  long long d = (min_ctas + RB - 1) / RB;
-  if (d < 1) d = 1;
-  while (d > 1 && RB * d > slots) --d;
-  if (d > KT) d = KT;
-  long long g = RB * d;
-  if (g > slots) g = slots;                 // more row blocks than resident CTAs: plain stream-K
+  long long g = occ * sms;
+  if (g > RB * KT) g = RB * KT;
   *G = (int)g;
   const long long U = RB * KT;
   const long long per = U / g;
   *maxc = (int)((KT + per - 1) / (per > 0 ? per : 1)) + 1;
+  if (allow_cluster && env_int("AF_TC_DEBUG", 0))
+    fprintf(stderr, "[gemv_tc] N=%d K=%d NB=%d epi=%d i4=%d: RB=%lld stream-K G=%lld\n", N, K, NB, epi, (int)i4, RB, g);
+}
+
+void gemv_tc_grid(int N, int K, int NB, int epi, bool i4, int* G, int* csize) {
+  int maxc = 0;
+  plan_geometry(N, K, NB, epi, i4, G, &maxc, csize);
 }
 
 void gemv_tc_plan(int N, int K, int NB, int* S_out, int* nt_out) {
@@ -509,7 +564,7 @@ static cudaError_t launch_tc(GemvTcArgs a, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G);
   cfg.blockDim = dim3((Cw<I4>::n + 1) * 32);
-  cfg.dynamicSmemBytes = smem_bytes(a.NB, I4);
+  cfg.dynamicSmemBytes = smem_for_ctas_per_sm(smem_bytes(a.NB, I4), (G + sm_count() - 1) / sm_count());
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   int na = 0;

@@ -26,10 +26,11 @@ static cudaLaunchConfig_t mkcfg(dim3 g, dim3 b, size_t smem, cudaStream_t st, bo
 // scaling (one read of x). Vector path: D % 4 == 0 (fp32) or D % 8 == 0 (fp16) with aligned rows.
 template <bool XF16, int PER>
 __global__ void __launch_bounds__(1024) rmsnorm_kernel(const void* x, int ldx, const __half* g, float floor,
-                                                       __half* out, int ldo, int D) {
+                                                       __half* out, int ldo, int D, L2Pf pf) {
   const int b = blockIdx.x;
   constexpr int VW = XF16 ? 8 : 4;                   // elements per vector load
   float v[PER * VW];
+  l2_prefetch(pf, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
   pdl_wait();
   const int nvec = D / VW;
   float ss = 0.f;
@@ -141,7 +142,7 @@ __global__ void __launch_bounds__(256) cast_kernel(const void* src, void* dst, s
 
 
 cudaError_t rmsnorm_launch(const void* x, int x_f16, int ldx, const __half* g, float floor, __half* out, int ldo,
-                           int NB, int D, cudaStream_t st, bool pdl) {
+                           int NB, int D, cudaStream_t st, bool pdl, const L2Pf& pf) {
   cudaLaunchAttribute attr[1];
   const int VW = x_f16 ? 8 : 4;
   const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0) &&
@@ -151,7 +152,7 @@ cudaError_t rmsnorm_launch(const void* x, int x_f16, int ldx, const __half* g, f
   if (aligned && per <= 8) {
     const int threads = nvec < 1024 ? ((nvec + 31) / 32) * 32 : 1024;
     cudaLaunchConfig_t cfg = mkcfg(dim3(NB), dim3(threads), 0, st, pdl, attr);
-#define AF_RMS(XF, P) if (per <= P) return cudaLaunchKernelEx(&cfg, rmsnorm_kernel<XF, P>, x, ldx, g, floor, out, ldo, D);
+#define AF_RMS(XF, P) if (per <= P) return cudaLaunchKernelEx(&cfg, rmsnorm_kernel<XF, P>, x, ldx, g, floor, out, ldo, D, pf);
     if (x_f16) { AF_RMS(true, 1) AF_RMS(true, 2) AF_RMS(true, 4) AF_RMS(true, 8) }
     else { AF_RMS(false, 1) AF_RMS(false, 2) AF_RMS(false, 4) AF_RMS(false, 8) }
 #undef AF_RMS

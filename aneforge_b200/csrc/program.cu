@@ -174,6 +174,28 @@ struct OpCtx {
   }
 };
 
+// Optional L2 prefetch keys of an op: pf=<buffer> (a later kernel's weights), pfs=<bytes of that
+// region>, pfn=<bytes to prefetch>, pfg=<CTAs of the kernel that reads them>. The region splits
+// into pfg equal pieces (that kernel's CTAs read consecutive equal ranges in order) and the first
+// pfn/pfs of each piece is fetched, so every CTA starts on lines already in L2.
+static L2Pf parse_pf(OpCtx& c) {
+  L2Pf f;
+  const long long total = c.i("pfs", 0), want = c.i("pfn", 0), parts = c.i("pfg", 1);
+  if (total <= 0 || want <= 0 || parts < 1 || !c.has("pf")) return f;
+  f.base = static_cast<const char*>(c.ptr("pf", (size_t)total));
+  if (!f.base) return L2Pf();
+  f.bytes = (size_t)total;
+  f.stride = ((size_t)total / (size_t)parts) & ~(size_t)15;
+  if (f.stride < 16) return L2Pf();
+  const double frac = want < total ? (double)want / (double)total : 1.0;
+  f.piece = ((size_t)(frac * (double)f.stride) + 15) & ~(size_t)15;
+  if (f.piece > f.stride) f.piece = f.stride;
+  if (f.piece == f.stride) {                     // the whole region: 16 KB pieces back to back
+    f.piece = f.stride = 16384;
+  }
+  return f;
+}
+
 // Resolve a decode_mk op: the step-wide arguments, one MkLayer per layer, the launch plan.
 static bool mk_resolve(Program& p, const Op& op, bool dry, MkArgs& a, std::vector<MkLayer>& layers, MkPlan& plan,
                        std::string& why) {
@@ -292,7 +314,9 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     __half* out = (__half*)c.ptr("out", 2 * ((size_t)(nb - 1) * ldo + d));
     const float floor = (float)c.f("floor");
     if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
-    if (!dry) e = rmsnorm_launch(x, xf16, ldx, g, floor, out, ldo, nb, d, st, pdl);
+    const L2Pf pf = parse_pf(c);
+    if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+    if (!dry) e = rmsnorm_launch(x, xf16, ldx, g, floor, out, ldo, nb, d, st, pdl, pf);
   } else if (op.kind == "gemv" && c.has("wf") && (op.kv.at("wf") == "i8t" || op.kv.at("wf") == "i4t")) {
     GemvTcArgs a;
     const bool i4 = op.kv.at("wf") == "i4t";
@@ -328,6 +352,7 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     const bool want_gemm = c.i("gemm", 0) != 0;
     a.scratch_bytes = want_gemm ? 0 : gemv_tc_scratch_bytes(a.N, a.K, a.NB);
     if (a.scratch_bytes) a.scratch = c.ptr("scr", a.scratch_bytes);
+    a.pf = parse_pf(c);
     a.err = p.d_err;
     if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
     // prompt-sized row counts (prefill) run as a tensor-core GEMM unless the op asks for the GEMV
@@ -397,6 +422,7 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     a.kv_c = (float)c.f("kvc", 1.0);
     a.expand = c.i("expand", 0);
     a.prefetch = (int)c.i("prefetch", 0);
+    a.pf = parse_pf(c);
     a.err = p.d_err;
     if ((a.cos_t == nullptr) != (a.sin_t == nullptr)) c.err = "cos/sin must both be given";
     if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }

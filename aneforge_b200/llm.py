@@ -198,6 +198,46 @@ DECODE_MLPS = {"swiglu": emit_swiglu}
 _DECODE_CTX = ("pos",)
 
 
+def plan_l2_prefetch(pb, budget=None, mode=None):
+  """Attach L2 prefetch keys to a decode plan: each tensor-core GEMV's weights are (partly) fetched
+  into L2 by the kernel that runs before it - the previous GEMV once its own weight copies are all
+  requested, or an attention / norm kernel at its start - so HBM keeps streaming through the
+  dependent-launch gaps (kernel drain, attention, norms). Up to `budget` bytes per target (env
+  AF_L2_PF_MB, default 0: off), the first share of each of the target's CTA ranges. Off by default:
+  on B200 bulk prefetches queue on the issuing SM's copy engine, so beyond a few MB they slow the
+  issuing kernel more than they save.
+  mode "first": only the earliest kernel before the target issues; "all": every kernel in between."""
+  import ctypes
+  if budget is None:
+    budget = int(float(os.environ.get("AF_L2_PF_MB", "0")) * (1 << 20))
+  mode = mode or os.environ.get("AF_L2_PF_MODE", "first")
+  if budget <= 0:
+    return
+  lib = R.load_library()
+  ops = pb.ops
+
+  def tc_gemv(kind, kv):
+    return (kind == "gemv" and kv.get("wf") in ("i8t", "i4t") and "experts" not in kv and not kv.get("gemm"))
+
+  epis = {"f32": 0, "f16": 1, "resid": 2, "swiglu": 3}
+  issued = set()
+  for i, (kind, kv) in enumerate(ops):
+    if not (tc_gemv(kind, kv) or kind in ("attn_decode", "rmsnorm")):
+      continue
+    j = next((j for j in range(i + 1, len(ops)) if tc_gemv(*ops[j])), None)
+    if j is None or (mode == "first" and j in issued):
+      continue
+    t = ops[j][1]
+    total = pb.bufs[t["w"]].nbytes
+    grid, cs = ctypes.c_int(), ctypes.c_int()
+    rc = lib.af_gemv_tc_grid(int(t["n"]), int(t["k"]), int(t["nb"]), epis[t["epi"]], 2 if t["wf"] == "i4t" else 0,
+                             ctypes.byref(grid), ctypes.byref(cs))
+    if rc != 0:
+      continue
+    kv.update(pf=t["w"], pfs=total, pfn=min(total, budget), pfg=max(1, grid.value))
+    issued.add(j)
+
+
 # ------------------------------------------------------------------------------ the runner
 
 class LlamaPrefill:
@@ -435,6 +475,7 @@ class LlamaPrefill:
             ami="am.idx", amc="am.cnt", tok=at("tp.cand", 4 * NB), val="tp.cand", ibase=self.shard.vocab[0])
       pb.op("allgather", src="tp.cand", dst="tp.gath", n=2 * NB, ranks=self.tp.world)
       pb.op("tp_argmax", src="tp.gath", ranks=self.tp.world, nb=NB, tok="tok_out", pos="pos", hist="hist", histld=M)
+    plan_l2_prefetch(pb)
     ins = {"tok": (NB,), "pos": (NB,)}
     for li in range(cfg.n_layers):
       ins[f"L{li}.K"] = (NB, KV, M, dh); ins[f"L{li}.V"] = (NB, KV, M, dh)

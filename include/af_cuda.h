@@ -143,6 +143,12 @@ int af_gemv(int wf, int epi, const uint16_t* x, int ldx, const void* w, const ui
 size_t af_pack_i8_tiles_bytes(int n, int k);
 int af_pack_i8_tiles(const int8_t* codes, int n, int k, uint8_t* tiles, void* stream);
 size_t af_gemv_tc_scratch_bytes(int n, int k, int nb);
+/* Grid of the tensor-core GEMV for one shape on the current device (no counterpart in the
+ * reference): CTAs per 16-row slice (*grid) and the thread-block cluster size splitting each
+ * 64-row block (*csize; 0: stream-K). The CTAs' k ranges cover the packed weights in grid equal,
+ * contiguous, ordered pieces, which is what a plan's L2 prefetch of those weights follows.
+ * wf: 0 int8 tiles, 2 group-32 int4 tiles; epi as af_gemv_tc. Returns 0, or -1 on bad arguments. */
+int af_gemv_tc_grid(int n, int k, int nb, int epi, int wf, int* grid, int* csize);
 int af_gemv_tc(int epi, const uint16_t* x, int ldx, const void* tiles, const uint16_t* scales, const uint16_t* bias,
                void* y, int ldy, int nb, int n, int k, void* scratch, size_t scratch_bytes, void* stream);
 
