@@ -37,6 +37,21 @@ AF_DEV void l2_prefetch(const PF& pf, unsigned idx, unsigned n) {
   }
 }
 
+// The same spec through the load/store units: one `prefetch.global.L2` per 128-byte line, lines
+// idx, idx + n, ... of the spec's pieces (keeps the copy engine free for the issuing kernel's own
+// bulk copies).
+template <class PF>
+AF_DEV void l2_prefetch_lines(const PF& pf, unsigned idx, unsigned n) {
+  if (!pf.base) return;
+  const size_t lines_per_piece = (pf.piece + 127) / 128;
+  const size_t pieces = (pf.bytes + pf.stride - 1) / pf.stride;
+  const size_t total = pieces * lines_per_piece;
+  for (size_t i = idx; i < total; i += n) {
+    const size_t off = (i / lines_per_piece) * pf.stride + (i % lines_per_piece) * 128;
+    if (off < pf.bytes) asm volatile("prefetch.global.L2 [%0];" ::"l"(pf.base + off));
+  }
+}
+
 // ---- thread-block clusters: another CTA's shared memory, and the cluster-wide barrier
 // address of `p` (this CTA's shared memory) in the shared window of cluster rank `rank`
 AF_DEV uint32_t cluster_addr(const void* p, int rank) {

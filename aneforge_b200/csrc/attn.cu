@@ -43,6 +43,13 @@ AF_DEV void load_row_f16_sh(const __half* p, int lane, float* f, int epl, int la
     for (int e = 0; e < epl; ++e) f[e] = 0.f;
     return;
   }
+  if (epl == 4) {                                  // one 8-byte shared load
+    const uint2 u = *reinterpret_cast<const uint2*>(p + lane * 4);
+    const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    f[0] = x.x; f[1] = x.y; f[2] = y.x; f[3] = y.y;
+    return;
+  }
   for (int e = 0; e < epl; ++e) f[e] = __half2float(p[lane * epl + e]);
 }
 
@@ -71,9 +78,8 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
   int n_pre = 0;
   int pos = 0;
   float rc[EPL], rs[EPL];
-  if (warp == 0)
-    l2_prefetch(a.pf, ((blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * 32 + lane,
-                gridDim.x * gridDim.y * gridDim.z * 32);
+  l2_prefetch_lines(a.pf, ((blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * blockDim.x + threadIdx.x,
+                    gridDim.x * gridDim.y * gridDim.z * blockDim.x);
   if (a.prefetch) {
     pos = __ldcg(a.pos + b);
     if (pos >= 0 && pos < a.M) {
@@ -383,47 +389,50 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
   __shared__ float lw[64][G];      // per split: l_s
   __shared__ float den_s[G];
   if (a.cluster) {
-    // ---- cluster merge: this CTA's (acc, m, l) stay in its shared memory; rank 0 (split 0) reads
-    // every rank's through the cluster window and writes the head outputs
-    __shared__ float c_acc[G][DH];
-    __shared__ float c_m[G], c_l[G];
+    // ---- cluster merge: every split stores its (acc, m, l) straight into rank 0's merge area
+    // (dynamic shared memory after the staged rows, [n_split][G][DH + 2]); after one cluster barrier
+    // rank 0 (split 0) merges them from its own shared memory and the other CTAs leave
+    float* mrg = reinterpret_cast<float*>(kv_pre + (size_t)2 * a.pre_rows * DH * 2);
+    const uint32_t dst = cluster_addr(mrg, 0) + (uint32_t)split * G * (DH + 2) * 4;
     for (int i = threadIdx.x; i < G * DH; i += blockDim.x) {
       const int g = i / DH, dd = i - g * DH;
       float num, M, den;
       merge_warps(g, dd, num, M, den);
-      c_acc[g][dd] = num;
-      if (dd == 0) { c_m[g] = M; c_l[g] = den; }
+      const uint32_t at = dst + (uint32_t)(g * (DH + 2)) * 4;
+      asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(at + dd * 4), "f"(num) : "memory");
+      if (dd == 0) {
+        asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(at + DH * 4), "f"(M) : "memory");
+        asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(at + (DH + 1) * 4), "f"(den) : "memory");
+      }
     }
     cluster_sync_all();
-    if (split == 0) {
-      for (int i = threadIdx.x; i < a.n_split * G; i += blockDim.x) {
-        const int sp = i / G, g = i - sp * G;
-        fw[sp][g] = ld_cluster_f32(cluster_addr(&c_m[g], sp));
-        lw[sp][g] = ld_cluster_f32(cluster_addr(&c_l[g], sp));
-      }
-      __syncthreads();
-      if (threadIdx.x < G) {
-        const int g = threadIdx.x;
-        float M = -INFINITY;
-        for (int sp = 0; sp < a.n_split; ++sp) M = fmaxf(M, fw[sp][g]);
-        float den = 0.f;
-        for (int sp = 0; sp < a.n_split; ++sp) {
-          const float f = fw[sp][g] == -INFINITY ? 0.f : expf(fw[sp][g] - M);
-          den = fmaf(f, lw[sp][g], den);
-          fw[sp][g] = f;
-        }
-        den_s[g] = den;
-      }
-      __syncthreads();
-      for (int i = threadIdx.x; i < G * DH; i += blockDim.x) {
-        const int g = i / DH, dd = i - g * DH;
-        float num = 0.f;
-#pragma unroll 4
-        for (int sp = 0; sp < a.n_split; ++sp) num = fmaf(fw[sp][g], ld_cluster_f32(cluster_addr(&c_acc[g][dd], sp)), num);
-        a.out[(size_t)b * a.ld_out + (size_t)(kvh * G + g) * DH + dd] = f2h(num / den_s[g]);
-      }
+    if (split != 0) return;
+    for (int i = threadIdx.x; i < a.n_split * G; i += blockDim.x) {
+      const int sp = i / G, g = i - sp * G;
+      fw[sp][g] = mrg[(sp * G + g) * (DH + 2) + DH];
+      lw[sp][g] = mrg[(sp * G + g) * (DH + 2) + DH + 1];
     }
-    cluster_sync_all();          // no CTA leaves while rank 0 may still read its shared memory
+    __syncthreads();
+    if (threadIdx.x < G) {
+      const int g = threadIdx.x;
+      float M = -INFINITY;
+      for (int sp = 0; sp < a.n_split; ++sp) M = fmaxf(M, fw[sp][g]);
+      float den = 0.f;
+      for (int sp = 0; sp < a.n_split; ++sp) {
+        const float f = fw[sp][g] == -INFINITY ? 0.f : expf(fw[sp][g] - M);
+        den = fmaf(f, lw[sp][g], den);
+        fw[sp][g] = f;
+      }
+      den_s[g] = den;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * DH; i += blockDim.x) {
+      const int g = i / DH, dd = i - g * DH;
+      float num = 0.f;
+#pragma unroll 4
+      for (int sp = 0; sp < a.n_split; ++sp) num = fmaf(fw[sp][g], mrg[(sp * G + g) * (DH + 2) + dd], num);
+      a.out[(size_t)b * a.ld_out + (size_t)(kvh * G + g) * DH + dd] = f2h(num / den_s[g]);
+    }
     return;
   }
   float* part = a.part + (pair * a.n_split + split) * G * (DH + 2);
@@ -486,11 +495,13 @@ static cudaError_t launch_decode(const AttnDecodeArgs& a, cudaStream_t st, bool 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.n_split, a.KV, a.NB);
   cfg.blockDim = dim3(DEC_WARPS * 32);
-  cfg.dynamicSmemBytes = a.prefetch ? 2 * (size_t)a.pre_rows * DH * 2 : 0;
+  // staged cache rows, then (clusters) rank 0's merge area [n_split][G][DH + 2] fp32
+  cfg.dynamicSmemBytes = (a.prefetch ? 2 * (size_t)a.pre_rows * DH * 2 : 0) +
+                         (a.cluster ? (size_t)a.n_split * G * (DH + 2) * 4 : 0);
   static bool attrs_set = false;               // static + dynamic shared memory may pass 48 KB
   if (!attrs_set) {
     cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<DH, G, DIRECT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         2 * DEC_PRE_MAX * DH * 2);
+                                         2 * DEC_PRE_MAX * DH * 2 + DEC_CLUSTER_MAX * G * (DH + 2) * 4);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(attn_decode_kernel<DH, G, DIRECT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;

@@ -190,7 +190,6 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
     }
     if (!waited) pdl_wait();
     if (!ok) af_set_err(a.err, AF_DEV_WAIT_TIMEOUT);
-    l2_prefetch(a.pf, c, G);        // this CTA's share of a later kernel's weights
     // shared memory must outlive every copy this thread issued: wait (bounded) for the last use of
     // each weight stage and x slot to land before the thread exits
     for (int i = 0; i < in_flight; ++i) {
@@ -249,6 +248,8 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
       af_set_err(a.err, AF_DEV_WAIT_TIMEOUT);
       *reinterpret_cast<volatile int*>(&sh->cabort) = 1;
     }
+    // this CTA's stream is done: its share of a later kernel's weights into L2 meanwhile
+    if (u + (ktb - kta) >= u1) l2_prefetch_lines(a.pf, c * (CW * 32) + threadIdx.x, G * (CW * 32));
     // odd-tile warps hand their sums to the even-tile warps of the same row tile
 #pragma unroll
     for (int n = 0; n < NT; ++n)
@@ -507,6 +508,8 @@ static void plan_geometry(int N, int K, int NB, int epi, bool i4, int* G, int* m
       if (g > slots) break;
       if (d > 1) {
         const long long fit = i4 ? clusters_any<true>(NB, epi, (int)d) : clusters_any<false>(NB, epi, (int)d);
+        if (env_int("AF_TC_DEBUG", 0) > 1)
+          fprintf(stderr, "[gemv_tc]   RB=%lld d=%lld: %lld clusters fit\n", RB, d, fit);
         if (RB * 100 > fit * cfrac) continue;
       }
       const double balance = (double)g / (double)(sms * ((g + sms - 1) / sms));

@@ -30,7 +30,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_kernel(const void* x, int ldx, c
   const int b = blockIdx.x;
   constexpr int VW = XF16 ? 8 : 4;                   // elements per vector load
   float v[PER * VW];
-  l2_prefetch(pf, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
+  l2_prefetch_lines(pf, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
   pdl_wait();
   const int nvec = D / VW;
   float ss = 0.f;
