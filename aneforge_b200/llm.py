@@ -198,6 +198,17 @@ DECODE_MLPS = {"swiglu": emit_swiglu}
 _DECODE_CTX = ("pos",)
 
 
+def decode_nsplit(M, KV, NB=1):
+  """Split count of decode attention over a cache of M rows (see `_ctx`)."""
+  cap = max(1, (2 * 148) // max(1, KV * NB))
+  nsplit = max(1, min(64, cap, -(-M // 64)))
+  if nsplit > 8 and -(-M // 8) <= 512:
+    nsplit = 8
+  elif nsplit > 16 and -(-M // 16) <= 512:
+    nsplit = 16
+  return int(os.environ.get("AF_ATTN_NSPLIT", nsplit))
+
+
 def plan_l2_prefetch(pb, budget=None, mode=None):
   """Attach L2 prefetch keys to a decode plan: each tensor-core GEMV's weights are (partly) fetched
   into L2 by the kernel that runs before it - the previous GEMV once its own weight copies are all
@@ -384,13 +395,7 @@ class LlamaPrefill:
     # shared memory; 8 (then 16) is preferred while each split then holds at most 512 keys (on B200
     # clusters of 8 beat 16 at a few hundred keys); past that the splits merge through scratch (the
     # last CTA of each head merges them).
-    cap = max(1, (2 * 148) // max(1, cfg.n_kv_heads * NB))
-    nsplit = max(1, min(64, cap, -(-M // 64)))
-    if nsplit > 8 and -(-M // 8) <= 512:
-      nsplit = 8
-    elif nsplit > 16 and -(-M // 16) <= 512:
-      nsplit = 16
-    nsplit = int(os.environ.get("AF_ATTN_NSPLIT", nsplit))
+    nsplit = decode_nsplit(M, cfg.n_kv_heads, NB)
     return {"NB": NB, "M": M, "nsplit": nsplit, "scale": d["scale"], "kvc": d["kvc"], "expand": G > 1 and d["kvc"] != 1.0,
             "tp": self.tp is not None, "D": cfg.dim}
 

@@ -440,7 +440,8 @@ def kernel_bench(name, reps, warmup):
     return [t] + [t.clone() for _ in range(copies - 1)], sc
 
   I4 = {"gemv_i4_gu": (2 * 29568, 8192, R.EPI_SWIGLU), "gemv_i4_qkv": (80 * 128, 8192, R.EPI_F32),
-        "gemv_i4_o": (8192, 8192, R.EPI_RESID), "gemv_i4_down": (8192, 29568, R.EPI_RESID)}
+        "gemv_i4_o": (8192, 8192, R.EPI_RESID), "gemv_i4_down": (8192, 29568, R.EPI_RESID),
+        "gemv_i4_moe_gu": (2 * 14336, 4096, R.EPI_SWIGLU)}   # one Mixtral expert's gate|up
   if name in ("gemm_gu", "gemm_i4_gu"):
     # prefill: the tcgen05 GEMM over a 512-row (8B) / 2048-row (72B) prompt; FLOP-bound
     i4 = name == "gemm_i4_gu"
@@ -508,7 +509,8 @@ def kernel_bench(name, reps, warmup):
     qkv = torch.randn(1, (H + 2 * KV) * dh, generator=g, device=dev)
     p = torch.tensor([pos], dtype=torch.int32, device=dev)
     c, s_ = (torch.from_numpy(a).to(dev) for a in rope_tables(M, dh, CFG["rope_base"]))
-    nsplit = max(1, min(64, (2 * 148) // KV, -(-M // 32)))
+    from aneforge_b200.llm import decode_nsplit
+    nsplit = decode_nsplit(M, KV)                            # the decode program's split count
     scr = torch.zeros(K.attn_decode_scratch_bytes(1, KV, nsplit, H // KV, dh), dtype=torch.uint8, device=dev)
     kv_c = 127 * float(np.float16(1 / 127))
     nbytes = 2 * KV * (pos + 1) * dh * 2 + qkv.numel() * 4 + H * dh * 2
@@ -615,7 +617,7 @@ def main():
   ap.add_argument("--no-cpu-baseline", action="store_true")
   ap.add_argument("--kernel", default=None,
                   help="time one kernel alone: gemv_gu | gemv_qkv | gemv_o | gemv_down | gemv_cfg1 | attn | lm_head "
-                       "| gemv_i4_gu | gemv_i4_qkv | gemv_i4_o | gemv_i4_down | gemm_gu | gemm_i4_gu")
+                       "| gemv_i4_gu | gemv_i4_qkv | gemv_i4_o | gemv_i4_down | gemv_i4_moe_gu | gemm_gu | gemm_i4_gu")
   ap.add_argument("--reps", type=int, default=50)
   ap.add_argument("--profile-region", action="store_true",
                   help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
