@@ -68,6 +68,9 @@ SIGNATURES = [
   ("af_comm_unique_id", c_int, [c_void_p, c_size_t]),
   ("af_comm_init", c_int, [c_void_p, c_int, c_int, c_int, ctypes.POINTER(c_void_p)]),
   ("af_comm_destroy", None, [c_void_p]),
+  ("af_comm_p2p_handle", c_int, [c_void_p, c_size_t, c_void_p, c_size_t]),
+  ("af_comm_p2p_open", c_int, [c_void_p, c_void_p, c_size_t]),
+  ("af_comm_p2p_disable", None, [c_void_p]),
   ("af_program_set_comm", c_int, [c_void_p, c_void_p]),
   ("af_moe_gate", c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
   ("af_gemv_tc_expert", c_int, [c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,

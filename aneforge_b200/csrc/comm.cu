@@ -57,14 +57,101 @@ bool nccl_load(std::string& why) {
 
 }  // namespace
 
+// ---- one-shot all-reduce over NVLink peer memory (optional; set up by af_comm_p2p_open)
+//
+// Every rank owns one exchange buffer, mapped into every peer's address space through CUDA IPC:
+//   [2 sets][T source slots][cap floats]  data
+//   [2 sets][T source slots] u32          arrival flags (the call's epoch)
+//   u32                                   this rank's epoch counter
+// Call e (all ranks issue the same sequence of all-reduces) uses set e & 1: each rank stores its n
+// partial floats into slot `rank` of set e & 1 on every rank (its own included) with plain peer
+// stores, fences at system scope, then stores e into that slot's flag on every rank. It then waits
+// (bounded) until its own T flags read e and sums the T slots in rank order, so every rank computes
+// the same bits. Two sets make reuse safe: a rank can only write set s again (call e + 2) after
+// every peer has signalled call e + 1, which each does only after finishing call e.
+constexpr int P2P_MAX_RANKS = 8;
+constexpr long long P2P_SPIN = 1ll << 24;             // bounded waits (~1 s)
+
+struct P2pPeers {
+  char* base[P2P_MAX_RANKS];                          // every rank's exchange buffer (own included)
+};
+
 struct Comm {
   ncclComm_t nccl = nullptr;
   int nranks = 1, rank = 0, device = 0;
+  // peer-memory all-reduce
+  char* xbuf = nullptr;                               // this rank's exchange buffer
+  size_t cap = 0;                                     // floats per slot
+  size_t xbytes = 0;
+  char* peer[P2P_MAX_RANKS] = {};                     // opened IPC mappings (peer[rank] = xbuf)
+  bool p2p = false;
 };
 
-cudaError_t comm_all_reduce_f32(void* comm, const float* src, float* dst, size_t n, cudaStream_t st, std::string& why) {
+AF_HD size_t p2p_data_off(int set, int src, int T, size_t cap) { return ((size_t)set * T + src) * cap * 4; }
+AF_HD size_t p2p_flag_off(int set, int src, int T, size_t cap) { return (size_t)2 * T * cap * 4 + ((size_t)set * T + src) * 4; }
+AF_HD size_t p2p_epoch_off(int T, size_t cap) { return (size_t)2 * T * cap * 4 + (size_t)2 * T * 4; }
+AF_HD size_t p2p_bytes(int T, size_t cap) { return p2p_epoch_off(T, cap) + 16; }
+
+__global__ void __launch_bounds__(1024) p2p_all_reduce_kernel(P2pPeers peers, int T, int rank, size_t cap,
+                                                               const float* src, float* dst, int n, int* err) {
+  char* mine = peers.base[rank];
+  unsigned* epoch = reinterpret_cast<unsigned*>(mine + p2p_epoch_off(T, cap));
+  pdl_wait();
+  const unsigned e = *reinterpret_cast<volatile unsigned*>(epoch) + 1u;
+  const int set = (int)(e & 1u);
+  // push this rank's partial into slot `rank` of every rank
+  const int n4 = n / 4;
+  for (int p = 0; p < T; ++p) {
+    float4* d4 = reinterpret_cast<float4*>(peers.base[p] + p2p_data_off(set, rank, T, cap));
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) d4[i] = __ldcg(s4 + i);
+    float* d = reinterpret_cast<float*>(peers.base[p] + p2p_data_off(set, rank, T, cap));
+    for (int i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) d[i] = __ldcg(src + i);
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < T) {
+    unsigned* f = reinterpret_cast<unsigned*>(peers.base[threadIdx.x] + p2p_flag_off(set, rank, T, cap));
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
+  }
+  // wait for every rank's slot in this rank's buffer
+  __shared__ int timed_out;
+  if (threadIdx.x == 0) timed_out = 0;
+  __syncthreads();
+  if (threadIdx.x < T) {
+    const unsigned* f = reinterpret_cast<const unsigned*>(mine + p2p_flag_off(set, threadIdx.x, T, cap));
+    bool in = false;
+    for (long long i = 0; i < P2P_SPIN && !in; ++i) {
+      unsigned v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+      in = v == e;
+    }
+    if (!in) timed_out = 1;
+  }
+  __syncthreads();
+  if (timed_out && threadIdx.x == 0) af_set_err(err, AF_DEV_WAIT_TIMEOUT);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < T; ++s) acc += __ldcg(reinterpret_cast<const float*>(mine + p2p_data_off(set, s, T, cap)) + i);
+    dst[i] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(epoch) = e;
+  pdl_trigger();
+}
+
+cudaError_t comm_all_reduce_f32(void* comm, const float* src, float* dst, size_t n, cudaStream_t st, std::string& why,
+                                int* err) {
   Comm* c = static_cast<Comm*>(comm);
-  if (!c || !g_nccl.ok) { why = "no communicator"; return cudaErrorInvalidValue; }
+  if (!c) { why = "no communicator"; return cudaErrorInvalidValue; }
+  if (c->p2p && n <= c->cap && n % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+    P2pPeers peers;
+    for (int r = 0; r < P2P_MAX_RANKS; ++r) peers.base[r] = r < c->nranks ? c->peer[r] : nullptr;
+    const int threads = n >= 1024 ? 1024 : (int)((n + 31) / 32 * 32);
+    p2p_all_reduce_kernel<<<1, threads, 0, st>>>(peers, c->nranks, c->rank, c->cap, src, dst, (int)n, err);
+    return cudaGetLastError();
+  }
+  if (!g_nccl.ok || !c->nccl) { why = "no communicator"; return cudaErrorInvalidValue; }
   const ncclResult_t r = g_nccl.all_reduce(src, dst, n, ncclFloat32, ncclSum, c->nccl, st);
   if (r != ncclSuccess) { why = std::string("ncclAllReduce: ") + g_nccl.error_string(r); return cudaErrorUnknown; }
   return cudaSuccess;
@@ -164,8 +251,77 @@ int af_comm_init(const void* id, int nranks, int rank, int device, void** comm) 
 void af_comm_destroy(void* comm) {
   af::Comm* c = static_cast<af::Comm*>(comm);
   if (!c) return;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(c->device);
+  cudaDeviceSynchronize();
+  for (int r = 0; r < c->nranks && r < af::P2P_MAX_RANKS; ++r)
+    if (c->peer[r] && r != c->rank) cudaIpcCloseMemHandle(c->peer[r]);
+  if (c->xbuf) cudaFree(c->xbuf);
+  cudaSetDevice(prev);
   if (c->nccl && af::g_nccl.ok) af::g_nccl.comm_destroy(c->nccl);
   delete c;
+}
+
+int af_comm_p2p_handle(void* comm, size_t cap_floats, void* handle, size_t bytes) {
+  af::Comm* c = static_cast<af::Comm*>(comm);
+  if (!c || !handle || bytes < sizeof(cudaIpcMemHandle_t) || cap_floats == 0 || c->nranks > af::P2P_MAX_RANKS ||
+      c->xbuf) {
+    af::set_error_public("af_comm_p2p_handle: bad arguments");
+    return -1;
+  }
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(c->device);
+  c->cap = (cap_floats + 3) / 4 * 4;
+  c->xbytes = af::p2p_bytes(c->nranks, c->cap);
+  cudaError_t e = cudaMalloc(&c->xbuf, c->xbytes);
+  if (e == cudaSuccess) e = cudaMemset(c->xbuf, 0, c->xbytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), c->xbuf);
+  cudaDeviceSynchronize();
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) {
+    af::set_error_public(std::string("af_comm_p2p_handle: ") + cudaGetErrorString(e));
+    if (c->xbuf) cudaFree(c->xbuf);
+    c->xbuf = nullptr;
+    return -1;
+  }
+  return 0;
+}
+
+void af_comm_p2p_disable(void* comm) {
+  af::Comm* c = static_cast<af::Comm*>(comm);
+  if (c) c->p2p = false;
+}
+
+int af_comm_p2p_open(void* comm, const void* handles, size_t bytes_each) {
+  af::Comm* c = static_cast<af::Comm*>(comm);
+  if (!c || !handles || bytes_each < sizeof(cudaIpcMemHandle_t) || !c->xbuf) {
+    af::set_error_public("af_comm_p2p_open: bad arguments (call af_comm_p2p_handle first)");
+    return -1;
+  }
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(c->device);
+  for (int r = 0; r < c->nranks; ++r) {
+    if (r == c->rank) { c->peer[r] = c->xbuf; continue; }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, static_cast<const char*>(handles) + (size_t)r * bytes_each, sizeof(h));
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      for (int q = 0; q < r; ++q)
+        if (q != c->rank && c->peer[q]) { cudaIpcCloseMemHandle(c->peer[q]); c->peer[q] = nullptr; }
+      cudaSetDevice(prev);
+      af::set_error_public(std::string("af_comm_p2p_open: ") + cudaGetErrorString(e));
+      return -1;
+    }
+    c->peer[r] = static_cast<char*>(p);
+  }
+  c->p2p = true;
+  cudaSetDevice(prev);
+  return 0;
 }
 
 }  // extern "C"

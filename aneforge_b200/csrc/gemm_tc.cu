@@ -19,7 +19,8 @@
 // barrier. Warps 0-3 then read the accumulators (tcgen05.ld, 32 lanes each) and run the GEMV's
 // epilogues (F32 / F16 / RESID / SWIGLU).
 // Every wait is bounded; on a timeout the CTA records AF_DEV_WAIT_TIMEOUT, waits (bounded) for the
-// MMAs it issued, frees its tensor memory and returns. No copy uses cluster multicast.
+// MMAs it issued, frees its tensor memory and returns. Every copy lands in the issuing CTA's own
+// shared memory.
 #include <cuda.h>
 
 #include "af_common.cuh"
@@ -110,7 +111,7 @@ AF_DEV void i4_rows(uint32_t w, __half2 s_lo, __half2 s_hi, uint32_t& row_lo0, u
   row_hi1 = *reinterpret_cast<uint32_t*>(&a3);
 }
 
-// 2-D TMA tile load (no multicast) of box {64 K, 128 rows} at (k0, m0), completion on `bar`
+// 2-D TMA tile load into this CTA's shared memory of box {64 K, 128 rows} at (k0, m0), completion on `bar`
 AF_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int k0, int m0, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"

@@ -485,7 +485,7 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     if (!dry) {
       if (!p.comm) { why = op.kind + " needs a communicator (af_program_set_comm)"; return cudaErrorInvalidValue; }
       if (!red && c.i("ranks") != T) { why = "allgather: ranks does not match the communicator"; return cudaErrorInvalidValue; }
-      e = red ? comm_all_reduce_f32(p.comm, (const float*)src, (float*)dst, n, st, why)
+      e = red ? comm_all_reduce_f32(p.comm, (const float*)src, (float*)dst, n, st, why, p.d_err)
               : comm_all_gather_i32(p.comm, (const int*)src, (int*)dst, n, st, why);
       if (e != cudaSuccess) return e;
     }

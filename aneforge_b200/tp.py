@@ -123,6 +123,7 @@ class TensorParallel:
 
   def __init__(self, rank: int, world: int, device: int, handle):
     self.rank, self.world, self.device, self.handle = rank, world, device, handle
+    self.p2p = False
 
   @staticmethod
   def unique_id() -> bytes:
@@ -138,14 +139,42 @@ class TensorParallel:
     return cls(rank, world, device, h)
 
   @classmethod
-  def from_torch_distributed(cls, device: int) -> "TensorParallel":
+  def from_torch_distributed(cls, device: int, p2p: bool | None = None, p2p_floats: int = 16 * 8192) -> "TensorParallel":
     """Every rank of the default torch.distributed group calls this: rank 0 makes the NCCL id and
-    broadcasts it over the group, then each rank joins with its GPU."""
+    broadcasts it over the group, then each rank joins with its GPU. With `p2p` (default: on, env
+    AF_TP_P2P=0 turns it off) the ranks also map each other's exchange buffers so that the decode's
+    residual all-reduces (up to `p2p_floats` fp32 per call) run as one-shot peer-memory kernels;
+    if that setup fails on any rank, every rank keeps NCCL for them."""
+    import os
     import torch.distributed as dist
     rank, world = dist.get_rank(), dist.get_world_size()
     obj = [cls.unique_id() if rank == 0 else None]
     dist.broadcast_object_list(obj, src=0)
-    return cls.create(rank, world, device, obj[0])
+    tp = cls.create(rank, world, device, obj[0])
+    if p2p is None:
+      p2p = os.environ.get("AF_TP_P2P", "1") != "0"
+    if p2p and world > 1:
+      tp._p2p_setup(p2p_floats)
+    return tp
+
+  def _p2p_setup(self, cap_floats: int) -> None:
+    import torch.distributed as dist
+    lib = R.lib()
+    buf = ctypes.create_string_buffer(64)
+    ok = lib.af_comm_p2p_handle(self.handle, cap_floats, buf, 64) == 0
+    handles = [None] * self.world
+    dist.all_gather_object(handles, buf.raw if ok else None)
+    if all(h is not None for h in handles):
+      joined = ctypes.create_string_buffer(b"".join(handles), 64 * self.world)
+      ok = lib.af_comm_p2p_open(self.handle, joined, 64) == 0
+    else:
+      ok = False
+    flags = [None] * self.world
+    dist.all_gather_object(flags, ok)
+    self.p2p = all(flags)
+    if ok and not self.p2p:
+      # a peer could not map the buffers: nobody uses the peer path (it needs every rank)
+      lib.af_comm_p2p_disable(self.handle)
 
   def close(self) -> None:
     if self.handle:

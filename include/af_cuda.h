@@ -106,6 +106,16 @@ int af_program_set_options(void* prog, int use_graph, int use_pdl);
 int af_comm_unique_id(void* out, size_t bytes);
 int af_comm_init(const void* id, int nranks, int rank, int device, void** comm);
 void af_comm_destroy(void* comm);
+/* Optional one-shot all-reduce over NVLink peer memory for small fp32 all-reduces (the decode
+ * residual updates), replacing NCCL for them: every rank calls af_comm_p2p_handle (allocates its
+ * exchange buffer for up to cap_floats per call and writes its CUDA IPC handle, 64 bytes), the
+ * handles are exchanged between the ranks (rank order), then every rank calls af_comm_p2p_open with
+ * all of them. Each call waits (bounded, ~1 s) for the peers and records AF_DEV_WAIT_TIMEOUT in the
+ * program's error word if one never arrives. Up to 8 ranks, one process per GPU. */
+int af_comm_p2p_handle(void* comm, size_t cap_floats, void* handle, size_t bytes);
+int af_comm_p2p_open(void* comm, const void* handles, size_t bytes_each);
+/* Back to NCCL for every all-reduce (when another rank could not open the peer buffers). */
+void af_comm_p2p_disable(void* comm);
 int af_program_set_comm(void* prog, void* comm);
 
 /* Replaces ane_e5rt_program_share_buffer (ane_e5rt_dispatch.mm:687-714): rebind input `dst_in` to

@@ -108,7 +108,7 @@ def _gloo_rank(rank, world, port, q):
   made = {}
   TP.TensorParallel.unique_id = staticmethod(lambda: bytes(range(128)))
   TP.TensorParallel.create = classmethod(lambda cls, r, w, d, uid: made.setdefault("x", (r, w, d, uid)))
-  TP.TensorParallel.from_torch_distributed(device=rank)
+  TP.TensorParallel.from_torch_distributed(device=rank, p2p=False)
   dist.barrier()
   dist.destroy_process_group()
   q.put(made["x"])
@@ -130,3 +130,62 @@ def test_communicator_id_exchange_over_gloo():
     p.join(timeout=60)
     assert p.exitcode == 0
   assert [g[0] for g in got] == [0, 1] and all(g[1] == 2 and g[3] == bytes(range(128)) for g in got)
+
+
+class _FakeP2pLib:
+  """Stands in for libaf_cuda.so's peer-buffer entry points: a 64-byte handle derived from the rank,
+  and a record of the handles each rank opens."""
+
+  def __init__(self, rank, fail=False):
+    self.rank, self.fail, self.opened, self.disabled = rank, fail, None, False
+
+  def af_comm_p2p_handle(self, comm, cap, buf, nbytes):
+    import ctypes
+    ctypes.memmove(buf, bytes([self.rank]) * 64, 64)
+    return 0
+
+  def af_comm_p2p_open(self, comm, joined, each):
+    self.opened = bytes(joined.raw)
+    return -1 if self.fail else 0
+
+  def af_comm_p2p_disable(self, comm):
+    self.disabled = True
+
+
+def _p2p_rank(rank, world, port, fail_rank, q):
+  import torch.distributed as dist
+  os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+  dist.init_process_group("gloo", rank=rank, world_size=world)
+  fake = _FakeP2pLib(rank, fail=rank == fail_rank)
+  TP.R.lib = lambda: fake
+  tp = TP.TensorParallel(rank, world, rank, handle=object())
+  tp._p2p_setup(1024)
+  dist.barrier()
+  dist.destroy_process_group()
+  q.put((rank, tp.p2p, fake.opened, fake.disabled))
+
+
+@pytest.mark.parametrize("fail_rank", [-1, 1])
+def test_peer_buffer_handles_exchanged_in_rank_order(fail_rank):
+  """Every rank opens all ranks' handles in rank order; if one rank cannot open them, every rank
+  falls back (the peer all-reduce needs all of them)."""
+  import multiprocessing as mp
+  import socket
+  with socket.socket() as s:
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+  ctx = mp.get_context("spawn")
+  q = ctx.Queue()
+  world = 3
+  procs = [ctx.Process(target=_p2p_rank, args=(r, world, port, fail_rank, q)) for r in range(world)]
+  for p in procs:
+    p.start()
+  got = sorted(q.get(timeout=120) for _ in procs)
+  for p in procs:
+    p.join(timeout=60)
+    assert p.exitcode == 0
+  want = b"".join(bytes([r]) * 64 for r in range(world))
+  for rank, on, opened, disabled in got:
+    assert opened == want
+    assert on == (fail_rank < 0)
+    assert disabled == (fail_rank >= 0 and rank != fail_rank)

@@ -18,7 +18,7 @@ def _cfg(case):
   return Config(dim=1024, n_layers=2, n_heads=8, n_kv_heads=2, ffn_dim=2816, vocab=4096, rope_base=1e6), {"qkv_bias": True}
 
 
-def _rank(rank, world, port, case, prompt, q):
+def _rank(rank, world, port, case, prompt, q, p2p):
   import torch.distributed as dist
   os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
   torch.cuda.set_device(rank)
@@ -29,7 +29,8 @@ def _rank(rank, world, port, case, prompt, q):
   from aneforge_b200.tp import TensorParallel
   cfg, extra = _cfg(case)
   w = random_llama_weights(cfg, seed=21, **extra)
-  tp = TensorParallel.from_torch_distributed(rank)
+  tp = TensorParallel.from_torch_distributed(rank, p2p=p2p)
+  assert tp.p2p == p2p
   m = LlamaPrefill(to_b200_cfg(cfg), w, compress="int8" if case == "int8" else "int4_g32", device=rank, tp=tp)
   toks = m.generate(prompt, 24, max_len=64)
   m.release()
@@ -39,8 +40,9 @@ def _rank(rank, world, port, case, prompt, q):
   q.put((rank, toks))
 
 
-@pytest.mark.parametrize("case", ["int8", "int4_g32"])
-def test_tensor_parallel_2_gpus_matches_oracle(case):
+@pytest.mark.parametrize("case,p2p", [("int8", False), ("int8", True), ("int4_g32", True)])
+def test_tensor_parallel_2_gpus_matches_oracle(case, p2p):
+  """NCCL for every collective, or the residual all-reduces over NVLink peer memory."""
   if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
     pytest.skip("needs 2 GPUs")
   import multiprocessing as mp
@@ -54,7 +56,7 @@ def test_tensor_parallel_2_gpus_matches_oracle(case):
     port = s.getsockname()[1]
   ctx = mp.get_context("spawn")
   q = ctx.Queue()
-  procs = [ctx.Process(target=_rank, args=(r, 2, port, case, prompt, q)) for r in range(2)]
+  procs = [ctx.Process(target=_rank, args=(r, 2, port, case, prompt, q, p2p)) for r in range(2)]
   for p in procs:
     p.start()
   got = dict(q.get(timeout=600) for _ in procs)
