@@ -57,6 +57,8 @@ bool nccl_load(std::string& why) {
 
 }  // namespace
 
+cudaError_t add_f32_launch(float* y, const float* x, size_t n, cudaStream_t st);
+
 // ---- one-shot all-reduce over NVLink peer memory (optional; set up by af_comm_p2p_open)
 //
 // Every rank owns one exchange buffer, mapped into every peer's address space through CUDA IPC:
@@ -93,7 +95,8 @@ AF_HD size_t p2p_epoch_off(int T, size_t cap) { return (size_t)2 * T * cap * 4 +
 AF_HD size_t p2p_bytes(int T, size_t cap) { return p2p_epoch_off(T, cap) + 16; }
 
 __global__ void __launch_bounds__(1024) p2p_all_reduce_kernel(P2pPeers peers, int T, int rank, size_t cap,
-                                                               const float* src, float* dst, int n, int* err) {
+                                                               const float* src, float* dst, float* addto, int n,
+                                                               int* err) {
   char* mine = peers.base[rank];
   unsigned* epoch = reinterpret_cast<unsigned*>(mine + p2p_epoch_off(T, cap));
   pdl_wait();
@@ -133,7 +136,8 @@ __global__ void __launch_bounds__(1024) p2p_all_reduce_kernel(P2pPeers peers, in
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     float acc = 0.f;
     for (int s = 0; s < T; ++s) acc += __ldcg(reinterpret_cast<const float*>(mine + p2p_data_off(set, s, T, cap)) + i);
-    dst[i] = acc;
+    if (addto) addto[i] += acc;        // the residual update, as the separate add would do it
+    else dst[i] = acc;
   }
   __syncthreads();
   if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(epoch) = e;
@@ -141,20 +145,20 @@ __global__ void __launch_bounds__(1024) p2p_all_reduce_kernel(P2pPeers peers, in
 }
 
 cudaError_t comm_all_reduce_f32(void* comm, const float* src, float* dst, size_t n, cudaStream_t st, std::string& why,
-                                int* err) {
+                                int* err, float* addto) {
   Comm* c = static_cast<Comm*>(comm);
   if (!c) { why = "no communicator"; return cudaErrorInvalidValue; }
   if (c->p2p && n <= c->cap && n % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
     P2pPeers peers;
     for (int r = 0; r < P2P_MAX_RANKS; ++r) peers.base[r] = r < c->nranks ? c->peer[r] : nullptr;
     const int threads = n >= 1024 ? 1024 : (int)((n + 31) / 32 * 32);
-    p2p_all_reduce_kernel<<<1, threads, 0, st>>>(peers, c->nranks, c->rank, c->cap, src, dst, (int)n, err);
+    p2p_all_reduce_kernel<<<1, threads, 0, st>>>(peers, c->nranks, c->rank, c->cap, src, dst, addto, (int)n, err);
     return cudaGetLastError();
   }
   if (!g_nccl.ok || !c->nccl) { why = "no communicator"; return cudaErrorInvalidValue; }
   const ncclResult_t r = g_nccl.all_reduce(src, dst, n, ncclFloat32, ncclSum, c->nccl, st);
   if (r != ncclSuccess) { why = std::string("ncclAllReduce: ") + g_nccl.error_string(r); return cudaErrorUnknown; }
-  return cudaSuccess;
+  return addto ? add_f32_launch(addto, dst, n, st) : cudaSuccess;
 }
 
 cudaError_t comm_all_gather_i32(void* comm, const int* src, int* dst, size_t n, cudaStream_t st, std::string& why) {

@@ -481,11 +481,12 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     const bool red = op.kind == "allreduce";
     void* src = c.ptr("src", 4 * n);
     void* dst = c.ptr("dst", 4 * n * (red ? 1 : (size_t)c.i("ranks")));
+    float* addto = red ? (float*)c.ptr("addto", 4 * n, true) : nullptr;     // allreduce: y += sum
     if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
     if (!dry) {
       if (!p.comm) { why = op.kind + " needs a communicator (af_program_set_comm)"; return cudaErrorInvalidValue; }
       if (!red && c.i("ranks") != T) { why = "allgather: ranks does not match the communicator"; return cudaErrorInvalidValue; }
-      e = red ? comm_all_reduce_f32(p.comm, (const float*)src, (float*)dst, n, st, why, p.d_err)
+      e = red ? comm_all_reduce_f32(p.comm, (const float*)src, (float*)dst, n, st, why, p.d_err, addto)
               : comm_all_gather_i32(p.comm, (const int*)src, (int*)dst, n, st, why);
       if (e != cudaSuccess) return e;
     }

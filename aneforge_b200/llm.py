@@ -139,8 +139,7 @@ def _emit_row_parallel(pb, ctx, name, lin: DevLinear, x):
   if ctx.get("tp"):
     n = ctx["NB"] * ctx["D"]
     _emit_linear(pb, ctx, name, lin, x, "tp.part", "f32")
-    pb.op("allreduce", src="tp.part", dst="tp.part", n=n)
-    pb.op("add", y="h", x="tp.part", n=n)
+    pb.op("allreduce", src="tp.part", dst="tp.part", n=n, addto="h")
   else:
     _emit_linear(pb, ctx, name, lin, x, "h", "resid")
 
