@@ -8,13 +8,16 @@
 // the MMA reads through shared-memory descriptors:
 //   row r, 16-byte chunk c (8 fp16 along K) of a slice lives at (r / 8) * 1024 + (r % 8) * 128 +
 //   ((c ^ (r % 8)) * 16)  - eight-row atoms 1024 bytes apart (the descriptor's stride offset).
-// Roles: warp 5 (one thread) issues, per slice, a TMA tensor copy of the A tile (the copy engine
-// applies the 128-byte swizzle; rows past M read as zeros) and bulk copies of the raw packed weight
-// units of the slice (4 row blocks x 2 k tiles); warps 0-3 turn the raw units into the fp16 B slice
+// The raw packed weights have a ring of their own (4 x 16 KB), so their copies run ahead of the MMAs
+// instead of waiting for a whole operand stage to free up.
+// Roles: warp 9 (one thread) bulk-copies the raw packed weight units of each slice (4 row blocks x 2
+// k tiles) into the raw ring, starting before the programmatic-launch wait; warp 10 (one thread)
+// issues per slice a TMA tensor copy of the A tile (the copy engine applies the 128-byte swizzle;
+// rows past M read as zeros); warps 0-7 turn the raw units into the fp16 B slice
 // (a weight tile lane's 16 bytes are 2 rows x 8 consecutive columns - the GEMV's column permutation;
 // int8 codes become exact fp16 by a byte permute under the exponent of 1024 and one subtract, the
 // per-row scale is applied to the fp32 result; group-32 int4 codes become fp16 code * scale since
-// the scale changes along K inside a slice); warp 4 owns the tensor memory and one of its threads
+// the scale changes along K inside a slice); warp 8 owns the tensor memory and one of its threads
 // issues the MMAs, committing each slice to its "empty" barrier and the last to the accumulator
 // barrier. Warps 0-3 then read the accumulators (tcgen05.ld, 32 lanes each) and run the GEMV's
 // epilogues (F32 / F16 / RESID / SWIGLU).
@@ -35,15 +38,22 @@ constexpr int STAGES = 3;
 constexpr int A_BYTES = BM * BK * 2;          // 16 KB
 constexpr int B_BYTES = BN * BK * 2;          // 32 KB
 constexpr int RAW_BYTES = (BN / 64) * 2 * tc::UNIT;   // 16 KB: raw int8 units of one slice (int4: less)
-constexpr int STAGE = A_BYTES + B_BYTES + RAW_BYTES;
-constexpr int CONV = 128;                     // warps 0-3: converters, then epilogue
-constexpr int THREADS = CONV + 64;            // + warp 4 (TMEM owner, MMA issuer) + warp 5 (copies)
+constexpr int STAGE = A_BYTES + B_BYTES;      // one slice's MMA operands
+constexpr int RSTAGES = 4;                    // raw weight ring, ahead of the operand ring
+constexpr int CONV = 256;                     // warps 0-7 convert (two per SM sub-partition, to hide
+                                              // each other's latency); warps 0-3 then run the epilogue
+constexpr int MMA_WARP = CONV / 32;           // TMEM owner, MMA issuer
+constexpr int RAW_WARP = MMA_WARP + 1;        // raw weight copies
+constexpr int A_WARP = MMA_WARP + 2;          // A tiles
+constexpr int THREADS = CONV + 96;
 constexpr int TMEM_COLS = 256;
 constexpr long long LIMIT = 1ll << 26;
 }  // namespace gm
 
 struct GemmShared {
-  uint64_t raw[gm::STAGES];                   // A tile + raw weight units landed (copy bytes)
+  uint64_t raw_full[gm::RSTAGES];             // raw weight units landed (copy bytes)
+  uint64_t raw_empty[gm::RSTAGES];            // the converters are done with them
+  uint64_t a_full[gm::STAGES];                // A tile landed (TMA bytes)
   uint64_t full[gm::STAGES];                  // fp16 B slice written (converters)
   uint64_t empty[gm::STAGES];                 // the slice's MMAs finished reading (tcgen05.commit)
   uint64_t accum;
@@ -124,7 +134,8 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
   // the swizzled slices need 1024-byte aligned bases
   const uint32_t raw = smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
-  GemmShared* sh = reinterpret_cast<GemmShared*>(smem + gm::STAGES * gm::STAGE);
+  unsigned char* rawring = smem + gm::STAGES * gm::STAGE;
+  GemmShared* sh = reinterpret_cast<GemmShared*>(rawring + gm::RSTAGES * gm::RAW_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int MT = (a.NB + gm::BM - 1) / gm::BM;
   const int mt = blockIdx.x % MT, nt = blockIdx.x / MT;     // M fastest: CTAs sharing a weight tile run together
@@ -134,8 +145,12 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
   constexpr int UNIT = I4 ? tc::UNIT4 : tc::UNIT;
 
   if (threadIdx.x == 0) {
+    for (int s = 0; s < gm::RSTAGES; ++s) {
+      mbar_init(&sh->raw_full[s], 1);
+      mbar_init(&sh->raw_empty[s], gm::CONV);
+    }
     for (int s = 0; s < gm::STAGES; ++s) {
-      mbar_init(&sh->raw[s], 1);
+      mbar_init(&sh->a_full[s], 1);
       mbar_init(&sh->full[s], gm::CONV);
       mbar_init(&sh->empty[s], 1);
     }
@@ -143,7 +158,7 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
     sh->abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 4) {
+  if (warp == gm::MMA_WARP) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                  ::"r"(smem_u32(&sh->tmem)), "r"(gm::TMEM_COLS) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -154,48 +169,71 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
   const uint32_t tmem = sh->tmem;
   volatile int* abort = &sh->abort;
 
-  if (warp == 5) {
-    // ---------------------------------------------------------------- copies (one thread)
+  if (warp == gm::RAW_WARP) {
+    // ------------------------------------------------- raw weight copies (one thread, no launch wait:
+    // the weights never change, so the ring fills while the preceding kernel still runs)
     if (lane == 0) {
       const char* W = reinterpret_cast<const char*>(a.w);
       int issued = 0;
-      // weights never change: the first slices' units may go out before the programmatic wait
+      for (int kb = 0; kb < KB; ++kb) {
+        const int r = kb % gm::RSTAGES;
+        if (kb >= gm::RSTAGES &&
+            !gm_wait(&sh->raw_empty[r], (uint32_t)(((kb / gm::RSTAGES) - 1) & 1), abort)) {
+          *abort = 1;
+          break;
+        }
+        unsigned char* rs = rawring + r * gm::RAW_BYTES;
+        const int kt = kb * 2, nk = min(2, KT - kt);
+        uint32_t bytes = 0;
+        for (int rbi = 0; rbi < gm::BN / 64; ++rbi)
+          if (n0 / 64 + rbi < RB) bytes += (uint32_t)nk * UNIT;
+        mbar_arrive_expect_tx(&sh->raw_full[r], bytes);
+        for (int rbi = 0; rbi < gm::BN / 64; ++rbi) {
+          const int rb = n0 / 64 + rbi;
+          if (rb < RB)
+            bulk_g2s(rs + rbi * 2 * UNIT, W + ((size_t)rb * KT + kt) * UNIT, nk * UNIT, &sh->raw_full[r]);
+        }
+        issued = kb + 1;
+      }
+      // shared memory must outlive every copy issued: wait (time-bounded only) for the last ones
+      for (int kb = issued - 1; kb >= 0 && kb >= issued - gm::RSTAGES; --kb) {
+        const int r = kb % gm::RSTAGES;
+        for (long long i = 0;
+             i < gm::LIMIT && !mbar_try_wait(&sh->raw_full[r], (uint32_t)((kb / gm::RSTAGES) & 1)); ++i) {
+        }
+      }
+    }
+  } else if (warp == gm::A_WARP) {
+    // ---------------------------------------------------------------- A tiles (one thread)
+    if (lane == 0) {
+      pdl_wait();                                     // A is the preceding kernel's output
+      int issued = 0;
       for (int kb = 0; kb < KB; ++kb) {
         const int s = kb % gm::STAGES;
         if (kb >= gm::STAGES && !gm_wait(&sh->empty[s], (uint32_t)(((kb / gm::STAGES) - 1) & 1), abort)) {
           *abort = 1;
           break;
         }
-        unsigned char* st = smem + s * gm::STAGE;
-        const int kt = kb * 2, nk = min(2, KT - kt);
-        uint32_t bytes = 0;
-        for (int rbi = 0; rbi < gm::BN / 64; ++rbi)
-          if (n0 / 64 + rbi < RB) bytes += (uint32_t)nk * UNIT;
-        mbar_arrive_expect_tx(&sh->raw[s], bytes + gm::A_BYTES);
-        for (int rbi = 0; rbi < gm::BN / 64; ++rbi) {
-          const int rb = n0 / 64 + rbi;
-          if (rb < RB)
-            bulk_g2s(st + gm::A_BYTES + gm::B_BYTES + rbi * 2 * UNIT, W + ((size_t)rb * KT + kt) * UNIT, nk * UNIT,
-                     &sh->raw[s]);
-        }
-        if (kb == 0) pdl_wait();                      // A is the preceding kernel's output
-        tma_load_2d(st, &amap, kb * gm::BK, m0, &sh->raw[s]);
+        mbar_arrive_expect_tx(&sh->a_full[s], gm::A_BYTES);
+        tma_load_2d(smem + s * gm::STAGE, &amap, kb * gm::BK, m0, &sh->a_full[s]);
         issued = kb + 1;
       }
-      if (issued == 0) pdl_wait();
-      // shared memory must outlive every copy issued: wait (time-bounded only) for the last slices
       for (int kb = issued - 1; kb >= 0 && kb >= issued - gm::STAGES; --kb) {
         const int s = kb % gm::STAGES;
-        for (long long i = 0; i < gm::LIMIT && !mbar_try_wait(&sh->raw[s], (uint32_t)((kb / gm::STAGES) & 1)); ++i) {
+        for (long long i = 0; i < gm::LIMIT && !mbar_try_wait(&sh->a_full[s], (uint32_t)((kb / gm::STAGES) & 1)); ++i) {
         }
       }
     }
-  } else if (warp == 4) {
+  } else if (warp == gm::MMA_WARP) {
     // ---------------------------------------------------------------- MMA issuer (one thread)
     if (lane == 0) {
       for (int kb = 0; kb < KB; ++kb) {
         const int s = kb % gm::STAGES;
-        if (!gm_wait(&sh->full[s], (uint32_t)((kb / gm::STAGES) & 1), abort)) { *abort = 1; break; }
+        if (!gm_wait(&sh->a_full[s], (uint32_t)((kb / gm::STAGES) & 1), abort) ||
+            !gm_wait(&sh->full[s], (uint32_t)((kb / gm::STAGES) & 1), abort)) {
+          *abort = 1;
+          break;
+        }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t abase = smem_u32(smem + s * gm::STAGE);
         const uint32_t bbase = abase + gm::A_BYTES;
@@ -212,11 +250,16 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
     // ---------------------------------------------------------------- converters (warps 0-3)
     const int t = threadIdx.x;
     for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % gm::STAGES;
-      if (!gm_wait(&sh->raw[s], (uint32_t)((kb / gm::STAGES) & 1), abort)) { *abort = 1; break; }
+      const int s = kb % gm::STAGES, r = kb % gm::RSTAGES;
+      // the raw units landed, and the MMAs of the slice that last used this B slot are done
+      if (!gm_wait(&sh->raw_full[r], (uint32_t)((kb / gm::RSTAGES) & 1), abort) ||
+          (kb >= gm::STAGES && !gm_wait(&sh->empty[s], (uint32_t)(((kb / gm::STAGES) - 1) & 1), abort))) {
+        *abort = 1;
+        break;
+      }
       unsigned char* st = smem + s * gm::STAGE;
       unsigned char* Bs = st + gm::A_BYTES;
-      const unsigned char* Rw = Bs + gm::B_BYTES;
+      const unsigned char* Rw = rawring + r * gm::RAW_BYTES;
       const int kt0 = kb * 2;
 #pragma unroll 4
       for (int q = t; q < gm::BN / 64 * 2 * 128; q += gm::CONV) {
@@ -247,6 +290,7 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
       // generic-proxy stores -> visible to the tensor core's async proxy, then signal the slice
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive(&sh->full[s]);
+      mbar_arrive(&sh->raw_empty[r]);
     }
   }
 
@@ -303,13 +347,15 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == 4) {
+  if (warp == gm::MMA_WARP) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(gm::TMEM_COLS) : "memory");
   }
 }
 
-size_t gemm_tc_smem_bytes() { return (size_t)gm::STAGES * gm::STAGE + sizeof(GemmShared) + 1024; }
+size_t gemm_tc_smem_bytes() {
+  return (size_t)gm::STAGES * gm::STAGE + (size_t)gm::RSTAGES * gm::RAW_BYTES + sizeof(GemmShared) + 1024;
+}
 
 // cuTensorMapEncodeTiled, resolved through the runtime at first use: the library does not link the
 // driver library, so it loads (and exports its symbols) on hosts without a GPU driver
