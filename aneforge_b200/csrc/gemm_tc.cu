@@ -10,14 +10,14 @@
 //   ((c ^ (r % 8)) * 16)  - eight-row atoms 1024 bytes apart (the descriptor's stride offset).
 // The raw packed weights have a ring of their own (4 x 16 KB), so their copies run ahead of the MMAs
 // instead of waiting for a whole operand stage to free up.
-// Roles: warp 9 (one thread) bulk-copies the raw packed weight units of each slice (4 row blocks x 2
-// k tiles) into the raw ring, starting before the programmatic-launch wait; warp 10 (one thread)
+// Roles: warp 13 (one thread) bulk-copies the raw packed weight units of each slice (4 row blocks x 2
+// k tiles) into the raw ring, starting before the programmatic-launch wait; warp 14 (one thread)
 // issues per slice a TMA tensor copy of the A tile (the copy engine applies the 128-byte swizzle;
-// rows past M read as zeros); warps 0-7 turn the raw units into the fp16 B slice
+// rows past M read as zeros); warps 0-11 turn the raw units into the fp16 B slice
 // (a weight tile lane's 16 bytes are 2 rows x 8 consecutive columns - the GEMV's column permutation;
 // int8 codes become exact fp16 by a byte permute under the exponent of 1024 and one subtract, the
 // per-row scale is applied to the fp32 result; group-32 int4 codes become fp16 code * scale since
-// the scale changes along K inside a slice); warp 8 owns the tensor memory and one of its threads
+// the scale changes along K inside a slice); warp 12 owns the tensor memory and one of its threads
 // issues the MMAs, committing each slice to its "empty" barrier and the last to the accumulator
 // barrier. Warps 0-3 then read the accumulators (tcgen05.ld, 32 lanes each) and run the GEMV's
 // epilogues (F32 / F16 / RESID / SWIGLU).
@@ -40,7 +40,7 @@ constexpr int B_BYTES = BN * BK * 2;          // 32 KB
 constexpr int RAW_BYTES = (BN / 64) * 2 * tc::UNIT;   // 16 KB: raw int8 units of one slice (int4: less)
 constexpr int STAGE = A_BYTES + B_BYTES;      // one slice's MMA operands
 constexpr int RSTAGES = 4;                    // raw weight ring, ahead of the operand ring
-constexpr int CONV = 256;                     // warps 0-7 convert (two per SM sub-partition, to hide
+constexpr int CONV = 384;                     // warps 0-11 convert (three per SM sub-partition, to hide
                                               // each other's latency); warps 0-3 then run the epilogue
 constexpr int MMA_WARP = CONV / 32;           // TMEM owner, MMA issuer
 constexpr int RAW_WARP = MMA_WARP + 1;        // raw weight copies
