@@ -201,8 +201,8 @@ def decode_nsplit(M, KV, NB=1):
   """Split count of decode attention over a cache of M rows (see `_ctx`)."""
   cap = max(1, (2 * 148) // max(1, KV * NB))
   nsplit = max(1, min(64, cap, -(-M // 64)))
-  if nsplit > 8 and -(-M // 8) <= 512:
-    nsplit = 8
+  if nsplit > 12 and -(-M // 12) <= 512:
+    nsplit = 12
   elif nsplit > 16 and -(-M // 16) <= 512:
     nsplit = 16
   return int(os.environ.get("AF_ATTN_NSPLIT", nsplit))
@@ -391,9 +391,9 @@ class LlamaPrefill:
     # split-K over the cache: one split per 64 cache rows (the kernel also keeps >= 64 keys per
     # busy split at shorter positions), but all CTAs in one wave (2 CTAs of 8 warps per SM) and at
     # most 64 splits. Up to 16 splits of a head run as one thread-block cluster and merge in its
-    # shared memory; 8 (then 16) is preferred while each split then holds at most 512 keys (on B200
-    # clusters of 8 beat 16 at a few hundred keys); past that the splits merge through scratch (the
-    # last CTA of each head merges them).
+    # shared memory; at most 12 (then 16) while each split then holds at most 512 keys (on B200,
+    # decoding at positions 512-830, clusters of 10-12 beat 8 and 16); past that the splits merge
+    # through scratch (the last CTA of each head merges them).
     nsplit = decode_nsplit(M, cfg.n_kv_heads, NB)
     return {"NB": NB, "M": M, "nsplit": nsplit, "scale": d["scale"], "kvc": d["kvc"], "expand": G > 1 and d["kvc"] != 1.0,
             "tp": self.tp is not None, "D": cfg.dim}

@@ -195,7 +195,7 @@ def _attn_ref(qkv, Kc, Vc, pos, cos, sin, H, KV, dh, kv_c, expand):
 
 @pytest.mark.parametrize("dh,H,KV", [(128, 32, 8), (128, 16, 4), (64, 8, 8), (64, 8, 2), (64, 16, 2), (32, 4, 1),
                                      (16, 4, 2)])
-@pytest.mark.parametrize("n_split", [1, 2, 4, 16, 24])
+@pytest.mark.parametrize("n_split", [1, 2, 4, 12, 16, 24])
 @pytest.mark.parametrize("expand", [False, True])
 def test_attn_decode(K, dh, H, KV, n_split, expand):
   rng = np.random.default_rng(dh + H + n_split)
