@@ -30,9 +30,20 @@ __global__ void __launch_bounds__(1024) rmsnorm_kernel(const void* x, int ldx, c
   const int b = blockIdx.x;
   constexpr int VW = XF16 ? 8 : 4;                   // elements per vector load
   float v[PER * VW];
+  const int nvec = D / VW;
+  // γ is a weight: this thread's γ values are read before the programmatic-launch wait, so only the
+  // row read remains after it
+  __half gh[PER * VW];
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int vi = threadIdx.x + k * blockDim.x;
+    if (vi < nvec) {
+      if (VW == 8) *reinterpret_cast<uint4*>(gh + k * VW) = __ldg(reinterpret_cast<const uint4*>(g) + vi);
+      else *reinterpret_cast<uint2*>(gh + k * VW) = __ldg(reinterpret_cast<const uint2*>(g) + vi);
+    }
+  }
   l2_prefetch_lines(pf, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
   pdl_wait();
-  const int nvec = D / VW;
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < PER; ++k) {
@@ -67,7 +78,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_kernel(const void* x, int ldx, c
     if (vi < nvec) {
       __half o[VW];
 #pragma unroll
-      for (int e = 0; e < VW; ++e) o[e] = __float2half_rn(__fdiv_rn(v[k * VW + e], sn) * __half2float(g[vi * VW + e]));
+      for (int e = 0; e < VW; ++e) o[e] = __float2half_rn(__fdiv_rn(v[k * VW + e], sn) * __half2float(gh[k * VW + e]));
       __half* dst = out + (size_t)b * ldo + (size_t)vi * VW;
       if (VW == 8) *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(o);
       else *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(o);
@@ -146,6 +157,7 @@ cudaError_t rmsnorm_launch(const void* x, int x_f16, int ldx, const __half* g, f
   cudaLaunchAttribute attr[1];
   const int VW = x_f16 ? 8 : 4;
   const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(g) % 16 == 0) &&
                        (ldx % VW == 0) && (ldo % 8 == 0) && (D % 8 == 0);
   const int nvec = D / VW;
   const int per = (nvec + 1023) / 1024;
