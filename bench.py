@@ -518,6 +518,19 @@ def kernel_bench(name, reps, warmup):
     fn = lambda i: K.attn_decode(qkv, kc, vc, p, c, s_, H, KV, dh, float(np.float16(1 / np.sqrt(dh))), kv_c, True,
                                  nsplit, scr, out=o)
     what = f"attn_decode H{H}/KV{KV} dh{dh} pos {pos} nsplit {nsplit} (KV cache {2 * KV * (pos + 1) * dh * 2} B)"
+  elif name == "rmsnorm":
+    # the decode's pre-attention / pre-MLP norm: one fp32 residual row -> fp16
+    xs = [torch.randn(1, D, generator=g, device=dev) for _ in range(64)]
+    gam = (torch.randn(D, generator=g, device=dev) * 0.5 + 1.0).half()
+    nbytes = D * 4 + D * 2 + D * 2
+    fn = lambda i: K.rmsnorm(xs[i % 64], gam, float(np.float16(np.sqrt(D * 1e-5))))
+    what = f"rmsnorm fp32 row of {D} -> fp16"
+  elif name == "moe_gate":
+    # Mixtral router tail: softmax over 8 experts, top-2, renormalise
+    lg = [torch.randn(1, 8, generator=g, device=dev) for _ in range(64)]
+    nbytes = 8 * 4 + 8 * 4 + 2 * 4
+    fn = lambda i: K.moe_gate(lg[i % 64], 2)
+    what = "moe_gate E=8 k=2, one row"
   elif name == "lm_head":
     W = (torch.randn(V, D, generator=g, device=dev) * 0.02).half()
     x = torch.randn(1, D, generator=g, device=dev).half()
@@ -617,7 +630,8 @@ def main():
   ap.add_argument("--no-cpu-baseline", action="store_true")
   ap.add_argument("--kernel", default=None,
                   help="time one kernel alone: gemv_gu | gemv_qkv | gemv_o | gemv_down | gemv_cfg1 | attn | lm_head "
-                       "| gemv_i4_gu | gemv_i4_qkv | gemv_i4_o | gemv_i4_down | gemv_i4_moe_gu | gemm_gu | gemm_i4_gu")
+                       "| gemv_i4_gu | gemv_i4_qkv | gemv_i4_o | gemv_i4_down | gemv_i4_moe_gu | gemm_gu | gemm_i4_gu "
+                       "| rmsnorm | moe_gate")
   ap.add_argument("--reps", type=int, default=50)
   ap.add_argument("--profile-region", action="store_true",
                   help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
