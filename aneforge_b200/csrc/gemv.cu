@@ -17,6 +17,7 @@
 // thread keeps R x 16 bytes in flight.
 #include "af_common.cuh"
 #include "af_kernels.h"
+#include "tc_common.cuh"
 
 namespace af {
 
@@ -240,6 +241,158 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
   }
 }
 
+// ---- the fp16 lm_head for 2..16 sequences on the tensor pipe (mma.sync m16n8k16, fp32 accumulate)
+// The CUDA-core kernel above is bandwidth-bound for one sequence but compute-bound from about four:
+// it re-streams the head per 4-row tile at ~4x the single-row time. Here one launch reads the head
+// once: each warp owns 16 vocabulary rows and walks K in 32-wide chunks with 16-byte loads (rows g and
+// g + 8 of the fragment from lanes 4g..4g+3, x from the same k positions: the k order inside a chunk
+// is permuted identically for both operands, so the dot products are unchanged); the batch is the
+// MMA's N (8 per n-tile). Epilogue: optional fp32 logits, then the argmax of the CUDA-core kernel
+// (per-CTA candidates, ties to the lowest index, the last CTA merges and advances pos / history).
+template <int NT>
+__global__ void __launch_bounds__(256) lm_head_tc_kernel(GemvArgs a) {
+  constexpr int NW = 8, U = 4;                       // warps per CTA, 32-wide chunks per load batch
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int row0 = (blockIdx.x * NW + warp) * 16;
+  const int K = a.K, NB = a.NB;
+  const __half* W = static_cast<const __half*>(a.w);
+  const int ra = row0 + g, rb = row0 + g + 8;
+  const __half* wa = W + (size_t)(ra < a.N ? ra : 0) * K + 8 * t;
+  const __half* wb = W + (size_t)(rb < a.N ? rb : 0) * K + 8 * t;
+  const __half* xr[NT];
+  bool xv[NT];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    const int b = n * 8 + g;
+    xv[n] = b < NB;
+    xr[n] = a.x + (size_t)(xv[n] ? b : 0) * a.ldx + 8 * t;
+  }
+  float acc[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc[n][q] = 0.f;
+  pdl_wait();
+  const int nchunk = K / 32;
+  for (int c0 = 0; c0 < nchunk; c0 += U) {
+    uint4 A0[U], A1[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + u;
+      A0[u] = c < nchunk ? ldg_stream(wa + (size_t)c * 32) : make_uint4(0u, 0u, 0u, 0u);
+      A1[u] = c < nchunk ? ldg_stream(wb + (size_t)c * 32) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + u;
+      if (c >= nchunk) break;
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const uint4 xq = xv[n] ? *reinterpret_cast<const uint4*>(xr[n] + (size_t)c * 32) : make_uint4(0u, 0u, 0u, 0u);
+        // k-step 0: elements 0..3 of each lane's 8; k-step 1: elements 4..7
+        const uint32_t f0[4] = {A0[u].x, A1[u].x, A0[u].y, A1[u].y};
+        const uint32_t f1[4] = {A0[u].z, A1[u].z, A0[u].w, A1[u].w};
+        mma_16816(acc[n], f0, xq.x, xq.y);
+        mma_16816(acc[n], f1, xq.z, xq.w);
+      }
+    }
+  }
+  pdl_trigger();
+  // ---- this warp's rows: logits, then the best (value, row) per batch column over its 16 rows
+  __shared__ float cv[NW][16];
+  __shared__ int ci[NW][16];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int b = n * 8 + 2 * t + h;
+      float v0 = acc[n][h], v1 = acc[n][2 + h];           // rows ra, rb
+      if (a.y && b < NB) {
+        if (ra < a.N) reinterpret_cast<float*>(a.y)[(size_t)b * a.ldy + ra] = v0;
+        if (rb < a.N) reinterpret_cast<float*>(a.y)[(size_t)b * a.ldy + rb] = v1;
+      }
+      float best = ra < a.N ? v0 : -INFINITY;
+      int bi = ra < a.N ? ra : 0x7fffffff;
+      if (rb < a.N && (v1 > best || bi == 0x7fffffff)) { best = v1; bi = rb; }
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {                  // over g: lanes with the same t
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+      }
+      if (g == 0 && b < 16) { cv[warp][b] = best; ci[warp][b] = bi; }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < NB) {
+    const int b = threadIdx.x;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int w = 0; w < NW; ++w)
+      if (cv[w][b] > best || (cv[w][b] == best && ci[w][b] < bi)) { best = cv[w][b]; bi = ci[w][b]; }
+    a.am_val[(size_t)blockIdx.x * NB + b] = best;
+    a.am_idx[(size_t)blockIdx.x * NB + b] = bi;
+  }
+  __threadfence();
+  __syncthreads();
+  __shared__ int last;
+  if (threadIdx.x == 0) last = (atomicAdd(a.am_count, 1) == (int)gridDim.x - 1);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // the last CTA: one warp per batch column merges the CTAs' candidates in index order
+  for (int b = warp; b < NB; b += NW) {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int j = lane; j < (int)gridDim.x; j += 32) {
+      const float v = __ldcg(a.am_val + (size_t)j * NB + b);
+      const int ix = __ldcg(a.am_idx + (size_t)j * NB + b);
+      if (v > best || (v == best && ix < bi)) { best = v; bi = ix; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    if (lane == 0) {
+      a.tok_out[b] = bi + a.idx_base;
+      if (a.val_out) a.val_out[b] = best;
+      if (a.pos_adv) {
+        const int p = __ldcg(a.pos_adv + b);
+        if (a.hist && p >= 0 && p < a.hist_ld) a.hist[(size_t)b * a.hist_ld + p] = bi;
+        a.pos_adv[b] = p + 1;
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *a.am_count = 0;
+}
+
+static int lm_head_tc_ctas(int N) { return (N + 127) / 128; }
+
+static bool lm_head_tc_ok(const GemvArgs& a) {
+  static const int on = env_int("AF_LM_HEAD_TC", 1);
+  return on && a.wf == W_F16 && a.epi == EPI_ARGMAX && a.NB >= 2 && a.NB <= 16 && a.K % 32 == 0 && a.ldx % 8 == 0 &&
+         !a.scale && !a.bias && (reinterpret_cast<uintptr_t>(a.w) & 15) == 0 &&
+         (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
+}
+
+static cudaError_t lm_head_tc_launch(const GemvArgs& a, cudaStream_t st, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(lm_head_tc_ctas(a.N));
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = a.NB <= 8 ? cudaLaunchKernelEx(&cfg, lm_head_tc_kernel<1>, a) : cudaLaunchKernelEx(&cfg, lm_head_tc_kernel<2>, a);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
 template <int WF, int NB, int R, int EPI>
 static cudaError_t launch_one(const GemvArgs& a, int ctas, size_t smem, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
@@ -301,6 +454,8 @@ static int tile_template(int epi, int nb_tile, int nb_total) {
 cudaError_t gemv_launch(const GemvArgs& a0, cudaStream_t st, bool pdl) {
   if (a0.K % (a0.wf == W_I8 ? 16 : a0.wf == W_F16 ? 8 : 32)) return cudaErrorInvalidValue;
   if (a0.NB < 1) return cudaErrorInvalidValue;
+  // one launch over every row (gemv_argmax_scratch sizes the partial slots for it too)
+  if (lm_head_tc_ok(a0)) return lm_head_tc_launch(a0, st, pdl);
   const int ctas_am = a0.epi == EPI_ARGMAX ? gemv_argmax_ctas(a0.wf, a0.N, a0.K, a0.NB) : 0;
   for (int b0 = 0, t = 0; b0 < a0.NB; b0 += 4, ++t) {
     GemvArgs a = a0;
@@ -355,6 +510,8 @@ int gemv_argmax_ctas(int wf, int N, int K, int NB) {
 void gemv_argmax_scratch(int wf, int N, int K, int NB, size_t* slot_floats, size_t* counters) {
   const int tiles = (NB + 3) / 4;
   *slot_floats = (size_t)tiles * gemv_argmax_ctas(wf, N, K, NB) * 4;
+  const size_t tc = (size_t)lm_head_tc_ctas(N) * NB;       // the tensor-core head's slots
+  if (tc > *slot_floats) *slot_floats = tc;
   *counters = (size_t)tiles;
 }
 

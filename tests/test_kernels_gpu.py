@@ -158,6 +158,29 @@ def test_lm_head_argmax_large_vocab_and_pos_advance(K):
   assert int(pos.item()) == 42
 
 
+@pytest.mark.parametrize("NB", [2, 9, 16])
+def test_lm_head_argmax_batched_large_vocab(K, NB):
+  """Batches of 2-16 rows take the tensor-core head (one pass over the weights): logits within fp32
+  summation-order noise of the reference, tokens equal to the kernel's own logits' argmax and to the
+  reference's wherever its top-2 gap is above that noise; positions advance."""
+  rng = np.random.default_rng(13 + NB)
+  V, D = 128256, 4096
+  W = (rng.standard_normal((V, D), dtype=F32) * F32(0.02)).astype(F16)
+  x = rng.standard_normal((NB, D), dtype=F32).astype(F16)
+  pos = torch.tensor([3 + b % 4 for b in range(NB)], dtype=torch.int32, device="cuda")
+  tok, lg = K.lm_head_argmax(cuda(x), cuda(W), pos=pos)
+  ref = x.astype(F32) @ W.astype(F32).T
+  lgn = lg.cpu().numpy()
+  assert np.abs(lgn - ref).max() <= 1e-4 * np.abs(ref).max()
+  t = tok.cpu().numpy()
+  for b in range(NB):
+    assert t[b] == int(np.argmax(lgn[b]))
+    top2 = np.sort(ref[b])[-2:]
+    if top2[1] - top2[0] > 1e-4 * np.abs(ref).max():
+      assert t[b] == int(np.argmax(ref[b]))
+    assert int(pos[b].item()) == 4 + b % 4
+
+
 @pytest.mark.parametrize("D", [64, 2048, 4096])
 @pytest.mark.parametrize("xf16", [False, True])
 def test_rmsnorm_matches_reference_lowering(K, D, xf16):
