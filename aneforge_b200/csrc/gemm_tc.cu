@@ -50,6 +50,19 @@ constexpr int TMEM_COLS = 256;
 constexpr long long LIMIT = 1ll << 26;
 }  // namespace gm
 
+// per output-tile width: 256 columns (the default) or 128 (prompt-sized shapes with few tiles, so
+// that more SMs get one)
+template <int BNV>
+struct Gt {
+  static constexpr int BN = BNV;
+  static constexpr int B_BYTES = BN * gm::BK * 2;
+  static constexpr int RAW_BYTES = (BN / 64) * 2 * tc::UNIT;
+  static constexpr int STAGE = gm::A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = BN;
+  // kind::f16, fp16 A and B (K-major), fp32 accumulate, M = 128, N = BN
+  static constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(gm::BM >> 4) << 24);
+};
+
 struct GemmShared {
   uint64_t raw_full[gm::RSTAGES];             // raw weight units landed (copy bytes)
   uint64_t raw_empty[gm::RSTAGES];            // the converters are done with them
@@ -78,14 +91,11 @@ AF_DEV uint64_t smem_desc(uint32_t addr) {
          ((uint64_t)2 << 61);
 }
 
-// kind::f16, fp16 A and B (K-major), fp32 accumulate, M = 128, N = 256
-constexpr uint32_t GEMM_IDESC = (1u << 4) | ((uint32_t)(gm::BN >> 3) << 17) | ((uint32_t)(gm::BM >> 4) << 24);
-
-AF_DEV void mma_f16(uint32_t tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+AF_DEV void mma_f16(uint32_t tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
-      ::"r"(tmem), "l"(adesc), "l"(bdesc), "r"(GEMM_IDESC), "r"(accumulate) : "memory");
+      ::"r"(tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
 }
 
 AF_DEV void mma_commit(uint64_t* bar) {
@@ -128,18 +138,19 @@ AF_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int k0, int m0, uint6
       ::"r"(smem_u32(dst)), "l"(map), "r"(k0), "r"(m0), "r"(smem_u32(bar)) : "memory");
 }
 
-template <bool I4>
+template <bool I4, int BNV>
 __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, const __grid_constant__ CUtensorMap amap) {
+  using T = Gt<BNV>;
   extern __shared__ unsigned char smem_raw[];
   // the swizzled slices need 1024-byte aligned bases
   const uint32_t raw = smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
-  unsigned char* rawring = smem + gm::STAGES * gm::STAGE;
-  GemmShared* sh = reinterpret_cast<GemmShared*>(rawring + gm::RSTAGES * gm::RAW_BYTES);
+  unsigned char* rawring = smem + gm::STAGES * T::STAGE;
+  GemmShared* sh = reinterpret_cast<GemmShared*>(rawring + gm::RSTAGES * T::RAW_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int MT = (a.NB + gm::BM - 1) / gm::BM;
   const int mt = blockIdx.x % MT, nt = blockIdx.x / MT;     // M fastest: CTAs sharing a weight tile run together
-  const int m0 = mt * gm::BM, n0 = nt * gm::BN;
+  const int m0 = mt * gm::BM, n0 = nt * T::BN;
   const int KT = a.K / 32, RB = a.Np / 64;
   const int KB = (a.K + gm::BK - 1) / gm::BK;
   constexpr int UNIT = I4 ? tc::UNIT4 : tc::UNIT;
@@ -160,7 +171,7 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
   }
   if (warp == gm::MMA_WARP) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                 ::"r"(smem_u32(&sh->tmem)), "r"(gm::TMEM_COLS) : "memory");
+                 ::"r"(smem_u32(&sh->tmem)), "r"(T::TMEM_COLS) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -182,13 +193,13 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
           *abort = 1;
           break;
         }
-        unsigned char* rs = rawring + r * gm::RAW_BYTES;
+        unsigned char* rs = rawring + r * T::RAW_BYTES;
         const int kt = kb * 2, nk = min(2, KT - kt);
         uint32_t bytes = 0;
-        for (int rbi = 0; rbi < gm::BN / 64; ++rbi)
+        for (int rbi = 0; rbi < T::BN / 64; ++rbi)
           if (n0 / 64 + rbi < RB) bytes += (uint32_t)nk * UNIT;
         mbar_arrive_expect_tx(&sh->raw_full[r], bytes);
-        for (int rbi = 0; rbi < gm::BN / 64; ++rbi) {
+        for (int rbi = 0; rbi < T::BN / 64; ++rbi) {
           const int rb = n0 / 64 + rbi;
           if (rb < RB)
             bulk_g2s(rs + rbi * 2 * UNIT, W + ((size_t)rb * KT + kt) * UNIT, nk * UNIT, &sh->raw_full[r]);
@@ -215,7 +226,7 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
           break;
         }
         mbar_arrive_expect_tx(&sh->a_full[s], gm::A_BYTES);
-        tma_load_2d(smem + s * gm::STAGE, &amap, kb * gm::BK, m0, &sh->a_full[s]);
+        tma_load_2d(smem + s * T::STAGE, &amap, kb * gm::BK, m0, &sh->a_full[s]);
         issued = kb + 1;
       }
       for (int kb = issued - 1; kb >= 0 && kb >= issued - gm::STAGES; --kb) {
@@ -235,11 +246,11 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t abase = smem_u32(smem + s * gm::STAGE);
+        const uint32_t abase = smem_u32(smem + s * T::STAGE);
         const uint32_t bbase = abase + gm::A_BYTES;
 #pragma unroll
         for (int ks = 0; ks < gm::BK / 16; ++ks)
-          mma_f16(tmem, smem_desc(abase + ks * 32), smem_desc(bbase + ks * 32), (kb | ks) != 0);
+          mma_f16(tmem, smem_desc(abase + ks * 32), smem_desc(bbase + ks * 32), T::IDESC, (kb | ks) != 0);
         mma_commit(&sh->empty[s]);
       }
       // completes once every MMA issued so far has finished (also on abort, so that the tensor
@@ -257,12 +268,12 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
         *abort = 1;
         break;
       }
-      unsigned char* st = smem + s * gm::STAGE;
+      unsigned char* st = smem + s * T::STAGE;
       unsigned char* Bs = st + gm::A_BYTES;
-      const unsigned char* Rw = rawring + r * gm::RAW_BYTES;
+      const unsigned char* Rw = rawring + r * T::RAW_BYTES;
       const int kt0 = kb * 2;
 #pragma unroll 4
-      for (int q = t; q < gm::BN / 64 * 2 * 128; q += gm::CONV) {
+      for (int q = t; q < T::BN / 64 * 2 * 128; q += gm::CONV) {
         const int u = q >> 7, rbi = u >> 1, kti = u & 1;
         const int w = (q >> 5) & 3, ln = q & 31, g = ln >> 2, t4 = ln & 3;
         const int nb = rbi * 64 + w * 16 + g;                 // row of the B slice (and nb + 8)
@@ -303,7 +314,7 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
     } else {
       const int m = m0 + warp * 32 + lane;
 #pragma unroll 1
-      for (int c0 = 0; c0 < gm::BN; c0 += 32) {
+      for (int c0 = 0; c0 < T::BN; c0 += 32) {
         uint32_t v[32];
         tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
         if (m >= a.NB) continue;
@@ -349,13 +360,17 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
   __syncthreads();
   if (warp == gm::MMA_WARP) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(gm::TMEM_COLS) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(T::TMEM_COLS) : "memory");
   }
 }
 
-size_t gemm_tc_smem_bytes() {
-  return (size_t)gm::STAGES * gm::STAGE + (size_t)gm::RSTAGES * gm::RAW_BYTES + sizeof(GemmShared) + 1024;
+template <int BNV>
+static size_t smem_for() {
+  using T = Gt<BNV>;
+  return (size_t)gm::STAGES * T::STAGE + (size_t)gm::RSTAGES * T::RAW_BYTES + sizeof(GemmShared) + 1024;
 }
+
+size_t gemm_tc_smem_bytes() { return smem_for<256>(); }
 
 // cuTensorMapEncodeTiled, resolved through the runtime at first use: the library does not link the
 // driver library, so it loads (and exports its symbols) on hosts without a GPU driver
@@ -400,14 +415,27 @@ cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
   a.Np = (a.N + 63) / 64 * 64;
   CUtensorMap amap;
   if (!make_amap(a, &amap)) return cudaErrorInvalidValue;
-  const int MT = (a.NB + gm::BM - 1) / gm::BM, NT = (a.N + gm::BN - 1) / gm::BN;
-  const size_t smem = gemm_tc_smem_bytes();
-  void* fn = i4 ? (void*)gemm_tc_kernel<true> : (void*)gemm_tc_kernel<false>;
-  static bool attr[2] = {false, false};
-  if (!attr[i4]) {
+  // 128-column tiles when 256-column ones would leave SMs idle (few output tiles: the prompt-sized
+  // qkv / o / down shapes), 256 otherwise (half the A re-reads per output)
+  static const int sms = [] {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+  }();
+  static const int narrow_ok = env_int("AF_GEMM_NARROW", 1);
+  const int MT = (a.NB + gm::BM - 1) / gm::BM;
+  const bool narrow = narrow_ok == 2 || (narrow_ok && MT * ((a.N + 255) / 256) < sms);
+  const int BNV = narrow ? 128 : 256;
+  const int NT = (a.N + BNV - 1) / BNV;
+  const size_t smem = narrow ? smem_for<128>() : smem_for<256>();
+  void* fn = narrow ? (i4 ? (void*)gemm_tc_kernel<true, 128> : (void*)gemm_tc_kernel<false, 128>)
+                    : (i4 ? (void*)gemm_tc_kernel<true, 256> : (void*)gemm_tc_kernel<false, 256>);
+  static bool attr[4] = {false, false, false, false};
+  if (!attr[2 * narrow + i4]) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    attr[i4] = true;
+    attr[2 * narrow + i4] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(MT * NT));
