@@ -21,6 +21,7 @@
 #include "af_common.cuh"
 #include "af_kernels.h"
 #include "attn_common.cuh"
+#include "tc_common.cuh"
 
 namespace af {
 
@@ -643,6 +644,160 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnPrefillArgs a, co
     for (int e = 0; e < EPL; ++e) a.out[(size_t)i * a.H * DH + (size_t)h * DH + lane * EPL + e] = f2h(acc[e] / l);
 }
 
+// ---- prefill causal attention on the tensor pipe (head dim 128): flash-attention style, mma.sync
+// m16n8k16 with fp32 accumulators. CTA = (head, 64 query rows), 4 warps of 16 rows. Per 64-key block
+// of the head's kv group: K and V rows staged in shared memory (rows padded to 136 halves so the
+// fragment loads hit 32 distinct banks; the GQA expansion factor applied while staging), S = Q K^T
+// (Q fragments held in registers), causal and length masks, online softmax in fp32 per row, then
+// P (rounded to fp16, the MMA operand) times V through ldmatrix.trans fragments into the fp32 output
+// accumulators.
+constexpr int FA_BQ = 64, FA_BK = 64, FA_LD = 136;
+
+AF_DEV void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+
+AF_DEV uint32_t pack_h2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__global__ void __launch_bounds__(128) attn_prefill_fa_kernel(AttnPrefillArgs a, const __half* qbuf) {
+  constexpr int DH = 128;
+  __shared__ __align__(16) __half Ks[FA_BK][FA_LD];
+  __shared__ __align__(16) __half Vs[FA_BK][FA_LD];
+  const int h = blockIdx.x, q0 = blockIdx.y * FA_BQ;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int G = a.H / a.KV, kvh = h / G;
+  const int r0 = q0 + warp * 16 + g, r1 = r0 + 8;           // this lane's two query rows
+  // Q fragments for the 8 k-steps of the head dimension
+  uint32_t qf[8][4];
+  const __half* qb = qbuf + (size_t)h * a.S * DH;
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const int c = ks * 16 + 2 * t;
+    qf[ks][0] = r0 < a.S ? *reinterpret_cast<const uint32_t*>(qb + (size_t)r0 * DH + c) : 0u;
+    qf[ks][1] = r1 < a.S ? *reinterpret_cast<const uint32_t*>(qb + (size_t)r1 * DH + c) : 0u;
+    qf[ks][2] = r0 < a.S ? *reinterpret_cast<const uint32_t*>(qb + (size_t)r0 * DH + c + 8) : 0u;
+    qf[ks][3] = r1 < a.S ? *reinterpret_cast<const uint32_t*>(qb + (size_t)r1 * DH + c + 8) : 0u;
+  }
+  float o[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) o[n][q] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const __half* kb = a.kc + (size_t)kvh * a.ldm * DH;
+  const __half* vb = a.vc + (size_t)kvh * a.ldm * DH;
+  const int last_q = min(q0 + FA_BQ, a.S) - 1;
+  for (int j0 = 0; j0 <= last_q; j0 += FA_BK) {
+    __syncthreads();                                     // the previous block's K / V are consumed
+    for (int i = threadIdx.x; i < FA_BK * (DH / 8); i += blockDim.x) {
+      const int r = i / (DH / 8), c = (i % (DH / 8)) * 8;
+      uint4 kq = make_uint4(0u, 0u, 0u, 0u), vq = make_uint4(0u, 0u, 0u, 0u);
+      if (j0 + r < a.S) {
+        kq = *reinterpret_cast<const uint4*>(kb + (size_t)(j0 + r) * DH + c);
+        vq = *reinterpret_cast<const uint4*>(vb + (size_t)(j0 + r) * DH + c);
+        if (a.expand) {
+          __half* kh = reinterpret_cast<__half*>(&kq);
+          __half* vh = reinterpret_cast<__half*>(&vq);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            kh[e] = f2h(round_f16(a.kv_c * h2f(kh[e])));
+            vh[e] = f2h(round_f16(a.kv_c * h2f(vh[e])));
+          }
+        }
+      }
+      *reinterpret_cast<uint4*>(&Ks[r][c]) = kq;
+      *reinterpret_cast<uint4*>(&Vs[r][c]) = vq;
+    }
+    __syncthreads();
+    // S = Q K^T for this warp's 16 rows x 64 keys
+    float sc[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) sc[n][q] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&Ks[n * 8 + g][ks * 16 + 2 * t]);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&Ks[n * 8 + g][ks * 16 + 8 + 2 * t]);
+        mma_16816(sc[n], qf[ks], b0, b1);
+      }
+    }
+    // scale, causal / length mask, block row maxima
+    float bm0 = -INFINITY, bm1 = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int j = j0 + n * 8 + 2 * t + e;
+        const float s0 = (j <= r0 && j < a.S) ? sc[n][e] * a.scale : -INFINITY;
+        const float s1 = (j <= r1 && j < a.S) ? sc[n][2 + e] * a.scale : -INFINITY;
+        sc[n][e] = s0; sc[n][2 + e] = s1;
+        bm0 = fmaxf(bm0, s0); bm1 = fmaxf(bm1, s1);
+      }
+    }
+#pragma unroll
+    for (int off = 1; off <= 2; off <<= 1) {
+      bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, off));
+      bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, off));
+    }
+    const float mn0 = fmaxf(m0, bm0), mn1 = fmaxf(m1, bm1);
+    const float c0 = mn0 == -INFINITY ? 1.f : expf(m0 - mn0);
+    const float c1 = mn1 == -INFINITY ? 1.f : expf(m1 - mn1);
+    float ps0 = 0.f, ps1 = 0.f;
+    uint32_t pf[4][4];                                   // P as fp16 A fragments, 4 k-steps of 16 keys
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const float p00 = sc[n][0] == -INFINITY ? 0.f : expf(sc[n][0] - mn0);
+      const float p01 = sc[n][1] == -INFINITY ? 0.f : expf(sc[n][1] - mn0);
+      const float p10 = sc[n][2] == -INFINITY ? 0.f : expf(sc[n][2] - mn1);
+      const float p11 = sc[n][3] == -INFINITY ? 0.f : expf(sc[n][3] - mn1);
+      ps0 += p00 + p01; ps1 += p10 + p11;
+      pf[n >> 1][(n & 1) * 2 + 0] = pack_h2(p00, p01);
+      pf[n >> 1][(n & 1) * 2 + 1] = pack_h2(p10, p11);
+    }
+#pragma unroll
+    for (int off = 1; off <= 2; off <<= 1) {
+      ps0 += __shfl_xor_sync(0xffffffffu, ps0, off);
+      ps1 += __shfl_xor_sync(0xffffffffu, ps1, off);
+    }
+    l0 = l0 * c0 + ps0; l1 = l1 * c1 + ps1;
+    m0 = mn0; m1 = mn1;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) { o[n][0] *= c0; o[n][1] *= c0; o[n][2] *= c1; o[n][3] *= c1; }
+    // O += P V: for key step ks, dh tiles n (8 columns each) via ldmatrix.trans of V rows
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+      for (int n = 0; n < 16; n += 2) {
+        // matrices: (keys ks*16 + 0..7, dh n*8..), (keys +8..15, dh n*8..), (keys 0..7, dh (n+1)*8..), (keys 8..15, dh (n+1)*8..)
+        const int mi = lane >> 3, rr = lane & 7;
+        const int key = ks * 16 + (mi & 1) * 8 + rr;
+        const int col = (n + (mi >> 1)) * 8;
+        uint32_t b00, b01, b10, b11;
+        ldsm_x4_trans((uint32_t)__cvta_generic_to_shared(&Vs[key][col]), b00, b01, b10, b11);
+        // a k-step's A fragment: {a0, a1, a2, a3} = {P[g][2t..], P[g+8][2t..], P[g][8+2t..], P[g+8][8+2t..]}
+        const uint32_t A[4] = {pf[ks][0], pf[ks][1], pf[ks][2], pf[ks][3]};
+        mma_16816(o[n], A, b00, b01);
+        mma_16816(o[n + 1], A, b10, b11);
+      }
+    }
+  }
+  // normalise and store [S][H * DH] fp16
+  const float il0 = l0 > 0.f ? 1.f / l0 : 0.f, il1 = l1 > 0.f ? 1.f / l1 : 0.f;
+#pragma unroll
+  for (int n = 0; n < 16; ++n) {
+    const int c = h * DH + n * 8 + 2 * t;
+    if (r0 < a.S)
+      *reinterpret_cast<__half2*>(a.out + (size_t)r0 * a.H * DH + c) = __floats2half2_rn(o[n][0] * il0, o[n][1] * il0);
+    if (r1 < a.S)
+      *reinterpret_cast<__half2*>(a.out + (size_t)r1 * a.H * DH + c) = __floats2half2_rn(o[n][2] * il1, o[n][3] * il1);
+  }
+}
+
 cudaError_t rope_kv_prefill_launch(const AttnPrefillArgs& a, __half* qbuf, cudaStream_t st) {
   if (a.S <= 0 || a.KV <= 0 || a.H % a.KV) return cudaErrorInvalidValue;
   dim3 grid(a.S, a.H + a.KV);
@@ -657,6 +812,11 @@ cudaError_t rope_kv_prefill_launch(const AttnPrefillArgs& a, __half* qbuf, cudaS
 }
 
 cudaError_t attn_prefill_with_q(const AttnPrefillArgs& a, const __half* qbuf, cudaStream_t st) {
+  static const int fa = env_int("AF_PREFILL_FA", 1);
+  if (fa && a.dh == 128 && a.S >= 16) {
+    attn_prefill_fa_kernel<<<dim3(a.H, (a.S + FA_BQ - 1) / FA_BQ), 128, 0, st>>>(a, qbuf);
+    return cudaGetLastError();
+  }
   dim3 grid(a.H, (a.S + 3) / 4);
   switch (a.dh) {
     case 16: attn_prefill_kernel<16><<<grid, 128, 0, st>>>(a, qbuf); break;

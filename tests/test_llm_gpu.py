@@ -81,6 +81,24 @@ def test_generate_matches_reference_golden(tag):
   m.release()
 
 
+@pytest.mark.parametrize("S", [16, 150])
+def test_long_prompt_prefill_tensor_core_attention(S):
+  """Prefill over several 64-row query tiles and 64-key blocks with a ragged tail (head dim 128,
+  GQA 4:1): the tensor-core causal attention against the oracle's prefill at device precision."""
+  from aneforge_b200.llm import LlamaPrefill
+  cfg = Config(dim=1024, n_layers=2, n_heads=8, n_kv_heads=2, ffn_dim=2048, vocab=2048, rope_base=500000.0)
+  w = random_llama_weights(cfg, seed=21)
+  m = LlamaPrefill(to_b200_cfg(cfg), w, compress="int8")
+  prompt = list(np.random.default_rng(22).integers(0, cfg.vocab, S))
+  pl = m.prefill(prompt)[0]
+  om = OracleModel(cfg, w, "int8", precision="device")
+  hid, _ = om.prefill_hidden(prompt)
+  ol = om.logits(hid[-1].astype(F32))
+  assert np.abs(pl - ol).max() <= 1e-2 * np.abs(ol).max()
+  assert cosine(pl, ol) > 0.9999
+  m.release()
+
+
 def test_sampled_and_on_token_paths():
   from aneforge_b200.llm import LlamaPrefill
   cfg, w, z = llm_case("int8")
