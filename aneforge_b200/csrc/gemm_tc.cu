@@ -40,6 +40,7 @@ constexpr int B_BYTES = BN * BK * 2;          // 32 KB
 constexpr int RAW_BYTES = (BN / 64) * 2 * tc::UNIT;   // 16 KB: raw int8 units of one slice (int4: less)
 constexpr int STAGE = A_BYTES + B_BYTES;      // one slice's MMA operands
 constexpr int RSTAGES = 4;                    // raw weight ring, ahead of the operand ring
+constexpr int MAX_STAGES = 6, MAX_RSTAGES = 4;  // ring depths a kernel variant may use (below)
 constexpr int CONV = 384;                     // warps 0-11 convert (three per SM sub-partition, to hide
                                               // each other's latency); warps 0-3 then run the epilogue
 constexpr int MMA_WARP = CONV / 32;           // TMEM owner, MMA issuer
@@ -64,11 +65,11 @@ struct Gt {
 };
 
 struct GemmShared {
-  uint64_t raw_full[gm::RSTAGES];             // raw weight units landed (copy bytes)
-  uint64_t raw_empty[gm::RSTAGES];            // the converters are done with them
-  uint64_t a_full[gm::STAGES];                // A tile landed (TMA bytes)
-  uint64_t full[gm::STAGES];                  // fp16 B slice written (converters)
-  uint64_t empty[gm::STAGES];                 // the slice's MMAs finished reading (tcgen05.commit)
+  uint64_t raw_full[gm::MAX_RSTAGES];         // raw weight units landed (copy bytes)
+  uint64_t raw_empty[gm::MAX_RSTAGES];        // the converters are done with them
+  uint64_t a_full[gm::MAX_STAGES];            // A tile landed (TMA bytes)
+  uint64_t full[gm::MAX_STAGES];              // fp16 B slice written (converters)
+  uint64_t empty[gm::MAX_STAGES];             // the slice's MMAs finished reading (tcgen05.commit)
   uint64_t accum;
   uint32_t tmem;
   int abort;
@@ -138,15 +139,20 @@ AF_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int k0, int m0, uint6
       ::"r"(smem_u32(dst)), "l"(map), "r"(k0), "r"(m0), "r"(smem_u32(bar)) : "memory");
 }
 
-template <bool I4, int BNV>
+// NS = operand ring depth (A + converted B slices), NR = raw weight ring depth. One k-slice takes
+// about the same time whatever the tile width (the wait from a slice's MMA completion through the
+// next A load / conversion of that slot to its MMA dominates), so a deeper operand ring is what
+// speeds up a tile: 128-column tiles fit six slices in shared memory, 256-column tiles three.
+template <bool I4, int BNV, int NS, int NR>
 __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, const __grid_constant__ CUtensorMap amap) {
+  static_assert(NS <= gm::MAX_STAGES && NR <= gm::MAX_RSTAGES, "ring deeper than the barrier arrays");
   using T = Gt<BNV>;
   extern __shared__ unsigned char smem_raw[];
   // the swizzled slices need 1024-byte aligned bases
   const uint32_t raw = smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
-  unsigned char* rawring = smem + gm::STAGES * T::STAGE;
-  GemmShared* sh = reinterpret_cast<GemmShared*>(rawring + gm::RSTAGES * T::RAW_BYTES);
+  unsigned char* rawring = smem + NS * T::STAGE;
+  GemmShared* sh = reinterpret_cast<GemmShared*>(rawring + NR * T::RAW_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int MT = (a.NB + gm::BM - 1) / gm::BM;
   const int mt = blockIdx.x % MT, nt = blockIdx.x / MT;     // M fastest: CTAs sharing a weight tile run together
@@ -156,11 +162,11 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
   constexpr int UNIT = I4 ? tc::UNIT4 : tc::UNIT;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < gm::RSTAGES; ++s) {
+    for (int s = 0; s < NR; ++s) {
       mbar_init(&sh->raw_full[s], 1);
       mbar_init(&sh->raw_empty[s], gm::CONV);
     }
-    for (int s = 0; s < gm::STAGES; ++s) {
+    for (int s = 0; s < NS; ++s) {
       mbar_init(&sh->a_full[s], 1);
       mbar_init(&sh->full[s], gm::CONV);
       mbar_init(&sh->empty[s], 1);
@@ -187,9 +193,9 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
       const char* W = reinterpret_cast<const char*>(a.w);
       int issued = 0;
       for (int kb = 0; kb < KB; ++kb) {
-        const int r = kb % gm::RSTAGES;
-        if (kb >= gm::RSTAGES &&
-            !gm_wait(&sh->raw_empty[r], (uint32_t)(((kb / gm::RSTAGES) - 1) & 1), abort)) {
+        const int r = kb % NR;
+        if (kb >= NR &&
+            !gm_wait(&sh->raw_empty[r], (uint32_t)(((kb / NR) - 1) & 1), abort)) {
           *abort = 1;
           break;
         }
@@ -207,10 +213,10 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
         issued = kb + 1;
       }
       // shared memory must outlive every copy issued: wait (time-bounded only) for the last ones
-      for (int kb = issued - 1; kb >= 0 && kb >= issued - gm::RSTAGES; --kb) {
-        const int r = kb % gm::RSTAGES;
+      for (int kb = issued - 1; kb >= 0 && kb >= issued - NR; --kb) {
+        const int r = kb % NR;
         for (long long i = 0;
-             i < gm::LIMIT && !mbar_try_wait(&sh->raw_full[r], (uint32_t)((kb / gm::RSTAGES) & 1)); ++i) {
+             i < gm::LIMIT && !mbar_try_wait(&sh->raw_full[r], (uint32_t)((kb / NR) & 1)); ++i) {
         }
       }
     }
@@ -220,8 +226,8 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
       pdl_wait();                                     // A is the preceding kernel's output
       int issued = 0;
       for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % gm::STAGES;
-        if (kb >= gm::STAGES && !gm_wait(&sh->empty[s], (uint32_t)(((kb / gm::STAGES) - 1) & 1), abort)) {
+        const int s = kb % NS;
+        if (kb >= NS && !gm_wait(&sh->empty[s], (uint32_t)(((kb / NS) - 1) & 1), abort)) {
           *abort = 1;
           break;
         }
@@ -229,9 +235,9 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
         tma_load_2d(smem + s * T::STAGE, &amap, kb * gm::BK, m0, &sh->a_full[s]);
         issued = kb + 1;
       }
-      for (int kb = issued - 1; kb >= 0 && kb >= issued - gm::STAGES; --kb) {
-        const int s = kb % gm::STAGES;
-        for (long long i = 0; i < gm::LIMIT && !mbar_try_wait(&sh->a_full[s], (uint32_t)((kb / gm::STAGES) & 1)); ++i) {
+      for (int kb = issued - 1; kb >= 0 && kb >= issued - NS; --kb) {
+        const int s = kb % NS;
+        for (long long i = 0; i < gm::LIMIT && !mbar_try_wait(&sh->a_full[s], (uint32_t)((kb / NS) & 1)); ++i) {
         }
       }
     }
@@ -239,9 +245,9 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
     // ---------------------------------------------------------------- MMA issuer (one thread)
     if (lane == 0) {
       for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % gm::STAGES;
-        if (!gm_wait(&sh->a_full[s], (uint32_t)((kb / gm::STAGES) & 1), abort) ||
-            !gm_wait(&sh->full[s], (uint32_t)((kb / gm::STAGES) & 1), abort)) {
+        const int s = kb % NS;
+        if (!gm_wait(&sh->a_full[s], (uint32_t)((kb / NS) & 1), abort) ||
+            !gm_wait(&sh->full[s], (uint32_t)((kb / NS) & 1), abort)) {
           *abort = 1;
           break;
         }
@@ -261,10 +267,10 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
     // ---------------------------------------------------------------- converters (warps 0-3)
     const int t = threadIdx.x;
     for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % gm::STAGES, r = kb % gm::RSTAGES;
+      const int s = kb % NS, r = kb % NR;
       // the raw units landed, and the MMAs of the slice that last used this B slot are done
-      if (!gm_wait(&sh->raw_full[r], (uint32_t)((kb / gm::RSTAGES) & 1), abort) ||
-          (kb >= gm::STAGES && !gm_wait(&sh->empty[s], (uint32_t)(((kb / gm::STAGES) - 1) & 1), abort))) {
+      if (!gm_wait(&sh->raw_full[r], (uint32_t)((kb / NR) & 1), abort) ||
+          (kb >= NS && !gm_wait(&sh->empty[s], (uint32_t)(((kb / NS) - 1) & 1), abort))) {
         *abort = 1;
         break;
       }
@@ -364,13 +370,13 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
   }
 }
 
-template <int BNV>
+template <int BNV, int NS, int NR>
 static size_t smem_for() {
   using T = Gt<BNV>;
-  return (size_t)gm::STAGES * T::STAGE + (size_t)gm::RSTAGES * T::RAW_BYTES + sizeof(GemmShared) + 1024;
+  return (size_t)NS * T::STAGE + (size_t)NR * T::RAW_BYTES + sizeof(GemmShared) + 1024;
 }
 
-size_t gemm_tc_smem_bytes() { return smem_for<256>(); }
+size_t gemm_tc_smem_bytes() { return smem_for<256, gm::STAGES, gm::RSTAGES>(); }
 
 // cuTensorMapEncodeTiled, resolved through the runtime at first use: the library does not link the
 // driver library, so it loads (and exports its symbols) on hosts without a GPU driver
@@ -428,14 +434,23 @@ cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
   const bool narrow = narrow_ok == 2 || (narrow_ok && MT * ((a.N + 255) / 256) < sms);
   const int BNV = narrow ? 128 : 256;
   const int NT = (a.N + BNV - 1) / BNV;
-  const size_t smem = narrow ? smem_for<128>() : smem_for<256>();
-  void* fn = narrow ? (i4 ? (void*)gemm_tc_kernel<true, 128> : (void*)gemm_tc_kernel<false, 128>)
-                    : (i4 ? (void*)gemm_tc_kernel<true, 256> : (void*)gemm_tc_kernel<false, 256>);
-  static bool attr[4] = {false, false, false, false};
-  if (!attr[2 * narrow + i4]) {
+  // ring depths: 128-column tiles run six operand slices (AF_GEMM_DEEP=0: three, as 256-column
+  // tiles do; a 256-column variant with four operand and two raw slices measured slower)
+  static const int deep = env_int("AF_GEMM_DEEP", 1);
+  const int var = narrow ? (deep >= 1 ? 1 : 0) : 2;
+  static const size_t smems[3] = {smem_for<128, 3, 4>(), smem_for<128, 6, 4>(), smem_for<256, 3, 4>()};
+  void* const fns[2][3] = {
+      {(void*)gemm_tc_kernel<false, 128, 3, 4>, (void*)gemm_tc_kernel<false, 128, 6, 4>,
+       (void*)gemm_tc_kernel<false, 256, 3, 4>},
+      {(void*)gemm_tc_kernel<true, 128, 3, 4>, (void*)gemm_tc_kernel<true, 128, 6, 4>,
+       (void*)gemm_tc_kernel<true, 256, 3, 4>}};
+  const size_t smem = smems[var];
+  void* fn = fns[i4 ? 1 : 0][var];
+  static bool attr[2][3] = {};
+  if (!attr[i4 ? 1 : 0][var]) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    attr[2 * narrow + i4] = true;
+    attr[i4 ? 1 : 0][var] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(MT * NT));

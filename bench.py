@@ -432,6 +432,43 @@ def kernel_bench(name, reps, warmup):
   g.manual_seed(7)
   D, F, H, KV, dh, V = CFG["dim"], CFG["ffn_dim"], CFG["n_heads"], CFG["n_kv_heads"], 128, CFG["vocab"]
   st = torch.cuda.Stream(dev)
+  if name == "prefill":
+    # the whole prefill program of the selected model over its benchmark prompt (time to first hidden
+    # state: embed, per layer norm + tcgen05 GEMMs + RoPE / cache write + causal attention, final norm)
+    from aneforge_b200 import llm as L
+    spec = MODELS[MODEL]
+    mlp = "moe" if spec.get("moe") else "swiglu"
+    cfg = L.LlamaConfig(**CFG, layers=[L.LayerSpec(mlp=mlp) for _ in range(CFG["n_layers"])])
+    w = make_weights(cfg, dev, seed=1234, qkv_bias=spec["qkv_bias"], moe=bool(spec.get("moe")))
+    m = L.LlamaPrefill(cfg, w, compress=spec["compress"], device=0, moe_compress=spec.get("moe_compress", "same"))
+    m._load()
+    del w
+    torch.cuda.empty_cache()
+    ids = np.random.default_rng(99).integers(0, cfg.vocab, PROMPT).astype(np.int32)
+    pre = m._prefiller(PROMPT)
+    prog = pre["prog"]
+    prog.set_input("ids", ids)
+    for _ in range(warmup):
+      prog.execute_async()
+    prog.sync()
+    ps = torch.cuda.ExternalStream(prog.stream(), device=dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ps)
+    for _ in range(reps):
+      prog.execute_async()             # weights (GBs) exceed L2: every run streams them from HBM
+    e1.record(ps)
+    prog.sync()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    nl, hd = CFG["n_layers"], CFG.get("head_dim") or D // H
+    ex = CFG.get("extra", {}).get("n_experts_per_tok", 1) if spec.get("moe") else 1
+    lin = 2.0 * PROMPT * nl * (D * (H + 2 * KV) * hd + H * hd * D + 3 * D * F * ex)
+    att = 2.0 * nl * H * hd * PROMPT * (PROMPT + 1)      # causal QK^T + PV
+    del ps
+    m.release()
+    return {"kernel": name, "what": f"prefill program, {MODEL} {spec['compress']}, {PROMPT} tokens",
+            "ms_per_prefill": round(ms, 3), "tokens_per_s": round(PROMPT / (ms * 1e-3), 1),
+            "tflops": round((lin + att) / (ms * 1e-3) / 1e12, 1), "reps": reps, "warmup": warmup}
 
   def int8_tiles(N, Kd, copies):
     W = (torch.randn(N, Kd, generator=g, device=dev) * 0.02).half()
@@ -442,10 +479,14 @@ def kernel_bench(name, reps, warmup):
   I4 = {"gemv_i4_gu": (2 * 29568, 8192, R.EPI_SWIGLU), "gemv_i4_qkv": (80 * 128, 8192, R.EPI_F32),
         "gemv_i4_o": (8192, 8192, R.EPI_RESID), "gemv_i4_down": (8192, 29568, R.EPI_RESID),
         "gemv_i4_moe_gu": (2 * 14336, 4096, R.EPI_SWIGLU)}   # one Mixtral expert's gate|up
-  if name in ("gemm_gu", "gemm_i4_gu"):
-    # prefill: the tcgen05 GEMM over a 512-row (8B) / 2048-row (72B) prompt; FLOP-bound
+  if name in ("gemm_gu", "gemm_i4_gu", "gemm_qkv", "gemm_o", "gemm_down"):
+    # prefill: the tcgen05 GEMM over a 512-row (8B) / 2048-row (72B) prompt; FLOP-bound. qkv / o /
+    # down are the 8B prompt shapes with fewer 256-column tiles than SMs (128-column tiles)
     i4 = name == "gemm_i4_gu"
-    M, N, Kd = (2048, 2 * 29568, 8192) if i4 else (512, 2 * F, D)
+    M, N, Kd = {"gemm_gu": (512, 2 * F, D), "gemm_i4_gu": (2048, 2 * 29568, 8192),
+                "gemm_qkv": (512, (H + 2 * KV) * dh, D), "gemm_o": (512, D, H * dh),
+                "gemm_down": (512, D, F)}[name]
+    epi = R.EPI_SWIGLU if name in ("gemm_gu", "gemm_i4_gu") else R.EPI_F16
     W = (torch.randn(N, Kd, generator=g, device=dev) * 0.02).half()
     if i4:
       pk, sc = K.quantize_g32_i4(W); tiles = K.pack_i4_tiles(pk, sc, N, Kd); sc = None
@@ -453,8 +494,8 @@ def kernel_bench(name, reps, warmup):
       q, sc = K.quantize_per_row_i8(W); tiles = K.pack_i8_tiles(q)
     del W
     x = torch.randn(M, Kd, generator=g, device=dev).half()
-    y = torch.empty(M, N // 2, device=dev, dtype=torch.float16)
-    fn = lambda i: K.gemm_tc(x, tiles, sc, N, Kd, wf=R.W_I4G32 if i4 else R.W_I8, epi=R.EPI_SWIGLU, y=y)
+    y = torch.empty(M, N // 2 if epi == R.EPI_SWIGLU else N, device=dev, dtype=torch.float16)
+    fn = lambda i: K.gemm_tc(x, tiles, sc, N, Kd, wf=R.W_I4G32 if i4 else R.W_I8, epi=epi, y=y)
     flops = 2.0 * M * N * Kd
     with torch.cuda.stream(st):
       for i in range(warmup):
@@ -473,7 +514,8 @@ def kernel_bench(name, reps, warmup):
     except Exception:
       tpk, tkind = 1590.0, "fallback"
     tf = flops / (us * 1e-6) / 1e12
-    return {"kernel": name, "what": f"gemm_tc {'int4_g32' if i4 else 'int8'} M={M} N={N} K={Kd} swiglu",
+    return {"kernel": name, "what": f"gemm_tc {'int4_g32' if i4 else 'int8'} M={M} N={N} K={Kd} "
+                                    f"{'swiglu' if epi == R.EPI_SWIGLU else 'f16'}",
             "us_per_launch": round(us, 1), "tflops": round(tf, 1), "peak_tflops": tpk, "peak_kind": tkind,
             "frac": round(tf / tpk, 4), "reps": reps, "warmup": warmup}
   if name in I4:                                            # Qwen2-72B shapes, group-32 int4
@@ -631,7 +673,8 @@ def main():
   ap.add_argument("--kernel", default=None,
                   help="time one kernel alone: gemv_gu | gemv_qkv | gemv_o | gemv_down | gemv_cfg1 | attn | lm_head "
                        "| gemv_i4_gu | gemv_i4_qkv | gemv_i4_o | gemv_i4_down | gemv_i4_moe_gu | gemm_gu | gemm_i4_gu "
-                       "| rmsnorm | moe_gate")
+                       "| gemm_qkv | gemm_o | gemm_down "
+                       "| rmsnorm | moe_gate | prefill (the whole prefill program of --model)")
   ap.add_argument("--reps", type=int, default=50)
   ap.add_argument("--profile-region", action="store_true",
                   help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
