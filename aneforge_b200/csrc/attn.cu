@@ -663,11 +663,25 @@ AF_DEV uint32_t pack_h2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// 16-byte global -> shared copy that bypasses registers; src_bytes 0 writes zeros (rows past the
+// prompt: V must be 0 there, since a masked key's P of 0 times a non-finite V would not vanish)
+AF_DEV void cp_async16(void* dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+AF_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+AF_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+constexpr int FA_SMEM = 2 * 2 * FA_BK * FA_LD * 2;   // K and V, two 64-key blocks in flight: 68 KB
+
 __global__ void __launch_bounds__(128) attn_prefill_fa_kernel(AttnPrefillArgs a, const __half* qbuf) {
   constexpr int DH = 128;
-  __shared__ __align__(16) __half Ks[FA_BK][FA_LD];
-  __shared__ __align__(16) __half Vs[FA_BK][FA_LD];
-  const int h = blockIdx.x, q0 = blockIdx.y * FA_BQ;
+  extern __shared__ __align__(16) unsigned char fa_smem[];
+  __half (*Kb)[FA_BK][FA_LD] = reinterpret_cast<__half (*)[FA_BK][FA_LD]>(fa_smem);   // [2][64][136]
+  __half (*Vb)[FA_BK][FA_LD] = Kb + 2;
+  // the last query tiles see the most keys: they take the lowest block indices, so they start first
+  const int h = blockIdx.x, q0 = (gridDim.y - 1 - blockIdx.y) * FA_BQ;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int G = a.H / a.KV, kvh = h / G;
   const int r0 = q0 + warp * 16 + g, r1 = r0 + 8;           // this lane's two query rows
@@ -691,28 +705,44 @@ __global__ void __launch_bounds__(128) attn_prefill_fa_kernel(AttnPrefillArgs a,
   const __half* kb = a.kc + (size_t)kvh * a.ldm * DH;
   const __half* vb = a.vc + (size_t)kvh * a.ldm * DH;
   const int last_q = min(q0 + FA_BQ, a.S) - 1;
-  for (int j0 = 0; j0 <= last_q; j0 += FA_BK) {
-    __syncthreads();                                     // the previous block's K / V are consumed
-    for (int i = threadIdx.x; i < FA_BK * (DH / 8); i += blockDim.x) {
-      const int r = i / (DH / 8), c = (i % (DH / 8)) * 8;
-      uint4 kq = make_uint4(0u, 0u, 0u, 0u), vq = make_uint4(0u, 0u, 0u, 0u);
-      if (j0 + r < a.S) {
-        kq = *reinterpret_cast<const uint4*>(kb + (size_t)(j0 + r) * DH + c);
-        vq = *reinterpret_cast<const uint4*>(vb + (size_t)(j0 + r) * DH + c);
-        if (a.expand) {
-          __half* kh = reinterpret_cast<__half*>(&kq);
-          __half* vh = reinterpret_cast<__half*>(&vq);
+  const int nblk = last_q / FA_BK + 1;
+  // each thread copies the same 16-byte chunks of every block (i = tid + 128 k), so it can apply
+  // the expansion factor to its own chunks once they land, before the block-wide barrier
+  auto stage = [&](int blk) {
+    const int j0 = blk * FA_BK, buf = blk & 1;
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            kh[e] = f2h(round_f16(a.kv_c * h2f(kh[e])));
-            vh[e] = f2h(round_f16(a.kv_c * h2f(vh[e])));
-          }
+    for (int i = threadIdx.x; i < FA_BK * (DH / 8); i += 128) {
+      const int r = i / (DH / 8), c = (i % (DH / 8)) * 8;
+      const bool ok = j0 + r < a.S;
+      const size_t row = ok ? (size_t)(j0 + r) : 0;
+      cp_async16(&Kb[buf][r][c], kb + row * DH + c, ok ? 16 : 0);
+      cp_async16(&Vb[buf][r][c], vb + row * DH + c, ok ? 16 : 0);
+    }
+    cp_async_commit();
+  };
+  stage(0);
+  for (int blk = 0; blk < nblk; ++blk) {
+    const int j0 = blk * FA_BK, buf = blk & 1;
+    if (blk + 1 < nblk) {
+      stage(blk + 1);                                    // its buffer was released at the end of blk - 1
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    if (a.expand) {
+#pragma unroll
+      for (int i = threadIdx.x; i < FA_BK * (DH / 8); i += 128) {
+        const int r = i / (DH / 8), c = (i % (DH / 8)) * 8;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          Kb[buf][r][c + e] = f2h(round_f16(a.kv_c * h2f(Kb[buf][r][c + e])));
+          Vb[buf][r][c + e] = f2h(round_f16(a.kv_c * h2f(Vb[buf][r][c + e])));
         }
       }
-      *reinterpret_cast<uint4*>(&Ks[r][c]) = kq;
-      *reinterpret_cast<uint4*>(&Vs[r][c]) = vq;
     }
     __syncthreads();
+    __half (*Ks)[FA_LD] = Kb[buf];
+    __half (*Vs)[FA_LD] = Vb[buf];
     // S = Q K^T for this warp's 16 rows x 64 keys
     float sc[8][4];
 #pragma unroll
@@ -785,6 +815,7 @@ __global__ void __launch_bounds__(128) attn_prefill_fa_kernel(AttnPrefillArgs a,
         mma_16816(o[n + 1], A, b10, b11);
       }
     }
+    __syncthreads();                                     // every warp is done with this buffer
   }
   // normalise and store [S][H * DH] fp16
   const float il0 = l0 > 0.f ? 1.f / l0 : 0.f, il1 = l1 > 0.f ? 1.f / l1 : 0.f;
@@ -814,7 +845,10 @@ cudaError_t rope_kv_prefill_launch(const AttnPrefillArgs& a, __half* qbuf, cudaS
 cudaError_t attn_prefill_with_q(const AttnPrefillArgs& a, const __half* qbuf, cudaStream_t st) {
   static const int fa = env_int("AF_PREFILL_FA", 1);
   if (fa && a.dh == 128 && a.S >= 16) {
-    attn_prefill_fa_kernel<<<dim3(a.H, (a.S + FA_BQ - 1) / FA_BQ), 128, 0, st>>>(a, qbuf);
+    static const cudaError_t attr =
+        cudaFuncSetAttribute(attn_prefill_fa_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM);
+    if (attr != cudaSuccess) return attr;
+    attn_prefill_fa_kernel<<<dim3(a.H, (a.S + FA_BQ - 1) / FA_BQ), 128, FA_SMEM, st>>>(a, qbuf);
     return cudaGetLastError();
   }
   dim3 grid(a.H, (a.S + 3) / 4);

@@ -40,7 +40,7 @@ constexpr int B_BYTES = BN * BK * 2;          // 32 KB
 constexpr int RAW_BYTES = (BN / 64) * 2 * tc::UNIT;   // 16 KB: raw int8 units of one slice (int4: less)
 constexpr int STAGE = A_BYTES + B_BYTES;      // one slice's MMA operands
 constexpr int RSTAGES = 4;                    // raw weight ring, ahead of the operand ring
-constexpr int MAX_STAGES = 6, MAX_RSTAGES = 4;  // ring depths a kernel variant may use (below)
+constexpr int MAX_STAGES = 4, MAX_RSTAGES = 8;  // ring depths a kernel variant may use (below)
 constexpr int CONV = 384;                     // warps 0-11 convert (three per SM sub-partition, to hide
                                               // each other's latency); warps 0-3 then run the epilogue
 constexpr int MMA_WARP = CONV / 32;           // TMEM owner, MMA issuer
@@ -140,9 +140,9 @@ AF_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int k0, int m0, uint6
 }
 
 // NS = operand ring depth (A + converted B slices), NR = raw weight ring depth. One k-slice takes
-// about the same time whatever the tile width (the wait from a slice's MMA completion through the
-// next A load / conversion of that slot to its MMA dominates), so a deeper operand ring is what
-// speeds up a tile: 128-column tiles fit six slices in shared memory, 256-column tiles three.
+// about the same time (~1 µs on the 8B prompt shapes) whatever the tile width, so 128-column tiles
+// run far below the tensor pipe's rate; deeper rings recover 10-15 % of that: 128-column tiles fit
+// four operand and eight raw slices in shared memory, 256-column tiles three and four.
 template <bool I4, int BNV, int NS, int NR>
 __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, const __grid_constant__ CUtensorMap amap) {
   static_assert(NS <= gm::MAX_STAGES && NR <= gm::MAX_RSTAGES, "ring deeper than the barrier arrays");
@@ -434,15 +434,16 @@ cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
   const bool narrow = narrow_ok == 2 || (narrow_ok && MT * ((a.N + 255) / 256) < sms);
   const int BNV = narrow ? 128 : 256;
   const int NT = (a.N + BNV - 1) / BNV;
-  // ring depths: 128-column tiles run six operand slices (AF_GEMM_DEEP=0: three, as 256-column
-  // tiles do; a 256-column variant with four operand and two raw slices measured slower)
+  // ring depths: 128-column tiles run four operand and eight raw slices (AF_GEMM_DEEP=0: three and
+  // four, as 256-column tiles do). Measured on the 8B prompt shapes (qkv / o / down, µs): 3+4 143 /
+  // 69 / 162, 6+4 130 / 62 / 138, 4+8 128 / 62 / 134; for 256-column tiles 4+2 was slower than 3+4.
   static const int deep = env_int("AF_GEMM_DEEP", 1);
   const int var = narrow ? (deep >= 1 ? 1 : 0) : 2;
-  static const size_t smems[3] = {smem_for<128, 3, 4>(), smem_for<128, 6, 4>(), smem_for<256, 3, 4>()};
+  static const size_t smems[3] = {smem_for<128, 3, 4>(), smem_for<128, 4, 8>(), smem_for<256, 3, 4>()};
   void* const fns[2][3] = {
-      {(void*)gemm_tc_kernel<false, 128, 3, 4>, (void*)gemm_tc_kernel<false, 128, 6, 4>,
+      {(void*)gemm_tc_kernel<false, 128, 3, 4>, (void*)gemm_tc_kernel<false, 128, 4, 8>,
        (void*)gemm_tc_kernel<false, 256, 3, 4>},
-      {(void*)gemm_tc_kernel<true, 128, 3, 4>, (void*)gemm_tc_kernel<true, 128, 6, 4>,
+      {(void*)gemm_tc_kernel<true, 128, 3, 4>, (void*)gemm_tc_kernel<true, 128, 4, 8>,
        (void*)gemm_tc_kernel<true, 256, 3, 4>}};
   const size_t smem = smems[var];
   void* fn = fns[i4 ? 1 : 0][var];

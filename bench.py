@@ -432,13 +432,16 @@ def kernel_bench(name, reps, warmup):
   g.manual_seed(7)
   D, F, H, KV, dh, V = CFG["dim"], CFG["ffn_dim"], CFG["n_heads"], CFG["n_kv_heads"], 128, CFG["vocab"]
   st = torch.cuda.Stream(dev)
-  if name == "prefill":
+  if name in ("prefill", "prefill_1layer"):
     # the whole prefill program of the selected model over its benchmark prompt (time to first hidden
-    # state: embed, per layer norm + tcgen05 GEMMs + RoPE / cache write + causal attention, final norm)
+    # state: embed, per layer norm + tcgen05 GEMMs + RoPE / cache write + causal attention, final norm);
+    # `prefill_1layer` is one layer of it with a 4096-token vocabulary (the small case for captures
+    # of the prefill attention kernel)
     from aneforge_b200 import llm as L
     spec = MODELS[MODEL]
     mlp = "moe" if spec.get("moe") else "swiglu"
-    cfg = L.LlamaConfig(**CFG, layers=[L.LayerSpec(mlp=mlp) for _ in range(CFG["n_layers"])])
+    cd = dict(CFG, n_layers=1, vocab=4096) if name == "prefill_1layer" else CFG
+    cfg = L.LlamaConfig(**cd, layers=[L.LayerSpec(mlp=mlp) for _ in range(cd["n_layers"])])
     w = make_weights(cfg, dev, seed=1234, qkv_bias=spec["qkv_bias"], moe=bool(spec.get("moe")))
     m = L.LlamaPrefill(cfg, w, compress=spec["compress"], device=0, moe_compress=spec.get("moe_compress", "same"))
     m._load()
@@ -460,13 +463,13 @@ def kernel_bench(name, reps, warmup):
     prog.sync()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
-    nl, hd = CFG["n_layers"], CFG.get("head_dim") or D // H
+    nl, hd = cd["n_layers"], CFG.get("head_dim") or D // H
     ex = CFG.get("extra", {}).get("n_experts_per_tok", 1) if spec.get("moe") else 1
     lin = 2.0 * PROMPT * nl * (D * (H + 2 * KV) * hd + H * hd * D + 3 * D * F * ex)
     att = 2.0 * nl * H * hd * PROMPT * (PROMPT + 1)      # causal QK^T + PV
     del ps
     m.release()
-    return {"kernel": name, "what": f"prefill program, {MODEL} {spec['compress']}, {PROMPT} tokens",
+    return {"kernel": name, "what": f"prefill program, {MODEL} {spec['compress']}, {nl} layers, {PROMPT} tokens",
             "ms_per_prefill": round(ms, 3), "tokens_per_s": round(PROMPT / (ms * 1e-3), 1),
             "tflops": round((lin + att) / (ms * 1e-3) / 1e12, 1), "reps": reps, "warmup": warmup}
 
@@ -674,7 +677,7 @@ def main():
                   help="time one kernel alone: gemv_gu | gemv_qkv | gemv_o | gemv_down | gemv_cfg1 | attn | lm_head "
                        "| gemv_i4_gu | gemv_i4_qkv | gemv_i4_o | gemv_i4_down | gemv_i4_moe_gu | gemm_gu | gemm_i4_gu "
                        "| gemm_qkv | gemm_o | gemm_down "
-                       "| rmsnorm | moe_gate | prefill (the whole prefill program of --model)")
+                       "| rmsnorm | moe_gate | prefill (the whole prefill program of --model) | prefill_1layer")
   ap.add_argument("--reps", type=int, default=50)
   ap.add_argument("--profile-region", action="store_true",
                   help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
