@@ -82,9 +82,36 @@ def decide_kind(W, compress, atol=0.05, block_size=32) -> str:
     pass
   Wh = W.detach().float().cpu().numpy() if hasattr(W, "detach") else np.asarray(W, F32)
   kind, _ = _blob.decide(Wh, compress, atol, block_size)
+  return kind
+
+
+# encodings with no packed device format yet: the device multiplies by their decoded values,
+# stored as an fp16 matrix and run on the fp16-weight kernels. An accepted LUT4 weight and a sparse
+# weight decode to fp16 values exactly, so these match the reference's arithmetic; a blockwise
+# weight's int8 x fp16-scale product is rounded to fp16 once (the reference keeps it at the
+# operand precision of its matmul, fp16 on the ANE). They stream 2 bytes per weight, not 0.5 / 1.
+DENSE_KINDS = ("lut4", "blockwise", "sparse")
+
+
+def _decoded_fp16(W, compress, atol, block_size):
+  """(kind, fp32 matrix of decoded values or None) for one weight: None for the kinds the
+  device quantizes itself (int8, int4_g32, fp16)."""
+  if compress in (None, "int8", "int4_g32"):
+    return decide_kind(W, compress, atol, block_size), None
+  Wh = W.detach().float().cpu().numpy() if hasattr(W, "detach") else np.asarray(W, F32)
+  W2 = Wh.reshape(Wh.shape[0], -1)
+  kind, payload = _blob.decide(Wh, compress, atol, block_size)
+  if kind == "lut4":
+    return kind, _blob.lut4_dense(W2, *payload).reshape(Wh.shape)
+  if kind == "blockwise":
+    q, sc, nb = payload
+    OUT, IN = W2.shape
+    return kind, (q.astype(F32).reshape(OUT, nb, IN // nb) * sc.astype(F32)[:, :, None]).reshape(Wh.shape)
+  if kind == "sparse":
+    return kind, np.asarray(Wh, np.float16).astype(F32)
   if kind not in ("int8", "fp16", "int4_g32"):
     raise NotImplementedError(f"compress={compress!r}: the {kind} device decoder is not built yet")
-  return kind
+  return kind, None
 
 
 def _quantize(W, kind, device):
@@ -106,10 +133,20 @@ def encode_linear(parts, compress, device, biases=None, swiglu=False, atol=0.05,
   `swiglu=True` takes (gate, up) and interleaves them for the fused silu(gate)*up epilogue;
   otherwise the rows are concatenated (q|k|v)."""
   torch = torch_mod()
-  kinds = {decide_kind(P, compress, atol, block_size) for P in parts}
+  dec = [_decoded_fp16(P, compress, atol, block_size) for P in parts]
+  # a decoded encoding runs as an fp16 matrix of its values (DENSE_KINDS)
+  kinds = {"fp16" if k in DENSE_KINDS else k for k, _ in dec}
+  if len(kinds) > 1 and "fp16" in kinds:
+    # parts of one fused projection that the reference encodes differently (e.g. an accepted LUT
+    # for q, per-row int8 for k): all parts run as fp16 matrices of their decoded values
+    dec = [(k, d) if d is not None else ("fp16", _blob.dense_of(
+        P.detach().float().cpu().numpy() if hasattr(P, "detach") else np.asarray(P, F32), compress,
+        compress_atol=atol, block_size=block_size)) for P, (k, d) in zip(parts, dec)]
+    kinds = {"fp16"}
   if len(kinds) != 1:
-    raise NotImplementedError(f"fused projection parts encode differently: {sorted(kinds)}")
+    raise NotImplementedError(f"fused projection parts encode differently: {sorted(k for k, _ in dec)}")
   kind = kinds.pop()
+  parts = [P if d is None else torch.from_numpy(np.ascontiguousarray(d)) for P, (_, d) in zip(parts, dec)]
   K = int(parts[0].shape[1])
   enc = [_quantize(P, kind, device) for P in parts]
   if swiglu:

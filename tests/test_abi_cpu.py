@@ -74,6 +74,33 @@ def test_package_encoding_policy_matches_reference(name, mode):
   np.testing.assert_array_equal(_blob.dense_of(M, comp).astype(F32), qz[f"enc_{name}_{mode}_deq"])
 
 
+@pytest.mark.parametrize("mode", ["int4", "blockwise", "sparse"])
+def test_decoded_encodings_match_oracle_values(mode):
+  """Encodings with no packed device format (an accepted LUT4, blockwise, sparse) run as fp16
+  matrices of their decoded values: those values must be the oracle's dequantized matrix
+  (exactly for LUT4 and sparse; blockwise within one fp16 rounding)."""
+  from aneforge_b200 import weights as W
+  from oracle.quant import encode_weight
+  rng = np.random.default_rng(5)
+  if mode == "int4":
+    lut = np.linspace(-0.05, 0.05, 16).astype(np.float16)
+    A = lut[rng.integers(0, 16, (48, 96))].astype(np.float32)
+  elif mode == "sparse":
+    A = rng.normal(0, 0.02, (48, 96)).astype(np.float32) * (rng.random((48, 96)) < 0.3)
+  else:
+    A = rng.normal(0, 0.02, (48, 96)).astype(np.float32)
+  kind, dense = W._decoded_fp16(A, mode, 0.05, 32)
+  ref = encode_weight(A, mode, 0.05, 32)
+  assert kind == ref.kind == {"int4": "lut4", "blockwise": "blockwise", "sparse": "sparse"}[mode]
+  if mode == "blockwise":
+    assert np.allclose(dense, ref.deq, rtol=2 ** -10, atol=0)
+  else:
+    assert np.array_equal(dense, ref.deq) and np.array_equal(dense.astype(np.float16).astype(np.float32), dense)
+  # a near-Gaussian weight under "int4" is rejected by the LUT gate and stays per-row int8
+  g = rng.normal(0, 0.02, (48, 96)).astype(np.float32)
+  assert W._decoded_fp16(g, "int4", 0.05, 32) == ("int8", None)
+
+
 def test_gqa_expand_factor():
   from aneforge_b200 import _blob
   assert _blob.gqa_expand_factor(8, 4, "int8") == 127 * float(np.float16(1 / 127))

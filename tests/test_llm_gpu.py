@@ -99,6 +99,46 @@ def test_long_prompt_prefill_tensor_core_attention(S):
   m.release()
 
 
+@pytest.mark.parametrize("mixed", [False, True])
+def test_lut4_weights_run_decoded_on_fp16_path(mixed):
+  """compress="int4" on weights the reference's LUT gate accepts: the accepted LUT4 matrices run
+  as fp16 matrices of their codebook values (with `mixed`, k stays Gaussian and per-row int8, so
+  the fused q|k|v falls back to decoded fp16 for all three parts). Same bars as the golden tests."""
+  from aneforge_b200.llm import LlamaPrefill
+  cfg = Config(dim=256, n_layers=2, n_heads=4, n_kv_heads=2, ffn_dim=512, vocab=512, rope_base=10000.0,
+               head_dim=64)
+  w = random_llama_weights(cfg, seed=31, std=0.05)
+  rng = np.random.default_rng(32)
+  # 12 distinct values: the reference's 16-centre k-means reproduces them exactly, so the gate accepts
+  lut = np.linspace(-0.1, 0.1, 12).astype(F16)
+  for lw in w["layers"]:
+    for k in ("wq", "wk", "wv", "wo", "wgate", "wup", "wdown"):
+      if not (mixed and k == "wk"):
+        lw[k] = lut[rng.integers(0, 12, lw[k].shape)]
+  from aneforge_b200.weights import _decoded_fp16
+  parts = {"qkv": ("wq", "wk", "wv"), "o": ("wo",), "gu": ("wgate", "wup"), "down": ("wdown",)}
+  m = LlamaPrefill(to_b200_cfg(cfg), w, compress="int4")
+  dl = m._load()["layers"]
+  n_lut = 0
+  for i in range(2):
+    for proj, names in parts.items():
+      kinds = [_decoded_fp16(w["layers"][i][n], "int4", 0.05, 32)[0] for n in names]
+      n_lut += kinds.count("lut4")
+      # a projection with any accepted LUT part runs decoded in fp16; the rest stay per-row int8
+      assert dl[i][proj].wf == ("f16" if "lut4" in kinds else "i8t"), (i, proj, kinds)
+  assert n_lut >= 8
+  prompt = list(np.random.default_rng(33).integers(0, cfg.vocab, 40))
+  toks = m.generate(prompt, 16, max_len=64)
+  om = OracleModel(cfg, w, "int4", precision="device")
+  assert teacher_forced_check(om, prompt, toks, 64, n_check=16) <= 1
+  pl = m.prefill(prompt)[0]
+  hid, _ = om.prefill_hidden(prompt)
+  ol = om.logits(hid[-1].astype(F32))
+  assert np.abs(pl - ol).max() <= 1e-2 * np.abs(ol).max()
+  assert cosine(pl, ol) > 0.999
+  m.release()
+
+
 def test_sampled_and_on_token_paths():
   from aneforge_b200.llm import LlamaPrefill
   cfg, w, z = llm_case("int8")
