@@ -431,7 +431,11 @@ cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
   }();
   static const int narrow_ok = env_int("AF_GEMM_NARROW", 1);
   const int MT = (a.NB + gm::BM - 1) / gm::BM;
-  const bool narrow = narrow_ok == 2 || (narrow_ok && MT * ((a.N + 255) / 256) < sms);
+  // 128-column tiles only where they add no wave: twice the tiles must fit in as many waves of
+  // `sms` CTAs as the 256-column tiles (AF_GEMM_NARROW: 0 never, 2 always, 1 this rule)
+  const int wide_tiles = MT * ((a.N + 255) / 256), narrow_tiles = MT * ((a.N + 127) / 128);
+  const bool narrow = narrow_ok == 2 || (narrow_ok == 1 && wide_tiles < sms &&
+                                         (narrow_tiles + sms - 1) / sms == (wide_tiles + sms - 1) / sms);
   const int BNV = narrow ? 128 : 256;
   const int NT = (a.N + BNV - 1) / BNV;
   // ring depths: 128-column tiles run four operand and eight raw slices (AF_GEMM_DEEP=0: three and
