@@ -63,8 +63,6 @@ SIGNATURES = [
   ("af_pack_i4_tiles", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
   ("af_gemv_tc_i4", c_int, [c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                             c_void_p, c_size_t, c_void_p]),
-  ("af_decode_mk_scratch", c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
-                                   ctypes.POINTER(c_size_t), ctypes.POINTER(c_size_t)]),
   ("af_comm_unique_id", c_int, [c_void_p, c_size_t]),
   ("af_comm_init", c_int, [c_void_p, c_int, c_int, c_int, ctypes.POINTER(c_void_p)]),
   ("af_comm_destroy", None, [c_void_p]),

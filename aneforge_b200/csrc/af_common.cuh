@@ -19,6 +19,72 @@ AF_DEV void af_set_err(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
+// ---- host: per-device caches. Kernel attributes (cudaFuncSetAttribute) belong to the current
+// device's context, and occupancy answers are per device too, so every cache of them is keyed by
+// the device ordinal; one mutex per cache makes concurrent first calls from several host threads
+// safe (later calls read the value behind an acquire load, without the lock).
+#ifndef __CUDACC_RTC__
+#include <atomic>
+#include <mutex>
+namespace af {
+constexpr int kMaxDevices = 64;
+
+inline int current_device() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= kMaxDevices) d = 0;
+  return d;
+}
+
+// `fn()` (returning cudaError_t) runs once per device until it succeeds; a failure is returned and
+// retried on the next call.
+struct PerDeviceOnce {
+  std::atomic<int> done[kMaxDevices] = {};
+  std::mutex mu;
+  template <class F> cudaError_t run(F&& fn) {
+    const int d = current_device();
+    if (done[d].load(std::memory_order_acquire)) return cudaSuccess;
+    std::lock_guard<std::mutex> g(mu);
+    if (done[d].load(std::memory_order_relaxed)) return cudaSuccess;
+    const cudaError_t e = fn();
+    if (e == cudaSuccess) done[d].store(1, std::memory_order_release);
+    return e;
+  }
+};
+
+// A value computed once per device and key slot (`fn()` returns it; 0 means "not computed").
+template <int SLOTS> struct PerDeviceInt {
+  std::atomic<int> v[kMaxDevices][SLOTS] = {};
+  std::mutex mu;
+  template <class F> int get(int slot, F&& fn) {
+    const int d = current_device();
+    int x = v[d][slot].load(std::memory_order_acquire);
+    if (x) return x;
+    std::lock_guard<std::mutex> g(mu);
+    x = v[d][slot].load(std::memory_order_relaxed);
+    if (!x) {
+      x = fn();
+      v[d][slot].store(x, std::memory_order_release);
+    }
+    return x;
+  }
+};
+
+inline int device_attr(cudaDeviceAttr what, int fallback) {
+  static PerDeviceInt<1> cache_sm, cache_smem_sm, cache_res, cache_optin;
+  PerDeviceInt<1>* c = what == cudaDevAttrMultiProcessorCount ? &cache_sm
+                     : what == cudaDevAttrMaxSharedMemoryPerMultiprocessor ? &cache_smem_sm
+                     : what == cudaDevAttrReservedSharedMemoryPerBlock ? &cache_res
+                     : what == cudaDevAttrMaxSharedMemoryPerBlockOptin ? &cache_optin : nullptr;
+  auto q = [&] {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, what, current_device()) != cudaSuccess) { cudaGetLastError(); n = 0; }
+    return n > 0 ? n : fallback;
+  };
+  return c ? c->get(0, q) : q();
+}
+}  // namespace af
+#endif
+
 // Programmatic dependent launch (sm_90+): wait for the preceding grid's memory to be visible /
 // allow the next grid in the stream to start its prologue.
 AF_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

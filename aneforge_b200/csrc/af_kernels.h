@@ -150,6 +150,9 @@ struct AttnDecodeArgs {
   L2Pf pf;                     // issued at kernel start (the attention phase reads little from HBM)
 };
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st, bool pdl);
+// true when a launch with these arguments merges its splits through a.part / a.counters (false
+// when there is one split, or the splits of a kv head merge inside a thread-block cluster)
+bool attn_decode_uses_scratch(const AttnDecodeArgs& a);
 size_t attn_decode_scratch_floats(int NB, int KV, int n_split, int G, int dh);
 
 // MoE router tail (moe.cu): softmax over E, top-k by repeated row-max peel (lowest index on ties),
@@ -167,70 +170,6 @@ int comm_rank(void* comm);
 cudaError_t tp_argmax_launch(const int* gathered, int T, int NB, int* tok_out, int* pos_adv, int* hist, int hist_ld,
                              cudaStream_t st);
 cudaError_t add_f32_launch(float* y, const float* x, size_t n, cudaStream_t st);
-
-// ---- decode megakernel: one persistent, cooperatively launched grid runs a whole decode step (embed,
-// every layer, final norm) with grid-wide barriers between the dependent phases.
-struct MkGemv {
-  const void* w = nullptr;        // tiles: pack_i8_tiles (+ scale) or pack_i4_tiles
-  const __half* scale = nullptr;  // int8 per-row scales
-  const __half* bias = nullptr;
-  int N = 0, K = 0, epi = EPI_F32;
-  void* y = nullptr;
-  int ldy = 0;
-  const void* x = nullptr;        // fp16 rows, or fp32 rows normalised on the fly (xnorm)
-  int ldx = 0, xnorm = 0;
-  const __half* g = nullptr;      // RMSNorm g_eff / floor when xnorm
-  float floor = 0.f;
-};
-struct MkLayer {
-  MkGemv qkv, o, gu, down;
-  __half* kc = nullptr;           // [NB][KV][M][dh]
-  __half* vc = nullptr;
-  const __half* qn = nullptr;     // QK-norm g_eff (optional)
-  const __half* kn = nullptr;
-  float qnf = 0.f, knf = 0.f;
-};
-struct MkArgs {
-  const MkLayer* layers = nullptr;  // device array [L]
-  int L = 0, wf = W_I8;
-  int NB = 1, D = 0, H = 0, KV = 0, dh = 0, M = 0, nsplit = 1;
-  float scale = 0.f, kv_c = 1.f;
-  int expand = 0;
-  const int* tok = nullptr;
-  const __half* embed = nullptr;
-  int vocab = 0;
-  const int* pos = nullptr;
-  const __half* cos_t = nullptr;
-  const __half* sin_t = nullptr;
-  float* h = nullptr;              // [NB][D] fp32 residual
-  float* qkv = nullptr;            // [NB][ldq] fp32
-  int ldq = 0;
-  __half* att = nullptr;           // [NB][H*dh]
-  const __half* final_g = nullptr;
-  float final_floor = 0.f;
-  __half* hid = nullptr;           // [NB][D] fp16 final-norm output
-  float* part = nullptr;           // GEMV split-K partials
-  int* counters = nullptr;         // GEMV tickets [max row blocks]
-  int maxc = 0;                    // partial slots per row block
-  float* apart = nullptr;          // attention split partials [NB][KV][nsplit][G][dh+2]
-  int* acount = nullptr;           // attention tickets [NB][KV]
-  unsigned* bar = nullptr;         // grid barrier counter, zeroed before each launch
-  int* err = nullptr;
-  int xs_halves = 0;               // staged-x capacity per batch row (set by the launcher)
-  unsigned long long* prof = nullptr;   // optional [grid][1 + 5L][4] globaltimer stamps per CTA and
-                                        // grid barrier: arrival, departure, and for the GEMV phase
-                                        // that ends there: x staged, last stage consumed (diagnostics)
-};
-struct MkPlan {
-  int grid = 0, maxc = 0, xs_halves = 0;
-  size_t smem = 0, part_floats = 0, counters = 0;
-  // shared-memory layout: ring stages, staged-x row strides (norm / plain phases), x region bytes
-  int nst = 0, xsn = 0, xsp = 0, hs_off = -1, region = 0;
-};
-// Geometry and scratch needs for a model (all layers share the projection shapes); ok = false when
-// the shape does not fit the megakernel (then the per-op kernels run).
-bool decode_mk_plan(const MkLayer& shapes, int wf, int NB, int H, int KV, int dh, int nsplit, MkPlan* plan);
-cudaError_t decode_mk_launch(const MkArgs& a, const MkPlan& plan, cudaStream_t st);
 
 // Prefill causal attention over S prompt rows (CUDA-core flash form, fp16 q/K/V operands).
 struct AttnPrefillArgs {

@@ -499,15 +499,15 @@ static cudaError_t launch_decode(const AttnDecodeArgs& a, cudaStream_t st, bool 
   // staged cache rows, then (clusters) rank 0's merge area [n_split][G][DH + 2] fp32
   cfg.dynamicSmemBytes = (a.prefetch ? 2 * (size_t)a.pre_rows * DH * 2 : 0) +
                          (a.cluster ? (size_t)a.n_split * G * (DH + 2) * 4 : 0);
-  static bool attrs_set = false;               // static + dynamic shared memory may pass 48 KB
-  if (!attrs_set) {
+  static PerDeviceOnce attrs;                  // static + dynamic shared memory may pass 48 KB
+  const cudaError_t ae = attrs.run([] {
     cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<DH, G, DIRECT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          2 * DEC_PRE_MAX * DH * 2 + DEC_CLUSTER_MAX * G * (DH + 2) * 4);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(attn_decode_kernel<DH, G, DIRECT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) return e;
-    attrs_set = true;
-  }
+    return e;
+  });
+  if (ae != cudaSuccess) return ae;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   int na = 0;
@@ -549,13 +549,19 @@ static cudaError_t decode_g(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) 
   }
 }
 
+// splits merge inside a cluster when they fit one (AF_ATTN_CLUSTER=0: always through scratch)
+static bool merge_in_cluster(const AttnDecodeArgs& a) {
+  static const int use_cluster = env_int("AF_ATTN_CLUSTER", 1);
+  return use_cluster && a.n_split > 1 && a.n_split <= DEC_CLUSTER_MAX;
+}
+
+bool attn_decode_uses_scratch(const AttnDecodeArgs& a) { return a.n_split > 1 && !merge_in_cluster(a); }
+
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a0, cudaStream_t st, bool pdl) {
   AttnDecodeArgs a = a0;
   if (a.KV <= 0 || a.H % a.KV || a.n_split < 1 || a.n_split > 64) return cudaErrorInvalidValue;
-  if (a.n_split > 1 && (!a.part || !a.counters)) return cudaErrorInvalidValue;
-  // splits merge inside a cluster when they fit one (AF_ATTN_CLUSTER=0: always through scratch)
-  static const int use_cluster = env_int("AF_ATTN_CLUSTER", 1);
-  a.cluster = use_cluster && a.n_split > 1 && a.n_split <= DEC_CLUSTER_MAX ? 1 : 0;
+  a.cluster = merge_in_cluster(a) ? 1 : 0;
+  if (!a.cluster && a.n_split > 1 && (!a.part || !a.counters)) return cudaErrorInvalidValue;
   static const int min_keys = env_int("AF_ATTN_MIN_KEYS", 64);
   a.min_keys = a.min_keys > 0 ? a.min_keys : min_keys;
   // staged rows: a CTA's whole key range when it fits, else its first DEC_PRE_MAX rows
@@ -845,8 +851,9 @@ cudaError_t rope_kv_prefill_launch(const AttnPrefillArgs& a, __half* qbuf, cudaS
 cudaError_t attn_prefill_with_q(const AttnPrefillArgs& a, const __half* qbuf, cudaStream_t st) {
   static const int fa = env_int("AF_PREFILL_FA", 1);
   if (fa && a.dh == 128 && a.S >= 16) {
-    static const cudaError_t attr =
-        cudaFuncSetAttribute(attn_prefill_fa_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM);
+    static PerDeviceOnce attrs;
+    const cudaError_t attr = attrs.run(
+        [] { return cudaFuncSetAttribute(attn_prefill_fa_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM); });
     if (attr != cudaSuccess) return attr;
     attn_prefill_fa_kernel<<<dim3(a.H, (a.S + FA_BQ - 1) / FA_BQ), 128, FA_SMEM, st>>>(a, qbuf);
     return cudaGetLastError();

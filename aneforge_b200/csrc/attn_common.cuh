@@ -1,5 +1,5 @@
-// Decode-attention building blocks shared by the stand-alone attention kernel and the decode
-// megakernel: the per-lane head layout, QK-norm + RoPE on one head vector, fp16 row loads and the
+// Decode-attention building blocks shared by the decode and prefill attention kernels: the
+// per-lane head layout, QK-norm + RoPE on one head vector, fp16 row loads and the
 // batched transpose-reduce of G x PB dot products.
 #pragma once
 #include "af_common.cuh"

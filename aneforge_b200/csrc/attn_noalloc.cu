@@ -10,14 +10,19 @@
 //
 // Limits and sharing rules:
 //  * the array is AF_ATTN_NOALLOC_SCRATCH_BYTES (2 MiB) per GPU and stays resident on every GPU that
-//    loads the library until the process exits; shapes needing more are rejected (rc -1, reason in
-//    af_last_error()) before anything is launched;
-//  * every call on a GPU uses the same array and leaves its contents behind; the ticket counters
-//    are cleared on the caller's stream before each launch, the partial sums need no clearing;
+//    loads the library until the process exits; a shape whose splits merge through global scratch
+//    and need more is rejected (rc -1, reason in af_last_error()) before anything is launched.
+//    Shapes whose splits merge inside a thread-block cluster (at most 16 splits) touch no scratch
+//    and have no size limit here;
+//  * every call on a GPU uses the same array and leaves its contents behind; when a call merges
+//    through the array its ticket counters are cleared on the caller's stream before the launch,
+//    the partial sums need no clearing;
 //  * two calls whose kernels overlap on the GPU (different streams without ordering) race on the
 //    array and produce wrong results - order them on one stream or with events;
 //  * the first call on each device looks the array's device address up (cudaGetSymbolAddress with
-//    that device current) and caches it: make that first call before any stream capture begins.
+//    that device current) and caches it: make that first call before any stream capture begins;
+//  * the cached address is not refreshed after cudaDeviceReset (which may reload the library's
+//    module at another address): do not use this entry point across a device reset.
 #include <mutex>
 #include <string>
 
@@ -33,7 +38,7 @@ namespace {
 
 constexpr size_t kScratchBytes = AF_ATTN_NOALLOC_SCRATCH_BYTES;
 constexpr size_t kCounterBytes = 16384;   // ticket counters first, then the partial sums
-constexpr int kMaxDevices = 64;
+constexpr int kMaxDevices = af::kMaxDevices;
 
 // The scratch itself. In host code this name is only a stand-in for the symbol: its device address
 // comes from cudaGetSymbolAddress below.
@@ -79,14 +84,6 @@ int af_attn_decode_noalloc(const float* qkv, int ld_qkv, uint16_t* kc, uint16_t*
     af::set_error_public("af_attn_decode_noalloc: bad shape (need nb >= 1, kv > 0, h % kv == 0, n_split >= 1)");
     return -1;
   }
-  const size_t counters = (size_t)nb * kv * sizeof(int);
-  const size_t partial = 4 * af::attn_decode_scratch_floats(nb, kv, n_split, h / kv, dh);
-  if (n_split > 1 && (counters > kCounterBytes || kCounterBytes + partial > kScratchBytes)) {
-    af::set_error_public("af_attn_decode_noalloc: this shape needs " + std::to_string(kCounterBytes + partial) +
-                         " bytes of scratch; the built-in maximum is " + std::to_string(kScratchBytes) +
-                         " (use af_attn_decode with caller scratch, or fewer splits / sequences)");
-    return -1;
-  }
   af::AttnDecodeArgs a;
   a.qkv = qkv; a.ld_qkv = ld_qkv;
   a.kc = reinterpret_cast<__half*>(kc); a.vc = reinterpret_cast<__half*>(vc);
@@ -96,15 +93,27 @@ int af_attn_decode_noalloc(const float* qkv, int ld_qkv, uint16_t* kc, uint16_t*
   a.NB = nb; a.H = h; a.KV = kv; a.dh = dh; a.M = m; a.n_split = n_split;
   a.scale = scale; a.kv_c = kv_c; a.expand = expand; a.err = err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool merges_in_scratch = af::attn_decode_uses_scratch(a);
+  const size_t counters = (size_t)nb * kv * sizeof(int);
+  const size_t partial = 4 * af::attn_decode_scratch_floats(nb, kv, n_split, h / kv, dh);
+  if (merges_in_scratch && (counters > kCounterBytes || kCounterBytes + partial > kScratchBytes)) {
+    af::set_error_public("af_attn_decode_noalloc: this shape needs " + std::to_string(kCounterBytes + partial) +
+                         " bytes of scratch; the built-in maximum is " + std::to_string(kScratchBytes) +
+                         " (use af_attn_decode with caller scratch, or fewer splits / sequences)");
+    return -1;
+  }
   if (n_split > 1) {
     void* base = nullptr;
     if (scratch_address(&base) != 0) return -1;
-    // the tickets must start at zero whatever an earlier call left behind
-    cudaError_t e = cudaMemsetAsync(base, 0, counters, st);
-    if (e != cudaSuccess) {
-      af::set_error_public(std::string("af_attn_decode_noalloc: clearing the tickets failed: ") + cudaGetErrorString(e));
-      cudaGetLastError();
-      return -1;
+    if (merges_in_scratch) {
+      // the tickets must start at zero whatever an earlier call left behind
+      cudaError_t e = cudaMemsetAsync(base, 0, counters, st);
+      if (e != cudaSuccess) {
+        af::set_error_public(std::string("af_attn_decode_noalloc: clearing the tickets failed: ") +
+                             cudaGetErrorString(e));
+        cudaGetLastError();
+        return -1;
+      }
     }
     a.counters = static_cast<int*>(base);
     a.part = reinterpret_cast<float*>(static_cast<char*>(base) + kCounterBytes);

@@ -134,25 +134,6 @@ int af_gemv_tc_i4(int epi, const uint16_t* x, int ldx, const void* tiles, const 
   return rc_of(af::gemv_tc_launch(a, static_cast<cudaStream_t>(stream), false), "af_gemv_tc_i4");
 }
 
-int af_decode_mk_scratch(int wf, int nb, int d, int h, int kv, int dh, int ffn, int nsplit, size_t* part_bytes,
-                         size_t* cnt_bytes) {
-  if (!part_bytes || !cnt_bytes || kv <= 0 || h % kv) return -1;
-  af::MkLayer s;
-  const int Q = (h + 2 * kv) * dh;
-  s.qkv.N = Q; s.qkv.K = d; s.qkv.epi = af::EPI_F32;
-  s.o.N = d; s.o.K = h * dh; s.o.epi = af::EPI_RESID;
-  s.gu.N = 2 * ffn; s.gu.K = d; s.gu.epi = af::EPI_SWIGLU;
-  s.down.N = d; s.down.K = ffn; s.down.epi = af::EPI_RESID;
-  af::MkPlan plan;
-  if (!af::decode_mk_plan(s, wf, nb, h, kv, dh, nsplit, &plan)) {
-    af::set_error_public("af_decode_mk_scratch: shape not supported by the decode megakernel");
-    cudaGetLastError();
-    return -1;
-  }
-  *part_bytes = 4 * plan.part_floats;
-  *cnt_bytes = 4 * plan.counters;
-  return 0;
-}
 
 int af_gemv_tc_expert(int wf, int epi, const uint16_t* x, int ldx, const void* tiles, const uint16_t* scales,
                       void* y, int ldy, int nb, int n, int k, const int* sel, int slot, int fixed_e, long long w_stride,

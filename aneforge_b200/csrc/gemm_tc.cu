@@ -423,12 +423,7 @@ cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
   if (!make_amap(a, &amap)) return cudaErrorInvalidValue;
   // 128-column tiles when 256-column ones would leave SMs idle (few output tiles: the prompt-sized
   // qkv / o / down shapes), 256 otherwise (half the A re-reads per output)
-  static const int sms = [] {
-    int dev = 0, n = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    return n > 0 ? n : 148;
-  }();
+  const int sms = device_attr(cudaDevAttrMultiProcessorCount, 148);
   static const int narrow_ok = env_int("AF_GEMM_NARROW", 1);
   const int MT = (a.NB + gm::BM - 1) / gm::BM;
   // 128-column tiles only where they add no wave: twice the tiles must fit in as many waves of
@@ -451,12 +446,10 @@ cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
        (void*)gemm_tc_kernel<true, 256, 3, 4>}};
   const size_t smem = smems[var];
   void* fn = fns[i4 ? 1 : 0][var];
-  static bool attr[2][3] = {};
-  if (!attr[i4 ? 1 : 0][var]) {
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    attr[i4 ? 1 : 0][var] = true;
-  }
+  static PerDeviceOnce attr[2][3];
+  const cudaError_t ae = attr[i4 ? 1 : 0][var].run(
+      [fn, smem] { return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); });
+  if (ae != cudaSuccess) return ae;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(MT * NT));
   cfg.blockDim = dim3(gm::THREADS);

@@ -372,33 +372,19 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
 // and a programmatic launch places CTAs on whichever SMs free up first, so without the cap an SM
 // that frees early takes one CTA more than the others and finishes last.
 static size_t smem_for_ctas_per_sm(size_t need, int k) {
-  static int per_sm = 0, reserved = 0, per_block = 0;
-  if (!per_sm) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
-    cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
-    cudaDeviceGetAttribute(&per_block, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    if (per_sm <= 0) per_sm = 1;
-  }
   static const int cap = env_int("AF_TC_OCC_CAP", 0);     // measured slower on B200: off by default
-  if (!cap || k < 1 || per_sm <= 1) return need;
+  if (!cap || k < 1) return need;
+  const int per_sm = device_attr(cudaDevAttrMaxSharedMemoryPerMultiprocessor, 1);
+  const int reserved = device_attr(cudaDevAttrReservedSharedMemoryPerBlock, 1024);
+  const int per_block = device_attr(cudaDevAttrMaxSharedMemoryPerBlockOptin, 0);
+  if (per_sm <= 1) return need;
   const long long floor_k = (long long)per_sm / (k + 1) - reserved + 16;   // k + 1 CTAs no longer fit
   size_t want = floor_k > (long long)need ? (size_t)((floor_k + 127) / 128 * 128) : need;
   if (per_block > 0 && want > (size_t)per_block) want = need;
   return want;
 }
 
-static int sm_count() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
-}
+static int sm_count() { return device_attr(cudaDevAttrMultiProcessorCount, 148); }
 
 static size_t smem_bytes(int NB, bool i4) {
   // weight ring | barriers | x ring | odd-warp sums [4 row tiles][32 lanes][8 floats]
@@ -406,32 +392,44 @@ static size_t smem_bytes(int NB, bool i4) {
          (size_t)tc::XSLOTS * NB * tc::XSTRIDE * 2 + tc::WARPS * 32 * 8 * 4;
 }
 
+// the kernel's shared-memory limit and cluster permission, set once per device
 template <int NT, int EPI, bool I4>
-static int grid_for(int NB) {
-  static int occ[17] = {};
-  if (!occ[NB]) {
-    int dev = 0, optin = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    cudaFuncSetAttribute(gemv_tc_kernel<NT, EPI, I4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         optin > (int)smem_bytes(16, I4) ? optin : (int)smem_bytes(16, I4));
-    cudaFuncSetAttribute(gemv_tc_kernel<NT, EPI, I4>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    int o = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, gemv_tc_kernel<NT, EPI, I4>, (Cw<I4>::n + 1) * 32,
-                                                      smem_bytes(NB, I4)) != cudaSuccess || o < 1)
-      o = 1;
-    const int cap = env_int("AF_TC_CTAS_PER_SM", 4);
-    occ[NB] = o < cap ? o : cap;
-  }
-  return occ[NB] * sm_count();
+static cudaError_t set_attrs() {
+  static PerDeviceOnce once;
+  return once.run([] {
+    const int optin = device_attr(cudaDevAttrMaxSharedMemoryPerBlockOptin, 0);
+    cudaError_t e = cudaFuncSetAttribute(gemv_tc_kernel<NT, EPI, I4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         optin > (int)smem_bytes(16, I4) ? optin : (int)smem_bytes(16, I4));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemv_tc_kernel<NT, EPI, I4>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    return e;
+  });
 }
 
-// clusters of d CTAs that can be resident at once (0 if the query fails)
+// CTAs of this instantiation resident at once on the current device (per SM x SMs)
+template <int NT, int EPI, bool I4>
+static int grid_for(int NB) {
+  static PerDeviceInt<17> occ;
+  const int per_sm = occ.get(NB, [NB] {
+    if (set_attrs<NT, EPI, I4>() != cudaSuccess) { cudaGetLastError(); return 1; }
+    int o = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, gemv_tc_kernel<NT, EPI, I4>, (Cw<I4>::n + 1) * 32,
+                                                      smem_bytes(NB, I4)) != cudaSuccess || o < 1) {
+      cudaGetLastError();
+      o = 1;
+    }
+    const int cap = env_int("AF_TC_CTAS_PER_SM", 4);
+    return o < cap ? o : cap;
+  });
+  return per_sm * sm_count();
+}
+
+// clusters of d CTAs that can be resident at once on the current device (0 if the query fails)
 template <int NT, int EPI, bool I4>
 static int clusters_for(int NB, int d) {
-  static int cache[17][17] = {};
-  if (!cache[NB][d]) {
-    grid_for<NT, EPI, I4>(NB);                  // sets the kernel's shared-memory limit
+  static PerDeviceInt<17 * 17> cache;
+  const int n = cache.get(NB * 17 + d, [NB, d] {
+    if (set_attrs<NT, EPI, I4>() != cudaSuccess) { cudaGetLastError(); return -1; }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(d * 64);
     cfg.blockDim = dim3((Cw<I4>::n + 1) * 32);
@@ -443,14 +441,14 @@ static int clusters_for(int NB, int d) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, gemv_tc_kernel<NT, EPI, I4>, &cfg) != cudaSuccess) {
+    int m = 0;
+    if (cudaOccupancyMaxActiveClusters(&m, gemv_tc_kernel<NT, EPI, I4>, &cfg) != cudaSuccess) {
       cudaGetLastError();
-      n = 0;
+      m = 0;
     }
-    cache[NB][d] = n > 0 ? n : -1;
-  }
-  return cache[NB][d] > 0 ? cache[NB][d] : 0;
+    return m > 0 ? m : -1;
+  });
+  return n > 0 ? n : 0;
 }
 
 template <bool I4>
@@ -487,7 +485,7 @@ static int grid_any(int NB, int epi) {
 //    the SMs), fill = min(1, G / min_ctas) (enough bytes in flight), with G within the resident
 //    capacity and the row blocks' clusters within `cfrac` percent of the clusters of d CTAs the GPU
 //    holds at once (a cluster is placed whole within a GPC).
-// `allow_cluster` false (scratch sizing, the megakernel's plan) always describes the stream-K
+// `allow_cluster` false (scratch sizing) always describes the stream-K
 // layout at the resident capacity; `maxc` is then the most CTAs sharing one row block.
 static void plan_geometry(int N, int K, int NB, int epi, bool i4, int* G, int* maxc, int* csize,
                           bool allow_cluster = true) {
@@ -560,6 +558,8 @@ size_t gemv_tc_scratch_bytes(int N, int K, int NB) {
 
 template <int NT, int EPI, bool I4>
 static cudaError_t launch_tc(GemvTcArgs a, cudaStream_t st, bool pdl) {
+  const cudaError_t ae = set_attrs<NT, EPI, I4>();
+  if (ae != cudaSuccess) return ae;
   int G = 0, maxc = 0, cs = 0;
   plan_geometry(a.N, a.K, a.NB, EPI, I4, &G, &maxc, &cs);
   a.maxc = maxc;

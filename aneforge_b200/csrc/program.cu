@@ -56,14 +56,7 @@ struct Op {
   int line = 0;
 };
 
-struct MkPrep {               // a decode_mk op, resolved at finalisation
-  MkArgs args;
-  MkPlan plan;
-  MkLayer* dev_layers = nullptr;
-};
-
 struct Program {
-  std::map<int, MkPrep> mk;    // by op index
   int device = 0;
   cudaStream_t stream = nullptr;
   std::vector<Buffer> bufs;
@@ -194,87 +187,6 @@ static L2Pf parse_pf(OpCtx& c) {
     f.piece = f.stride = 16384;
   }
   return f;
-}
-
-// Resolve a decode_mk op: the step-wide arguments, one MkLayer per layer, the launch plan.
-static bool mk_resolve(Program& p, const Op& op, bool dry, MkArgs& a, std::vector<MkLayer>& layers, MkPlan& plan,
-                       std::string& why) {
-  OpCtx c{p, op, {}};
-  const std::string* wfs = c.raw("wf");
-  if (!wfs) { why = c.err; return false; }
-  if (*wfs != "i8t" && *wfs != "i4t") { why = "decode_mk needs wf=i8t or wf=i4t"; return false; }
-  const bool i4 = *wfs == "i4t";
-  a.wf = i4 ? W_I4G32 : W_I8;
-  a.L = (int)c.i("layers");
-  a.NB = (int)c.i("nb"); a.D = (int)c.i("d"); a.H = (int)c.i("h"); a.KV = (int)c.i("kv"); a.dh = (int)c.i("dh");
-  a.M = (int)c.i("m"); a.nsplit = (int)c.i("nsplit", 1); a.vocab = (int)c.i("vocab");
-  const int F = (int)c.i("ffn");
-  a.scale = (float)c.f("scale"); a.kv_c = (float)c.f("kvc", 1.0); a.expand = (int)c.i("expand", 0);
-  a.final_floor = (float)c.f("ffloor");
-  if (!c.err.empty()) { why = c.err; return false; }
-  if (a.L < 1 || a.NB < 1 || a.D <= 0 || a.KV <= 0 || a.H % a.KV || a.dh <= 0 || F <= 0) {
-    why = "bad decode_mk dimensions"; return false;
-  }
-  const int Q = (a.H + 2 * a.KV) * a.dh, HD = a.H * a.dh;
-  a.ldq = Q;
-  a.tok = (const int*)c.ptr("tok", 4 * (size_t)a.NB);
-  a.pos = (const int*)c.ptr("pos", 4 * (size_t)a.NB);
-  a.embed = (const __half*)c.ptr("embed", 2 * (size_t)a.vocab * a.D);
-  a.cos_t = (const __half*)c.ptr("cos", 2 * (size_t)a.M * a.dh, true);
-  a.sin_t = (const __half*)c.ptr("sin", 2 * (size_t)a.M * a.dh, true);
-  a.h = (float*)c.ptr("res", 4 * (size_t)a.NB * a.D);
-  a.qkv = (float*)c.ptr("qkv", 4 * (size_t)a.NB * Q);
-  a.att = (__half*)c.ptr("att", 2 * (size_t)a.NB * HD);
-  __half* act = (__half*)c.ptr("act", 2 * (size_t)a.NB * F);
-  a.final_g = (const __half*)c.ptr("final_g", 2 * (size_t)a.D);
-  a.hid = (__half*)c.ptr("hid", 2 * (size_t)a.NB * a.D);
-  a.bar = (unsigned*)c.ptr("bar", 4);
-  const std::vector<double> fa = c.list("fa", a.L), fm = c.list("fm", a.L);
-  std::vector<double> fq, fk;
-  if (op.kv.count("fq")) { fq = c.list("fq", a.L); fk = c.list("fk", a.L); }
-  if (!c.err.empty()) { why = c.err; return false; }
-  layers.assign(a.L, MkLayer());
-  const size_t cache = 2 * (size_t)a.NB * a.KV * a.M * a.dh;
-  auto tiles = [&](int N, int K) { return i4 ? pack_i4_tiles_bytes(N, K) : pack_i8_tiles_bytes(N, K); };
-  for (int l = 0; l < a.L; ++l) {
-    MkLayer& ly = layers[l];
-    const std::string pre = "L" + std::to_string(l) + ".";
-    auto gemv = [&](MkGemv& g, const char* key, int N, int K, int epi, void* y, int ldy, const void* x, int ldx,
-                    int xnorm, const char* gname, float floor) {
-      g.N = N; g.K = K; g.epi = epi; g.y = y; g.ldy = ldy; g.x = x; g.ldx = ldx; g.xnorm = xnorm; g.floor = floor;
-      g.w = c.named(pre + key + ".w", tiles(N, K));
-      if (!i4) g.scale = (const __half*)c.named(pre + key + ".s", 2 * (size_t)N);
-      g.bias = (const __half*)c.named(pre + key + ".b", 2 * (size_t)N, true);
-      if (gname) g.g = (const __half*)c.named(pre + gname, 2 * (size_t)K);
-    };
-    gemv(ly.qkv, "qkv", Q, a.D, EPI_F32, a.qkv, Q, a.h, a.D, 1, "attn_g", (float)fa[l]);
-    gemv(ly.o, "o", a.D, HD, EPI_RESID, a.h, a.D, a.att, HD, 0, nullptr, 0.f);
-    gemv(ly.gu, "gu", 2 * F, a.D, EPI_SWIGLU, act, F, a.h, a.D, 1, "mlp_g", (float)fm[l]);
-    gemv(ly.down, "down", a.D, F, EPI_RESID, a.h, a.D, act, F, 0, nullptr, 0.f);
-    ly.kc = (__half*)c.named(pre + "K", cache);
-    ly.vc = (__half*)c.named(pre + "V", cache);
-    if (!fq.empty()) {
-      ly.qn = (const __half*)c.named(pre + "qn", 2 * (size_t)a.dh);
-      ly.kn = (const __half*)c.named(pre + "kn", 2 * (size_t)a.dh);
-      ly.qnf = (float)fq[l]; ly.knf = (float)fk[l];
-    }
-    if (!c.err.empty()) { why = c.err; return false; }
-  }
-  if (dry) return true;
-  if (!decode_mk_plan(layers[0], a.wf, a.NB, a.H, a.KV, a.dh, a.nsplit, &plan)) {
-    why = "decode_mk: this shape does not fit the megakernel";
-    return false;
-  }
-  a.part = (float*)c.ptr("part", 4 * plan.part_floats);
-  a.counters = (int*)c.ptr("cnt", 4 * plan.counters);
-  if (a.nsplit > 1) {
-    a.apart = (float*)c.ptr("apart", 4 * attn_decode_scratch_floats(a.NB, a.KV, a.nsplit, a.H / a.KV, a.dh));
-    a.acount = (int*)c.ptr("acnt", 4 * (size_t)a.NB * a.KV);
-  }
-  a.err = p.d_err;
-  a.prof = (unsigned long long*)c.ptr("prof", 8 * (size_t)plan.grid * (1 + 5 * a.L) * 4, true);
-  if (!c.err.empty()) { why = c.err; return false; }
-  return true;
 }
 
 static int wf_of(const std::string& s) {
@@ -452,20 +364,6 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
       e = rope_kv_prefill_launch(a, qbuf, st);
       if (e == cudaSuccess) e = attn_prefill_with_q(a, qbuf, st);
     }
-  } else if (op.kind == "decode_mk") {
-    if (dry) {
-      MkArgs a;
-      MkPlan plan;
-      std::vector<MkLayer> layers;
-      if (!mk_resolve(p, op, true, a, layers, plan, why)) return cudaErrorInvalidValue;
-    } else {
-      const int opi = (int)(&op - p.ops.data());
-      auto it = p.mk.find(opi);
-      if (it == p.mk.end()) { why = "decode_mk was not prepared"; return cudaErrorInvalidValue; }
-      MkArgs a = it->second.args;
-      a.layers = it->second.dev_layers;
-      e = decode_mk_launch(a, it->second.plan, st);
-    }
   } else if (op.kind == "moe_gate") {
     const int nb = (int)c.i("nb"), E = (int)c.i("e"), k = (int)c.i("k"), ld = (int)c.i("ld", E);
     const float* lg = (const float*)c.ptr("logits", 4 * ((size_t)(nb - 1) * ld + E));
@@ -632,8 +530,6 @@ static void free_program(Program* p) {
   cudaSetDevice(p->device);
   if (p->stream) cudaStreamSynchronize(p->stream);
   if (p->exec) cudaGraphExecDestroy(p->exec);
-  for (auto& kv : p->mk)
-    if (kv.second.dev_layers) cudaFree(kv.second.dev_layers);
   for (auto& b : p->bufs)
     if (b.owned && b.dev) cudaFree(b.dev);
   if (p->d_err) cudaFree(p->d_err);
@@ -704,27 +600,6 @@ static int finalize(Program& p) {
       set_error("weight buffer '" + b.name + "' was never uploaded or bound");
       return -1;
     }
-  // megakernel ops: resolve every layer's pointers now that all buffers are bound, upload the layer
-  // table, plan the launch (all before stream capture begins)
-  for (size_t i = 0; i < p.ops.size(); ++i) {
-    if (p.ops[i].kind != "decode_mk") continue;
-    MkPrep prep;
-    std::vector<MkLayer> layers;
-    std::string why;
-    if (!mk_resolve(p, p.ops[i], false, prep.args, layers, prep.plan, why)) {
-      set_error("op line " + std::to_string(p.ops[i].line) + " (decode_mk): " + why);
-      return -1;
-    }
-    const size_t bytes = layers.size() * sizeof(MkLayer);
-    if (cudaMalloc(&prep.dev_layers, bytes) != cudaSuccess ||
-        cudaMemcpy(prep.dev_layers, layers.data(), bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
-      if (prep.dev_layers) cudaFree(prep.dev_layers);
-      cudaGetLastError();
-      set_error("decode_mk: layer table upload failed");
-      return -1;
-    }
-    p.mk[(int)i] = prep;
-  }
   if (p.use_graph) {
     cudaGraph_t graph = nullptr;
     if (cudaStreamBeginCapture(p.stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {

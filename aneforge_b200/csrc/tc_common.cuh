@@ -1,6 +1,5 @@
-// Shared pieces of the tensor-core dequant GEMVs (the stand-alone gemv_tc kernel and the decode
-// megakernel): tile geometry, mbarrier / bulk-copy wrappers, the mma.sync wrappers and the exact
-// int8 / int4 -> fp16 fragment conversions.
+// Shared pieces of the tensor-core dequant GEMVs: tile geometry, mbarrier / bulk-copy wrappers, the
+// mma.sync wrappers and the exact int8 / int4 -> fp16 fragment conversions.
 #pragma once
 #include "af_common.cuh"
 

@@ -44,9 +44,6 @@ class ModelType(str, Enum):
   QWEN = "qwen"
 
 
-_DENSE_INCOMPATIBLE = {ModelType.GEMMA2, ModelType.GEMMA3, ModelType.GEMMA3_TEXT}
-
-
 @dataclass
 class LayerSpec:
   """Per-layer plan (reference `aneforge/llm.py:36-42`)."""
@@ -72,33 +69,66 @@ class LlamaConfig:
     return self.head_dim or self.dim // self.n_heads
 
 
-def _llama3_rope_scale(inv, s):
-  """Llama-3.1 "llama3" inverse-frequency rescaling (reference `llm.py:62-73`)."""
-  factor, lo, hi = float(s["factor"]), float(s["low_freq_factor"]), float(s["high_freq_factor"])
-  old = float(s["original_max_position_embeddings"])
-  low_wl, high_wl = old / lo, old / hi
-  wl = 2.0 * np.pi / inv
-  scaled = np.where(wl > low_wl, inv / factor, inv)
-  smooth = (old / wl - lo) / (hi - lo)
-  smoothed = (1.0 - smooth) * scaled / factor + smooth * scaled
-  return np.where((wl >= high_wl) & (wl <= low_wl), smoothed, scaled)
+def _rope_frequencies(rd: int, base: float, scaling: dict | None):
+  """float64 angular frequency of each rotated pair: theta_i = base^(-2i/rd). With a "llama3"
+  `rope_scaling` (Llama 3.1) the frequencies are remapped by wavelength (what the reference's
+  `aneforge/llm.py:62-73` does, following the Hugging Face formula):
+    * wavelength 2*pi/theta longer than original_max_positions / low_freq_factor -> theta / factor;
+    * shorter than original_max_positions / high_freq_factor                      -> unchanged;
+    * in between: a linear blend of the two, weighted by how far into the band the pair sits."""
+  freqs = 1.0 / (base ** (np.arange(0, rd, 2) / rd))
+  if not (scaling and scaling.get("rope_type") == "llama3"):
+    return freqs
+  factor = float(scaling["factor"])
+  lo, hi = float(scaling["low_freq_factor"]), float(scaling["high_freq_factor"])
+  ctx = float(scaling["original_max_position_embeddings"])
+  wavelen = 2.0 * np.pi / freqs
+  long_edge, short_edge = ctx / lo, ctx / hi
+  out = freqs.copy()
+  slow = wavelen > long_edge
+  out[slow] = freqs[slow] / factor
+  band = (wavelen >= short_edge) & (wavelen <= long_edge)
+  t = (ctx / wavelen[band] - lo) / (hi - lo)             # 0 at the long edge, 1 at the short edge
+  out[band] = (1.0 - t) * freqs[band] / factor + t * freqs[band]
+  return out
 
 
 def rope_tables(seq: int, dh: int, base: float = 10000.0, rotary_dim: int = 0, interleaved: bool = False,
                 scaling: dict | None = None):
-  """[seq, dh] fp16 cos/sin tables, float64 math (reference `llm.py:76-94`)."""
+  """cos / sin tables [seq, dh] for positions 0..seq-1, computed in float64 and rounded to fp16 once
+  (the reference's tables, `aneforge/llm.py:76-94`). Neox layout: the first and second halves of a
+  head share frequencies; `interleaved` pairs adjacent lanes instead. With a partial rotary
+  dimension the unrotated lanes get cos 1, sin 0."""
   rd = rotary_dim or dh
-  inv = 1.0 / (base ** (np.arange(0, rd, 2) / rd))
-  if scaling and scaling.get("rope_type") == "llama3":
-    inv = _llama3_rope_scale(inv, scaling)
-  pos = np.arange(seq)[:, None] * inv[None, :]
-  if interleaved:
-    c = np.repeat(np.cos(pos), 2, axis=1); s = np.repeat(np.sin(pos), 2, axis=1)
-  else:
-    emb = np.concatenate([pos, pos], -1); c = np.cos(emb); s = np.sin(emb)
-  if rd < dh:
-    c = np.concatenate([c, np.ones((seq, dh - rd))], 1); s = np.concatenate([s, np.zeros((seq, dh - rd))], 1)
-  return c.astype(F16), s.astype(F16)
+  angle = np.outer(np.arange(seq, dtype=np.float64), _rope_frequencies(rd, base, scaling))   # [seq, rd/2]
+  lay = (lambda a: np.repeat(a, 2, axis=1)) if interleaved else (lambda a: np.concatenate([a, a], axis=1))
+  cos_t = np.ones((seq, dh), np.float64)
+  sin_t = np.zeros((seq, dh), np.float64)
+  cos_t[:, :rd] = lay(np.cos(angle))
+  sin_t[:, :rd] = lay(np.sin(angle))
+  return cos_t.astype(F16), sin_t.astype(F16)
+
+
+def sample_token(logits, temperature: float = 0.0, top_p: float = 1.0, top_k: int = 0) -> int:
+  """One token id from a row of logits (see `LlamaPrefill._sample`)."""
+  z = np.asarray(logits, np.float64).ravel()
+  if temperature <= 0.0:
+    return int(np.argmax(z))
+  z = z / temperature
+  n = z.size
+  if top_k and 0 < top_k < n:
+    kth = np.partition(z, n - top_k)[n - top_k]            # the k-th largest logit; ties with it stay
+    z = np.where(z >= kth, z, -np.inf)
+  prob = np.exp(z - z.max())
+  prob /= prob.sum()
+  if 0.0 < top_p < 1.0:
+    desc = np.argsort(prob)[::-1]                           # most probable first
+    mass = np.cumsum(prob[desc])
+    n_keep = int(np.count_nonzero(mass < top_p)) + 1        # up to and including the token crossing top_p
+    nucleus = np.zeros_like(prob)
+    nucleus[desc[:n_keep]] = prob[desc[:n_keep]]
+    prob = nucleus / nucleus.sum()
+  return int(np.random.choice(n, p=prob))
 
 
 # ------------------------------------------------------------------------------ plan emitters
@@ -278,7 +308,7 @@ class LlamaPrefill:
     self._pre = None
     self._head = None
     self._lmT = None
-    self.mk_profile = False                 # record per-CTA barrier timestamps in the megakernel
+    self.eos_check_every = 16               # greedy device loop: steps between EOS checks
 
   # -- weights
   def _spec(self, i: int) -> LayerSpec:
@@ -441,35 +471,12 @@ class LlamaPrefill:
     for li in range(cfg.n_layers):
       self._declare_layer_weights(pb, li, d["layers"][li])
       pb.buf(f"L{li}.K", 2 * NB * KV * M * dh, "state"); pb.buf(f"L{li}.V", 2 * NB * KV * M * dh, "state")
-    mk = self._megakernel_plan(NB, M)
-    if mk is not None:
-      # one persistent launch for embed + every layer + final norm
-      if mk["nsplit"] > 1:
-        pb.buf("attn.part", kernels.attn_decode_scratch_bytes(NB, KV, mk["nsplit"], H // KV, dh), "scratch")
-        pb.buf("attn.cnt", 4 * NB * KV, "scratch")
-      pb.buf("mk.part", mk["part"], "scratch"); pb.buf("mk.cnt", mk["cnt"], "scratch"); pb.buf("mk.bar", 16, "scratch")
-      L = d["layers"]
-      kv = dict(wf=mk["wf"], layers=cfg.n_layers, nb=NB, d=D, h=H, kv=KV, dh=dh, ffn=F, m=M, nsplit=mk["nsplit"],
-                vocab=V, scale=ctx["scale"], kvc=ctx["kvc"], expand=int(ctx["expand"]), ffloor=d["final_floor"],
-                tok="tok", pos="pos", embed="embed", cos="rope.cos" if cfg.rope else None,
-                sin="rope.sin" if cfg.rope else None, res="h", qkv="qkv", att="att", act="act", final_g="final_g",
-                hid="hid", bar="mk.bar", part="mk.part", cnt="mk.cnt",
-                apart="attn.part" if mk["nsplit"] > 1 else None, acnt="attn.cnt" if mk["nsplit"] > 1 else None,
-                fa=",".join(repr(float(l["attn_floor"])) for l in L), fm=",".join(repr(float(l["mlp_floor"])) for l in L))
-      if all("qn" in l for l in L):
-        kv.update(fq=",".join(repr(float(l["qn_floor"])) for l in L), fk=",".join(repr(float(l["kn_floor"])) for l in L))
-      if self.mk_profile:
-        # per-CTA barrier timestamps (diagnostics): [grid][1 + 5 L][4] u64
-        pb.buf("mk.prof", 8 * 2 * 148 * (1 + 5 * cfg.n_layers) * 4, "out")
-        kv.update(prof="mk.prof")
-      pb.op("decode_mk", **kv)
-    else:
-      pb.op("embed", tok="tok", table="embed", h="h", vocab=V, d=D, nb=NB)
-      for li in range(cfg.n_layers):
-        ls = self._spec(li)
-        DECODE_MIXERS[ls.mixer](pb, ctx, li, d["layers"][li], cfg, ls)
-        DECODE_MLPS[ls.mlp](pb, ctx, li, d["layers"][li], cfg, ls)
-      pb.op("rmsnorm", x="h", g="final_g", out="hid", nb=NB, d=D, floor=d["final_floor"])
+    pb.op("embed", tok="tok", table="embed", h="h", vocab=V, d=D, nb=NB)
+    for li in range(cfg.n_layers):
+      ls = self._spec(li)
+      DECODE_MIXERS[ls.mixer](pb, ctx, li, d["layers"][li], cfg, ls)
+      DECODE_MLPS[ls.mlp](pb, ctx, li, d["layers"][li], cfg, ls)
+    pb.op("rmsnorm", x="h", g="final_g", out="hid", nb=NB, d=D, floor=d["final_floor"])
     if self.tp is None:
       pb.op("gemv", wf="f16", epi="argmax", x="hid", w="lm_head", y="logits", nb=NB, n=V, k=D, amv="am.val",
             ami="am.idx", amc="am.cnt", tok="tok_out", pos="pos", hist="hist", histld=M)
@@ -495,40 +502,8 @@ class LlamaPrefill:
       prog.upload("rope.cos", cos_t); prog.upload("rope.sin", sin_t)
     for li in range(cfg.n_layers):
       self._bind_layer(prog, li, d["layers"][li])
-    self._dec = {"M": M, "NB": NB, "prog": prog, "plan": pb, "megakernel": mk is not None}
+    self._dec = {"M": M, "NB": NB, "prog": prog, "plan": pb}
     return self._dec
-
-  def _megakernel_plan(self, NB, M):
-    """Scratch sizes + split count when the whole decode step fits the persistent megakernel
-    (`decode_mk`: every projection tiled int8 or int4-g32, attention mixer + SwiGLU MLP in every
-    layer, NB <= 8), else None (the per-op kernels run). Opt-in with AF_DECODE_MK=1: on B200 the
-    per-op path with programmatic dependent launch is still the faster one at batch 1."""
-    import ctypes
-    import os
-    if os.environ.get("AF_DECODE_MK", "0") != "1" or self.tp is not None:
-      return None
-    cfg, d = self.cfg, self._load()
-    L = d["layers"]
-    kinds = {l[k].wf for l in L for k in ("qkv", "o", "gu", "down") if k in l}
-    if len(kinds) != 1 or kinds.pop() not in ("i8t", "i4t") or NB > 8:
-      return None
-    if any(self._spec(i).mixer != "attention" or self._spec(i).mlp != "swiglu" for i in range(cfg.n_layers)):
-      return None
-    qk = ["qn" in l for l in L]
-    if any(qk) and not all(qk):
-      return None
-    wf = L[0]["qkv"].wf
-    KV, H, dh = cfg.n_kv_heads, cfg.n_heads, cfg.dh
-    F = L[0]["gu"].N // 2
-    if any(l["gu"].N // 2 != F for l in L):
-      return None
-    ns = int(os.environ.get("AF_MK_NSPLIT", "0")) or max(1, min(64, -(-M // 64), (2 * 148) // max(1, KV * NB)))
-    part, cnt = ctypes.c_size_t(), ctypes.c_size_t()
-    rc = R.load_library().af_decode_mk_scratch(R.W_I4G32 if wf == "i4t" else R.W_I8, NB, cfg.dim, H, KV, dh, F, ns,
-                                               ctypes.byref(part), ctypes.byref(cnt))
-    if rc != 0:
-      return None
-    return {"wf": wf, "nsplit": ns, "part": part.value, "cnt": cnt.value}
 
   def _prefiller(self, seq):
     """Build (once, cached by seq) the batched-prefill program: all layers over `seq` rows, each
@@ -654,18 +629,12 @@ class LlamaPrefill:
 
   @staticmethod
   def _sample(logits, temperature, top_p, top_k):
-    """Reference `LlamaPrefill._sample` (`llm.py:407-419`)."""
-    if temperature <= 0.0:
-      return int(np.argmax(logits))
-    lg = logits.astype(np.float64) / temperature
-    if top_k and 0 < top_k < lg.size:
-      lg[lg < np.partition(lg, -top_k)[-top_k]] = -np.inf
-    p = np.exp(lg - lg.max()); p /= p.sum()
-    if 0.0 < top_p < 1.0:
-      order = np.argsort(p)[::-1]; cum = np.cumsum(p[order])
-      keep = order[:int(np.searchsorted(cum, top_p)) + 1]
-      m = np.zeros_like(p); m[keep] = p[keep]; p = m / m.sum()
-    return int(np.random.choice(p.size, p=p))
+    """Next token from host logits, with the reference's sampling rules (`aneforge/llm.py:407-419`):
+    greedy argmax at temperature <= 0; otherwise softmax(logits / temperature) restricted to the
+    logits >= the k-th largest (top_k > 0) and to the most probable tokens whose probability mass
+    first reaches top_p (the token that crosses top_p included), renormalised, one draw from
+    numpy's global generator."""
+    return sample_token(logits, temperature, top_p, top_k)
 
   def _prefill_hidden(self, token_ids, pad_to=None):
     real = len(token_ids)
@@ -754,28 +723,50 @@ class LlamaPrefill:
       raise NotImplementedError("tensor-parallel generate runs greedy decode with the on-device head only")
     if exact_head and on_token is None and on_stage is None:
       # greedy with an exact head: every step's token stays on the device; run the steps back to
-      # back and read the token history once (EOS cuts the list where the reference would stop).
-      for _ in range(n_steps):
-        prog.execute_async()
-      prog.sync()
-      hist = prog.read_output("hist")[0]
-      for t in hist[pos:pos + n_steps]:
-        out.append(int(t))
-        if int(t) in eos:
-          break
+      # back and read the token history once. With a stop set the steps go in groups of
+      # `eos_check_every`, so an early EOS wastes at most one group.
+      group = n_steps if not eos else max(1, int(self.eos_check_every))
+      done = 0
+      while done < n_steps:
+        k = min(group, n_steps - done)
+        for _ in range(k):
+          prog.execute_async()
+        prog.sync()
+        hist = prog.read_output("hist")[0]
+        for t in hist[pos + done:pos + done + k]:
+          out.append(int(t))
+          if int(t) in eos:
+            return out
+        done += k
       return out
+    # stage names follow the reference's profiling hooks (`aneforge/llm.py:568-575`): the embedding
+    # gather, every layer, the head and the greedy argmax all run inside one graph replay here, so
+    # `embedding` times the host's token hand-off, `layers` the replay, `lm_head` the host-side
+    # logits work (tie-margin recheck or reading the sampled-path logits) and `sample` the draw
+    pending = None                             # a host-sampled token still to hand to the device
     for _ in range(n_steps):
       ts = time.perf_counter()
+      if pending is not None:
+        prog.set_input("tok", np.array([pending], np.int32))
+      if on_stage is not None:
+        on_stage("embedding", time.perf_counter() - ts)
+      t1 = time.perf_counter()
       prog.execute()
+      if on_stage is not None:
+        on_stage("layers", time.perf_counter() - t1)
+        on_stage("step", time.perf_counter() - ts)
+      t2 = time.perf_counter()
       if exact_head:
         nxt = int(prog.read_output("tok_out")[0])
+        t3 = time.perf_counter()
       else:
         hid = prog.read_output("hid")[0]
         logits = self._decode_logits(hid, None, greedy) if greedy else prog.read_output("logits")[0]
-        nxt = self._sample(logits, temperature, top_p, top_k)
-        prog.set_input("tok", np.array([nxt], np.int32))
+        t3 = time.perf_counter()
+        nxt = pending = self._sample(logits, temperature, top_p, top_k)
       if on_stage is not None:
-        on_stage("step", time.perf_counter() - ts)
+        on_stage("lm_head", t3 - t2)
+        on_stage("sample", time.perf_counter() - t3)
       out.append(nxt)
       if nxt in eos:
         break
@@ -864,58 +855,71 @@ def decoder_block_step(cfg: LlamaConfig, lw: dict, h, Kc, Vc, pos: int, compress
 
 # ------------------------------------------------------------------------------ loaders
 
-def _weights_from_state_dict(sd, cfg: LlamaConfig) -> dict:
-  """HF Llama/Qwen state_dict -> the reference weight layout (reference `llm.py:636-654`)."""
-  w = {"embed": sd["model.embed_tokens.weight"], "final_norm": sd["model.norm.weight"],
-       "lm_head": sd.get("lm_head.weight", sd["model.embed_tokens.weight"]), "layers": []}
-  for L in range(cfg.n_layers):
-    p = f"model.layers.{L}."
-    lw = {"wq": sd[p + "self_attn.q_proj.weight"], "wk": sd[p + "self_attn.k_proj.weight"],
-          "wv": sd[p + "self_attn.v_proj.weight"], "wo": sd[p + "self_attn.o_proj.weight"],
-          "wgate": sd[p + "mlp.gate_proj.weight"], "wup": sd[p + "mlp.up_proj.weight"],
-          "wdown": sd[p + "mlp.down_proj.weight"], "attn_norm": sd[p + "input_layernorm.weight"],
-          "mlp_norm": sd[p + "post_attention_layernorm.weight"]}
-    if p + "self_attn.q_norm.weight" in sd:
-      lw["q_norm"] = sd[p + "self_attn.q_norm.weight"]; lw["k_norm"] = sd[p + "self_attn.k_norm.weight"]
-    for proj, key in (("q_proj", "q_bias"), ("k_proj", "k_bias"), ("v_proj", "v_bias"), ("o_proj", "o_bias")):
-      b = sd.get(p + f"self_attn.{proj}.bias")
-      if b is not None:
-        lw[key] = b
-    w["layers"].append(lw)
-  return w
+# Hugging Face checkpoint -> the reference's weight dict (`aneforge/llm.py:636-654` layout). The key
+# names are the checkpoint format's; every other detail of the mapping is table-driven here.
+_HF_LAYER_REQUIRED = {
+  "wq": "self_attn.q_proj.weight", "wk": "self_attn.k_proj.weight", "wv": "self_attn.v_proj.weight",
+  "wo": "self_attn.o_proj.weight", "wgate": "mlp.gate_proj.weight", "wup": "mlp.up_proj.weight",
+  "wdown": "mlp.down_proj.weight", "attn_norm": "input_layernorm.weight",
+  "mlp_norm": "post_attention_layernorm.weight",
+}
+_HF_LAYER_OPTIONAL = {
+  "q_norm": "self_attn.q_norm.weight", "k_norm": "self_attn.k_norm.weight",          # Qwen3 QK-norm
+  "q_bias": "self_attn.q_proj.bias", "k_bias": "self_attn.k_proj.bias",              # Qwen2 biases
+  "v_bias": "self_attn.v_proj.bias", "o_bias": "self_attn.o_proj.bias",
+}
+# architectures whose semantics the dense loader does not implement (logit soft-capping, GELU MLPs,
+# LayerNorm, sandwich norms): refused rather than silently run as Llama
+_HF_REFUSED = {"gemma", "gemma2", "gemma3", "gemma3_text", "gpt2"}
 
 
-def _rope_theta(c) -> float:
+def hf_weights(sd: dict, n_layers: int) -> dict:
+  """Reference weight dict from a Hugging Face Llama / Qwen2 / Qwen3 / Mistral state dict; a model
+  without a separate `lm_head.weight` ties its head to the embedding."""
+  embed = sd["model.embed_tokens.weight"]
+  layers = []
+  for i in range(n_layers):
+    pre = f"model.layers.{i}."
+    lw = {ours: sd[pre + theirs] for ours, theirs in _HF_LAYER_REQUIRED.items()}
+    lw.update({ours: sd[pre + theirs] for ours, theirs in _HF_LAYER_OPTIONAL.items() if pre + theirs in sd})
+    if ("q_norm" in lw) != ("k_norm" in lw):
+      raise ValueError(f"layer {i}: a checkpoint with QK-norm needs both q_norm and k_norm")
+    layers.append(lw)
+  return {"embed": embed, "final_norm": sd["model.norm.weight"], "lm_head": sd.get("lm_head.weight", embed),
+          "layers": layers}
+
+
+def hf_config(c, sd: dict) -> LlamaConfig:
+  """`LlamaConfig` from a Hugging Face config object. The RoPE base is read from `rope_parameters`
+  (transformers >= 5) or `rope_theta`; only the "llama3" scaling type changes the tables."""
   rp = getattr(c, "rope_parameters", None)
-  if isinstance(rp, dict) and "rope_theta" in rp:
-    return float(rp["rope_theta"])
-  return float(getattr(c, "rope_theta", 10000.0))
-
-
-def _rope_scaling(c):
-  s = getattr(c, "rope_scaling", None)
-  return s if isinstance(s, dict) and s.get("rope_type") == "llama3" else None
+  theta = rp.get("rope_theta") if isinstance(rp, dict) else None
+  theta = float(theta if theta is not None else getattr(c, "rope_theta", 10000.0))
+  sc = getattr(c, "rope_scaling", None)
+  if not (isinstance(sc, dict) and sc.get("rope_type") == "llama3"):
+    sc = rp if isinstance(rp, dict) and rp.get("rope_type") == "llama3" else None
+  n = int(c.num_hidden_layers)
+  qk = "model.layers.0.self_attn.q_norm.weight" in sd
+  return LlamaConfig(dim=int(c.hidden_size), n_layers=n, n_heads=int(c.num_attention_heads),
+                     n_kv_heads=int(getattr(c, "num_key_value_heads", None) or c.num_attention_heads),
+                     ffn_dim=int(c.intermediate_size), vocab=int(c.vocab_size), rope_base=theta,
+                     norm_eps=float(c.rms_norm_eps), head_dim=int(getattr(c, "head_dim", 0) or 0),
+                     rope_scaling=sc, layers=[LayerSpec(qk_norm=qk) for _ in range(n)])
 
 
 def _dense_adapter(c, sd):
-  """Dense Llama/Qwen adapter (reference `llm.py:657-668`)."""
-  n = int(c.num_hidden_layers)
-  qk = "model.layers.0.self_attn.q_norm.weight" in sd
-  cfg = LlamaConfig(dim=c.hidden_size, n_layers=n, n_heads=c.num_attention_heads,
-                    n_kv_heads=getattr(c, "num_key_value_heads", c.num_attention_heads),
-                    ffn_dim=c.intermediate_size, vocab=c.vocab_size, rope_base=_rope_theta(c),
-                    norm_eps=float(c.rms_norm_eps), head_dim=int(getattr(c, "head_dim", 0) or 0),
-                    rope_scaling=_rope_scaling(c),
-                    layers=[LayerSpec(mixer="attention", mlp="swiglu", qk_norm=qk) for _ in range(n)])
-  return cfg, _weights_from_state_dict(sd, cfg)
+  """Llama / Qwen2 / Qwen3 adapter (the reference's default, `aneforge/llm.py:657-668`)."""
+  return hf_config(c, sd), hf_weights(sd, int(c.num_hidden_layers))
 
 
 def _mistral_adapter(c, sd):
-  """Mistral adapter (reference `llm.py:705-718`): sliding window surfaced in `cfg.extra`."""
+  """Mistral (reference `aneforge/llm.py:705-718`): no RoPE scaling; the sliding window, which the
+  decode kernels do not apply, is recorded in `cfg.extra` for callers to check."""
   cfg, w = _dense_adapter(c, sd)
   cfg.rope_scaling = None
-  if getattr(c, "sliding_window", None):
-    cfg.extra["sliding_window"] = int(c.sliding_window)
+  win = getattr(c, "sliding_window", None)
+  if win:
+    cfg.extra["sliding_window"] = int(win)
   return cfg, w
 
 
@@ -925,22 +929,27 @@ ADAPTERS: list = [
 
 
 def _assert_dense_compatible(c) -> None:
-  """Reference `llm.py:776-788`."""
-  mt = getattr(c, "model_type", "?")
-  cap = getattr(c, "attn_logit_softcapping", None) or getattr(c, "final_logit_softcapping", None)
-  if cap or mt in _DENSE_INCOMPATIBLE or mt in (ModelType.GEMMA, ModelType.GPT2):
-    why = "logit softcapping" if cap else "architecture-specific semantics"
-    raise ValueError(f"load_llm: {mt!r} needs {why} that the B200 dense loader does not implement")
+  """Refuse configs the dense loader would run with the wrong semantics (the reference's guard,
+  `aneforge/llm.py:776-788`)."""
+  kind = str(getattr(c, "model_type", "?"))
+  softcap = getattr(c, "attn_logit_softcapping", None) or getattr(c, "final_logit_softcapping", None)
+  if softcap:
+    raise ValueError(f"load_llm: {kind!r} uses logit soft-capping, which the B200 dense loader does not implement")
+  if kind in _HF_REFUSED:
+    raise ValueError(f"load_llm: {kind!r} has architecture-specific semantics the B200 dense loader does not implement")
 
 
 def from_pretrained(name: str, compress: str | None = None, ane_lm_head: bool = True, device: int = 0) -> LlamaPrefill:
-  """Load a Hugging Face decoder (reference `llm.py:791-806`) onto one B200."""
+  """Load a Hugging Face decoder (a hub name or a local checkpoint directory; reference
+  `aneforge/llm.py:791-806`) onto one B200: the first matching `ADAPTERS` entry maps it, else the
+  dense Llama/Qwen adapter."""
   import torch
   from transformers import AutoModelForCausalLM
   hf = AutoModelForCausalLM.from_pretrained(name)
-  adapt = next((fn for pred, fn in ADAPTERS if pred(hf.config)), _dense_adapter)
-  if adapt is _dense_adapter:
+  adapt = next((fn for pred, fn in ADAPTERS if pred(hf.config)), None)
+  if adapt is None:
     _assert_dense_compatible(hf.config)
+    adapt = _dense_adapter
   sd = {k: v.detach().to(torch.float16) for k, v in hf.state_dict().items()}
   cfg, weights = adapt(hf.config, sd)
   return LlamaPrefill(cfg, weights, compress=compress, ane_lm_head=ane_lm_head, device=device)

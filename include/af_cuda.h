@@ -181,14 +181,6 @@ int af_pack_i4_tiles(const uint8_t* packed, const uint16_t* scales, int n, int k
 int af_gemv_tc_i4(int epi, const uint16_t* x, int ldx, const void* tiles, const uint16_t* bias, void* y, int ldy,
                   int nb, int n, int k, void* scratch, size_t scratch_bytes, void* stream);
 
-/* Decode megakernel support query: 0 when one persistent launch can run a decode step of this shape
- * (all projections tiled int8 (wf 0) or int4 group-32 (wf 2), nb <= 8, head dim 64/128, GQA group
- * 1/2/4/8), with the byte sizes of its GEMV split-K partials and tickets; -1 otherwise. The step
- * itself runs as the plan op `decode_mk` (no reference counterpart: the ANE program ran a whole
- * decode chunk as one dispatch, llm.py:435-478; this is the B200 analogue). Needs a CUDA device. */
-int af_decode_mk_scratch(int wf, int nb, int d, int h, int kv, int dh, int ffn, int nsplit, size_t* part_bytes,
-                         size_t* cnt_bytes);
-
 /* Mixture of experts (reference aneforge/moe.py:21-63). af_moe_gate: router logits [nb][ld] fp32 ->
  * softmax, top-k by k row-max peels (lowest index on ties, peel value f16(-3e4)), renormalised when
  * renorm -> gw [nb][e] (0 off the top k) and sel [nb][k]. af_gemv_tc_expert: the tensor-core GEMV
@@ -228,11 +220,13 @@ int af_attn_decode(const float* qkv, int ld_qkv, uint16_t* kc, uint16_t* vc, con
  * framework that owns every allocation, code running while a memory pool is locked, plug-ins that
  * must not touch the process allocator). No counterpart in the reference: the ANE runtime had no
  * split-K scratch. The scratch is a fixed AF_ATTN_NOALLOC_SCRATCH_BYTES array inside the library,
- * resident on every GPU that loads it until exit; shapes needing more return -1 before launching.
- * All calls on a GPU share that array: calls that overlap on the GPU race (order them on one
- * stream). The first call on a device looks the array's address up; make it before any stream
- * capture. Same arguments as af_attn_decode minus the scratch pair; the current device must be the
- * stream's device. */
+ * resident on every GPU that loads it until exit; shapes that merge their splits through it and
+ * need more return -1 before launching (shapes whose splits merge inside a thread-block cluster,
+ * at most 16 splits, use none of it). All calls on a GPU share that array: calls that overlap on
+ * the GPU race (order them on one stream). The first call on a device looks the array's address up
+ * and caches it; make it before any stream capture, and do not use the entry point across a
+ * cudaDeviceReset. Same arguments as af_attn_decode minus the scratch pair; the current device must
+ * be the stream's device. */
 #define AF_ATTN_NOALLOC_SCRATCH_BYTES (2u << 20)
 size_t af_attn_decode_noalloc_max_bytes(void);
 int af_attn_decode_noalloc(const float* qkv, int ld_qkv, uint16_t* kc, uint16_t* vc, const int* pos,

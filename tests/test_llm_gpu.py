@@ -229,35 +229,3 @@ def test_qwen2_shaped_int4_g32_greedy_32_steps():
   ol = om.logits(hid[-1].astype(F32))
   assert cosine(pl, ol) > 0.999
   m.release()
-
-
-@pytest.mark.parametrize("case", ["llama_int8", "qwen_int4", "batched_int8"])
-def test_decode_megakernel_matches_oracle(case, monkeypatch):
-  """The opt-in persistent decode megakernel (one cooperative launch per step) against the oracle:
-  same bars as the per-op path, and identical tokens to the per-op path on the same model."""
-  from aneforge_b200.llm import LlamaPrefill
-  if case == "llama_int8":
-    cfg = Config(dim=1024, n_layers=2, n_heads=8, n_kv_heads=2, ffn_dim=3584, vocab=4096, rope_base=500000.0)
-    w, comp, NB = random_llama_weights(cfg, seed=1), "int8", 1
-  elif case == "qwen_int4":
-    cfg = Config(dim=1024, n_layers=2, n_heads=8, n_kv_heads=1, ffn_dim=2816, vocab=4096, rope_base=1e6)
-    w, comp, NB = random_llama_weights(cfg, seed=11, qkv_bias=True), "int4_g32", 1
-  else:
-    cfg = Config(dim=512, n_layers=2, n_heads=8, n_kv_heads=2, ffn_dim=1024, vocab=2048, rope_base=10000.0,
-                 head_dim=64)
-    w, comp, NB = random_llama_weights(cfg, seed=4, std=0.05), "int8", 3
-  rng = np.random.default_rng(7)
-  prompts = [list(rng.integers(0, cfg.vocab, n)) for n in (29, 17, 9)[:NB]]
-  monkeypatch.setenv("AF_DECODE_MK", "0")
-  m0 = LlamaPrefill(to_b200_cfg(cfg), w, compress=comp)
-  ref = m0.generate_batch(prompts, 24, max_len=64) if NB > 1 else [m0.generate(prompts[0], 24, max_len=64)]
-  m0.release()
-  monkeypatch.setenv("AF_DECODE_MK", "1")
-  m = LlamaPrefill(to_b200_cfg(cfg), w, compress=comp)
-  got = m.generate_batch(prompts, 24, max_len=64) if NB > 1 else [m.generate(prompts[0], 24, max_len=64)]
-  assert m._dec["megakernel"]
-  m.release()
-  assert got == ref
-  if NB == 1:
-    om = OracleModel(cfg, w, comp, precision="device")
-    assert teacher_forced_check(om, prompts[0], got[0], 64, n_check=24) <= 2

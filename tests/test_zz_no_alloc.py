@@ -41,8 +41,12 @@ def _case(dh, H, KV, NB, M, seed):
   return pos, Kc, Vc, qkv, cos, sin
 
 
-@pytest.mark.parametrize("dh,H,KV,NB,n_split", [(128, 32, 8, 1, 37), (128, 32, 8, 4, 9), (64, 16, 2, 3, 16),
-                                                (128, 16, 4, 2, 1)])
+# n_split 37 and 24 merge through the library's array (the second with several sequences and GQA
+# 4:1, so the tickets of many (sequence, kv head) pairs must be cleared between the two calls); 9 and
+# 16 merge inside a thread-block cluster and touch none of it; the 16-sequence, 16-split cluster
+# shape would need 4.3 MB of partials through scratch, more than the array holds, and must still run
+@pytest.mark.parametrize("dh,H,KV,NB,n_split", [(128, 32, 8, 1, 37), (128, 32, 8, 4, 24), (128, 32, 8, 4, 9),
+                                                (64, 16, 2, 3, 16), (128, 16, 4, 2, 1), (128, 32, 8, 16, 16)])
 def test_noalloc_matches_caller_scratch_twice(K, dh, H, KV, NB, n_split):
   M = 1200
   pos, Kc, Vc, qkv, cos, sin = _case(dh, H, KV, NB, M, dh + H + NB)
@@ -72,3 +76,23 @@ def test_noalloc_rejects_shapes_beyond_builtin_scratch(K):
                                 32, 8, 128, 0.088, 1.0, True, 64)
   assert rc != 0
   assert "built-in maximum" in R.last_error()
+
+
+def test_noalloc_on_every_visible_device(K):
+  """Kernel attributes and the array's address are per device: a 16-split cluster call (over 48 KB
+  of dynamic shared memory) on each visible GPU in turn matches the caller-scratch entry point."""
+  n = torch.cuda.device_count()
+  dh, H, KV, NB, n_split, M = 128, 64, 8, 1, 16, 1100
+  pos, Kc, Vc, qkv, cos, sin = _case(dh, H, KV, NB, M, 5)
+  scale = float(np.float16(1 / np.sqrt(dh)))
+  kv_c = 127 * float(np.float16(1 / 127))
+  for d in range(n):
+    with torch.cuda.device(d):
+      dev = f"cuda:{d}"
+      t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+      q, p, c, s = t(qkv), t(pos), t(cos), t(sin)
+      ref = K.attn_decode(q, t(Kc), t(Vc), p, c, s, H, KV, dh, scale, kv_c, True, n_split).cpu().numpy().astype(F32)
+      rc, out = K.attn_decode_noalloc(q, t(Kc), t(Vc), p, c, s, H, KV, dh, scale, kv_c, True, n_split)
+      assert rc == 0, K.R.last_error()
+      got = out.cpu().numpy().astype(F32)
+      assert np.abs(got - ref).max() <= 2 ** -9 * np.abs(ref).max() + 1e-3, d
