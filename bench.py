@@ -148,49 +148,47 @@ class ClockSampler:
             "samples": len(self.samples), "source": "nvml"}
 
 
-class _LazyLayers:
-  """The model's layer list, generated on access (seeded per layer) and not kept: a 72B model's fp16
-  weights (145 GB) never exist at once, only the packed int4 copy the loader keeps."""
-
-  def __init__(self, cfg, device, seed, qkv_bias, moe=False):
-    self.cfg, self.device, self.seed, self.qkv_bias, self.moe = cfg, device, seed, qkv_bias, moe
-
-  def __len__(self):
-    return self.cfg.n_layers
-
-  def __getitem__(self, i):
-    import torch
-    if not 0 <= i < len(self):
-      raise IndexError(i)
-    cfg, dev = self.cfg, self.device
-    g = torch.Generator(device=dev)
-    g.manual_seed(self.seed * 1000 + i)
-    R = lambda *s: (torch.randn(*s, generator=g, device=dev, dtype=torch.float32) * 0.02).half()
-    D, dh = cfg.dim, cfg.dh
-    lw = {"wq": R(cfg.n_heads * dh, D), "wk": R(cfg.n_kv_heads * dh, D), "wv": R(cfg.n_kv_heads * dh, D),
-          "wo": R(D, cfg.n_heads * dh), "attn_norm": torch.ones(D, device=dev), "mlp_norm": torch.ones(D, device=dev)}
-    if self.moe:
-      E, F = cfg.extra["n_experts"], cfg.ffn_dim
-      lw.update(router=R(E, D), wgate_exps=R(E, F, D), wup_exps=R(E, F, D), wdown_exps=R(E, F, D))
-    else:
-      lw.update(wgate=R(cfg.ffn_dim, D), wup=R(cfg.ffn_dim, D), wdown=R(D, cfg.ffn_dim))
-    if self.qkv_bias:
-      lw.update(q_bias=R(cfg.n_heads * dh), k_bias=R(cfg.n_kv_heads * dh), v_bias=R(cfg.n_kv_heads * dh))
-    return lw
-
-  def __iter__(self):
-    return (self[i] for i in range(len(self)))
-
-
 def make_weights(cfg, device, seed=0, qkv_bias=False, moe=False):
-  """Seeded N(0, 0.02) fp16 weights generated on the device, reference dict layout (layers lazily)."""
-  import torch
-  g = torch.Generator(device=device)
-  g.manual_seed(seed)
-  R = lambda *s: (torch.randn(*s, generator=g, device=device, dtype=torch.float32) * 0.02).half()
-  D = cfg.dim
-  return {"embed": R(cfg.vocab, D), "lm_head": R(cfg.vocab, D), "final_norm": torch.ones(D, device=device),
-          "layers": _LazyLayers(cfg, device, seed, qkv_bias, moe)}
+  """Seeded N(0, 0.02) fp16 weights generated on the device (`aneforge_b200.synthetic`)."""
+  from aneforge_b200.synthetic import make_weights as mw
+  return mw(cfg, device, seed=seed, qkv_bias=qkv_bias, moe=moe)
+
+
+def decode_cache_len(args):
+  """Cache rows of the timed decode program: every step (warm-up, timed, e2e) fits."""
+  e2e_steps = max(8, args.steps // 2)
+  return PROMPT + args.warmup + args.steps + e2e_steps + 8, e2e_steps
+
+
+def workload_config(args, ws, tp_on):
+  """The `config` object of the JSON line; both arms print the same one."""
+  spec = MODELS[MODEL]
+  NB = args.batch
+  units = 1 if tp_on else ws
+  M, _ = decode_cache_len(args)
+  from types import SimpleNamespace
+  cfg = SimpleNamespace(**{k: v for k, v in CFG.items() if k != "extra"}, extra=CFG.get("extra", {}),
+                        dh=CFG["dim"] // CFG["n_heads"])
+  step_bytes = algorithmic_bytes_per_step(cfg, NB, PROMPT + args.warmup + args.steps // 2, spec["compress"],
+                                          spec["qkv_bias"], spec.get("moe_compress"))
+  return {"workload": spec["workload"], "model": MODEL + "-shaped", "global_batch": NB * units, "batch_per_gpu": NB,
+          "seq_len": PROMPT, "decode_pos": f"{PROMPT}..{M}",
+          "parallelism": f"tp{ws}" if tp_on else (f"replicas{ws}" if ws > 1 else "single"),
+          "l2": f"weights {step_bytes / 1e9:.1f} GB per step >> 126 MB L2 (no flush needed)"}
+
+
+def host_info():
+  """The host cores the CPU baseline ran on."""
+  model = None
+  try:
+    out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+    for line in out.splitlines():
+      if line.lower().startswith("model name"):
+        model = line.split(":", 1)[1].strip()
+        break
+  except Exception:
+    pass
+  return {"cpu_count": os.cpu_count(), "lscpu_model": model, "blas_threads": blas_threads()}
 
 
 def _proj_bytes(n_params, rows, fmt):
@@ -259,9 +257,9 @@ def run_b200(args):
   if ws > 1:
     dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=600))
   tp = None
-  if args.tp and ws > 1:
+  if ws > 1 and not args.replicas:
     # one model sharded over the ranks (tensor parallel, strong scaling): same weights and prompt on
-    # every rank; otherwise every rank runs its own replica on its own sequences (weak scaling)
+    # every rank; with --replicas every rank runs its own replica on its own sequences (weak scaling)
     from aneforge_b200.tp import TensorParallel
     tp = TensorParallel.from_torch_distributed(local)
   spec = MODELS[MODEL]
@@ -276,8 +274,7 @@ def run_b200(args):
   del w
   torch.cuda.empty_cache()
   load_s = time.perf_counter() - t_load
-  e2e_steps = max(8, args.steps // 2)
-  M = PROMPT + args.warmup + args.steps + e2e_steps + 8      # every step (timed, warm-up, e2e) fits the cache
+  M, e2e_steps = decode_cache_len(args)
   rng = np.random.default_rng(99 + (0 if tp else rank))
   prompts = [list(rng.integers(0, cfg.vocab, PROMPT)) for _ in range(NB)]
   dec = m._decoder(M, NB)
@@ -385,10 +382,7 @@ def run_b200(args):
       "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
       "scaling": "strong" if tp else "weak",
       "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic",
-      "config": {"workload": spec["workload"], "model": MODEL + "-shaped",
-                 "global_batch": NB * units, "batch_per_gpu": NB, "seq_len": PROMPT, "decode_pos": f"{PROMPT}..{M}",
-                 "parallelism": f"tp{ws}" if tp else (f"replicas{ws}" if ws > 1 else "single"),
-                 "l2": f"weights {step_bytes / 1e9:.1f} GB per step >> 126 MB L2 (no flush needed)"},
+      "config": workload_config(args, ws, tp is not None),
       "e2e": {"value": round(e2e_tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * NB,
               "d2h_bytes_per_step": 4 * NB,
               "how": "program API, pinned host token ids in/out every step, host sync per step"},
@@ -410,6 +404,38 @@ def run_b200(args):
   torch.cuda.synchronize()
   import gc
   gc.collect()
+
+  # ---- end to end through `LlamaPrefill.generate` (the reference's public call, llm.py:560-633):
+  # host prompt ids in, the benchmark prompt prefilled, `--gen-tokens` greedy tokens back on the
+  # host. One untimed call builds the programs; then the time to first token (prefill + the head's
+  # argmax) and the whole call are timed on the host clock (each call ends with a device sync)
+  gen = None
+  G = args.gen_tokens
+  if NB == 1 and G > 0:
+    Mg = PROMPT + G + 8
+    p0 = prompts[0]
+    m.generate(p0, G, max_len=Mg)
+    if ws > 1:
+      dist.barrier()
+    t0 = time.perf_counter()
+    m.generate(p0, 1, max_len=Mg)
+    ttft = time.perf_counter() - t0
+    if ws > 1:
+      dist.barrier()
+    t0 = time.perf_counter()
+    toks = m.generate(p0, G, max_len=Mg)
+    total = time.perf_counter() - t0
+    if ws > 1:
+      t = torch.tensor([ttft, total], device=dev, dtype=torch.float64)
+      dist.all_reduce(t, op=dist.ReduceOp.MAX)
+      ttft, total = (float(v) for v in t.tolist())
+    gen = {"tokens": len(toks), "prompt": PROMPT, "ttft_ms": round(ttft * 1e3, 2), "total_s": round(total, 4),
+           "tokens_per_s": round(len(toks) / total, 2),
+           "decode_tokens_per_s": round((len(toks) - 1) / max(total - ttft, 1e-9), 2),
+           "h2d_bytes": 4 * PROMPT, "d2h_bytes": 4 * len(toks),
+           "how": "LlamaPrefill.generate(prompt, max_new_tokens) on host ids, TTFT included, max over ranks"}
+  if result is not None and gen is not None:
+    result["e2e"]["generate"] = gen
   m.release()
   if tp is not None:
     tp.close()
@@ -622,36 +648,45 @@ def profile_traffic(name="gemv_tc_gate_up_llama8b.md"):
     return None
 
 
-def cpu_baseline(steps=3, layers=1):
-  """The reference path on the host: oracle decode of a `layers`-deep slice of the same model +
-  the full lm_head, scaled to the model's depth. Returns (tokens/s, description)."""
+def cpu_reference(steps=3, warmup=1, layers=1, max_steps=30):
+  """The reference path on the host: the oracle's decode of a `layers`-deep slice of the same model
+  plus the full lm_head and argmax, each step scaled to the model's depth (layer time x depth / layers
+  + head time). `warmup` untimed then `steps` timed steps (at most `max_steps`, so a run stays within
+  about a minute of host time). Returns (tokens/s, description, seconds per scaled step)."""
   from oracle.model import OracleModel, Config, random_llama_weights
   spec = MODELS[MODEL]
+  steps = max(1, min(int(steps), max_steps))
+  warmup = max(1, min(int(warmup), 5))
   cfg = Config(dim=CFG["dim"], n_layers=layers, n_heads=CFG["n_heads"], n_kv_heads=CFG["n_kv_heads"],
                ffn_dim=CFG["ffn_dim"], vocab=CFG["vocab"], rope_base=CFG["rope_base"], norm_eps=CFG["norm_eps"])
   w = random_llama_weights(cfg, seed=5, qkv_bias=spec["qkv_bias"])
   w["embed"] = np.zeros((cfg.vocab, cfg.dim), np.float16)   # only gathered rows are read; values do not change the time
   om = OracleModel(cfg, w, spec["compress"], precision="device")
-  M = PROMPT + steps + 2
+  M = PROMPT + warmup + steps + 2
   om._tables(M)
   caches = om.new_caches(M)
   rng = np.random.default_rng(1)
   for Kc, Vc in caches:
     Kc[:, :PROMPT] = rng.standard_normal(Kc[:, :PROMPT].shape, dtype=np.float32).astype(np.float16)
     Vc[:, :PROMPT] = rng.standard_normal(Vc[:, :PROMPT].shape, dtype=np.float32).astype(np.float16)
-  tok = 7
-  om.decode_step(tok, PROMPT - 1, caches)                 # warm BLAS / page in
+  tok, pos = 7, PROMPT
+  for _ in range(warmup):                                  # warm BLAS / page in
+    hid = om.decode_step(tok, pos, caches)
+    tok = int(np.argmax(om.logits(hid.astype(np.float32))))
+    pos += 1
   t_layers, t_head = 0.0, 0.0
-  for s in range(steps):
+  for _ in range(steps):
     t0 = time.perf_counter()
-    hid = om.decode_step(tok, PROMPT + s, caches)
+    hid = om.decode_step(tok, pos, caches)
     t1 = time.perf_counter()
     tok = int(np.argmax(om.logits(hid.astype(np.float32))))
     t2 = time.perf_counter()
     t_layers += t1 - t0; t_head += t2 - t1
+    pos += 1
   per_tok = t_layers / steps * (CFG["n_layers"] / layers) + t_head / steps
-  return 1.0 / per_tok, (f"{steps} decode steps of a {layers}-layer slice + full lm_head, scaled to "
-                         f"{CFG['n_layers']} layers")
+  return 1.0 / per_tok, (f"{steps} timed decode steps (after {warmup}) of a {layers}-layer slice at positions "
+                         f"{PROMPT}.., each plus the full {CFG['vocab']}-row lm_head and argmax, layer time scaled "
+                         f"to {CFG['n_layers']} layers"), per_tok
 
 
 def blas_threads():
@@ -670,7 +705,11 @@ def main():
   ap.add_argument("--batch", type=int, default=1)
   ap.add_argument("--model", default="llama3-8b", choices=sorted(MODELS))
   ap.add_argument("--tp", action="store_true",
-                  help="with --gpus N > 1: shard one model over the N ranks (tensor parallel) instead of N replicas")
+                  help="(the default with --gpus N > 1) shard one model over the N ranks: tensor parallel")
+  ap.add_argument("--replicas", action="store_true",
+                  help="with --gpus N > 1: N independent replicas (weak scaling) instead of tensor parallel")
+  ap.add_argument("--gen-tokens", type=int, default=128,
+                  help="tokens of the end-to-end LlamaPrefill.generate figure (0: skip)")
   ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
   ap.add_argument("--no-cpu-baseline", action="store_true")
   ap.add_argument("--kernel", default=None,
@@ -691,27 +730,27 @@ def main():
   if args.impl == "reference":
     if rank != 0:
       return
-    vals = []
-    for _ in range(max(1, min(args.steps, 3))):
-      v, how = cpu_baseline()
-      vals.append(v)
-    v = float(np.median(vals))
+    v, how, per_step = cpu_reference(args.steps, args.warmup)
+    tp_on = ws > 1 and not args.replicas
+    info = host_info()
     print(json.dumps({"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tokens/s",
                       "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-                      "scaling": "weak", "vs_baseline": None, "dtype": "int8 weights, fp32 numpy", "data": "synthetic",
-                      "config": {"workload": MODELS[MODEL]["workload"],
-                                 "global_batch": args.batch, "seq_len": PROMPT},
-                      "cpu_baseline": {"value": round(v, 4), "unit": "tokens/s", "cores": blas_threads(),
-                                       "kind": "port", "sample": how},
+                      "scaling": "strong" if tp_on else "weak", "vs_baseline": None,
+                      "dtype": MODELS[MODEL]["dtype"] + " (numpy fp32 on the host)", "data": "synthetic",
+                      "config": workload_config(args, ws, tp_on),
+                      "ms_per_step": round(per_step * 1e3, 2),
+                      "cpu_baseline": {"value": round(v, 4), "unit": "tokens/s", "cores": info["blas_threads"],
+                                       "kind": "port", "sample": how, **info},
                       "e2e": {"value": round(v, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                               "d2h_bytes_per_step": 0}}))
     return
   res = run_b200(args)
   if rank == 0 and res is not None:
     if not args.no_cpu_baseline and ws == 1:
-      v, how = cpu_baseline()
-      res["cpu_baseline"] = {"value": round(v, 4), "unit": "tokens/s", "cores": blas_threads(), "kind": "port",
-                             "sample": how}
+      v, how, _ = cpu_reference(3, 1)
+      info = host_info()
+      res["cpu_baseline"] = {"value": round(v, 4), "unit": "tokens/s", "cores": info["blas_threads"], "kind": "port",
+                             "sample": how, **info}
     print(json.dumps(res), flush=True)
 
 

@@ -135,6 +135,17 @@ class Linear:
     else:
       self.WT = np.ascontiguousarray(self.enc.deq.reshape(self.enc.deq.shape[0], -1).T)
 
+  @classmethod
+  def from_codes(cls, q: np.ndarray, s: np.ndarray, bias=None) -> "Linear":
+    """An int8 per-row Linear from codes [OUT, IN] and fp16 scales [OUT] already produced by the
+    per-row quantizer (`quant.quantize_per_row`), skipping the encode step."""
+    lin = cls.__new__(cls)
+    lin.enc = quant.Encoded("int8", None, (np.asarray(q, np.int8), np.asarray(s, F16)))
+    lin.bias = None if bias is None else np.asarray(bias, F32).astype(F16).astype(F32)
+    lin.qT = np.ascontiguousarray(np.asarray(q).astype(F32).T)
+    lin.s = np.asarray(s, F16).astype(F32)
+    return lin
+
   def __call__(self, x: np.ndarray) -> np.ndarray:
     if self.enc.kind == "int8":
       y = (x @ self.qT) * self.s
@@ -290,15 +301,24 @@ class OracleModel:
   def prefill_hidden(self, token_ids):
     """Batched prefill (reference `_prefiller`/`_attn_prefill_kv`, `llm.py:149-169`, `:489-519`).
     Returns (hidden [S, D] fp16 port, [(K [KV,S,dh] f16, V f16)] per layer)."""
+    ids = np.asarray(token_ids)
+    return self.causal_pass(np.asarray(self.embed[ids]), self.layers)
+
+  def causal_pass(self, rows, layers):
+    """The batched-prefill numerics over embedding rows [S, D] (fp16 port) through `layers`, an
+    iterable of encoded layers (`_encode_layer` output, or `encoded_layer_from_codes`) consumed one
+    at a time - a caller may build each layer on demand so that only one is in memory. Returns
+    (hidden [S, D] fp16, [(K, V)] per layer). Causal attention over the rows is also the decode
+    recurrence along the same tokens (teacher forcing): every matmul operand is rounded to fp16 in
+    device mode either way, so a cached fp16 K/V row and the fresh fp32 one enter alike."""
     cfg = self.cfg
     H, KV, dh = cfg.n_heads, cfg.n_kv_heads, cfg.dh
-    ids = np.asarray(token_ids)
-    S = len(ids)
+    S = int(np.shape(rows)[0])
     self._tables(S)
     c, s = self.cos[:S], self.sin[:S]
-    h = np.asarray(self.embed[ids]).astype(F16).astype(F32)
+    h = np.asarray(rows).astype(F16).astype(F32)
     kv = []
-    for L in self.layers:
+    for L in layers:
       q, k, v = self._qkv(L, h, S)
       q = rope(q.transpose(1, 0, 2), c, s)                         # [H, S, dh]
       k = rope(k.transpose(1, 0, 2), c, s); v = v.transpose(1, 0, 2)
@@ -307,6 +327,16 @@ class OracleModel:
       h = h + self._lin(L["wo"], a.transpose(1, 0, 2).reshape(S, H * dh))
       h = self._mlp(L, h)
     return rms_norm(h, self.final_g, self.final_floor).astype(F16), kv
+
+  def encoded_layer_from_codes(self, codes: dict, norms: dict):
+    """An encoded int8 layer from per-row codes: `codes` maps wq/wk/wv/wo/wgate/wup/wdown to
+    (q, s) or (q, s, bias); `norms` maps attn_norm/mlp_norm (and q_norm/k_norm) to gamma."""
+    L = {}
+    for key, parts in codes.items():
+      L[key] = Linear.from_codes(*parts)
+    for key, gamma in norms.items():
+      L[key] = rms_consts(gamma, self.cfg.norm_eps)
+    return L
 
   def logits(self, hidden_row) -> np.ndarray:
     """Host fp32 lm_head (reference `llm.py:349-355`)."""
