@@ -193,4 +193,70 @@ cudaError_t rope_kv_prefill_launch(const AttnPrefillArgs& a, __half* qbuf, cudaS
 // causal attention of the staged q rows against cache rows 0..i
 cudaError_t attn_prefill_with_q(const AttnPrefillArgs& a, const __half* qbuf, cudaStream_t st);
 
+// ---- generic graph ops (graph_ops.cu): what `compile(graph)` lowers nodes onto when no fused kernel
+// covers them. fp32 values, fp16-rounded matmul operands, rank <= GRAPH_MAX_RANK.
+constexpr int GRAPH_MAX_RANK = 5;
+enum GraphBinary : int { G_ADD = 0, G_SUB, G_MUL, G_DIV, G_MAX, G_MIN, G_POW, G_GT, G_GE, G_LT, G_LE, G_EQ, G_NE,
+                         G_SELECT };
+enum GraphUnary : int { U_RELU = 0, U_SILU, U_SIGMOID, U_TANH, U_EXP, U_SQRT, U_ABS, U_SQUARE, U_SIN, U_COS, U_ERF,
+                        U_LOG, U_RSQRT, U_INV, U_MULS, U_ADDS, U_CLIP, U_NOT, U_FLOOR, U_CEIL, U_ROUND, U_SIGN,
+                        U_GELU_TANH, U_GELU, U_SOFTPLUS };
+enum GraphReduce : int { RD_SUM = 0, RD_MEAN, RD_MAX, RD_MIN, RD_SUMSQ, RD_L2, RD_L1 };
+struct GraphEwArgs {          // y[i] = op(a[.], b[.]) (select: a ? b : c) over the output shape
+  const float* a = nullptr;
+  const float* b = nullptr;
+  const float* c = nullptr;
+  float* y = nullptr;
+  int op = 0, rank = 0;
+  long long n = 0;
+  long long shape[GRAPH_MAX_RANK] = {};
+  long long sa[GRAPH_MAX_RANK] = {}, sb[GRAPH_MAX_RANK] = {}, sc[GRAPH_MAX_RANK] = {};
+};
+struct GraphCopyArgs {        // y at strides sy <- x at strides sx, over `shape`
+  const float* x = nullptr;
+  float* y = nullptr;
+  int rank = 0;
+  long long n = 0;
+  long long shape[GRAPH_MAX_RANK] = {};
+  long long sx[GRAPH_MAX_RANK] = {}, sy[GRAPH_MAX_RANK] = {};
+};
+struct GraphReduceArgs {      // contiguous x of `shape`; reduce the axes whose bit is set in mask
+  const float* x = nullptr;
+  float* y = nullptr;
+  int op = 0, rank = 0, mask = 0;
+  long long n_out = 0;
+  long long shape[GRAPH_MAX_RANK] = {};
+};
+struct GraphLinearArgs {      // y[r][n] = (sum_k f16(x[r][k]) w[n][k]) * scale[n] + bias[n]
+  const float* x = nullptr;
+  const void* w = nullptr;    // int8 [N][K] codes (int8 != 0) or fp16 [N][K]
+  const __half* scale = nullptr;
+  const __half* bias = nullptr;
+  float* y = nullptr;
+  long long rows = 0, ldx = 0, ldy = 0, N = 0, K = 0;
+  int int8 = 0;
+};
+struct GraphBmmArgs {         // y[b][m][n] = sum_k f16(a) f16(b)
+  const float* a = nullptr;
+  const float* b = nullptr;
+  float* y = nullptr;
+  long long batch = 1, M = 0, N = 0, K = 0;
+  int brank = 0;
+  long long bshape[GRAPH_MAX_RANK] = {};
+  long long sa[GRAPH_MAX_RANK] = {}, sb[GRAPH_MAX_RANK] = {};
+  long long sam = 0, sak = 0, sbk = 0, sbn = 0;
+  int round_b = 1;            // 0: b is a baked weight used at full fp32 (bmm_weight)
+};
+cudaError_t graph_ew_launch(const GraphEwArgs& a, cudaStream_t st);
+cudaError_t graph_unary_launch(const float* x, float* y, long long n, int op, float k, float k2, cudaStream_t st);
+cudaError_t graph_copy_launch(const GraphCopyArgs& a, cudaStream_t st);
+cudaError_t graph_reduce_launch(const GraphReduceArgs& a, cudaStream_t st);
+cudaError_t graph_softmax_launch(const float* x, float* y, long long outer, long long n, long long inner, cudaStream_t st);
+cudaError_t graph_rms_launch(const float* x, float* y, const __half* g, float floor, long long rows, int d,
+                             cudaStream_t st);
+cudaError_t graph_layernorm_launch(const float* x, float* y, const __half* g, const __half* b, float eps,
+                                   long long rows, int d, cudaStream_t st);
+cudaError_t graph_linear_launch(const GraphLinearArgs& a, cudaStream_t st);
+cudaError_t graph_bmm_launch(const GraphBmmArgs& a, cudaStream_t st);
+
 }  // namespace af

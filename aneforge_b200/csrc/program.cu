@@ -155,6 +155,16 @@ struct OpCtx {
     }
     return p.bufs[root].dev;
   }
+  // comma-separated integers (graph shapes and strides); empty when the key is absent or "-"
+  std::vector<long long> ints(const char* k) {
+    std::vector<long long> v;
+    auto it = op.kv.find(k);
+    if (it == op.kv.end() || it->second == "-") return v;
+    std::stringstream ss(it->second);
+    std::string item;
+    while (std::getline(ss, item, ',')) v.push_back(strtoll(item.c_str(), nullptr, 10));
+    return v;
+  }
   std::vector<double> list(const char* k, size_t n) {
     std::vector<double> v;
     auto it = op.kv.find(k);
@@ -202,6 +212,159 @@ static int epi_of(const std::string& s) {
   if (s == "swiglu") return EPI_SWIGLU;
   if (s == "argmax") return EPI_ARGMAX;
   return -1;
+}
+
+// ------------------------------------------------------------------------------------ graph ops
+
+// elements an N-d view spans: 1 + sum over axes of (extent - 1) * stride (strides >= 0)
+static size_t view_span(const std::vector<long long>& shape, const std::vector<long long>& stride) {
+  long long hi = 0;
+  for (size_t d = 0; d < shape.size(); ++d) {
+    if (shape[d] <= 0) return 0;
+    hi += (shape[d] - 1) * stride[d];
+  }
+  return (size_t)hi + 1;
+}
+
+static bool fill_nd(const std::vector<long long>& v, long long (&out)[GRAPH_MAX_RANK]) {
+  if (v.size() > (size_t)GRAPH_MAX_RANK) return false;
+  for (size_t d = 0; d < v.size(); ++d) out[d] = v[d];
+  return true;
+}
+
+static long long numel_of(const std::vector<long long>& shape) {
+  long long n = 1;
+  for (long long d : shape) n *= d;
+  return n;
+}
+
+// The generic graph ops (`g_*`, graph_ops.cu). Every operand size is checked against its buffer
+// before anything launches, so a plan with a bad shape fails at compile time.
+static bool graph_op(OpCtx& c, const Op& op, bool dry, cudaStream_t st, cudaError_t& e, std::string& why) {
+  auto bad = [&](const std::string& m) { why = m; return false; };
+  auto rank_ok = [&](const std::vector<long long>& sh, const std::vector<long long>& st1) {
+    return !sh.empty() && sh.size() <= (size_t)GRAPH_MAX_RANK && st1.size() == sh.size();
+  };
+  if (op.kind == "g_ew") {
+    GraphEwArgs a;
+    const auto shape = c.ints("shape"), sa = c.ints("sa"), sb = c.ints("sb"), sc = c.ints("sc");
+    a.op = (int)c.i("op");
+    if (!rank_ok(shape, sa)) return bad("g_ew: bad shape / sa");
+    a.rank = (int)shape.size();
+    a.n = numel_of(shape);
+    fill_nd(shape, a.shape); fill_nd(sa, a.sa);
+    a.a = (const float*)c.ptr("a", 4 * view_span(shape, sa));
+    if (c.has("b")) {
+      if (sb.size() != shape.size()) return bad("g_ew: bad sb");
+      fill_nd(sb, a.sb);
+      a.b = (const float*)c.ptr("b", 4 * view_span(shape, sb));
+    }
+    if (a.op == G_SELECT) {
+      if (sc.size() != shape.size() || !a.b) return bad("g_ew select: needs b and c with strides");
+      fill_nd(sc, a.sc);
+      a.c = (const float*)c.ptr("c", 4 * view_span(shape, sc));
+    } else if (a.op < 0 || a.op > G_NE) {
+      return bad("g_ew: unknown op");
+    }
+    a.y = (float*)c.ptr("y", 4 * (size_t)a.n);
+    if (!c.err.empty()) return bad(c.err);
+    if (!dry) e = graph_ew_launch(a, st);
+  } else if (op.kind == "g_un") {
+    const long long n = c.i("n");
+    const int u = (int)c.i("op");
+    const float k = (float)c.f("k", 0.0), k2 = (float)c.f("k2", 0.0);
+    const float* x = (const float*)c.ptr("x", 4 * (size_t)n);
+    float* y = (float*)c.ptr("y", 4 * (size_t)n);
+    if (u < 0 || u > U_SOFTPLUS) return bad("g_un: unknown op");
+    if (!c.err.empty()) return bad(c.err);
+    if (!dry) e = graph_unary_launch(x, y, n, u, k, k2, st);
+  } else if (op.kind == "g_copy") {
+    GraphCopyArgs a;
+    const auto shape = c.ints("shape"), sx = c.ints("sx"), sy = c.ints("sy");
+    if (!rank_ok(shape, sx) || sy.size() != shape.size()) return bad("g_copy: bad shape / strides");
+    a.rank = (int)shape.size();
+    a.n = numel_of(shape);
+    fill_nd(shape, a.shape); fill_nd(sx, a.sx); fill_nd(sy, a.sy);
+    a.x = (const float*)c.ptr("x", 4 * view_span(shape, sx));
+    a.y = (float*)c.ptr("y", 4 * view_span(shape, sy));
+    if (!c.err.empty()) return bad(c.err);
+    if (!dry) e = graph_copy_launch(a, st);
+  } else if (op.kind == "g_reduce") {
+    GraphReduceArgs a;
+    const auto shape = c.ints("shape");
+    if (shape.empty() || shape.size() > (size_t)GRAPH_MAX_RANK) return bad("g_reduce: bad shape");
+    a.rank = (int)shape.size();
+    fill_nd(shape, a.shape);
+    a.op = (int)c.i("op");
+    a.mask = (int)c.i("mask");
+    if (a.op < 0 || a.op > RD_L1) return bad("g_reduce: unknown op");
+    long long nout = 1;
+    for (int d = 0; d < a.rank; ++d) nout *= ((a.mask >> d) & 1) ? 1 : shape[d];
+    a.n_out = nout;
+    a.x = (const float*)c.ptr("x", 4 * (size_t)numel_of(shape));
+    a.y = (float*)c.ptr("y", 4 * (size_t)nout);
+    if (!c.err.empty()) return bad(c.err);
+    if (!dry) e = graph_reduce_launch(a, st);
+  } else if (op.kind == "g_softmax") {
+    const long long outer = c.i("outer"), n = c.i("n"), inner = c.i("inner");
+    const size_t total = 4 * (size_t)(outer * n * inner);
+    const float* x = (const float*)c.ptr("x", total);
+    float* y = (float*)c.ptr("y", total);
+    if (!c.err.empty()) return bad(c.err);
+    if (!dry) e = graph_softmax_launch(x, y, outer, n, inner, st);
+  } else if (op.kind == "g_rms" || op.kind == "g_ln") {
+    const long long rows = c.i("rows");
+    const int d = (int)c.i("d");
+    const float* x = (const float*)c.ptr("x", 4 * (size_t)(rows * d));
+    float* y = (float*)c.ptr("y", 4 * (size_t)(rows * d));
+    const __half* g = (const __half*)c.ptr("g", 2 * (size_t)d);
+    if (op.kind == "g_rms") {
+      const float floor = (float)c.f("floor");
+      if (!c.err.empty()) return bad(c.err);
+      if (!dry) e = graph_rms_launch(x, y, g, floor, rows, d, st);
+    } else {
+      const __half* b = (const __half*)c.ptr("b", 2 * (size_t)d, true);
+      const float eps = (float)c.f("eps");
+      if (!c.err.empty()) return bad(c.err);
+      if (!dry) e = graph_layernorm_launch(x, y, g, b, eps, rows, d, st);
+    }
+  } else if (op.kind == "g_linear") {
+    GraphLinearArgs a;
+    a.rows = c.i("rows"); a.N = c.i("n"); a.K = c.i("k");
+    a.ldx = c.i("ldx", a.K); a.ldy = c.i("ldy", a.N);
+    a.int8 = (int)c.i("i8", 0);
+    if (a.rows < 1 || a.N < 1 || a.K < 1 || a.ldx < a.K || a.ldy < a.N) return bad("g_linear: bad dimensions");
+    a.x = (const float*)c.ptr("x", 4 * (size_t)((a.rows - 1) * a.ldx + a.K));
+    a.w = c.ptr("w", (size_t)(a.N * a.K) * (a.int8 ? 1 : 2));
+    a.scale = (const __half*)c.ptr("s", 2 * (size_t)a.N, !a.int8);
+    a.bias = (const __half*)c.ptr("bias", 2 * (size_t)a.N, true);
+    a.y = (float*)c.ptr("y", 4 * (size_t)((a.rows - 1) * a.ldy + a.N));
+    if (!c.err.empty()) return bad(c.err);
+    if (!dry) e = graph_linear_launch(a, st);
+  } else if (op.kind == "g_bmm") {
+    GraphBmmArgs a;
+    const auto bshape = c.ints("bshape"), sa = c.ints("sa"), sb = c.ints("sb");
+    a.M = c.i("m"); a.N = c.i("n"); a.K = c.i("k");
+    a.sam = c.i("sam"); a.sak = c.i("sak"); a.sbk = c.i("sbk"); a.sbn = c.i("sbn");
+    a.round_b = (int)c.i("rb", 1);
+    if (bshape.size() > (size_t)GRAPH_MAX_RANK || sa.size() != bshape.size() || sb.size() != bshape.size())
+      return bad("g_bmm: bad batch shape / strides");
+    if (a.M < 1 || a.N < 1 || a.K < 1) return bad("g_bmm: bad dimensions");
+    a.brank = (int)bshape.size();
+    fill_nd(bshape, a.bshape); fill_nd(sa, a.sa); fill_nd(sb, a.sb);
+    a.batch = numel_of(bshape);
+    std::vector<long long> ash(bshape), ast(sa), bsh(bshape), bst(sb);
+    ash.push_back(a.M); ast.push_back(a.sam); ash.push_back(a.K); ast.push_back(a.sak);
+    bsh.push_back(a.K); bst.push_back(a.sbk); bsh.push_back(a.N); bst.push_back(a.sbn);
+    a.a = (const float*)c.ptr("a", 4 * view_span(ash, ast));
+    a.b = (const float*)c.ptr("b", 4 * view_span(bsh, bst));
+    a.y = (float*)c.ptr("y", 4 * (size_t)(a.batch * a.M * a.N));
+    if (!c.err.empty()) return bad(c.err);
+    if (!dry) e = graph_bmm_launch(a, st);
+  } else {
+    return bad("unknown op kind '" + op.kind + "'");
+  }
+  return true;
 }
 
 // ------------------------------------------------------------------------------------ op launchers
@@ -364,6 +527,8 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
       e = rope_kv_prefill_launch(a, qbuf, st);
       if (e == cudaSuccess) e = attn_prefill_with_q(a, qbuf, st);
     }
+  } else if (op.kind.compare(0, 2, "g_") == 0) {
+    if (!graph_op(c, op, dry, st, e, why)) return cudaErrorInvalidValue;
   } else if (op.kind == "moe_gate") {
     const int nb = (int)c.i("nb"), E = (int)c.i("e"), k = (int)c.i("k"), ld = (int)c.i("ld", E);
     const float* lg = (const float*)c.ptr("logits", 4 * ((size_t)(nb - 1) * ld + E));
