@@ -258,5 +258,7 @@ cudaError_t graph_layernorm_launch(const float* x, float* y, const __half* g, co
                                    long long rows, int d, cudaStream_t st);
 cudaError_t graph_linear_launch(const GraphLinearArgs& a, cudaStream_t st);
 cudaError_t graph_bmm_launch(const GraphBmmArgs& a, cudaStream_t st);
+cudaError_t graph_decode_ctx_launch(const int* pos, const __half* cos_t, const __half* sin_t, int M, int dh, float* oh,
+                                    float* inv, float* mask, float* cosp, float* sinp, cudaStream_t st);
 
 }  // namespace af

@@ -269,6 +269,26 @@ __global__ void bmm_kernel(GraphBmmArgs a) {
   }
 }
 
+// The reference's per-step decode inputs (`aneforge/llm.py:585-590`) built on the device from the
+// resident position: oh / inv (one-hot of pos over the M cache rows and its complement), the additive
+// mask (0 up to pos, f16(-1e4) beyond) and the position's RoPE row (cos 1 / sin 0 without tables).
+__global__ void decode_ctx_kernel(const int* pos, const __half* cos_t, const __half* sin_t, int M, int dh, float* oh,
+                                  float* inv, float* mask, float* cosp, float* sinp) {
+  const int p = *pos;
+  const bool ok = p >= 0 && p < M;
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < M; j += gridDim.x * blockDim.x) {
+    const bool hit = ok && j == p;
+    oh[j] = hit ? 1.f : 0.f;
+    inv[j] = hit ? 0.f : 1.f;
+    mask[j] = (ok && j <= p) ? 0.f : -10000.f;
+  }
+  if (blockIdx.x == 0)
+    for (int d = threadIdx.x; d < dh; d += blockDim.x) {
+      cosp[d] = (ok && cos_t) ? __half2float(cos_t[(size_t)p * dh + d]) : 1.f;
+      sinp[d] = (ok && sin_t) ? __half2float(sin_t[(size_t)p * dh + d]) : 0.f;
+    }
+}
+
 int grid_for(long long work, int per_block) {
   long long g = (work + per_block - 1) / per_block;
   if (g < 1) g = 1;
@@ -328,6 +348,13 @@ cudaError_t graph_linear_launch(const GraphLinearArgs& a, cudaStream_t st) {
   const long long warps = (a.rows + 3) / 4 * a.N;
   if (a.int8) linear_kernel<true><<<grid_for(warps * 32, 256), 256, 0, st>>>(a);
   else linear_kernel<false><<<grid_for(warps * 32, 256), 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t graph_decode_ctx_launch(const int* pos, const __half* cos_t, const __half* sin_t, int M, int dh, float* oh,
+                                    float* inv, float* mask, float* cosp, float* sinp, cudaStream_t st) {
+  if (M <= 0 || dh <= 0) return cudaErrorInvalidValue;
+  decode_ctx_kernel<<<grid_for(M, 256), 256, 0, st>>>(pos, cos_t, sin_t, M, dh, oh, inv, mask, cosp, sinp);
   return cudaGetLastError();
 }
 

@@ -260,7 +260,7 @@ static bool graph_op(OpCtx& c, const Op& op, bool dry, cudaStream_t st, cudaErro
       a.b = (const float*)c.ptr("b", 4 * view_span(shape, sb));
     }
     if (a.op == G_SELECT) {
-      if (sc.size() != shape.size() || !a.b) return bad("g_ew select: needs b and c with strides");
+      if (sc.size() != shape.size() || !c.has("b")) return bad("g_ew select: needs b and c with strides");
       fill_nd(sc, a.sc);
       a.c = (const float*)c.ptr("c", 4 * view_span(shape, sc));
     } else if (a.op < 0 || a.op > G_NE) {
@@ -361,6 +361,19 @@ static bool graph_op(OpCtx& c, const Op& op, bool dry, cudaStream_t st, cudaErro
     a.y = (float*)c.ptr("y", 4 * (size_t)(a.batch * a.M * a.N));
     if (!c.err.empty()) return bad(c.err);
     if (!dry) e = graph_bmm_launch(a, st);
+  } else if (op.kind == "g_decode_ctx") {
+    const int M = (int)c.i("m"), dh = (int)c.i("dh");
+    const int* pos = (const int*)c.ptr("pos", 4);
+    const __half* cos_t = (const __half*)c.ptr("cos", 2 * (size_t)M * dh, true);
+    const __half* sin_t = (const __half*)c.ptr("sin", 2 * (size_t)M * dh, true);
+    float* oh = (float*)c.ptr("oh", 4 * (size_t)M);
+    float* inv = (float*)c.ptr("inv", 4 * (size_t)M);
+    float* mask = (float*)c.ptr("mask", 4 * (size_t)M);
+    float* cosp = (float*)c.ptr("cosp", 4 * (size_t)dh);
+    float* sinp = (float*)c.ptr("sinp", 4 * (size_t)dh);
+    if (M < 1 || dh < 1) return bad("g_decode_ctx: bad dimensions");
+    if (!c.err.empty()) return bad(c.err);
+    if (!dry) e = graph_decode_ctx_launch(pos, cos_t, sin_t, M, dh, oh, inv, mask, cosp, sinp, st);
   } else {
     return bad("unknown op kind '" + op.kind + "'");
   }

@@ -29,6 +29,7 @@ from . import _blob
 from . import _runtime as R
 from .plan import PlanBuilder, at
 from .weights import DevLinear, encode_linear, rms_weights, to_device, fp16_bits_exact
+from .blocks import is_graph_builder
 
 F16, F32 = np.float16, np.float32
 
@@ -220,10 +221,16 @@ def emit_swiglu(pb, ctx, li, lw, cfg, ls):
   _emit_row_parallel(pb, ctx, f"{pre}.down", lw["down"], "act")
 
 
+# Registry values are either fused plan emitters f(pb, ctx, li, lw, cfg, ls) - the hot path - or
+# graph builders in the reference's form (`aneforge/llm.py:240-245`; see `blocks`), which the
+# programs lower through `_compile.Lowering`: a plugin written for the reference registers here
+# unchanged. GeGLU and the GPT-2 GELU MLP run as graph builders.
+from . import blocks as _blocks  # noqa: E402
+
 PREFILL_MIXERS = {"attention": emit_attention_prefill}
-PREFILL_MLPS = {"swiglu": emit_swiglu}
+PREFILL_MLPS = {"swiglu": emit_swiglu, "geglu": _blocks.geglu, "gelu_new": _blocks.gelu_mlp}
 DECODE_MIXERS = {"attention": emit_attention_decode}
-DECODE_MLPS = {"swiglu": emit_swiglu}
+DECODE_MLPS = {"swiglu": emit_swiglu, "geglu": _blocks.geglu, "gelu_new": _blocks.gelu_mlp}
 _DECODE_CTX = ("pos",)
 
 
@@ -340,20 +347,25 @@ class LlamaPrefill:
     for i in range(cfg.n_layers):
       lw = self.w["layers"][i]
       ls = self._spec(i)
-      if ls.mixer != "attention":
-        raise NotImplementedError(f"mixer {ls.mixer!r} has no B200 emitter")
+      if ls.mixer not in DECODE_MIXERS:
+        raise NotImplementedError(f"mixer {ls.mixer!r} has no B200 emitter or graph builder")
       if ls.mlp not in DECODE_MLPS:
-        raise NotImplementedError(f"mlp {ls.mlp!r} has no B200 emitter")
+        raise NotImplementedError(f"mlp {ls.mlp!r} has no B200 emitter or graph builder")
       d = {}
-      d["qkv"] = encode_linear([lw["wq"], lw["wk"], lw["wv"]], c, dev,
-                               biases=[lw.get("q_bias"), lw.get("k_bias"), lw.get("v_bias")], atol=atol,
-                               block_size=bs)
-      d["o"] = encode_linear([lw["wo"]], c, dev, biases=[lw.get("o_bias")], atol=atol, block_size=bs)
-      d["attn_g"], d["attn_floor"] = rms_weights(lw["attn_norm"], cfg.norm_eps, dev)
+      if not is_graph_builder(DECODE_MIXERS[ls.mixer]):
+        # the fused attention mixer; a graph-builder mixer is lowered from the host weights instead
+        d["qkv"] = encode_linear([lw["wq"], lw["wk"], lw["wv"]], c, dev,
+                                 biases=[lw.get("q_bias"), lw.get("k_bias"), lw.get("v_bias")], atol=atol,
+                                 block_size=bs)
+        d["o"] = encode_linear([lw["wo"]], c, dev, biases=[lw.get("o_bias")], atol=atol, block_size=bs)
+        d["attn_g"], d["attn_floor"] = rms_weights(lw["attn_norm"], cfg.norm_eps, dev)
+        if ls.qk_norm:
+          d["qn"], d["qn_floor"] = rms_weights(lw["q_norm"], cfg.norm_eps, dev)
+          d["kn"], d["kn_floor"] = rms_weights(lw["k_norm"], cfg.norm_eps, dev)
+      if is_graph_builder(DECODE_MLPS[ls.mlp]):
+        layers.append(d)
+        continue
       d["mlp_g"], d["mlp_floor"] = rms_weights(lw["mlp_norm"], cfg.norm_eps, dev)
-      if ls.qk_norm:
-        d["qn"], d["qn_floor"] = rms_weights(lw["q_norm"], cfg.norm_eps, dev)
-        d["kn"], d["kn_floor"] = rms_weights(lw["k_norm"], cfg.norm_eps, dev)
       if ls.mlp == "swiglu":
         d["gu"] = encode_linear([lw["wgate"], lw["wup"]], c, dev, swiglu=True, atol=atol, block_size=bs)
         d["down"] = encode_linear([lw["wdown"]], c, dev, atol=atol, block_size=bs)
@@ -472,10 +484,27 @@ class LlamaPrefill:
       self._declare_layer_weights(pb, li, d["layers"][li])
       pb.buf(f"L{li}.K", 2 * NB * KV * M * dh, "state"); pb.buf(f"L{li}.V", 2 * NB * KV * M * dh, "state")
     pb.op("embed", tok="tok", table="embed", h="h", vocab=V, d=D, nb=NB)
+    lows, gstates = [], []
+    graph_mix = [is_graph_builder(DECODE_MIXERS[self._spec(i).mixer]) for i in range(cfg.n_layers)]
+    graph_mlp = [is_graph_builder(DECODE_MLPS[self._spec(i).mlp]) for i in range(cfg.n_layers)]
+    if (any(graph_mix) or any(graph_mlp)) and (NB != 1 or self.tp is not None):
+      raise NotImplementedError("graph-builder layers decode one sequence on one GPU (the reference's runner)")
+    if any(graph_mix):
+      # the reference's per-step decode inputs, built on the device from the resident position
+      for k, n in (("oh", M), ("inv", M), ("mask", M), ("cosp", dh), ("sinp", dh)):
+        pb.buf(f"dctx.{k}", 4 * n, "tmp")
+      pb.op("g_decode_ctx", pos="pos", cos="rope.cos" if cfg.rope else None, sin="rope.sin" if cfg.rope else None,
+            m=M, dh=dh, oh="dctx.oh", inv="dctx.inv", mask="dctx.mask", cosp="dctx.cosp", sinp="dctx.sinp")
     for li in range(cfg.n_layers):
       ls = self._spec(li)
-      DECODE_MIXERS[ls.mixer](pb, ctx, li, d["layers"][li], cfg, ls)
-      DECODE_MLPS[ls.mlp](pb, ctx, li, d["layers"][li], cfg, ls)
+      if graph_mix[li]:
+        gstates += self._lower_graph_mixer(pb, li, DECODE_MIXERS[ls.mixer], M, lows)
+      else:
+        DECODE_MIXERS[ls.mixer](pb, ctx, li, d["layers"][li], cfg, ls)
+      if graph_mlp[li]:
+        self._lower_graph_mlp(pb, li, DECODE_MLPS[ls.mlp], NB, lows, "dec")
+      else:
+        DECODE_MLPS[ls.mlp](pb, ctx, li, d["layers"][li], cfg, ls)
     pb.op("rmsnorm", x="h", g="final_g", out="hid", nb=NB, d=D, floor=d["final_floor"])
     if self.tp is None:
       pb.op("gemv", wf="f16", epi="argmax", x="hid", w="lm_head", y="logits", nb=NB, n=V, k=D, amv="am.val",
@@ -502,8 +531,73 @@ class LlamaPrefill:
       prog.upload("rope.cos", cos_t); prog.upload("rope.sin", sin_t)
     for li in range(cfg.n_layers):
       self._bind_layer(prog, li, d["layers"][li])
-    self._dec = {"M": M, "NB": NB, "prog": prog, "plan": pb}
+    for low in lows:
+      low.finish(prog)
+    self._dec = {"M": M, "NB": NB, "prog": prog, "plan": pb, "graphs": lows, "gstates": gstates}
     return self._dec
+
+  # -- graph-builder registry entries (the reference's form; lowered by `_compile.Lowering`)
+  def _lower_graph_mlp(self, pb, li, fn, rows, lows, tag):
+    """An MLP graph builder h -> h' over `rows` residual rows: its input is the program's fp32
+    residual `h`, its result is copied back into it."""
+    from ._compile import Lowering
+    from .graph import input as ginput, topo_order
+    cfg = self.cfg
+    x = ginput((rows, cfg.dim))
+    out = fn(x, self.w["layers"][li], cfg, self._spec(li))
+    low = Lowering(pb, self.compress, self.compress_atol, self.block_size, self.device, prefix=f"L{li}.{tag}.mlp")
+    low.set_value(x, "h")
+    order = topo_order(out)
+    stray = [t for t in order if t.op == "input" and t is not x]
+    if stray:
+      raise ValueError(f"layer {li}: an MLP graph builder may only read its input (found {len(stray)} more)")
+    low.lower(order, {id(t): f"n{i}" for i, t in enumerate(order)})
+    if low.value(out) != "h":
+      pb.op("copy", dst="h", src=low.value(out), bytes=4 * rows * cfg.dim)
+    lows.append(low)
+
+  def _lower_graph_mixer(self, pb, li, fn, M, lows):
+    """A decode-mixer graph builder (x, w, cfg, ls, ctx, M) -> (h, state pairs): x is the residual,
+    ctx the per-step inputs the program builds from the position, and every (out, in) state pair a
+    resident fp16 state buffer (the reference aliases it with `share_buffer`) that the step reads
+    at its start and writes back at its end. Returns [(state buffer, elements)]."""
+    from . import blocks
+    from ._compile import Lowering
+    from .graph import input as ginput, topo_order
+    cfg = self.cfg
+    x = ginput((1, cfg.dim))
+    ctx = blocks.decode_inputs(M, cfg.dh)
+    out, pairs = fn(x, self.w["layers"][li], cfg, self._spec(li), ctx, M)
+    low = Lowering(pb, self.compress, self.compress_atol, self.block_size, self.device, prefix=f"L{li}.mix")
+    low.set_value(x, "h")
+    for k, t in ctx.items():
+      low.set_value(t, f"dctx.{k}")
+    states = []
+    for j, (o, i) in enumerate(pairs):
+      if o.shape != i.shape:
+        raise ValueError(f"layer {li}: state pair {j} changes shape {i.shape} -> {o.shape}")
+      sb = pb.buf(f"L{li}.gs{j}", 2 * i.size, "state")
+      v = low._buf(f"gs{j}.v", 4 * i.size)
+      pb.op("cast", src=sb, dst=v, n=i.size, mode=0)
+      low.set_value(i, v)
+      states.append((sb, i.size))
+    order = topo_order(out, *[o for o, _ in pairs])
+    known = {id(x), *(id(t) for t in ctx.values()), *(id(i) for _, i in pairs)}
+    stray = [t for t in order if t.op == "input" and id(t) not in known]
+    if stray:
+      raise ValueError(f"layer {li}: a mixer graph reads {len(stray)} input(s) that are neither ctx nor state")
+    low.lower(order, {id(t): f"n{i}" for i, t in enumerate(order)})
+    for j, (o, _) in enumerate(pairs):
+      pb.op("cast", src=low.value(o), dst=f"L{li}.gs{j}", n=o.size, mode=1)
+    pb.op("copy", dst="h", src=low.value(out), bytes=4 * cfg.dim)
+    lows.append(low)
+    return states
+
+  def _batched_prefill_ok(self) -> bool:
+    """Batched prefill needs the fused attention mixer in every layer (the reference's rule:
+    batched prefill supports attention layers only)."""
+    return all(self._spec(i).mixer == "attention" and not is_graph_builder(DECODE_MIXERS["attention"])
+               for i in range(self.cfg.n_layers))
 
   def _prefiller(self, seq):
     """Build (once, cached by seq) the batched-prefill program: all layers over `seq` rows, each
@@ -534,12 +628,19 @@ class LlamaPrefill:
       self._declare_layer_weights(pb, li, d["layers"][li])
       pb.buf(f"L{li}.K", 2 * KV * seq * dh, "out"); pb.buf(f"L{li}.V", 2 * KV * seq * dh, "out")
     pb.op("embed", tok="ids", table="embed", h="h", vocab=V, d=D, nb=seq)
+    lows = []
     for li in range(cfg.n_layers):
       ls = self._spec(li)
-      if ls.mixer != "attention":
+      if ls.mixer != "attention" or is_graph_builder(PREFILL_MIXERS[ls.mixer]):
         raise NotImplementedError("batched prefill supports attention layers only")
       PREFILL_MIXERS[ls.mixer](pb, ctx, li, d["layers"][li], cfg, ls)
-      PREFILL_MLPS[ls.mlp](pb, ctx, li, d["layers"][li], cfg, ls)
+      mlp = PREFILL_MLPS.get(ls.mlp)
+      if mlp is None:
+        raise NotImplementedError(f"mlp {ls.mlp!r} has no prefill emitter or graph builder")
+      if is_graph_builder(mlp):
+        self._lower_graph_mlp(pb, li, mlp, seq, lows, "pre")
+      else:
+        mlp(pb, ctx, li, d["layers"][li], cfg, ls)
     pb.op("rmsnorm", x="h", g="final_g", out="hid", nb=seq, d=D, floor=d["final_floor"])
     outs = {"hid": (seq, D)}
     for li in range(cfg.n_layers):
@@ -553,7 +654,9 @@ class LlamaPrefill:
       prog.upload("rope.cos", cos_t); prog.upload("rope.sin", sin_t)
     for li in range(cfg.n_layers):
       self._bind_layer(prog, li, d["layers"][li])
-    self._pre = {"seq": seq, "prog": prog}
+    for low in lows:
+      low.finish(prog)
+    self._pre = {"seq": seq, "prog": prog, "graphs": lows}
     return self._pre
 
   def _head_program(self, NB=1):
@@ -671,8 +774,12 @@ class LlamaPrefill:
 
   def _reset_state(self, dec):
     for li in range(self.cfg.n_layers):
+      if is_graph_builder(DECODE_MIXERS[self._spec(li).mixer]):
+        continue
       for nm in ("K", "V"):
         dec["prog"].tensor(f"L{li}.{nm}", (dec["NB"], self.cfg.n_kv_heads, dec["M"], self.cfg.dh)).zero_()
+    for name, n in dec.get("gstates", ()):
+      dec["prog"].tensor(name, (n,)).zero_()
 
   def generate(self, token_ids, max_new_tokens=40, eos_id=None, max_len=None, on_token=None,
                temperature=0.0, top_p=1.0, top_k=0, batched_prefill=True, prefill_pad=None, on_stage=None,
@@ -693,7 +800,7 @@ class LlamaPrefill:
       torch.cuda.synchronize()
     out = []
     t0 = time.perf_counter()
-    if batched_prefill and len(prompt) > 1:
+    if batched_prefill and len(prompt) > 1 and self._batched_prefill_ok():
       pre, real, seq = self._prefill_hidden(prompt, prefill_pad)
       hid = pre["prog"].read_output("hid")
       logits0 = self._decode_logits(hid[real - 1], None, greedy)

@@ -50,7 +50,7 @@ class Config:
   rotary_dim: int = 0; rope_scaling: dict | None = None
   extra: dict = field(default_factory=dict)
   qk_norm: bool = False
-  mlp: str = "swiglu"            # "swiglu" or "moe"
+  mlp: str = "swiglu"            # "swiglu", "geglu" or "moe"
 
   @property
   def dh(self) -> int:
@@ -456,8 +456,19 @@ def _mlp_with_moe(self, L, h):
     self._cur_layer = L
     return _moe(self, L["moe"], h)
   hn = rms_norm(h, *L["mlp_norm"])
-  act = silu(self._lin(L["wgate"], hn)) * self._lin(L["wup"], hn)
+  g = self._lin(L["wgate"], hn)
+  act = (gelu_tanh(g) if self.cfg.mlp == "geglu" else silu(g)) * self._lin(L["wup"], hn)
   return (h + self._lin(L["wdown"], act)).astype(F32)
+
+
+def gelu_tanh(x: np.ndarray) -> np.ndarray:
+  """The reference's GeGLU activation built from graph ops (`aneforge/llm.py:184-187`):
+  (x * 0.5) * (tanh((x + x^3 * 0.044715) * sqrt(2/pi)) + 1), its scalar constants baked fp16 like
+  every constant of the reference program."""
+  c1 = F32(np.float16(0.044715))
+  c2 = F32(np.float16(np.sqrt(2.0 / np.pi)))
+  x = x.astype(F32)
+  return ((x * F32(0.5)) * (np.tanh((x + (x ** 3) * c1) * c2) + F32(1.0))).astype(F32)
 
 
 OracleModel._mlp = _mlp_with_moe
