@@ -76,6 +76,10 @@ struct GemvTcArgs {
   int s_stride = 0;            // halves between experts' per-row scales
   const float* rw = nullptr;
   int rw_e = 0;
+  // expert parallel: this GPU holds experts [e_base, e_base + n_exp) of the model; `sel` holds global
+  // expert ids (a selected expert held elsewhere makes the whole launch a no-op here) and the
+  // routing-weight column of local expert e is e_base + e
+  int e_base = 0, n_exp = 0;
   // set by the launcher
   int Np = 0, Kp = 0, S = 1, maxc = 1;
   int csize = 0;               // > 1: thread-block clusters of csize CTAs split each row block's k range

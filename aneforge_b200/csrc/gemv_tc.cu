@@ -70,7 +70,7 @@ AF_DEV void epilogue(const GemvTcArgs& a, float (&acc)[NT][4], int rt, int g, in
           if (EPI == EPI_F32) reinterpret_cast<float*>(a.y)[o] = v;
           else if (EPI == EPI_F16) reinterpret_cast<__half*>(a.y)[o] = f2h(v);
           else if (EPI == EPI_RESID) {
-            if (a.rw) v *= __ldcg(a.rw + (size_t)b * a.rw_e + a.fixed_e);
+            if (a.rw) v *= __ldcg(a.rw + (size_t)b * a.rw_e + a.e_base + a.fixed_e);
             reinterpret_cast<float*>(a.y)[o] = __ldcg(reinterpret_cast<const float*>(a.y) + o) + v;
           }
         }
@@ -94,7 +94,10 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
   int expert = a.fixed_e;
   if (a.sel) {
     pdl_wait();
-    expert = __ldcg(a.sel + a.slot);
+    expert = __ldcg(a.sel + a.slot) - a.e_base;
+    // expert parallel: an expert held by another GPU contributes nothing here (uniform over the grid:
+    // every thread of every CTA leaves before any barrier)
+    if (a.n_exp > 0 && (expert < 0 || expert >= a.n_exp)) return;
   }
   if (a.sel || a.fixed_e) {
     a.w = static_cast<const char*>(a.w) + (size_t)expert * a.w_stride;

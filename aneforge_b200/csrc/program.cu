@@ -430,6 +430,9 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
       a.slot = (int)c.i("slot", 0);
       a.fixed_e = (int)c.i("fixe", 0);
       if (a.fixed_e < 0 || a.fixed_e >= nexp) c.err = "fixe out of range";
+      a.e_base = (int)c.i("ebase", 0);
+      a.n_exp = nexp;
+      if (a.e_base < 0) c.err = "ebase < 0";
     }
     a.rw_e = (int)c.i("rwe", 0);
     a.rw = (const float*)c.ptr("rw", 4 * (size_t)a.NB * (a.rw_e > 0 ? a.rw_e : 1), true);

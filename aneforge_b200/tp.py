@@ -45,15 +45,23 @@ class Shard:
   kv_heads: tuple[int, int]      # local kv heads
   ffn: tuple[int, int]           # local FFN rows / down columns
   vocab: tuple[int, int]         # local lm_head rows
+  experts: tuple[int, int] = (0, 0)   # mixture of experts: the experts this rank holds (expert parallel)
 
 
 def plan_shard(cfg, rank: int, world: int) -> Shard:
+  """Rank `rank`'s shard. Dense layers split heads and FFN rows (tensor parallel); the experts of a
+  mixture-of-experts layer are split whole over the ranks (expert parallel: E / world experts per
+  GPU, each with its full FFN), their router replicated."""
   H, KV, F, V = cfg.n_heads, cfg.n_kv_heads, cfg.ffn_dim, cfg.vocab
   if H % world or KV % world:
     raise ValueError(f"tensor parallel {world} needs heads ({H}) and kv heads ({KV}) divisible by it")
   hq, hk = H // world, KV // world
+  E = int(cfg.extra.get("n_experts", 0) or 0)
+  if E and E % world:
+    raise ValueError(f"expert parallel {world} needs the expert count ({E}) divisible by it")
+  ex = (rank * E // world, (rank + 1) * E // world) if E else (0, 0)
   return Shard(rank, world, (rank * hq, (rank + 1) * hq), (rank * hk, (rank + 1) * hk),
-               split_even(F, world, 32 if F % 32 == 0 else 1)[rank], split_even(V, world)[rank])
+               split_even(F, world, 32 if F % 32 == 0 else 1)[rank], split_even(V, world)[rank], ex)
 
 
 def _rows(a, lo, hi):
@@ -86,6 +94,8 @@ def shard_layer(lw: dict, cfg, s: Shard) -> dict:
       out[k] = _rows(v, f0, f1)
     elif k == "wdown":
       out[k] = _cols(v, f0, f1)
+    elif k in ("wgate_exps", "wup_exps", "wdown_exps"):
+      out[k] = v[s.experts[0]:s.experts[1]]        # whole experts (expert parallel)
     else:
       out[k] = v                         # norms (attention / MLP / QK-norm) are replicated
   return out
@@ -110,8 +120,11 @@ class _ShardedLayers:
 def shard_model(cfg, weights: dict, s: Shard):
   """(local config, local weights) of shard `s`. The local config has the local head / FFN counts;
   vocabulary, model width and the embedding stay full; `lm_head` holds the local vocabulary rows."""
+  extra = dict(cfg.extra)
+  if extra.get("n_experts"):
+    extra["ep_experts"] = tuple(s.experts)          # global ids of the local experts; n_experts stays global
   local = replace(cfg, n_heads=s.q_heads[1] - s.q_heads[0], n_kv_heads=s.kv_heads[1] - s.kv_heads[0],
-                  ffn_dim=s.ffn[1] - s.ffn[0], head_dim=cfg.dh)
+                  ffn_dim=s.ffn[1] - s.ffn[0], head_dim=cfg.dh, extra=extra)
   w = dict(weights)
   w["layers"] = _ShardedLayers(weights["layers"], cfg, s)
   w["lm_head"] = _rows(weights["lm_head"], *s.vocab)

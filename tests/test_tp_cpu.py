@@ -189,3 +189,86 @@ def test_peer_buffer_handles_exchanged_in_rank_order(fail_rank):
     assert opened == want
     assert on == (fail_rank < 0)
     assert disabled == (fail_rank >= 0 and rank != fail_rank)
+
+
+# ---------------------------------------------------------------------------- expert parallel
+
+def _ep_rank(rank, world, port, q):
+  """One gloo rank of the expert-parallel MoE algebra: route the (replicated) rows with the full
+  router, run only the experts this rank's shard holds, and all-reduce the partial outputs."""
+  import torch
+  import torch.distributed as dist
+  os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+  dist.init_process_group("gloo", rank=rank, world_size=world)
+  from oracle.model import topk_gate, softmax, silu
+  cfg, lw, x = _ep_case()
+  s = TP.plan_shard(cfg, rank, world)
+  local = TP.shard_layer(lw, cfg, s)
+  probs = softmax(x @ local["router"].T)
+  gw = topk_gate(probs, 2)
+  gw = gw / gw.sum(1, keepdims=True)
+  part = np.zeros_like(x)
+  for j, e in enumerate(range(*s.experts)):
+    act = silu(x @ local["wgate_exps"][j].T) * (x @ local["wup_exps"][j].T)
+    part += gw[:, e:e + 1] * (act @ local["wdown_exps"][j])
+  t = torch.from_numpy(part)
+  dist.all_reduce(t)
+  q.put((rank, s.experts, t.numpy()))
+  dist.barrier()
+  dist.destroy_process_group()
+
+
+def _ep_case():
+  rng = np.random.default_rng(7)
+  E, D, F = 8, 32, 48
+  cfg = LlamaConfig(dim=D, n_layers=1, n_heads=8, n_kv_heads=4, ffn_dim=F, vocab=20,
+                    extra={"n_experts": E, "n_experts_per_tok": 2})
+  lw = {"router": rng.standard_normal((E, D)).astype(F32), "wgate_exps": rng.standard_normal((E, F, D)).astype(F32) * 0.2,
+        "wup_exps": rng.standard_normal((E, F, D)).astype(F32) * 0.2,
+        "wdown_exps": rng.standard_normal((E, F, D)).astype(F32) * 0.2, "mlp_norm": np.ones(D, F32)}
+  return cfg, lw, rng.standard_normal((5, D)).astype(F32)
+
+
+@pytest.mark.parametrize("world", [2])
+def test_expert_parallel_dispatch_and_combine_over_gloo(world):
+  """Experts split whole over `world` gloo ranks: every expert is held once, and the all-reduce of
+  the ranks' partial outputs equals the dense all-expert MoE of the reference (`aneforge/moe.py:48-63`)."""
+  import multiprocessing as mp
+  import socket
+  from oracle.model import topk_gate, softmax, silu
+  with socket.socket() as sk:
+    sk.bind(("127.0.0.1", 0))
+    port = sk.getsockname()[1]
+  ctx = mp.get_context("spawn")
+  q = ctx.Queue()
+  procs = [ctx.Process(target=_ep_rank, args=(r, world, port, q)) for r in range(world)]
+  for p in procs:
+    p.start()
+  got = dict((r, (ex, y)) for r, ex, y in (q.get(timeout=120) for _ in procs))
+  for p in procs:
+    p.join(timeout=60)
+    assert p.exitcode == 0
+  spans = sorted(got[r][0] for r in range(world))
+  assert spans[0][0] == 0 and spans[-1][1] == 8 and all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
+  cfg, lw, x = _ep_case()
+  gw = topk_gate(softmax(x @ lw["router"].T), 2)
+  gw = gw / gw.sum(1, keepdims=True)
+  ref = np.zeros_like(x)
+  for e in range(8):
+    act = silu(x @ lw["wgate_exps"][e].T) * (x @ lw["wup_exps"][e].T)
+    ref += gw[:, e:e + 1] * (act @ lw["wdown_exps"][e])
+  for r in range(world):
+    np.testing.assert_allclose(got[r][1], ref, rtol=1e-5, atol=1e-5)
+
+
+def test_expert_parallel_shard_plan():
+  cfg = LlamaConfig(dim=4096, n_layers=1, n_heads=32, n_kv_heads=8, ffn_dim=14336, vocab=32000,
+                    extra={"n_experts": 8, "n_experts_per_tok": 2})
+  for world in (1, 2, 4, 8):
+    shards = [TP.plan_shard(cfg, r, world) for r in range(world)]
+    assert [s.experts for s in shards] == [(r * 8 // world, (r + 1) * 8 // world) for r in range(world)]
+    local, _ = TP.shard_model(cfg, {"layers": [], "lm_head": np.zeros((32000, 4))}, shards[-1])
+    assert local.extra["n_experts"] == 8 and local.extra["ep_experts"] == shards[-1].experts
+  with pytest.raises(ValueError):
+    TP.plan_shard(LlamaConfig(dim=64, n_layers=1, n_heads=4, n_kv_heads=4, ffn_dim=64, vocab=10,
+                              extra={"n_experts": 6}), 0, 4)

@@ -13,6 +13,10 @@ torch = pytest.importorskip("torch")
 
 def _cfg(case):
   from oracle.model import Config
+  if case == "moe":
+    # Mixtral-like: attention int8 (tensor parallel), 8 group-32 int4 experts (expert parallel, 4 per GPU)
+    return Config(dim=512, n_layers=2, n_heads=8, n_kv_heads=2, ffn_dim=384, vocab=2048, rope_base=10000.0,
+                  head_dim=64, extra={"n_experts": 8, "n_experts_per_tok": 2, "norm_topk_prob": True}), {"moe": True}
   if case == "int8":
     return Config(dim=1024, n_layers=2, n_heads=8, n_kv_heads=2, ffn_dim=3584, vocab=4096, rope_base=500000.0), {}
   return Config(dim=1024, n_layers=2, n_heads=8, n_kv_heads=2, ffn_dim=2816, vocab=4096, rope_base=1e6), {"qkv_bias": True}
@@ -28,10 +32,14 @@ def _rank(rank, world, port, case, prompt, q, p2p):
   from aneforge_b200.llm import LlamaPrefill
   from aneforge_b200.tp import TensorParallel
   cfg, extra = _cfg(case)
-  w = random_llama_weights(cfg, seed=21, **extra)
+  w = _weights(case, cfg, extra)
   tp = TensorParallel.from_torch_distributed(rank, p2p=p2p)
   assert tp.p2p == p2p
-  m = LlamaPrefill(to_b200_cfg(cfg), w, compress="int8" if case == "int8" else "int4_g32", device=rank, tp=tp)
+  if case == "moe":
+    from tests.test_moe_gpu import _b200_cfg
+    m = LlamaPrefill(_b200_cfg(cfg), w, compress="int8", device=rank, tp=tp, moe_compress="int4_g32")
+  else:
+    m = LlamaPrefill(to_b200_cfg(cfg), w, compress="int8" if case == "int8" else "int4_g32", device=rank, tp=tp)
   toks = m.generate(prompt, 24, max_len=64)
   m.release()
   tp.close()
@@ -40,9 +48,22 @@ def _rank(rank, world, port, case, prompt, q, p2p):
   q.put((rank, toks))
 
 
-@pytest.mark.parametrize("case,p2p", [("int8", False), ("int8", True), ("int4_g32", True)])
+def _weights(case, cfg, extra):
+  from oracle.model import random_llama_weights
+  if case != "moe":
+    return random_llama_weights(cfg, seed=21, **extra)
+  w = random_llama_weights(cfg, seed=21, std=0.05, moe=True)
+  for lw in w["layers"]:
+    # a well-separated router: no top-k choice sits on a near tie (see tests/test_moe_gpu.py)
+    lw["router"] = (lw["router"].astype(np.float32) * 10).astype(np.float16)
+  return w
+
+
+@pytest.mark.parametrize("case,p2p", [("int8", False), ("int8", True), ("int4_g32", True), ("moe", True)])
 def test_tensor_parallel_2_gpus_matches_oracle(case, p2p):
-  """NCCL for every collective, or the residual all-reduces over NVLink peer memory."""
+  """NCCL for every collective, or the residual all-reduces over NVLink peer memory; `moe`: the
+  Mixtral-like model with tensor-parallel attention and expert-parallel experts (4 of 8 per GPU,
+  combined by the all-reduce)."""
   if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
     pytest.skip("needs 2 GPUs")
   import multiprocessing as mp
@@ -64,6 +85,9 @@ def test_tensor_parallel_2_gpus_matches_oracle(case, p2p):
     p.join(timeout=120)
     assert p.exitcode == 0
   assert got[0] == got[1] and len(got[0]) == 24
-  w = random_llama_weights(cfg, seed=21, **extra)
-  om = OracleModel(cfg, w, "int8" if case == "int8" else "int4_g32", precision="device")
+  w = _weights(case, cfg, extra)
+  if case == "moe":
+    om = OracleModel(cfg, w, "int8", precision="device", moe_compress="int4_g32")
+  else:
+    om = OracleModel(cfg, w, "int8" if case == "int8" else "int4_g32", precision="device")
   assert teacher_forced_check(om, prompt, got[0], 64, n_check=24) <= 2
