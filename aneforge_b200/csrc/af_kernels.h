@@ -152,8 +152,17 @@ struct AttnDecodeArgs {
   // (0: the launcher's default)
   int min_keys = 0;
   L2Pf pf;                     // issued at kernel start (the attention phase reads little from HBM)
+  // cache rows between consecutive sequences' caches (-1: KV * M, one cache per sequence). 0: every
+  // row b of the batch is a query of ONE sequence at its own position pos[b], all reading the same
+  // cache (speculative verify); the new K / V rows are then written beforehand by
+  // kv_append_launch and write_kv is 0
+  int kv_seq_rows = -1;
+  int write_kv = 1;
 };
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st, bool pdl);
+// QK-norm + RoPE of each batch row's k at pos[b], written with its v into cache row pos[b] (the
+// cache addressing of AttnDecodeArgs: kv_seq_rows 0 = one shared cache); grid (NB, KV)
+cudaError_t kv_append_launch(const AttnDecodeArgs& a, cudaStream_t st, bool pdl);
 // true when a launch with these arguments merges its splits through a.part / a.counters (false
 // when there is one split, or the splits of a kv head merge inside a thread-block cluster)
 bool attn_decode_uses_scratch(const AttnDecodeArgs& a);

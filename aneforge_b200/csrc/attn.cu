@@ -79,6 +79,7 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
   int n_pre = 0;
   int pos = 0;
   float rc[EPL], rs[EPL];
+  const size_t seq_rows = a.kv_seq_rows < 0 ? (size_t)a.KV * a.M : (size_t)a.kv_seq_rows;
   l2_prefetch_lines(a.pf, ((blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * blockDim.x + threadIdx.x,
                     gridDim.x * gridDim.y * gridDim.z * blockDim.x);
   if (a.prefetch) {
@@ -93,8 +94,8 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         if (n_pre > 0) {
           const uint32_t bytes = (uint32_t)n_pre * DH * 2;
-          const __half* kb0 = a.kc + (((size_t)b * a.KV + kvh) * a.M + j00) * DH;
-          const __half* vb0 = a.vc + (((size_t)b * a.KV + kvh) * a.M + j00) * DH;
+          const __half* kb0 = a.kc + ((size_t)b * seq_rows + (size_t)kvh * a.M + j00) * DH;
+          const __half* vb0 = a.vc + ((size_t)b * seq_rows + (size_t)kvh * a.M + j00) * DH;
           const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&kv_bar);
           asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(2 * bytes) : "memory");
           asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
@@ -141,13 +142,15 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
       vv[e] = active ? __ldcg(qkv + (size_t)(H + KV) * DH + (size_t)kvh * DH + lane * EPL + e) : 0.f;
     }
     norm_rope_head_pre<DH>(k, lane, a.kn_g, a.kn_floor, rope, rc, rs);
-    const size_t slot = (((size_t)b * KV + kvh) * a.M + pos) * DH;
+    const size_t slot = ((size_t)b * seq_rows + (size_t)kvh * a.M + pos) * DH;
     if (active)
 #pragma unroll
       for (int e = 0; e < EPL; ++e) {
         const __half kh = f2h(k[e]), vh = f2h(vv[e]);
-        a.kc[slot + lane * EPL + e] = kh;
-        a.vc[slot + lane * EPL + e] = vh;
+        if (a.write_kv) {
+          a.kc[slot + lane * EPL + e] = kh;
+          a.vc[slot + lane * EPL + e] = vh;
+        }
         kn_s[lane * EPL + e] = h2f(kh);
         vn_s[lane * EPL + e] = h2f(vh);
       }
@@ -168,8 +171,8 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 2) attn_decode_kernel(AttnDeco
 #pragma unroll
     for (int e = 0; e < EPL; ++e) acc[g][e] = 0.f;
   }
-  const __half* kbase = a.kc + ((size_t)b * KV + kvh) * a.M * DH;
-  const __half* vbase = a.vc + ((size_t)b * KV + kvh) * a.M * DH;
+  const __half* kbase = a.kc + ((size_t)b * seq_rows + (size_t)kvh * a.M) * DH;
+  const __half* vbase = a.vc + ((size_t)b * seq_rows + (size_t)kvh * a.M) * DH;
   const float c = a.kv_c;
   const int my_idx = lane >> DB::SHIFT;                 // value index this lane ends up holding
   const int my_g = my_idx / PB, my_p = my_idx % PB;
@@ -572,6 +575,63 @@ cudaError_t attn_decode_launch(const AttnDecodeArgs& a0, cudaStream_t st, bool p
     case 32: return decode_g<32>(a, st, pdl);
     case 64: return decode_g<64>(a, st, pdl);
     case 128: return decode_g<128>(a, st, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// ----------------------------------------------------------------------------------- K/V append
+
+// grid (NB, KV), one warp: the k of batch row b, kv head kvh (QK-norm, RoPE at pos[b]) and its v,
+// written to cache row pos[b] - the same values the decode kernel forms for its own row
+template <int DH>
+__global__ void __launch_bounds__(32) kv_append_kernel(AttnDecodeArgs a) {
+  using HL = HeadLayout<DH>;
+  constexpr int EPL = HL::EPL;
+  const int b = blockIdx.x, kvh = blockIdx.y, lane = threadIdx.x;
+  const bool active = lane < HL::LANES;
+  pdl_wait();
+  const int pos = __ldcg(a.pos + b);
+  if (pos < 0 || pos >= a.M) {
+    if (lane == 0 && kvh == 0) af_set_err(a.err, AF_DEV_BAD_POS);
+    return;
+  }
+  float rc[EPL], rs[EPL];
+  load_rope_row<DH>(a.cos_t, a.sin_t, pos, lane, rc, rs);
+  const float* qkv = a.qkv + (size_t)b * a.ld_qkv;
+  float k[EPL], vv[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    k[e] = active ? __ldcg(qkv + (size_t)a.H * DH + (size_t)kvh * DH + lane * EPL + e) : 0.f;
+    vv[e] = active ? __ldcg(qkv + (size_t)(a.H + a.KV) * DH + (size_t)kvh * DH + lane * EPL + e) : 0.f;
+  }
+  norm_rope_head_pre<DH>(k, lane, a.kn_g, a.kn_floor, a.cos_t != nullptr, rc, rs);
+  const size_t seq_rows = a.kv_seq_rows < 0 ? (size_t)a.KV * a.M : (size_t)a.kv_seq_rows;
+  const size_t slot = ((size_t)b * seq_rows + (size_t)kvh * a.M + pos) * DH;
+  if (active)
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      a.kc[slot + lane * EPL + e] = f2h(k[e]);
+      a.vc[slot + lane * EPL + e] = f2h(vv[e]);
+    }
+  pdl_trigger();
+}
+
+cudaError_t kv_append_launch(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
+  if (a.NB < 1 || a.KV <= 0 || a.M <= 0) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.NB, a.KV);
+  cfg.blockDim = dim3(32);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  switch (a.dh) {
+    case 16: return cudaLaunchKernelEx(&cfg, kv_append_kernel<16>, a);
+    case 32: return cudaLaunchKernelEx(&cfg, kv_append_kernel<32>, a);
+    case 64: return cudaLaunchKernelEx(&cfg, kv_append_kernel<64>, a);
+    case 128: return cudaLaunchKernelEx(&cfg, kv_append_kernel<128>, a);
     default: return cudaErrorInvalidValue;
   }
 }

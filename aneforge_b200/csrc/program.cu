@@ -487,13 +487,33 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     }
     if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
     if (!dry) e = gemv_launch(a, st, pdl);
-  } else if (op.kind == "attn_decode") {
+  } else if (op.kind == "attn_decode" || op.kind == "kv_append") {
     AttnDecodeArgs a;
     a.NB = c.i("nb"); a.H = c.i("h"); a.KV = c.i("kv"); a.dh = c.i("dh"); a.M = c.i("m");
     a.n_split = c.i("nsplit", 1);
     a.ld_qkv = c.i("ldqkv", (a.H + 2 * a.KV) * a.dh);
     a.ld_out = c.i("ldo", a.H * a.dh);
-    const size_t cache = 2 * (size_t)a.NB * a.KV * a.M * a.dh;
+    // seqrows: cache rows between sequences (absent: KV * M each; 0: all rows query one shared cache)
+    a.kv_seq_rows = (int)c.i("seqrows", -1);
+    a.write_kv = (int)c.i("wkv", 1);
+    const size_t rows = a.kv_seq_rows < 0 ? (size_t)a.NB * a.KV * a.M
+                                          : (size_t)(a.NB - 1) * a.kv_seq_rows + (size_t)a.KV * a.M;
+    const size_t cache = 2 * rows * a.dh;
+    if (op.kind == "kv_append") {
+      a.qkv = (const float*)c.ptr("qkv", 4 * ((size_t)(a.NB - 1) * a.ld_qkv + (a.H + 2 * a.KV) * a.dh));
+      a.kc = (__half*)c.ptr("kc", cache);
+      a.vc = (__half*)c.ptr("vc", cache);
+      a.pos = (const int*)c.ptr("pos", 4 * (size_t)a.NB);
+      a.cos_t = (const __half*)c.ptr("cos", 2 * (size_t)a.M * a.dh, true);
+      a.sin_t = (const __half*)c.ptr("sin", 2 * (size_t)a.M * a.dh, true);
+      a.kn_g = (const __half*)c.ptr("kn", 2 * (size_t)a.dh, true);
+      a.kn_floor = (float)c.f("knf", 0.0);
+      a.err = p.d_err;
+      if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+      if (!dry) e = kv_append_launch(a, st, pdl);
+      if (e != cudaSuccess) why = std::string("launch failed: ") + cudaGetErrorString(e);
+      return e;
+    }
     a.qkv = (const float*)c.ptr("qkv", 4 * ((size_t)(a.NB - 1) * a.ld_qkv + (a.H + 2 * a.KV) * a.dh));
     a.kc = (__half*)c.ptr("kc", cache);
     a.vc = (__half*)c.ptr("vc", cache);
@@ -513,6 +533,9 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     a.kv_c = (float)c.f("kvc", 1.0);
     a.expand = c.i("expand", 0);
     a.prefetch = (int)c.i("prefetch", 0);
+    // rows of a shared cache are written by the kv_append launch just before: none may be staged
+    // before the launch wait
+    if (a.kv_seq_rows == 0 && a.prefetch) c.err = "prefetch needs one cache per sequence";
     a.pf = parse_pf(c);
     a.err = p.d_err;
     if ((a.cos_t == nullptr) != (a.sin_t == nullptr)) c.err = "cos/sin must both be given";

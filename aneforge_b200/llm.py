@@ -192,6 +192,12 @@ def emit_attention_decode(pb, ctx, li, lw, cfg, ls):
     kv.update(qn=f"{pre}.qn", kn=f"{pre}.kn", qnf=lw["qn_floor"], knf=lw["kn_floor"])
   if ctx["nsplit"] > 1:
     kv.update(part="attn.part", cnt="attn.cnt")
+  if ctx.get("verify"):
+    # speculative verify: the NB rows are consecutive tokens of ONE sequence sharing one cache; their
+    # K / V rows are appended first, then each row attends up to its own position
+    kv.update(seqrows=0, wkv=0, prefetch=0)
+    pb.op("kv_append", **{k: v for k, v in kv.items() if k in ("qkv", "kc", "vc", "pos", "nb", "h", "kv", "dh", "m",
+                                                              "cos", "sin", "kn", "knf", "seqrows")})
   pb.op("attn_decode", **kv)
   _emit_row_parallel(pb, ctx, f"{pre}.o", lw["o"], "att")
 
@@ -312,6 +318,7 @@ class LlamaPrefill:
     self._chunk_max_layers = 1 << 30
     self._dev = None
     self._dec = None
+    self._ver = None
     self._pre = None
     self._head = None
     self._lmT = None
@@ -450,10 +457,33 @@ class LlamaPrefill:
     if self._dec is not None:
       self._dec["prog"].release()
       self._dec = None
+    self._dec = self._build_decoder(M, NB, verify=False)
+    return self._dec
+
+  def _verifier(self, M, Kq):
+    """The speculative-verify program (cached by (M, Kq)): the decode step over Kq consecutive tokens
+    of one sequence at positions pos[0..Kq) sharing one resident cache - each row appends its K / V
+    and attends up to its own position; the head's greedy argmax gives the target's next token after
+    each of them (the reference's multi-token verify, `aneforge/speculative.py:21-106`)."""
+    M, Kq = int(M), int(Kq)
+    if self._ver is not None and self._ver["M"] == M and self._ver["NB"] == Kq:
+      return self._ver
+    if self._ver is not None:
+      self._ver["prog"].release()
+      self._ver = None
+    if any(self._spec(i).mixer != "attention" or is_graph_builder(DECODE_MIXERS["attention"])
+           for i in range(self.cfg.n_layers)) or self.tp is not None:
+      raise NotImplementedError("speculative verify needs the fused attention mixer on one GPU")
+    self._ver = self._build_decoder(M, Kq, verify=True)
+    return self._ver
+
+  def _build_decoder(self, M, NB, verify):
     cfg, d = self.cfg, self._load()
     D, H, KV, dh, V = cfg.dim, cfg.n_heads, cfg.n_kv_heads, cfg.dh, cfg.vocab
     Q = (H + 2 * KV) * dh
     ctx = self._ctx(NB, M)
+    ctx["verify"] = verify
+    CB = 1 if verify else NB                                # sequences with a cache of their own
     pb = PlanBuilder()
     pb.buf("tok", 4 * NB, "state"); pb.buf("pos", 4 * NB, "state")
     pb.buf("tok_out", 4 * NB, "out"); pb.buf("hist", 4 * NB * M, "out")
@@ -482,7 +512,7 @@ class LlamaPrefill:
     pb.buf("am.cnt", 4 * ((NB + 3) // 4), "scratch")
     for li in range(cfg.n_layers):
       self._declare_layer_weights(pb, li, d["layers"][li])
-      pb.buf(f"L{li}.K", 2 * NB * KV * M * dh, "state"); pb.buf(f"L{li}.V", 2 * NB * KV * M * dh, "state")
+      pb.buf(f"L{li}.K", 2 * CB * KV * M * dh, "state"); pb.buf(f"L{li}.V", 2 * CB * KV * M * dh, "state")
     pb.op("embed", tok="tok", table="embed", h="h", vocab=V, d=D, nb=NB)
     lows, gstates = [], []
     graph_mix = [is_graph_builder(DECODE_MIXERS[self._spec(i).mixer]) for i in range(cfg.n_layers)]
@@ -518,7 +548,7 @@ class LlamaPrefill:
     plan_l2_prefetch(pb)
     ins = {"tok": (NB,), "pos": (NB,)}
     for li in range(cfg.n_layers):
-      ins[f"L{li}.K"] = (NB, KV, M, dh); ins[f"L{li}.V"] = (NB, KV, M, dh)
+      ins[f"L{li}.K"] = (CB, KV, M, dh); ins[f"L{li}.V"] = (CB, KV, M, dh)
     outs = {"tok_out": (NB,), "hist": (NB, M), "hid": (NB, D), "logits": (NB, VL)}
     dt = {"tok": "int32", "pos": "int32", "tok_out": "int32", "hist": "int32", "logits": "fp32"}
     prog = R.Program.from_text(pb.text(), ins, outs, self.device, dt)
@@ -533,8 +563,7 @@ class LlamaPrefill:
       self._bind_layer(prog, li, d["layers"][li])
     for low in lows:
       low.finish(prog)
-    self._dec = {"M": M, "NB": NB, "prog": prog, "plan": pb, "graphs": lows, "gstates": gstates}
-    return self._dec
+    return {"M": M, "NB": NB, "CB": CB, "prog": prog, "plan": pb, "graphs": lows, "gstates": gstates}
 
   # -- graph-builder registry entries (the reference's form; lowered by `_compile.Lowering`)
   def _lower_graph_mlp(self, pb, li, fn, rows, lows, tag):
@@ -694,7 +723,7 @@ class LlamaPrefill:
     return self
 
   def release(self) -> None:
-    for k in ("_dec", "_pre", "_head"):
+    for k in ("_dec", "_ver", "_pre", "_head"):
       v = getattr(self, k)
       if v is not None:
         v["prog"].release()
@@ -764,7 +793,7 @@ class LlamaPrefill:
     """Copy the prefill K/V [KV, real, dh] into decode cache slot `slot`, positions [0, real)
     (reference `_seed_cache`, `llm.py:546-558`) - device to device."""
     cfg = self.cfg
-    KV, dh, M, NB = cfg.n_kv_heads, cfg.dh, dec["M"], dec["NB"]
+    KV, dh, M, NB = cfg.n_kv_heads, cfg.dh, dec["M"], dec.get("CB", dec["NB"])
     seq = pre["seq"]
     for li in range(cfg.n_layers):
       for nm in ("K", "V"):
@@ -777,7 +806,7 @@ class LlamaPrefill:
       if is_graph_builder(DECODE_MIXERS[self._spec(li).mixer]):
         continue
       for nm in ("K", "V"):
-        dec["prog"].tensor(f"L{li}.{nm}", (dec["NB"], self.cfg.n_kv_heads, dec["M"], self.cfg.dh)).zero_()
+        dec["prog"].tensor(f"L{li}.{nm}", (dec.get("CB", dec["NB"]), self.cfg.n_kv_heads, dec["M"], self.cfg.dh)).zero_()
     for name, n in dec.get("gstates", ()):
       dec["prog"].tensor(name, (n,)).zero_()
 
