@@ -213,6 +213,15 @@ class Lowering:
         nbytes = R.load_library().af_gemv_tc_scratch_bytes(N, K, min(rows, 16))
         kv["scr"] = self.pb.buf("gemv.scr", nbytes, "scratch")
       self.pb.op("gemv", **kv)
+    elif lin.kind in ("lut4", "blockwise"):
+      # packed palette / blockwise codes: the CUDA-core GEMV streams them as they are
+      xh = self._buf(f"{nm}.xh", 2 * rows * K)
+      self.pb.op("cast", src=x, dst=xh, n=rows * K, mode=1)
+      kv["gs"] = kv.pop("s")
+      if lin.kind == "blockwise":
+        kv["grp"] = lin.group
+      kv.update(wf=lin.wf, epi="f32", x=xh, w=wb, y=y, nb=rows)
+      self.pb.op("gemv", **kv)
     else:
       if lin.kind not in ("int8", "fp16"):
         raise NotImplementedError(f"generic matmul over {lin.kind} weights")

@@ -14,7 +14,10 @@ inline int env_int(const char* name, int dflt) {
   return v && *v ? atoi(v) : dflt;
 }
 
-enum WFormat : int { W_I8 = 0, W_F16 = 1, W_I4G32 = 2 };
+// W_LUT4: 4-bit indices (two per byte, low nibble first) into a 16-entry fp16 codebook per row
+// (gscale [N][16]); W_I8G: int8 codes with one fp16 scale per `group` consecutive elements of a row
+// (gscale [N][K / group]) - the reference's palettized and blockwise encodings, streamed packed
+enum WFormat : int { W_I8 = 0, W_F16 = 1, W_I4G32 = 2, W_LUT4 = 3, W_I8G = 4 };
 
 // L2 prefetch of (part of) a later kernel's weights, issued by a kernel whose own phase leaves HBM
 // idle: pieces of `piece` bytes every `stride` bytes of [base, base + bytes), spread evenly over the
@@ -31,7 +34,8 @@ struct GemvArgs {
   int ldx = 0;
   const void* w = nullptr;     // codes / fp16 weights, [N] rows
   const __half* scale = nullptr;   // int8: [N] per-row scale
-  const __half* gscale = nullptr;  // int4: [N][K/32] group scales
+  const __half* gscale = nullptr;  // int4: [N][K/32] group scales; LUT4: [N][16] codebooks; I8G: [N][K/group]
+  int group = 32;                  // I8G: elements per scale (a multiple of 16)
   const __half* bias = nullptr;    // [N] or null
   void* y = nullptr;           // output (see Epilogue); ARGMAX: optional fp32 logits
   int ldy = 0;

@@ -29,6 +29,15 @@ template <>
 struct WTraits<W_F16> { static constexpr int EPC = 8; };
 template <>
 struct WTraits<W_I4G32> { static constexpr int EPC = 32; };
+template <>
+struct WTraits<W_LUT4> { static constexpr int EPC = 32; };
+template <>
+struct WTraits<W_I8G> { static constexpr int EPC = 16; };
+
+// elements per 16-byte chunk of a weight format (host side)
+static int chunk_elems(int wf) {
+  return wf == W_I8 || wf == W_I8G ? 16 : wf == W_F16 ? 8 : 32;
+}
 
 // Rows per thread group: 8 for one sequence (128 B of weights in flight per thread), fewer as the
 // batch grows; the SWIGLU epilogue always works on blocks of 8 packed rows (4 gate + 4 up), the
@@ -56,6 +65,18 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
 #pragma unroll
     for (int b = 0; b < NB; ++b) acc[r][b] = 0.f;
 
+  // LUT4: the codebooks of this CTA's rows (at most 8 groups x 8 rows), decoded to fp32 once
+  __shared__ float lut_s[WF == W_LUT4 ? 64 * 16 : 1];
+  if (WF == W_LUT4) {
+    const int cta_row0 = blockIdx.x * G * R;
+    for (int i = threadIdx.x; i < G * R * 16; i += blockDim.x) {
+      const int row = cta_row0 + i / 16;
+      lut_s[i] = row < a.N ? h2f(a.gscale[(size_t)row * 16 + (i & 15)]) : 0.f;
+    }
+    __syncthreads();
+  }
+  const int ngroups = WF == W_I8G ? a.K / a.group : 0;
+
   bool waited = false;
   for (int c = tid; c < nch; c += TG) {
     uint4 wv[R];
@@ -72,6 +93,13 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
         gs[r] = row < a.N ? h2f(a.gscale[(size_t)row * nch + c]) : 0.f;
       }
     }
+    if (WF == W_I8G) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int row = row0 + r;
+        gs[r] = row < a.N ? h2f(a.gscale[(size_t)row * ngroups + (c * EPC) / a.group]) : 0.f;
+      }
+    }
     if (!waited) { pdl_wait(); waited = true; }
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
@@ -84,7 +112,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
       for (int r = 0; r < R; ++r) {
         const uint32_t* wu = reinterpret_cast<const uint32_t*>(&wv[r]);
         float s = 0.f;
-        if (WF == W_I8) {
+        if (WF == W_I8 || WF == W_I8G) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             float f0, f1, f2, f3;
@@ -94,6 +122,14 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
             s = fmaf(f2, xf[4 * q + 2], s);
             s = fmaf(f3, xf[4 * q + 3], s);
           }
+          if (WF == W_I8) acc[r][b] += s;
+          else acc[r][b] = fmaf(gs[r], s, acc[r][b]);
+        } else if (WF == W_LUT4) {
+          const float* lut = lut_s + (grp * R + r) * 16;
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) s = fmaf(lut[(wu[q] >> (4 * i)) & 15u], xf[8 * q + i], s);
           acc[r][b] += s;
         } else if (WF == W_F16) {
           float wf[8];
@@ -452,7 +488,9 @@ static int tile_template(int epi, int nb_tile, int nb_total) {
 // Host entry: the batch is processed in tiles of up to 4 rows of x (weights re-streamed per tile).
 // Argmax tiles each own a counter and a partial region of the scratch (see gemv_argmax_scratch).
 cudaError_t gemv_launch(const GemvArgs& a0, cudaStream_t st, bool pdl) {
-  if (a0.K % (a0.wf == W_I8 ? 16 : a0.wf == W_F16 ? 8 : 32)) return cudaErrorInvalidValue;
+  if (a0.K % chunk_elems(a0.wf)) return cudaErrorInvalidValue;
+  if (a0.wf == W_I8G && (a0.group < 16 || a0.group % 16 || a0.K % a0.group)) return cudaErrorInvalidValue;
+  if ((a0.wf == W_LUT4 || a0.wf == W_I8G) && (!a0.gscale || a0.epi == EPI_ARGMAX)) return cudaErrorInvalidValue;
   if (a0.NB < 1) return cudaErrorInvalidValue;
   // one launch over every row (gemv_argmax_scratch sizes the partial slots for it too)
   if (lm_head_tc_ok(a0)) return lm_head_tc_launch(a0, st, pdl);
@@ -490,6 +528,14 @@ cudaError_t gemv_launch(const GemvArgs& a0, cudaStream_t st, bool pdl) {
     AF_GEMV_CASE(W_I4G32, EPI_F16)
     AF_GEMV_CASE(W_I4G32, EPI_RESID)
     AF_GEMV_CASE(W_I4G32, EPI_SWIGLU)
+    AF_GEMV_CASE(W_LUT4, EPI_F32)
+    AF_GEMV_CASE(W_LUT4, EPI_F16)
+    AF_GEMV_CASE(W_LUT4, EPI_RESID)
+    AF_GEMV_CASE(W_LUT4, EPI_SWIGLU)
+    AF_GEMV_CASE(W_I8G, EPI_F32)
+    AF_GEMV_CASE(W_I8G, EPI_F16)
+    AF_GEMV_CASE(W_I8G, EPI_RESID)
+    AF_GEMV_CASE(W_I8G, EPI_SWIGLU)
 #undef AF_GEMV_CASE
     if (e != cudaSuccess) return e;
   }
@@ -498,8 +544,7 @@ cudaError_t gemv_launch(const GemvArgs& a0, cudaStream_t st, bool pdl) {
 
 // Number of CTAs of one argmax tile launch (every tile of a launch uses the same width).
 int gemv_argmax_ctas(int wf, int N, int K, int NB) {
-  const int epc = wf == W_I8 ? 16 : wf == W_F16 ? 8 : 32;
-  const int tg = pick_tg(K / epc);
+  const int tg = pick_tg(K / chunk_elems(wf));
   const int G = 256 / tg;
   const int R = rows_per_group(tile_template(EPI_ARGMAX, NB < 4 ? NB : 4, NB), EPI_ARGMAX);
   return (N + G * R - 1) / (G * R);

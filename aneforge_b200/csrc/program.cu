@@ -203,6 +203,8 @@ static int wf_of(const std::string& s) {
   if (s == "i8") return W_I8;
   if (s == "f16") return W_F16;
   if (s == "i4") return W_I4G32;
+  if (s == "l4") return W_LUT4;
+  if (s == "i8g") return W_I8G;
   return -1;
 }
 static int epi_of(const std::string& s) {
@@ -462,10 +464,17 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     const int out_cols = a.epi == EPI_SWIGLU ? a.N / 2 : a.N;
     a.ldy = c.i("ldy", out_cols);
     a.x = (const __half*)c.ptr("x", 2 * ((size_t)(a.NB - 1) * a.ldx + a.K));
-    const size_t wbytes = a.wf == W_I8 ? (size_t)a.N * a.K : a.wf == W_F16 ? (size_t)a.N * a.K * 2 : (size_t)a.N * a.K / 2;
+    const size_t wbytes = (a.wf == W_I8 || a.wf == W_I8G) ? (size_t)a.N * a.K
+                          : a.wf == W_F16 ? (size_t)a.N * a.K * 2 : (size_t)a.N * a.K / 2;
     a.w = c.ptr("w", wbytes);
     if (a.wf == W_I8) a.scale = (const __half*)c.ptr("s", 2 * (size_t)a.N);
     if (a.wf == W_I4G32) a.gscale = (const __half*)c.ptr("gs", 2 * (size_t)a.N * (a.K / 32));
+    if (a.wf == W_LUT4) a.gscale = (const __half*)c.ptr("gs", 2 * (size_t)a.N * 16);
+    if (a.wf == W_I8G) {
+      a.group = (int)c.i("grp", 32);
+      if (a.group < 16 || a.group % 16 || a.K % a.group) c.err = "grp must be a multiple of 16 dividing k";
+      else a.gscale = (const __half*)c.ptr("gs", 2 * (size_t)a.N * (a.K / a.group));
+    }
     a.bias = (const __half*)c.ptr("bias", 2 * (size_t)a.N, true);
     const size_t esz = (a.epi == EPI_F16 || a.epi == EPI_SWIGLU) ? 2 : 4;
     a.y = c.ptr("y", esz * ((size_t)(a.NB - 1) * a.ldy + out_cols), a.epi == EPI_ARGMAX);

@@ -156,8 +156,10 @@ def _emit_linear(pb, ctx, name, lin: DevLinear, x, y, epi, nb=None):
       if nbytes:
         pb.buf("gemv.scr", nbytes, "scratch")        # one split-K scratch shared by every GEMV
         kv["scr"] = "gemv.scr"
-  elif lin.kind == "int4_g32" and not lin.tiled:
-    kv["gs"] = f"{name}.s"
+  elif lin.kind in ("int4_g32", "lut4", "blockwise") and not lin.tiled:
+    kv["gs"] = f"{name}.s"                             # group scales / per-row codebooks
+    if lin.kind == "blockwise":
+      kv["grp"] = lin.group
   if lin.bias is not None:
     kv["bias"] = f"{name}.b"
   pb.op("gemv", **kv)

@@ -50,6 +50,7 @@ class DevLinear:
   N: int
   K: int
   tiled: bool = False  # int8 / int4_g32 in tensor-core fragment tiles (K % 32 == 0) vs row-major
+  group: int = 0       # blockwise: elements per scale
 
   @property
   def wf(self) -> str:
@@ -57,6 +58,10 @@ class DevLinear:
       return "i8t" if self.tiled else "i8"
     if self.kind == "int4_g32":
       return "i4t" if self.tiled else "i4"
+    if self.kind == "lut4":
+      return "l4"
+    if self.kind == "blockwise":
+      return "i8g"
     return "f16"
 
   @property
@@ -85,11 +90,12 @@ def decide_kind(W, compress, atol=0.05, block_size=32) -> str:
   return kind
 
 
-# encodings with no packed device format yet: the device multiplies by their decoded values,
-# stored as an fp16 matrix and run on the fp16-weight kernels. An accepted LUT4 weight and a sparse
-# weight decode to fp16 values exactly, so these match the reference's arithmetic; a blockwise
-# weight's int8 x fp16-scale product is rounded to fp16 once (the reference keeps it at the
-# operand precision of its matmul, fp16 on the ANE). They stream 2 bytes per weight, not 0.5 / 1.
+# Accepted LUT4 and blockwise weights stream packed (`_packed`: 4-bit codes + per-row codebook, or
+# int8 codes + per-block scales, on the CUDA-core GEMV) when every part of a fused projection takes
+# that encoding and the shape fits (LUT4: K % 32 == 0; blockwise: blocks a multiple of 16). The rest
+# - a sparse weight, projections whose parts encode differently, other shapes - run as fp16 matrices
+# of their decoded values on the fp16-weight kernels: exact for LUT4 and sparse values; a blockwise
+# weight's int8 x fp16-scale product is then rounded to fp16 once.
 DENSE_KINDS = ("lut4", "blockwise", "sparse")
 
 
@@ -128,11 +134,60 @@ def _quantize(W, kind, device):
   return Wd.half().contiguous(), None
 
 
+def _packed(parts, compress, atol, block_size):
+  """(kind, [(codes, side data)] per part, group) when every part takes the same packed encoding the
+  device streams as such - an accepted LUT4 palette (codes 4-bit, one 16-entry fp16 codebook per row,
+  K a multiple of 32) or accepted blockwise int8 (one fp16 scale per block, block a multiple of 16)
+  - else None."""
+  if compress not in ("int4", "blockwise", "auto"):
+    return None
+  hosts = [P.detach().float().cpu().numpy() if hasattr(P, "detach") else np.asarray(P, F32) for P in parts]
+  K = hosts[0].shape[1]
+  decided = [_blob.decide(W, compress, atol, block_size) for W in hosts]
+  kinds = {k for k, _ in decided}
+  if len(kinds) != 1:
+    return None
+  kind = kinds.pop()
+  if kind == "lut4" and K % 32 == 0:
+    return kind, [(packed, np.tile(lut.astype(F16), (W.shape[0], 1))) for W, (_, (packed, lut)) in zip(hosts, decided)], 0
+  if kind == "blockwise":
+    nbs = {nb for _, (_, _, nb) in decided}
+    group = K // nbs.pop() if len(nbs) == 1 else 0
+    if group and group % 16 == 0:
+      return kind, [(q, s) for _, (q, s, _) in decided], group
+  return None
+
+
+def _encode_packed(parts, kind, enc, group, device, biases, swiglu) -> DevLinear:
+  torch = torch_mod()
+  dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device)
+  if swiglu:
+    (cg, sg), (cu, su) = enc
+    codes = layout.interleave_blocks(cg, cu, layout.SWIGLU_HALF)
+    side = layout.interleave_blocks(sg, su, layout.SWIGLU_HALF)
+  else:
+    codes = np.concatenate([c for c, _ in enc], 0)
+    side = np.concatenate([s for _, s in enc], 0)
+  N, K = int(codes.shape[0]), int(parts[0].shape[1])
+  b = None
+  if biases is not None and any(x is not None for x in biases):
+    if swiglu:
+      raise NotImplementedError("bias on a gate/up projection")
+    b = torch.cat([torch.zeros(int(P.shape[0]), dtype=torch.float16, device=device) if x is None
+                   else to_device(x, device).float().half() for P, x in zip(parts, biases)]).contiguous()
+  w = dev(codes.view(np.uint8) if kind == "lut4" else codes.astype(np.int8))
+  return DevLinear(kind, w, dev(side.astype(F16)), b, N, K, False, group)
+
+
 def encode_linear(parts, compress, device, biases=None, swiglu=False, atol=0.05, block_size=32) -> DevLinear:
   """Encode one or more [N_i, K] matrices sharing their input into one device projection.
   `swiglu=True` takes (gate, up) and interleaves them for the fused silu(gate)*up epilogue;
   otherwise the rows are concatenated (q|k|v)."""
   torch = torch_mod()
+  packed = _packed(parts, compress, atol, block_size)
+  if packed is not None:
+    kind, enc, group = packed
+    return _encode_packed(parts, kind, enc, group, device, biases, swiglu)
   dec = [_decoded_fp16(P, compress, atol, block_size) for P in parts]
   # a decoded encoding runs as an fp16 matrix of its values (DENSE_KINDS)
   kinds = {"fp16" if k in DENSE_KINDS else k for k, _ in dec}

@@ -57,11 +57,11 @@ def test_compile_generic_ops_match_interpreter():
   model.release()
 
 
-@pytest.mark.parametrize("compress", ["int8", None, "int4_g32"])
+@pytest.mark.parametrize("compress", ["int8", None, "int4_g32", "blockwise"])
 @pytest.mark.parametrize("rows,K", [(1, 256), (20, 256), (40, 256), (3, 24)])
 def test_compile_linear_paths(compress, rows, K):
   """A `linear` on each path: tensor-core GEMV (<= 16 rows, 16-row slices above), tcgen05 GEMM
-  (>= 32 rows), and the generic matmul (contraction not a multiple of 32)."""
+  (>= 32 rows), the packed blockwise GEMV, and the generic matmul (contraction not a multiple of 32)."""
   from aneforge_b200 import compile as afc
   if compress == "int4_g32" and K % 32:
     pytest.skip("group-32 int4 needs K % 32 == 0 (falls back to fp16, covered by compress=None)")

@@ -100,10 +100,11 @@ def test_long_prompt_prefill_tensor_core_attention(S):
 
 
 @pytest.mark.parametrize("mixed", [False, True])
-def test_lut4_weights_run_decoded_on_fp16_path(mixed):
-  """compress="int4" on weights the reference's LUT gate accepts: the accepted LUT4 matrices run
-  as fp16 matrices of their codebook values (with `mixed`, k stays Gaussian and per-row int8, so
-  the fused q|k|v falls back to decoded fp16 for all three parts). Same bars as the golden tests."""
+def test_lut4_weights_run_packed(mixed):
+  """compress="int4" on weights the reference's LUT gate accepts: the accepted LUT4 matrices stream
+  packed (4-bit codes + a per-row codebook) through the LUT4 GEMV; with `mixed`, k stays Gaussian and
+  per-row int8, so the fused q|k|v falls back to decoded fp16 for all three parts. Same bars as the
+  golden tests."""
   from aneforge_b200.llm import LlamaPrefill
   cfg = Config(dim=256, n_layers=2, n_heads=4, n_kv_heads=2, ffn_dim=512, vocab=512, rope_base=10000.0,
                head_dim=64)
@@ -124,8 +125,9 @@ def test_lut4_weights_run_decoded_on_fp16_path(mixed):
     for proj, names in parts.items():
       kinds = [_decoded_fp16(w["layers"][i][n], "int4", 0.05, 32)[0] for n in names]
       n_lut += kinds.count("lut4")
-      # a projection with any accepted LUT part runs decoded in fp16; the rest stay per-row int8
-      assert dl[i][proj].wf == ("f16" if "lut4" in kinds else "i8t"), (i, proj, kinds)
+      # all parts accepted: packed LUT4; some accepted: decoded fp16; none: per-row int8
+      want = "l4" if set(kinds) == {"lut4"} else ("f16" if "lut4" in kinds else "i8t")
+      assert dl[i][proj].wf == want, (i, proj, kinds)
   assert n_lut >= 8
   prompt = list(np.random.default_rng(33).integers(0, cfg.vocab, 40))
   toks = m.generate(prompt, 16, max_len=64)
@@ -227,5 +229,27 @@ def test_qwen2_shaped_int4_g32_greedy_32_steps():
   pl = m.prefill(prompt)[0]
   hid, _ = om.prefill_hidden(prompt)
   ol = om.logits(hid[-1].astype(F32))
+  assert cosine(pl, ol) > 0.999
+  m.release()
+
+
+def test_blockwise_weights_run_packed():
+  """compress="blockwise" (`aneforge/_blob.py:46-56`): every projection's 32-column blocks pass the
+  reference's gate, so the int8 codes stream with their per-block fp16 scales (the blockwise GEMV)."""
+  from aneforge_b200.llm import LlamaPrefill
+  cfg = Config(dim=256, n_layers=2, n_heads=4, n_kv_heads=2, ffn_dim=512, vocab=512, rope_base=10000.0,
+               head_dim=64)
+  w = random_llama_weights(cfg, seed=35, std=0.05)
+  m = LlamaPrefill(to_b200_cfg(cfg), w, compress="blockwise")
+  dl = m._load()["layers"]
+  assert all(dl[i][p].wf == "i8g" and dl[i][p].group == 32 for i in range(2) for p in ("qkv", "o", "gu", "down"))
+  prompt = list(np.random.default_rng(36).integers(0, cfg.vocab, 40))
+  toks = m.generate(prompt, 16, max_len=64)
+  om = OracleModel(cfg, w, "blockwise", precision="device")
+  assert teacher_forced_check(om, prompt, toks, 64, n_check=16) <= 1
+  pl = m.prefill(prompt)[0]
+  hid, _ = om.prefill_hidden(prompt)
+  ol = om.logits(hid[-1].astype(F32))
+  assert np.abs(pl - ol).max() <= 1e-2 * np.abs(ol).max()
   assert cosine(pl, ol) > 0.999
   m.release()
