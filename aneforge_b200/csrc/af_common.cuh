@@ -114,7 +114,9 @@ AF_DEV void l2_prefetch_lines(const PF& pf, unsigned idx, unsigned n) {
   const size_t total = pieces * lines_per_piece;
   for (size_t i = idx; i < total; i += n) {
     const size_t off = (i / lines_per_piece) * pf.stride + (i % lines_per_piece) * 128;
-    if (off < pf.bytes) asm volatile("prefetch.global.L2 [%0];" ::"l"(pf.base + off));
+    if (off >= pf.bytes) continue;
+    if (pf.keep) asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(pf.base + off));
+    else asm volatile("prefetch.global.L2 [%0];" ::"l"(pf.base + off));
   }
 }
 

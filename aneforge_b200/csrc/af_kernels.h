@@ -25,6 +25,7 @@ enum WFormat : int { W_I8 = 0, W_F16 = 1, W_I4G32 = 2, W_LUT4 = 3, W_I8G = 4 };
 struct L2Pf {
   const char* base = nullptr;
   size_t bytes = 0, piece = 0, stride = 0;
+  int keep = 0;                // prefetch with the evict-last L2 priority (survives evict-first streams)
 };
 enum Epilogue : int { EPI_F32 = 0, EPI_F16 = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
 
@@ -84,6 +85,7 @@ struct GemvTcArgs {
   // expert ids (a selected expert held elsewhere makes the whole launch a no-op here) and the
   // routing-weight column of local expert e is e_base + e
   int e_base = 0, n_exp = 0;
+  int evict_first = 0;         // weight stages with the evict-first L2 policy (read once per step)
   // set by the launcher
   int Np = 0, Kp = 0, S = 1, maxc = 1;
   int csize = 0;               // > 1: thread-block clusters of csize CTAs split each row block's k range
@@ -180,7 +182,7 @@ cudaError_t moe_gate_launch(const float* logits, int ld, int NB, int E, int k, i
 // ---- tensor parallel (comm.cu): collectives on a program's stream, cross-rank argmax, residual add
 // dst = sum over the ranks of src; with `addto`, addto += that sum instead (dst then scratch)
 cudaError_t comm_all_reduce_f32(void* comm, const float* src, float* dst, size_t n, cudaStream_t st, std::string& why,
-                                int* err = nullptr, float* addto = nullptr);
+                                int* err = nullptr, float* addto = nullptr, bool pdl = false);
 cudaError_t comm_all_gather_i32(void* comm, const int* src, int* dst, size_t n, cudaStream_t st, std::string& why);
 int comm_size(void* comm);
 int comm_rank(void* comm);

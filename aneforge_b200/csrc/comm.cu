@@ -62,17 +62,18 @@ cudaError_t add_f32_launch(float* y, const float* x, size_t n, cudaStream_t st);
 // ---- one-shot all-reduce over NVLink peer memory (optional; set up by af_comm_p2p_open)
 //
 // Every rank owns one exchange buffer, mapped into every peer's address space through CUDA IPC:
-//   [2 sets][T source slots][cap floats]  data
-//   [2 sets][T source slots] u32          arrival flags (the call's epoch)
-//   u32                                   this rank's epoch counter
-// Call e (all ranks issue the same sequence of all-reduces) uses set e & 1: each rank stores its n
-// partial floats into slot `rank` of set e & 1 on every rank (its own included) with plain peer
-// stores, fences at system scope, then stores e into that slot's flag on every rank. It then waits
-// (bounded) until its own T flags read e and sums the T slots in rank order, so every rank computes
-// the same bits. Two sets make reuse safe: a rank can only write set s again (call e + 2) after
-// every peer has signalled call e + 1, which each does only after finishing call e.
+//   [2 sets][T source slots][cap] u64 words   value bits (low 32) | call epoch (high 32)
+//   u32                                       this rank's epoch counter
+// Call e (all ranks issue the same sequence of all-reduces) uses set e & 1. Each rank stores word
+// i = (partial[i], e) into slot `rank` of every rank's buffer (its own included) with plain 8-byte
+// peer stores, then polls its own buffer until every slot's word i carries epoch e and sums the T
+// values in rank order, so every rank computes the same bits. A word is one aligned 8-byte store,
+// so its value and epoch become visible together: no fence and no separate flag round trip (the
+// low-latency protocol of NCCL's LL transport). Two sets make reuse safe: a rank writes set s again
+// (call e + 2) only after it has read every peer's call e + 1 words, which each peer stores only
+// after finishing its reads of call e. Every poll is bounded; a timeout is recorded in the error word.
 constexpr int P2P_MAX_RANKS = 8;
-constexpr long long P2P_SPIN = 1ll << 24;             // bounded waits (~1 s)
+constexpr long long P2P_SPIN = 1ll << 22;             // bounded polls per word (well above any wait)
 
 struct P2pPeers {
   char* base[P2P_MAX_RANKS];                          // every rank's exchange buffer (own included)
@@ -83,15 +84,14 @@ struct Comm {
   int nranks = 1, rank = 0, device = 0;
   // peer-memory all-reduce
   char* xbuf = nullptr;                               // this rank's exchange buffer
-  size_t cap = 0;                                     // floats per slot
+  size_t cap = 0;                                     // words per slot
   size_t xbytes = 0;
   char* peer[P2P_MAX_RANKS] = {};                     // opened IPC mappings (peer[rank] = xbuf)
   bool p2p = false;
 };
 
-AF_HD size_t p2p_data_off(int set, int src, int T, size_t cap) { return ((size_t)set * T + src) * cap * 4; }
-AF_HD size_t p2p_flag_off(int set, int src, int T, size_t cap) { return (size_t)2 * T * cap * 4 + ((size_t)set * T + src) * 4; }
-AF_HD size_t p2p_epoch_off(int T, size_t cap) { return (size_t)2 * T * cap * 4 + (size_t)2 * T * 4; }
+AF_HD size_t p2p_data_off(int set, int src, int T, size_t cap) { return ((size_t)set * T + src) * cap * 8; }
+AF_HD size_t p2p_epoch_off(int T, size_t cap) { return (size_t)2 * T * cap * 8; }
 AF_HD size_t p2p_bytes(int T, size_t cap) { return p2p_epoch_off(T, cap) + 16; }
 
 __global__ void __launch_bounds__(1024) p2p_all_reduce_kernel(P2pPeers peers, int T, int rank, size_t cap,
@@ -102,58 +102,57 @@ __global__ void __launch_bounds__(1024) p2p_all_reduce_kernel(P2pPeers peers, in
   pdl_wait();
   const unsigned e = *reinterpret_cast<volatile unsigned*>(epoch) + 1u;
   const int set = (int)(e & 1u);
-  // push this rank's partial into slot `rank` of every rank
-  const int n4 = n / 4;
-  for (int p = 0; p < T; ++p) {
-    float4* d4 = reinterpret_cast<float4*>(peers.base[p] + p2p_data_off(set, rank, T, cap));
-    const float4* s4 = reinterpret_cast<const float4*>(src);
-    for (int i = threadIdx.x; i < n4; i += blockDim.x) d4[i] = __ldcg(s4 + i);
-    float* d = reinterpret_cast<float*>(peers.base[p] + p2p_data_off(set, rank, T, cap));
-    for (int i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) d[i] = __ldcg(src + i);
-  }
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x < T) {
-    unsigned* f = reinterpret_cast<unsigned*>(peers.base[threadIdx.x] + p2p_flag_off(set, rank, T, cap));
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
-  }
-  // wait for every rank's slot in this rank's buffer
-  __shared__ int timed_out;
-  if (threadIdx.x == 0) timed_out = 0;
-  __syncthreads();
-  if (threadIdx.x < T) {
-    const unsigned* f = reinterpret_cast<const unsigned*>(mine + p2p_flag_off(set, threadIdx.x, T, cap));
-    bool in = false;
-    for (long long i = 0; i < P2P_SPIN && !in; ++i) {
-      unsigned v;
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-      in = v == e;
+  // push: word i of this rank's slot on every rank
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const unsigned long long w = ((unsigned long long)e << 32) | __float_as_uint(__ldcg(src + i));
+    for (int p = 0; p < T; ++p) {
+      unsigned long long* d = reinterpret_cast<unsigned long long*>(peers.base[p] + p2p_data_off(set, rank, T, cap)) + i;
+      asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(d), "l"(w) : "memory");
     }
-    if (!in) timed_out = 1;
   }
-  __syncthreads();
-  if (timed_out && threadIdx.x == 0) af_set_err(err, AF_DEV_WAIT_TIMEOUT);
+  // reduce: every rank's word i, in rank order, once it carries this call's epoch
+  bool late = false;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     float acc = 0.f;
-    for (int s = 0; s < T; ++s) acc += __ldcg(reinterpret_cast<const float*>(mine + p2p_data_off(set, s, T, cap)) + i);
+    for (int s = 0; s < T; ++s) {
+      const unsigned long long* w = reinterpret_cast<const unsigned long long*>(mine + p2p_data_off(set, s, T, cap)) + i;
+      unsigned long long v = 0;
+      bool in = false;
+      for (long long k = 0; k < P2P_SPIN && !in; ++k) {
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(w) : "memory");
+        in = (unsigned)(v >> 32) == e;
+      }
+      late |= !in;
+      acc += __uint_as_float((unsigned)(v & 0xffffffffull));
+    }
     if (addto) addto[i] += acc;        // the residual update, as the separate add would do it
     else dst[i] = acc;
   }
+  if (late) af_set_err(err, AF_DEV_WAIT_TIMEOUT);
   __syncthreads();
   if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(epoch) = e;
   pdl_trigger();
 }
 
 cudaError_t comm_all_reduce_f32(void* comm, const float* src, float* dst, size_t n, cudaStream_t st, std::string& why,
-                                int* err, float* addto) {
+                                int* err, float* addto, bool pdl) {
   Comm* c = static_cast<Comm*>(comm);
   if (!c) { why = "no communicator"; return cudaErrorInvalidValue; }
-  if (c->p2p && n <= c->cap && n % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+  if (c->p2p && n <= c->cap) {
     P2pPeers peers;
     for (int r = 0; r < P2P_MAX_RANKS; ++r) peers.base[r] = r < c->nranks ? c->peer[r] : nullptr;
     const int threads = n >= 1024 ? 1024 : (int)((n + 31) / 32 * 32);
-    p2p_all_reduce_kernel<<<1, threads, 0, st>>>(peers, c->nranks, c->rank, c->cap, src, dst, addto, (int)n, err);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(threads);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, p2p_all_reduce_kernel, peers, c->nranks, c->rank, c->cap, src, dst, addto, (int)n,
+                              err);
   }
   if (!g_nccl.ok || !c->nccl) { why = "no communicator"; return cudaErrorInvalidValue; }
   const ncclResult_t r = g_nccl.all_reduce(src, dst, n, ncclFloat32, ncclSum, c->nccl, st);
@@ -277,7 +276,7 @@ int af_comm_p2p_handle(void* comm, size_t cap_floats, void* handle, size_t bytes
   int prev = 0;
   cudaGetDevice(&prev);
   cudaSetDevice(c->device);
-  c->cap = (cap_floats + 3) / 4 * 4;
+  c->cap = (cap_floats + 3) / 4 * 4;                 // words per slot
   c->xbytes = af::p2p_bytes(c->nranks, c->cap);
   cudaError_t e = cudaMalloc(&c->xbuf, c->xbytes);
   if (e == cudaSuccess) e = cudaMemset(c->xbuf, 0, c->xbytes);

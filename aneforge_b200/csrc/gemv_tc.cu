@@ -146,6 +146,7 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
       return;
     }
     const char* W = reinterpret_cast<const char*>(a.w);
+    const uint64_t pol = a.evict_first ? l2_evict_first_policy() : 0;
     int stage = 0, xs = 0;
     uint32_t phase = 0, xphase = 0;
     int in_flight = 0;
@@ -163,8 +164,8 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
           for (; kt < kce && in_flight < tc::STAGES; kt += F::ks) {
             const int nk = min(F::ks, kce - kt);
             mbar_arrive_expect_tx(&sh->full[stage], (uint32_t)nk * F::unit);
-            bulk_g2s(ring + (size_t)stage * F::stage, W + ((size_t)rb * KT + kt) * F::unit, nk * F::unit,
-                     &sh->full[stage]);
+            bulk_w(ring + (size_t)stage * F::stage, W + ((size_t)rb * KT + kt) * F::unit, nk * F::unit,
+                   &sh->full[stage], a.evict_first, pol);
             ++in_flight;
             if (++stage == tc::STAGES) { stage = 0; phase ^= 1; }
           }
@@ -183,8 +184,8 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
           const int nk = min(F::ks, kce - kt);
           if (!mbar_wait(&sh->empty[stage], phase ^ 1)) { ok = false; break; }
           mbar_arrive_expect_tx(&sh->full[stage], (uint32_t)nk * F::unit);
-          bulk_g2s(ring + (size_t)stage * F::stage, W + ((size_t)rb * KT + kt) * F::unit, nk * F::unit,
-                   &sh->full[stage]);
+          bulk_w(ring + (size_t)stage * F::stage, W + ((size_t)rb * KT + kt) * F::unit, nk * F::unit,
+                 &sh->full[stage], a.evict_first, pol);
           in_flight = min(in_flight + 1, tc::STAGES);
           if (++stage == tc::STAGES) { stage = 0; phase ^= 1; }
         }

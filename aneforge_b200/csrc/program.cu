@@ -196,6 +196,7 @@ static L2Pf parse_pf(OpCtx& c) {
   if (f.piece == f.stride) {                     // the whole region: 16 KB pieces back to back
     f.piece = f.stride = 16384;
   }
+  f.keep = (int)c.i("pfk", 0);
   return f;
 }
 
@@ -447,6 +448,8 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     if (a.scratch_bytes) a.scratch = c.ptr("scr", a.scratch_bytes);
     a.pf = parse_pf(c);
     a.err = p.d_err;
+    static const int evict_first = env_int("AF_L2_EVICT_FIRST", 0);
+    a.evict_first = (int)c.i("ef", evict_first);
     if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
     // prompt-sized row counts (prefill) run as a tensor-core GEMM unless the op asks for the GEMV
     const bool gemm = want_gemm && nexp == 1;
@@ -597,7 +600,7 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     if (!dry) {
       if (!p.comm) { why = op.kind + " needs a communicator (af_program_set_comm)"; return cudaErrorInvalidValue; }
       if (!red && c.i("ranks") != T) { why = "allgather: ranks does not match the communicator"; return cudaErrorInvalidValue; }
-      e = red ? comm_all_reduce_f32(p.comm, (const float*)src, (float*)dst, n, st, why, p.d_err, addto)
+      e = red ? comm_all_reduce_f32(p.comm, (const float*)src, (float*)dst, n, st, why, p.d_err, addto, pdl)
               : comm_all_gather_i32(p.comm, (const int*)src, (int*)dst, n, st, why);
       if (e != cudaSuccess) return e;
     }

@@ -65,6 +65,27 @@ AF_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) 
                ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 
+// An L2 policy that evicts the lines it touches first: for data read once per step (the weights),
+// so the stream does not push out lines that are still to be used.
+AF_DEV uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// bulk_g2s with an L2 cache-policy hint
+AF_DEV void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol) : "memory");
+}
+
+// weight stage copy: evict-first when `hint`
+AF_DEV void bulk_w(void* dst, const void* src, uint32_t bytes, uint64_t* bar, bool hint, uint64_t pol) {
+  if (hint) bulk_g2s_hint(dst, src, bytes, bar, pol);
+  else bulk_g2s(dst, src, bytes, bar);
+}
+
 AF_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(tc::CWARPS * 32) : "memory"); }
 
 AF_DEV void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {

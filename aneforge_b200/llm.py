@@ -275,6 +275,25 @@ def plan_l2_prefetch(pb, budget=None, mode=None):
     return (kind == "gemv" and kv.get("wf") in ("i8t", "i4t") and "experts" not in kv and not kv.get("gemm"))
 
   epis = {"f32": 0, "f16": 1, "resid": 2, "swiglu": 3}
+
+  def attach(kv, t, keep):
+    total = pb.bufs[t["w"]].nbytes
+    grid, cs = ctypes.c_int(), ctypes.c_int()
+    if lib.af_gemv_tc_grid(int(t["n"]), int(t["k"]), int(t["nb"]), epis[t["epi"]], 2 if t["wf"] == "i4t" else 0,
+                           ctypes.byref(grid), ctypes.byref(cs)) != 0:
+      return False
+    kv.update(pf=t["w"], pfs=total, pfn=min(total, budget), pfg=max(1, grid.value), pfk=int(keep))
+    return True
+
+  if mode == "ahead":
+    # each layer's attention (latency-bound: HBM nearly idle) prefetches the NEXT layer's fused qkv
+    # weights with the evict-last priority, so that they survive the layer's MLP stream
+    attn = [i for i, (kind, _) in enumerate(ops) if kind == "attn_decode"]
+    for i, j2 in zip(attn, attn[1:]):
+      q = max((j for j in range(i + 1, j2) if tc_gemv(*ops[j])), default=None)
+      if q is not None:
+        attach(ops[i][1], ops[q][1], keep=True)
+    return
   issued = set()
   for i, (kind, kv) in enumerate(ops):
     if not (tc_gemv(kind, kv) or kind in ("attn_decode", "rmsnorm")):

@@ -637,6 +637,65 @@ def kernel_bench(name, reps, warmup):
           "reps": reps, "warmup": warmup, "timing": "CUDA events around one CUDA-graph replay of `reps` back-to-back launches"}
 
 
+def timeline(args):
+  """Kernel timeline of decode-step graph replays (the `--timeline` mode): CUPTI kernel records
+  through torch.profiler over 3 steps after warm-up, each kernel's wall share = its end minus the
+  previous kernel's end (overlapped launches count once), summed per kernel kind and per layer."""
+  import collections
+  import torch
+  from aneforge_b200 import llm as L
+  spec = MODELS[MODEL]
+  dev = torch.device("cuda", 0)
+  torch.cuda.set_device(dev)
+  mlp = "moe" if spec.get("moe") else "swiglu"
+  cfg = L.LlamaConfig(**CFG, layers=[L.LayerSpec(mlp=mlp) for _ in range(CFG["n_layers"])])
+  w = make_weights(cfg, dev, seed=1234, qkv_bias=spec["qkv_bias"], moe=bool(spec.get("moe")))
+  m = L.LlamaPrefill(cfg, w, compress=spec["compress"], moe_compress=spec.get("moe_compress", "same"))
+  m._load()
+  del w
+  NB = args.batch
+  M = PROMPT + 64
+  dec = m._decoder(M, NB)
+  prog = dec["prog"]
+  m._reset_state(dec)
+  rng = np.random.default_rng(99)
+  for b in range(NB):
+    pre, real, _ = m._prefill_hidden(list(rng.integers(0, cfg.vocab, PROMPT)))
+    m._seed_cache(dec, pre, real, slot=b)
+  torch.cuda.synchronize()
+  prog.set_input("tok", np.full(NB, 7, np.int32)); prog.set_input("pos", np.full(NB, PROMPT, np.int32))
+  for _ in range(max(args.warmup, 3)):
+    prog.execute_async()
+  prog.sync()
+  with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+    for _ in range(3):
+      prog.execute_async()
+    prog.sync()
+    torch.cuda.synchronize()
+  ev = sorted((e for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA),
+              key=lambda e: e.time_range.start)
+  per = len(ev) // 3
+  step = ev[per:2 * per]                                   # the middle step
+  kinds = {"gemv_tc_kernel<1, 0": "qkv (f32 epi)", "gemv_tc_kernel<1, 2": "o / down (resid epi)",
+           "gemv_tc_kernel<1, 3": "gate|up (swiglu epi)", "attn_decode": "attention", "rmsnorm": "rmsnorm",
+           "gemv_kernel": "lm_head + argmax", "embed": "embed", "moe_gate": "moe gate", "lm_head_tc": "lm_head (tensor pipe)"}
+  share, busy, count = collections.defaultdict(float), collections.defaultdict(float), collections.Counter()
+  t0 = step[0].time_range.start
+  prev = t0
+  for e in step:
+    k = next((v for s, v in kinds.items() if s in e.name), e.name[:40])
+    end = e.time_range.end
+    share[k] += max(0.0, end - prev)
+    busy[k] += e.time_range.end - e.time_range.start
+    count[k] += 1
+    prev = max(prev, end)
+  span = prev - t0
+  return {"mode": "timeline", "model": MODEL, "batch": NB, "kernels_per_step": per, "step_us": round(span, 1),
+          "per_kind": {k: {"launches": count[k], "wall_share_us": round(share[k], 1), "busy_us": round(busy[k], 1),
+                           "wall_share_frac": round(share[k] / span, 4)} for k in share},
+          "how": "torch.profiler CUDA kernel records of 3 CUDA-graph replays after warm-up; the middle step"}
+
+
 def profile_traffic(name="gemv_tc_gate_up_llama8b.md"):
   """DRAM bytes per launch of the dominant kernel from the committed ncu summary (or None)."""
   import re
@@ -718,11 +777,16 @@ def main():
                        "| gemm_qkv | gemm_o | gemm_down "
                        "| rmsnorm | moe_gate | prefill (the whole prefill program of --model) | prefill_1layer")
   ap.add_argument("--reps", type=int, default=50)
+  ap.add_argument("--timeline", action="store_true",
+                  help="print the kernel timeline of decode-step graph replays (CUPTI through torch.profiler)")
   ap.add_argument("--profile-region", action="store_true",
                   help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
   args = ap.parse_args()
   select_model(args.model)
   ws, rank, _ = _dist()
+  if args.timeline:
+    print(json.dumps(timeline(args)), flush=True)
+    return
   if args.kernel:
     for name in args.kernel.split(","):
       print(json.dumps(kernel_bench(name, args.reps, max(args.warmup, 3))), flush=True)
