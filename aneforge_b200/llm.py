@@ -400,6 +400,9 @@ class LlamaPrefill:
       else:
         d.update(DECODE_MLP_LOADERS[ls.mlp](self, lw, dev))
       layers.append(d)
+      free = getattr(self.w["layers"], "free", None)
+      if free is not None:
+        free(i)                              # a lazily read checkpoint layer is on the device now
     fg, ff = rms_weights(self.w["final_norm"], cfg.norm_eps, dev)
     lm = self.w["lm_head"]
     self._head_exact = fp16_bits_exact(lm)
@@ -423,7 +426,7 @@ class LlamaPrefill:
       prog.bind(f"L{li}.egu.w", ex.gu_w); prog.bind(f"L{li}.edown.w", ex.down_w)
       if ex.gu_s is not None:
         prog.bind(f"L{li}.egu.s", ex.gu_s); prog.bind(f"L{li}.edown.s", ex.down_s)
-    for key in ("qkv", "o", "gu", "down", "router"):
+    for key in ("qkv", "o", "gu", "down", "router", "shgu", "shdown", "shg"):
       if key not in d:
         continue
       lin = d[key]
@@ -442,7 +445,7 @@ class LlamaPrefill:
       pb.buf(f"L{li}.egu.w", ex.gu_w.numel(), "weight"); pb.buf(f"L{li}.edown.w", ex.down_w.numel(), "weight")
       if ex.gu_s is not None:
         pb.buf(f"L{li}.egu.s", ex.gu_s.numel() * 2, "weight"); pb.buf(f"L{li}.edown.s", ex.down_s.numel() * 2, "weight")
-    for key in ("qkv", "o", "gu", "down", "router"):
+    for key in ("qkv", "o", "gu", "down", "router", "shgu", "shdown", "shg"):
       if key not in d:
         continue
       lin = d[key]
@@ -466,7 +469,7 @@ class LlamaPrefill:
     # through scratch (the last CTA of each head merges them).
     nsplit = decode_nsplit(M, cfg.n_kv_heads, NB)
     return {"NB": NB, "M": M, "nsplit": nsplit, "scale": d["scale"], "kvc": d["kvc"], "expand": G > 1 and d["kvc"] != 1.0,
-            "tp": self.tp is not None, "D": cfg.dim}
+            "tp": self.tp is not None, "tp_rank": self.tp.rank if self.tp is not None else 0, "D": cfg.dim}
 
   # -- programs
   def _decoder(self, M, NB=1):
@@ -512,7 +515,7 @@ class LlamaPrefill:
     pb.buf("h", 4 * NB * D, "tmp"); pb.buf("xn", 2 * NB * D, "tmp"); pb.buf("qkv", 4 * NB * Q, "tmp")
     pb.buf("att", 2 * NB * H * dh, "tmp")
     F = max([l["gu"].N // 2 for l in d["layers"] if "gu" in l] + [l["experts"].F for l in d["layers"] if "experts" in l]
-            + [1])
+            + [l["shgu"].N // 2 for l in d["layers"] if "shgu" in l] + [1])
     pb.buf("act", 2 * NB * F, "tmp")
     VL = int(d["lm_head"].shape[0])                       # local vocabulary rows (all of them without TP)
     pb.buf("embed", 2 * V * D, "weight"); pb.buf("lm_head", 2 * VL * D, "weight"); pb.buf("final_g", 2 * D, "weight")
@@ -667,7 +670,7 @@ class LlamaPrefill:
     pb.buf("h", 4 * seq * D, "tmp"); pb.buf("xn", 2 * seq * D, "tmp"); pb.buf("qkv", 4 * seq * Q, "tmp")
     pb.buf("att", 2 * seq * H * dh, "tmp"); pb.buf("qbuf", 2 * seq * H * dh, "tmp")
     F = max([l["gu"].N // 2 for l in d["layers"] if "gu" in l] + [l["experts"].F for l in d["layers"] if "experts" in l]
-            + [1])
+            + [l["shgu"].N // 2 for l in d["layers"] if "shgu" in l] + [1])
     pb.buf("act", 2 * seq * F, "tmp")
     if self.tp is not None:
       pb.buf("tp.part", 4 * seq * D, "tmp")

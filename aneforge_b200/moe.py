@@ -20,10 +20,38 @@ from .weights import encode_experts, encode_linear
 
 
 def load_moe(runner, lw, dev):
-  """Router (graph compress=) and experts (`moe_compress`) of one layer."""
-  c = runner.compress
-  return {"router": encode_linear([lw["router"]], c, dev, atol=runner.compress_atol, block_size=runner.block_size),
-          "experts": encode_experts(lw["wgate_exps"], lw["wup_exps"], lw["wdown_exps"], runner.moe_compress, dev)}
+  """Router (graph compress=) and experts (`moe_compress`) of one layer, plus Qwen2-MoE's shared
+  expert and its gate when the layer has them (graph compress=, like the router)."""
+  c, kw = runner.compress, dict(atol=runner.compress_atol, block_size=runner.block_size)
+  d = {"router": encode_linear([lw["router"]], c, dev, **kw),
+       "experts": encode_experts(lw["wgate_exps"], lw["wup_exps"], lw["wdown_exps"], runner.moe_compress, dev)}
+  if "wgate_sh" in lw:
+    d["shgu"] = encode_linear([lw["wgate_sh"], lw["wup_sh"]], c, dev, swiglu=True, **kw)
+    d["shdown"] = encode_linear([lw["wdown_sh"]], c, dev, **kw)
+    d["shg"] = encode_linear([lw["shared_gate"]], c, dev, **kw)
+  return d
+
+
+def _shared_expert(pb, ctx, pre, lw, y):
+  """Qwen2-MoE's always-on shared expert (`aneforge/moe.py:60-62`): y += sigmoid(xn . g) *
+  down(silu(gate(xn)) * up(xn)) per row; the sigmoid gate scales the down projection's residual
+  epilogue like a routing weight."""
+  NB = ctx["NB"]
+  pb.buf("moe.shg", 4 * NB, "tmp")
+  llm._emit_linear(pb, ctx, f"{pre}.shg", lw["shg"], "xn", "moe.shg", "f32")
+  pb.op("g_un", op=2, x="moe.shg", y="moe.shg", n=NB)                 # sigmoid, in place
+  llm._emit_linear(pb, ctx, f"{pre}.shgu", lw["shgu"], "xn", "act", "swiglu")
+  down = lw["shdown"]
+  kv = dict(wf=down.wf, epi="resid", x="act", w=f"{pre}.shdown.w", y=y, nb=NB, n=down.N, k=down.K, rw="moe.shg", rwe=1)
+  if down.kind == "int8":
+    kv["s"] = f"{pre}.shdown.s"
+  if not down.tiled:
+    raise NotImplementedError("the shared expert runs on the tensor-core GEMV: compress='int8' (K % 32 == 0) "
+                              "or 'int4_g32'")
+  nbytes = R.load_library().af_gemv_tc_scratch_bytes(down.N, down.K, NB)
+  if nbytes:
+    kv["scr"] = pb.buf("gemv.scr", nbytes, "scratch")
+  pb.op("gemv", **kv)                                     # per-row gate applied in the residual epilogue
 
 
 def _expert_gemvs(pb, pre, ex, NB, E, k, sparse, y="h", e_base=0):
@@ -70,11 +98,65 @@ def emit_moe(pb, ctx, li, lw, cfg, ls):
   pb.op("moe_gate", logits="moe.logits", nb=NB, e=E, k=k, renorm=int(renorm), gw="moe.gw", sel="moe.sel")
   if not ep:
     _expert_gemvs(pb, pre, ex, NB, E, k, sparse=NB == 1)
+    if "shgu" in lw:
+      _shared_expert(pb, ctx, pre, lw, "h")
     return
   n = NB * cfg.dim
   pb.op("fill", dst="tp.part", bytes=4 * n, value=0)
   _expert_gemvs(pb, pre, ex, NB, E, k, sparse=NB == 1, y="tp.part", e_base=e0)
+  if "shgu" in lw and ctx.get("tp_rank", 0) == 0:
+    _shared_expert(pb, ctx, pre, lw, "tp.part")        # replicated weights: added once, by rank 0
   pb.op("allreduce", src="tp.part", dst="tp.part", n=n, addto="h")
+
+
+def load_gguf(path: str, n_layers: int | None = None, compress: str | None = None, **runner_kw) -> "llm.LlamaPrefill":
+  """A Qwen-MoE GGUF checkpoint as a runner (reference `aneforge/moe.py:129-173`): Qwen3-MoE
+  (QK-norm) or Qwen2-MoE / Qwen1.5-MoE (QKV biases, the sigmoid-gated shared expert, no top-k
+  renormalisation). The architecture's features are read off the tensors present; `n_layers`
+  keeps the first layers only. Layer weights are dequantized to fp16 when the runner encodes them
+  and dropped right after, so the host never holds the whole model; the embedding and lm_head are
+  kept fp32 as the reference keeps them."""
+  from .gguf_file import GGUFFile, LazyLayers
+  import numpy as np
+  g = GGUFFile(path)
+  total = int(g.scalar("block_count", 0))
+  n = total if n_layers is None else min(int(n_layers), total)
+  dim, heads = int(g.scalar("embedding_length", 0)), int(g.scalar("attention.head_count", 0))
+  ffn = g.shape("blk.0.ffn_gate_exps.weight")[1]      # [dim, ffn, E]: Qwen1.5 has no ffn length key
+  qk_norm = g.has("blk.0.attn_q_norm.weight")
+  shared = g.has("blk.0.ffn_gate_shexp.weight")
+  cfg = llm.LlamaConfig(
+    dim=dim, n_layers=n, n_heads=heads, n_kv_heads=int(g.scalar("attention.head_count_kv", heads)),
+    ffn_dim=int(ffn), vocab=g.rows("token_embd.weight"), rope_base=float(g.scalar("rope.freq_base", 10000.0)),
+    norm_eps=float(g.scalar("attention.layer_norm_rms_epsilon", 1e-6)),
+    head_dim=int(g.scalar("attention.key_length", 0) or dim // heads),
+    layers=[llm.LayerSpec(mixer="attention", mlp="moe", qk_norm=qk_norm) for _ in range(n)],
+    extra={"n_experts": int(g.scalar("expert_count", 0)), "n_experts_per_tok": int(g.scalar("expert_used_count", 0)),
+           "norm_topk_prob": g.arch != "qwen2moe"})
+
+  def layer(i):
+    b = f"blk.{i}."
+    lw = {"wq": g.get(b + "attn_q.weight"), "wk": g.get(b + "attn_k.weight"), "wv": g.get(b + "attn_v.weight"),
+          "wo": g.get(b + "attn_output.weight"), "attn_norm": g.get(b + "attn_norm.weight"),
+          "mlp_norm": g.get(b + "ffn_norm.weight"), "router": g.get(b + "ffn_gate_inp.weight"),
+          "wgate_exps": g.get(b + "ffn_gate_exps.weight"), "wup_exps": g.get(b + "ffn_up_exps.weight"),
+          # stored [E, dim, ffn]; the MoE layer takes [E, ffn, dim]
+          "wdown_exps": np.ascontiguousarray(g.get(b + "ffn_down_exps.weight").transpose(0, 2, 1))}
+    for key, t in (("q_norm", "attn_q_norm.weight"), ("k_norm", "attn_k_norm.weight"),
+                   ("q_bias", "attn_q.bias"), ("k_bias", "attn_k.bias"), ("v_bias", "attn_v.bias")):
+      if g.has(b + t):
+        lw[key] = g.get(b + t)
+    if shared:
+      lw.update(wgate_sh=g.get(b + "ffn_gate_shexp.weight"), wup_sh=g.get(b + "ffn_up_shexp.weight"),
+                wdown_sh=g.get(b + "ffn_down_shexp.weight"),
+                shared_gate=g.get(b + "ffn_gate_inp_shexp.weight").reshape(1, dim))
+    g.release_pages()
+    return lw
+
+  head = "output.weight" if g.has("output.weight") else "token_embd.weight"     # tied embeddings
+  w = {"embed": g.get("token_embd.weight", np.float32), "final_norm": g.get("output_norm.weight"),
+       "lm_head": g.get(head, np.float32), "layers": LazyLayers(layer, n)}
+  return llm.LlamaPrefill(cfg, w, compress=compress, **runner_kw)
 
 
 llm.DECODE_MLP_LOADERS["moe"] = load_moe

@@ -211,6 +211,11 @@ class OracleModel:
     E, ffn, dim = lw["wgate_exps"].shape
     gtile = max(1, min(E, 65536 // ffn))
     m = {"router": Linear(lw["router"], None, c, self.atol, self.bs), "E": E, "ffn": ffn}
+    if "wgate_sh" in lw:
+      # Qwen2-MoE's always-on shared expert and its sigmoid gate (`aneforge/moe.py:60-62`): plain
+      # `linear`s, encoded by the graph's compress= like the router
+      for key in ("wgate_sh", "wup_sh", "wdown_sh", "shared_gate"):
+        m[key] = Linear(lw[key], None, self.compress, self.atol, self.bs)
     for key in ("wgate_exps", "wup_exps"):
       tiles = []
       for s0 in range(0, E, gtile):
@@ -448,6 +453,10 @@ def _moe(self, m, h):
   act = silu(experts("wgate_exps")) * experts("wup_exps")
   out = np.einsum("tef,efd->etd", self._mm_in(act), m["wdown"], dtype=F32)   # [E, T, dim]
   comb = (out * gw.T[:, :, None]).sum(axis=0).astype(F32)
+  if "wgate_sh" in m:
+    sh_act = silu(self._lin(m["wgate_sh"], hn)) * self._lin(m["wup_sh"], hn)
+    gate = (F32(1.0) / (F32(1.0) + np.exp(-self._lin(m["shared_gate"], hn)))).astype(F32)   # [T, 1]
+    comb = (comb + self._lin(m["wdown_sh"], sh_act) * gate).astype(F32)
   return (h + comb).astype(F32)
 
 
@@ -496,9 +505,11 @@ def decoder_block_step(cfg: Config, lw: dict, h: np.ndarray, Kc, Vc, pos: int, c
 
 
 def random_llama_weights(cfg: Config, seed: int = 0, std: float = 0.02, dtype=F16, moe: bool = False,
-                         qkv_bias: bool = False):
+                         qkv_bias: bool = False, shared_expert: int = 0):
   """Seeded N(0, std) weights in the reference layout, unit norms (the shape of
-  `tests/_helpers.py:make_random_llama_model`, with the benchmark's N(0, 0.02))."""
+  `tests/_helpers.py:make_random_llama_model`, with the benchmark's N(0, 0.02)). `shared_expert` > 0
+  adds a Qwen2-MoE shared expert of that width and its sigmoid gate to every MoE layer (the keys
+  `aneforge/moe.py:165-167` loads)."""
   rng = np.random.default_rng(seed)
   R = lambda *s: (rng.standard_normal(s, dtype=F32) * F32(std)).astype(dtype)
   dh, D = cfg.dh, cfg.dim
@@ -513,6 +524,9 @@ def random_llama_weights(cfg: Config, seed: int = 0, std: float = 0.02, dtype=F1
       lw["router"] = R(E, D)
       lw["wgate_exps"] = R(E, cfg.ffn_dim, D); lw["wup_exps"] = R(E, cfg.ffn_dim, D)
       lw["wdown_exps"] = R(E, cfg.ffn_dim, D)
+      if shared_expert:
+        Fs = int(shared_expert)
+        lw["wgate_sh"] = R(Fs, D); lw["wup_sh"] = R(Fs, D); lw["wdown_sh"] = R(D, Fs); lw["shared_gate"] = R(1, D)
     else:
       lw["wgate"] = R(cfg.ffn_dim, D); lw["wup"] = R(cfg.ffn_dim, D); lw["wdown"] = R(D, cfg.ffn_dim)
     w["layers"].append(lw)

@@ -111,3 +111,57 @@ def test_moe_decoder_matches_oracle(experts):
   for p, b in zip(prompts, batch):
     assert m.generate(p, 12, max_len=48) == b
   m.release()
+
+
+@pytest.mark.parametrize("compress", ["int8", "int4_g32"])
+def test_moe_shared_expert_matches_oracle(compress):
+  """Qwen2-MoE layers: routed experts plus the sigmoid-gated shared expert (`aneforge/moe.py:60-62`),
+  decode at batch 1 and 3 and the prefill GEMM rows, against the oracle's teacher-forced pass."""
+  from aneforge_b200.llm import LlamaPrefill
+  from tests.test_llm_gpu import teacher_forced_check
+  cfg = _moe_cfg()
+  cfg.extra["norm_topk_prob"] = False                     # Qwen1.5-MoE does not renormalise the top-k
+  w = random_llama_weights(cfg, seed=41, std=0.05, moe=True, shared_expert=640)
+  for lw in w["layers"]:
+    lw["router"] = (lw["router"].astype(np.float32) * 10).astype(F16)
+    lw["shared_gate"] = (lw["shared_gate"].astype(np.float32) * 20).astype(F16)   # gates away from 0.5
+  m = LlamaPrefill(_b200_cfg(cfg), w, compress=compress, moe_compress=compress)
+  prompt = list(np.random.default_rng(42).integers(0, cfg.vocab, 37))       # >= 32 rows: prefill GEMM
+  toks = m.generate(prompt, 20, max_len=96)
+  om = OracleModel(cfg, w, compress, precision="device", moe_compress=compress)
+  assert teacher_forced_check(om, prompt, toks, 96, n_check=20) <= 2
+  # the shared expert changes the output: the same model without it decodes another sequence
+  w2 = {**w, "layers": [{k: v for k, v in lw.items() if not k.endswith("_sh") and k != "shared_gate"}
+                        for lw in w["layers"]]}
+  m2 = LlamaPrefill(_b200_cfg(cfg), w2, compress=compress, moe_compress=compress)
+  assert m2.generate(prompt, 20, max_len=96) != toks
+  m2.release()
+  prompts = [prompt, list(np.random.default_rng(43).integers(0, cfg.vocab, 11))]
+  batch = m.generate_batch(prompts, 10, max_len=64)
+  for p, b in zip(prompts, batch):
+    assert m.generate(p, 10, max_len=64) == b
+  m.release()
+
+
+@pytest.mark.parametrize("arch", ["qwen2moe", "qwen3moe"])
+def test_load_gguf_decodes_like_the_oracle(tmp_path, arch):
+  """A Qwen-MoE GGUF (Q8_0 experts) through `moe.load_gguf` onto the device, against the oracle
+  on the same host weights."""
+  pytest.importorskip("gguf")
+  from aneforge_b200.moe import load_gguf
+  from tests.test_llm_gpu import teacher_forced_check
+  from tests.test_moe_cpu import _write_qwen_moe_gguf
+  path = tmp_path / "m.gguf"
+  _write_qwen_moe_gguf(path, arch, np.random.default_rng(8), dim=256, heads=4, kv=2, ffn=128, E=4, vocab=512,
+                        router_scale=10.0)          # expert choices well clear of ties
+  m = load_gguf(str(path), compress="int8")
+  c = m.cfg
+  oc = Config(dim=c.dim, n_layers=c.n_layers, n_heads=c.n_heads, n_kv_heads=c.n_kv_heads, ffn_dim=c.ffn_dim,
+              vocab=c.vocab, rope_base=c.rope_base, norm_eps=c.norm_eps, head_dim=c.head_dim, extra=dict(c.extra))
+  ow = {"embed": m.w["embed"], "final_norm": m.w["final_norm"], "lm_head": m.w["lm_head"],
+        "layers": [m.w["layers"][i] for i in range(c.n_layers)]}
+  prompt = list(np.random.default_rng(9).integers(0, c.vocab, 13))
+  toks = m.generate(prompt, 16, max_len=48)
+  om = OracleModel(oc, ow, "int8", precision="device")
+  assert teacher_forced_check(om, prompt, toks, 48, n_check=16) <= 2
+  m.release()
