@@ -56,6 +56,7 @@ SIGNATURES = [
   ("af_pack_i8_tiles_bytes", c_size_t, [c_int, c_int]),
   ("af_pack_i8_tiles", c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
   ("af_gemv_tc_scratch_bytes", c_size_t, [c_int, c_int, c_int]),
+  ("af_gemv_chain_scratch_bytes", c_size_t, [c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_int), c_int, c_int]),
   ("af_gemv_tc_grid", c_int, [c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
   ("af_gemv_tc", c_int, [c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                          c_void_p, c_size_t, c_void_p]),

@@ -94,6 +94,48 @@ struct GemvTcArgs {
   int* counters = nullptr;
 };
 cudaError_t gemv_tc_launch(const GemvTcArgs& a, cudaStream_t st, bool pdl);
+
+// A chain of tiled GEMVs run by one persistent launch (gemv_chain.cu): job j + 1 reads what job j
+// (and the RMSNorm attached to it) wrote, while every CTA keeps streaming the weights of its later
+// jobs into its ring. All jobs share the weight format and the batch (1..16 rows).
+constexpr int CHAIN_MAX_JOBS = 8;
+struct ChainJob {
+  const void* w = nullptr;          // pack_i8_tiles / pack_i4_tiles layout
+  const __half* scale = nullptr;    // int8: [N] per-row scales
+  const __half* bias = nullptr;
+  const __half* x = nullptr;        // [NB][ldx] fp16
+  int ldx = 0;
+  void* y = nullptr;                // EPI_F32 / EPI_F16 / EPI_RESID (fp32 y += ..) / EPI_SWIGLU (fp16)
+  int ldy = 0;
+  int N = 0, K = 0, epi = EPI_F32;
+  // optional RMSNorm run once the job is complete (before the next job starts):
+  // nout[b] = fp16(nx[b] / max(|nx[b]|, nfloor) * ng) over nd columns, nx fp32
+  const float* nx = nullptr;
+  int ldnx = 0;
+  const __half* ng = nullptr;
+  float nfloor = 0.f;
+  __half* nout = nullptr;
+  int ldno = 0, nd = 0;
+  // set by the launcher
+  int RB = 0, KT = 0, maxc = 1;
+  long long U = 0;
+  int* cnt = nullptr;               // [RB] arrival tickets
+  float* part = nullptr;            // [RB][maxc][64][NT * 8] partial sums
+};
+struct GemvChainArgs {
+  ChainJob job[CHAIN_MAX_JOBS];
+  int njobs = 0, NB = 1, wf = W_I8;
+  void* scratch = nullptr;          // gemv_chain_scratch_bytes; zero before the first launch
+  size_t scratch_bytes = 0;
+  int* err = nullptr;
+  int evict_first = 0;
+  // set by the launcher
+  int* done = nullptr;              // [njobs] row blocks finished
+  int* ready = nullptr;             // [njobs] job (and its norm) complete
+  int* exits = nullptr;             // CTAs finished
+};
+cudaError_t gemv_chain_launch(GemvChainArgs a, cudaStream_t st, bool pdl);
+size_t gemv_chain_scratch_bytes(const GemvChainArgs& a);
 // Prefill GEMM on tcgen05 (gemm_tc.cu): same arguments as the tiled GEMV with NB = M prompt rows.
 cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl);
 size_t gemv_tc_scratch_bytes(int N, int K, int NB);

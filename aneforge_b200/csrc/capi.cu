@@ -96,6 +96,21 @@ int af_pack_i8_tiles(const int8_t* codes, int n, int k, uint8_t* tiles, void* st
 size_t af_pack_i8_tiles_bytes(int n, int k) { return af::pack_i8_tiles_bytes(n, k); }
 
 size_t af_gemv_tc_scratch_bytes(int n, int k, int nb) { return af::gemv_tc_scratch_bytes(n, k, nb); }
+size_t af_gemv_chain_scratch_bytes(int njobs, const int* n, const int* k, int nb, int wf) {
+  if (njobs < 1 || njobs > af::CHAIN_MAX_JOBS || !n || !k || nb < 1 || nb > 16 ||
+      (wf != af::W_I8 && wf != af::W_I4G32))
+    return 0;
+  af::GemvChainArgs a;
+  a.njobs = njobs;
+  a.NB = nb;
+  a.wf = wf;
+  for (int j = 0; j < njobs; ++j) {
+    if (n[j] <= 0 || k[j] <= 0 || k[j] % 32) return 0;
+    a.job[j].N = n[j];
+    a.job[j].K = k[j];
+  }
+  return af::gemv_chain_scratch_bytes(a);
+}
 int af_gemv_tc_grid(int n, int k, int nb, int epi, int wf, int* grid, int* csize) {
   if (!grid || !csize || n <= 0 || k <= 0 || nb < 1 || (wf != af::W_I8 && wf != af::W_I4G32) || epi < 0 ||
       epi > af::EPI_SWIGLU)

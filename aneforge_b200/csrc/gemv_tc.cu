@@ -79,13 +79,6 @@ AF_DEV void epilogue(const GemvTcArgs& a, float (&acc)[NT][4], int rt, int g, in
   }
 }
 
-// consumer warps per CTA: one per row tile (int8), or two splitting the k tiles (int4, whose
-// conversion costs more instructions per byte)
-template <bool I4> struct Cw { static constexpr int n = I4 ? 8 : 4; };
-
-template <int CW>
-AF_DEV void consumer_sync_n() { asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory"); }
-
 template <int NT, int EPI, bool I4>
 __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArgs a) {
   constexpr int CW = Cw<I4>::n;

@@ -454,6 +454,54 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     // prompt-sized row counts (prefill) run as a tensor-core GEMM unless the op asks for the GEMV
     const bool gemm = want_gemm && nexp == 1;
     if (!dry) e = gemm ? gemm_tc_launch(a, st, pdl) : gemv_tc_launch(a, st, pdl);
+  } else if (op.kind == "gemv_chain") {
+    // jobs=n nb= wf=i8t|i4t scr= and per job j: j<j>.{w,s,b,x,ldx,y,ldy,n,k,epi} plus an optional
+    // norm run after the job: j<j>.{nx,ldnx,ng,nf,nout,ldno,nd}
+    GemvChainArgs a;
+    const std::string* wfs = c.raw("wf");
+    if (!wfs || (*wfs != "i8t" && *wfs != "i4t")) { why = "gemv_chain: wf must be i8t or i4t"; return cudaErrorInvalidValue; }
+    const bool i4 = *wfs == "i4t";
+    a.wf = i4 ? W_I4G32 : W_I8;
+    a.NB = (int)c.i("nb");
+    a.njobs = (int)c.i("jobs");
+    if (a.njobs < 1 || a.njobs > CHAIN_MAX_JOBS || a.NB < 1 || a.NB > 16) { why = "gemv_chain: bad jobs / nb"; return cudaErrorInvalidValue; }
+    for (int j = 0; j < a.njobs && c.err.empty(); ++j) {
+      ChainJob& J = a.job[j];
+      const std::string p = "j" + std::to_string(j) + ".";
+      auto K = [&](const char* s) { return p + s; };
+      J.N = (int)c.i(K("n").c_str());
+      J.K = (int)c.i(K("k").c_str());
+      const std::string* es = c.raw(K("epi").c_str());
+      if (!es) break;
+      J.epi = epi_of(*es);
+      if (J.epi < 0 || J.epi == EPI_ARGMAX) { c.err = "gemv_chain: bad epi"; break; }
+      J.ldx = (int)c.i(K("ldx").c_str(), J.K);
+      const int out_cols = J.epi == EPI_SWIGLU ? J.N / 2 : J.N;
+      J.ldy = (int)c.i(K("ldy").c_str(), out_cols);
+      J.x = (const __half*)c.ptr(K("x").c_str(), 2 * ((size_t)(a.NB - 1) * J.ldx + J.K));
+      J.w = c.ptr(K("w").c_str(), i4 ? pack_i4_tiles_bytes(J.N, J.K) : pack_i8_tiles_bytes(J.N, J.K));
+      if (!i4) J.scale = (const __half*)c.ptr(K("s").c_str(), 2 * (size_t)J.N);
+      J.bias = (const __half*)c.ptr(K("b").c_str(), 2 * (size_t)J.N, true);
+      const size_t esz = (J.epi == EPI_F16 || J.epi == EPI_SWIGLU) ? 2 : 4;
+      J.y = c.ptr(K("y").c_str(), esz * ((size_t)(a.NB - 1) * J.ldy + out_cols));
+      if (c.has(K("nx").c_str())) {
+        J.nd = (int)c.i(K("nd").c_str());
+        J.ldnx = (int)c.i(K("ldnx").c_str(), J.nd);
+        J.ldno = (int)c.i(K("ldno").c_str(), J.nd);
+        J.nx = (const float*)c.ptr(K("nx").c_str(), 4 * ((size_t)(a.NB - 1) * J.ldnx + J.nd));
+        J.ng = (const __half*)c.ptr(K("ng").c_str(), 2 * (size_t)J.nd);
+        J.nfloor = (float)c.f(K("nf").c_str());
+        J.nout = (__half*)c.ptr(K("nout").c_str(), 2 * ((size_t)(a.NB - 1) * J.ldno + J.nd));
+      }
+    }
+    if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+    a.scratch_bytes = gemv_chain_scratch_bytes(a);
+    a.scratch = c.ptr("scr", a.scratch_bytes);
+    a.err = p.d_err;
+    static const int evict_first = env_int("AF_L2_EVICT_FIRST", 0);
+    a.evict_first = (int)c.i("ef", evict_first);
+    if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+    if (!dry) e = gemv_chain_launch(a, st, pdl);
   } else if (op.kind == "gemv") {
     GemvArgs a;
     const std::string* wfs = c.raw("wf");

@@ -88,6 +88,13 @@ AF_DEV void bulk_w(void* dst, const void* src, uint32_t bytes, uint64_t* bar, bo
 
 AF_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(tc::CWARPS * 32) : "memory"); }
 
+// consumer warps per CTA: one per row tile (int8), or two splitting the k tiles (int4, whose
+// conversion costs more instructions per byte)
+template <bool I4> struct Cw { static constexpr int n = I4 ? 8 : 4; };
+
+template <int CW>
+AF_DEV void consumer_sync_n() { asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory"); }
+
 AF_DEV void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "

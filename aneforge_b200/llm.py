@@ -253,6 +253,75 @@ def decode_nsplit(M, KV, NB=1):
   return int(os.environ.get("AF_ATTN_NSPLIT", nsplit))
 
 
+def plan_gemv_chains(pb, enable=None):
+  """Fuse runs of consecutive tensor-core GEMVs - each optionally followed by an RMSNorm - into
+  `gemv_chain` ops: one persistent launch per run whose CTAs stream every job's weights back to
+  back (csrc/gemv_chain.cu). In a decode step the runs are o -> norm -> gate|up -> down -> norm ->
+  next qkv, broken by each attention. Same results as the separate launches up to the fp32
+  summation order of split row blocks. Env AF_GEMV_CHAIN=0 keeps the separate launches."""
+  import ctypes
+  if enable is None:
+    enable = os.environ.get("AF_GEMV_CHAIN", "1") != "0"
+  if not enable:
+    return
+  lib = R.load_library()
+
+  def chainable(kind, kv):
+    return (kind == "gemv" and kv.get("wf") in ("i8t", "i4t") and kv.get("epi") in ("f32", "f16", "resid", "swiglu")
+            and kv.get("experts", "-") == "-" and not kv.get("gemm") and kv.get("rw", "-") == "-"
+            and kv.get("sel", "-") == "-" and int(kv["nb"]) <= 16 and "pf" not in kv)
+
+  def norm_tail(kind, kv):
+    return kind == "rmsnorm" and not int(kv.get("xf16", 0)) and "pf" not in kv
+
+  out, run = [], []
+  keys = {"w": "w", "s": "s", "bias": "b", "x": "x", "ldx": "ldx", "y": "y", "ldy": "ldy", "n": "n", "k": "k",
+          "epi": "epi"}
+
+  def flush():
+    for s in range(0, len(run), 8):
+      emit(run[s:s + 8])
+    run.clear()
+
+  def emit(jobs):
+    if len(jobs) < 2:
+      for g, n in jobs:                                  # a lone GEMV stays a plain launch
+        out.append(("gemv", g))
+        if n is not None:
+          out.append(("rmsnorm", n))
+      return
+    nb, wf = int(jobs[0][0]["nb"]), jobs[0][0]["wf"]
+    Ns = (ctypes.c_int * len(jobs))(*[int(g["n"]) for g, _ in jobs])
+    Ks = (ctypes.c_int * len(jobs))(*[int(g["k"]) for g, _ in jobs])
+    nbytes = lib.af_gemv_chain_scratch_bytes(len(jobs), Ns, Ks, nb, 2 if wf == "i4t" else 0)
+    if not nbytes:
+      raise RuntimeError("gemv_chain: no scratch size for these shapes")
+    kv = dict(jobs=len(jobs), nb=nb, wf=wf, scr=pb.buf("chain.scr", nbytes, "scratch"))
+    for j, (g, n) in enumerate(jobs):
+      p = f"j{j}."
+      kv.update({p + ck: g[gk] for gk, ck in keys.items() if g.get(gk, "-") != "-"})
+      if n is not None:
+        kv.update({p + "nx": n["x"], p + "ng": n["g"], p + "nf": n["floor"], p + "nout": n["out"], p + "nd": n["d"]})
+        if "ldx" in n:
+          kv[p + "ldnx"] = n["ldx"]
+        if "ldo" in n:
+          kv[p + "ldno"] = n["ldo"]
+    out.append(("gemv_chain", kv))
+
+  for kind, kv in pb.ops:
+    if chainable(kind, kv):
+      if run and (run[0][0]["wf"] != kv["wf"] or int(run[0][0]["nb"]) != int(kv["nb"])):
+        flush()
+      run.append((kv, None))
+    elif norm_tail(kind, kv) and run and run[-1][1] is None and int(kv["nb"]) == int(run[0][0]["nb"]):
+      run[-1] = (run[-1][0], kv)
+    else:
+      flush()
+      out.append((kind, kv))
+  flush()
+  pb.ops[:] = out
+
+
 def plan_l2_prefetch(pb, budget=None, mode=None):
   """Attach L2 prefetch keys to a decode plan: each tensor-core GEMV's weights are (partly) fetched
   into L2 by the kernel that runs before it - the previous GEMV once its own weight copies are all
@@ -569,6 +638,7 @@ class LlamaPrefill:
             ami="am.idx", amc="am.cnt", tok=at("tp.cand", 4 * NB), val="tp.cand", ibase=self.shard.vocab[0])
       pb.op("allgather", src="tp.cand", dst="tp.gath", n=2 * NB, ranks=self.tp.world)
       pb.op("tp_argmax", src="tp.gath", ranks=self.tp.world, nb=NB, tok="tok_out", pos="pos", hist="hist", histld=M)
+    plan_gemv_chains(pb)
     plan_l2_prefetch(pb)
     ins = {"tok": (NB,), "pos": (NB,)}
     for li in range(cfg.n_layers):
@@ -1030,7 +1100,7 @@ _HF_LAYER_OPTIONAL = {
 }
 # architectures whose semantics the dense loader does not implement (logit soft-capping, GELU MLPs,
 # LayerNorm, sandwich norms): refused rather than silently run as Llama
-_HF_REFUSED = {"gemma", "gemma2", "gemma3", "gemma3_text", "gpt2"}
+_HF_REFUSED = {"gemma2", "gemma3", "gemma3_text", "gpt2"}
 
 
 def hf_weights(sd: dict, n_layers: int) -> dict:
@@ -1083,7 +1153,24 @@ def _mistral_adapter(c, sd):
   return cfg, w
 
 
+def _gemma_adapter(c, sd):
+  """Gemma (reference `aneforge/llm.py:685-702`): Llama-shaped attention, the GeGLU MLP (tanh GELU,
+  the "geglu" graph builder) and two conventions baked into the weights - the input embedding is
+  scaled by sqrt(hidden) (the head keeps the unscaled, tied rows) and the RMSNorm weights are
+  stored as w with the model applying (1 + w)."""
+  cfg, w = _dense_adapter(c, sd)
+  cfg.rope_scaling = None
+  cfg.layers = [LayerSpec(mixer="attention", mlp="geglu") for _ in range(cfg.n_layers)]
+  w["embed"] = np.asarray(w["embed"]) * np.sqrt(c.hidden_size)      # float64: rounded once, at the port
+  for lw in w["layers"]:
+    lw["attn_norm"] = lw["attn_norm"] + 1.0
+    lw["mlp_norm"] = lw["mlp_norm"] + 1.0
+  w["final_norm"] = w["final_norm"] + 1.0
+  return cfg, w
+
+
 ADAPTERS: list = [
+  (lambda c: getattr(c, "model_type", None) == ModelType.GEMMA, _gemma_adapter),
   (lambda c: getattr(c, "model_type", None) == ModelType.MISTRAL, _mistral_adapter),
 ]
 
@@ -1110,6 +1197,8 @@ def from_pretrained(name: str, compress: str | None = None, ane_lm_head: bool = 
   if adapt is None:
     _assert_dense_compatible(hf.config)
     adapt = _dense_adapter
-  sd = {k: v.detach().to(torch.float16) for k, v in hf.state_dict().items()}
+  # fp16 numpy state dict: the weights are baked to fp16 (or quantized) anyway, and the adapters'
+  # weight arithmetic (Gemma's scaled embedding and 1 + w norms) follows numpy's fp16 rules
+  sd = {k: v.detach().to(torch.float16).numpy() for k, v in hf.state_dict().items()}
   cfg, weights = adapt(hf.config, sd)
   return LlamaPrefill(cfg, weights, compress=compress, ane_lm_head=ane_lm_head, device=device)

@@ -109,6 +109,43 @@ def emit_moe(pb, ctx, li, lw, cfg, ls):
   pb.op("allreduce", src="tp.part", dst="tp.part", n=n, addto="h")
 
 
+def hf_moe_adapter(c, sd):
+  """Qwen3-MoE Hugging Face checkpoints (reference `aneforge/moe.py:70-107`): attention as in the
+  dense adapter; a sparse layer's router is `mlp.gate`, its experts the fused
+  `mlp.experts.gate_up_proj` [E, 2 ffn, dim] (gate rows first) and `mlp.experts.down_proj`
+  [E, dim, ffn], re-laid as the MoE layer's [E, ffn, dim] matrices. `decoder_sparse_step` and
+  `mlp_only_layers` choose which layers are sparse; the others are SwiGLU layers."""
+  import numpy as np
+  cfg = llm.hf_config(c, sd)
+  n = cfg.n_layers
+  step = int(getattr(c, "decoder_sparse_step", 1) or 1)
+  dense_only = set(getattr(c, "mlp_only_layers", None) or [])
+  sparse = [li not in dense_only and (li + 1) % step == 0 for li in range(n)]
+  qk = cfg.layers[0].qk_norm if cfg.layers else False
+  cfg.layers = [llm.LayerSpec(mixer="attention", mlp="moe" if s else "swiglu", qk_norm=qk) for s in sparse]
+  cfg.extra.update(n_experts=int(c.num_experts), n_experts_per_tok=int(c.num_experts_per_tok),
+                   norm_topk_prob=bool(getattr(c, "norm_topk_prob", True)))
+  embed = sd["model.embed_tokens.weight"]
+  w = {"embed": embed, "final_norm": sd["model.norm.weight"], "lm_head": sd.get("lm_head.weight", embed), "layers": []}
+  for li in range(n):
+    pre = f"model.layers.{li}."
+    lw = {ours: sd[pre + theirs] for ours, theirs in llm._HF_LAYER_REQUIRED.items()
+          if not (sparse[li] and theirs.startswith("mlp."))}
+    lw.update({ours: sd[pre + theirs] for ours, theirs in llm._HF_LAYER_OPTIONAL.items() if pre + theirs in sd})
+    if sparse[li]:
+      gu = np.asarray(sd[pre + "mlp.experts.gate_up_proj"])
+      F = gu.shape[1] // 2
+      lw["router"] = sd[pre + "mlp.gate.weight"]
+      lw["wgate_exps"] = np.ascontiguousarray(gu[:, :F])
+      lw["wup_exps"] = np.ascontiguousarray(gu[:, F:])
+      lw["wdown_exps"] = np.ascontiguousarray(np.asarray(sd[pre + "mlp.experts.down_proj"]).transpose(0, 2, 1))
+    w["layers"].append(lw)
+  return cfg, w
+
+
+llm.ADAPTERS.append((lambda c: bool(getattr(c, "num_experts", 0)), hf_moe_adapter))
+
+
 def load_gguf(path: str, n_layers: int | None = None, compress: str | None = None, **runner_kw) -> "llm.LlamaPrefill":
   """A Qwen-MoE GGUF checkpoint as a runner (reference `aneforge/moe.py:129-173`): Qwen3-MoE
   (QK-norm) or Qwen2-MoE / Qwen1.5-MoE (QKV biases, the sigmoid-gated shared expert, no top-k

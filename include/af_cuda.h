@@ -153,6 +153,10 @@ int af_gemv(int wf, int epi, const uint16_t* x, int ldx, const void* w, const ui
 size_t af_pack_i8_tiles_bytes(int n, int k);
 int af_pack_i8_tiles(const int8_t* codes, int n, int k, uint8_t* tiles, void* stream);
 size_t af_gemv_tc_scratch_bytes(int n, int k, int nb);
+/* Scratch of a plan's `gemv_chain` op (no counterpart in the reference: several tensor-core GEMVs,
+ * each with an optional RMSNorm after it, in one persistent launch) for njobs jobs of shapes
+ * n[j] x k[j] at batch nb; wf 0 int8 tiles, 2 group-32 int4 tiles. 0 on bad arguments. */
+size_t af_gemv_chain_scratch_bytes(int njobs, const int* n, const int* k, int nb, int wf);
 /* Grid of the tensor-core GEMV for one shape on the current device (no counterpart in the
  * reference): CTAs per 16-row slice (*grid) and the thread-block cluster size splitting each
  * 64-row block (*csize; 0: stream-K). The CTAs' k ranges cover the packed weights in grid equal,

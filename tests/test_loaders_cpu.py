@@ -15,6 +15,7 @@ def _tiny(kind, tmp_path, **extra):
   torch.manual_seed(0)
   common = dict(hidden_size=64, intermediate_size=128, num_hidden_layers=2, num_attention_heads=4,
                 num_key_value_heads=2, vocab_size=97, max_position_embeddings=256, rms_norm_eps=1e-6)
+  hd = extra.pop("head_dim", 16)
   common.update(extra)
   if kind == "llama":
     cfg = transformers.LlamaConfig(**common)
@@ -23,11 +24,18 @@ def _tiny(kind, tmp_path, **extra):
     cfg = transformers.Qwen2Config(**common)
     model = transformers.Qwen2ForCausalLM(cfg)
   elif kind == "qwen3":
-    cfg = transformers.Qwen3Config(head_dim=16, **common)
+    cfg = transformers.Qwen3Config(head_dim=hd, **common)
     model = transformers.Qwen3ForCausalLM(cfg)
   elif kind == "mistral":
     cfg = transformers.MistralConfig(sliding_window=64, **common)
     model = transformers.MistralForCausalLM(cfg)
+  elif kind == "gemma":
+    cfg = transformers.GemmaConfig(head_dim=hd, hidden_act="gelu_pytorch_tanh", **common)
+    model = transformers.GemmaForCausalLM(cfg)
+  elif kind == "qwen3_moe":
+    cfg = transformers.Qwen3MoeConfig(head_dim=hd, moe_intermediate_size=32, num_experts=4, num_experts_per_tok=2,
+                                      mlp_only_layers=[1], norm_topk_prob=False, **common)
+    model = transformers.Qwen3MoeForCausalLM(cfg)
   else:
     raise ValueError(kind)
   d = tmp_path / kind
@@ -47,12 +55,12 @@ def test_from_pretrained_maps_checkpoint(kind, tmp_path):
   assert cfg.norm_eps == pytest.approx(c.rms_norm_eps)
   sd = model.state_dict()
   w = m.w
-  np.testing.assert_array_equal(np.asarray(w["embed"].float()), sd["model.embed_tokens.weight"].half().float().numpy())
+  np.testing.assert_array_equal(np.asarray(w["embed"], np.float32), sd["model.embed_tokens.weight"].half().float().numpy())
   for i in range(cfg.n_layers):
     lw = w["layers"][i]
     pre = f"model.layers.{i}."
-    np.testing.assert_array_equal(np.asarray(lw["wq"].float()), sd[pre + "self_attn.q_proj.weight"].half().float().numpy())
-    np.testing.assert_array_equal(np.asarray(lw["wdown"].float()), sd[pre + "mlp.down_proj.weight"].half().float().numpy())
+    np.testing.assert_array_equal(np.asarray(lw["wq"], np.float32), sd[pre + "self_attn.q_proj.weight"].half().float().numpy())
+    np.testing.assert_array_equal(np.asarray(lw["wdown"], np.float32), sd[pre + "mlp.down_proj.weight"].half().float().numpy())
     assert ("q_bias" in lw) == (kind == "qwen2")
     assert ("q_norm" in lw) == (kind == "qwen3")
     assert cfg.layers[i].qk_norm == (kind == "qwen3")
@@ -62,7 +70,52 @@ def test_from_pretrained_maps_checkpoint(kind, tmp_path):
     assert cfg.extra["sliding_window"] == 64 and cfg.rope_scaling is None
   if kind == "llama":
     # untied head: its own rows
-    np.testing.assert_array_equal(np.asarray(w["lm_head"].float()), sd["lm_head.weight"].half().float().numpy())
+    np.testing.assert_array_equal(np.asarray(w["lm_head"], np.float32), sd["lm_head.weight"].half().float().numpy())
+
+
+def _oracle_cfg(cfg):
+  from oracle.model import Config
+  return Config(dim=cfg.dim, n_layers=cfg.n_layers, n_heads=cfg.n_heads, n_kv_heads=cfg.n_kv_heads,
+                ffn_dim=cfg.ffn_dim, vocab=cfg.vocab, rope_base=cfg.rope_base, norm_eps=cfg.norm_eps,
+                head_dim=cfg.head_dim, rope_scaling=cfg.rope_scaling, extra=dict(cfg.extra),
+                qk_norm=cfg.layers[0].qk_norm, mlp="geglu" if cfg.layers[0].mlp == "geglu" else "swiglu")
+
+
+def _hf_last_logits(model, prompt):
+  with torch.no_grad():
+    return model(torch.tensor([prompt])).logits[0, -1].float().numpy()
+
+
+@pytest.mark.parametrize("kind", ["gemma", "qwen3_moe"])
+def test_adapter_runs_like_transformers(kind, tmp_path):
+  """Gemma (GeGLU, sqrt(hidden)-scaled embedding, 1 + w norms) and Qwen3-MoE (fused expert tensors,
+  dense layers from `mlp_only_layers`, QK-norm, no top-k renormalisation): the adapted weights run
+  through the oracle give the checkpoint's own next-token logits (transformers on the CPU)."""
+  from aneforge_b200 import llm
+  d, model = _tiny(kind, tmp_path)
+  m = llm.from_pretrained(str(d))
+  cfg, w = m.cfg, m.w
+  if kind == "gemma":
+    assert [ls.mlp for ls in cfg.layers] == ["geglu", "geglu"]
+    sd = model.state_dict()
+    e = sd["model.embed_tokens.weight"].half().numpy()
+    np.testing.assert_array_equal(np.asarray(w["lm_head"]), e)                  # tied, unscaled
+    np.testing.assert_allclose(w["embed"], e.astype(np.float64) * np.sqrt(64))
+    np.testing.assert_array_equal(w["layers"][0]["attn_norm"],
+                                  sd["model.layers.0.input_layernorm.weight"].half().numpy() + np.float16(1))
+  else:
+    assert [ls.mlp for ls in cfg.layers] == ["moe", "swiglu"]
+    assert cfg.extra == {"n_experts": 4, "n_experts_per_tok": 2, "norm_topk_prob": False}
+    assert w["layers"][0]["wgate_exps"].shape == (4, 32, 64) and w["layers"][0]["wdown_exps"].shape == (4, 32, 64)
+    assert "wgate" in w["layers"][1] and "router" not in w["layers"][1]
+  om = OracleModel(_oracle_cfg(cfg), w, None, precision="fp32")
+  prompt = [3, 17, 42, 5, 88, 1, 60]
+  hid, _ = om.prefill_hidden(prompt)
+  got = om.logits(hid[-1].astype(np.float32))
+  ref = _hf_last_logits(model.float(), prompt)
+  cos = float(got @ ref / (np.linalg.norm(got) * np.linalg.norm(ref)))
+  assert cos > 0.999, cos
+  assert np.abs(got - ref).max() < 0.02 * np.abs(ref).max()
 
 
 def test_llama3_rope_scaling_read_from_checkpoint(tmp_path):
@@ -83,7 +136,7 @@ def test_dense_loader_refuses_unsupported_architectures():
   from aneforge_b200 import llm
 
   class C:
-    model_type = "gemma2"
+    model_type = "gpt2"
   with pytest.raises(ValueError):
     llm._assert_dense_compatible(C())
 
