@@ -166,8 +166,9 @@ class Lowering:
       pb.op("g_rms", x=self.value(t.srcs[0]), y=y, g=self._weight(f"{nm}.g", g), floor=floor, rows=n // D, d=D)
     elif op == "layer_norm":
       D = t.shape[-1]
-      kv = dict(x=self.value(t.srcs[0]), y=y, g=self._weight(f"{nm}.g", a["gamma"].astype(F16)), eps=a["eps"],
-                rows=n // D, d=D)
+      # eps rounded to fp16, as the reference's emitter bakes it (`_compile.py:762`)
+      kv = dict(x=self.value(t.srcs[0]), y=y, g=self._weight(f"{nm}.g", a["gamma"].astype(F16)),
+                eps=float(np.float16(a["eps"])), rows=n // D, d=D)
       if a.get("beta") is not None:
         kv["b"] = self._weight(f"{nm}.b", a["beta"].astype(F16))
       pb.op("g_ln", **kv)

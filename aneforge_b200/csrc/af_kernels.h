@@ -162,6 +162,10 @@ cudaError_t rmsnorm_launch(const void* x, int x_f16, int ldx, const __half* g, f
                            const L2Pf& pf = L2Pf());
 
 // h[b][:] = f32(table[tok[b]][:]); records AF_DEV_BAD_TOKEN and writes zeros on an out-of-range id.
+cudaError_t layernorm_launch(const float* x, int ldx, const __half* g, const __half* b, float eps, __half* out, int ldo,
+                             int NB, int D, cudaStream_t st, bool pdl);
+cudaError_t add_pos_launch(float* h, int ldh, const __half* table, int npos, const int* pos, int NB, int D, int* err,
+                           cudaStream_t st, bool pdl);
 cudaError_t embed_launch(const int* tok, const __half* table, int vocab, float* h, int ldh, int NB, int D,
                          int* err, cudaStream_t st, bool pdl);
 

@@ -174,6 +174,75 @@ cudaError_t rmsnorm_launch(const void* x, int x_f16, int ldx, const __half* g, f
   return cudaLaunchKernelEx(&cfg, rmsnorm_scalar_kernel<false>, x, ldx, g, floor, out, ldo, D);
 }
 
+// Block-wide sum (blockDim a multiple of 32, at most 1024); `red` holds 32 floats.
+static __device__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  __syncthreads();                          // red is reused by the next call
+  return t;
+}
+
+// LayerNorm of fp32 rows into fp16 (reference `_e_layer_norm`, `aneforge/_compile.py:758-776`):
+// xc = x - mean(x); out = xc * (1 / sqrt(mean(xc^2) + eps)) * g + b, each step rounded in fp32.
+__global__ void __launch_bounds__(256) layernorm_kernel(const float* x, int ldx, const __half* g, const __half* bta,
+                                                        float eps, __half* out, int ldo, int D) {
+  __shared__ float red[32];
+  const float* xr = x + (size_t)blockIdx.x * ldx;
+  pdl_wait();
+  float s = 0.f;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) s += __ldcg(xr + i);
+  const float mu = __fdiv_rn(block_sum(s, red), (float)D);
+  float v = 0.f;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    const float c = __fsub_rn(__ldcg(xr + i), mu);
+    v = fmaf(c, c, v);
+  }
+  const float var = __fdiv_rn(block_sum(v, red), (float)D);
+  const float rr = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, eps)));
+  pdl_trigger();
+  __half* o = out + (size_t)blockIdx.x * ldo;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    const float xn = __fmul_rn(__fsub_rn(__ldcg(xr + i), mu), rr);
+    o[i] = f2h(__fadd_rn(__fmul_rn(xn, h2f(g[i])), bta ? h2f(bta[i]) : 0.f));
+  }
+}
+
+cudaError_t layernorm_launch(const float* x, int ldx, const __half* g, const __half* b, float eps, __half* out, int ldo,
+                             int NB, int D, cudaStream_t st, bool pdl) {
+  if (NB < 1 || D < 1) return cudaErrorInvalidValue;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = mkcfg(dim3(NB), dim3(256), 0, st, pdl, attr);
+  return cudaLaunchKernelEx(&cfg, layernorm_kernel, x, ldx, g, b, eps, out, ldo, D);
+}
+
+// Learned positional embedding (GPT-2's wpe): h[b] += table[p] with p = pos[b] (decode) or b (the
+// rows of a prompt), a position outside the table recorded as AF_DEV_BAD_POS.
+__global__ void __launch_bounds__(256) add_pos_kernel(float* h, int ldh, const __half* table, int npos, const int* pos,
+                                                      int D, int* err) {
+  const int b = blockIdx.x;
+  pdl_wait();
+  const int p = pos ? __ldcg(pos + b) : b;
+  if (p < 0 || p >= npos) {
+    if (threadIdx.x == 0) af_set_err(err, AF_DEV_BAD_POS);
+    return;
+  }
+  pdl_trigger();
+  float* hr = h + (size_t)b * ldh;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) hr[i] = __fadd_rn(hr[i], h2f(table[(size_t)p * D + i]));
+}
+
+cudaError_t add_pos_launch(float* h, int ldh, const __half* table, int npos, const int* pos, int NB, int D, int* err,
+                           cudaStream_t st, bool pdl) {
+  if (NB < 1 || D < 1) return cudaErrorInvalidValue;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = mkcfg(dim3(NB), dim3(256), 0, st, pdl, attr);
+  return cudaLaunchKernelEx(&cfg, add_pos_kernel, h, ldh, table, npos, pos, D, err);
+}
+
 cudaError_t embed_launch(const int* tok, const __half* table, int vocab, float* h, int ldh, int NB, int D, int* err,
                          cudaStream_t st, bool pdl) {
   cudaLaunchAttribute attr[1];

@@ -397,6 +397,24 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     float* h = (float*)c.ptr("h", 4 * ((size_t)(nb - 1) * ldh + d));
     if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
     if (!dry) e = embed_launch(tok, table, vocab, h, ldh, nb, d, p.d_err, st, pdl);
+  } else if (op.kind == "layernorm") {
+    const int nb = c.i("nb"), d = c.i("d");
+    const int ldx = c.i("ldx", d), ldo = c.i("ldo", d);
+    const float* x = (const float*)c.ptr("x", 4 * ((size_t)(nb - 1) * ldx + d));
+    const __half* g = (const __half*)c.ptr("g", 2 * (size_t)d);
+    const __half* b = (const __half*)c.ptr("b", 2 * (size_t)d, true);
+    __half* out = (__half*)c.ptr("out", 2 * ((size_t)(nb - 1) * ldo + d));
+    const float eps = (float)c.f("eps");
+    if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+    if (!dry) e = layernorm_launch(x, ldx, g, b, eps, out, ldo, nb, d, st, pdl);
+  } else if (op.kind == "add_pos") {
+    const int nb = c.i("nb"), d = c.i("d"), npos = c.i("npos");
+    const int ldh = c.i("ldh", d);
+    float* h = (float*)c.ptr("h", 4 * ((size_t)(nb - 1) * ldh + d));
+    const __half* table = (const __half*)c.ptr("table", 2 * (size_t)npos * d);
+    const int* pos = (const int*)c.ptr("pos", 4 * (size_t)nb, true);
+    if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+    if (!dry) e = add_pos_launch(h, ldh, table, npos, pos, nb, d, p.d_err, st, pdl);
   } else if (op.kind == "rmsnorm") {
     const int nb = c.i("nb"), d = c.i("d"), xf16 = c.i("xf16", 0);
     const int ldx = c.i("ldx", d), ldo = c.i("ldo", d);

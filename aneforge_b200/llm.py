@@ -177,12 +177,40 @@ def _emit_row_parallel(pb, ctx, name, lin: DevLinear, x):
     _emit_linear(pb, ctx, name, lin, x, "h", "resid")
 
 
+def _emit_attn_norm(pb, cfg, pre, lw, nb):
+  """The attention input norm of `nb` residual rows into `xn`: RMSNorm, or LayerNorm (GPT-2,
+  `cfg.norm_type == "layer"`, eps rounded to fp16 as the reference bakes it)."""
+  if cfg.norm_type == "layer":
+    pb.op("layernorm", x="h", g=f"{pre}.attn_lw", b=f"{pre}.attn_lb", eps=float(np.float16(cfg.norm_eps)), out="xn",
+          nb=nb, d=cfg.dim)
+  else:
+    pb.op("rmsnorm", x="h", g=f"{pre}.attn_g", out="xn", nb=nb, d=cfg.dim, floor=lw["attn_floor"])
+
+
+def _emit_final_norm(pb, cfg, d, nb):
+  if cfg.norm_type == "layer":
+    pb.op("layernorm", x="h", g="final_g", b="final_b", eps=float(np.float16(cfg.norm_eps)), out="hid", nb=nb,
+          d=cfg.dim)
+  else:
+    pb.op("rmsnorm", x="h", g="final_g", out="hid", nb=nb, d=cfg.dim, floor=d["final_floor"])
+
+
+def _emit_embedding(pb, cfg, d, nb, pos):
+  """Embedding rows into the fp32 residual, plus GPT-2's learned position rows (`wpe`) at `pos`
+  (a per-row position buffer) or at the row index (a prompt)."""
+  pb.op("embed", tok="tok" if pos else "ids", table="embed", h="h", vocab=cfg.vocab, d=cfg.dim, nb=nb)
+  if "wpe" in d:
+    P = int(d["wpe"].shape[0])
+    pb.buf("wpe", 2 * P * cfg.dim, "weight")
+    pb.op("add_pos", h="h", table="wpe", npos=P, pos=pos, nb=nb, d=cfg.dim)
+
+
 def emit_attention_decode(pb, ctx, li, lw, cfg, ls):
   """`_attn_decode` (reference `llm.py:214-237`): norm -> fused QKV GEMV -> RoPE + cache write at
   pos + GQA split-K attention -> o_proj GEMV with the residual add fused."""
   D, H, KV, dh, NB, M = cfg.dim, cfg.n_heads, cfg.n_kv_heads, cfg.dh, ctx["NB"], ctx["M"]
   pre = f"L{li}"
-  pb.op("rmsnorm", x="h", g=f"{pre}.attn_g", out="xn", nb=NB, d=D, floor=lw["attn_floor"])
+  _emit_attn_norm(pb, cfg, pre, lw, NB)
   _emit_linear(pb, ctx, f"{pre}.qkv", lw["qkv"], "xn", "qkv", "f32")
   # prefetch=1: the step's position is only advanced by its last kernel (the head), so attention may
   # stage its first cache rows before the qkv projection finishes
@@ -208,7 +236,7 @@ def emit_attention_prefill(pb, ctx, li, lw, cfg, ls):
   """`_attn_prefill_kv` (reference `llm.py:149-169`): K (roped) and V land in cache layout."""
   D, H, KV, dh, S = cfg.dim, cfg.n_heads, cfg.n_kv_heads, cfg.dh, ctx["NB"]
   pre = f"L{li}"
-  pb.op("rmsnorm", x="h", g=f"{pre}.attn_g", out="xn", nb=S, d=D, floor=lw["attn_floor"])
+  _emit_attn_norm(pb, cfg, pre, lw, S)
   _emit_linear(pb, ctx, f"{pre}.qkv", lw["qkv"], "xn", "qkv", "f32")
   kv = dict(qkv="qkv", kc=f"{pre}.K", vc=f"{pre}.V", out="att", qbuf="qbuf", s=S, h=H, kv=KV, dh=dh, ldm=S,
             scale=ctx["scale"], kvc=ctx["kvc"], expand=int(ctx["expand"]))
@@ -455,7 +483,11 @@ class LlamaPrefill:
                                  biases=[lw.get("q_bias"), lw.get("k_bias"), lw.get("v_bias")], atol=atol,
                                  block_size=bs)
         d["o"] = encode_linear([lw["wo"]], c, dev, biases=[lw.get("o_bias")], atol=atol, block_size=bs)
-        d["attn_g"], d["attn_floor"] = rms_weights(lw["attn_norm"], cfg.norm_eps, dev)
+        if cfg.norm_type == "layer":
+          d["attn_lw"] = to_device(lw["attn_norm_w"], dev, torch.float16)
+          d["attn_lb"] = to_device(lw["attn_norm_b"], dev, torch.float16)
+        else:
+          d["attn_g"], d["attn_floor"] = rms_weights(lw["attn_norm"], cfg.norm_eps, dev)
         if ls.qk_norm:
           d["qn"], d["qn_floor"] = rms_weights(lw["q_norm"], cfg.norm_eps, dev)
           d["kn"], d["kn_floor"] = rms_weights(lw["k_norm"], cfg.norm_eps, dev)
@@ -472,10 +504,17 @@ class LlamaPrefill:
       free = getattr(self.w["layers"], "free", None)
       if free is not None:
         free(i)                              # a lazily read checkpoint layer is on the device now
-    fg, ff = rms_weights(self.w["final_norm"], cfg.norm_eps, dev)
+    extra = {}
+    if cfg.norm_type == "layer":
+      fg, ff = to_device(self.w["final_norm_w"], dev, torch.float16), None
+      extra["final_b"] = to_device(self.w["final_norm_b"], dev, torch.float16)
+    else:
+      fg, ff = rms_weights(self.w["final_norm"], cfg.norm_eps, dev)
+    if self.w.get("wpe") is not None:
+      extra["wpe"] = to_device(self.w["wpe"], dev, torch.float16)       # learned positions (GPT-2)
     lm = self.w["lm_head"]
     self._head_exact = fp16_bits_exact(lm)
-    self._dev = {"layers": layers, "final_g": fg, "final_floor": ff,
+    self._dev = {"layers": layers, "final_g": fg, "final_floor": ff, **extra,
                  "embed": to_device(self.w["embed"], dev, torch.float16),
                  "lm_head": to_device(lm, dev, torch.float16),
                  "kvc": _blob.gqa_expand_factor(cfg.n_kv_heads, cfg.n_heads // cfg.n_kv_heads, c, atol, bs),
@@ -487,7 +526,17 @@ class LlamaPrefill:
     d = self._load()
     proj = sum(l[k].nbytes for l in d["layers"] for k in ("qkv", "o", "gu", "down") if k in l)
     return {"projections": proj, "lm_head": d["lm_head"].numel() * 2,
-            "norms": sum(l["attn_g"].numel() * 2 + l["mlp_g"].numel() * 2 for l in d["layers"])}
+            "norms": sum(l[k].numel() * 2 for l in d["layers"] for k in ("attn_g", "mlp_g", "attn_lw", "attn_lb")
+                         if k in l)}
+
+  def _bind_globals(self, prog):
+    """The final norm's weights and GPT-2's position table."""
+    d = self._load()
+    prog.bind("final_g", d["final_g"])
+    if "final_b" in d:
+      prog.bind("final_b", d["final_b"])
+    if "wpe" in d:
+      prog.bind("wpe", d["wpe"])
 
   def _bind_layer(self, prog, li, d, with_kv_state=True):
     if "experts" in d:
@@ -504,7 +553,7 @@ class LlamaPrefill:
         prog.bind(f"L{li}.{key}.s", lin.s)
       if lin.bias is not None:
         prog.bind(f"L{li}.{key}.b", lin.bias)
-    for key in ("attn_g", "mlp_g", "qn", "kn"):
+    for key in ("attn_g", "mlp_g", "qn", "kn", "attn_lw", "attn_lb"):
       if key in d:
         prog.bind(f"L{li}.{key}", d[key])
 
@@ -523,7 +572,7 @@ class LlamaPrefill:
         pb.buf(f"L{li}.{key}.s", lin.s.numel() * 2, "weight")
       if lin.bias is not None:
         pb.buf(f"L{li}.{key}.b", lin.bias.numel() * 2, "weight")
-    for key in ("attn_g", "mlp_g", "qn", "kn"):
+    for key in ("attn_g", "mlp_g", "qn", "kn", "attn_lw", "attn_lb"):
       if key in d:
         pb.buf(f"L{li}.{key}", d[key].numel() * 2, "weight")
 
@@ -570,7 +619,14 @@ class LlamaPrefill:
     self._ver = self._build_decoder(M, Kq, verify=True)
     return self._ver
 
+  def _check_positions(self, n):
+    """A learned position table bounds the sequence (reference `aneforge/llm.py:298-303`)."""
+    wpe = self.w.get("wpe")
+    if wpe is not None and n > np.shape(wpe)[0]:
+      raise ValueError(f"sequence length {n} exceeds this model's {np.shape(wpe)[0]} max positions")
+
   def _build_decoder(self, M, NB, verify):
+    self._check_positions(M)
     cfg, d = self.cfg, self._load()
     D, H, KV, dh, V = cfg.dim, cfg.n_heads, cfg.n_kv_heads, cfg.dh, cfg.vocab
     Q = (H + 2 * KV) * dh
@@ -588,6 +644,8 @@ class LlamaPrefill:
     pb.buf("act", 2 * NB * F, "tmp")
     VL = int(d["lm_head"].shape[0])                       # local vocabulary rows (all of them without TP)
     pb.buf("embed", 2 * V * D, "weight"); pb.buf("lm_head", 2 * VL * D, "weight"); pb.buf("final_g", 2 * D, "weight")
+    if cfg.norm_type == "layer":
+      pb.buf("final_b", 2 * D, "weight")
     if cfg.rope:
       pb.buf("rope.cos", 2 * M * dh, "weight"); pb.buf("rope.sin", 2 * M * dh, "weight")
     if self.tp is not None:
@@ -606,7 +664,7 @@ class LlamaPrefill:
     for li in range(cfg.n_layers):
       self._declare_layer_weights(pb, li, d["layers"][li])
       pb.buf(f"L{li}.K", 2 * CB * KV * M * dh, "state"); pb.buf(f"L{li}.V", 2 * CB * KV * M * dh, "state")
-    pb.op("embed", tok="tok", table="embed", h="h", vocab=V, d=D, nb=NB)
+    _emit_embedding(pb, cfg, d, NB, "pos")
     lows, gstates = [], []
     graph_mix = [is_graph_builder(DECODE_MIXERS[self._spec(i).mixer]) for i in range(cfg.n_layers)]
     graph_mlp = [is_graph_builder(DECODE_MLPS[self._spec(i).mlp]) for i in range(cfg.n_layers)]
@@ -628,7 +686,7 @@ class LlamaPrefill:
         self._lower_graph_mlp(pb, li, DECODE_MLPS[ls.mlp], NB, lows, "dec")
       else:
         DECODE_MLPS[ls.mlp](pb, ctx, li, d["layers"][li], cfg, ls)
-    pb.op("rmsnorm", x="h", g="final_g", out="hid", nb=NB, d=D, floor=d["final_floor"])
+    _emit_final_norm(pb, cfg, d, NB)
     if self.tp is None:
       pb.op("gemv", wf="f16", epi="argmax", x="hid", w="lm_head", y="logits", nb=NB, n=V, k=D, amv="am.val",
             ami="am.idx", amc="am.cnt", tok="tok_out", pos="pos", hist="hist", histld=M)
@@ -649,7 +707,8 @@ class LlamaPrefill:
     if self.tp is not None:
       prog.set_comm(self.tp.handle)
     prog.share_buffer(0, "tok_out", 0, "tok")              # device-resident token feedback
-    prog.bind("embed", d["embed"]); prog.bind("lm_head", d["lm_head"]); prog.bind("final_g", d["final_g"])
+    prog.bind("embed", d["embed"]); prog.bind("lm_head", d["lm_head"])
+    self._bind_globals(prog)
     if cfg.rope:
       cos_t, sin_t = rope_tables(M, dh, cfg.rope_base, cfg.rotary_dim, cfg.rope_interleaved, cfg.rope_scaling)
       prog.upload("rope.cos", cos_t); prog.upload("rope.sin", sin_t)
@@ -731,6 +790,7 @@ class LlamaPrefill:
     if self._pre is not None:
       self._pre["prog"].release()
       self._pre = None
+    self._check_positions(seq)
     cfg, d = self.cfg, self._load()
     D, H, KV, dh, V = cfg.dim, cfg.n_heads, cfg.n_kv_heads, cfg.dh, cfg.vocab
     Q = (H + 2 * KV) * dh
@@ -745,12 +805,14 @@ class LlamaPrefill:
     if self.tp is not None:
       pb.buf("tp.part", 4 * seq * D, "tmp")
     pb.buf("embed", 2 * V * D, "weight"); pb.buf("final_g", 2 * D, "weight")
+    if cfg.norm_type == "layer":
+      pb.buf("final_b", 2 * D, "weight")
     if cfg.rope:
       pb.buf("rope.cos", 2 * seq * dh, "weight"); pb.buf("rope.sin", 2 * seq * dh, "weight")
     for li in range(cfg.n_layers):
       self._declare_layer_weights(pb, li, d["layers"][li])
       pb.buf(f"L{li}.K", 2 * KV * seq * dh, "out"); pb.buf(f"L{li}.V", 2 * KV * seq * dh, "out")
-    pb.op("embed", tok="ids", table="embed", h="h", vocab=V, d=D, nb=seq)
+    _emit_embedding(pb, cfg, d, seq, None)
     lows = []
     for li in range(cfg.n_layers):
       ls = self._spec(li)
@@ -764,14 +826,15 @@ class LlamaPrefill:
         self._lower_graph_mlp(pb, li, mlp, seq, lows, "pre")
       else:
         mlp(pb, ctx, li, d["layers"][li], cfg, ls)
-    pb.op("rmsnorm", x="h", g="final_g", out="hid", nb=seq, d=D, floor=d["final_floor"])
+    _emit_final_norm(pb, cfg, d, seq)
     outs = {"hid": (seq, D)}
     for li in range(cfg.n_layers):
       outs[f"L{li}.K"] = (KV, seq, dh); outs[f"L{li}.V"] = (KV, seq, dh)
     prog = R.Program.from_text(pb.text(), {"ids": (seq,)}, outs, self.device, {"ids": "int32"})
     if self.tp is not None:
       prog.set_comm(self.tp.handle)
-    prog.bind("embed", d["embed"]); prog.bind("final_g", d["final_g"])
+    prog.bind("embed", d["embed"])
+    self._bind_globals(prog)
     if cfg.rope:
       cos_t, sin_t = rope_tables(seq, dh, cfg.rope_base, cfg.rotary_dim, cfg.rope_interleaved, cfg.rope_scaling)
       prog.upload("rope.cos", cos_t); prog.upload("rope.sin", sin_t)
@@ -1100,7 +1163,7 @@ _HF_LAYER_OPTIONAL = {
 }
 # architectures whose semantics the dense loader does not implement (logit soft-capping, GELU MLPs,
 # LayerNorm, sandwich norms): refused rather than silently run as Llama
-_HF_REFUSED = {"gemma2", "gemma3", "gemma3_text", "gpt2"}
+_HF_REFUSED = {"gemma2", "gemma3", "gemma3_text"}
 
 
 def hf_weights(sd: dict, n_layers: int) -> dict:
@@ -1169,7 +1232,41 @@ def _gemma_adapter(c, sd):
   return cfg, w
 
 
+def _gpt2_adapter(c, sd):
+  """GPT-2 (reference `aneforge/llm.py:730-767`): LayerNorm with bias, learned positions (`wpe`,
+  added to the embedding) instead of RoPE, biases on every projection, the tanh-GELU MLP
+  ("gelu_new", a graph builder) and the head tied to the token embedding. HF stores the
+  projections as Conv1D [in, out]; they are transposed to [out, in]. Checkpoints that rescale the
+  attention per layer or upcast it are refused (their logits would differ)."""
+  for flag in ("scale_attn_by_inverse_layer_idx", "reorder_and_upcast_attn"):
+    if getattr(c, flag, False):
+      raise ValueError(f"load_gpt2: {flag} is set, which this GPT-2 adapter does not implement")
+  g = lambda *names: next(getattr(c, n) for n in names if getattr(c, n, None) is not None)
+  n, D, H = int(g("n_layer", "num_hidden_layers")), int(g("n_embd", "hidden_size")), int(g("n_head", "num_attention_heads"))
+  F = int(getattr(c, "n_inner", None) or getattr(c, "intermediate_size", None) or 4 * D)
+  cfg = LlamaConfig(dim=D, n_layers=n, n_heads=H, n_kv_heads=H, ffn_dim=F, vocab=int(c.vocab_size),
+                    norm_eps=float(g("layer_norm_epsilon", "layer_norm_eps")), norm_type="layer", rope=False,
+                    layers=[LayerSpec(mixer="attention", mlp="gelu_new") for _ in range(n)])
+  T = lambda a: np.ascontiguousarray(np.asarray(a).T)
+  wte = sd["transformer.wte.weight"]
+  w = {"embed": wte, "wpe": sd["transformer.wpe.weight"], "final_norm_w": sd["transformer.ln_f.weight"],
+       "final_norm_b": sd["transformer.ln_f.bias"], "lm_head": sd.get("lm_head.weight", wte), "layers": []}
+  for i in range(n):
+    p = f"transformer.h.{i}."
+    qkv, bqkv = T(sd[p + "attn.c_attn.weight"]), np.asarray(sd[p + "attn.c_attn.bias"])
+    lw = {"attn_norm_w": sd[p + "ln_1.weight"], "attn_norm_b": sd[p + "ln_1.bias"],
+          "wo": T(sd[p + "attn.c_proj.weight"]), "o_bias": sd[p + "attn.c_proj.bias"],
+          "mlp_norm_w": sd[p + "ln_2.weight"], "mlp_norm_b": sd[p + "ln_2.bias"],
+          "wfc": T(sd[p + "mlp.c_fc.weight"]), "fc_bias": sd[p + "mlp.c_fc.bias"],
+          "wproj": T(sd[p + "mlp.c_proj.weight"]), "proj_bias": sd[p + "mlp.c_proj.bias"]}
+    for j, (wk, bk) in enumerate((("wq", "q_bias"), ("wk", "k_bias"), ("wv", "v_bias"))):
+      lw[wk], lw[bk] = np.ascontiguousarray(qkv[j * D:(j + 1) * D]), bqkv[j * D:(j + 1) * D]
+    w["layers"].append(lw)
+  return cfg, w
+
+
 ADAPTERS: list = [
+  (lambda c: getattr(c, "model_type", None) == ModelType.GPT2, _gpt2_adapter),
   (lambda c: getattr(c, "model_type", None) == ModelType.GEMMA, _gemma_adapter),
   (lambda c: getattr(c, "model_type", None) == ModelType.MISTRAL, _mistral_adapter),
 ]

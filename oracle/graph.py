@@ -20,7 +20,7 @@ from __future__ import annotations
 import numpy as np
 
 from . import quant
-from .model import Linear, rms_consts, rms_norm, softmax
+from .model import Linear, layer_norm, rms_consts, rms_norm, softmax
 
 F16, F32 = np.float16, np.float32
 
@@ -129,12 +129,9 @@ class GraphInterp:
         g, floor = rms_consts(a["gamma"], a["eps"])
         r = rms_norm(s[0], g, floor)
       elif op == "layer_norm":
-        x = s[0]
-        mu = x.mean(-1, keepdims=True)
-        var = ((x - mu) ** 2).mean(-1, keepdims=True)
-        r = (x - mu) / np.sqrt(var + F32(a["eps"])) * np.asarray(a["gamma"], F16).astype(F32)
-        if a.get("beta") is not None:
-          r = r + np.asarray(a["beta"], F16).astype(F32)
+        beta = a.get("beta")
+        r = layer_norm(s[0], np.asarray(a["gamma"], F16),
+                       np.zeros(t.shape[-1], F16) if beta is None else np.asarray(beta, F16), a["eps"])
       elif op == "matmul":
         x = s[0]
         r = self._linear(t)(_f16(x).reshape(-1, x.shape[-1])).reshape(t.shape)

@@ -50,7 +50,9 @@ class Config:
   rotary_dim: int = 0; rope_scaling: dict | None = None
   extra: dict = field(default_factory=dict)
   qk_norm: bool = False
-  mlp: str = "swiglu"            # "swiglu", "geglu" or "moe"
+  mlp: str = "swiglu"            # "swiglu", "geglu", "gelu_new" or "moe"
+  norm_type: str = "rms"         # "rms" or "layer" (LayerNorm with bias, GPT-2)
+  rope: bool = True              # False: learned positions (`wpe`) added to the embedding
 
   @property
   def dh(self) -> int:
@@ -99,6 +101,29 @@ def rms_norm(x: np.ndarray, g_eff: np.ndarray, floor) -> np.ndarray:
   nrm = np.sqrt(np.sum(x * x, axis=-1, keepdims=True, dtype=F32)).astype(F32)
   sn = np.maximum(nrm, F32(floor))
   return ((x / sn) * g_eff.astype(F32)).astype(F32)
+
+
+def layer_norm(x: np.ndarray, g: np.ndarray, b: np.ndarray, eps) -> np.ndarray:
+  """Reference `_e_layer_norm` (`_compile.py:758-776`) in fp32: xc = x - mean(x),
+  xc * rsqrt(mean(xc^2) + eps) * g + b, eps rounded to fp16 as the emitter bakes it."""
+  x = x.astype(F32)
+  xc = (x - x.mean(axis=-1, keepdims=True, dtype=F32)).astype(F32)
+  var = (xc * xc).mean(axis=-1, keepdims=True, dtype=F32)
+  rr = (F32(1.0) / np.sqrt(var + F32(np.float16(eps)))).astype(F32)
+  return ((xc * rr) * np.asarray(g, F32) + np.asarray(b, F32)).astype(F32)
+
+
+def norm_consts(w: dict, key: str, cfg) -> tuple:
+  """An encoded norm: ("ln", gamma, beta, eps) for LayerNorm models, else the RMSNorm constants."""
+  if cfg.norm_type == "layer":
+    return ("ln", np.asarray(w[key + "_w"], F16), np.asarray(w[key + "_b"], F16), cfg.norm_eps)
+  return rms_consts(w[key], cfg.norm_eps)
+
+
+def apply_norm(x: np.ndarray, spec) -> np.ndarray:
+  if len(spec) == 4 and isinstance(spec[0], str):
+    return layer_norm(x, *spec[1:])
+  return rms_norm(x, *spec)
 
 
 def rope(x: np.ndarray, c: np.ndarray, s: np.ndarray) -> np.ndarray:
@@ -178,7 +203,8 @@ class OracleModel:
     self.Mx = (encode_weight(Mx, compress, compress_atol, block_size).deq.astype(F32)
                if self.g > 1 else None)
     self.layers = [self._encode_layer(lw) for lw in weights["layers"]]
-    self.final_g, self.final_floor = rms_consts(weights["final_norm"], cfg.norm_eps)
+    self.final_norm = norm_consts(weights, "final_norm", cfg)
+    self.wpe = weights.get("wpe")
     self.lmT = np.ascontiguousarray(np.asarray(weights["lm_head"]).T, F32)
     self.embed = weights["embed"]
 
@@ -189,13 +215,16 @@ class OracleModel:
          "wk": Linear(lw["wk"], lw.get("k_bias"), c, self.atol, self.bs),
          "wv": Linear(lw["wv"], lw.get("v_bias"), c, self.atol, self.bs),
          "wo": Linear(lw["wo"], lw.get("o_bias"), c, self.atol, self.bs)}
-    L["attn_norm"] = rms_consts(lw["attn_norm"], cfg.norm_eps)
-    L["mlp_norm"] = rms_consts(lw["mlp_norm"], cfg.norm_eps)
+    L["attn_norm"] = norm_consts(lw, "attn_norm", cfg)
+    L["mlp_norm"] = norm_consts(lw, "mlp_norm", cfg)
     if "q_norm" in lw:
       L["q_norm"] = rms_consts(lw["q_norm"], cfg.norm_eps)
       L["k_norm"] = rms_consts(lw["k_norm"], cfg.norm_eps)
     if "router" in lw:
       L["moe"] = self._encode_moe(lw)
+    elif "wfc" in lw:                                              # GPT-2 GELU MLP, with biases
+      L["wfc"] = Linear(lw["wfc"], lw.get("fc_bias"), c, self.atol, self.bs)
+      L["wproj"] = Linear(lw["wproj"], lw.get("proj_bias"), c, self.atol, self.bs)
     else:
       L["wgate"] = Linear(lw["wgate"], None, c, self.atol, self.bs)
       L["wup"] = Linear(lw["wup"], None, c, self.atol, self.bs)
@@ -253,7 +282,7 @@ class OracleModel:
   def _qkv(self, L, h, S):
     cfg = self.cfg
     H, KV, dh = cfg.n_heads, cfg.n_kv_heads, cfg.dh
-    xn = rms_norm(h, *L["attn_norm"])
+    xn = apply_norm(h, L["attn_norm"])
     q = self._lin(L["wq"], xn).reshape(S, H, dh)
     k = self._lin(L["wk"], xn).reshape(S, KV, dh)
     v = self._lin(L["wv"], xn).reshape(S, KV, dh)
@@ -275,7 +304,7 @@ class OracleModel:
   def _mlp(self, L, h):
     if "moe" in L:
       return self._moe(L["moe"], h)
-    hn = rms_norm(h, *L["mlp_norm"])
+    hn = apply_norm(h, L["mlp_norm"])
     act = silu(self._lin(L["wgate"], hn)) * self._lin(L["wup"], hn)
     return (h + self._lin(L["wdown"], act)).astype(F32)
 
@@ -286,8 +315,9 @@ class OracleModel:
     H, dh = cfg.n_heads, cfg.dh
     q, k, v = self._qkv(L, h, 1)
     q, k, v = q[0], k[0], v[0]                                     # [H, dh], [KV, dh]
-    c, s = self.cos[pos], self.sin[pos]
-    q = rope(q, c, s); k = rope(k, c, s)
+    if cfg.rope:
+      c, s = self.cos[pos], self.sin[pos]
+      q = rope(q, c, s); k = rope(k, c, s)
     # Kout = Kin*inv + k*oh: fp32 internally, slot `pos` holds the unrounded k
     Kw = Kc[:, : pos + 1].astype(F32); Vw = Vc[:, : pos + 1].astype(F32)
     Kw[:, pos] = k; Vw[:, pos] = v
@@ -299,9 +329,11 @@ class OracleModel:
   def decode_step(self, tok: int, pos: int, caches) -> np.ndarray:
     """Embedding gather -> all layers -> final norm; returns the fp16 hidden port [D]."""
     h = np.asarray(self.embed[tok])[None].astype(F16).astype(F32)
+    if self.wpe is not None:
+      h = (h + np.asarray(self.wpe[pos], F32)).astype(F32)
     for L, (Kc, Vc) in zip(self.layers, caches):
       h = self.decode_layer(L, h, Kc, Vc, pos)
-    return rms_norm(h, self.final_g, self.final_floor).astype(F16)[0]
+    return apply_norm(h, self.final_norm).astype(F16)[0]
 
   def prefill_hidden(self, token_ids):
     """Batched prefill (reference `_prefiller`/`_attn_prefill_kv`, `llm.py:149-169`, `:489-519`).
@@ -322,16 +354,19 @@ class OracleModel:
     self._tables(S)
     c, s = self.cos[:S], self.sin[:S]
     h = np.asarray(rows).astype(F16).astype(F32)
+    if self.wpe is not None:                                       # learned positions 0..S-1, fp32 add
+      h = (h + np.asarray(self.wpe[:S], F32)).astype(F32)
     kv = []
     for L in layers:
       q, k, v = self._qkv(L, h, S)
-      q = rope(q.transpose(1, 0, 2), c, s)                         # [H, S, dh]
-      k = rope(k.transpose(1, 0, 2), c, s); v = v.transpose(1, 0, 2)
+      q, k, v = q.transpose(1, 0, 2), k.transpose(1, 0, 2), v.transpose(1, 0, 2)   # [H, S, dh]
+      if cfg.rope:
+        q = rope(q, c, s); k = rope(k, c, s)
       kv.append((k.astype(F16), v.astype(F16)))
       a = self._attend(q, self._expand(k), self._expand(v), lambda i: i + 1)
       h = h + self._lin(L["wo"], a.transpose(1, 0, 2).reshape(S, H * dh))
       h = self._mlp(L, h)
-    return rms_norm(h, self.final_g, self.final_floor).astype(F16), kv
+    return apply_norm(h, self.final_norm).astype(F16), kv
 
   def encoded_layer_from_codes(self, codes: dict, norms: dict):
     """An encoded int8 layer from per-row codes: `codes` maps wq/wk/wv/wo/wgate/wup/wdown to
@@ -441,7 +476,7 @@ def _moe(self, m, h):
   E, k = e["n_experts"], e["n_experts_per_tok"]
   ffn, T = m["ffn"], h.shape[0]
   L = self._cur_layer
-  hn = rms_norm(h, *L["mlp_norm"])
+  hn = apply_norm(h, L["mlp_norm"])
   probs = softmax(self._lin(m["router"], hn))
   gw = topk_gate(probs, k)
   if e.get("norm_topk_prob", True):
@@ -464,7 +499,9 @@ def _mlp_with_moe(self, L, h):
   if "moe" in L:
     self._cur_layer = L
     return _moe(self, L["moe"], h)
-  hn = rms_norm(h, *L["mlp_norm"])
+  hn = apply_norm(h, L["mlp_norm"])
+  if "wfc" in L:                                                   # GPT-2 (`aneforge/llm.py:178-183`)
+    return (h + self._lin(L["wproj"], gelu_tanh(self._lin(L["wfc"], hn)))).astype(F32)
   g = self._lin(L["wgate"], hn)
   act = (gelu_tanh(g) if self.cfg.mlp == "geglu" else silu(g)) * self._lin(L["wup"], hn)
   return (h + self._lin(L["wdown"], act)).astype(F32)

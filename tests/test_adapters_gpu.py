@@ -18,7 +18,7 @@ def need_gpu():
     pytest.skip("no CUDA device")
 
 
-@pytest.mark.parametrize("kind", ["gemma", "qwen3_moe", "qwen2"])
+@pytest.mark.parametrize("kind", ["gemma", "qwen3_moe", "qwen2", "gpt2"])
 def test_hf_checkpoint_decodes_like_the_oracle(kind, tmp_path):
   from aneforge_b200 import llm
   d, _ = _tiny(kind, tmp_path, hidden_size=256, intermediate_size=512, num_attention_heads=4, num_key_value_heads=2,
@@ -26,6 +26,7 @@ def test_hf_checkpoint_decodes_like_the_oracle(kind, tmp_path):
   m = llm.from_pretrained(str(d), compress="int8")
   prompt = list(np.random.default_rng(3).integers(0, 512, 19))
   toks = m.generate(prompt, 16, max_len=48)
+  assert m.generate(prompt[:5], 16, max_len=48, batched_prefill=False) == m.generate(prompt[:5], 16, max_len=48)
   om = OracleModel(_oracle_cfg(m.cfg), m.w, "int8", precision="device")
   assert teacher_forced_check(om, prompt, toks, 48, n_check=16) <= 2
   m.release()

@@ -29,6 +29,12 @@ def _tiny(kind, tmp_path, **extra):
   elif kind == "mistral":
     cfg = transformers.MistralConfig(sliding_window=64, **common)
     model = transformers.MistralForCausalLM(cfg)
+  elif kind == "gpt2":
+    cfg = transformers.GPT2Config(n_embd=common["hidden_size"], n_layer=common["num_hidden_layers"],
+                                  n_head=common["num_attention_heads"], n_inner=common["intermediate_size"],
+                                  vocab_size=common["vocab_size"], n_positions=common["max_position_embeddings"],
+                                  initializer_range=common.get("initializer_range", 0.02))
+    model = transformers.GPT2LMHeadModel(cfg)
   elif kind == "gemma":
     cfg = transformers.GemmaConfig(head_dim=hd, hidden_act="gelu_pytorch_tanh", **common)
     model = transformers.GemmaForCausalLM(cfg)
@@ -78,15 +84,17 @@ def _oracle_cfg(cfg):
   return Config(dim=cfg.dim, n_layers=cfg.n_layers, n_heads=cfg.n_heads, n_kv_heads=cfg.n_kv_heads,
                 ffn_dim=cfg.ffn_dim, vocab=cfg.vocab, rope_base=cfg.rope_base, norm_eps=cfg.norm_eps,
                 head_dim=cfg.head_dim, rope_scaling=cfg.rope_scaling, extra=dict(cfg.extra),
-                qk_norm=cfg.layers[0].qk_norm, mlp="geglu" if cfg.layers[0].mlp == "geglu" else "swiglu")
+                qk_norm=cfg.layers[0].qk_norm, norm_type=cfg.norm_type, rope=cfg.rope,
+                mlp=cfg.layers[0].mlp if cfg.layers[0].mlp in ("geglu", "gelu_new") else "swiglu")
 
 
 def _hf_last_logits(model, prompt):
+  model.eval()                                             # GPT-2 has dropout
   with torch.no_grad():
     return model(torch.tensor([prompt])).logits[0, -1].float().numpy()
 
 
-@pytest.mark.parametrize("kind", ["gemma", "qwen3_moe"])
+@pytest.mark.parametrize("kind", ["gemma", "qwen3_moe", "gpt2"])
 def test_adapter_runs_like_transformers(kind, tmp_path):
   """Gemma (GeGLU, sqrt(hidden)-scaled embedding, 1 + w norms) and Qwen3-MoE (fused expert tensors,
   dense layers from `mlp_only_layers`, QK-norm, no top-k renormalisation): the adapted weights run
@@ -103,6 +111,11 @@ def test_adapter_runs_like_transformers(kind, tmp_path):
     np.testing.assert_allclose(w["embed"], e.astype(np.float64) * np.sqrt(64))
     np.testing.assert_array_equal(w["layers"][0]["attn_norm"],
                                   sd["model.layers.0.input_layernorm.weight"].half().numpy() + np.float16(1))
+  elif kind == "gpt2":
+    assert cfg.norm_type == "layer" and not cfg.rope and [ls.mlp for ls in cfg.layers] == ["gelu_new", "gelu_new"]
+    sd = model.state_dict()
+    np.testing.assert_array_equal(w["layers"][1]["wk"], sd["transformer.h.1.attn.c_attn.weight"].half().numpy()[:, 64:128].T)
+    np.testing.assert_array_equal(w["wpe"], sd["transformer.wpe.weight"].half().numpy())
   else:
     assert [ls.mlp for ls in cfg.layers] == ["moe", "swiglu"]
     assert cfg.extra == {"n_experts": 4, "n_experts_per_tok": 2, "norm_topk_prob": False}
@@ -136,7 +149,7 @@ def test_dense_loader_refuses_unsupported_architectures():
   from aneforge_b200 import llm
 
   class C:
-    model_type = "gpt2"
+    model_type = "gemma3_text"
   with pytest.raises(ValueError):
     llm._assert_dense_compatible(C())
 
