@@ -214,13 +214,17 @@ class Lowering:
         nbytes = R.load_library().af_gemv_tc_scratch_bytes(N, K, min(rows, 16))
         kv["scr"] = self.pb.buf("gemv.scr", nbytes, "scratch")
       self.pb.op("gemv", **kv)
-    elif lin.kind in ("lut4", "blockwise"):
-      # packed palette / blockwise codes: the CUDA-core GEMV streams them as they are
+    elif lin.kind in ("lut4", "blockwise", "sparse"):
+      # packed palette / blockwise codes / sparse bitmask: the CUDA-core GEMVs stream them as they are
       xh = self._buf(f"{nm}.xh", 2 * rows * K)
       self.pb.op("cast", src=x, dst=xh, n=rows * K, mode=1)
       kv["gs"] = kv.pop("s")
       if lin.kind == "blockwise":
         kv["grp"] = lin.group
+      if lin.kind == "sparse":
+        rb = self._buf(f"{nm}.ro", lin.rowoff.numel() * 4, "weight")
+        self.binds.append((rb, lin.rowoff))
+        kv.update(ro=rb, nnz=lin.s.numel())
       kv.update(wf=lin.wf, epi="f32", x=xh, w=wb, y=y, nb=rows)
       self.pb.op("gemv", **kv)
     else:

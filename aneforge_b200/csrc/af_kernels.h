@@ -16,8 +16,10 @@ inline int env_int(const char* name, int dflt) {
 
 // W_LUT4: 4-bit indices (two per byte, low nibble first) into a 16-entry fp16 codebook per row
 // (gscale [N][16]); W_I8G: int8 codes with one fp16 scale per `group` consecutive elements of a row
-// (gscale [N][K / group]) - the reference's palettized and blockwise encodings, streamed packed
-enum WFormat : int { W_I8 = 0, W_F16 = 1, W_I4G32 = 2, W_LUT4 = 3, W_I8G = 4 };
+// (gscale [N][K / group]); W_SPARSE: a K-bit keep mask per row (w = [N][K/32] 32-bit words, bit j of
+// word i = column 32 i + j) with the row's kept fp16 values in column order (gscale, the row's first
+// at rowoff[row]) - the reference's palettized, blockwise and bitmask-sparse encodings, streamed packed
+enum WFormat : int { W_I8 = 0, W_F16 = 1, W_I4G32 = 2, W_LUT4 = 3, W_I8G = 4, W_SPARSE = 5 };
 
 // L2 prefetch of (part of) a later kernel's weights, issued by a kernel whose own phase leaves HBM
 // idle: pieces of `piece` bytes every `stride` bytes of [base, base + bytes), spread evenly over the
@@ -37,6 +39,7 @@ struct GemvArgs {
   const __half* scale = nullptr;   // int8: [N] per-row scale
   const __half* gscale = nullptr;  // int4: [N][K/32] group scales; LUT4: [N][16] codebooks; I8G: [N][K/group]
   int group = 32;                  // I8G: elements per scale (a multiple of 16)
+  const int* rowoff = nullptr;     // SPARSE: [N + 1] offsets of each row's values in gscale
   const __half* bias = nullptr;    // [N] or null
   void* y = nullptr;           // output (see Epilogue); ARGMAX: optional fp32 logits
   int ldy = 0;
@@ -56,6 +59,7 @@ struct GemvArgs {
 };
 
 cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t st, bool pdl);
+cudaError_t gemv_sparse_launch(const GemvArgs& a, cudaStream_t st, bool pdl);
 
 // Tensor-core int8 GEMV over fragment-tile packed weights (gemv_tc.cu). Epilogues F32/F16/RESID/SWIGLU.
 struct GemvTcArgs {

@@ -488,6 +488,7 @@ static int tile_template(int epi, int nb_tile, int nb_total) {
 // Host entry: the batch is processed in tiles of up to 4 rows of x (weights re-streamed per tile).
 // Argmax tiles each own a counter and a partial region of the scratch (see gemv_argmax_scratch).
 cudaError_t gemv_launch(const GemvArgs& a0, cudaStream_t st, bool pdl) {
+  if (a0.wf == W_SPARSE) return gemv_sparse_launch(a0, st, pdl);
   if (a0.K % chunk_elems(a0.wf)) return cudaErrorInvalidValue;
   if (a0.wf == W_I8G && (a0.group < 16 || a0.group % 16 || a0.K % a0.group)) return cudaErrorInvalidValue;
   if ((a0.wf == W_LUT4 || a0.wf == W_I8G) && (!a0.gscale || a0.epi == EPI_ARGMAX)) return cudaErrorInvalidValue;

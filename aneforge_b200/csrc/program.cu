@@ -206,6 +206,7 @@ static int wf_of(const std::string& s) {
   if (s == "i4") return W_I4G32;
   if (s == "l4") return W_LUT4;
   if (s == "i8g") return W_I8G;
+  if (s == "sp") return W_SPARSE;
   return -1;
 }
 static int epi_of(const std::string& s) {
@@ -534,7 +535,8 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     a.ldy = c.i("ldy", out_cols);
     a.x = (const __half*)c.ptr("x", 2 * ((size_t)(a.NB - 1) * a.ldx + a.K));
     const size_t wbytes = (a.wf == W_I8 || a.wf == W_I8G) ? (size_t)a.N * a.K
-                          : a.wf == W_F16 ? (size_t)a.N * a.K * 2 : (size_t)a.N * a.K / 2;
+                          : a.wf == W_F16 ? (size_t)a.N * a.K * 2
+                          : a.wf == W_SPARSE ? (size_t)a.N * (a.K / 32) * 4 : (size_t)a.N * a.K / 2;
     a.w = c.ptr("w", wbytes);
     if (a.wf == W_I8) a.scale = (const __half*)c.ptr("s", 2 * (size_t)a.N);
     if (a.wf == W_I4G32) a.gscale = (const __half*)c.ptr("gs", 2 * (size_t)a.N * (a.K / 32));
@@ -543,6 +545,11 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
       a.group = (int)c.i("grp", 32);
       if (a.group < 16 || a.group % 16 || a.K % a.group) c.err = "grp must be a multiple of 16 dividing k";
       else a.gscale = (const __half*)c.ptr("gs", 2 * (size_t)a.N * (a.K / a.group));
+    }
+    if (a.wf == W_SPARSE) {
+      if (a.K % 32 || a.epi == EPI_ARGMAX) c.err = "sparse weights need k % 32 == 0 and no argmax epilogue";
+      a.gscale = (const __half*)c.ptr("gs", 2 * (size_t)c.i("nnz"));
+      a.rowoff = (const int*)c.ptr("ro", 4 * ((size_t)a.N + 1));
     }
     a.bias = (const __half*)c.ptr("bias", 2 * (size_t)a.N, true);
     const size_t esz = (a.epi == EPI_F16 || a.epi == EPI_SWIGLU) ? 2 : 4;

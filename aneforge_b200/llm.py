@@ -156,10 +156,12 @@ def _emit_linear(pb, ctx, name, lin: DevLinear, x, y, epi, nb=None):
       if nbytes:
         pb.buf("gemv.scr", nbytes, "scratch")        # one split-K scratch shared by every GEMV
         kv["scr"] = "gemv.scr"
-  elif lin.kind in ("int4_g32", "lut4", "blockwise") and not lin.tiled:
-    kv["gs"] = f"{name}.s"                             # group scales / per-row codebooks
+  elif lin.kind in ("int4_g32", "lut4", "blockwise", "sparse") and not lin.tiled:
+    kv["gs"] = f"{name}.s"                             # group scales / per-row codebooks / kept values
     if lin.kind == "blockwise":
       kv["grp"] = lin.group
+    if lin.kind == "sparse":
+      kv.update(ro=f"{name}.ro", nnz=lin.s.numel())
   if lin.bias is not None:
     kv["bias"] = f"{name}.b"
   pb.op("gemv", **kv)
@@ -553,6 +555,8 @@ class LlamaPrefill:
         prog.bind(f"L{li}.{key}.s", lin.s)
       if lin.bias is not None:
         prog.bind(f"L{li}.{key}.b", lin.bias)
+      if lin.rowoff is not None:
+        prog.bind(f"L{li}.{key}.ro", lin.rowoff)
     for key in ("attn_g", "mlp_g", "qn", "kn", "attn_lw", "attn_lb"):
       if key in d:
         prog.bind(f"L{li}.{key}", d[key])
@@ -572,6 +576,8 @@ class LlamaPrefill:
         pb.buf(f"L{li}.{key}.s", lin.s.numel() * 2, "weight")
       if lin.bias is not None:
         pb.buf(f"L{li}.{key}.b", lin.bias.numel() * 2, "weight")
+      if lin.rowoff is not None:
+        pb.buf(f"L{li}.{key}.ro", lin.rowoff.numel() * 4, "weight")
     for key in ("attn_g", "mlp_g", "qn", "kn", "attn_lw", "attn_lb"):
       if key in d:
         pb.buf(f"L{li}.{key}", d[key].numel() * 2, "weight")

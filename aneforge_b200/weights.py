@@ -51,6 +51,7 @@ class DevLinear:
   K: int
   tiled: bool = False  # int8 / int4_g32 in tensor-core fragment tiles (K % 32 == 0) vs row-major
   group: int = 0       # blockwise: elements per scale
+  rowoff: object = None  # sparse: [N + 1] int32 offsets of each row's values in `s`
 
   @property
   def wf(self) -> str:
@@ -62,13 +63,16 @@ class DevLinear:
       return "l4"
     if self.kind == "blockwise":
       return "i8g"
+    if self.kind == "sparse":
+      return "sp"
     return "f16"
 
   @property
   def nbytes(self) -> int:
     n = self.w.numel() * self.w.element_size()
-    if self.s is not None:
-      n += self.s.numel() * self.s.element_size()
+    for t in (self.s, self.rowoff):
+      if t is not None:
+        n += t.numel() * t.element_size()
     return n
 
 
@@ -90,12 +94,13 @@ def decide_kind(W, compress, atol=0.05, block_size=32) -> str:
   return kind
 
 
-# Accepted LUT4 and blockwise weights stream packed (`_packed`: 4-bit codes + per-row codebook, or
-# int8 codes + per-block scales, on the CUDA-core GEMV) when every part of a fused projection takes
-# that encoding and the shape fits (LUT4: K % 32 == 0; blockwise: blocks a multiple of 16). The rest
-# - a sparse weight, projections whose parts encode differently, other shapes - run as fp16 matrices
-# of their decoded values on the fp16-weight kernels: exact for LUT4 and sparse values; a blockwise
-# weight's int8 x fp16-scale product is then rounded to fp16 once.
+# Accepted LUT4, blockwise and sparse weights stream packed (`_packed`: 4-bit codes + per-row
+# codebook, int8 codes + per-block scales, or a keep bitmask + the kept fp16 values, on the CUDA-core
+# GEMVs) when every part of a fused projection takes that encoding and the shape fits (LUT4 and
+# sparse: K % 32 == 0; blockwise: blocks a multiple of 16). The rest - projections whose parts
+# encode differently, other shapes - run as fp16 matrices of their decoded values on the fp16-weight
+# kernels: exact for LUT4 and sparse values; a blockwise weight's int8 x fp16-scale product is then
+# rounded to fp16 once.
 DENSE_KINDS = ("lut4", "blockwise", "sparse")
 
 
@@ -139,7 +144,7 @@ def _packed(parts, compress, atol, block_size):
   device streams as such - an accepted LUT4 palette (codes 4-bit, one 16-entry fp16 codebook per row,
   K a multiple of 32) or accepted blockwise int8 (one fp16 scale per block, block a multiple of 16)
   - else None."""
-  if compress not in ("int4", "blockwise", "auto"):
+  if compress not in ("int4", "blockwise", "auto", "sparse"):
     return None
   hosts = [P.detach().float().cpu().numpy() if hasattr(P, "detach") else np.asarray(P, F32) for P in parts]
   K = hosts[0].shape[1]
@@ -148,6 +153,8 @@ def _packed(parts, compress, atol, block_size):
   if len(kinds) != 1:
     return None
   kind = kinds.pop()
+  if kind == "sparse" and K % 32 == 0:
+    return kind, [(np.asarray(W, np.float16), None) for W in hosts], 0
   if kind == "lut4" and K % 32 == 0:
     return kind, [(packed, np.tile(lut.astype(F16), (W.shape[0], 1))) for W, (_, (packed, lut)) in zip(hosts, decided)], 0
   if kind == "blockwise":
@@ -158,9 +165,37 @@ def _packed(parts, compress, atol, block_size):
   return None
 
 
+def _encode_sparse(mats, device, swiglu):
+  """(mask words [N][K/32] int32, kept values fp16, row offsets [N+1] int32) of the fused fp16
+  matrix: the reference's `sparsify` bit order (LSB first) per row, values in column order."""
+  torch = torch_mod()
+  W = (layout.interleave_blocks(mats[0], mats[1], layout.SWIGLU_HALF) if swiglu
+       else np.concatenate(mats, 0) if len(mats) > 1 else mats[0])
+  nz = W != 0
+  mask = np.packbits(nz, axis=1, bitorder="little").view("<u4").view(np.int32)
+  counts = nz.sum(axis=1, dtype=np.int64)
+  if counts.sum() >= 2 ** 31:
+    raise NotImplementedError("a sparse projection with 2^31 or more kept values")
+  rowoff = np.zeros(W.shape[0] + 1, np.int32)
+  rowoff[1:] = np.cumsum(counts)
+  dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device)
+  vals = W[nz].astype(np.float16)
+  return dev(mask), dev(vals if vals.size else np.zeros(1, np.float16)), dev(rowoff)
+
+
 def _encode_packed(parts, kind, enc, group, device, biases, swiglu) -> DevLinear:
   torch = torch_mod()
   dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device)
+  if kind == "sparse":
+    mask, vals, rowoff = _encode_sparse([m for m, _ in enc], device, swiglu)
+    N, K = int(mask.shape[0]), int(parts[0].shape[1])
+    b = None
+    if biases is not None and any(x is not None for x in biases):
+      if swiglu:
+        raise NotImplementedError("bias on a gate/up projection")
+      b = torch.cat([torch.zeros(int(P.shape[0]), dtype=torch.float16, device=device) if x is None
+                     else to_device(x, device).float().half() for P, x in zip(parts, biases)]).contiguous()
+    return DevLinear("sparse", mask, vals, b, N, K, False, 0, rowoff)
   if swiglu:
     (cg, sg), (cu, su) = enc
     codes = layout.interleave_blocks(cg, cu, layout.SWIGLU_HALF)

@@ -14,6 +14,7 @@ import re
 import numpy as np
 import pytest
 
+from oracle import quant as Q
 from tests._golden import load
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -127,3 +128,26 @@ def test_swiglu_interleave_layout():
   assert w.shape == (32, 2)
   assert torch.equal(w[:8], g[:8]) and torch.equal(w[8:16], u[:8])
   assert torch.equal(w[16:24], g[8:]) and torch.equal(w[24:], u[8:])
+
+
+def test_sparse_device_encoding_round_trips():
+  """The sparse projection's device payload (keep-mask words, kept values, row offsets) decodes to
+  the fused fp16 matrix - gate/up interleaved in blocks of 4 rows - with the reference's LSB-first
+  bit order (`aneforge/_blob.py:59-64`)."""
+  import torch
+  from aneforge_b200 import layout
+  from aneforge_b200.weights import _encode_sparse
+  rng = np.random.default_rng(0)
+  g, u = (np.where(rng.random((16, 96)) < 0.7, 0, rng.standard_normal((16, 96))).astype(np.float16) for _ in range(2))
+  for mats, swiglu in (([g], False), ([g, u], True), ([g, u], False)):
+    mask, vals, ro = _encode_sparse(mats, torch.device("cpu"), swiglu)
+    W = layout.interleave_blocks(g, u, layout.SWIGLU_HALF) if swiglu else np.concatenate(mats, 0)
+    m, v, r = mask.numpy().view(np.uint32), vals.numpy(), ro.numpy()
+    D = np.zeros_like(W)
+    for i in range(W.shape[0]):
+      cols = [c for c in range(W.shape[1]) if (m[i, c // 32] >> (c % 32)) & 1]
+      D[i, cols] = v[r[i]:r[i + 1]]
+    np.testing.assert_array_equal(D, W)
+    ref_mask, ref_vals = Q.sparsify(W)                   # the oracle's restatement of the encoder
+    np.testing.assert_array_equal(np.frombuffer(mask.numpy().tobytes(), np.uint8), np.asarray(ref_mask, np.uint8))
+    np.testing.assert_array_equal(v[:r[-1]], np.asarray(ref_vals, np.float16))

@@ -253,3 +253,33 @@ def test_blockwise_weights_run_packed():
   assert np.abs(pl - ol).max() <= 1e-2 * np.abs(ol).max()
   assert cosine(pl, ol) > 0.999
   m.release()
+
+
+def test_sparse_weights_run_packed():
+  """compress="sparse" (`aneforge/_blob.py:59-64`): pruned projections (about 70 % zeros) pass the
+  reference's at-most-half-nonzero gate and stream as keep bitmask + kept fp16 values (the sparse
+  GEMV, swiglu and residual epilogues included); decode and prefill against the oracle."""
+  from aneforge_b200.llm import LlamaPrefill
+  cfg = Config(dim=256, n_layers=2, n_heads=4, n_kv_heads=2, ffn_dim=512, vocab=512, rope_base=10000.0,
+               head_dim=64)
+  w = random_llama_weights(cfg, seed=37, std=0.08)
+  rng = np.random.default_rng(38)
+  for lw in w["layers"]:
+    for k in ("wq", "wk", "wv", "wo", "wgate", "wup", "wdown"):
+      lw[k] = np.where(rng.random(lw[k].shape) < 0.7, 0, lw[k]).astype(lw[k].dtype)
+  m = LlamaPrefill(to_b200_cfg(cfg), w, compress="sparse")
+  dl = m._load()["layers"]
+  assert all(dl[i][p].wf == "sp" for i in range(2) for p in ("qkv", "o", "gu", "down"))
+  lin = dl[0]["gu"]
+  assert lin.nbytes < 0.45 * 2 * lin.N * lin.K                   # mask + kept values vs fp16
+  prompt = list(np.random.default_rng(39).integers(0, cfg.vocab, 40))
+  toks = m.generate(prompt, 16, max_len=64)
+  om = OracleModel(cfg, w, "sparse", precision="device")
+  assert teacher_forced_check(om, prompt, toks, 64, n_check=16) <= 1
+  pl = m.prefill(prompt)[0]
+  hid, _ = om.prefill_hidden(prompt)
+  ol = om.logits(hid[-1].astype(F32))
+  assert cosine(pl, ol) > 0.999
+  batch = m.generate_batch([prompt, prompt[:7], prompt[:23]], 8, max_len=64)
+  assert batch[0] == toks[:8]
+  m.release()
