@@ -3,6 +3,8 @@ projections: the B200 replacement for baking weights into the e5rt BLOBFILE
 (`aneforge/_compile.py:112-188`, `_blob.py:67-86`)."""
 from __future__ import annotations
 
+import hashlib
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -214,10 +216,89 @@ def _encode_packed(parts, kind, enc, group, device, biases, swiglu) -> DevLinear
   return DevLinear(kind, w, dev(side.astype(F16)), b, N, K, False, group)
 
 
+# ---- content-addressed cache of packed projections (the B200 counterpart of the reference's
+# content-addressed program cache, `aneforge/_compile.py:898-923`): the device payload of a
+# projection keyed by the SHA-256 of everything that decides it - the format version, compress=,
+# the gate tolerance and block size, the fused layout, and every part's and bias's dtype, shape and
+# bytes. Host-heavy encodings (the LUT4 palettizer, blockwise, sparse) are then paid once per
+# checkpoint. On when AF_WEIGHT_CACHE names a directory (or `set_weight_cache`); AF_FORCE_REPACK=1
+# re-encodes and overwrites. Weights given as device tensors are not hashed (no host copy is made).
+CACHE_FORMAT = 1
+_cache_dir = None
+
+
+def set_weight_cache(path) -> None:
+  """Directory of the packed-projection cache (None: AF_WEIGHT_CACHE, unset: off)."""
+  global _cache_dir
+  _cache_dir = None if path is None else str(path)
+
+
+def weight_cache_dir():
+  return _cache_dir or os.environ.get("AF_WEIGHT_CACHE") or None
+
+
+def _host_bytes(a):
+  if a is None:
+    return b"-"
+  if hasattr(a, "detach"):
+    if a.device.type != "cpu":
+      return None
+    a = a.detach().numpy()
+  a = np.ascontiguousarray(np.asarray(a))
+  return f"{a.dtype.str}{a.shape}".encode(), memoryview(a).cast("B")
+
+
+def _cache_key(parts, biases, compress, swiglu, atol, block_size):
+  h = hashlib.sha256(f"afw{CACHE_FORMAT}|{compress}|{int(swiglu)}|{atol!r}|{block_size}|{len(parts)}".encode())
+  for a in list(parts) + list(biases or [None] * len(parts)):
+    hb = _host_bytes(a)
+    if hb is None:
+      return None
+    for piece in (hb if isinstance(hb, tuple) else (hb,)):
+      h.update(piece)
+  return h.hexdigest()
+
+
+def _cache_load(path, device):
+  torch = torch_mod()
+  d = torch.load(path, map_location=device, weights_only=True)
+  m = d["meta"]
+  return DevLinear(m["kind"], d["w"], d.get("s"), d.get("bias"), int(m["N"]), int(m["K"]), bool(m["tiled"]),
+                   int(m["group"]), d.get("rowoff"))
+
+
+def _cache_store(path, lin: DevLinear):
+  torch = torch_mod()
+  d = {"meta": {"kind": lin.kind, "N": lin.N, "K": lin.K, "tiled": lin.tiled, "group": lin.group},
+       "w": lin.w.detach().cpu()}
+  for k in ("s", "bias", "rowoff"):
+    t = getattr(lin, k)
+    if t is not None:
+      d[k] = t.detach().cpu()
+  os.makedirs(os.path.dirname(path), exist_ok=True)
+  tmp = f"{path}.{os.getpid()}.tmp"
+  torch.save(d, tmp)
+  os.replace(tmp, path)                       # atomic: a concurrent reader sees all or nothing
+
+
 def encode_linear(parts, compress, device, biases=None, swiglu=False, atol=0.05, block_size=32) -> DevLinear:
   """Encode one or more [N_i, K] matrices sharing their input into one device projection.
   `swiglu=True` takes (gate, up) and interleaves them for the fused silu(gate)*up epilogue;
-  otherwise the rows are concatenated (q|k|v)."""
+  otherwise the rows are concatenated (q|k|v). Goes through the packed-projection cache when one is
+  configured."""
+  root = weight_cache_dir()
+  key = _cache_key(parts, biases, compress, swiglu, atol, block_size) if root else None
+  if key is None:
+    return _encode_linear(parts, compress, device, biases, swiglu, atol, block_size)
+  path = os.path.join(root, key[:2], key + ".pt")
+  if os.path.exists(path) and os.environ.get("AF_FORCE_REPACK", "0") == "0":
+    return _cache_load(path, device)
+  lin = _encode_linear(parts, compress, device, biases, swiglu, atol, block_size)
+  _cache_store(path, lin)
+  return lin
+
+
+def _encode_linear(parts, compress, device, biases=None, swiglu=False, atol=0.05, block_size=32) -> DevLinear:
   torch = torch_mod()
   packed = _packed(parts, compress, atol, block_size)
   if packed is not None:

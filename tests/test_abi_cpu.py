@@ -151,3 +151,37 @@ def test_sparse_device_encoding_round_trips():
     ref_mask, ref_vals = Q.sparsify(W)                   # the oracle's restatement of the encoder
     np.testing.assert_array_equal(np.frombuffer(mask.numpy().tobytes(), np.uint8), np.asarray(ref_mask, np.uint8))
     np.testing.assert_array_equal(v[:r[-1]], np.asarray(ref_vals, np.float16))
+
+
+@pytest.mark.parametrize("compress", ["blockwise", "sparse"])
+def test_packed_projection_cache_round_trips(tmp_path, monkeypatch, compress):
+  """The content-addressed packed-projection cache: a second encode of the same weights loads the
+  stored payload (no host encoding runs), equal tensors; other weights or settings miss."""
+  import torch
+  from aneforge_b200 import weights as Wm
+  rng = np.random.default_rng(1)
+  g = (rng.standard_normal((64, 128)) * 0.05).astype(np.float16)
+  u = (rng.standard_normal((64, 128)) * 0.05).astype(np.float16)
+  if compress == "sparse":
+    g, u = (np.where(rng.random(x.shape) < 0.7, 0, x).astype(np.float16) for x in (g, u))
+  Wm.set_weight_cache(tmp_path)
+  try:
+    cpu = torch.device("cpu")
+    a = Wm.encode_linear([g, u], compress, cpu, swiglu=True)
+    assert a.kind == compress and len(list(tmp_path.rglob("*.pt"))) == 1
+    calls = []
+    monkeypatch.setattr(Wm, "_encode_linear", lambda *args, **kw: calls.append(1))
+    b = Wm.encode_linear([g, u], compress, cpu, swiglu=True)
+    assert not calls
+    assert (b.kind, b.N, b.K, b.group) == (a.kind, a.N, a.K, a.group)
+    for k in ("w", "s", "bias", "rowoff"):
+      ta, tb = getattr(a, k), getattr(b, k)
+      assert (ta is None) == (tb is None)
+      if ta is not None:
+        assert torch.equal(ta, tb)
+    monkeypatch.undo()
+    Wm.set_weight_cache(tmp_path)
+    Wm.encode_linear([g, u], compress, cpu, swiglu=False)   # another layout: a second entry
+    assert len(list(tmp_path.rglob("*.pt"))) == 2
+  finally:
+    Wm.set_weight_cache(None)
