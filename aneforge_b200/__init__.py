@@ -8,6 +8,7 @@ CUDA device the runtime raises.
 from . import graph  # noqa: F401
 from . import llm  # noqa: F401
 from . import moe  # noqa: F401  (registers the "moe" MLP with the runner)
+from . import hybrid  # noqa: F401  (registers the gated DeltaNet / gated attention mixers)
 from ._compile import Model, MultiModel, compile, compile_multi  # noqa: F401,A004
 from .graph import Tensor, concat, const, gather, input, maximum, minimum, select, split, stack, where  # noqa: F401,A004
 from .llm import LlamaConfig, LayerSpec, LlamaPrefill, from_pretrained, rope_tables  # noqa: F401

@@ -19,6 +19,25 @@ AF_DEV void af_set_err(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
+// Wall-clock bound of a device-side wait, on top of its iteration limit (a suspended
+// `mbarrier.try_wait` or a slow poll can make an iteration limit minutes long): `spent()` turns
+// true once the wait has lasted `limit_ns` (checked every 64 calls).
+AF_DEV uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+struct SpinBudget {
+  uint64_t t0 = 0;
+  uint32_t n = 0;
+  AF_DEV bool spent(uint64_t limit_ns = 2000000000ull) {
+    if ((++n & 63) != 0) return false;
+    const uint64_t t = global_ns();
+    if (t0 == 0) { t0 = t; return false; }
+    return t - t0 > limit_ns;
+  }
+};
+
 // ---- host: per-device caches. Kernel attributes (cudaFuncSetAttribute) belong to the current
 // device's context, and occupancy answers are per device too, so every cache of them is keyed by
 // the device ordinal; one mutex per cache makes concurrent first calls from several host threads

@@ -109,8 +109,13 @@ AF_DEV void chain_norm(const ChainJob& J, int NB, ChainShared* sh) {
   }
 }
 
+// CTAs that work on job J: all G, or one per unit when the job has fewer units than CTAs (every
+// working CTA then has a non-empty range, so a row block's pieces are exactly CTAs cf..cl)
+AF_HD int job_grid(const ChainJob& J, int G) { return J.U < (long long)G ? (int)J.U : G; }
+
 AF_DEV bool wait_flag(const int* f) {
-  for (long long i = 0; i < FLAG_LIMIT; ++i) {
+  SpinBudget budget;
+  for (long long i = 0; i < FLAG_LIMIT && !budget.spent(); ++i) {
     int v;
     asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
     if (v) return true;
@@ -161,8 +166,10 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_chain_kernel(const 
       for (int j = 0; j < a.njobs && ok; ++j) {
         const ChainJob& J = a.job[j];
         const char* W = static_cast<const char*>(J.w);
-        const long long u1 = unit_begin(c + 1, J.U, G);
-        for (long long u = unit_begin(c, J.U, G); u < u1 && ok;) {
+        const int Gj = job_grid(J, G);
+        if (c >= Gj) continue;
+        const long long u1 = unit_begin(c + 1, J.U, Gj);
+        for (long long u = unit_begin(c, J.U, Gj); u < u1 && ok;) {
           const int rb = (int)(u / J.KT), kta = (int)(u % J.KT);
           const int ktb = (int)min((long long)J.KT, kta + (u1 - u));
           for (int kc = kta; kc < ktb && ok; kc += tc::XKT) {
@@ -201,8 +208,10 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_chain_kernel(const 
           if (!wait_flag(a.ready + j - 1)) { ok = false; break; }
           asm volatile("fence.proxy.async.global;" ::: "memory");   // generic writes -> bulk-copy reads
         }
-        const long long u1 = unit_begin(c + 1, J.U, G);
-        for (long long u = unit_begin(c, J.U, G); u < u1 && ok;) {
+        const int Gj = job_grid(J, G);
+        if (c >= Gj) continue;
+        const long long u1 = unit_begin(c + 1, J.U, Gj);
+        for (long long u = unit_begin(c, J.U, Gj); u < u1 && ok;) {
           const int kta = (int)(u % J.KT);
           const int ktb = (int)min((long long)J.KT, kta + (u1 - u));
           for (int kc = kta; kc < ktb; kc += tc::XKT) {
@@ -250,8 +259,10 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_chain_kernel(const 
   for (int j = 0; j < a.njobs && !quit; ++j) {
     const ChainJob& J = a.job[j];
     const int KT = J.KT;
-    const long long U = J.U, u1 = unit_begin(c + 1, U, G);
-    for (long long u = unit_begin(c, U, G); u < u1;) {
+    const int Gj = job_grid(J, G);
+    if (c >= Gj) continue;
+    const long long U = J.U, u1 = unit_begin(c + 1, U, Gj);
+    for (long long u = unit_begin(c, U, Gj); u < u1;) {
       const int rb = (int)(u / KT), kta = (int)(u % KT);
       const int ktb = (int)min((long long)KT, kta + (u1 - u));
       float acc[NT][4], acc2[NT][4];
@@ -310,7 +321,7 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_chain_kernel(const 
         finished = true;
       } else {
         // a piece of a shared row block: publish it; the last piece to arrive sums them all
-        const int cf = owner_of((long long)rb * KT, U, G), cl = owner_of((long long)rb * KT + KT - 1, U, G);
+        const int cf = owner_of((long long)rb * KT, U, Gj), cl = owner_of((long long)rb * KT + KT - 1, U, Gj);
         const int nc = cl - cf + 1, jj = c - cf;
         const int r0 = rtw * 16 + g, r1 = r0 + 8;
         if (!par) {
@@ -439,8 +450,9 @@ size_t chain_layout(GemvChainArgs& a, int G) {
     J.KT = J.K / 32;
     J.U = (long long)J.RB * J.KT;
     int maxc = 1;
+    const int Gj = job_grid(J, G);
     for (int rb = 0; rb < J.RB; ++rb) {
-      const int n = owner_h((long long)rb * J.KT + J.KT - 1, J.U, G) - owner_h((long long)rb * J.KT, J.U, G) + 1;
+      const int n = owner_h((long long)rb * J.KT + J.KT - 1, J.U, Gj) - owner_h((long long)rb * J.KT, J.U, Gj) + 1;
       if (n > maxc) maxc = n;
     }
     J.maxc = maxc;

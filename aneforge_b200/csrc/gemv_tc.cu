@@ -306,7 +306,8 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
       } else {
         if (threadIdx.x == 0) {
           bool in = false;
-          for (long long i = 0; i < tc::WAIT_LIMIT && !in; ++i) {
+          SpinBudget budget;
+          for (long long i = 0; i < tc::WAIT_LIMIT && !in && !budget.spent(); ++i) {
             int v;
             asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(a.counters + rb) : "memory");
             in = v >= nc - 1;

@@ -45,9 +45,12 @@ AF_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-AF_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {   // bounded
-  for (long long i = 0; i < tc::WAIT_LIMIT; ++i)
+AF_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {   // bounded: iterations and ~2 s
+  SpinBudget budget;
+  for (long long i = 0; i < tc::WAIT_LIMIT; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (budget.spent()) return false;
+  }
   return false;
 }
 

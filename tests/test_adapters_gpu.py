@@ -30,3 +30,36 @@ def test_hf_checkpoint_decodes_like_the_oracle(kind, tmp_path):
   om = OracleModel(_oracle_cfg(m.cfg), m.w, "int8", precision="device")
   assert teacher_forced_check(om, prompt, toks, 48, n_check=16) <= 2
   m.release()
+
+
+@pytest.mark.parametrize("compress", [None, "int8"])
+def test_qwen35_hybrid_decodes_like_transformers(compress):
+  """A Qwen3.5 hybrid (three gated-DeltaNet layers, one gated-attention layer; reference
+  `aneforge/qwen35.py`, `tests/test_qwen35.py:87-117`) through `hybrid.adapt` onto the device: the
+  graph-builder mixers keep their conv / recurrent / K-V states resident. Its greedy tokens are the
+  checkpoint's own next-token argmax (transformers, fp32, on the same prefix) except near ties."""
+  from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5TextConfig
+  from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5ForCausalLM
+  from aneforge_b200 import hybrid, llm
+  torch.manual_seed(0)
+  ct = Qwen3_5TextConfig(hidden_size=256, num_hidden_layers=4, num_attention_heads=4, num_key_value_heads=2,
+                         head_dim=64, partial_rotary_factor=0.25, linear_num_key_heads=2, linear_num_value_heads=4,
+                         linear_key_head_dim=64, linear_value_head_dim=64, linear_conv_kernel_dim=4, vocab_size=512,
+                         intermediate_size=512, rms_norm_eps=1e-6, initializer_range=0.08)
+  hf = Qwen3_5ForCausalLM(ct).eval()
+  sd = {k: v.detach().half().numpy() for k, v in hf.state_dict().items()}
+  cfg, w = hybrid.adapt(ct, sd, prefix="model.")
+  m = llm.LlamaPrefill(cfg, w, compress=compress)
+  prompt = list(np.random.default_rng(5).integers(0, 512, 12))
+  toks = m.generate(prompt, 10, max_len=32)
+  with torch.no_grad():
+    lg = hf(torch.tensor([prompt + toks])).logits[0].float().numpy()
+  ties = 0
+  for i, t in enumerate(toks):
+    ref = lg[len(prompt) - 1 + i]
+    if int(np.argmax(ref)) != t:
+      top = np.sort(ref)[-2:]
+      assert top[1] - ref[t] < 0.05 * np.abs(ref).max(), f"step {i}: device {t} vs transformers {int(np.argmax(ref))}"
+      ties += 1
+  assert ties <= 2
+  m.release()
