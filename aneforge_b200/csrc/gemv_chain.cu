@@ -391,6 +391,11 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_chain_kernel(const 
 namespace {
 
 constexpr size_t CHAIN_HDR = 256;                // done[8] | ready[8] | exits
+// Every chain op of a program shares one scratch buffer, so the counters (which must read zero at
+// the start of every launch) live at the same place for every job slot whatever the chain's shapes:
+// CHAIN_CNT_CAP row-block tickets per job slot, then the partial sums (rewritten before each read)
+constexpr int CHAIN_CNT_CAP = 4096;
+constexpr size_t CHAIN_CNT_BYTES = (size_t)CHAIN_MAX_JOBS * CHAIN_CNT_CAP * 4;
 
 size_t chain_smem(int NB, bool i4) {
   return (size_t)tc::STAGES * (i4 ? tc::STAGE_BYTES4 : tc::STAGE_BYTES) + CHAIN_SH_BYTES +
@@ -443,7 +448,7 @@ size_t align256(size_t n) { return (n + 255) / 256 * 256; }
 // per-job geometry and the scratch layout for a grid of G CTAs; returns the scratch bytes
 size_t chain_layout(GemvChainArgs& a, int G) {
   const int NT = a.NB > 8 ? 2 : 1;
-  size_t off = CHAIN_HDR;
+  size_t off = CHAIN_HDR + CHAIN_CNT_BYTES;
   for (int j = 0; j < a.njobs; ++j) {
     ChainJob& J = a.job[j];
     J.RB = (J.N + 63) / 64;
@@ -456,7 +461,6 @@ size_t chain_layout(GemvChainArgs& a, int G) {
       if (n > maxc) maxc = n;
     }
     J.maxc = maxc;
-    off += align256((size_t)J.RB * 4);
   }
   for (int j = 0; j < a.njobs; ++j) {
     const ChainJob& J = a.job[j];
@@ -471,11 +475,8 @@ void chain_bind(GemvChainArgs& a) {
   a.done = reinterpret_cast<int*>(base);
   a.ready = a.done + CHAIN_MAX_JOBS;
   a.exits = a.ready + CHAIN_MAX_JOBS;
-  size_t off = CHAIN_HDR;
-  for (int j = 0; j < a.njobs; ++j) {
-    a.job[j].cnt = reinterpret_cast<int*>(base + off);
-    off += align256((size_t)a.job[j].RB * 4);
-  }
+  for (int j = 0; j < a.njobs; ++j) a.job[j].cnt = reinterpret_cast<int*>(base + CHAIN_HDR) + (size_t)j * CHAIN_CNT_CAP;
+  size_t off = CHAIN_HDR + CHAIN_CNT_BYTES;
   for (int j = 0; j < a.njobs; ++j) {
     ChainJob& J = a.job[j];
     J.part = reinterpret_cast<float*>(base + off);
@@ -489,6 +490,7 @@ bool chain_valid(const GemvChainArgs& a) {
   for (int j = 0; j < a.njobs; ++j) {
     const ChainJob& J = a.job[j];
     if (J.N <= 0 || J.K <= 0 || J.K % 32 || J.ldx % 8 || J.ldx < J.K || !J.w || !J.x || !J.y) return false;
+    if ((J.N + 63) / 64 > CHAIN_CNT_CAP) return false;
     if ((reinterpret_cast<uintptr_t>(J.w) & 15) || (reinterpret_cast<uintptr_t>(J.x) & 15)) return false;
     if (J.epi < EPI_F32 || J.epi > EPI_SWIGLU) return false;
     if (J.epi == EPI_SWIGLU && J.N % 16) return false;

@@ -7,9 +7,10 @@ final norm, the lm_head and the greedy argmax, replayed as one CUDA graph over a
 KV cache. Weights are random N(0, 0.02) (no checkpoints here), quantized per row to int8 on the
 GPU with the reference's encoder; the prompt is 512 uniform token ids, prefilled before timing.
 
-Under torchrun (N > 1) each rank runs an independent replica of the whole model (weak scaling);
-the timed region is bracketed by a barrier + device sync on every rank and the slowest rank's time
-is reported.
+Under torchrun (N > 1) the model runs tensor parallel over the N GPUs (strong scaling: heads, FFN
+rows and vocabulary split, residual all-reduces over NVLink peer memory; experts split whole for the
+MoE model); `--replicas` runs N independent copies instead (weak scaling). The timed region is
+bracketed by a barrier + device sync on every rank and the slowest rank's time is reported.
 
 `--impl reference` times the reference algorithm's CPU path (the numpy restatement of ANEForge's
 decode driver in `oracle/`, run with every host thread BLAS offers) on the same workload, on a
@@ -38,6 +39,7 @@ MODELS = {
     cfg=dict(dim=4096, n_layers=32, n_heads=32, n_kv_heads=8, ffn_dim=14336, vocab=128256, rope_base=500000.0,
              norm_eps=1e-5),
     compress="int8", prompt=512, qkv_bias=False, traffic_profile="gemv_tc_gate_up_llama8b.md",
+    chain_traffic_profile="gemv_chain_llama8b.md",
     metric="int8 decode tokens/s (Llama-3-8B-shaped, greedy)",
     workload="config 3: Llama-3-8B-shaped int8 per-row greedy decode",
     dtype="int8 weights, fp16 activations, fp32 accumulation"),
@@ -45,6 +47,7 @@ MODELS = {
     cfg=dict(dim=8192, n_layers=80, n_heads=64, n_kv_heads=8, ffn_dim=29568, vocab=152064, rope_base=1e6,
              norm_eps=1e-6),
     compress="int4_g32", prompt=2048, qkv_bias=True, traffic_profile="gemv_tc_i4_gate_up_qwen72b.md",
+    chain_traffic_profile="gemv_chain_i4_qwen72b.md",
     metric="int4 decode tokens/s (Qwen2-72B-shaped, greedy)",
     workload="config 4: Qwen2-72B-shaped group-32 int4 greedy decode",
     dtype="int4 group-32 weights, fp16 activations, fp32 accumulation"),
@@ -247,6 +250,63 @@ def _run_lin(kernels, R, x, lin, y, scr):
     kernels.gemv_tc(x, lin.w, lin.s, lin.N, lin.K, epi=R.EPI_SWIGLU, y=y, scratch=scr)
 
 
+def chain_bytes(pb, kv, NB):
+  """Algorithmic bytes of one `gemv_chain` launch: every job's packed weights, scales and bias,
+  its x rows in, its y rows out (plus the residual read for a residual epilogue), and each norm's
+  fp32 rows in, gamma and fp16 rows out."""
+  total = 0
+  for j in range(int(kv["jobs"])):
+    p = f"j{j}."
+    n, k, epi = int(kv[p + "n"]), int(kv[p + "k"]), kv[p + "epi"]
+    for key in ("w", "s", "b"):
+      if p + key in kv:
+        total += pb.bufs[kv[p + key]].nbytes
+    out = n // 2 if epi == "swiglu" else n
+    total += NB * k * 2 + NB * out * (2 if epi in ("swiglu", "f16") else 4) + (NB * n * 4 if epi == "resid" else 0)
+    if p + "nd" in kv:
+      d = int(kv[p + "nd"])
+      total += NB * d * 4 + d * 2 + NB * d * 2
+  return total
+
+
+def time_chains(m, dec, NB, reps=4):
+  """The decode step's `gemv_chain` launches (o, norm, gate|up, down, norm, next qkv of every layer)
+  replayed alone as one program on its own stream, timed with CUDA events: (us per launch,
+  algorithmic bytes per launch). The layers' weights (several GB, above L2) stream from HBM."""
+  import torch
+  from aneforge_b200 import _runtime as R
+  from aneforge_b200.plan import PlanBuilder
+  pb = dec["plan"]
+  ops = [(k, kv) for k, kv in pb.ops if k == "gemv_chain"]
+  if not ops:
+    return None
+  # the layers' weights (bound below), the chain's own buffers and the final norm; not the embedding,
+  # head or rope tables of the decode program
+  keep = {n: b for n, b in pb.bufs.items() if b.role != "weight" or n.startswith("L") or n == "final_g"}
+  sub = PlanBuilder(bufs=keep, ops=list(ops))
+  prog = R.Program.from_text(sub.text(), {}, {}, m.device)
+  d = m._load()
+  for li in range(m.cfg.n_layers):
+    m._bind_layer(prog, li, d["layers"][li])
+  prog.bind("final_g", d["final_g"])
+  for _ in range(2):
+    prog.execute_async()
+  prog.sync()
+  stream = torch.cuda.ExternalStream(prog.stream(), device=torch.device("cuda", m.device))
+  e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+  e0.record(stream)
+  for _ in range(reps):
+    prog.execute_async()
+  e1.record(stream)
+  prog.sync()
+  torch.cuda.synchronize()
+  us = e0.elapsed_time(e1) * 1e3 / (reps * len(ops))
+  nbytes = sum(chain_bytes(pb, kv, NB) for _, kv in ops) / len(ops)
+  del stream
+  prog.release()
+  return us, nbytes
+
+
 def run_b200(args):
   import torch
   import torch.distributed as dist
@@ -371,12 +431,33 @@ def run_b200(args):
   k_us = k0.elapsed_time(k1) * 1e3 / reps
   del kgraph
   gu_bytes = gu[0].nbytes + NB * cfg.dim * 2 + NB * cfg.ffn_dim * 2
+  chain = time_chains(m, dec, NB)
   peak, peak_kind = _peaks()
   step_bytes = algorithmic_bytes_per_step(cfg, NB, PROMPT + args.warmup + args.steps // 2, spec["compress"],
                                           spec["qkv_bias"], spec.get("moe_compress"))
   result = None
   if rank == 0:
     achieved = gu_bytes / (k_us * 1e-6) / 1e9
+    peak_note = f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback"
+    gate_up = {"kernel": f"gemv_tc {gu[0].kind} gate|up + silu*mul ({gu[0].N}x{gu[0].K}, mma.sync)",
+               "achieved": round(achieved, 1), "frac": round(achieved / peak, 4), "launch_us": round(k_us, 2),
+               "algorithmic_bytes": gu_bytes}
+    if chain is not None:
+      c_us, c_bytes = chain
+      c_ach = c_bytes / (c_us * 1e-6) / 1e9
+      roofline = {"bound": "hbm", "kernel": "gemv_chain_kernel: o, rmsnorm, gate|up, down, rmsnorm, next qkv "
+                                            "(one persistent launch per layer, mma.sync)",
+                  "achieved": round(c_ach, 1), "peak": peak, "unit": "GB/s", "frac": round(c_ach / peak, 4),
+                  "traffic": profile_traffic(spec.get("chain_traffic_profile", "")),
+                  "traffic_source": f"ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/{spec.get('chain_traffic_profile')}",
+                  "peak_kind": peak_note, "launch_us": round(c_us, 2), "algorithmic_bytes": int(c_bytes),
+                  "how": "the step's chain launches replayed alone as one program, CUDA events on its stream",
+                  "gate_up_alone": gate_up}
+    else:
+      roofline = {"bound": "hbm", "kernel": gate_up["kernel"], "achieved": gate_up["achieved"], "peak": peak,
+                  "unit": "GB/s", "frac": gate_up["frac"], "traffic": profile_traffic(spec["traffic_profile"]),
+                  "traffic_source": f"ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/{spec['traffic_profile']}",
+                  "peak_kind": peak_note, "launch_us": gate_up["launch_us"], "algorithmic_bytes": gu_bytes}
     result = {
       "metric": METRIC, "value": round(tok_s, 2), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
       "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
@@ -386,12 +467,7 @@ def run_b200(args):
       "e2e": {"value": round(e2e_tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * NB,
               "d2h_bytes_per_step": 4 * NB,
               "how": "program API, pinned host token ids in/out every step, host sync per step"},
-      "roofline": {"bound": "hbm", "kernel": f"gemv_tc {gu[0].kind} gate|up + silu*mul ({gu[0].N}x{gu[0].K}, mma.sync)",
-                   "achieved": round(achieved, 1),
-                   "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": profile_traffic(spec["traffic_profile"]),
-                   "traffic_source": f"ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/{spec['traffic_profile']}",
-                   "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
-                   "launch_us": round(k_us, 2), "algorithmic_bytes": gu_bytes},
+      "roofline": roofline,
       "step_roofline": {"algorithmic_bytes": int(step_bytes), "achieved_gbs": round(step_bytes / (ms_step * 1e-3) / 1e9, 1),
                         "frac": round(step_bytes / (ms_step * 1e-3) / 1e9 / peak / (ws if tp else 1), 4),
                         "per": "GPU (the model's bytes are split over the tensor-parallel ranks)" if tp else "GPU"},
@@ -498,6 +574,26 @@ def kernel_bench(name, reps, warmup):
     return {"kernel": name, "what": f"prefill program, {MODEL} {spec['compress']}, {nl} layers, {PROMPT} tokens",
             "ms_per_prefill": round(ms, 3), "tokens_per_s": round(PROMPT / (ms * 1e-3), 1),
             "tflops": round((lin + att) / (ms * 1e-3) / 1e12, 1), "reps": reps, "warmup": warmup}
+
+  if name == "chain":
+    # the decode step's chained GEMV launch (o, norm, gate|up, down, norm, next qkv) of a 4-layer
+    # model of the selected shape with a 4096-token vocabulary: ~0.9 GB of layer weights for the
+    # 8B shape, above L2; the small case for captures of gemv_chain_kernel
+    from aneforge_b200 import llm as L
+    spec = MODELS[MODEL]
+    cd = dict(CFG, n_layers=4, vocab=4096)
+    cfg = L.LlamaConfig(**cd, layers=[L.LayerSpec() for _ in range(4)])
+    w = make_weights(cfg, dev, seed=1234, qkv_bias=spec["qkv_bias"])
+    m = L.LlamaPrefill(cfg, w, compress=spec["compress"], device=0)
+    m._load()
+    del w
+    dec = m._decoder(PROMPT + 64, 1)
+    us, nbytes = time_chains(m, dec, 1, reps=max(reps // 4, 2))
+    peak, _ = _peaks()
+    m.release()
+    return {"kernel": name, "what": f"gemv_chain {MODEL} {spec['compress']}: o, norm, gate|up, down, norm, next qkv",
+            "us_per_launch": round(us, 2), "algorithmic_bytes": int(nbytes),
+            "gbs": round(nbytes / (us * 1e-6) / 1e9, 1), "frac": round(nbytes / (us * 1e-6) / 1e9 / peak, 4)}
 
   def int8_tiles(N, Kd, copies):
     W = (torch.randn(N, Kd, generator=g, device=dev) * 0.02).half()
@@ -676,7 +772,7 @@ def timeline(args):
               key=lambda e: e.time_range.start)
   per = len(ev) // 3
   step = ev[per:2 * per]                                   # the middle step
-  kinds = {"gemv_tc_kernel<1, 0": "qkv (f32 epi)", "gemv_tc_kernel<1, 2": "o / down (resid epi)",
+  kinds = {"gemv_chain_kernel": "chain (o, norm, gate|up, down, norm, next qkv)", "gemv_tc_kernel<1, 0": "qkv (f32 epi)", "gemv_tc_kernel<1, 2": "o / down (resid epi)",
            "gemv_tc_kernel<1, 3": "gate|up (swiglu epi)", "attn_decode": "attention", "rmsnorm": "rmsnorm",
            "gemv_kernel": "lm_head + argmax", "embed": "embed", "moe_gate": "moe gate", "lm_head_tc": "lm_head (tensor pipe)"}
   share, busy, count = collections.defaultdict(float), collections.defaultdict(float), collections.Counter()
@@ -775,7 +871,7 @@ def main():
                   help="time one kernel alone: gemv_gu | gemv_qkv | gemv_o | gemv_down | gemv_cfg1 | attn | lm_head "
                        "| gemv_i4_gu | gemv_i4_qkv | gemv_i4_o | gemv_i4_down | gemv_i4_moe_gu | gemm_gu | gemm_i4_gu "
                        "| gemm_qkv | gemm_o | gemm_down "
-                       "| rmsnorm | moe_gate | prefill (the whole prefill program of --model) | prefill_1layer")
+                       "| rmsnorm | moe_gate | prefill (the whole prefill program of --model) | prefill_1layer | chain")
   ap.add_argument("--reps", type=int, default=50)
   ap.add_argument("--timeline", action="store_true",
                   help="print the kernel timeline of decode-step graph replays (CUPTI through torch.profiler)")
