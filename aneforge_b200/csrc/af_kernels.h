@@ -137,6 +137,7 @@ struct GemvChainArgs {
   int* done = nullptr;              // [njobs] row blocks finished
   int* ready = nullptr;             // [njobs] job (and its norm) complete
   int* exits = nullptr;             // CTAs finished
+  int nstages = 6;                  // weight ring depth
 };
 cudaError_t gemv_chain_launch(GemvChainArgs a, cudaStream_t st, bool pdl);
 size_t gemv_chain_scratch_bytes(const GemvChainArgs& a);

@@ -18,7 +18,7 @@
 // (deterministic) and runs the epilogue. Nobody waits for a partial.
 //
 // Job boundaries. The CTA that finishes a job's last row block runs the job's RMSNorm (if any) and
-// then publishes the job as ready (release); a second producer thread per CTA waits (bounded, with
+// then publishes the job as ready (release); a second producer thread per CTA (its own warp) waits (bounded, with
 // acquire) for the previous job to be ready before it copies the next job's x chunks into the x
 // ring. Counters are reset by the CTA that last uses them, so the launch can be replayed.
 //
@@ -37,18 +37,19 @@ namespace af {
 
 namespace {
 
+constexpr int CHAIN_MAX_STAGES = 12;          // weight ring depth: 6 at 4 CTAs per SM, 12 at 2
 constexpr long long FLAG_LIMIT = 1ll << 21;     // ~1 s of L2 polls with 32 ns sleeps
 
 struct ChainShared {
-  uint64_t full[tc::STAGES];
-  uint64_t empty[tc::STAGES];
+  uint64_t full[CHAIN_MAX_STAGES];
+  uint64_t empty[CHAIN_MAX_STAGES];
   uint64_t xfull[tc::XSLOTS];
   uint64_t xempty[tc::XSLOTS];
   int cabort;        // a consumer gave up (written by consumers, read after a consumer barrier)
   int bcast;         // thread 0's ticket result for the other consumer threads
   float nsum[8];     // per-warp partial sums of the RMSNorm tail
 };
-constexpr int CHAIN_SH_BYTES = 256;
+constexpr int CHAIN_SH_BYTES = 512;
 static_assert(sizeof(ChainShared) <= CHAIN_SH_BYTES, "ChainShared grew past its slot");
 
 // the epilogue of one 16-row tile of job J (rows rt*16 + g and + 8, batch columns of this lane)
@@ -85,16 +86,41 @@ AF_DEV void chain_epilogue(const ChainJob& J, int NB, const float (&acc)[NT][4],
   }
 }
 
-// the job's RMSNorm on this CTA's NT threads (the rmsnorm kernel's formula: x / max(|x|, floor) * g)
+// the job's RMSNorm on this CTA's consumer threads (the rmsnorm kernel's formula:
+// x / max(|x|, floor) * g). It sits on the chain's critical path (every CTA waits for it), so each
+// thread keeps NL independent 16-byte loads in flight instead of one L2 round trip per element.
 template <int CW>
 AF_DEV void chain_norm(const ChainJob& J, int NB, ChainShared* sh) {
+  constexpr int NL = 4;
   const int tid = threadIdx.x, nthr = CW * 32, warp = tid >> 5, lane = tid & 31;
+  const bool vec = (J.nd % 4) == 0 && (J.ldnx % 4) == 0 && (J.ldno % 4) == 0 &&
+                   (reinterpret_cast<uintptr_t>(J.nx) & 15) == 0 && (reinterpret_cast<uintptr_t>(J.nout) & 7) == 0 &&
+                   (reinterpret_cast<uintptr_t>(J.ng) & 7) == 0;
+  const int n4 = J.nd / 4;
   for (int b = 0; b < NB; ++b) {
     const float* x = J.nx + (size_t)b * J.ldnx;
+    __half* out = J.nout + (size_t)b * J.ldno;
     float ss = 0.f;
-    for (int i = tid; i < J.nd; i += nthr) {
-      const float v = __ldcg(x + i);
-      ss = fmaf(v, v, ss);
+    if (vec) {
+      const float4* x4 = reinterpret_cast<const float4*>(x);
+      for (int i0 = tid; i0 < n4; i0 += nthr * NL) {
+        float4 v[NL];
+#pragma unroll
+        for (int u = 0; u < NL; ++u) {
+          const int i = i0 + u * nthr;
+          v[u] = i < n4 ? __ldcg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < NL; ++u) {
+          ss = fmaf(v[u].x, v[u].x, ss); ss = fmaf(v[u].y, v[u].y, ss);
+          ss = fmaf(v[u].z, v[u].z, ss); ss = fmaf(v[u].w, v[u].w, ss);
+        }
+      }
+    } else {
+      for (int i = tid; i < J.nd; i += nthr) {
+        const float v = __ldcg(x + i);
+        ss = fmaf(v, v, ss);
+      }
     }
     ss = warp_sum(ss);
     if (lane == 0) sh->nsum[warp] = ss;
@@ -103,8 +129,33 @@ AF_DEV void chain_norm(const ChainJob& J, int NB, ChainShared* sh) {
 #pragma unroll
     for (int w = 0; w < CW; ++w) tot += sh->nsum[w];
     const float sn = fmaxf(sqrtf(tot), J.nfloor);
-    __half* out = J.nout + (size_t)b * J.ldno;
-    for (int i = tid; i < J.nd; i += nthr) out[i] = f2h(__fdiv_rn(__ldcg(x + i), sn) * h2f(J.ng[i]));
+    if (vec) {
+      const float4* x4 = reinterpret_cast<const float4*>(x);
+      const uint2* g4 = reinterpret_cast<const uint2*>(J.ng);
+      uint2* o4 = reinterpret_cast<uint2*>(out);
+      for (int i0 = tid; i0 < n4; i0 += nthr * NL) {
+        float4 v[NL];
+        uint2 gv[NL];
+#pragma unroll
+        for (int u = 0; u < NL; ++u) {
+          const int i = i0 + u * nthr;
+          if (i < n4) { v[u] = __ldcg(x4 + i); gv[u] = __ldg(g4 + i); }
+        }
+#pragma unroll
+        for (int u = 0; u < NL; ++u) {
+          const int i = i0 + u * nthr;
+          if (i >= n4) continue;
+          const __half2* g2 = reinterpret_cast<const __half2*>(&gv[u]);
+          const float2 ga = __half22float2(g2[0]), gb = __half22float2(g2[1]);
+          __half2 r[2];
+          r[0] = __halves2half2(f2h(__fdiv_rn(v[u].x, sn) * ga.x), f2h(__fdiv_rn(v[u].y, sn) * ga.y));
+          r[1] = __halves2half2(f2h(__fdiv_rn(v[u].z, sn) * gb.x), f2h(__fdiv_rn(v[u].w, sn) * gb.y));
+          o4[i] = *reinterpret_cast<const uint2*>(r);
+        }
+      }
+    } else {
+      for (int i = tid; i < J.nd; i += nthr) out[i] = f2h(__fdiv_rn(__ldcg(x + i), sn) * h2f(J.ng[i]));
+    }
     consumer_sync_n<CW>();           // nsum is reused by the next row
   }
 }
@@ -112,6 +163,15 @@ AF_DEV void chain_norm(const ChainJob& J, int NB, ChainShared* sh) {
 // CTAs that work on job J: all G, or one per unit when the job has fewer units than CTAs (every
 // working CTA then has a non-empty range, so a row block's pieces are exactly CTAs cf..cl)
 AF_HD int job_grid(const ChainJob& J, int G) { return J.U < (long long)G ? (int)J.U : G; }
+
+// a ticket: release orders this CTA's earlier writes (made CTA-wide by the barrier before it) ahead of
+// the count, acquire makes the writes of the CTAs counted before visible (to the CTA after the
+// barrier that follows); no full memory barrier per thread
+AF_DEV int ticket(int* p) {
+  int r;
+  asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(r) : "l"(p) : "memory");
+  return r;
+}
 
 AF_DEV bool wait_flag(const int* f) {
   SpinBudget budget;
@@ -126,23 +186,31 @@ AF_DEV bool wait_flag(const int* f) {
 
 }  // namespace
 
+// consumer warps, then the weight producer's warp, then the x producer's warp (each producer is one
+// thread of a warp of its own, so that neither waits behind the other's spins)
+template <bool I4> struct ChainThreads {
+  static constexpr int n = (Cw<I4>::n + 2) * 32;
+  static constexpr int min_ctas = I4 ? 3 : 4;     // resident CTAs per SM the register budget keeps
+};
+
 template <int NT, bool I4>
-__global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_chain_kernel(const __grid_constant__ GemvChainArgs a) {
+__global__ void __launch_bounds__(ChainThreads<I4>::n, ChainThreads<I4>::min_ctas) gemv_chain_kernel(const __grid_constant__ GemvChainArgs a) {
   constexpr int CW = Cw<I4>::n;
   using F = tc::Fmt<I4>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   unsigned char* ring = smem_raw;                                          // [STAGES][F::stage]
-  ChainShared* sh = reinterpret_cast<ChainShared*>(smem_raw + tc::STAGES * F::stage);
-  __half* xring = reinterpret_cast<__half*>(smem_raw + tc::STAGES * F::stage + CHAIN_SH_BYTES);
+  const int NS = a.nstages;                                               // weight ring depth
+  ChainShared* sh = reinterpret_cast<ChainShared*>(smem_raw + NS * F::stage);
+  __half* xring = reinterpret_cast<__half*>(smem_raw + NS * F::stage + CHAIN_SH_BYTES);
   const int NB = a.NB;
   const int xslot_halves = NB * tc::XSTRIDE;
-  float* red = reinterpret_cast<float*>(smem_raw + tc::STAGES * F::stage + CHAIN_SH_BYTES +
+  float* red = reinterpret_cast<float*>(smem_raw + NS * F::stage + CHAIN_SH_BYTES +
                                         (size_t)tc::XSLOTS * xslot_halves * 2);   // [4][32][NT*4]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x, c = blockIdx.x;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < tc::STAGES; ++s) {
+    for (int s = 0; s < NS; ++s) {
       mbar_init(&sh->full[s], 1);
       mbar_init(&sh->empty[s], CW);
     }
@@ -155,8 +223,8 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_chain_kernel(const 
   }
   __syncthreads();
 
-  if (warp == CW) {
-    if (lane == 0) {
+  if (warp >= CW) {
+    if (warp == CW && lane == 0) {
       // ---------------------------------------------------------- weight producer: every job's
       // weights back to back, never waiting for data (the weights are constant)
       const uint64_t pol = a.evict_first ? l2_evict_first_policy() : 0;
@@ -181,7 +249,7 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_chain_kernel(const 
               bulk_w(ring + (size_t)stage * F::stage, W + ((size_t)rb * J.KT + kt) * F::unit, nk * F::unit,
                      &sh->full[stage], a.evict_first, pol);
               ++issued;
-              if (++stage == tc::STAGES) { stage = 0; phase ^= 1; }
+              if (++stage == NS) { stage = 0; phase ^= 1; }
             }
           }
           u += ktb - kta;
@@ -189,12 +257,12 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_chain_kernel(const 
       }
       if (!ok) af_set_err(a.err, AF_DEV_WAIT_TIMEOUT);
       // the ring must outlive every copy issued: wait (bounded) for the last ones to land
-      const int tail = issued < tc::STAGES ? issued : tc::STAGES;
+      const int tail = issued < NS ? issued : NS;
       for (int i = 0; i < tail; ++i) {
-        if (--stage < 0) { stage = tc::STAGES - 1; phase ^= 1; }
+        if (--stage < 0) { stage = NS - 1; phase ^= 1; }
         mbar_wait(&sh->full[stage], phase);
       }
-    } else if (lane == 1) {
+    } else if (warp == CW + 1 && lane == 0) {
       // ---------------------------------------------------------- x producer: a job's input rows
       // once the previous job (and its norm) is complete
       int xs = 0, issued = 0;
@@ -285,7 +353,7 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_chain_kernel(const 
                                         lane, rtw, par, acc, acc2);
           __syncwarp();
           if (lane == 0) mbar_arrive(&sh->empty[stage]);
-          if (++stage == tc::STAGES) { stage = 0; phase ^= 1; }
+          if (++stage == NS) { stage = 0; phase ^= 1; }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh->xempty[xs]);
@@ -333,28 +401,36 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_chain_kernel(const 
             __stcg(reinterpret_cast<float2*>(slot + (size_t)r0 * NBP + c0), make_float2(acc[n][0], acc[n][1]));
             __stcg(reinterpret_cast<float2*>(slot + (size_t)r1 * NBP + c0), make_float2(acc[n][2], acc[n][3]));
           }
-          __threadfence();
         }
         consumer_sync_n<CW>();
-        if (threadIdx.x == 0) sh->bcast = atomicAdd(J.cnt + rb, 1);
+        if (threadIdx.x == 0) sh->bcast = ticket(J.cnt + rb);
         consumer_sync_n<CW>();
         if (sh->bcast == nc - 1) {
-          __threadfence();
           if (!par) {
             float s[NT][4];
 #pragma unroll
             for (int n = 0; n < NT; ++n)
 #pragma unroll
               for (int q = 0; q < 4; ++q) s[n][q] = 0.f;
-            for (int p = 0; p < nc; ++p) {            // piece order: deterministic
-              const float* sp = J.part + (((size_t)rb * J.maxc + p) * 64) * NBP;
+            // the pieces in order (deterministic), two pieces' loads in flight at a time
+            for (int p0 = 0; p0 < nc; p0 += 2) {
 #pragma unroll
               for (int n = 0; n < NT; ++n) {
                 const int c0 = n * 8 + 2 * t;
                 if (c0 >= NB) continue;
-                const float2 p0 = __ldcg(reinterpret_cast<const float2*>(sp + (size_t)r0 * NBP + c0));
-                const float2 p1 = __ldcg(reinterpret_cast<const float2*>(sp + (size_t)r1 * NBP + c0));
-                s[n][0] += p0.x; s[n][1] += p0.y; s[n][2] += p1.x; s[n][3] += p1.y;
+                float2 q0[2], q1[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                  if (p0 + u >= nc) break;
+                  const float* sp = J.part + (((size_t)rb * J.maxc + p0 + u) * 64) * NBP;
+                  q0[u] = __ldcg(reinterpret_cast<const float2*>(sp + (size_t)r0 * NBP + c0));
+                  q1[u] = __ldcg(reinterpret_cast<const float2*>(sp + (size_t)r1 * NBP + c0));
+                }
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                  if (p0 + u >= nc) break;
+                  s[n][0] += q0[u].x; s[n][1] += q0[u].y; s[n][2] += q1[u].x; s[n][3] += q1[u].y;
+                }
               }
             }
             chain_epilogue<NT, I4>(J, NB, s, rt, g, t);
@@ -364,15 +440,12 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_chain_kernel(const 
         }
       }
       if (finished) {
-        __threadfence();                     // this row block's outputs before its count
-        consumer_sync_n<CW>();
-        if (threadIdx.x == 0) sh->bcast = atomicAdd(a.done + j, 1);
+        consumer_sync_n<CW>();               // this row block's outputs before its count
+        if (threadIdx.x == 0) sh->bcast = ticket(a.done + j);
         consumer_sync_n<CW>();
         if (sh->bcast == J.RB - 1) {
           // the job's last row block: its norm, then the job is ready for the next one
-          __threadfence();
           if (J.nd) chain_norm<CW>(J, NB, sh);
-          __threadfence();
           consumer_sync_n<CW>();
           if (threadIdx.x == 0) {
             a.done[j] = 0;
@@ -397,8 +470,15 @@ constexpr size_t CHAIN_HDR = 256;                // done[8] | ready[8] | exits
 constexpr int CHAIN_CNT_CAP = 4096;
 constexpr size_t CHAIN_CNT_BYTES = (size_t)CHAIN_MAX_JOBS * CHAIN_CNT_CAP * 4;
 
+// CTAs per SM the chain is sized for (env AF_CHAIN_CTAS_PER_SM: 4 with a 6-stage ring, or 2 with 12)
+int chain_ctas_per_sm() {
+  static const int v = env_int("AF_CHAIN_CTAS_PER_SM", 4) <= 2 ? 2 : 4;
+  return v;
+}
+int chain_stages() { return chain_ctas_per_sm() == 2 ? CHAIN_MAX_STAGES : 6; }
+
 size_t chain_smem(int NB, bool i4) {
-  return (size_t)tc::STAGES * (i4 ? tc::STAGE_BYTES4 : tc::STAGE_BYTES) + CHAIN_SH_BYTES +
+  return (size_t)chain_stages() * (i4 ? tc::STAGE_BYTES4 : tc::STAGE_BYTES) + CHAIN_SH_BYTES +
          (size_t)tc::XSLOTS * NB * tc::XSTRIDE * 2 + tc::WARPS * 32 * 8 * 4;
 }
 
@@ -418,12 +498,12 @@ int chain_grid(int NB) {
   const int per_sm = occ.get(NB, [NB] {
     if (chain_attrs<NT, I4>() != cudaSuccess) { cudaGetLastError(); return 0; }
     int o = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, gemv_chain_kernel<NT, I4>, (Cw<I4>::n + 1) * 32,
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, gemv_chain_kernel<NT, I4>, ChainThreads<I4>::n,
                                                       chain_smem(NB, I4)) != cudaSuccess) {
       cudaGetLastError();
       o = 0;
     }
-    const int cap = env_int("AF_CHAIN_CTAS_PER_SM", 4);
+    const int cap = chain_ctas_per_sm();
     return o < cap ? o : cap;
   });
   return per_sm * device_attr(cudaDevAttrMultiProcessorCount, 148);
@@ -506,7 +586,7 @@ cudaError_t launch_chain(const GemvChainArgs& a, int G, cudaStream_t st, bool pd
   if (ae != cudaSuccess) return ae;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G);
-  cfg.blockDim = dim3((Cw<I4>::n + 1) * 32);
+  cfg.blockDim = dim3(ChainThreads<I4>::n);
   cfg.dynamicSmemBytes = chain_smem(a.NB, I4);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -534,6 +614,7 @@ cudaError_t gemv_chain_launch(GemvChainArgs a, cudaStream_t st, bool pdl) {
   const size_t need = chain_layout(a, G);
   if (!a.scratch || a.scratch_bytes < need) return cudaErrorInvalidValue;
   chain_bind(a);
+  a.nstages = chain_stages();
   const bool two = a.NB > 8;
   cudaError_t e = i4 ? (two ? launch_chain<2, true>(a, G, st, pdl) : launch_chain<1, true>(a, G, st, pdl))
                      : (two ? launch_chain<2, false>(a, G, st, pdl) : launch_chain<1, false>(a, G, st, pdl));

@@ -542,9 +542,7 @@ void gemv_tc_plan(int N, int K, int NB, int* S_out, int* nt_out) {
   *nt_out = NB <= 8 ? 1 : 2;
 }
 
-size_t gemv_tc_scratch_bytes(int N, int K, int NB) {
-  // enough for either weight format and every epilogue (the grid may differ with shared memory)
-  const int nb = NB > 16 ? 16 : NB;
+static size_t scratch_for_slice(int N, int K, int nb) {
   int G = 0, maxc = 0, maxc4 = 0, cs = 0;
   plan_geometry(N, K, nb, EPI_F32, false, &G, &maxc, &cs, false);
   plan_geometry(N, K, nb, EPI_F32, true, &G, &maxc4, &cs, false);
@@ -552,6 +550,15 @@ size_t gemv_tc_scratch_bytes(int N, int K, int NB) {
   const int NT = nb <= 8 ? 1 : 2;
   const size_t RB = (N + 63) / 64;
   return tc::CNT_BYTES + RB * maxc * 64 * NT * 8 * 4;
+}
+
+size_t gemv_tc_scratch_bytes(int N, int K, int NB) {
+  // enough for either weight format and every epilogue (the grid may differ with shared memory);
+  // a batch above 16 runs as 16-row slices and a remainder, whose grid (and so its split) differs
+  if (NB <= 16) return scratch_for_slice(N, K, NB);
+  const size_t full = scratch_for_slice(N, K, 16);
+  const size_t rest = NB % 16 ? scratch_for_slice(N, K, NB % 16) : 0;
+  return full > rest ? full : rest;
 }
 
 template <int NT, int EPI, bool I4>

@@ -715,7 +715,11 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     why = "unknown op kind '" + op.kind + "'";
     return cudaErrorInvalidValue;
   }
-  if (e != cudaSuccess) why = std::string("launch failed: ") + cudaGetErrorString(e);
+  if (e != cudaSuccess) {
+    why = std::string("launch failed: ") + cudaGetErrorString(e) + " [";
+    for (const auto& kv : op.kv) why += " " + kv.first + "=" + kv.second;
+    why += " ]";
+  }
   return e;
 }
 

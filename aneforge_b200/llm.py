@@ -288,10 +288,12 @@ def plan_gemv_chains(pb, enable=None):
   `gemv_chain` ops: one persistent launch per run whose CTAs stream every job's weights back to
   back (csrc/gemv_chain.cu). In a decode step the runs are o -> norm -> gate|up -> down -> norm ->
   next qkv, broken by each attention. Same results as the separate launches up to the fp32
-  summation order of split row blocks. Env AF_GEMV_CHAIN=0 keeps the separate launches."""
+  summation order of split row blocks. Off by default (env AF_GEMV_CHAIN=1 turns it on): on B200
+  the chain's split-K reductions through L2 and its per-job barrier make a layer's chain slower
+  than the separate cluster-reduced launches (91 against ~60 us at Llama-3-8B shapes)."""
   import ctypes
   if enable is None:
-    enable = os.environ.get("AF_GEMV_CHAIN", "1") != "0"
+    enable = os.environ.get("AF_GEMV_CHAIN", "0") == "1"
   if not enable:
     return
   lib = R.load_library()
