@@ -46,14 +46,15 @@ def test_qwen35_hybrid_decodes_like_transformers(compress):
                          head_dim=64, partial_rotary_factor=0.25, linear_num_key_heads=2, linear_num_value_heads=4,
                          linear_key_head_dim=64, linear_value_head_dim=64, linear_conv_kernel_dim=4, vocab_size=512,
                          intermediate_size=512, rms_norm_eps=1e-6, initializer_range=0.08)
-  hf = Qwen3_5ForCausalLM(ct).eval()
-  sd = {k: v.detach().half().numpy() for k, v in hf.state_dict().items()}
+  with torch.device("cpu"):                                # the reference model runs on the host
+    hf = Qwen3_5ForCausalLM(ct).eval().cpu()
+  sd = {k: v.detach().cpu().half().numpy() for k, v in hf.state_dict().items()}
   cfg, w = hybrid.adapt(ct, sd, prefix="model.")
   m = llm.LlamaPrefill(cfg, w, compress=compress)
   prompt = list(np.random.default_rng(5).integers(0, 512, 12))
   toks = m.generate(prompt, 10, max_len=32)
   with torch.no_grad():
-    lg = hf(torch.tensor([prompt + toks])).logits[0].float().numpy()
+    lg = hf(torch.tensor([prompt + toks], device="cpu")).logits[0].float().cpu().numpy()
   ties = 0
   for i, t in enumerate(toks):
     ref = lg[len(prompt) - 1 + i]
