@@ -232,6 +232,8 @@ cudaError_t moe_gate_launch(const float* logits, int ld, int NB, int E, int k, i
 
 // ---- tensor parallel (comm.cu): collectives on a program's stream, cross-rank argmax, residual add
 // dst = sum over the ranks of src; with `addto`, addto += that sum instead (dst then scratch)
+cudaError_t comm_all_reduce_rms_f32(void* comm, const float* src, float* tmp, float* h, int NB, int D, const __half* g,
+                                    float floor, __half* out, cudaStream_t st, std::string& why, int* err, bool pdl);
 cudaError_t comm_all_reduce_f32(void* comm, const float* src, float* dst, size_t n, cudaStream_t st, std::string& why,
                                 int* err = nullptr, float* addto = nullptr, bool pdl = false);
 cudaError_t comm_all_gather_i32(void* comm, const int* src, int* dst, size_t n, cudaStream_t st, std::string& why);

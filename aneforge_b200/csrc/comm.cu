@@ -160,6 +160,90 @@ cudaError_t comm_all_reduce_f32(void* comm, const float* src, float* dst, size_t
   return addto ? add_f32_launch(addto, dst, n, st) : cudaSuccess;
 }
 
+// The residual all-reduce fused with the RMSNorm that reads the residual next (a tensor-parallel
+// decode step's o / down projections): h += the ranks' partials summed in rank order (the protocol
+// of p2p_all_reduce_kernel), then out = fp16(h / max(|h|, floor) * g) per row with the rmsnorm
+// kernel's formula. One launch and one boundary instead of two; every rank computes the same bits.
+__global__ void __launch_bounds__(1024) p2p_all_reduce_rms_kernel(P2pPeers peers, int T, int rank, size_t cap,
+                                                                   const float* src, float* h, int NB, int D,
+                                                                   const __half* g, float floor, __half* out, int* err) {
+  char* mine = peers.base[rank];
+  unsigned* epoch = reinterpret_cast<unsigned*>(mine + p2p_epoch_off(T, cap));
+  __shared__ float red[32];
+  pdl_wait();
+  const unsigned e = *reinterpret_cast<volatile unsigned*>(epoch) + 1u;
+  const int set = (int)(e & 1u);
+  const int n = NB * D;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const unsigned long long w = ((unsigned long long)e << 32) | __float_as_uint(__ldcg(src + i));
+    for (int p = 0; p < T; ++p) {
+      unsigned long long* d = reinterpret_cast<unsigned long long*>(peers.base[p] + p2p_data_off(set, rank, T, cap)) + i;
+      asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(d), "l"(w) : "memory");
+    }
+  }
+  bool late = false;
+  for (int b = 0; b < NB; ++b) {
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) {
+      const int idx = b * D + i;
+      float acc = 0.f;
+      for (int s = 0; s < T; ++s) {
+        const unsigned long long* w = reinterpret_cast<const unsigned long long*>(mine + p2p_data_off(set, s, T, cap)) + idx;
+        unsigned long long v = 0;
+        bool in = false;
+        for (long long k = 0; k < P2P_SPIN && !in; ++k) {
+          asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(w) : "memory");
+          in = (unsigned)(v >> 32) == e;
+        }
+        late |= !in;
+        acc += __uint_as_float((unsigned)(v & 0xffffffffull));
+      }
+      const float hv = h[idx] + acc;
+      h[idx] = hv;
+      ss = fmaf(hv, hv, ss);
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int wv = 0; wv < (int)(blockDim.x >> 5); ++wv) tot += red[wv];
+    const float sn = fmaxf(sqrtf(tot), floor);
+    for (int i = threadIdx.x; i < D; i += blockDim.x)      // the h values this thread just wrote
+      out[(size_t)b * D + i] = f2h(__fdiv_rn(h[(size_t)b * D + i], sn) * h2f(g[i]));
+    __syncthreads();                                       // red is reused by the next row
+  }
+  if (late) af_set_err(err, AF_DEV_WAIT_TIMEOUT);
+  __syncthreads();
+  if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(epoch) = e;
+  pdl_trigger();
+}
+
+cudaError_t comm_all_reduce_rms_f32(void* comm, const float* src, float* tmp, float* h, int NB, int D, const __half* g,
+                                    float floor, __half* out, cudaStream_t st, std::string& why, int* err, bool pdl) {
+  Comm* c = static_cast<Comm*>(comm);
+  if (!c) { why = "no communicator"; return cudaErrorInvalidValue; }
+  const size_t n = (size_t)NB * D;
+  if (c->p2p && n <= c->cap) {
+    P2pPeers peers;
+    for (int r = 0; r < P2P_MAX_RANKS; ++r) peers.base[r] = r < c->nranks ? c->peer[r] : nullptr;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(D >= 1024 ? 1024 : (D + 31) / 32 * 32);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, p2p_all_reduce_rms_kernel, peers, c->nranks, c->rank, c->cap, src, h, NB, D, g,
+                              floor, out, err);
+  }
+  // NCCL: the all-reduce (added into h), then the norm
+  cudaError_t e = comm_all_reduce_f32(comm, src, tmp, n, st, why, err, h, false);
+  if (e != cudaSuccess) return e;
+  return rmsnorm_launch(h, 0, D, g, floor, out, D, NB, D, st, false, L2Pf());
+}
+
 cudaError_t comm_all_gather_i32(void* comm, const int* src, int* dst, size_t n, cudaStream_t st, std::string& why) {
   Comm* c = static_cast<Comm*>(comm);
   if (!c || !g_nccl.ok) { why = "no communicator"; return cudaErrorInvalidValue; }

@@ -677,6 +677,23 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
               : comm_all_gather_i32(p.comm, (const int*)src, (int*)dst, n, st, why);
       if (e != cudaSuccess) return e;
     }
+  } else if (op.kind == "allreduce_rms") {
+    // tensor parallel: h += sum over the ranks of src, then out = rmsnorm(h) (one fused launch on
+    // the peer-memory path; all-reduce + norm otherwise)
+    const int nb = (int)c.i("nb"), d = (int)c.i("d");
+    const size_t n = (size_t)nb * d;
+    const float* src = (const float*)c.ptr("src", 4 * n);
+    float* tmp = (float*)c.ptr("dst", 4 * n);
+    float* h = (float*)c.ptr("h", 4 * n);
+    const __half* g = (const __half*)c.ptr("g", 2 * (size_t)d);
+    __half* out = (__half*)c.ptr("out", 2 * n);
+    const float floor = (float)c.f("floor");
+    if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+    if (!dry) {
+      if (!p.comm) { why = "allreduce_rms needs a communicator (af_program_set_comm)"; return cudaErrorInvalidValue; }
+      e = comm_all_reduce_rms_f32(p.comm, src, tmp, h, nb, d, g, floor, out, st, why, p.d_err, pdl);
+      if (e != cudaSuccess) return e;
+    }
   } else if (op.kind == "tp_argmax") {
     const int T = (int)c.i("ranks"), nb = (int)c.i("nb");
     const int* g = (const int*)c.ptr("src", 4 * (size_t)T * 2 * nb);

@@ -354,6 +354,33 @@ def plan_gemv_chains(pb, enable=None):
   pb.ops[:] = out
 
 
+def plan_fuse_allreduce_norm(pb, enable=None):
+  """Tensor parallel: each residual all-reduce followed by the RMSNorm of the same residual becomes
+  one `allreduce_rms` op (csrc/comm.cu): h += the ranks' sum, then the norm, in one launch. Env
+  AF_TP_FUSED_NORM=0 keeps them apart."""
+  if enable is None:
+    enable = os.environ.get("AF_TP_FUSED_NORM", "1") != "0"
+  if not enable:
+    return
+  out = []
+  ops = pb.ops
+  i = 0
+  while i < len(ops):
+    kind, kv = ops[i]
+    if (kind == "allreduce" and i + 1 < len(ops) and ops[i + 1][0] == "rmsnorm" and kv.get("addto", "-") != "-"):
+      nk = ops[i + 1][1]
+      nb, d = int(nk["nb"]), int(nk["d"])
+      if (nk["x"] == kv["addto"] and nb * d == int(kv["n"]) and not int(nk.get("xf16", 0))
+          and int(nk.get("ldx", d)) == d and int(nk.get("ldo", d)) == d and "pf" not in nk):
+        out.append(("allreduce_rms", dict(src=kv["src"], dst=kv["dst"], h=kv["addto"], nb=nb, d=d, g=nk["g"],
+                                          out=nk["out"], floor=nk["floor"])))
+        i += 2
+        continue
+    out.append((kind, kv))
+    i += 1
+  pb.ops[:] = out
+
+
 def plan_l2_prefetch(pb, budget=None, mode=None):
   """Attach L2 prefetch keys to a decode plan: each tensor-core GEMV's weights are (partly) fetched
   into L2 by the kernel that runs before it - the previous GEMV once its own weight copies are all
@@ -705,6 +732,7 @@ class LlamaPrefill:
       pb.op("allgather", src="tp.cand", dst="tp.gath", n=2 * NB, ranks=self.tp.world)
       pb.op("tp_argmax", src="tp.gath", ranks=self.tp.world, nb=NB, tok="tok_out", pos="pos", hist="hist", histld=M)
     plan_gemv_chains(pb)
+    plan_fuse_allreduce_norm(pb)
     plan_l2_prefetch(pb)
     ins = {"tok": (NB,), "pos": (NB,)}
     for li in range(cfg.n_layers):
