@@ -467,7 +467,7 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     if (a.scratch_bytes) a.scratch = c.ptr("scr", a.scratch_bytes);
     a.pf = parse_pf(c);
     a.err = p.d_err;
-    static const int evict_first = env_int("AF_L2_EVICT_FIRST", 0);
+    static const int evict_first = env_int("AF_L2_EVICT_FIRST", 1);
     a.evict_first = (int)c.i("ef", evict_first);
     if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
     // prompt-sized row counts (prefill) run as a tensor-core GEMM unless the op asks for the GEMV
@@ -517,7 +517,7 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     a.scratch_bytes = gemv_chain_scratch_bytes(a);
     a.scratch = c.ptr("scr", a.scratch_bytes);
     a.err = p.d_err;
-    static const int evict_first = env_int("AF_L2_EVICT_FIRST", 0);
+    static const int evict_first = env_int("AF_L2_EVICT_FIRST", 1);
     a.evict_first = (int)c.i("ef", evict_first);
     if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
     if (!dry) e = gemv_chain_launch(a, st, pdl);
