@@ -143,20 +143,26 @@ AF_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int k0, int m0, uint6
 // about the same time (~1 µs on the 8B prompt shapes) whatever the tile width, so 128-column tiles
 // run far below the tensor pipe's rate; deeper rings recover 10-15 % of that: 128-column tiles fit
 // four operand and eight raw slices in shared memory, 256-column tiles three and four.
-template <bool I4, int BNV, int NS, int NR>
+// MM = 128-row M tiles per CTA: with MM = 2 each converted B slice feeds two M tiles (two TMEM
+// accumulators side by side), so every weight byte is dequantised once per 256 prompt rows.
+template <bool I4, int BNV, int NS, int NR, int MM>
 __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, const __grid_constant__ CUtensorMap amap) {
   static_assert(NS <= gm::MAX_STAGES && NR <= gm::MAX_RSTAGES, "ring deeper than the barrier arrays");
+  static_assert(MM * BNV <= 512, "accumulators beyond the 512 TMEM columns");
   using T = Gt<BNV>;
+  constexpr int STG = MM * gm::A_BYTES + T::B_BYTES;        // one slice: MM A tiles, then B
+  constexpr uint32_t TCOLS = (uint32_t)(MM * T::TMEM_COLS);
   extern __shared__ unsigned char smem_raw[];
   // the swizzled slices need 1024-byte aligned bases
   const uint32_t raw = smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
-  unsigned char* rawring = smem + NS * T::STAGE;
+  unsigned char* rawring = smem + NS * STG;
   GemmShared* sh = reinterpret_cast<GemmShared*>(rawring + NR * T::RAW_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int MT = (a.NB + gm::BM - 1) / gm::BM;
+  const int MT = (a.NB + gm::BM * MM - 1) / (gm::BM * MM);
   const int mt = blockIdx.x % MT, nt = blockIdx.x / MT;     // M fastest: CTAs sharing a weight tile run together
-  const int m0 = mt * gm::BM, n0 = nt * T::BN;
+  const int m0 = mt * gm::BM * MM, n0 = nt * T::BN;
+  const int mlive = min(MM, (a.NB - m0 + gm::BM - 1) / gm::BM);   // M tiles of this CTA holding prompt rows
   const int KT = a.K / 32, RB = a.Np / 64;
   const int KB = (a.K + gm::BK - 1) / gm::BK;
   constexpr int UNIT = I4 ? tc::UNIT4 : tc::UNIT;
@@ -177,7 +183,7 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
   }
   if (warp == gm::MMA_WARP) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                 ::"r"(smem_u32(&sh->tmem)), "r"(T::TMEM_COLS) : "memory");
+                 ::"r"(smem_u32(&sh->tmem)), "r"(TCOLS) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -231,8 +237,9 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
           *abort = 1;
           break;
         }
-        mbar_arrive_expect_tx(&sh->a_full[s], gm::A_BYTES);
-        tma_load_2d(smem + s * T::STAGE, &amap, kb * gm::BK, m0, &sh->a_full[s]);
+        mbar_arrive_expect_tx(&sh->a_full[s], (uint32_t)(mlive * gm::A_BYTES));
+        for (int i = 0; i < mlive; ++i)
+          tma_load_2d(smem + s * STG + i * gm::A_BYTES, &amap, kb * gm::BK, m0 + i * gm::BM, &sh->a_full[s]);
         issued = kb + 1;
       }
       for (int kb = issued - 1; kb >= 0 && kb >= issued - NS; --kb) {
@@ -252,11 +259,13 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t abase = smem_u32(smem + s * T::STAGE);
-        const uint32_t bbase = abase + gm::A_BYTES;
+        const uint32_t abase = smem_u32(smem + s * STG);
+        const uint32_t bbase = abase + MM * gm::A_BYTES;
+        for (int i = 0; i < mlive; ++i)
 #pragma unroll
-        for (int ks = 0; ks < gm::BK / 16; ++ks)
-          mma_f16(tmem, smem_desc(abase + ks * 32), smem_desc(bbase + ks * 32), T::IDESC, (kb | ks) != 0);
+          for (int ks = 0; ks < gm::BK / 16; ++ks)
+            mma_f16(tmem + (uint32_t)(i * T::BN), smem_desc(abase + i * gm::A_BYTES + ks * 32),
+                    smem_desc(bbase + ks * 32), T::IDESC, (kb | ks) != 0);
         mma_commit(&sh->empty[s]);
       }
       // completes once every MMA issued so far has finished (also on abort, so that the tensor
@@ -274,8 +283,8 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
         *abort = 1;
         break;
       }
-      unsigned char* st = smem + s * T::STAGE;
-      unsigned char* Bs = st + gm::A_BYTES;
+      unsigned char* st = smem + s * STG;
+      unsigned char* Bs = st + MM * gm::A_BYTES;
       const unsigned char* Rw = rawring + r * T::RAW_BYTES;
       const int kt0 = kb * 2;
 #pragma unroll 4
@@ -318,11 +327,12 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
     if (!ok) {
       af_set_err(a.err, AF_DEV_WAIT_TIMEOUT);
     } else {
-      const int m = m0 + warp * 32 + lane;
+      for (int mi = 0; mi < mlive; ++mi) {
+      const int m = m0 + mi * gm::BM + warp * 32 + lane;
 #pragma unroll 1
       for (int c0 = 0; c0 < T::BN; c0 += 32) {
         uint32_t v[32];
-        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(mi * T::BN + c0), v);
         if (m >= a.NB) continue;
         const int nbase = n0 + c0;
         float f[32];
@@ -360,20 +370,21 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
           }
         }
       }
+      }
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == gm::MMA_WARP) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(T::TMEM_COLS) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS) : "memory");
   }
 }
 
-template <int BNV, int NS, int NR>
+template <int BNV, int NS, int NR, int MM = 1>
 static size_t smem_for() {
   using T = Gt<BNV>;
-  return (size_t)NS * T::STAGE + (size_t)NR * T::RAW_BYTES + sizeof(GemmShared) + 1024;
+  return (size_t)NS * (MM * gm::A_BYTES + T::B_BYTES) + (size_t)NR * T::RAW_BYTES + sizeof(GemmShared) + 1024;
 }
 
 size_t gemm_tc_smem_bytes() { return smem_for<256, gm::STAGES, gm::RSTAGES>(); }
@@ -425,7 +436,11 @@ cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
   // qkv / o / down shapes), 256 otherwise (half the A re-reads per output)
   const int sms = device_attr(cudaDevAttrMultiProcessorCount, 148);
   static const int narrow_ok = env_int("AF_GEMM_NARROW", 1);
-  const int MT = (a.NB + gm::BM - 1) / gm::BM;
+  // two 128-row M tiles per CTA (one dequantisation of each weight slice per 256 prompt rows) when
+  // the prompt has more than one M tile (AF_GEMM_MM=1: one tile per CTA)
+  static const int mm_env = env_int("AF_GEMM_MM", 1);
+  const int MM = (mm_env >= 2 && a.NB > gm::BM) ? 2 : 1;
+  const int MT = (a.NB + gm::BM * MM - 1) / (gm::BM * MM);
   // 128-column tiles only where they add no wave: twice the tiles must fit in as many waves of
   // `sms` CTAs as the 256-column tiles (AF_GEMM_NARROW: 0 never, 2 always, 1 this rule)
   const int wide_tiles = MT * ((a.N + 255) / 256), narrow_tiles = MT * ((a.N + 127) / 128);
@@ -437,16 +452,21 @@ cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
   // four, as 256-column tiles do). Measured on the 8B prompt shapes (qkv / o / down, µs): 3+4 143 /
   // 69 / 162, 6+4 130 / 62 / 138, 4+8 128 / 62 / 134; for 256-column tiles 4+2 was slower than 3+4.
   static const int deep = env_int("AF_GEMM_DEEP", 1);
-  const int var = narrow ? (deep >= 1 ? 1 : 0) : 2;
-  static const size_t smems[3] = {smem_for<128, 3, 4>(), smem_for<128, 4, 8>(), smem_for<256, 3, 4>()};
-  void* const fns[2][3] = {
-      {(void*)gemm_tc_kernel<false, 128, 3, 4>, (void*)gemm_tc_kernel<false, 128, 4, 8>,
-       (void*)gemm_tc_kernel<false, 256, 3, 4>},
-      {(void*)gemm_tc_kernel<true, 128, 3, 4>, (void*)gemm_tc_kernel<true, 128, 4, 8>,
-       (void*)gemm_tc_kernel<true, 256, 3, 4>}};
+  // MM = 2: 128-column tiles with three operand and eight raw slices, 256-column with two and four
+  // (the second A tile per slice takes the shared memory of one operand stage)
+  const int var = MM == 2 ? (narrow ? 3 : 4) : (narrow ? (deep >= 1 ? 1 : 0) : 2);
+  static const size_t smems[5] = {smem_for<128, 3, 4>(), smem_for<128, 4, 8>(), smem_for<256, 3, 4>(),
+                                  smem_for<128, 3, 8, 2>(), smem_for<256, 2, 4, 2>()};
+  void* const fns[2][5] = {
+      {(void*)gemm_tc_kernel<false, 128, 3, 4, 1>, (void*)gemm_tc_kernel<false, 128, 4, 8, 1>,
+       (void*)gemm_tc_kernel<false, 256, 3, 4, 1>, (void*)gemm_tc_kernel<false, 128, 3, 8, 2>,
+       (void*)gemm_tc_kernel<false, 256, 2, 4, 2>},
+      {(void*)gemm_tc_kernel<true, 128, 3, 4, 1>, (void*)gemm_tc_kernel<true, 128, 4, 8, 1>,
+       (void*)gemm_tc_kernel<true, 256, 3, 4, 1>, (void*)gemm_tc_kernel<true, 128, 3, 8, 2>,
+       (void*)gemm_tc_kernel<true, 256, 2, 4, 2>}};
   const size_t smem = smems[var];
   void* fn = fns[i4 ? 1 : 0][var];
-  static PerDeviceOnce attr[2][3];
+  static PerDeviceOnce attr[2][5];
   const cudaError_t ae = attr[i4 ? 1 : 0][var].run(
       [fn, smem] { return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); });
   if (ae != cudaSuccess) return ae;

@@ -357,9 +357,10 @@ def plan_gemv_chains(pb, enable=None):
 def plan_fuse_allreduce_norm(pb, enable=None):
   """Tensor parallel: each residual all-reduce followed by the RMSNorm of the same residual becomes
   one `allreduce_rms` op (csrc/comm.cu): h += the ranks' sum, then the norm, in one launch. Env
-  AF_TP_FUSED_NORM=0 keeps them apart."""
+  AF_TP_FUSED_NORM=1 turns it on; off by default: at TP2 on the 8B shape the single-CTA fused launch
+  measured 460.8 against 465.7 tok/s for the all-reduce and the rmsnorm kernel apart."""
   if enable is None:
-    enable = os.environ.get("AF_TP_FUSED_NORM", "1") != "0"
+    enable = os.environ.get("AF_TP_FUSED_NORM", "0") == "1"
   if not enable:
     return
   out = []

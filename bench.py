@@ -852,6 +852,20 @@ def blas_threads():
     return os.cpu_count() or 1
 
 
+class _JsonOut:
+  """stdout carries the JSON line(s) only: everything else written to file descriptor 1 while the
+  bench runs (NCCL's version banner, library messages, Python prints) goes to stderr."""
+
+  def __init__(self):
+    sys.stdout.flush()
+    self.fd = os.dup(1)
+    os.dup2(2, 1)
+    sys.stdout = sys.stderr
+
+  def emit(self, obj):
+    os.write(self.fd, (json.dumps(obj) + "\n").encode())
+
+
 def main():
   ap = argparse.ArgumentParser()
   ap.add_argument("--gpus", type=int, default=1)
@@ -880,12 +894,13 @@ def main():
   args = ap.parse_args()
   select_model(args.model)
   ws, rank, _ = _dist()
+  out = _JsonOut()
   if args.timeline:
-    print(json.dumps(timeline(args)), flush=True)
+    out.emit(timeline(args))
     return
   if args.kernel:
     for name in args.kernel.split(","):
-      print(json.dumps(kernel_bench(name, args.reps, max(args.warmup, 3))), flush=True)
+      out.emit(kernel_bench(name, args.reps, max(args.warmup, 3)))
     return
   if args.impl == "reference":
     if rank != 0:
@@ -893,7 +908,7 @@ def main():
     v, how, per_step = cpu_reference(args.steps, args.warmup)
     tp_on = ws > 1 and not args.replicas
     info = host_info()
-    print(json.dumps({"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tokens/s",
+    out.emit({"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tokens/s",
                       "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
                       "scaling": "strong" if tp_on else "weak", "vs_baseline": None,
                       "dtype": MODELS[MODEL]["dtype"] + " (numpy fp32 on the host)", "data": "synthetic",
@@ -902,7 +917,7 @@ def main():
                       "cpu_baseline": {"value": round(v, 4), "unit": "tokens/s", "cores": info["blas_threads"],
                                        "kind": "port", "sample": how, **info},
                       "e2e": {"value": round(v, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                              "d2h_bytes_per_step": 0}}))
+                              "d2h_bytes_per_step": 0}})
     return
   res = run_b200(args)
   if rank == 0 and res is not None:
@@ -911,7 +926,7 @@ def main():
       info = host_info()
       res["cpu_baseline"] = {"value": round(v, 4), "unit": "tokens/s", "cores": info["blas_threads"], "kind": "port",
                              "sample": how, **info}
-    print(json.dumps(res), flush=True)
+    out.emit(res)
 
 
 if __name__ == "__main__":
