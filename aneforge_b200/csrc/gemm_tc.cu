@@ -437,9 +437,12 @@ cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
   const int sms = device_attr(cudaDevAttrMultiProcessorCount, 148);
   static const int narrow_ok = env_int("AF_GEMM_NARROW", 1);
   // two 128-row M tiles per CTA (one dequantisation of each weight slice per 256 prompt rows) when
-  // the prompt has more than one M tile (AF_GEMM_MM=1: one tile per CTA)
-  static const int mm_env = env_int("AF_GEMM_MM", 1);
-  const int MM = (mm_env >= 2 && a.NB > gm::BM) ? 2 : 1;
+  // that still gives every SM a 256-column tile: measured on the 8B 512-row prompt, gate|up 285.7 ->
+  // 203.6 µs and the 72B 2048-row int4 gate|up 2333 -> 1752 µs, while the narrow o / down shapes
+  // (64 CTAs) got slower (64 -> 93, 136 -> 182 µs). AF_GEMM_MM: 0 this rule, 1 never, 2 always.
+  static const int mm_env = env_int("AF_GEMM_MM", 0);
+  const int tiles2 = ((a.NB + 2 * gm::BM - 1) / (2 * gm::BM)) * ((a.N + 255) / 256);
+  const int MM = a.NB > gm::BM && (mm_env == 2 || (mm_env == 0 && tiles2 >= sms)) ? 2 : 1;
   const int MT = (a.NB + gm::BM * MM - 1) / (gm::BM * MM);
   // 128-column tiles only where they add no wave: twice the tiles must fit in as many waves of
   // `sms` CTAs as the 256-column tiles (AF_GEMM_NARROW: 0 never, 2 always, 1 this rule)
