@@ -33,21 +33,27 @@ def test_hf_checkpoint_decodes_like_the_oracle(kind, tmp_path):
 
 
 @pytest.mark.parametrize("compress", [None, "int8"])
-def test_qwen35_hybrid_decodes_like_transformers(compress):
+def test_qwen35_hybrid_decodes_like_transformers(compress, monkeypatch):
   """A Qwen3.5 hybrid (three gated-DeltaNet layers, one gated-attention layer; reference
   `aneforge/qwen35.py`, `tests/test_qwen35.py:87-117`) through `hybrid.adapt` onto the device: the
   graph-builder mixers keep their conv / recurrent / K-V states resident. Its greedy tokens are the
   checkpoint's own next-token argmax (transformers, fp32, on the same prefix) except near ties."""
   from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5TextConfig
-  from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5ForCausalLM
+  from transformers.models.qwen3_5 import modeling_qwen3_5 as q35
   from aneforge_b200 import hybrid, llm
+  # The reference model runs on the host: its constructor must pick transformers' torch kernels,
+  # not the Triton / CUDA ones it selects when those libraries are importable.
+  for name in ("FusedRMSNormGated", "chunk_gated_delta_rule", "fused_recurrent_gated_delta_rule",
+               "causal_conv1d_fn", "causal_conv1d_update"):
+    if hasattr(q35, name):
+      monkeypatch.setattr(q35, name, None)
   torch.manual_seed(0)
   ct = Qwen3_5TextConfig(hidden_size=256, num_hidden_layers=4, num_attention_heads=4, num_key_value_heads=2,
                          head_dim=64, partial_rotary_factor=0.25, linear_num_key_heads=2, linear_num_value_heads=4,
                          linear_key_head_dim=64, linear_value_head_dim=64, linear_conv_kernel_dim=4, vocab_size=512,
                          intermediate_size=512, rms_norm_eps=1e-6, initializer_range=0.08)
   with torch.device("cpu"):                                # the reference model runs on the host
-    hf = Qwen3_5ForCausalLM(ct).eval().cpu()
+    hf = q35.Qwen3_5ForCausalLM(ct).eval().cpu()
   sd = {k: v.detach().cpu().half().numpy() for k, v in hf.state_dict().items()}
   cfg, w = hybrid.adapt(ct, sd, prefix="model.")
   m = llm.LlamaPrefill(cfg, w, compress=compress)
