@@ -37,7 +37,8 @@ def test_qwen35_hybrid_decodes_like_transformers(compress, monkeypatch):
   """A Qwen3.5 hybrid (three gated-DeltaNet layers, one gated-attention layer; reference
   `aneforge/qwen35.py`, `tests/test_qwen35.py:87-117`) through `hybrid.adapt` onto the device: the
   graph-builder mixers keep their conv / recurrent / K-V states resident. Its greedy tokens are the
-  checkpoint's own next-token argmax (transformers, fp32, on the same prefix) except near ties."""
+  checkpoint's own next-token argmax (transformers, fp32, on the same prefix; under int8 with the
+  decoder projections as the device decodes them) except near ties."""
   from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5TextConfig
   from transformers.models.qwen3_5 import modeling_qwen3_5 as q35
   from aneforge_b200 import hybrid, llm
@@ -55,6 +56,14 @@ def test_qwen35_hybrid_decodes_like_transformers(compress, monkeypatch):
   with torch.device("cpu"):                                # the reference model runs on the host
     hf = q35.Qwen3_5ForCausalLM(ct).eval().cpu()
   sd = {k: v.detach().cpu().half().numpy() for k, v in hf.state_dict().items()}
+  if compress:
+    # the reference multiplies by what the device streams: each decoder-layer projection as its
+    # `compress` encoding decodes (embedding and lm_head stay fp16 on the device)
+    from aneforge_b200 import _blob
+    with torch.no_grad():
+      for mod in hf.model.layers.modules():
+        if isinstance(mod, torch.nn.Linear):
+          mod.weight.copy_(torch.from_numpy(_blob.dense_of(mod.weight.half().numpy(), compress)))
   cfg, w = hybrid.adapt(ct, sd, prefix="model.")
   m = llm.LlamaPrefill(cfg, w, compress=compress)
   prompt = list(np.random.default_rng(5).integers(0, 512, 12))
