@@ -259,11 +259,18 @@ struct AttnPrefillArgs {
   int S = 0, H = 0, KV = 0, dh = 0;
   float scale = 0.f, kv_c = 1.f;
   int expand = 0;
+  __half* kvx = nullptr;       // optional [2][KV][S][dh]: K and V times the GQA factor (expand), for the
+                               // tensor-core attention
+  int* err = nullptr;          // device error word (AF_DEV_WAIT_TIMEOUT if a pipeline wait gives up)
 };
-// rope q (-> qbuf [H][S][dh] fp16) and k, write roped K / raw V into cache rows 0..S-1
+// rope q (-> qbuf [H][S][dh] fp16) and k, write roped K / raw V into cache rows 0..S-1 (and, with
+// expand and kvx, the expanded copies)
 cudaError_t rope_kv_prefill_launch(const AttnPrefillArgs& a, __half* qbuf, cudaStream_t st);
 // causal attention of the staged q rows against cache rows 0..i
 cudaError_t attn_prefill_with_q(const AttnPrefillArgs& a, const __half* qbuf, cudaStream_t st);
+// the tcgen05 form (attn_prefill_tc.cu): head dim 128; with expand it reads kvx
+bool attn_prefill_tc_ok(const AttnPrefillArgs& a);
+cudaError_t attn_prefill_tc_launch(const AttnPrefillArgs& a, const __half* qbuf, cudaStream_t st);
 
 // ---- generic graph ops (graph_ops.cu): what `compile(graph)` lowers nodes onto when no fused kernel
 // covers them. fp32 values, fp16-rounded matmul operands, rank <= GRAPH_MAX_RANK.

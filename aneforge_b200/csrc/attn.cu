@@ -664,8 +664,14 @@ __global__ void __launch_bounds__(32) rope_kv_prefill_kernel(AttnPrefillArgs a, 
 #pragma unroll
       for (int e = 0; e < EPL; ++e) {
         const size_t o = ((size_t)kvh * a.ldm + s) * DH + lane * EPL + e;
-        a.kc[o] = f2h(v[e]);
-        a.vc[o] = f2h(row[(size_t)(a.H + a.KV + kvh) * DH + lane * EPL + e]);
+        const __half kh = f2h(v[e]), vh = f2h(row[(size_t)(a.H + a.KV + kvh) * DH + lane * EPL + e]);
+        a.kc[o] = kh;
+        a.vc[o] = vh;
+        if (a.expand && a.kvx) {                           // f16(c * f16(k)), as the attention reads them
+          const size_t x = ((size_t)kvh * a.S + s) * DH + lane * EPL + e;
+          a.kvx[x] = f2h(a.kv_c * h2f(kh));
+          a.kvx[(size_t)a.KV * a.S * DH + x] = f2h(a.kv_c * h2f(vh));
+        }
       }
   }
 }
@@ -909,7 +915,9 @@ cudaError_t rope_kv_prefill_launch(const AttnPrefillArgs& a, __half* qbuf, cudaS
 }
 
 cudaError_t attn_prefill_with_q(const AttnPrefillArgs& a, const __half* qbuf, cudaStream_t st) {
-  static const int fa = env_int("AF_PREFILL_FA", 1);
+  // AF_PREFILL_FA: 2 (default) the tcgen05 kernel where it applies, 1 the mma.sync kernel, 0 neither
+  static const int fa = env_int("AF_PREFILL_FA", 2);
+  if (fa >= 2 && attn_prefill_tc_ok(a)) return attn_prefill_tc_launch(a, qbuf, st);
   if (fa && a.dh == 128 && a.S >= 16) {
     static PerDeviceOnce attrs;
     const cudaError_t attr = attrs.run(

@@ -29,6 +29,7 @@
 #include "af_common.cuh"
 #include "af_kernels.h"
 #include "tc_common.cuh"
+#include "tcgen05.cuh"
 
 namespace af {
 
@@ -83,39 +84,6 @@ AF_DEV bool gm_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   return false;
 }
 
-// offset of 16-byte chunk c of row r in a 128-byte-swizzled K-major slice
-AF_DEV uint32_t sw128(int r, int c) { return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)); }
-
-// shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 bytes apart
-AF_DEV uint64_t smem_desc(uint32_t addr) {
-  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) |
-         ((uint64_t)2 << 61);
-}
-
-AF_DEV void mma_f16(uint32_t tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
-      ::"r"(tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
-}
-
-AF_DEV void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-AF_DEV void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
-        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
 // group-32 int4: 8 nibbles of one k-step (fragment slot order of pack_i4_tiles) -> the lane's two
 // rows' 4 values each, as code * scale in fp16
 AF_DEV void i4_rows(uint32_t w, __half2 s_lo, __half2 s_hi, uint32_t& row_lo0, uint32_t& row_lo1, uint32_t& row_hi0,
@@ -130,13 +98,6 @@ AF_DEV void i4_rows(uint32_t w, __half2 s_lo, __half2 s_hi, uint32_t& row_lo0, u
   row_lo1 = *reinterpret_cast<uint32_t*>(&a2);
   row_hi0 = *reinterpret_cast<uint32_t*>(&a1);
   row_hi1 = *reinterpret_cast<uint32_t*>(&a3);
-}
-
-// 2-D TMA tile load into this CTA's shared memory of box {64 K, 128 rows} at (k0, m0), completion on `bar`
-AF_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int k0, int m0, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-      ::"r"(smem_u32(dst)), "l"(map), "r"(k0), "r"(m0), "r"(smem_u32(bar)) : "memory");
 }
 
 // NS = operand ring depth (A + converted B slices), NR = raw weight ring depth. One k-slice takes
@@ -388,24 +349,6 @@ static size_t smem_for() {
 }
 
 size_t gemm_tc_smem_bytes() { return smem_for<256, gm::STAGES, gm::RSTAGES>(); }
-
-// cuTensorMapEncodeTiled, resolved through the runtime at first use: the library does not link the
-// driver library, so it loads (and exports its symbols) on hosts without a GPU driver
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_tiled() {
-  static EncodeTiledFn fn = [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      p = nullptr;
-    return reinterpret_cast<EncodeTiledFn>(p);
-  }();
-  return fn;
-}
 
 // The A operand's tensor map: fp16 [M rows][K] with row stride ldx, 64 x 128 boxes, 128-byte swizzle.
 static bool make_amap(const GemvTcArgs& a, CUtensorMap* map) {

@@ -645,6 +645,8 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     a.scale = (float)c.f("scale");
     a.kv_c = (float)c.f("kvc", 1.0);
     a.expand = c.i("expand", 0);
+    a.kvx = (__half*)c.ptr("kvx", 2 * 2 * (size_t)a.KV * a.S * a.dh, true);
+    a.err = p.d_err;
     if (a.ldm < a.S) c.err = "ldm < s";
     if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
     if (!dry) {

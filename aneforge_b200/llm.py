@@ -242,6 +242,9 @@ def emit_attention_prefill(pb, ctx, li, lw, cfg, ls):
   _emit_linear(pb, ctx, f"{pre}.qkv", lw["qkv"], "xn", "qkv", "f32")
   kv = dict(qkv="qkv", kc=f"{pre}.K", vc=f"{pre}.V", out="att", qbuf="qbuf", s=S, h=H, kv=KV, dh=dh, ldm=S,
             scale=ctx["scale"], kvc=ctx["kvc"], expand=int(ctx["expand"]))
+  if ctx["expand"]:
+    # K and V times the GQA factor, written once by the rope kernel for the tensor-core attention
+    kv.update(kvx=pb.buf("kvx", 2 * 2 * KV * S * dh, "tmp"))
   if cfg.rope:
     kv.update(cos="rope.cos", sin="rope.sin")
   if ls.qk_norm:

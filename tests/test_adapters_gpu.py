@@ -70,12 +70,17 @@ def test_qwen35_hybrid_decodes_like_transformers(compress, monkeypatch):
   toks = m.generate(prompt, 10, max_len=32)
   with torch.no_grad():
     lg = hf(torch.tensor([prompt + toks], device="cpu")).logits[0].float().cpu().numpy()
+  # fp16: the tie protocol of the dense checks. int8 adds per-row weight rounding on top of the
+  # fp16 recurrent state the reference's graph carries between steps (its own hybrid checks accept a
+  # hidden-state cosine of 0.96-0.99 at fp16), so a disagreement may sit within 10 % of the logit range.
+  margin, max_ties = (0.05, 2) if compress is None else (0.10, 3)
   ties = 0
   for i, t in enumerate(toks):
     ref = lg[len(prompt) - 1 + i]
     if int(np.argmax(ref)) != t:
       top = np.sort(ref)[-2:]
-      assert top[1] - ref[t] < 0.05 * np.abs(ref).max(), f"step {i}: device {t} vs transformers {int(np.argmax(ref))}"
+      assert top[1] - ref[t] < margin * np.abs(ref).max(), \
+          f"step {i}: device {t} vs transformers {int(np.argmax(ref))}"
       ties += 1
-  assert ties <= 2
+  assert ties <= max_ties
   m.release()

@@ -81,10 +81,11 @@ def test_generate_matches_reference_golden(tag):
   m.release()
 
 
-@pytest.mark.parametrize("S", [16, 150])
+@pytest.mark.parametrize("S", [16, 150, 600])
 def test_long_prompt_prefill_tensor_core_attention(S):
-  """Prefill over several 64-row query tiles and 64-key blocks with a ragged tail (head dim 128,
-  GQA 4:1): the tensor-core causal attention against the oracle's prefill at device precision."""
+  """Prefill over several 128-row query tiles and 128-key blocks with a ragged tail (head dim 128,
+  GQA 4:1, the int8 expansion factor): the tcgen05 causal attention against the oracle's prefill at
+  device precision."""
   from aneforge_b200.llm import LlamaPrefill
   cfg = Config(dim=1024, n_layers=2, n_heads=8, n_kv_heads=2, ffn_dim=2048, vocab=2048, rope_base=500000.0)
   w = random_llama_weights(cfg, seed=21)
