@@ -89,9 +89,17 @@ struct GemvTcArgs {
   // expert ids (a selected expert held elsewhere makes the whole launch a no-op here) and the
   // routing-weight column of local expert e is e_base + e
   int e_base = 0, n_exp = 0;
+  // routed batch (with fixed_e): this launch serves the rows rows[(e_base + fixed_e) * rld + r0 + b]
+  // for b < min(NB, rcnt[e_base + fixed_e] - r0) (none: the launch does nothing); route bit 0 gathers
+  // the x rows through that list, bit 1 scatters the output rows (and their routing weights)
+  const int* rows = nullptr;
+  const int* rcnt = nullptr;
+  int rld = 0, r0 = 0, route = 0;
   int evict_first = 0;         // weight stages with the evict-first L2 policy (read once per step)
   // set by the launcher
   int Np = 0, Kp = 0, S = 1, maxc = 1;
+  int nlive = 0;               // set in the kernel: batch rows this launch computes (NB unless routed)
+  int rbase = 0;               // set in the kernel: offset of this launch's first row in `rows`
   int csize = 0;               // > 1: thread-block clusters of csize CTAs split each row block's k range
   L2Pf pf;                     // issued by each CTA once its own weight copies are all requested
   float* part = nullptr;
@@ -229,6 +237,9 @@ size_t attn_decode_scratch_floats(int NB, int KV, int n_split, int G, int dh);
 // optional renormalisation -> gw [NB][E] (zeros off the top k) and sel [NB][k] (peel order)
 cudaError_t moe_gate_launch(const float* logits, int ld, int NB, int E, int k, int renorm, float* gw, int* sel,
                             cudaStream_t st, bool pdl);
+// per-expert row lists of a batch from the gate's selections: rows[e * rld + i] for i < cnt[e]
+cudaError_t moe_route_launch(const int* sel, int NB, int k, int E, int rld, int* rows, int* cnt, cudaStream_t st,
+                             bool pdl);
 
 // ---- tensor parallel (comm.cu): collectives on a program's stream, cross-rank argmax, residual add
 // dst = sum over the ranks of src; with `addto`, addto += that sum instead (dst then scratch)

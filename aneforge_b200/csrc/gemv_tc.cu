@@ -51,14 +51,15 @@ AF_DEV void epilogue(const GemvTcArgs& a, float (&acc)[NT][4], int rt, int g, in
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int b = n * 8 + 2 * t + h;
-      if (b >= a.NB) continue;
+      if (b >= a.nlive) continue;
+      const int yb = (a.route & 2) ? __ldcg(a.rows + a.rbase + b) : b;   // output row (scattered when routed)
       const float v0 = acc[n][h], v1 = acc[n][2 + h];
       if (EPI == EPI_SWIGLU) {
         if (r1 >= a.N) continue;
         float gv = I4 ? v0 : __fmul_rn(v0, h2f(a.scale[r0]));
         float uv = I4 ? v1 : __fmul_rn(v1, h2f(a.scale[r1]));
         if (a.bias) { gv = __fadd_rn(gv, h2f(a.bias[r0])); uv = __fadd_rn(uv, h2f(a.bias[r1])); }
-        reinterpret_cast<__half*>(a.y)[(size_t)b * a.ldy + rt * 8 + g] = f2h(silu_f(gv) * uv);
+        reinterpret_cast<__half*>(a.y)[(size_t)yb * a.ldy + rt * 8 + g] = f2h(silu_f(gv) * uv);
       } else {
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr) {
@@ -66,11 +67,11 @@ AF_DEV void epilogue(const GemvTcArgs& a, float (&acc)[NT][4], int rt, int g, in
           if (row >= a.N) continue;
           float v = I4 ? (rr ? v1 : v0) : __fmul_rn(rr ? v1 : v0, h2f(a.scale[row]));
           if (a.bias) v = __fadd_rn(v, h2f(a.bias[row]));
-          const size_t o = (size_t)b * a.ldy + row;
+          const size_t o = (size_t)yb * a.ldy + row;
           if (EPI == EPI_F32) reinterpret_cast<float*>(a.y)[o] = v;
           else if (EPI == EPI_F16) reinterpret_cast<__half*>(a.y)[o] = f2h(v);
           else if (EPI == EPI_RESID) {
-            if (a.rw) v *= __ldcg(a.rw + (size_t)b * a.rw_e + a.e_base + a.fixed_e);
+            if (a.rw) v *= __ldcg(a.rw + (size_t)yb * a.rw_e + a.e_base + a.fixed_e);
             reinterpret_cast<float*>(a.y)[o] = __ldcg(reinterpret_cast<const float*>(a.y) + o) + v;
           }
         }
@@ -97,6 +98,15 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
     if (a.scale) a.scale += (size_t)expert * a.s_stride;
   }
   a.fixed_e = expert;
+  a.nlive = a.NB;
+  if (a.route) {
+    // routed batch: the row list comes from the preceding kernel; an empty share is a no-op (uniform
+    // over the grid, before any barrier)
+    pdl_wait();
+    a.rbase = (a.e_base + expert) * a.rld + a.r0;
+    a.nlive = min(a.NB, __ldcg(a.rcnt + a.e_base + expert) - a.r0);
+    if (a.nlive <= 0) return;
+  }
   using F = tc::Fmt<I4>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   unsigned char* ring = smem_raw;                                          // [STAGES][F::stage]
@@ -169,9 +179,12 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
         if (!mbar_wait(&sh->xempty[xs], xphase ^ 1)) { ok = false; break; }
         const uint32_t xbytes = (uint32_t)(kce - kc) * 32 * 2;
         mbar_arrive_expect_tx(&sh->xfull[xs], xbytes * a.NB);
-        for (int b = 0; b < a.NB; ++b)
-          bulk_g2s(xring + (size_t)xs * xslot_halves + (size_t)b * tc::XSTRIDE, a.x + (size_t)b * a.ldx + (size_t)kc * 32,
+        for (int b = 0; b < a.NB; ++b) {
+          // routed: row b of the list (rows past the list repeat its first row: finite, never stored)
+          const int xb = (a.route & 1) ? __ldcg(a.rows + a.rbase + (b < a.nlive ? b : 0)) : b;
+          bulk_g2s(xring + (size_t)xs * xslot_halves + (size_t)b * tc::XSTRIDE, a.x + (size_t)xb * a.ldx + (size_t)kc * 32,
                    xbytes, &sh->xfull[xs]);
+        }
         if (++xs == tc::XSLOTS) { xs = 0; xphase ^= 1; }
         for (; kt < kce; kt += F::ks) {
           const int nk = min(F::ks, kce - kt);
@@ -597,7 +610,7 @@ static cudaError_t gemv_tc_launch16(GemvTcArgs a, cudaStream_t st, bool pdl);
 
 // Batches above 16 run as 16-row slices of x (the weights stream once per slice).
 cudaError_t gemv_tc_launch(const GemvTcArgs& a0, cudaStream_t st, bool pdl) {
-  if (a0.NB < 1) return cudaErrorInvalidValue;
+  if (a0.NB < 1 || (a0.route && (a0.NB > 16 || !a0.rows || !a0.rcnt || a0.sel))) return cudaErrorInvalidValue;
   for (int b0 = 0; b0 < a0.NB; b0 += 16) {
     GemvTcArgs a = a0;
     a.NB = a0.NB - b0 < 16 ? a0.NB - b0 : 16;

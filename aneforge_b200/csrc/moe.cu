@@ -70,6 +70,41 @@ cudaError_t moe_gate_launch(const float* logits, int ld, int NB, int E, int k, i
   return cudaLaunchKernelEx(&cfg, moe_gate_kernel, logits, ld, E, k, renorm, gw, sel);
 }
 
+// Per-expert row lists of a batch (the routed expert GEMVs gather their rows through them): thread
+// e walks the rows in order and lists each row that selected expert e; rows[e * rld + i], i < cnt[e].
+__global__ void __launch_bounds__(MOE_EMAX) moe_route_kernel(const int* sel, int NB, int k, int E, int rld, int* rows,
+                                                             int* cnt) {
+  const int e = threadIdx.x;
+  pdl_wait();
+  if (e < E) {
+    int n = 0;
+    for (int b = 0; b < NB; ++b)
+      for (int j = 0; j < k; ++j)
+        if (__ldcg(sel + (size_t)b * k + j) == e) {
+          if (n < rld) rows[(size_t)e * rld + n] = b;
+          ++n;
+          break;
+        }
+    cnt[e] = n < rld ? n : rld;
+  }
+  pdl_trigger();
+}
+
+cudaError_t moe_route_launch(const int* sel, int NB, int k, int E, int rld, int* rows, int* cnt, cudaStream_t st,
+                             bool pdl) {
+  if (NB < 1 || E < 1 || E > MOE_EMAX || k < 1 || k > E || rld < 1) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(MOE_EMAX);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, moe_route_kernel, sel, NB, k, E, rld, rows, cnt);
+}
+
 }  // namespace af
 
 extern "C" int af_moe_gate(const float* logits, int ld, int nb, int e, int k, int renorm, float* gw, int* sel,

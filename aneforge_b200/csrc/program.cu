@@ -439,7 +439,9 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     a.ldx = c.i("ldx", a.K);
     const int out_cols = a.epi == EPI_SWIGLU ? a.N / 2 : a.N;
     a.ldy = c.i("ldy", out_cols);
-    a.x = (const __half*)c.ptr("x", 2 * ((size_t)(a.NB - 1) * a.ldx + a.K));
+    // a routed launch gathers x rows / scatters y rows among xrows / yrows rows (default nb)
+    const int xrows = (int)c.i("xrows", a.NB), yrows = (int)c.i("yrows", a.NB);
+    a.x = (const __half*)c.ptr("x", 2 * ((size_t)(xrows - 1) * a.ldx + a.K));
     // experts (MoE): E experts' tiles back to back, expert from `sel[slot]` or `fixe`
     const int nexp = (int)c.i("experts", 1);
     const size_t tile_bytes = i4 ? pack_i4_tiles_bytes(a.N, a.K) : pack_i8_tiles_bytes(a.N, a.K);
@@ -456,12 +458,25 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
       a.n_exp = nexp;
       if (a.e_base < 0) c.err = "ebase < 0";
     }
+    // routed batch (moe_route lists): rows=, rcnt= over eg global experts, rld= rows per list,
+    // r0= this launch's first list entry, route= 1 gather x / 2 scatter y
+    a.route = (int)c.i("route", 0);
+    if (a.route) {
+      const int eg = (int)c.i("eg", a.e_base + nexp);
+      a.rld = (int)c.i("rld");
+      a.r0 = (int)c.i("r0", 0);
+      a.rows = (const int*)c.ptr("rows", 4 * (size_t)eg * a.rld);
+      a.rcnt = (const int*)c.ptr("rcnt", 4 * (size_t)eg);
+      if (nexp <= 1 || a.sel) c.err = "route needs experts and fixe";
+      if (a.route < 0 || a.route > 3 || a.NB > 16 || a.r0 < 0 || a.e_base + nexp > eg) c.err = "bad route";
+      if (((a.route & 1) && xrows < a.rld) || ((a.route & 2) && yrows < a.rld)) c.err = "route rows exceed x / y";
+    }
     a.rw_e = (int)c.i("rwe", 0);
-    a.rw = (const float*)c.ptr("rw", 4 * (size_t)a.NB * (a.rw_e > 0 ? a.rw_e : 1), true);
+    a.rw = (const float*)c.ptr("rw", 4 * (size_t)yrows * (a.rw_e > 0 ? a.rw_e : 1), true);
     if (a.rw && a.epi != EPI_RESID) c.err = "rw needs epi=resid";
     a.bias = (const __half*)c.ptr("bias", 2 * (size_t)a.N, true);
     const size_t esz = (a.epi == EPI_F16 || a.epi == EPI_SWIGLU) ? 2 : 4;
-    a.y = c.ptr("y", esz * ((size_t)(a.NB - 1) * a.ldy + out_cols));
+    a.y = c.ptr("y", esz * ((size_t)(yrows - 1) * a.ldy + out_cols));
     const bool want_gemm = c.i("gemm", 0) != 0;
     a.scratch_bytes = want_gemm ? 0 : gemv_tc_scratch_bytes(a.N, a.K, a.NB);
     if (a.scratch_bytes) a.scratch = c.ptr("scr", a.scratch_bytes);
@@ -663,6 +678,14 @@ static cudaError_t run_op(Program& p, const Op& op, bool dry, std::string& why) 
     const int renorm = (int)c.i("renorm", 1);
     if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
     if (!dry) e = moe_gate_launch(lg, ld, nb, E, k, renorm, gw, sel, st, pdl);
+  } else if (op.kind == "moe_route") {
+    // per-expert row lists of the batch: rows [e][rld], cnt [e]
+    const int nb = (int)c.i("nb"), E = (int)c.i("e"), k = (int)c.i("k"), rld = (int)c.i("rld", nb);
+    const int* sel = (const int*)c.ptr("sel", 4 * (size_t)nb * k);
+    int* rows = (int*)c.ptr("rows", 4 * (size_t)E * rld);
+    int* cnt = (int*)c.ptr("cnt", 4 * (size_t)E);
+    if (!c.err.empty()) { why = c.err; return cudaErrorInvalidValue; }
+    if (!dry) e = moe_route_launch(sel, nb, k, E, rld, rows, cnt, st, pdl);
   } else if (op.kind == "allreduce" || op.kind == "allgather") {
     // fp32 sum over the ranks / int32 gather of n elements per rank, on the program's communicator
     const size_t n = (size_t)c.i("n");

@@ -7,9 +7,11 @@ when `norm_topk_prob`) -> experts. The reference evaluates every expert densely 
 unselected ones by exactly 0; on the device:
   * one sequence (decode at batch 1): only the k selected experts run - their index is read by the
     expert GEMVs from device memory, so the graph is static and 1/4 of Mixtral's expert bytes move;
-  * several rows (batched decode, prefill): every expert runs densely over all rows with the
-    per-row routing weight applied in the down projection's residual epilogue (0 for unselected
-    rows), which at batch >= 32 reads the same bytes a sparse gather would.
+  * a decode batch (2-64 rows): a routing kernel lists each expert's rows; each expert's GEMVs
+    gather only those rows (16 a launch) and scatter the routing-weighted results back, so every
+    expert's weights stream about once per step and carry only its share of the rows;
+  * prefill (longer row counts): every expert runs densely over all rows with the per-row routing
+    weight applied in the down projection's residual epilogue (0 for unselected rows).
 Either way each selected expert's contribution is added to the fp32 residual, scaled by its weight.
 """
 from __future__ import annotations
@@ -54,6 +56,9 @@ def _shared_expert(pb, ctx, pre, lw, y):
   pb.op("gemv", **kv)                                     # per-row gate applied in the residual epilogue
 
 
+ROUTED_MAX_ROWS = 64           # batches up to this many rows take the routed expert GEMVs
+
+
 def _expert_gemvs(pb, pre, ex, NB, E, k, sparse, y="h", e_base=0):
   """The expert projections of one layer: `ex` holds experts [e_base, e_base + ex.E) of E; each
   selected expert's down projection adds its routing-weighted output into `y`."""
@@ -68,11 +73,28 @@ def _expert_gemvs(pb, pre, ex, NB, E, k, sparse, y="h", e_base=0):
   if ex.gu_s is not None:
     gu["s"] = f"{pre}.egu.s"; dn["s"] = f"{pre}.edown.s"
   # one sequence: the k selected experts, read on the device (a launch whose expert another GPU
-  # holds does nothing); several rows: every local expert densely with per-row weights
-  picks = [dict(sel="moe.sel", slot=s) for s in range(k)] if sparse else [dict(fixe=e) for e in range(ex.E)]
-  for p in picks:
-    pb.op("gemv", **gu, **p)
-    pb.op("gemv", **dn, **p)
+  # holds does nothing)
+  if sparse:
+    for s in range(k):
+      pb.op("gemv", **gu, sel="moe.sel", slot=s)
+      pb.op("gemv", **dn, sel="moe.sel", slot=s)
+    return
+  if NB > ROUTED_MAX_ROWS:
+    for e in range(ex.E):                    # every expert densely over all rows
+      pb.op("gemv", **gu, fixe=e)
+      pb.op("gemv", **dn, fixe=e)
+    return
+  # several rows: per local expert, only the rows routed to it (`moe_route` lists), up to 16 a
+  # launch; gate|up gathers those rows of xn into a compact act, down scatters its routing-weighted
+  # rows back into y. A list shorter than a launch's share leaves that launch empty (a no-op), so
+  # the batch's weights stream about once per expert instead of once per 16 rows.
+  R16 = min(16, NB)
+  gu.update(nb=R16, xrows=NB, route=1, rows="moe.rows", rcnt="moe.rcnt", rld=NB, eg=E)
+  dn.update(nb=R16, yrows=NB, route=2, rows="moe.rows", rcnt="moe.rcnt", rld=NB, eg=E)
+  for e in range(ex.E):
+    for r0 in range(0, NB, R16):
+      pb.op("gemv", **gu, fixe=e, r0=r0)
+      pb.op("gemv", **dn, fixe=e, r0=r0)
 
 
 def emit_moe(pb, ctx, li, lw, cfg, ls):
@@ -96,6 +118,9 @@ def emit_moe(pb, ctx, li, lw, cfg, ls):
   pb.op("rmsnorm", x="h", g=f"{pre}.mlp_g", out="xn", nb=NB, d=cfg.dim, floor=lw["mlp_floor"])
   llm._emit_linear(pb, ctx, f"{pre}.router", lw["router"], "xn", "moe.logits", "f32")
   pb.op("moe_gate", logits="moe.logits", nb=NB, e=E, k=k, renorm=int(renorm), gw="moe.gw", sel="moe.sel")
+  if 1 < NB <= ROUTED_MAX_ROWS:
+    pb.buf("moe.rows", 4 * E * NB, "tmp"); pb.buf("moe.rcnt", 4 * E, "tmp")
+    pb.op("moe_route", sel="moe.sel", nb=NB, e=E, k=k, rld=NB, rows="moe.rows", cnt="moe.rcnt")
   if not ep:
     _expert_gemvs(pb, pre, ex, NB, E, k, sparse=NB == 1)
     if "shgu" in lw:

@@ -1,13 +1,14 @@
 """Mixture-of-experts on the device against the oracle: the router tail (softmax + top-k peel with
 lowest-index ties + renormalisation), expert selection inside the tensor-core GEMV (index read from
-device memory, routing-weighted residual epilogue), and whole MoE decoders (sparse top-k at batch 1,
-dense with per-row weights at batch 3) with int8 and group-32 int4 experts."""
+device memory, routing-weighted residual epilogue), the routed batch GEMVs against the dense ones, and
+whole MoE decoders (sparse top-k at batch 1, routed at batch 2-3) with int8 and group-32 int4 experts."""
 import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
+from aneforge_b200 import _runtime as R                                          # noqa: E402
 from oracle import quant as Q                                                   # noqa: E402
 from oracle.model import Config, OracleModel, random_llama_weights, softmax, topk_gate   # noqa: E402
 
@@ -104,7 +105,7 @@ def test_moe_decoder_matches_oracle(experts):
   toks = m.generate(prompt, 24, max_len=64)
   om = OracleModel(cfg, w, "int8", precision="device", moe_compress=experts)
   assert teacher_forced_check(om, prompt, toks, 64, n_check=24) <= 2
-  # batch 3 runs the dense per-row-weighted experts: the same tokens as batch 1 for each sequence
+  # batch 3 runs the routed expert GEMVs: the same tokens as batch 1 for each sequence
   prompts = [prompt, list(np.random.default_rng(33).integers(0, cfg.vocab, 9)),
              list(np.random.default_rng(34).integers(0, cfg.vocab, 14))]
   batch = m.generate_batch(prompts, 12, max_len=48)
@@ -165,3 +166,60 @@ def test_load_gguf_decodes_like_the_oracle(tmp_path, arch):
   om = OracleModel(oc, ow, "int8", precision="device")
   assert teacher_forced_check(om, prompt, toks, 48, n_check=16) <= 2
   m.release()
+
+
+def _expert_plan(NB, E, k, ex, routed_max, monkeypatch):
+  """moe_gate -> (moe_route) -> the layer's expert GEMVs over NB rows of xn, adding into h."""
+  from aneforge_b200 import moe
+  from aneforge_b200.plan import PlanBuilder
+  monkeypatch.setattr(moe, "ROUTED_MAX_ROWS", routed_max)
+  D, F = ex.D, ex.F
+  pb = PlanBuilder()
+  pb.buf("moe.logits", 4 * NB * E, "in"); pb.buf("xn", 2 * NB * D, "in"); pb.buf("h", 4 * NB * D, "state")
+  pb.buf("moe.gw", 4 * NB * E, "tmp"); pb.buf("moe.sel", 4 * NB * k, "tmp"); pb.buf("act", 2 * NB * F, "tmp")
+  pb.buf("L0.egu.w", ex.gu_w.numel(), "weight"); pb.buf("L0.edown.w", ex.down_w.numel(), "weight")
+  if ex.gu_s is not None:
+    pb.buf("L0.egu.s", ex.gu_s.numel() * 2, "weight"); pb.buf("L0.edown.s", ex.down_s.numel() * 2, "weight")
+  pb.op("moe_gate", logits="moe.logits", nb=NB, e=E, k=k, renorm=1, gw="moe.gw", sel="moe.sel")
+  if 1 < NB <= routed_max:
+    pb.buf("moe.rows", 4 * E * NB, "tmp"); pb.buf("moe.rcnt", 4 * E, "tmp")
+    pb.op("moe_route", sel="moe.sel", nb=NB, e=E, k=k, rld=NB, rows="moe.rows", cnt="moe.rcnt")
+  moe._expert_gemvs(pb, "L0", ex, NB, E, k, sparse=False)
+  prog = R.Program.from_text(pb.text(), {"moe.logits": (NB, E), "xn": (NB, D), "h": (NB, D)}, {}, 0,
+                             {"moe.logits": "fp32", "h": "fp32"})
+  prog.bind("L0.egu.w", ex.gu_w); prog.bind("L0.edown.w", ex.down_w)
+  if ex.gu_s is not None:
+    prog.bind("L0.egu.s", ex.gu_s); prog.bind("L0.edown.s", ex.down_s)
+  return prog
+
+
+@pytest.mark.parametrize("experts", ["int8", "int4_g32"])
+@pytest.mark.parametrize("NB,hot", [(5, False), (24, False), (24, True), (64, True)])
+def test_routed_expert_gemvs_match_dense(experts, NB, hot, monkeypatch):
+  """Decode batches run each expert over the rows routed to it (`moe_route` lists; gate|up gathers
+  them, down scatters the routing-weighted rows back) instead of every expert over every row with
+  zero weights: the same residual, to fp32 rounding. `hot` sends every row to expert 0 first, so
+  its list spans several 16-row launches while other experts' lists are empty."""
+  import torch
+  from aneforge_b200 import weights
+  E, k, D, F = 8, 2, 256, 512
+  rng = np.random.default_rng(NB + 100 * hot)
+  wg = (rng.standard_normal((E, F, D)) * 0.05).astype(F16)
+  wu = (rng.standard_normal((E, F, D)) * 0.05).astype(F16)
+  wd = (rng.standard_normal((E, F, D)) * 0.05).astype(F16)
+  ex = weights.encode_experts(wg, wu, wd, experts, torch.device("cuda", 0))
+  logits = (rng.standard_normal((NB, E)) * 3).astype(F32)
+  if hot:
+    logits[:, 0] += 50.0
+  x = rng.standard_normal((NB, D)).astype(F16)
+  h0 = rng.standard_normal((NB, D)).astype(F32)
+  out = {}
+  for name, routed_max in (("routed", 64), ("dense", 0)):
+    prog = _expert_plan(NB, E, k, ex, routed_max, monkeypatch)
+    prog.set_input("moe.logits", logits); prog.set_input("xn", x); prog.set_input("h", h0)
+    prog.execute()
+    out[name] = prog.tensor("h", (NB, D), "fp32").cpu().numpy().copy()
+    prog.release()
+  d_r, d_d = out["routed"] - h0, out["dense"] - h0
+  assert np.abs(d_r - d_d).max() <= 1e-4 * np.abs(d_d).max(), np.abs(d_r - d_d).max()
+  assert np.abs(d_d).max() > 0.1                              # the experts did add something
