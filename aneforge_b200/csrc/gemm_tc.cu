@@ -251,7 +251,12 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
 #pragma unroll 4
       for (int q = t; q < T::BN / 64 * 2 * 128; q += gm::CONV) {
         const int u = q >> 7, rbi = u >> 1, kti = u & 1;
-        const int w = (q >> 5) & 3, ln = q & 31, g = ln >> 2, t4 = ln & 3;
+        // fragment lane of this thread: the 8 threads of each quarter warp take rows g and g ^ 5
+        // (g < 4) with their 4 chunks each, so their 16-byte stores cover the 8 swizzled positions of
+        // a 128-byte line exactly once (and their int8 loads 8 distinct 16-byte columns)
+        const int qi = q & 7, qp = (q >> 3) & 3;
+        const int g = qp ^ (5 * (qi >> 2)), t4 = qi & 3, ln = g * 4 + t4;
+        const int w = (q >> 5) & 3;
         const int nb = rbi * 64 + w * 16 + g;                 // row of the B slice (and nb + 8)
         const int kc = kti * 4 + t4;                          // 16-byte chunk of the slice's K
         uint32_t lo[4] = {0u, 0u, 0u, 0u}, hi[4] = {0u, 0u, 0u, 0u};
