@@ -41,7 +41,7 @@ constexpr int B_BYTES = BN * BK * 2;          // 32 KB
 constexpr int RAW_BYTES = (BN / 64) * 2 * tc::UNIT;   // 16 KB: raw int8 units of one slice (int4: less)
 constexpr int STAGE = A_BYTES + B_BYTES;      // one slice's MMA operands
 constexpr int RSTAGES = 4;                    // raw weight ring, ahead of the operand ring
-constexpr int MAX_STAGES = 4, MAX_RSTAGES = 8;  // ring depths a kernel variant may use (below)
+constexpr int MAX_STAGES = 6, MAX_RSTAGES = 8;  // ring depths a kernel variant may use (below)
 constexpr int CONV = 384;                     // warps 0-11 convert (three per SM sub-partition, to hide
                                               // each other's latency); warps 0-3 then run the epilogue
 constexpr int MMA_WARP = CONV / 32;           // TMEM owner, MMA issuer
@@ -405,19 +405,28 @@ cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
   static const int deep = env_int("AF_GEMM_DEEP", 1);
   // MM = 2: 128-column tiles with three operand and eight raw slices, 256-column with two and four
   // (the second A tile per slice takes the shared memory of one operand stage)
-  const int var = MM == 2 ? (narrow ? 3 : 4) : (narrow ? (deep >= 1 ? 1 : 0) : 2);
-  static const size_t smems[5] = {smem_for<128, 3, 4>(), smem_for<128, 4, 8>(), smem_for<256, 3, 4>(),
-                                  smem_for<128, 3, 8, 2>(), smem_for<256, 2, 4, 2>()};
-  void* const fns[2][5] = {
+  int var = MM == 2 ? (narrow ? 3 : 4) : (narrow ? (deep >= 1 ? 1 : 0) : 2);
+  // deeper operand rings at the same shared memory (measurement variants, AF_GEMM_RING=1): 128-column
+  // tiles with six operand and four raw slices, two-tile 256-column with three and two
+  static const int ring = env_int("AF_GEMM_RING", 0);
+  if (ring == 1 && var == 1) var = 5;
+  if (ring == 1 && var == 4) var = 6;
+  constexpr int NV = 7;
+  static const size_t smems[NV] = {smem_for<128, 3, 4>(), smem_for<128, 4, 8>(), smem_for<256, 3, 4>(),
+                                   smem_for<128, 3, 8, 2>(), smem_for<256, 2, 4, 2>(), smem_for<128, 6, 4>(),
+                                   smem_for<256, 3, 2, 2>()};
+  void* const fns[2][NV] = {
       {(void*)gemm_tc_kernel<false, 128, 3, 4, 1>, (void*)gemm_tc_kernel<false, 128, 4, 8, 1>,
        (void*)gemm_tc_kernel<false, 256, 3, 4, 1>, (void*)gemm_tc_kernel<false, 128, 3, 8, 2>,
-       (void*)gemm_tc_kernel<false, 256, 2, 4, 2>},
+       (void*)gemm_tc_kernel<false, 256, 2, 4, 2>, (void*)gemm_tc_kernel<false, 128, 6, 4, 1>,
+       (void*)gemm_tc_kernel<false, 256, 3, 2, 2>},
       {(void*)gemm_tc_kernel<true, 128, 3, 4, 1>, (void*)gemm_tc_kernel<true, 128, 4, 8, 1>,
        (void*)gemm_tc_kernel<true, 256, 3, 4, 1>, (void*)gemm_tc_kernel<true, 128, 3, 8, 2>,
-       (void*)gemm_tc_kernel<true, 256, 2, 4, 2>}};
+       (void*)gemm_tc_kernel<true, 256, 2, 4, 2>, (void*)gemm_tc_kernel<true, 128, 6, 4, 1>,
+       (void*)gemm_tc_kernel<true, 256, 3, 2, 2>}};
   const size_t smem = smems[var];
   void* fn = fns[i4 ? 1 : 0][var];
-  static PerDeviceOnce attr[2][5];
+  static PerDeviceOnce attr[2][NV];
   const cudaError_t ae = attr[i4 ? 1 : 0][var].run(
       [fn, smem] { return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); });
   if (ae != cudaSuccess) return ae;
