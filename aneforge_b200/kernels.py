@@ -208,6 +208,8 @@ def gemv_tc_expert(x, tiles, scales, N, K, E, wf=R.W_I8, epi=R.EPI_F32, y=None, 
                    scratch=None):
   """Tensor-core GEMV over E experts' tiles stored back to back; expert = sel[slot] or fixed_e."""
   import torch
+  if sel is None and not 0 <= fixed_e < E:
+    raise ValueError(f"fixed_e={fixed_e} outside the {E} experts of these tiles")
   NB = x.shape[0]
   cols = N // 2 if epi == R.EPI_SWIGLU else N
   if y is None:

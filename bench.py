@@ -209,7 +209,7 @@ def algorithmic_bytes_per_step(cfg, NB, pos, compress="int8", qkv_bias=False, mo
   D, H, KV, dh, F, V, L = cfg.dim, cfg.n_heads, cfg.n_kv_heads, cfg.dh, cfg.ffn_dim, cfg.vocab, cfg.n_layers
   if cfg.extra.get("n_experts"):
     # MoE: attention + router in `compress`; the experts a step reads in `moe_compress` - the top k at
-    # batch 1, every expert for larger batches (the dense per-row-weighted path)
+    # batch 1, every expert once for larger batches (each expert's routed rows share one pass)
     E, k = cfg.extra["n_experts"], cfg.extra["n_experts_per_tok"]
     attn = _proj_bytes((H + 2 * KV) * dh * D, (H + 2 * KV) * dh, compress) + _proj_bytes(D * H * dh, D, compress)
     router = _proj_bytes(E * D, E, compress)
@@ -404,8 +404,9 @@ def run_b200(args):
   # ---- dominant kernel: the fused gate|up int8 GEMV, timed alone on the program stream over the
   # 32 layers' own weights (3.7 GB > L2, so every launch streams from HBM)
   if "experts" in m._dev["layers"][0]:
-    # MoE: one expert's gate|up (2 F x D) per launch, cycling over the layers' experts
-    E = cfg.extra["n_experts"]
+    # MoE: one expert's gate|up (2 F x D) per launch, cycling over the layers' experts (the ones this
+    # GPU holds: all of them, or its share under expert parallelism)
+    E = m._dev["layers"][0]["experts"].E
     gu = [_ExpertGU(m._dev["layers"][i]["experts"], e) for i in range(cfg.n_layers) for e in range(E)][:4 * cfg.n_layers]
   else:
     gu = [m._dev["layers"][i]["gu"] for i in range(cfg.n_layers)]
