@@ -138,9 +138,13 @@ def sample_token(logits, temperature: float = 0.0, top_p: float = 1.0, top_k: in
 # activation buffers and shapes: h (fp32 residual [NB, D]), xn (fp16 [NB, D]), qkv, att, act, pos,
 # NB, M; `lw` is the layer's packed device weights (names of bound buffers, see _bind_layer).
 
-# Row counts from which a tiled projection runs as the tensor-core GEMM (prefill) instead of the GEMV:
-# the GEMV streams the weights once per 16 rows, the GEMM once per 128.
+# Row counts from which a tiled projection runs as the tensor-core GEMM instead of the GEMV: the GEMV
+# streams the weights once per 16 rows, the GEMM once per 128 (or 256) but walks its k slices at a
+# fixed pace whatever the rows. Prefill programs switch at 32 rows; decode programs (batches of
+# sequences) keep the GEMV below 128: measured on Mixtral at batch 32, the attention projections took
+# ~60 µs a launch on the GEMM against ~15 on two 16-row GEMV passes.
 GEMM_MIN_ROWS = 32
+DECODE_GEMM_MIN_ROWS = 128
 
 
 def _emit_linear(pb, ctx, name, lin: DevLinear, x, y, epi, nb=None):
@@ -149,7 +153,7 @@ def _emit_linear(pb, ctx, name, lin: DevLinear, x, y, epi, nb=None):
   if lin.kind == "int8":
     kv["s"] = f"{name}.s"
   if lin.kind in ("int8", "int4_g32") and lin.tiled:
-    if nb >= GEMM_MIN_ROWS:
+    if nb >= ctx.get("gemm_min", GEMM_MIN_ROWS):
       kv["gemm"] = 1                                 # prompt rows: the tcgen05 GEMM
     else:
       nbytes = R.load_library().af_gemv_tc_scratch_bytes(lin.N, lin.K, nb)
@@ -615,7 +619,7 @@ class LlamaPrefill:
       if key in d:
         pb.buf(f"L{li}.{key}", d[key].numel() * 2, "weight")
 
-  def _ctx(self, NB, M):
+  def _ctx(self, NB, M, decode=True):
     cfg, d = self.cfg, self._load()
     G = cfg.n_heads // cfg.n_kv_heads
     # split-K over the cache: one split per 64 cache rows (the kernel also keeps >= 64 keys per
@@ -626,7 +630,8 @@ class LlamaPrefill:
     # through scratch (the last CTA of each head merges them).
     nsplit = decode_nsplit(M, cfg.n_kv_heads, NB)
     return {"NB": NB, "M": M, "nsplit": nsplit, "scale": d["scale"], "kvc": d["kvc"], "expand": G > 1 and d["kvc"] != 1.0,
-            "tp": self.tp is not None, "tp_rank": self.tp.rank if self.tp is not None else 0, "D": cfg.dim}
+            "tp": self.tp is not None, "tp_rank": self.tp.rank if self.tp is not None else 0, "D": cfg.dim,
+            "gemm_min": DECODE_GEMM_MIN_ROWS if decode else GEMM_MIN_ROWS}
 
   # -- programs
   def _decoder(self, M, NB=1):
@@ -834,7 +839,7 @@ class LlamaPrefill:
     cfg, d = self.cfg, self._load()
     D, H, KV, dh, V = cfg.dim, cfg.n_heads, cfg.n_kv_heads, cfg.dh, cfg.vocab
     Q = (H + 2 * KV) * dh
-    ctx = self._ctx(seq, seq)
+    ctx = self._ctx(seq, seq, decode=False)
     pb = PlanBuilder()
     pb.buf("ids", 4 * seq, "in"); pb.buf("hid", 2 * seq * D, "out")
     pb.buf("h", 4 * seq * D, "tmp"); pb.buf("xn", 2 * seq * D, "tmp"); pb.buf("qkv", 4 * seq * Q, "tmp")

@@ -522,7 +522,7 @@ def run_b200(args):
   return result
 
 
-def kernel_bench(name, reps, warmup):
+def kernel_bench(name, reps, warmup, nb=1):
   """One hot kernel alone on the device (the `--kernel` mode; the small case the ncu summaries in
   profiles/ are captured on). Weights rotate over enough copies that every launch streams from HBM.
   Returns a dict with the launch time (CUDA events on the launching stream) and algorithmic GB/s."""
@@ -652,24 +652,24 @@ def kernel_bench(name, reps, warmup):
     del W
     t0 = K.pack_i4_tiles(pk, sc, N, Kd)
     tiles = [t0] + [t0.clone() for _ in range(copies - 1)]
-    x = torch.randn(1, Kd, generator=g, device=dev).half()
+    x = torch.randn(nb, Kd, generator=g, device=dev).half()
     y = K.gemv_tc_i4(x, tiles[0], N, Kd, epi=epi)
-    scr, _ = K.gemv_tc_scratch(N, Kd, 1, dev)
-    nbytes = N * Kd // 2 + 2 * (N * Kd // 32) + 2 * Kd + y.numel() * y.element_size() * (2 if epi == R.EPI_RESID else 1)
+    scr, _ = K.gemv_tc_scratch(N, Kd, nb, dev)
+    nbytes = N * Kd // 2 + 2 * (N * Kd // 32) + 2 * Kd * nb + y.numel() * y.element_size() * (2 if epi == R.EPI_RESID else 1)
     fn = lambda i: K.gemv_tc_i4(x, tiles[i % copies], N, Kd, epi=epi, y=y, scratch=scr)
-    what = f"gemv_tc int4_g32 {N}x{Kd} epi={epi}"
+    what = f"gemv_tc int4_g32 {N}x{Kd} epi={epi} rows={nb}"
   elif name in ("gemv_gu", "gemv_cfg1", "gemv_qkv", "gemv_o", "gemv_down"):
     N, Kd, epi = {"gemv_gu": (2 * F, D, R.EPI_SWIGLU), "gemv_cfg1": (4096, 4096, R.EPI_F16),
                   "gemv_qkv": ((H + 2 * KV) * dh, D, R.EPI_F32), "gemv_o": (D, H * dh, R.EPI_RESID),
                   "gemv_down": (D, F, R.EPI_RESID)}[name]
     copies = max(2, -(-300_000_000 // (N * Kd)))            # > 2x L2 of weights in rotation
     tiles, sc = int8_tiles(N, Kd, copies)
-    x = torch.randn(1, Kd, generator=g, device=dev).half()
+    x = torch.randn(nb, Kd, generator=g, device=dev).half()
     y = K.gemv_tc(x, tiles[0], sc, N, Kd, epi=epi)
-    scr, _ = K.gemv_tc_scratch(N, Kd, 1, dev)
-    nbytes = N * Kd + 2 * N + 2 * Kd + y.numel() * y.element_size() * (2 if epi == R.EPI_RESID else 1)
+    scr, _ = K.gemv_tc_scratch(N, Kd, nb, dev)
+    nbytes = N * Kd + 2 * N + 2 * Kd * nb + y.numel() * y.element_size() * (2 if epi == R.EPI_RESID else 1)
     fn = lambda i: K.gemv_tc(x, tiles[i % copies], sc, N, Kd, epi=epi, y=y, scratch=scr)
-    what = f"gemv_tc int8 {N}x{Kd} epi={epi}"
+    what = f"gemv_tc int8 {N}x{Kd} epi={epi} rows={nb}"
   elif name == "attn":
     M, pos = 1024, 576
     kc = torch.randn(1, KV, M, dh, generator=g, device=dev).half()
@@ -901,7 +901,7 @@ def main():
     return
   if args.kernel:
     for name in args.kernel.split(","):
-      out.emit(kernel_bench(name, args.reps, max(args.warmup, 3)))
+      out.emit(kernel_bench(name, args.reps, max(args.warmup, 3), args.batch))
     return
   if args.impl == "reference":
     if rank != 0:
