@@ -244,7 +244,7 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
       for (int kt = kc; kt < kce; kt += F::ks) {
         const int nk = min(F::ks, kce - kt);
         if (!mbar_wait(&sh->full[stage], phase)) { stuck = true; break; }
-        consume_stage<I4, NT, CW / 4>(ring + (size_t)stage * F::stage, nk, xsl + (kt - kc) * 32, tc::XSTRIDE, a.NB, lane,
+        consume_stage<I4, NT, CW / 4>(ring + (size_t)stage * F::stage, nk, xsl + (kt - kc) * 32, tc::XSTRIDE, a.nlive, lane,
                                       rtw, par, acc, acc2);
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh->empty[stage]);

@@ -185,10 +185,12 @@ AF_DEV void consume_stage(const unsigned char* sb, int nk, const __half* xk, int
       float tmp[NT][4];
       i4x8_to_frag(w.x, A);
 #pragma unroll
-      for (int n = 0; n < NT; ++n) mma_16816_z(tmp[n], A, xv[n].x, xv[n].y);
+      for (int n = 0; n < NT; ++n)
+        if (n * 8 < NB) mma_16816_z(tmp[n], A, xv[n].x, xv[n].y);   // n-tiles past the live rows: skipped
       i4x8_to_frag(w.y, A);
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
+        if (n * 8 >= NB) continue;
         mma_16816(tmp[n], A, xv[n].z, xv[n].w);
         ac[n][0] = fmaf(sc.x, tmp[n][0], ac[n][0]);
         ac[n][1] = fmaf(sc.x, tmp[n][1], ac[n][1]);
@@ -201,11 +203,13 @@ AF_DEV void consume_stage(const unsigned char* sb, int nk, const __half* xk, int
       i8x4_to_h2x2(w.x, A[0], A[1]);
       i8x4_to_h2x2(w.y, A[2], A[3]);
 #pragma unroll
-      for (int n = 0; n < NT; ++n) mma_16816(ac[n], A, xv[n].x, xv[n].y);
+      for (int n = 0; n < NT; ++n)
+        if (n * 8 < NB) mma_16816(ac[n], A, xv[n].x, xv[n].y);
       i8x4_to_h2x2(w.z, A[0], A[1]);
       i8x4_to_h2x2(w.w, A[2], A[3]);
 #pragma unroll
-      for (int n = 0; n < NT; ++n) mma_16816(ac[n], A, xv[n].z, xv[n].w);
+      for (int n = 0; n < NT; ++n)
+        if (n * 8 < NB) mma_16816(ac[n], A, xv[n].z, xv[n].w);
     }
   }
 }
