@@ -109,9 +109,10 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
   }
   using F = tc::Fmt<I4>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  unsigned char* ring = smem_raw;                                          // [STAGES][F::stage]
-  TcShared* sh = reinterpret_cast<TcShared*>(smem_raw + tc::STAGES * F::stage);
-  __half* xring = reinterpret_cast<__half*>(smem_raw + tc::STAGES * F::stage + SH_BYTES);
+  const int NS = a.nst;                                                    // weight ring depth (<= STAGES)
+  unsigned char* ring = smem_raw;                                          // [NS][F::stage]
+  TcShared* sh = reinterpret_cast<TcShared*>(smem_raw + NS * F::stage);
+  __half* xring = reinterpret_cast<__half*>(smem_raw + NS * F::stage + SH_BYTES);
   const int xslot_halves = a.NB * tc::XSTRIDE;                             // one x chunk
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -128,7 +129,7 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
   }
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < tc::STAGES; ++s) {
+    for (int s = 0; s < NS; ++s) {
       mbar_init(&sh->full[s], 1);
       mbar_init(&sh->empty[s], CW);
     }
@@ -164,13 +165,13 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
         int kt = kc;
         if (!waited) {
           // chunk 0: weights first, then wait for the producer kernel of x, then x
-          for (; kt < kce && in_flight < tc::STAGES; kt += F::ks) {
+          for (; kt < kce && in_flight < NS; kt += F::ks) {
             const int nk = min(F::ks, kce - kt);
             mbar_arrive_expect_tx(&sh->full[stage], (uint32_t)nk * F::unit);
             bulk_w(ring + (size_t)stage * F::stage, W + ((size_t)rb * KT + kt) * F::unit, nk * F::unit,
                    &sh->full[stage], a.evict_first, pol);
             ++in_flight;
-            if (++stage == tc::STAGES) { stage = 0; phase ^= 1; }
+            if (++stage == NS) { stage = 0; phase ^= 1; }
           }
           pdl_wait();
           waited = true;
@@ -192,8 +193,8 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
           mbar_arrive_expect_tx(&sh->full[stage], (uint32_t)nk * F::unit);
           bulk_w(ring + (size_t)stage * F::stage, W + ((size_t)rb * KT + kt) * F::unit, nk * F::unit,
                  &sh->full[stage], a.evict_first, pol);
-          in_flight = min(in_flight + 1, tc::STAGES);
-          if (++stage == tc::STAGES) { stage = 0; phase ^= 1; }
+          in_flight = min(in_flight + 1, NS);
+          if (++stage == NS) { stage = 0; phase ^= 1; }
         }
       }
       u += ktb - kta;
@@ -203,7 +204,7 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
     // shared memory must outlive every copy this thread issued: wait (bounded) for the last use of
     // each weight stage and x slot to land before the thread exits
     for (int i = 0; i < in_flight; ++i) {
-      if (--stage < 0) { stage = tc::STAGES - 1; phase ^= 1; }
+      if (--stage < 0) { stage = NS - 1; phase ^= 1; }
       mbar_wait(&sh->full[stage], phase);
     }
     for (int i = 0; i < tc::XSLOTS; ++i) {
@@ -221,7 +222,7 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
   // of a k tile are 8 consecutive x values: one 16-byte shared load per k tile.
   const int g = lane >> 2, t = lane & 3;
   const int rtw = warp & 3, par = warp >> 2;          // par: 0 with 4 consumer warps
-  float* red = reinterpret_cast<float*>(smem_raw + tc::STAGES * F::stage + SH_BYTES +
+  float* red = reinterpret_cast<float*>(smem_raw + NS * F::stage + SH_BYTES +
                                         (size_t)tc::XSLOTS * xslot_halves * 2);       // [4][32][NT*4]
   pdl_wait();
   pdl_trigger();
@@ -248,7 +249,7 @@ __global__ void __launch_bounds__((Cw<I4>::n + 1) * 32) gemv_tc_kernel(GemvTcArg
                                       rtw, par, acc, acc2);
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh->empty[stage]);
-        if (++stage == tc::STAGES) { stage = 0; phase ^= 1; }
+        if (++stage == NS) { stage = 0; phase ^= 1; }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh->xempty[xs]);
@@ -397,9 +398,16 @@ static size_t smem_for_ctas_per_sm(size_t need, int k) {
 
 static int sm_count() { return device_attr(cudaDevAttrMultiProcessorCount, 148); }
 
+// weight ring depth per format (AF_TC_STAGES / AF_TC_STAGES_I4, 2..6)
+static int ring_stages(bool i4) {
+  static const int s8 = env_int("AF_TC_STAGES", tc::STAGES), s4 = env_int("AF_TC_STAGES_I4", tc::STAGES);
+  const int s = i4 ? s4 : s8;
+  return s < 2 ? 2 : (s > tc::STAGES ? tc::STAGES : s);
+}
+
 static size_t smem_bytes(int NB, bool i4) {
   // weight ring | barriers | x ring | odd-warp sums [4 row tiles][32 lanes][8 floats]
-  return (size_t)tc::STAGES * (i4 ? tc::STAGE_BYTES4 : tc::STAGE_BYTES) + SH_BYTES +
+  return (size_t)ring_stages(i4) * (i4 ? tc::STAGE_BYTES4 : tc::STAGE_BYTES) + SH_BYTES +
          (size_t)tc::XSLOTS * NB * tc::XSTRIDE * 2 + tc::WARPS * 32 * 8 * 4;
 }
 
@@ -582,6 +590,7 @@ static cudaError_t launch_tc(GemvTcArgs a, cudaStream_t st, bool pdl) {
   plan_geometry(a.N, a.K, a.NB, EPI, I4, &G, &maxc, &cs);
   a.maxc = maxc;
   a.csize = cs;
+  a.nst = ring_stages(I4);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G);
   cfg.blockDim = dim3((Cw<I4>::n + 1) * 32);
