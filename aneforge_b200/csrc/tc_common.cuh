@@ -98,8 +98,10 @@ template <bool I4> struct Cw { static constexpr int n = I4 ? 8 : 4; };
 template <int CW>
 AF_DEV void consumer_sync_n() { asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory"); }
 
+// (not volatile: the MMA has no effect beyond its outputs, so the compiler may interleave independent
+// MMAs of neighbouring tiles; measured 1-2 % faster on the decode GEMVs)
 AF_DEV void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -109,7 +111,7 @@ AF_DEV void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32
 // d = a . b (a fresh accumulation: the C operand is zero)
 AF_DEV void mma_16816_z(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   const float z = 0.f;
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%10,%10,%10,%10};\n"
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
