@@ -99,6 +99,7 @@ struct GemvTcArgs {
   // set by the launcher
   int Np = 0, Kp = 0, S = 1, maxc = 1;
   int nst = 6;                 // set by the launcher: weight ring stages (<= tc::STAGES)
+  int ksplit = 1;              // set by the launcher: prefill GEMM k splits per output tile (RESID only)
   int nlive = 0;               // set in the kernel: batch rows this launch computes (NB unless routed)
   int rbase = 0;               // set in the kernel: offset of this launch's first row in `rows`
   int csize = 0;               // > 1: thread-block clusters of csize CTAs split each row block's k range

@@ -121,11 +121,15 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
   GemmShared* sh = reinterpret_cast<GemmShared*>(rawring + NR * T::RAW_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int MT = (a.NB + gm::BM * MM - 1) / (gm::BM * MM);
-  const int mt = blockIdx.x % MT, nt = blockIdx.x / MT;     // M fastest: CTAs sharing a weight tile run together
+  const int tiles = MT * ((a.N + T::BN - 1) / T::BN);
+  const int ksp = blockIdx.x / tiles, tile = blockIdx.x % tiles;  // k split of this CTA (split-K: RESID only)
+  const int mt = tile % MT, nt = tile / MT;                 // M fastest: CTAs sharing a weight tile run together
   const int m0 = mt * gm::BM * MM, n0 = nt * T::BN;
   const int mlive = min(MM, (a.NB - m0 + gm::BM - 1) / gm::BM);   // M tiles of this CTA holding prompt rows
   const int KT = a.K / 32, RB = a.Np / 64;
-  const int KB = (a.K + gm::BK - 1) / gm::BK;
+  const int KBT = (a.K + gm::BK - 1) / gm::BK;
+  const int kb0 = ksp * KBT / a.ksplit;                    // this CTA's slices [kb0, kb0 + KB)
+  const int KB = (ksp + 1) * KBT / a.ksplit - kb0;
   constexpr int UNIT = I4 ? tc::UNIT4 : tc::UNIT;
 
   if (threadIdx.x == 0) {
@@ -167,7 +171,7 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
           break;
         }
         unsigned char* rs = rawring + r * T::RAW_BYTES;
-        const int kt = kb * 2, nk = min(2, KT - kt);
+        const int kt = (kb0 + kb) * 2, nk = min(2, KT - kt);
         uint32_t bytes = 0;
         for (int rbi = 0; rbi < T::BN / 64; ++rbi)
           if (n0 / 64 + rbi < RB) bytes += (uint32_t)nk * UNIT;
@@ -200,7 +204,7 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
         }
         mbar_arrive_expect_tx(&sh->a_full[s], (uint32_t)(mlive * gm::A_BYTES));
         for (int i = 0; i < mlive; ++i)
-          tma_load_2d(smem + s * STG + i * gm::A_BYTES, &amap, kb * gm::BK, m0 + i * gm::BM, &sh->a_full[s]);
+          tma_load_2d(smem + s * STG + i * gm::A_BYTES, &amap, (kb0 + kb) * gm::BK, m0 + i * gm::BM, &sh->a_full[s]);
         issued = kb + 1;
       }
       for (int kb = issued - 1; kb >= 0 && kb >= issued - NS; --kb) {
@@ -247,7 +251,7 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
       unsigned char* st = smem + s * STG;
       unsigned char* Bs = st + MM * gm::A_BYTES;
       const unsigned char* Rw = rawring + r * T::RAW_BYTES;
-      const int kt0 = kb * 2;
+      const int kt0 = (kb0 + kb) * 2;
 #pragma unroll 4
       for (int q = t; q < T::BN / 64 * 2 * 128; q += gm::CONV) {
         const int u = q >> 7, rbi = u >> 1, kti = u & 1;
@@ -308,7 +312,7 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
           float x = __uint_as_float(v[j]);
           if (n < a.N) {
             if (!I4) x = __fmul_rn(x, h2f(a.scale[n]));
-            if (a.bias) x = __fadd_rn(x, h2f(a.bias[n]));
+            if (a.bias && ksp == 0) x = __fadd_rn(x, h2f(a.bias[n]));
           }
           f[j] = x;
         }
@@ -332,6 +336,7 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
             const size_t o = (size_t)m * a.ldy + n;
             if (a.epi == EPI_F32) reinterpret_cast<float*>(a.y)[o] = f[j];
             else if (a.epi == EPI_F16) reinterpret_cast<__half*>(a.y)[o] = f2h(f[j]);
+            else if (a.ksplit > 1) atomicAdd(reinterpret_cast<float*>(a.y) + o, f[j]);   // k splits meet in y
             else reinterpret_cast<float*>(a.y)[o] = __ldcg(reinterpret_cast<const float*>(a.y) + o) + f[j];
           }
         }
@@ -411,19 +416,30 @@ cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
   static const int ring = env_int("AF_GEMM_RING", 0);
   if (ring == 1 && var == 1) var = 5;
   if (ring == 1 && var == 4) var = 6;
-  constexpr int NV = 7;
+  // split-K for the residual epilogue (o / down prompt shapes, fewer tiles than SMs): AF_GEMM_SPLITK=S
+  // runs S CTAs per 128-column tile over disjoint k ranges on the half-size rings (two CTAs per SM),
+  // each adding its partial into the fp32 residual atomically (summation order then varies by run)
+  static const int splitk = env_int("AF_GEMM_SPLITK", 0);
+  a.ksplit = 1;
+  const int KBT = (a.K + gm::BK - 1) / gm::BK;
+  if (splitk >= 2 && a.epi == EPI_RESID && !a.bias && MM == 1 && BNV == 128 &&
+      MT * ((a.N + 127) / 128) * splitk <= 2 * sms && KBT >= 8 * splitk) {
+    var = 7;
+    a.ksplit = splitk;
+  }
+  constexpr int NV = 8;
   static const size_t smems[NV] = {smem_for<128, 3, 4>(), smem_for<128, 4, 8>(), smem_for<256, 3, 4>(),
                                    smem_for<128, 3, 8, 2>(), smem_for<256, 2, 4, 2>(), smem_for<128, 6, 4>(),
-                                   smem_for<256, 3, 2, 2>()};
+                                   smem_for<256, 3, 2, 2>(), smem_for<128, 2, 4>()};
   void* const fns[2][NV] = {
       {(void*)gemm_tc_kernel<false, 128, 3, 4, 1>, (void*)gemm_tc_kernel<false, 128, 4, 8, 1>,
        (void*)gemm_tc_kernel<false, 256, 3, 4, 1>, (void*)gemm_tc_kernel<false, 128, 3, 8, 2>,
        (void*)gemm_tc_kernel<false, 256, 2, 4, 2>, (void*)gemm_tc_kernel<false, 128, 6, 4, 1>,
-       (void*)gemm_tc_kernel<false, 256, 3, 2, 2>},
+       (void*)gemm_tc_kernel<false, 256, 3, 2, 2>, (void*)gemm_tc_kernel<false, 128, 2, 4, 1>},
       {(void*)gemm_tc_kernel<true, 128, 3, 4, 1>, (void*)gemm_tc_kernel<true, 128, 4, 8, 1>,
        (void*)gemm_tc_kernel<true, 256, 3, 4, 1>, (void*)gemm_tc_kernel<true, 128, 3, 8, 2>,
        (void*)gemm_tc_kernel<true, 256, 2, 4, 2>, (void*)gemm_tc_kernel<true, 128, 6, 4, 1>,
-       (void*)gemm_tc_kernel<true, 256, 3, 2, 2>}};
+       (void*)gemm_tc_kernel<true, 256, 3, 2, 2>, (void*)gemm_tc_kernel<true, 128, 2, 4, 1>}};
   const size_t smem = smems[var];
   void* fn = fns[i4 ? 1 : 0][var];
   static PerDeviceOnce attr[2][NV];
@@ -431,7 +447,7 @@ cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
       [fn, smem] { return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); });
   if (ae != cudaSuccess) return ae;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(MT * NT));
+  cfg.gridDim = dim3((unsigned)(MT * NT * a.ksplit));
   cfg.blockDim = dim3(gm::THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;

@@ -612,7 +612,8 @@ def kernel_bench(name, reps, warmup, nb=1):
     M, N, Kd = {"gemm_gu": (512, 2 * F, D), "gemm_i4_gu": (2048, 2 * 29568, 8192),
                 "gemm_qkv": (512, (H + 2 * KV) * dh, D), "gemm_o": (512, D, H * dh),
                 "gemm_down": (512, D, F)}[name]
-    epi = R.EPI_SWIGLU if name in ("gemm_gu", "gemm_i4_gu") else R.EPI_F16
+    # the prefill program's epilogues: SwiGLU for gate|up, f32 for qkv, the residual add for o / down
+    epi = {"gemm_gu": R.EPI_SWIGLU, "gemm_i4_gu": R.EPI_SWIGLU, "gemm_qkv": R.EPI_F32}.get(name, R.EPI_RESID)
     W = (torch.randn(N, Kd, generator=g, device=dev) * 0.02).half()
     if i4:
       pk, sc = K.quantize_g32_i4(W); tiles = K.pack_i4_tiles(pk, sc, N, Kd); sc = None
@@ -620,7 +621,8 @@ def kernel_bench(name, reps, warmup, nb=1):
       q, sc = K.quantize_per_row_i8(W); tiles = K.pack_i8_tiles(q)
     del W
     x = torch.randn(M, Kd, generator=g, device=dev).half()
-    y = torch.empty(M, N // 2 if epi == R.EPI_SWIGLU else N, device=dev, dtype=torch.float16)
+    y = (torch.empty(M, N // 2, device=dev, dtype=torch.float16) if epi == R.EPI_SWIGLU
+         else torch.zeros(M, N, device=dev, dtype=torch.float32))
     fn = lambda i: K.gemm_tc(x, tiles, sc, N, Kd, wf=R.W_I4G32 if i4 else R.W_I8, epi=epi, y=y)
     flops = 2.0 * M * N * Kd
     with torch.cuda.stream(st):
@@ -641,7 +643,7 @@ def kernel_bench(name, reps, warmup, nb=1):
       tpk, tkind = 1590.0, "fallback"
     tf = flops / (us * 1e-6) / 1e12
     return {"kernel": name, "what": f"gemm_tc {'int4_g32' if i4 else 'int8'} M={M} N={N} K={Kd} "
-                                    f"{'swiglu' if epi == R.EPI_SWIGLU else 'f16'}",
+                                    f"{ {R.EPI_SWIGLU: 'swiglu', R.EPI_F32: 'f32'}.get(epi, 'resid') }",
             "us_per_launch": round(us, 1), "tflops": round(tf, 1), "peak_tflops": tpk, "peak_kind": tkind,
             "frac": round(tf / tpk, 4), "reps": reps, "warmup": warmup}
   if name in I4:                                            # Qwen2-72B shapes, group-32 int4
