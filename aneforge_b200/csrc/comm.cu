@@ -94,16 +94,21 @@ AF_HD size_t p2p_data_off(int set, int src, int T, size_t cap) { return ((size_t
 AF_HD size_t p2p_epoch_off(int T, size_t cap) { return (size_t)2 * T * cap * 8; }
 AF_HD size_t p2p_bytes(int T, size_t cap) { return p2p_epoch_off(T, cap) + 16; }
 
-__global__ void __launch_bounds__(1024) p2p_all_reduce_kernel(P2pPeers peers, int T, int rank, size_t cap,
-                                                               const float* src, float* dst, float* addto, int n,
-                                                               int* err) {
+// The words are split over the grid's CTAs (each CTA pushes and polls its own share); every CTA reads
+// the epoch when it starts, and the last CTA to finish (a ticket next to the epoch) stores the new one,
+// so no CTA of this call can see it early.
+__global__ void __launch_bounds__(256) p2p_all_reduce_kernel(P2pPeers peers, int T, int rank, size_t cap,
+                                                              const float* src, float* dst, float* addto, int n,
+                                                              int* err) {
   char* mine = peers.base[rank];
   unsigned* epoch = reinterpret_cast<unsigned*>(mine + p2p_epoch_off(T, cap));
+  unsigned* ticket = epoch + 1;
   pdl_wait();
   const unsigned e = *reinterpret_cast<volatile unsigned*>(epoch) + 1u;
   const int set = (int)(e & 1u);
+  const int i0 = blockIdx.x * blockDim.x + threadIdx.x, step = gridDim.x * blockDim.x;
   // push: word i of this rank's slot on every rank
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+  for (int i = i0; i < n; i += step) {
     const unsigned long long w = ((unsigned long long)e << 32) | __float_as_uint(__ldcg(src + i));
     for (int p = 0; p < T; ++p) {
       unsigned long long* d = reinterpret_cast<unsigned long long*>(peers.base[p] + p2p_data_off(set, rank, T, cap)) + i;
@@ -112,7 +117,7 @@ __global__ void __launch_bounds__(1024) p2p_all_reduce_kernel(P2pPeers peers, in
   }
   // reduce: every rank's word i, in rank order, once it carries this call's epoch
   bool late = false;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+  for (int i = i0; i < n; i += step) {
     float acc = 0.f;
     for (int s = 0; s < T; ++s) {
       const unsigned long long* w = reinterpret_cast<const unsigned long long*>(mine + p2p_data_off(set, s, T, cap)) + i;
@@ -130,8 +135,17 @@ __global__ void __launch_bounds__(1024) p2p_all_reduce_kernel(P2pPeers peers, in
   }
   if (late) af_set_err(err, AF_DEV_WAIT_TIMEOUT);
   __syncthreads();
-  if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(epoch) = e;
+  if (threadIdx.x == 0 && atomicAdd(ticket, 1u) == gridDim.x - 1) {
+    *ticket = 0u;                      // every CTA of this call has read the epoch: the last one moves it
+    *reinterpret_cast<volatile unsigned*>(epoch) = e;
+  }
   pdl_trigger();
+}
+
+// CTAs of the peer all-reduce for n words: 256 threads each, up to 32 (one word per thread below that)
+static int p2p_ctas(size_t n) {
+  const size_t c = (n + 255) / 256;
+  return c < 1 ? 1 : (c > 32 ? 32 : (int)c);
 }
 
 cudaError_t comm_all_reduce_f32(void* comm, const float* src, float* dst, size_t n, cudaStream_t st, std::string& why,
@@ -141,10 +155,9 @@ cudaError_t comm_all_reduce_f32(void* comm, const float* src, float* dst, size_t
   if (c->p2p && n <= c->cap) {
     P2pPeers peers;
     for (int r = 0; r < P2P_MAX_RANKS; ++r) peers.base[r] = r < c->nranks ? c->peer[r] : nullptr;
-    const int threads = n >= 1024 ? 1024 : (int)((n + 31) / 32 * 32);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(1);
-    cfg.blockDim = dim3(threads);
+    cfg.gridDim = dim3(p2p_ctas(n));
+    cfg.blockDim = dim3(256);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
