@@ -297,13 +297,17 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
     if (!ok) {
       af_set_err(a.err, AF_DEV_WAIT_TIMEOUT);
     } else {
+      // A warp's 32 TMEM lanes are 32 output rows; each 32-column chunk goes through a padded
+      // shared-memory tile (the operand ring is idle once the accumulators are final) so that the
+      // global loads / stores walk rows with consecutive lanes on consecutive columns (coalesced).
+      float* stage = reinterpret_cast<float*>(smem) + warp * (32 * 33);
+      constexpr int W_SWIGLU = 16;                           // outputs per row per chunk (two groups of 8)
       for (int mi = 0; mi < mlive; ++mi) {
-      const int m = m0 + mi * gm::BM + warp * 32 + lane;
+      const int rowbase = m0 + mi * gm::BM + warp * 32;
 #pragma unroll 1
       for (int c0 = 0; c0 < T::BN; c0 += 32) {
         uint32_t v[32];
         tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(mi * T::BN + c0), v);
-        if (m >= a.NB) continue;
         const int nbase = n0 + c0;
         float f[32];
 #pragma unroll
@@ -316,30 +320,39 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
           }
           f[j] = x;
         }
-        if (a.epi == EPI_SWIGLU) {
-          // rows 16i..16i+7 gate, 16i+8..16i+15 up -> 8 outputs per 16 rows
+        const bool swiglu = a.epi == EPI_SWIGLU;
+        if (swiglu) {
+          // rows 16i..16i+7 gate, 16i+8..16i+15 up -> outputs 8i..8i+7 of the chunk
 #pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            const int r0 = nbase + 16 * i;
-            if (r0 + 16 > a.N) continue;
-            __half o[8];
+          for (int i = 0; i < 2; ++i)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) o[j] = f2h(silu_f(f[16 * i + j]) * f[16 * i + 8 + j]);
-            *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(a.y) + (size_t)m * a.ldy + r0 / 2) =
-                *reinterpret_cast<const uint4*>(o);
-          }
+            for (int j = 0; j < 8; ++j) stage[lane * 33 + 8 * i + j] = silu_f(f[16 * i + j]) * f[16 * i + 8 + j];
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
+          for (int j = 0; j < 32; ++j) stage[lane * 33 + j] = f[j];
+        }
+        __syncwarp();
+        const int W = swiglu ? W_SWIGLU : 32, lw = swiglu ? 4 : 5;
+        for (int idx = lane; idx < 32 * W; idx += 32) {
+          const int q = idx >> lw, j = idx & (W - 1);
+          const int m = rowbase + q;
+          if (m >= a.NB) continue;
+          const float val = stage[q * 33 + j];
+          if (swiglu) {
+            const int r0 = nbase + 16 * (j >> 3);
+            if (r0 + 16 > a.N) continue;
+            reinterpret_cast<__half*>(a.y)[(size_t)m * a.ldy + r0 / 2 + (j & 7)] = f2h(val);
+          } else {
             const int n = nbase + j;
-            if (n >= a.N) break;
+            if (n >= a.N) continue;
             const size_t o = (size_t)m * a.ldy + n;
-            if (a.epi == EPI_F32) reinterpret_cast<float*>(a.y)[o] = f[j];
-            else if (a.epi == EPI_F16) reinterpret_cast<__half*>(a.y)[o] = f2h(f[j]);
-            else if (a.ksplit > 1) atomicAdd(reinterpret_cast<float*>(a.y) + o, f[j]);   // k splits meet in y
-            else reinterpret_cast<float*>(a.y)[o] = __ldcg(reinterpret_cast<const float*>(a.y) + o) + f[j];
+            if (a.epi == EPI_F32) reinterpret_cast<float*>(a.y)[o] = val;
+            else if (a.epi == EPI_F16) reinterpret_cast<__half*>(a.y)[o] = f2h(val);
+            else if (a.ksplit > 1) atomicAdd(reinterpret_cast<float*>(a.y) + o, val);   // k splits meet in y
+            else reinterpret_cast<float*>(a.y)[o] = __ldcg(reinterpret_cast<const float*>(a.y) + o) + val;
           }
         }
+        __syncwarp();
       }
       }
     }
