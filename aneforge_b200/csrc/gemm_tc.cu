@@ -297,13 +297,15 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
     if (!ok) {
       af_set_err(a.err, AF_DEV_WAIT_TIMEOUT);
     } else {
-      // A warp's 32 TMEM lanes are 32 output rows; each 32-column chunk goes through a padded
-      // shared-memory tile (the operand ring is idle once the accumulators are final) so that the
-      // global loads / stores walk rows with consecutive lanes on consecutive columns (coalesced).
-      float* stage = reinterpret_cast<float*>(smem) + warp * (32 * 33);
-      constexpr int W_SWIGLU = 16;                           // outputs per row per chunk (two groups of 8)
+      // A warp's 32 TMEM lanes are 32 output rows. SwiGLU stores each row's 8-output groups as
+      // 16-byte vectors; the other epilogues stage each 32-column chunk in shared memory (the operand
+      // ring is idle once the accumulators are final; rows 144 bytes apart) and write it back as
+      // float4s with 8 consecutive lanes on one row's 128 bytes, so global loads and stores coalesce.
+      float* stage = reinterpret_cast<float*>(smem) + warp * (32 * 36);
+      const bool vec = a.N % 4 == 0 && a.ldy % 4 == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
       for (int mi = 0; mi < mlive; ++mi) {
       const int rowbase = m0 + mi * gm::BM + warp * 32;
+      const int m = rowbase + lane;
 #pragma unroll 1
       for (int c0 = 0; c0 < T::BN; c0 += 32) {
         uint32_t v[32];
@@ -320,36 +322,60 @@ __global__ void __launch_bounds__(gm::THREADS, 1) gemm_tc_kernel(GemvTcArgs a, c
           }
           f[j] = x;
         }
-        const bool swiglu = a.epi == EPI_SWIGLU;
-        if (swiglu) {
-          // rows 16i..16i+7 gate, 16i+8..16i+15 up -> outputs 8i..8i+7 of the chunk
-#pragma unroll
-          for (int i = 0; i < 2; ++i)
-#pragma unroll
-            for (int j = 0; j < 8; ++j) stage[lane * 33 + 8 * i + j] = silu_f(f[16 * i + j]) * f[16 * i + 8 + j];
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) stage[lane * 33 + j] = f[j];
-        }
-        __syncwarp();
-        const int W = swiglu ? W_SWIGLU : 32, lw = swiglu ? 4 : 5;
-        for (int idx = lane; idx < 32 * W; idx += 32) {
-          const int q = idx >> lw, j = idx & (W - 1);
-          const int m = rowbase + q;
+        if (a.epi == EPI_SWIGLU) {
+          // rows 16i..16i+7 gate, 16i+8..16i+15 up -> 8 outputs per 16 rows
           if (m >= a.NB) continue;
-          const float val = stage[q * 33 + j];
-          if (swiglu) {
-            const int r0 = nbase + 16 * (j >> 3);
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int r0 = nbase + 16 * i;
             if (r0 + 16 > a.N) continue;
-            reinterpret_cast<__half*>(a.y)[(size_t)m * a.ldy + r0 / 2 + (j & 7)] = f2h(val);
-          } else {
+            __half o[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = f2h(silu_f(f[16 * i + j]) * f[16 * i + 8 + j]);
+            *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(a.y) + (size_t)m * a.ldy + r0 / 2) =
+                *reinterpret_cast<const uint4*>(o);
+          }
+          continue;
+        }
+        if (!vec) {
+          if (m >= a.NB) continue;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
             const int n = nbase + j;
-            if (n >= a.N) continue;
+            if (n >= a.N) break;
             const size_t o = (size_t)m * a.ldy + n;
-            if (a.epi == EPI_F32) reinterpret_cast<float*>(a.y)[o] = val;
-            else if (a.epi == EPI_F16) reinterpret_cast<__half*>(a.y)[o] = f2h(val);
-            else if (a.ksplit > 1) atomicAdd(reinterpret_cast<float*>(a.y) + o, val);   // k splits meet in y
-            else reinterpret_cast<float*>(a.y)[o] = __ldcg(reinterpret_cast<const float*>(a.y) + o) + val;
+            if (a.epi == EPI_F32) reinterpret_cast<float*>(a.y)[o] = f[j];
+            else if (a.epi == EPI_F16) reinterpret_cast<__half*>(a.y)[o] = f2h(f[j]);
+            else if (a.ksplit > 1) atomicAdd(reinterpret_cast<float*>(a.y) + o, f[j]);   // k splits meet in y
+            else reinterpret_cast<float*>(a.y)[o] = __ldcg(reinterpret_cast<const float*>(a.y) + o) + f[j];
+          }
+          continue;
+        }
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4)
+          *reinterpret_cast<float4*>(stage + lane * 36 + 4 * q4) =
+              make_float4(f[4 * q4], f[4 * q4 + 1], f[4 * q4 + 2], f[4 * q4 + 3]);
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int q = 4 * k + (lane >> 3), jj = lane & 7;       // row q of the chunk, its float4 jj
+          const int mr = rowbase + q, n = nbase + 4 * jj;
+          if (mr >= a.NB || n >= a.N) continue;
+          const float4 val = *reinterpret_cast<const float4*>(stage + q * 36 + 4 * jj);
+          const size_t o = (size_t)mr * a.ldy + n;
+          if (a.epi == EPI_F32) {
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + o) = val;
+          } else if (a.epi == EPI_F16) {
+            const __half2 lo = __floats2half2_rn(val.x, val.y), hi = __floats2half2_rn(val.z, val.w);
+            *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(a.y) + o) =
+                make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+          } else if (a.ksplit > 1) {
+            float* yp = reinterpret_cast<float*>(a.y) + o;           // k splits meet in y
+            atomicAdd(yp, val.x); atomicAdd(yp + 1, val.y); atomicAdd(yp + 2, val.z); atomicAdd(yp + 3, val.w);
+          } else {
+            float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + o);
+            const float4 old = __ldcg(yp);
+            *yp = make_float4(old.x + val.x, old.y + val.y, old.z + val.z, old.w + val.w);
           }
         }
         __syncwarp();
