@@ -457,7 +457,8 @@ cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
   if (ring == 1 && var == 4) var = 6;
   // split-K for the residual epilogue (o / down prompt shapes, fewer tiles than SMs): AF_GEMM_SPLITK=S
   // runs S CTAs per 128-column tile over disjoint k ranges on the half-size rings (two CTAs per SM),
-  // each adding its partial into the fp32 residual atomically (summation order then varies by run)
+  // each adding its partial into the fp32 residual atomically (summation order then varies by run).
+  // Off by default: with the coalesced epilogue it measured slower (8B prompt o 50.8 -> 66.3 µs).
   static const int splitk = env_int("AF_GEMM_SPLITK", 0);
   a.ksplit = 1;
   const int KBT = (a.K + gm::BK - 1) / gm::BK;
