@@ -434,12 +434,15 @@ cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
   // (64 CTAs) got slower (64 -> 93, 136 -> 182 µs). AF_GEMM_MM: 0 this rule, 1 never, 2 always.
   static const int mm_env = env_int("AF_GEMM_MM", 0);
   const int tiles2 = ((a.NB + 2 * gm::BM - 1) / (2 * gm::BM)) * ((a.N + 255) / 256);
-  const int MM = a.NB > gm::BM && (mm_env == 2 || (mm_env == 0 && tiles2 >= sms)) ? 2 : 1;
+  // (AF_GEMM_MM=4, measurement: four M tiles on 128-column tiles, each weight slice dequantised once
+  // per 512 prompt rows)
+  const int MM = (mm_env == 4 && a.NB > 3 * gm::BM) ? 4
+                 : a.NB > gm::BM && (mm_env == 2 || (mm_env == 0 && tiles2 >= sms)) ? 2 : 1;
   const int MT = (a.NB + gm::BM * MM - 1) / (gm::BM * MM);
   // 128-column tiles only where they add no wave: twice the tiles must fit in as many waves of
   // `sms` CTAs as the 256-column tiles (AF_GEMM_NARROW: 0 never, 2 always, 1 this rule)
   const int wide_tiles = MT * ((a.N + 255) / 256), narrow_tiles = MT * ((a.N + 127) / 128);
-  const bool narrow = narrow_ok == 2 || (narrow_ok == 1 && wide_tiles < sms &&
+  const bool narrow = MM == 4 || narrow_ok == 2 || (narrow_ok == 1 && wide_tiles < sms &&
                                          (narrow_tiles + sms - 1) / sms == (wide_tiles + sms - 1) / sms);
   const int BNV = narrow ? 128 : 256;
   const int NT = (a.N + BNV - 1) / BNV;
@@ -449,7 +452,7 @@ cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
   static const int deep = env_int("AF_GEMM_DEEP", 1);
   // MM = 2: 128-column tiles with three operand and eight raw slices, 256-column with two and four
   // (the second A tile per slice takes the shared memory of one operand stage)
-  int var = MM == 2 ? (narrow ? 3 : 4) : (narrow ? (deep >= 1 ? 1 : 0) : 2);
+  int var = MM == 4 ? 8 : MM == 2 ? (narrow ? 3 : 4) : (narrow ? (deep >= 1 ? 1 : 0) : 2);
   // deeper operand rings at the same shared memory (measurement variants, AF_GEMM_RING=1): 128-column
   // tiles with six operand and four raw slices, two-tile 256-column with three and two
   static const int ring = env_int("AF_GEMM_RING", 0);
@@ -467,19 +470,21 @@ cudaError_t gemm_tc_launch(GemvTcArgs a, cudaStream_t st, bool pdl) {
     var = 7;
     a.ksplit = splitk;
   }
-  constexpr int NV = 8;
+  constexpr int NV = 9;
   static const size_t smems[NV] = {smem_for<128, 3, 4>(), smem_for<128, 4, 8>(), smem_for<256, 3, 4>(),
                                    smem_for<128, 3, 8, 2>(), smem_for<256, 2, 4, 2>(), smem_for<128, 6, 4>(),
-                                   smem_for<256, 3, 2, 2>(), smem_for<128, 2, 4>()};
+                                   smem_for<256, 3, 2, 2>(), smem_for<128, 2, 4>(), smem_for<128, 2, 4, 4>()};
   void* const fns[2][NV] = {
       {(void*)gemm_tc_kernel<false, 128, 3, 4, 1>, (void*)gemm_tc_kernel<false, 128, 4, 8, 1>,
        (void*)gemm_tc_kernel<false, 256, 3, 4, 1>, (void*)gemm_tc_kernel<false, 128, 3, 8, 2>,
        (void*)gemm_tc_kernel<false, 256, 2, 4, 2>, (void*)gemm_tc_kernel<false, 128, 6, 4, 1>,
-       (void*)gemm_tc_kernel<false, 256, 3, 2, 2>, (void*)gemm_tc_kernel<false, 128, 2, 4, 1>},
+       (void*)gemm_tc_kernel<false, 256, 3, 2, 2>, (void*)gemm_tc_kernel<false, 128, 2, 4, 1>,
+       (void*)gemm_tc_kernel<false, 128, 2, 4, 4>},
       {(void*)gemm_tc_kernel<true, 128, 3, 4, 1>, (void*)gemm_tc_kernel<true, 128, 4, 8, 1>,
        (void*)gemm_tc_kernel<true, 256, 3, 4, 1>, (void*)gemm_tc_kernel<true, 128, 3, 8, 2>,
        (void*)gemm_tc_kernel<true, 256, 2, 4, 2>, (void*)gemm_tc_kernel<true, 128, 6, 4, 1>,
-       (void*)gemm_tc_kernel<true, 256, 3, 2, 2>, (void*)gemm_tc_kernel<true, 128, 2, 4, 1>}};
+       (void*)gemm_tc_kernel<true, 256, 3, 2, 2>, (void*)gemm_tc_kernel<true, 128, 2, 4, 1>,
+       (void*)gemm_tc_kernel<true, 128, 2, 4, 4>}};
   const size_t smem = smems[var];
   void* fn = fns[i4 ? 1 : 0][var];
   static PerDeviceOnce attr[2][NV];
