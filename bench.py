@@ -355,13 +355,17 @@ def run_b200(args):
   for _ in range(args.warmup):
     prog.execute_async()
   prog.sync()
-  if ws > 1:
-    dist.barrier()
-  torch.cuda.synchronize()
-  e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-  if args.profile_region:
-    torch.cuda.profiler.start()         # ncu --profile-from-start off sees the timed steps only
-  with ClockSampler(local) as clk:
+  # the clock sampler (NVML set-up can take a while, differently on each rank) starts before the
+  # barrier, so every rank enters the timed region together: a rank that started late would hold
+  # the others in their all-reduce waits and their timers would count it
+  clk = ClockSampler(local)
+  with clk:
+    if ws > 1:
+      dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if args.profile_region:
+      torch.cuda.profiler.start()       # ncu --profile-from-start off sees the timed steps only
     e0.record(stream)
     for _ in range(args.steps):
       prog.execute_async()
