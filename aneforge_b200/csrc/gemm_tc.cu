@@ -19,8 +19,9 @@
 // per-row scale is applied to the fp32 result; group-32 int4 codes become fp16 code * scale since
 // the scale changes along K inside a slice); warp 12 owns the tensor memory and one of its threads
 // issues the MMAs, committing each slice to its "empty" barrier and the last to the accumulator
-// barrier. Warps 0-3 then read the accumulators (tcgen05.ld, 32 lanes each) and run the GEMV's
-// epilogues (F32 / F16 / RESID / SWIGLU).
+// barrier. Warps 0-3 then read the accumulators (tcgen05.ld, 32 lanes each: one output row per
+// lane) and run the GEMV's epilogues (F32 / F16 / RESID / SWIGLU); F32 / F16 / RESID stage each
+// 32-column chunk in the idle operand ring so that their global loads and stores run along rows.
 // Every wait is bounded; on a timeout the CTA records AF_DEV_WAIT_TIMEOUT, waits (bounded) for the
 // MMAs it issued, frees its tensor memory and returns. Every copy lands in the issuing CTA's own
 // shared memory.
