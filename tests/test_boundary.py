@@ -1,6 +1,7 @@
 """The drop-in boundary exactly as a reference maintainer binds it: the e5rt-shaped C ABI
 (`aneforge/_lib/ane_e5rt_dispatch.mm:416-725`, bound at `aneforge/_runtime.py:61-92`), through a
-ctypes table written the way INTEGRATION.md shows it (not this package's own binding).
+ctypes table written the way a reference maintainer would add it on the reference side (not this
+package's own binding).
 
 Contract under test (the shim's documented behaviour, kept by libaf_cuda.so):
   * `af_program_compile(dir, cache, mask, in_names, in_bytes, n_in, out_names, out_bytes, n_out)`
@@ -40,7 +41,7 @@ op cast src=t dst=y n=32 mode=1
 
 
 def bind():
-  """The reference-side ctypes table."""
+  """The reference-side ctypes table: one entry per e5rt-shaped call, the reference's argument types."""
   if not os.path.exists(LIB):
     pytest.skip("libaf_cuda.so is not built")
   lib = C.CDLL(LIB)
