@@ -1,5 +1,6 @@
-"""Plan rewrites on the host (no GPU): the chained-GEMV pass and the tensor-parallel all-reduce +
-RMSNorm fusion rewrite a decode plan's op list without changing what it computes."""
+"""Plan emission and rewrites on the host (no GPU): the chained-GEMV pass and the tensor-parallel
+all-reduce + RMSNorm fusion rewrite a decode plan's op list without changing what it computes; the
+MoE expert launches per batch size (selected, routed, dense) and the GEMM / GEMV choice per program."""
 from aneforge_b200.llm import plan_fuse_allreduce_norm, plan_gemv_chains
 from aneforge_b200.plan import PlanBuilder
 
@@ -64,3 +65,58 @@ def test_allreduce_norm_fusion():
   pb2.op("rmsnorm", x="other", g="g", out="xn", nb=1, d=8, floor=0.1)
   plan_fuse_allreduce_norm(pb2, enable=True)
   assert [k for k, _ in pb2.ops] == ["allreduce", "rmsnorm"]
+
+
+def _experts(E=8, F=512, D=256, kind="int8"):
+  from aneforge_b200.weights import DevExperts
+  return DevExperts(kind=kind, gu_w=None, gu_s=object() if kind == "int8" else None, down_w=None,
+                    down_s=object() if kind == "int8" else None, E=E, F=F, D=D)
+
+
+def test_routed_expert_gemvs_for_decode_batches():
+  """Decode batches of 2-64 rows: per expert, 16-row launches over the routed rows (gate|up gathers
+  x rows, down scatters y rows with their routing weights), ceil(NB / 16) launches each."""
+  from aneforge_b200 import moe
+  pb = PlanBuilder()
+  moe._expert_gemvs(pb, "L0", _experts(), 24, 8, 2, sparse=False)
+  gemvs = [kv for k, kv in pb.ops if k == "gemv"]
+  assert len(gemvs) == 8 * 2 * 2
+  for i, kv in enumerate(gemvs):
+    e, r0, down = i // 4, 16 * ((i // 2) % 2), i % 2 == 1
+    assert kv["fixe"] == e and kv["r0"] == r0 and kv["nb"] == 16 and kv["rld"] == 24 and kv["eg"] == 8
+    assert kv["rows"] == "moe.rows" and kv["rcnt"] == "moe.rcnt"
+    if down:
+      assert kv["route"] == 2 and kv["yrows"] == 24 and kv["rw"] == "moe.gw" and kv["x"] == "act"
+    else:
+      assert kv["route"] == 1 and kv["xrows"] == 24 and kv["x"] == "xn" and kv["y"] == "act"
+
+
+def test_expert_gemvs_batch_one_and_prefill():
+  """One row: the k selected experts read from device memory; prefill-sized row counts: every expert
+  densely with per-row weights (no routing lists)."""
+  from aneforge_b200 import moe
+  pb = PlanBuilder()
+  moe._expert_gemvs(pb, "L0", _experts(), 1, 8, 2, sparse=True)
+  assert [(kv.get("sel"), kv.get("slot")) for _, kv in pb.ops] == [("moe.sel", 0)] * 2 + [("moe.sel", 1)] * 2
+  pb = PlanBuilder()
+  moe._expert_gemvs(pb, "L0", _experts(), moe.ROUTED_MAX_ROWS + 1, 8, 2, sparse=False)
+  ops = [kv for _, kv in pb.ops]
+  assert len(ops) == 16 and all("route" not in kv and kv["nb"] == moe.ROUTED_MAX_ROWS + 1 for kv in ops)
+  assert [kv["fixe"] for kv in ops] == [e for e in range(8) for _ in range(2)]
+
+
+def test_decode_batches_keep_the_gemv():
+  """Tiled projections over prompt rows (>= 32) run as the tcgen05 GEMM; decode programs keep the
+  GEMV below 128 rows."""
+  from aneforge_b200 import llm
+  from aneforge_b200.weights import DevLinear
+  lin = DevLinear(kind="int8", w=None, s=object(), bias=None, N=4096, K=4096, tiled=True)
+  for ctx, want in (({"NB": 32, "gemm_min": llm.GEMM_MIN_ROWS}, True),
+                    ({"NB": 32, "gemm_min": llm.DECODE_GEMM_MIN_ROWS}, False),
+                    ({"NB": 128, "gemm_min": llm.DECODE_GEMM_MIN_ROWS}, True),
+                    ({"NB": 16}, False)):
+    pb = PlanBuilder()
+    llm._emit_linear(pb, ctx, "L0.o", lin, "att", "h", "resid")
+    (kind, kv), = pb.ops
+    assert kind == "gemv" and bool(kv.get("gemm")) == want, ctx
+    assert ("scr" in kv) == (not want)
