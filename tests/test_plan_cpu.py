@@ -120,3 +120,24 @@ def test_decode_batches_keep_the_gemv():
     (kind, kv), = pb.ops
     assert kind == "gemv" and bool(kv.get("gemm")) == want, ctx
     assert ("scr" in kv) == (not want)
+
+
+def test_prefill_attention_stages_expanded_kv_only_under_the_gqa_factor():
+  """Under int8 the reference's GQA expansion multiplies K and V by c = 127 * f16(1/127): the prefill
+  attention op then names a `kvx` buffer of [2][KV][S][dh] fp16 that the rope kernel fills with
+  f16(c * f16(x)) for the tensor-core attention; with c = 1 (or no grouping) it names none."""
+  from aneforge_b200 import llm
+  from aneforge_b200.weights import DevLinear
+  cfg = llm.LlamaConfig(dim=1024, n_layers=1, n_heads=8, n_kv_heads=2, ffn_dim=2048, vocab=4096)
+  lin = lambda n, k: DevLinear(kind="int8", w=None, s=object(), bias=None, N=n, K=k, tiled=True)
+  lw = {"qkv": lin((8 + 4) * 128, 1024), "o": lin(1024, 1024), "attn_floor": 0.1}
+  for expand in (True, False):
+    pb = PlanBuilder()
+    ctx = {"NB": 300, "scale": 128 ** -0.5, "kvc": 0.99993896484375 if expand else 1.0, "expand": expand,
+           "gemm_min": llm.GEMM_MIN_ROWS}
+    llm.emit_attention_prefill(pb, ctx, 0, lw, cfg, llm.LayerSpec())
+    (kv,) = [kv for k, kv in pb.ops if k == "attn_prefill"]
+    assert kv["expand"] == int(expand) and kv["s"] == 300 and kv["dh"] == 128
+    assert ("kvx" in kv) == expand
+    if expand:
+      assert pb.bufs["kvx"].nbytes == 2 * 2 * 2 * 300 * 128 and pb.bufs["kvx"].role == "tmp"
